@@ -1,0 +1,309 @@
+"""Prefill benchmark of the 27B-shaped Qwen3.5 hybrid decision scorer on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one packed prefill of a batch of 32 single-candidate requests (workload (a)
+of BASELINE's 27B config: prompt lengths log-normal, median 800, sigma 0.6, clipped to
+1..8192; synthetic uniform token ids; random-init bf16 weights of the 27B shape) through
+the C++ host and the sm_100a kernels, scored by the 8-label head on each final token.
+Weak scaling: every rank processes its own batch of 32 requests with a full weight
+replica; no collective on the hot path. Prints one JSON line on rank 0.
+
+`--impl reference` times the reference's CPU path on the host cores instead: the numpy
+restatement of the same forward (the reference's prefill exists only as GPU code; its CPU
+parity anchor is Transformers' PyTorch forward) on a bounded sample of the workload.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "system1-omni_b200"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "prefill tokens/s (27B-shape hybrid scorer, batch of 32 requests per GPU)"
+UNIT = "tokens/s"
+BATCH = 32
+
+
+def requests(rank, n=BATCH, seed=4):
+    rng = np.random.default_rng(seed + 1000 * rank)
+    x = np.exp(rng.normal(np.log(800.0), 0.6, n))
+    lens = np.clip(np.round(x), 1, 8192).astype(np.int64)
+    return [rng.integers(0, 151936, int(L)).astype(np.int32) for L in lens]
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = [s for s in self.samples if len(s) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p["hbm_gbs"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ CPU arm ----
+def cpu_sample(tokens=256, seed=0):
+    """Time the numpy restatement of one 4-layer period (3 GDN + 1 attention + MLPs) of
+    the 27B shape on one prompt of `tokens` tokens; return (tokens/s extrapolated to 64
+    layers, seconds, threads)."""
+    from threadpoolctl import threadpool_info
+    from oracle import model as OM
+    from oracle.bf16 import rnd
+    cfg = OM.preset("27b")
+    cfg = OM.Config(cfg.hidden, cfg.intermediate, ["gdn", "gdn", "gdn", "attn"], cfg.lin_k_heads, cfg.lin_v_heads,
+                    cfg.heads, cfg.kv_heads, 4096, name="27b-period")
+    rng = np.random.default_rng(seed)
+    W = {}
+    shared = {}
+    for name, shape, kind in OM.weight_shapes(cfg):
+        leaf = name.split(".")[-1]
+        key = (leaf, shape)
+        if key not in shared:  # one draw per distinct tensor shape: timing, not accuracy
+            x = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+            if leaf == "A_log":
+                x = np.log(rng.uniform(1, 16, shape)).astype(np.float32)
+            if leaf in ("norm", "dt_bias"):
+                x = x + np.float32(1)
+            shared[key] = x if kind == "f32" else rnd(x)
+        W[name] = shared[key]
+    ids = rng.integers(0, cfg.vocab, tokens)
+    t0 = time.perf_counter()
+    OM.run_sequence(cfg, W, ids, gdn_mode="fp32")
+    dt = time.perf_counter() - t0
+    threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    per_token_period = dt / tokens
+    return 1.0 / (per_token_period * 16), dt, threads
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample(args.cpu_tokens)
+    for _ in range(args.steps):
+        v, dt, threads = cpu_sample(args.cpu_tokens)
+        vals.append(v)
+    value = float(np.median(vals))
+    sample = (f"one {args.cpu_tokens}-token prompt through one 4-layer period (3 GDN + 1 attention + MLPs) of the "
+              f"27B shape, numpy float32 restatement, x16 periods (extrapolated to 64 layers)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "27b-a-batch32", "model": "qwen3.5-27b-shape", "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------ GPU arm ----
+def gemm_roofline(cs1, cfg, M, stream, torch):
+    """Time the projection GEMMs of one GDN layer, one attention layer and the MLP at the
+    workload's M with CUDA events on the launching stream; return TFLOP/s and ms."""
+    H, I_ = cfg.hidden, cfg.intermediate
+    kd, vd, hv = cfg.lin_k_heads * 128, cfg.lin_v_heads * 128, cfg.lin_v_heads
+    shapes = [((2 * kd + vd) + vd + 2 * hv, H, "store"), (H, vd, "residual"),
+              (2 * cfg.heads * 256 + 2 * cfg.kv_heads * 256, H, "store"), (H, cfg.heads * 256, "residual"),
+              (2 * I_, H, "swiglu"), (H, I_, "residual")]
+    h = cs1.cs1_gemm_create(0)
+    x = torch.randn(M, max(I_, H), device="cuda").to(torch.bfloat16) * 0.5
+    flops = 0.0
+    ms = 0.0
+    launches = 0
+    for N, K, kind in shapes:
+        w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
+        out_n = N // 2 if kind == "swiglu" else N
+        y = torch.zeros(M, out_n, device="cuda", dtype=torch.bfloat16)
+        xs = x[:, :K].contiguous()
+
+        def call():
+            if kind == "swiglu":
+                cs1.cs1_gemm_swiglu(h, xs, w, y, M, N // 2, K, out_n, stream)
+            elif kind == "residual":
+                cs1.cs1_gemm_residual(h, xs, w, y, M, N, K, out_n, stream)
+            else:
+                cs1.cs1_gemm(h, xs, w, y, M, N, K, out_n, stream)
+        for _ in range(3):
+            call()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        reps = 10
+        torch.cuda.synchronize()
+        s.record(torch.cuda.current_stream())
+        for _ in range(reps):
+            call()
+        e.record(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        ms += s.elapsed_time(e) / reps
+        flops += 2.0 * M * N * K
+        launches += 1
+        del w, y, xs
+    cs1.cs1_gemm_destroy(h)
+    return flops / (ms * 1e-3) / 1e12, ms, flops, launches
+
+
+def run_ours(args, rank, world, local):
+    import torch
+    from s1omni import Cs1, Model, preset
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    cfg = preset("27b")
+    seqs = requests(rank)
+    tokens = int(sum(len(s) for s in seqs))
+    cap = max(tokens, 1) + 64
+    model = Model(cfg, device=local, max_tokens=cap, max_seqs=BATCH)
+    model.init_random(seed=1234, std=0.02)
+    cs1 = Cs1()
+    stream = torch.cuda.ExternalStream(model.stream)
+    model.stage(seqs)
+    model.run_staged()           # eager pass: counts the launches
+    launches_per_step = model.last_launches
+    model.set_graphs(True)
+    for _ in range(max(args.warmup, 3)):
+        model.run_staged()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    with clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            model.run_staged()
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    logits = model.fetch_logits()
+    ok = bool(np.isfinite(logits).all()) and Cs1().cs1_fault_status(1) == 0
+    # end to end through the public API: host ids in, host logits out, every step
+    e2e_ms = []
+    for i in range(max(2, min(args.steps, 5))):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        model.forward(seqs)
+        e2e_ms.append((time.perf_counter() - t0) * 1e3)
+    e2e = float(np.median(e2e_ms[1:]))
+    h2d = tokens * 4 + tokens * 32 * 2 * 2 + BATCH * 4
+    d2h = BATCH * cfg.labels * 4
+    tmax = torch.tensor([ms, e2e], device="cuda")
+    tok = torch.tensor([float(tokens)], device="cuda")
+    if dist:
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(tok, op=dist.ReduceOp.SUM)
+    ms_max, e2e_max = float(tmax[0]), float(tmax[1])
+    total_tokens = float(tok[0])
+    result = None
+    if rank == 0:
+        tflops, gms, gflops, _ = gemm_roofline(cs1, cfg, tokens, torch.cuda.current_stream().cuda_stream, torch)
+        peak_tf, peak_bw, peak_kind = measured_peaks()
+        value = total_tokens / (ms_max * 1e-3)
+        proj = cfg.projection_flops_per_token() * tokens
+        cpu_v, cpu_dt, cpu_threads = cpu_sample(args.cpu_tokens) if not args.no_cpu else (None, 0.0, 0)
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform token ids, random-init weights)",
+            "config": {"workload": "27b-a-batch32", "model": "qwen3.5-27b-shape hybrid scorer (48 GDN + 16 attn)",
+                       "requests_per_gpu": BATCH, "tokens_per_gpu": tokens, "global_batch": BATCH * world,
+                       "seq_len": "log-normal median 800 sigma 0.6 clip 1..8192", "parallelism": f"replica x{world}",
+                       "l2": "weights (54 GB) and activations exceed L2 every step", "cuda_graphs": True},
+            "e2e": {"value": total_tokens / (e2e_max * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "roofline": {"bound": "tensor", "kernel": "tcgen05 projection GEMM (6 shapes of a layer set)",
+                         "achieved": tflops, "peak": peak_tf, "unit": "TFLOP/s", "frac": tflops / peak_tf,
+                         "peak_kind": peak_kind + " burst bf16", "traffic": None,
+                         "forward_projection_tflops": proj / (ms_max * 1e-3) / 1e12},
+            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
+                             "sample": f"one {args.cpu_tokens}-token prompt, one 4-layer period of the 27B shape "
+                                       f"(numpy float32 restatement), x16 periods"},
+            "clocks": clocks.summary(),
+            "checks": {"finite_logits_no_fault": ok},
+        }
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    model.close()
+    if result:
+        print(json.dumps(result), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-tokens", type=int, default=256)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,105 @@
+// C interface of libs1_model.so: the Qwen3.5 hybrid decision-model prefill host.
+//
+// The host side of the reference's worker, rebuilt in C++ above the cs1_* ABI of
+// qwen3_5_ops.h (the reference's host is Rust, which this build cannot compile):
+//   s1_model_create / set_weight / init_random   Model::load_with_graph and the weight arena
+//                                                (src/models/qwen3_5/native/src/model.rs:945-1076, 316-397)
+//   s1_model_forward                             Model::forward_batch -> forward_batch_layout ->
+//                                                run_with_attention (model.rs:1505, 1548-1632, 3178-3727)
+//                                                plus DecisionHead::score per candidate
+//                                                (src/models/open_jev/native/src/executor.rs:59-71)
+//   s1_model_forward_shared                      Model::try_forward_shared_prefix ->
+//                                                shared_prefix_with_original_rows (model.rs:1634-1907)
+//   s1_model_set_graphs                          the CUDA-graph cache keyed by the length vector
+//                                                (model.rs:1583-1614, 1959)
+// The model binds a cs1_* library by path at run time (dlopen, ABI version 9 check,
+// required + optional symbols), as the reference's loader does (cuda.rs:673-698), so
+// the same host drives this build's library or any other ABI-9 library.
+//
+// Errors: functions return 0 on success, else a cs1/CUDA error code or -1 for a host
+// error; s1_model_error() describes the last one. Not thread-safe: one caller at a time
+// per model (the reference serialises its Model behind a mutex, executor.rs:127).
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct s1_config {
+    int hidden;          // H
+    int intermediate;    // I (multiple of 128 for the fused SwiGLU projection)
+    int n_layers;
+    const int* layer_types;  // n_layers entries: 0 = Gated DeltaNet, 1 = gated full attention
+    int lin_k_heads;     // GDN key heads (HK)
+    int lin_v_heads;     // GDN value heads (HV)
+    int lin_k_dim;       // 128
+    int lin_v_dim;       // 128
+    int heads;           // attention query heads
+    int kv_heads;        // attention key/value heads
+    int head_dim;        // 256
+    int rotary_half;     // 32 (rotary on the first 64 dims)
+    double theta;        // rotary base
+    float eps;           // RMSNorm epsilon
+    int vocab;
+    int labels;          // scorer-head rows
+} s1_config;
+
+// Binds the cs1 library at `cs1_library_path`, selects `device`, allocates the weight
+// arena and scratch for packs of up to max_tokens rows and max_seqs sequences.
+// Returns null on failure (s1_model_error(NULL) then describes it).
+void* s1_model_create(const char* cs1_library_path, const s1_config* cfg, int device, int max_tokens,
+                      int max_seqs);
+void s1_model_destroy(void* model);
+const char* s1_model_error(void* model);
+
+// Parameter names: "embed", "final_norm", "head_w" (f32 [labels,H]), "head_b" (f32 [labels]),
+// and per layer i "l<i>.<leaf>" with leaf in input_norm, post_norm, gate, up, down and
+// GDN: in_qkv, in_z, in_b, in_a, conv, A_log, dt_bias, norm, out;
+// attention: q, k, v, q_norm, k_norm, o. Data are host bf16 (f32 for the head),
+// row-major in the Transformers shapes; `bytes` must match.
+int s1_model_set_weight(void* model, const char* name, const void* host_data, size_t bytes);
+// Fill every parameter on the device from a counter-based generator (benchmarks):
+// matrices ~ N(0, std), zero-centred norms ~ N(0, 0.1), gated-norm weight ~ 1 + N(0, 0.1),
+// conv ~ U(-0.5, 0.5), A_log = log U(1, 16), dt_bias ~ 1 + N(0, 0.1).
+int s1_model_init_random(void* model, uint64_t seed, float std);
+
+// Packed independent candidates: ids concatenated [sum lengths] (host), lengths[count].
+// Writes logits [count, labels] (host f32) and, if hidden is non-null, each candidate's
+// final-norm last-token row [count, H] (host f32).
+int s1_model_forward(void* model, const int32_t* ids, const size_t* lengths, size_t count, float* logits,
+                     float* hidden);
+// One shared prefix, computed once, then `count` suffixes continued from its GDN
+// states, conv history and attention K/V (positions continue at prefix_len).
+int s1_model_forward_shared(void* model, const int32_t* prefix_ids, size_t prefix_len, const int32_t* suffix_ids,
+                            const size_t* suffix_lengths, size_t count, float* logits, float* hidden);
+
+// Resident inputs (benchmarks): stage ids and lengths on the device once, then run the
+// forward on the model stream without host copies; fetch the logits afterwards.
+int s1_model_stage(void* model, const int32_t* ids, const size_t* lengths, size_t count);
+int s1_model_run_staged(void* model);
+int s1_model_fetch_logits(void* model, float* logits);
+
+// CUDA graphs for repeated length vectors (default off): 0 = eager, 1 = capture/replay.
+int s1_model_set_graphs(void* model, int enabled);
+// The model's cudaStream_t (for timing with events on the launching stream).
+void* s1_model_stream(void* model);
+// Kernel launches the last forward issued through the cs1 library (eager count).
+long s1_model_last_launches(void* model);
+// Fused projections (cs1_gemm_residual / cs1_gemm_swiglu) in use: 1 yes, 0 no.
+int s1_model_fused(void* model);
+
+// ---- packing policy (host integer logic, no GPU) ----
+// Launch ranges of candidates (src/models/open_jev/native/src/batching.rs:9-25): writes
+// the start of each range to starts[] (capacity count + 1; starts[ranges] = count) and
+// returns the number of ranges, or -1 on invalid arguments.
+int s1_pack_ranges(const size_t* lengths, size_t count, size_t max_sequences, size_t max_tokens, size_t* starts);
+// Shared prefix of 2..16 candidates (batching.rs:29-49): the common prefix floored to a
+// multiple of 64, or 0 if under 512 or if any candidate is shorter than `minimum`.
+size_t s1_shared_prefix(const int32_t* const* ids, const size_t* lengths, size_t count, size_t minimum);
+
+#ifdef __cplusplus
+}
+#endif

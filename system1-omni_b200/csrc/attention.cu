@@ -1,0 +1,428 @@
+// Full-attention layers of the Qwen3.5 prefill: q/k preparation and gated GQA
+// flash attention (head dim 256).
+//
+// attn_prep: one warp per (token, head); each lane holds 8 consecutive dims (one
+// 16-byte load). Per-head zero-centred RMSNorm (one bf16 rounding), then partial
+// rotary embedding on the first 2*half dims (rotate_half; each product and the
+// sum rounded to bf16 as Transformers does in bf16); the partner of dim d < half
+// (dim d + half) sits in lane ^ (half / 8). The gate half of each q row is copied out.
+//
+// flash attention: a CTA takes 128 queries of one head (8 warps x 16 rows) and
+// walks 64-key tiles up to its last query; K/V tiles are double-buffered with
+// cp.async; QK^T and PV run on mma.sync m16n8k16 (bf16 in, fp32 accumulate);
+// online softmax in base 2 with fp32 running max/sum; probabilities rounded to
+// bf16 for PV; the gated epilogue is bf16(bf16(att) * bf16(sigmoid(gate))).
+// One kernel serves every entry point through its arguments: packed sequences
+// (a SeqTable), an immutable shared prefix K/V read before each sequence's own
+// rows (positions continue after it), a windowed first query row, and the
+// bidirectional / prefix-bidirectional masks.
+#include <climits>
+
+#include "common.cuh"
+#include "ops_internal.h"
+#include "tc.cuh"
+
+S1_FAULT_WORD(attention)
+
+namespace s1 {
+namespace attn {
+
+constexpr int DH = 256;
+
+// ---------------------------------------------------------------- prep ----
+__global__ void prep_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
+                            const bf16* __restrict__ qw, const bf16* __restrict__ kw, const bf16* __restrict__ cosb,
+                            const bf16* __restrict__ sinb, bf16* __restrict__ q, bf16* __restrict__ gate,
+                            bf16* __restrict__ k, int T, int Hq, int Hk, int half, float eps) {
+    const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int heads = Hq + Hk;
+    if (warp >= T * heads) return;
+    const int t = warp / heads, hh = warp % heads;
+    const bool is_q = hh < Hq;
+    const int h = is_q ? hh : hh - Hq;
+    const bf16* src = is_q ? qg + (size_t)t * ld + (size_t)h * 2 * DH : kr + (size_t)t * ld + (size_t)h * DH;
+    const int d0 = lane * 8;
+    float x[8], w[8];
+    unpack8(ld8(src + d0), x);
+    unpack8(ld8((is_q ? qw : kw) + d0), w);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) ss = fmaf(x[i], x[i], ss);
+    const float inv = rsqrtf(warp_sum(ss) / DH + eps);
+#pragma unroll
+    for (int i = 0; i < 8; i++) x[i] = rbf(x[i] * inv * (1.f + w[i]));
+    const int rot = 2 * half;
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float partner = __shfl_xor_sync(0xffffffffu, x[i], half / 8);
+        const int d = d0 + i;
+        y[i] = x[i];
+        if (d < rot) {
+            const int fi = d % half;
+            const float c = f32(cosb[(size_t)t * half + fi]), s = f32(sinb[(size_t)t * half + fi]);
+            const float r = d < half ? -partner : partner;
+            y[i] = rbf(rbf(x[i] * c) + rbf(r * s));
+        }
+    }
+    if (is_q) {
+        st8(q + ((size_t)t * Hq + h) * DH + d0, pack8(y));
+        st8(gate + ((size_t)t * Hq + h) * DH + d0, ld8(src + DH + d0));
+    } else {
+        st8(k + ((size_t)t * Hk + h) * DH + d0, pack8(y));
+    }
+}
+
+// ---------------------------------------------------------------- flash ----
+constexpr int BM = 128, BN = 64, WARPS = 8, THREADS = WARPS * 32;
+constexpr int LDS = DH + 8;  // padded smem row (528 B): ldmatrix rows hit distinct banks
+constexpr int TILE_Q = BM * LDS, TILE_KV = BN * LDS;
+constexpr int SMEM = (TILE_Q + 4 * TILE_KV) * 2;
+
+struct Args {
+    const bf16* q;
+    const bf16* k;
+    const bf16* v;
+    int ldv;
+    const bf16* gate;
+    bf16* out;
+    const bf16* pk;   // shared prefix K [P][Hk][DH] (or null)
+    const bf16* pv;   // shared prefix V [P][Hk][DH]
+    int P;            // prefix length (positions of own rows start at P)
+    int q_base;       // first own query row computed (multiple of BM... any value)
+    int state;        // prefix-bidirectional boundary (0 = none)
+    int Hq, Hk;
+    float scale_log2;
+    int gated, causal;
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const uint32_t s = tc::smem_u32(smem);
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const bf16* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(tc::smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const bf16* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(tc::smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(THREADS, 1) flash_kernel(Args a, SeqTable tab) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    bf16* qs = reinterpret_cast<bf16*>(smem_raw);
+    bf16* ks = qs + TILE_Q;  // [2][BN][LDS]
+    bf16* vs = ks + 2 * TILE_KV;
+    const int seq = blockIdx.z, h = blockIdx.y, hk = h / (a.Hq / a.Hk);
+    const int off = tab.offset[seq];
+    const int len = tab.offset[seq + 1] - off;
+    const int qrows = len - a.q_base;
+    const int nblocks = (qrows + BM - 1) / BM;
+    if ((int)blockIdx.x >= nblocks) return;
+    const int qb = nblocks - 1 - (int)blockIdx.x;   // longest causal blocks first
+    const int q0 = a.q_base + qb * BM;               // first own query row of this block
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int P = a.P;
+    const int total = P + len;                        // keys visible to this sequence
+    const int qpos0 = P + q0;                         // absolute position of the block's first query
+    // keys needed: causal -> up to the block's last query; otherwise all
+    const int kv_end = a.causal ? min(total, qpos0 + BM) : total;
+
+    for (int c = tid; c < BM * (DH / 8); c += THREADS) {
+        const int r = c / (DH / 8), col = (c % (DH / 8)) * 8;
+        const int row = min(q0 + r, len - 1);
+        cp_async16(qs + r * LDS + col, a.q + ((size_t)(off + row) * a.Hq + h) * DH + col, q0 + r < len);
+    }
+    auto load_kv = [&](int tile, int buf) {
+        const int k0 = tile * BN;
+        for (int c = tid; c < BN * (DH / 8); c += THREADS) {
+            const int r = c / (DH / 8), col = (c % (DH / 8)) * 8;
+            const int key = min(k0 + r, total - 1);
+            const bool valid = k0 + r < total;
+            const bf16* ksrc;
+            const bf16* vsrc;
+            if (key < P) {
+                ksrc = a.pk + ((size_t)key * a.Hk + hk) * DH + col;
+                vsrc = a.pv + ((size_t)key * a.Hk + hk) * DH + col;
+            } else {
+                const size_t row = (size_t)(off + key - P);
+                ksrc = a.k + (row * a.Hk + hk) * DH + col;
+                vsrc = a.v + row * a.ldv + (size_t)hk * DH + col;
+            }
+            cp_async16(ks + buf * TILE_KV + r * LDS + col, ksrc, valid);
+            cp_async16(vs + buf * TILE_KV + r * LDS + col, vsrc, valid);
+        }
+    };
+    const int ntiles = (kv_end + BN - 1) / BN;
+    load_kv(0, 0);
+    cp_commit();
+
+    float o[DH / 8][4];
+#pragma unroll
+    for (int n = 0; n < DH / 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+    const int wrow0 = qpos0 + warp * 16;  // absolute position of this warp's first row
+    const int rows_valid = len - (q0 + warp * 16);
+
+    for (int tile = 0; tile < ntiles; tile++) {
+        const int buf = tile & 1;
+        if (tile + 1 < ntiles) load_kv(tile + 1, buf ^ 1);
+        cp_commit();
+        cp_wait<1>();
+        __syncthreads();
+        const int k0 = tile * BN;
+        const bf16* kb = ks + buf * TILE_KV;
+        const bf16* vb = vs + buf * TILE_KV;
+        // does this warp see any key of the tile?
+        bool active = rows_valid > 0;
+        if (a.causal) active = active && k0 <= wrow0 + 15;
+        if (active) {
+            float sc[BN / 8][4];
+#pragma unroll
+            for (int n = 0; n < BN / 8; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < DH; kk += 16) {
+                uint32_t af[4];
+                ldsm_x4(af, qs + (warp * 16 + (lane & 15)) * LDS + kk + (lane >> 4) * 8);
+#pragma unroll
+                for (int n = 0; n < BN / 8; n += 2) {
+                    uint32_t bfr[4];
+                    ldsm_x4(bfr, kb + (n * 8 + (lane & 7) + (lane >> 4) * 8) * LDS + kk + ((lane >> 3) & 1) * 8);
+                    mma16816(sc[n], af, bfr[0], bfr[1]);
+                    mma16816(sc[n + 1], af, bfr[2], bfr[3]);
+                }
+            }
+            float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int n = 0; n < BN / 8; n++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int key = k0 + n * 8 + 2 * t4 + (e & 1);
+                    const int qpos = wrow0 + g + (e >> 1) * 8;
+                    bool vis = key < total;
+                    if (a.causal) vis = vis && key <= qpos;
+                    else if (a.state > 0 && qpos < a.state) vis = vis && key < a.state;
+                    sc[n][e] = vis ? sc[n][e] * a.scale_log2 : -INFINITY;
+                    mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
+                }
+            float alpha[2], base2[2];
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+                const float mn = fmaxf(m[r], mx[r]);
+                base2[r] = mn == -INFINITY ? 0.f : mn;
+                alpha[r] = exp2f(m[r] - base2[r]);
+                m[r] = mn;
+                l[r] *= alpha[r];
+            }
+#pragma unroll
+            for (int n = 0; n < BN / 8; n++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    sc[n][e] = exp2f(sc[n][e] - base2[e >> 1]);
+                    l[e >> 1] += sc[n][e];
+                }
+#pragma unroll
+            for (int n = 0; n < DH / 8; n++) {
+                o[n][0] *= alpha[0];
+                o[n][1] *= alpha[0];
+                o[n][2] *= alpha[1];
+                o[n][3] *= alpha[1];
+            }
+#pragma unroll
+            for (int j = 0; j < BN / 16; j++) {
+                uint32_t pa[4];
+                pa[0] = pack_bf16x2(sc[2 * j][0], sc[2 * j][1]);
+                pa[1] = pack_bf16x2(sc[2 * j][2], sc[2 * j][3]);
+                pa[2] = pack_bf16x2(sc[2 * j + 1][0], sc[2 * j + 1][1]);
+                pa[3] = pack_bf16x2(sc[2 * j + 1][2], sc[2 * j + 1][3]);
+#pragma unroll
+                for (int n = 0; n < DH / 8; n += 2) {
+                    uint32_t bfr[4];
+                    ldsm_x4_t(bfr, vb + (j * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + n * 8 + (lane >> 4) * 8);
+                    mma16816(o[n], pa, bfr[0], bfr[1]);
+                    mma16816(o[n + 1], pa, bfr[2], bfr[3]);
+                }
+            }
+        }
+        __syncthreads();  // the next prefetch overwrites this buffer
+    }
+    cp_wait<0>();
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
+        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int lrow = q0 + warp * 16 + g + r * 8;  // own row index
+        if (lrow >= len) continue;
+        const float inv = 1.f / l[r];
+        const size_t orow = ((size_t)(off + lrow) * a.Hq + h) * DH;
+#pragma unroll
+        for (int n = 0; n < DH / 8; n++) {
+            const int col = n * 8 + 2 * t4;
+            float x0 = o[n][2 * r] * inv, x1 = o[n][2 * r + 1] * inv;
+            if (a.gated) {
+                const __nv_bfloat162 gv = *reinterpret_cast<const __nv_bfloat162*>(a.gate + orow + col);
+                x0 = rbf(x0) * rbf(sigmoid(__low2float(gv)));
+                x1 = rbf(x1) * rbf(sigmoid(__high2float(gv)));
+            }
+            *reinterpret_cast<uint32_t*>(a.out + orow + col) = pack_bf16x2(x0, x1);
+        }
+    }
+}
+
+int launch(Args a, const SeqTable& tab, cudaStream_t st) {
+    if (a.Hq <= 0 || a.Hk <= 0 || a.Hq % a.Hk || a.ldv % 8 || a.ldv < a.Hk * DH) return cudaErrorInvalidValue;
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (configured != cudaSuccess) return configured;
+    int max_rows = 0;
+    for (int i = 0; i < tab.count; i++) max_rows = max(max_rows, tab.offset[i + 1] - tab.offset[i] - a.q_base);
+    if (max_rows <= 0) return cudaSuccess;
+    const dim3 grid((max_rows + BM - 1) / BM, a.Hq, tab.count);
+    flash_kernel<<<grid, THREADS, SMEM, st>>>(a, tab);
+    return cudaGetLastError();
+}
+
+Args make_args(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out, int Hq, int Hk,
+               float scale, bool causal) {
+    Args a{};
+    a.q = static_cast<const bf16*>(q);
+    a.k = static_cast<const bf16*>(k);
+    a.v = static_cast<const bf16*>(v);
+    a.ldv = ldv;
+    a.gate = static_cast<const bf16*>(gate);
+    a.out = static_cast<bf16*>(out);
+    a.Hq = Hq;
+    a.Hk = Hk;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.gated = gate != nullptr;
+    a.causal = causal;
+    return a;
+}
+
+int single(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out, int T, int Hq, int Hk,
+           int Dh, float scale, int q_base, bool causal, int state, bool need_gate, void* stream) {
+    if (Dh != DH || T < 0 || !q || !k || !v || !out) return cudaErrorInvalidValue;
+    if (q_base < 0 || q_base > T || (need_gate && !gate && T > 0)) return cudaErrorInvalidValue;
+    if (T == q_base) return cudaSuccess;
+    SeqTable tab;
+    const size_t len = (size_t)T;
+    make_table(tab, &len, 1);
+    Args a = make_args(q, k, v, ldv, gate, out, Hq, Hk, scale, causal);
+    a.q_base = q_base;
+    a.state = state;
+    return launch(a, tab, static_cast<cudaStream_t>(stream));
+}
+
+}  // namespace attn
+}  // namespace s1
+
+using namespace s1;
+
+extern "C" {
+
+int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const void* kw, const void* cos,
+                  const void* sin, void* q, void* gate, void* k, int T, int Hq, int Hk, int Dh, int half, float eps,
+                  void* stream) {
+    if (ld % 8 != 0 || T < 0 || Hq < 0 || Hk < 0) return cudaErrorInvalidValue;
+    if (Dh != attn::DH || half <= 0 || half % 8 != 0 || 2 * half > Dh || ((half / 8) & (half / 8 - 1)))
+        return cudaErrorInvalidValue;
+    const long warps = (long)T * (Hq + Hk);
+    if (warps == 0) return cudaSuccess;
+    if (!aligned16(qg) || !aligned16(kr) || !aligned16(qw) || !aligned16(kw) || !aligned16(q) || !aligned16(gate) ||
+        !aligned16(k))
+        return cudaErrorInvalidValue;
+    constexpr int WPB = 8;
+    attn::prep_kernel<<<(unsigned)((warps + WPB - 1) / WPB), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const bf16*>(qg), static_cast<const bf16*>(kr), ld, static_cast<const bf16*>(qw),
+        static_cast<const bf16*>(kw), static_cast<const bf16*>(cos), static_cast<const bf16*>(sin),
+        static_cast<bf16*>(q), static_cast<bf16*>(gate), static_cast<bf16*>(k), T, Hq, Hk, half, eps);
+    return cudaGetLastError();
+}
+
+int cs1_attention(const void* q, const void* k, const void* v, int ldv, void* out, int T, int Hq, int Hk, int Dh,
+                  float scale, void* stream) {
+    return attn::single(q, k, v, ldv, nullptr, out, T, Hq, Hk, Dh, scale, 0, true, 0, false, stream);
+}
+
+int cs1_attention_gated(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out, int T,
+                        int Hq, int Hk, int Dh, float scale, void* stream) {
+    return attn::single(q, k, v, ldv, gate, out, T, Hq, Hk, Dh, scale, 0, true, 0, true, stream);
+}
+
+int cs1_attention_gated_bidirectional(const void* q, const void* k, const void* v, int ldv, const void* gate,
+                                      void* out, int T, int Hq, int Hk, int Dh, float scale, void* stream) {
+    return attn::single(q, k, v, ldv, gate, out, T, Hq, Hk, Dh, scale, 0, false, 0, true, stream);
+}
+
+int cs1_attention_gated_prefix_bidirectional(const void* q, const void* k, const void* v, int ldv, const void* gate,
+                                             void* out, int T, int state, int Hq, int Hk, int Dh, float scale,
+                                             void* stream) {
+    if (state <= 0 || state >= T || !gate) return cudaErrorInvalidValue;
+    return attn::single(q, k, v, ldv, gate, out, T, Hq, Hk, Dh, scale, 0, false, state, true, stream);
+}
+
+int cs1_attention_gated_prefix(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
+                               int T, int Hq, int Hk, int Dh, float scale, int q_base, void* stream) {
+    if (q_base % 64) return cudaErrorInvalidValue;
+    return attn::single(q, k, v, ldv, gate, out, T, Hq, Hk, Dh, scale, q_base, true, 0, true, stream);
+}
+
+int cs1_attention_gated_shared(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
+                               const void* prefix_k, const void* prefix_v, int suffix, int prefix, int Hq, int Hk,
+                               int Dh, float scale, void* stream) {
+    if (!q || !k || !v || !gate || !out || !prefix_k || !prefix_v || suffix <= 0 || prefix <= 0 || prefix % 64 ||
+        prefix > INT_MAX - suffix || Dh != attn::DH)
+        return cudaErrorInvalidValue;
+    SeqTable tab;
+    const size_t len = (size_t)suffix;
+    make_table(tab, &len, 1);
+    attn::Args a = attn::make_args(q, k, v, ldv, gate, out, Hq, Hk, scale, true);
+    a.pk = static_cast<const bf16*>(prefix_k);
+    a.pv = static_cast<const bf16*>(prefix_v);
+    a.P = prefix;
+    return attn::launch(a, tab, static_cast<cudaStream_t>(stream));
+}
+
+int cs1_attention_gated_shared_batch(const void* q, const void* k, const void* v, int ldv, const void* gate,
+                                     void* out, const void* prefix_k, const void* prefix_v, const size_t* lengths,
+                                     size_t count, int prefix, int Hq, int Hk, int Dh, float scale, void* stream) {
+    SeqTable tab;
+    if (!q || !k || !v || !gate || !out || Dh != attn::DH || prefix < 0 || !make_table(tab, lengths, count))
+        return cudaErrorInvalidValue;
+    if (prefix > 0 && (!prefix_k || !prefix_v)) return cudaErrorInvalidValue;
+    attn::Args a = attn::make_args(q, k, v, ldv, gate, out, Hq, Hk, scale, true);
+    a.pk = static_cast<const bf16*>(prefix_k);
+    a.pv = static_cast<const bf16*>(prefix_v);
+    a.P = prefix;
+    return attn::launch(a, tab, static_cast<cudaStream_t>(stream));
+}
+
+int cs1_attention_gated_batch(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
+                              const size_t* lengths, size_t count, int Hq, int Hk, int Dh, float scale,
+                              void* stream) {
+    return cs1_attention_gated_shared_batch(q, k, v, ldv, gate, out, nullptr, nullptr, lengths, count, 0, Hq, Hk,
+                                            Dh, scale, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,326 @@
+// Embedding gather, the Gated DeltaNet front end (causal depthwise conv1d + SiLU,
+// gates) and the elementwise activations of the Qwen3.5 prefill. All are
+// bandwidth-bound: 16-byte accesses, grids sized by rows x packs.
+//
+// Rounding points follow the reference's elementwise.cu:
+//   conv   y = bf16(silu(bf16(sum_j w[c,j] x[t-3+j,c])))    (F.conv1d then F.silu, both bf16)
+//   gates  beta = bf16(sigmoid(b)); g = -exp(A_log) softplus(a + dt_bias) (fp32, threshold 20)
+//   silu   out = bf16(bf16(silu(gate)) * up)
+#include <climits>
+
+#include "common.cuh"
+#include "ops_internal.h"
+
+namespace s1 {
+
+bool make_table(SeqTable& t, const size_t* lengths, size_t count) {
+    if (!lengths || count == 0 || count > (size_t)MAX_SEQS) return false;
+    t.count = (int)count;
+    t.max_len = 0;
+    size_t rows = 0;
+    t.offset[0] = 0;
+    for (size_t i = 0; i < count; i++) {
+        if (lengths[i] == 0 || lengths[i] > (size_t)INT_MAX - rows) return false;
+        rows += lengths[i];
+        t.offset[i + 1] = (int)rows;
+        if ((int)lengths[i] > t.max_len) t.max_len = (int)lengths[i];
+    }
+    return true;
+}
+
+namespace {
+
+constexpr int THREADS = 256;
+
+__global__ void embed_kernel(const int32_t* __restrict__ ids, const Pack8* __restrict__ table,
+                             Pack8* __restrict__ out, int packs, int T) {
+    for (int t = blockIdx.x; t < T; t += gridDim.x) {
+        const size_t id = (size_t)ids[t];
+        for (int i = threadIdx.x; i < packs; i += blockDim.x) out[(size_t)t * packs + i] = table[id * packs + i];
+    }
+}
+
+// Eight channels per thread. The row's position inside its sequence decides which
+// taps read the three rows of `history` (shared by every sequence) or zeros.
+__global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld,
+                                const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
+                                bf16* __restrict__ v, int key_packs, int value_packs, SeqTable tab) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int packs = 2 * key_packs + value_packs;
+    if (c >= packs) return;
+    float wt[8][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        float f[8];
+        unpack8(ld8(w + (size_t)c * 32 + i * 8), f);
+#pragma unroll
+        for (int e = 0; e < 8; e++) wt[(i * 8 + e) / 4][(i * 8 + e) % 4] = f[e];
+    }
+    const int T = tab.offset[tab.count];
+    for (int t = blockIdx.y; t < T; t += gridDim.y) {
+        const int s = seq_of(tab, t);
+        const int pos = t - tab.offset[s];
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int back = 3 - j;
+            const bf16* src = nullptr;
+            if (pos >= back)
+                src = qkv + (size_t)(t - back) * ld + (size_t)c * 8;
+            else if (history)
+                src = history + (size_t)(3 - back + pos) * ld + (size_t)c * 8;
+            if (src) {
+                float x[8];
+                unpack8(ld8(src), x);
+#pragma unroll
+                for (int e = 0; e < 8; e++) acc[e] = fmaf(wt[e][j], x[e], acc[e]);
+            }
+        }
+        float y[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) y[e] = silu(rbf(acc[e]));
+        const Pack8 o = pack8(y);
+        if (c < key_packs)
+            st8(q + (size_t)t * key_packs * 8 + (size_t)c * 8, o);
+        else if (c < 2 * key_packs)
+            st8(k + (size_t)t * key_packs * 8 + (size_t)(c - key_packs) * 8, o);
+        else
+            st8(v + (size_t)t * value_packs * 8 + (size_t)(c - 2 * key_packs) * 8, o);
+    }
+}
+
+__global__ void conv_scalar_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld,
+                                   const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
+                                   bf16* __restrict__ v, int key_dim, int value_dim, SeqTable tab) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int channels = 2 * key_dim + value_dim;
+    if (c >= channels) return;
+    const int T = tab.offset[tab.count];
+    for (int t = blockIdx.y; t < T; t += gridDim.y) {
+        const int s = seq_of(tab, t);
+        const int pos = t - tab.offset[s];
+        float acc = 0.f;
+        for (int j = 0; j < 4; j++) {
+            const int back = 3 - j;
+            float x = 0.f;
+            if (pos >= back)
+                x = f32(qkv[(size_t)(t - back) * ld + c]);
+            else if (history)
+                x = f32(history[(size_t)(3 - back + pos) * ld + c]);
+            acc = fmaf(f32(w[c * 4 + j]), x, acc);
+        }
+        const bf16 y = to_bf16(silu(rbf(acc)));
+        if (c < key_dim)
+            q[(size_t)t * key_dim + c] = y;
+        else if (c < 2 * key_dim)
+            k[(size_t)t * key_dim + c - key_dim] = y;
+        else
+            v[(size_t)t * value_dim + c - 2 * key_dim] = y;
+    }
+}
+
+__global__ void gates_kernel(const bf16* __restrict__ b, const bf16* __restrict__ a, int ld,
+                             const bf16* __restrict__ A_log, const bf16* __restrict__ dt_bias,
+                             bf16* __restrict__ beta, float* __restrict__ g, long n, int H) {
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const int h = (int)(i % H);
+        const size_t src = (size_t)(i / H) * ld + h;
+        beta[i] = to_bf16(sigmoid(f32(b[src])));
+        const float x = f32(a[src]) + f32(dt_bias[h]);
+        const float sp = x > 20.f ? x : log1pf(expf(x));
+        g[i] = -expf(f32(A_log[h])) * sp;
+    }
+}
+
+__global__ void sigmoid_gate_kernel(bf16* __restrict__ x, const bf16* __restrict__ gate, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        x[i] = to_bf16(f32(x[i]) * rbf(sigmoid(f32(gate[i]))));
+}
+
+__global__ void silu_mul_vec_kernel(const bf16* __restrict__ gu, int ld, bf16* __restrict__ out, int I, long T) {
+    const int packs = I / 8;
+    const long n = T * packs;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long t = i / packs;
+        const int j = (int)(i % packs) * 8;
+        float g[8], u[8], o[8];
+        unpack8(ld8(gu + t * ld + j), g);
+        unpack8(ld8(gu + t * ld + I + j), u);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o[e] = rbf(silu(g[e])) * u[e];
+        st8(out + t * I + j, pack8(o));
+    }
+}
+
+__global__ void silu_mul_scalar_kernel(const bf16* __restrict__ gu, int ld, bf16* __restrict__ out, int I, long T) {
+    const long n = T * I;
+    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+        const long t = i / I;
+        const int j = (int)(i % I);
+        out[i] = to_bf16(rbf(silu(f32(gu[t * ld + j]))) * f32(gu[t * ld + I + j]));
+    }
+}
+
+__global__ void finite_kernel(const uint16_t* __restrict__ x, size_t n, uint32_t* flag) {
+    bool bad = false;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        bad |= (x[i] & 0x7f80u) == 0x7f80u;
+    if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicExch(flag, 1u);
+}
+
+unsigned grid_for(size_t n) {
+    const size_t b = (n + THREADS - 1) / THREADS;
+    return (unsigned)(b < 148 * 32 ? (b ? b : 1) : 148 * 32);
+}
+
+int conv_launch(const void* qkv, const void* history, int ld, const void* w, void* q, void* k, void* v,
+                const SeqTable& tab, int key_dim, int value_dim, cudaStream_t st) {
+    const int T = tab.offset[tab.count];
+    const int rows = T < 65535 ? T : 65535;
+    const bool vec = key_dim % 8 == 0 && value_dim % 8 == 0 && ld % 8 == 0 && aligned16(qkv) && aligned16(w) &&
+                     aligned16(q) && aligned16(k) && aligned16(v) && (!history || aligned16(history));
+    if (vec) {
+        const int packs = (2 * key_dim + value_dim) / 8;
+        conv_vec_kernel<<<dim3((packs + 127) / 128, rows), 128, 0, st>>>(
+            static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld, static_cast<const bf16*>(w),
+            static_cast<bf16*>(q), static_cast<bf16*>(k), static_cast<bf16*>(v), key_dim / 8, value_dim / 8, tab);
+    } else {
+        const int ch = 2 * key_dim + value_dim;
+        conv_scalar_kernel<<<dim3((ch + 127) / 128, rows), 128, 0, st>>>(
+            static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld, static_cast<const bf16*>(w),
+            static_cast<bf16*>(q), static_cast<bf16*>(k), static_cast<bf16*>(v), key_dim, value_dim, tab);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace s1
+
+using namespace s1;
+
+extern "C" int cs1_embed(const int32_t* ids, const void* table, void* out, int T, int D, void* stream) {
+    if (D <= 0 || D % 8 != 0 || T < 0) return cudaErrorInvalidValue;
+    if (T == 0) return cudaSuccess;
+    if (!aligned16(table) || !aligned16(out)) return cudaErrorInvalidValue;
+    const int grid = T < 65535 ? T : 65535;
+    embed_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(ids, static_cast<const Pack8*>(table),
+                                                                      static_cast<Pack8*>(out), D / 8, T);
+    return cudaGetLastError();
+}
+
+extern "C" int cs1_gdn_conv(const void* qkv, int ld, const void* w, void* q, void* k, void* v, int T, int key_dim,
+                            int value_dim, void* stream) {
+    if (T < 0 || key_dim < 0 || value_dim < 0 || ld < 2 * key_dim + value_dim) return cudaErrorInvalidValue;
+    if (T == 0 || 2 * key_dim + value_dim == 0) return cudaSuccess;
+    SeqTable tab;
+    const size_t len = (size_t)T;
+    make_table(tab, &len, 1);
+    return conv_launch(qkv, nullptr, ld, w, q, k, v, tab, key_dim, value_dim, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cs1_gdn_conv_vector(const void* qkv, int ld, const void* w, void* q, void* k, void* v, int T,
+                                   int key_dim, int value_dim, void* stream) {
+    return cs1_gdn_conv(qkv, ld, w, q, k, v, T, key_dim, value_dim, stream);
+}
+
+extern "C" int cs1_gdn_conv_prefix(const void* qkv, const void* history, int ld, const void* w, void* q, void* k,
+                                   void* v, int T, int key_dim, int value_dim, void* stream) {
+    if (!qkv || !history || !w || !q || !k || !v || T <= 0 || key_dim <= 0 || value_dim <= 0 ||
+        ld < 2 * key_dim + value_dim)
+        return cudaErrorInvalidValue;
+    SeqTable tab;
+    const size_t len = (size_t)T;
+    make_table(tab, &len, 1);
+    return conv_launch(qkv, history, ld, w, q, k, v, tab, key_dim, value_dim, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cs1_gdn_conv_batch(const void* qkv, const void* history, int ld, const void* w, void* q, void* k,
+                                  void* v, const size_t* lengths, size_t count, int key_dim, int value_dim,
+                                  void* stream) {
+    SeqTable tab;
+    if (!qkv || !w || !q || !k || !v || key_dim <= 0 || value_dim <= 0 || ld < 2 * key_dim + value_dim ||
+        !make_table(tab, lengths, count))
+        return cudaErrorInvalidValue;
+    return conv_launch(qkv, history, ld, w, q, k, v, tab, key_dim, value_dim, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cs1_gdn_gates(const void* b, const void* a, int ld, const void* A_log, const void* dt_bias,
+                             void* beta, float* g, int T, int H, void* stream) {
+    if (T < 0 || H < 0 || ld < H) return cudaErrorInvalidValue;
+    const long n = (long)T * H;
+    if (n == 0) return cudaSuccess;
+    gates_kernel<<<grid_for(n), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const bf16*>(b), static_cast<const bf16*>(a), ld, static_cast<const bf16*>(A_log),
+        static_cast<const bf16*>(dt_bias), static_cast<bf16*>(beta), g, n, H);
+    return cudaGetLastError();
+}
+
+extern "C" int cs1_sigmoid_gate(void* x, const void* gate, size_t n, void* stream) {
+    if (n == 0) return cudaSuccess;
+    sigmoid_gate_kernel<<<grid_for(n), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<bf16*>(x), static_cast<const bf16*>(gate), n);
+    return cudaGetLastError();
+}
+
+extern "C" int cs1_silu_mul(const void* gate_up, int ld, void* out, int T, int I, void* stream) {
+    if (T < 0 || I < 0 || ld < 2 * I) return cudaErrorInvalidValue;
+    const long n = (long)T * I;
+    if (n == 0) return cudaSuccess;
+    auto st = static_cast<cudaStream_t>(stream);
+    if (I % 8 == 0 && ld % 8 == 0 && aligned16(gate_up) && aligned16(out))
+        silu_mul_vec_kernel<<<grid_for(n / 8), THREADS, 0, st>>>(static_cast<const bf16*>(gate_up), ld,
+                                                                  static_cast<bf16*>(out), I, T);
+    else
+        silu_mul_scalar_kernel<<<grid_for(n), THREADS, 0, st>>>(static_cast<const bf16*>(gate_up), ld,
+                                                                 static_cast<bf16*>(out), I, T);
+    return cudaGetLastError();
+}
+
+extern "C" int cs1_bf16_finite(const void* x, size_t n, uint32_t* flag, void* stream) {
+    auto st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(uint32_t), st);
+    if (e != cudaSuccess) return e;
+    if (n) finite_kernel<<<grid_for(n), THREADS, 0, st>>>(static_cast<const uint16_t*>(x), n, flag);
+    return cudaGetLastError();
+}
+
+// ---- counter-based random fill (weights for benchmarks; not a Transformers init) ----
+namespace s1 {
+namespace {
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__device__ __forceinline__ float unit(uint64_t bits) { return ((bits >> 40) + 0.5f) * (1.0f / 16777216.0f); }
+
+// kind 0: a + b * N(0,1) (Box-Muller); 1: U(a, b); 2: log U(a, b). dtype 0 bf16, 1 f32.
+__global__ void fill_kernel(void* dst, size_t n, int kind, uint64_t seed, float a, float b, int dtype) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t r1 = mix64(seed ^ mix64(2 * i)), r2 = mix64(seed ^ mix64(2 * i + 1));
+        float x;
+        if (kind == 0) {
+            const float u1 = unit(r1), u2 = unit(r2);
+            x = a + b * sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+        } else {
+            x = a + (b - a) * unit(r1);
+            if (kind == 2) x = logf(x);
+        }
+        if (dtype == 0) static_cast<bf16*>(dst)[i] = to_bf16(x);
+        else static_cast<float*>(dst)[i] = x;
+    }
+}
+
+}  // namespace
+}  // namespace s1
+
+extern "C" int cs1_fill_random(void* dst, size_t n, int kind, uint64_t seed, float a, float b, int dtype,
+                               void* stream) {
+    if (!dst || kind < 0 || kind > 2 || dtype < 0 || dtype > 1) return cudaErrorInvalidValue;
+    if (n == 0) return cudaSuccess;
+    s1::fill_kernel<<<s1::grid_for(n), s1::THREADS, 0, static_cast<cudaStream_t>(stream)>>>(dst, n, kind, seed, a, b,
+                                                                                        dtype);
+    return cudaGetLastError();
+}

@@ -1,0 +1,789 @@
+// Chunked Gated DeltaNet prefill (chunks of 64 tokens, K = V = 128 per head).
+//
+// Recurrence, per value head h (key head h / (H / HK)), q and k L2-normalised, q scaled:
+//   S_t = e^{g_t} S_{t-1} + k_t (beta_t (v_t - e^{g_t} S_{t-1}^T k_t))^T,   o_t = S_t^T q_t
+// in the chunk (WY / UT-transform) form of Transformers' torch_chunk_gated_delta_rule:
+//   per chunk: cum = cumsum(g); A_ij = beta_i k_i.k_j e^{cum_i - cum_j} (j < i); T = (I + A)^-1
+//              u = T diag(beta) v;  w = T diag(beta) (k e^cum);  qd = q e^cum;  kd = k e^{last - cum}
+//              P_ij = q_i.k_j e^{cum_i - cum_j} (j <= i)
+//   scan:      v_new = u - w S;  o = qd S + P v_new;  S = e^{last} S + kd^T v_new
+//
+// Two kernels:
+//  1. gdn_prep (parallel over chunk x head x sequence): everything that does not
+//     depend on the state, written to the workspace in the layouts the scan's
+//     tensor-core operands want (w and qd [64 t][128 k], P [64 t][64 j], kd^T
+//     [128 k][64 t], u^T [128 v][64 t]) as bfloat16, plus e^{last} per chunk.
+//  2. gdn_scan (one CTA per head x sequence, serial over chunks) on tcgen05:
+//     the state is kept transposed, S^T [v][k], so that TMEM lane = value column v
+//     and every contraction is an M = 128, K-major MMA:
+//        (wS)^T  [v][t] = S^T w^T           (qd S)^T [v][t] = S^T qd^T
+//        (P v_new)^T [v][t] += v_new^T P^T   (kd^T v_new)^T [v][k] = v_new^T kd
+//     Thread v holds row v of S^T in fp32 registers across chunks, writes its bf16
+//     copy to shared memory as the MMA operand, forms v_new = bf16(u - wS) from
+//     TMEM, and applies S = e^{last} S + update. w, qd, P, kd^T arrive by TMA,
+//     double-buffered one chunk ahead.
+// Rounding points follow the reference kernel (gdn_prefill.cu:1-15 of the reference):
+// u, w, qd, kd, P, the per-chunk state copy and v_new in bfloat16, state and
+// accumulations in fp32.
+//
+// The FP32 operator (cs1_gdn_prefill_fp32, gdn_fp32.cu) shares the prep kernel
+// with float32 outputs and runs its own float32 scan.
+#include <algorithm>
+#include <climits>
+#include <cmath>
+#include <new>
+#include <type_traits>
+
+#include "common.cuh"
+#include "gdn.cuh"
+#include "ops_internal.h"
+#include "tc.cuh"
+
+S1_FAULT_WORD(gdn)
+
+namespace s1 {
+namespace gdn {
+
+using namespace s1::tc;
+
+bool make_gdn_table(GdnTable& g, const SeqTable& t) {
+    g.seq = t;
+    int slots = 0;
+    for (int i = 0; i < t.count; i++) {
+        g.chunk_base[i] = slots;
+        const int len = t.offset[i + 1] - t.offset[i];
+        slots += (len + C - 1) / C;
+    }
+    g.chunk_base[t.count] = slots;
+    g.max_chunks = (t.max_len + C - 1) / C;
+    return true;
+}
+
+Layout::Layout(long slots, int H, bool f32) {
+    const long e = f32 ? 4 : 2;
+    const long n = (long)H * slots;
+    long at = 0;
+    auto take = [&](long bytes) {
+        const long off = at;
+        at = (at + bytes + 1023) / 1024 * 1024;
+        return off;
+    };
+    w = take(n * C * K * e);
+    qd = take(n * C * K * e);
+    p = take(n * C * C * e);
+    kdt = take(n * K * C * e);
+    ut = take(n * V * C * e);
+    decay = take(n * 4);
+    total = at;
+}
+
+// ---------------------------------------------------------------- prep ----
+// 256 threads; shared: kn, qn fp32 [64][129]; A/T fp32 [64][65] x 2; tb fp32 [64][65];
+// staged bf16-rounded k e^cum and v as fp32 [64][129].
+constexpr int PREP_THREADS = 256;
+constexpr int LDK = K + 1;
+constexpr int LDC = C + 1;
+constexpr int PREP_SMEM = (3 * C * LDK + 3 * C * LDC + 5 * C) * 4;
+
+template <bool F32>
+__global__ void __launch_bounds__(PREP_THREADS) gdn_prep(const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                          const bf16* __restrict__ v, const float* __restrict__ g,
+                                                          const bf16* __restrict__ beta, Work ws, GdnTable tab,
+                                                          int H, int HK, float scale) {
+    using OutT = typename std::conditional<F32, float, bf16>::type;
+    const int seq = blockIdx.z;
+    const int start = tab.seq.offset[seq];
+    const int len = tab.seq.offset[seq + 1] - start;
+    const int c = blockIdx.x;
+    if (c * C >= len) return;
+    const int h = blockIdx.y, hk = h / (H / HK);
+    const long slot = (long)h * ws.slots + tab.chunk_base[seq] + c;
+    const int t0 = start + c * C;
+    const int n = min(C, len - c * C);
+
+    extern __shared__ float sm[];
+    float* kn = sm;                 // [C][LDK] normalised k
+    float* qn = kn + C * LDK;       // [C][LDK] normalised, scaled q
+    float* st = qn + C * LDK;       // [C][LDK] staging: bf16(k e^cum) then v
+    float* A = st + C * LDK;        // [C][LDC]
+    float* Tm = A + C * LDC;        // [C][LDC]
+    float* tb = Tm + C * LDC;       // [C][LDC]  T diag(beta) (bf16-rounded unless F32)
+    float* cum = tb + C * LDC;      // [C]
+    float* bet = cum + C;
+    float* ecum = bet + C;
+    float* erem = ecum + C;
+    float* gg = erem + C;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    if (tid < C) {
+        gg[tid] = tid < n ? g[(size_t)(t0 + tid) * H + h] : 0.f;
+        bet[tid] = tid < n ? f32(beta[(size_t)(t0 + tid) * H + h]) : 0.f;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float s = 0.f;
+        for (int i = 0; i < C; i++) {
+            s += gg[i];
+            cum[i] = s;
+        }
+        ws.decay[slot] = expf(s);
+    }
+    __syncthreads();
+    if (tid < C) {
+        ecum[tid] = expf(cum[tid]);
+        erem[tid] = expf(cum[C - 1] - cum[tid]);
+    }
+    // L2 norms: one warp per row, lane covers 4 dims.
+    for (int r = warp; r < C; r += PREP_THREADS / 32) {
+        float kx[4], qx[4], ks = 0.f, qs = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int d = lane + 32 * e;
+            kx[e] = r < n ? f32(k[((size_t)(t0 + r) * HK + hk) * K + d]) : 0.f;
+            qx[e] = r < n ? f32(q[((size_t)(t0 + r) * HK + hk) * K + d]) : 0.f;
+            ks = fmaf(kx[e], kx[e], ks);
+            qs = fmaf(qx[e], qx[e], qs);
+        }
+        ks = warp_sum(ks);
+        qs = warp_sum(qs);
+        const float kinv = rsqrtf(ks + 1e-6f), qinv = rsqrtf(qs + 1e-6f) * scale;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int d = lane + 32 * e;
+            kn[r * LDK + d] = kx[e] * kinv;
+            qn[r * LDK + d] = qx[e] * qinv;
+        }
+    }
+    __syncthreads();
+
+    // Pair products: A (strictly lower, with beta_i and the decay) and P (lower incl. diagonal).
+    OutT* P = reinterpret_cast<OutT*>(ws.p) + slot * C * C;
+    for (int x = tid; x < C * C; x += PREP_THREADS) {
+        const int i = x / C, j = x % C;
+        float a = 0.f, p = 0.f;
+        if (j <= i) {
+            const float* ki = kn + i * LDK;
+            const float* qi = qn + i * LDK;
+            const float* kj = kn + j * LDK;
+            float dk = 0.f, dq = 0.f;
+#pragma unroll 8
+            for (int d = 0; d < K; d++) {
+                dk = fmaf(ki[d], kj[d], dk);
+                dq = fmaf(qi[d], kj[d], dq);
+            }
+            const float dec = expf(cum[i] - cum[j]);
+            if (j < i) a = bet[i] * dk * dec;
+            p = dq * dec;
+        }
+        A[i * LDC + j] = a;
+        if constexpr (F32) P[x] = p; else P[x] = to_bf16(p);
+    }
+    __syncthreads();
+
+    // T = (I + A)^-1 by forward substitution, one column per thread.
+    if (tid < C) {
+        const int j = tid;
+        for (int r = 0; r < C; r++) {
+            float acc = r == j ? 1.f : 0.f;
+            for (int m = j; m < r; m++) acc = fmaf(-A[r * LDC + m], Tm[m * LDC + j], acc);
+            Tm[r * LDC + j] = r < j ? 0.f : acc;
+        }
+    }
+    __syncthreads();
+    for (int x = tid; x < C * C; x += PREP_THREADS) {
+        const int i = x / C, j = x % C;
+        const float val = Tm[i * LDC + j] * bet[j];
+        tb[i * LDC + j] = F32 ? val : rbf(val);
+    }
+    // k e^cum staged (bf16-rounded unless F32)
+    for (int x = tid; x < C * K; x += PREP_THREADS) {
+        const int j = x / K, d = x % K;
+        const float val = kn[j * LDK + d] * ecum[j];
+        st[j * LDK + d] = F32 ? val : rbf(val);
+    }
+    __syncthreads();
+
+    // w[t][d] = sum_j tb[t][j] kw[j][d]; thread: d = tid % 128, rows t = tid/128 + 2i
+    OutT* W = reinterpret_cast<OutT*>(ws.w) + slot * C * K;
+    {
+        const int d = tid & 127, tg = tid >> 7;
+        for (int t = tg; t < C; t += 2) {
+            float acc = 0.f;
+            for (int j = 0; j <= t; j++) acc = fmaf(tb[t * LDC + j], st[j * LDK + d], acc);
+            if constexpr (F32) W[t * K + d] = acc; else W[t * K + d] = to_bf16(acc);
+        }
+    }
+    // qd[t][d] and kd^T[d][t]
+    OutT* QD = reinterpret_cast<OutT*>(ws.qd) + slot * C * K;
+    OutT* KDT = reinterpret_cast<OutT*>(ws.kdt) + slot * K * C;
+    for (int x = tid; x < C * K; x += PREP_THREADS) {
+        const int t = x / K, d = x % K;
+        const float a = qn[t * LDK + d] * ecum[t];
+        if constexpr (F32) QD[x] = a; else QD[x] = to_bf16(a);
+        const int d2 = x / C, t2 = x % C;
+        const float b = kn[t2 * LDK + d2] * erem[t2];
+        if constexpr (F32) KDT[x] = b; else KDT[x] = to_bf16(b);
+    }
+    __syncthreads();
+    // v staged, then u^T[v][t] = sum_j tb[t][j] v[j][v]
+    for (int x = tid; x < C * V; x += PREP_THREADS) {
+        const int j = x / V, d = x % V;
+        st[j * LDK + d] = j < n ? f32(v[((size_t)(t0 + j) * H + h) * V + d]) : 0.f;
+    }
+    __syncthreads();
+    OutT* UT = reinterpret_cast<OutT*>(ws.ut) + slot * V * C;
+    {
+        const int d = tid & 127, tg = tid >> 7;
+        for (int t = tg; t < C; t += 2) {
+            float acc = 0.f;
+            for (int j = 0; j <= t; j++) acc = fmaf(tb[t * LDC + j], st[j * LDK + d], acc);
+            if constexpr (F32) UT[d * C + t] = acc; else UT[d * C + t] = to_bf16(acc);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- scan ----
+// 160 threads: warps 0..3 own TMEM lanes / value columns 0..127, warp 4 lane 0
+// issues TMA and MMA. Shared memory (1024-aligned tiles, 128B swizzle):
+//   ST   S^T bf16 [128 v][128 k]  as two [128][64] sub-tiles      32 KB
+//   VN   v_new^T bf16 [128 v][64 t]                                16 KB
+//   per buffer b (2): W [64][128] (2 sub-tiles), QD (2), P [64][64], KDT [128][64]   56 KB each
+constexpr int SCAN_THREADS = 160;
+constexpr int SUB64 = 64 * 128;        // bytes of a [64 rows][64 bf16] tile
+constexpr int SUB128 = 128 * 128;      // bytes of a [128 rows][64 bf16] tile
+constexpr int OFF_ST = 0;
+constexpr int OFF_VN = OFF_ST + 2 * SUB128;
+constexpr int OFF_BUF = OFF_VN + SUB128;
+constexpr int BUF_W = 0, BUF_QD = 2 * SUB64, BUF_P = 4 * SUB64, BUF_KDT = 5 * SUB64;
+constexpr int BUF_BYTES = 5 * SUB64 + SUB128;
+constexpr int OFF_BAR = OFF_BUF + 2 * BUF_BYTES;
+constexpr int SCAN_SMEM = OFF_BAR + 128 + 1024;
+constexpr uint32_t TX_BYTES = BUF_BYTES;
+
+struct ScanMaps {
+    CUtensorMap w, qd, p, kdt;
+};
+
+__global__ void __launch_bounds__(SCAN_THREADS, 1)
+    gdn_scan(const __grid_constant__ ScanMaps maps, Work ws, GdnTable tab, bf16* __restrict__ o, int H,
+             const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + OFF_BAR;
+    auto full = [&](int b) { return bars + 8u * b; };          // TMA landed, count 1 + tx
+    auto empty = [&](int b) { return bars + 8u * (2 + b); };   // MMAs done with buffer b
+    const uint32_t s_ready = bars + 32, ws_done = bars + 40, vn_ready = bars + 48, upd_done = bars + 56;
+    const uint32_t drain = bars + 64;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 72);
+
+    const int h = blockIdx.x, seq = blockIdx.y;
+    const int start = tab.seq.offset[seq];
+    const int len = tab.seq.offset[seq + 1] - start;
+    const int NC = (len + C - 1) / C;
+    const long slot0 = (long)h * ws.slots + tab.chunk_base[seq];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        mbar_init(full(0), 1);
+        mbar_init(full(1), 1);
+        mbar_init(empty(0), 1);
+        mbar_init(empty(1), 1);
+        mbar_init(s_ready, 128);
+        mbar_init(ws_done, 1);
+        mbar_init(vn_ready, 128);
+        mbar_init(upd_done, 1);
+        mbar_init(drain, 1);
+        mbar_fence_init();
+    }
+    if (warp == 4) {
+        tmem_alloc(smem_u32(tmem_slot), 256);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // TMEM columns: [0,64) (wS)^T, [64,128) o^T, [128,256) S^T update
+
+    if (warp == 4) {
+        if (lane == 0) {
+            constexpr uint32_t ID64 = idesc(128, 64, AB_BF16);
+            constexpr uint32_t ID128 = idesc(128, 128, AB_BF16);
+            auto issue_load = [&](int c) {
+                const int b = c & 1;
+                const uint32_t dst = base + OFF_BUF + b * BUF_BYTES;
+                const int row = (int)((slot0 + c) * C);
+                mbar_expect_tx(full(b), TX_BYTES);
+                tma_load_2d(dst + BUF_W, &maps.w, full(b), 0, row);
+                tma_load_2d(dst + BUF_W + SUB64, &maps.w, full(b), 64, row);
+                tma_load_2d(dst + BUF_QD, &maps.qd, full(b), 0, row);
+                tma_load_2d(dst + BUF_QD + SUB64, &maps.qd, full(b), 64, row);
+                tma_load_2d(dst + BUF_P, &maps.p, full(b), 0, row);
+                tma_load_2d(dst + BUF_KDT, &maps.kdt, full(b), 0, (int)((slot0 + c) * K));
+            };
+            int issued = 0;
+            if (NC > 0) issue_load(0), issued++;
+            if (NC > 1) issue_load(1), issued++;
+            bool ok = true;
+            for (int c = 0; c < NC && ok; c++) {
+                const int b = c & 1;
+                const uint32_t ph = (uint32_t)(c >> 1) & 1u;
+                const uint32_t cp = (uint32_t)c & 1u;
+                if (!mbar_wait(full(b), ph) || !mbar_wait(s_ready, cp)) {
+                    atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t buf = base + OFF_BUF + b * BUF_BYTES;
+                // (wS)^T -> cols [0,64), (qd S)^T -> cols [64,128); K = 128 over two sub-tiles
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t sub = (uint32_t)(kk >> 2), off = (uint32_t)(kk & 3) * 32;
+                    const uint64_t a = desc_sw128(base + OFF_ST + sub * SUB128 + off);
+                    mma_bf16(tmem + 0, a, desc_sw128(buf + BUF_W + sub * SUB64 + off), ID64, kk > 0);
+                    mma_bf16(tmem + 64, a, desc_sw128(buf + BUF_QD + sub * SUB64 + off), ID64, kk > 0);
+                }
+                mma_commit(ws_done);
+                if (!mbar_wait(vn_ready, cp)) {
+                    atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                    break;
+                }
+                tc_fence_after();
+                // o^T += v_new^T P^T ; S^T update = v_new^T kd  (K = 64 tokens)
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint32_t off = (uint32_t)kk * 32;
+                    const uint64_t a = desc_sw128(base + OFF_VN + off);
+                    mma_bf16(tmem + 64, a, desc_sw128(buf + BUF_P + off), ID64, 1);
+                    mma_bf16(tmem + 128, a, desc_sw128(buf + BUF_KDT + off), ID128, kk > 0);
+                }
+                mma_commit(upd_done);
+                mma_commit(empty(b));
+                if (c + 2 < NC) {
+                    if (!mbar_wait(empty(b), ph)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    issue_load(c + 2);
+                    issued++;
+                }
+            }
+            mma_commit(drain);
+            (void)mbar_wait(drain, 0);
+            // Every TMA load issued has landed before exit (already true on success).
+            for (int c = std::max(0, issued - 2); c < issued; c++) (void)mbar_wait(full(c & 1), (uint32_t)(c >> 1) & 1u);
+        }
+    } else {
+        // Thread v = threadIdx.x owns TMEM lane v and row v of S^T.
+        const int vcol = threadIdx.x;
+        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+        float S[K];
+        if (s_in) {
+            const float* si = s_in + (long)seq * s_in_stride + (size_t)h * K * V;
+#pragma unroll
+            for (int kk = 0; kk < K; kk++) S[kk] = si[(size_t)kk * V + vcol];
+        } else {
+#pragma unroll
+            for (int kk = 0; kk < K; kk++) S[kk] = 0.f;
+        }
+        const bf16* UT = reinterpret_cast<const bf16*>(ws.ut);
+        uint8_t* st_tile = smem + OFF_ST;
+        uint8_t* vn_tile = smem + OFF_VN;
+        for (int c = 0; c < NC; c++) {
+            const uint32_t cp = (uint32_t)c & 1u;
+            // u^T row for this chunk (prefetched before the MMAs need it)
+            float u[C];
+            {
+                const bf16* ur = UT + ((slot0 + c) * V + vcol) * C;
+#pragma unroll
+                for (int i = 0; i < C / 8; i++) unpack8(ld8(ur + i * 8), u + i * 8);
+            }
+            // S^T row v as bf16 into the swizzled operand tile
+#pragma unroll
+            for (int ch = 0; ch < 16; ch++) {
+                const int sub = ch >> 3;
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) f[e] = S[ch * 8 + e];
+                *reinterpret_cast<Pack8*>(st_tile + sub * SUB128 + sw128_offset(vcol, ch & 7)) = pack8(f);
+            }
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(s_ready);
+            if (!mbar_wait(ws_done, cp)) {
+                atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            // v_new = bf16(u - wS)
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                float ws_[32];
+                tmem_ld32(lane_addr + half * 32, ws_);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) f[e] = u[half * 32 + i * 8 + e] - ws_[i * 8 + e];
+                    *reinterpret_cast<Pack8*>(vn_tile + sw128_offset(vcol, half * 4 + i)) = pack8(f);
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(vn_ready);
+            if (!mbar_wait(upd_done, cp)) {
+                atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            // o rows of this chunk, column v
+            const int rows = min(C, len - c * C);
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                float ov[32];
+                tmem_ld32(lane_addr + 64 + half * 32, ov);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++) {
+                    const int t = half * 32 + i;
+                    if (t < rows) o[((size_t)(start + c * C + t) * H + h) * V + vcol] = to_bf16(ov[i]);
+                }
+            }
+            // S = e^{last} S + update
+            const float dec = ws.decay[slot0 + c];
+#pragma unroll
+            for (int q4 = 0; q4 < 4; q4++) {
+                float up[32];
+                tmem_ld32(lane_addr + 128 + q4 * 32, up);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++) S[q4 * 32 + i] = fmaf(S[q4 * 32 + i], dec, up[i]);
+            }
+            tc_fence_before();
+        }
+        if (s_out) {
+            float* so = s_out + (long)seq * (long)H * K * V + (size_t)h * K * V;
+#pragma unroll
+            for (int kk = 0; kk < K; kk++) so[(size_t)kk * V + vcol] = S[kk];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
+// Zero-token sequences never reach the kernels; s_out for an empty call is a copy.
+int run(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o, void* workspace,
+        size_t workspace_bytes, const SeqTable& seqs, int H, int HK, float scale, const void* s_in,
+        long s_in_stride, void* s_out, cudaStream_t st) {
+    if (!q || !k || !v || !g || !beta || !o || !workspace || H <= 0 || HK <= 0 || H % HK) return cudaErrorInvalidValue;
+    GdnTable tab;
+    make_gdn_table(tab, seqs);
+    const long slots = tab.chunk_base[seqs.count];
+    const Layout L(slots, H, false);
+    if ((size_t)L.total > workspace_bytes) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 1023) != 0) return cudaErrorInvalidValue;
+    static const cudaError_t configured = [] {
+        cudaError_t e = cudaFuncSetAttribute(gdn_prep<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gdn_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM);
+        return e;
+    }();
+    if (configured != cudaSuccess) return configured;
+    uint8_t* b = static_cast<uint8_t*>(workspace);
+    Work ws{b + L.w, b + L.qd, b + L.p, b + L.kdt, b + L.ut, reinterpret_cast<float*>(b + L.decay), slots};
+    gdn_prep<false><<<dim3(tab.max_chunks, H, seqs.count), PREP_THREADS, PREP_SMEM, st>>>(
+        static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), g,
+        static_cast<const bf16*>(beta), ws, tab, H, HK, scale);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    ScanMaps maps;
+    const uint64_t rows64 = (uint64_t)H * slots * C, rows128 = (uint64_t)H * slots * K;
+    int r = host::make_map_2d(&maps.w, ws.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, K, K, 64, 64,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!r) r = host::make_map_2d(&maps.qd, ws.qd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, K, K, 64, 64,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!r) r = host::make_map_2d(&maps.p, ws.p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, C, C, 64, 64,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!r) r = host::make_map_2d(&maps.kdt, ws.kdt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows128, C, C, 128, 64,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+    if (r) return r;
+    gdn_scan<<<dim3(H, seqs.count), SCAN_THREADS, SCAN_SMEM, st>>>(maps, ws, tab, static_cast<bf16*>(o), H,
+                                                                   static_cast<const float*>(s_in), s_in_stride,
+                                                                   static_cast<float*>(s_out));
+    return cudaGetLastError();
+}
+
+size_t workspace_bytes_for(long slots, int H, bool f32) { return (size_t)Layout(slots, H, f32).total + 1024; }
+
+// ------------------------------------------------------------ FP32 scan ----
+// The FP32 operator: same prep with float32 outputs, then a float32 CUDA-core scan.
+// One CTA per (head, sequence, 32 value columns); S [128 k][32 v] in shared memory.
+constexpr int F32_THREADS = 256;
+constexpr int F32_VB = 32;
+constexpr int F32_SMEM = (C * K * 2 + C * C + K * C + F32_VB * C + K * F32_VB + C * F32_VB) * 4;
+
+template <typename OutT>
+__global__ void __launch_bounds__(F32_THREADS) gdn_scan_f32(Work ws, GdnTable tab, OutT* __restrict__ o, int H,
+                                                            const float* __restrict__ s_in, long s_in_stride,
+                                                            float* __restrict__ s_out) {
+    extern __shared__ float fs[];
+    float* w = fs;                  // [64][128]
+    float* qd = w + C * K;          // [64][128]
+    float* P = qd + C * K;          // [64][64]
+    float* kdt = P + C * C;         // [128][64]
+    float* ut = kdt + K * C;        // [32 v][64 t]
+    float* S = ut + F32_VB * C;     // [128 k][32 v]
+    float* vn = S + K * F32_VB;     // [64 t][32 v]
+    const int h = blockIdx.x, seq = blockIdx.y, v0 = blockIdx.z * F32_VB;
+    const int start = tab.seq.offset[seq];
+    const int len = tab.seq.offset[seq + 1] - start;
+    const int NC = (len + C - 1) / C;
+    const long slot0 = (long)h * ws.slots + tab.chunk_base[seq];
+    const int tid = threadIdx.x;
+    for (int x = tid; x < K * F32_VB; x += F32_THREADS) {
+        const int kk = x / F32_VB, vv = x % F32_VB;
+        S[x] = s_in ? s_in[(long)seq * s_in_stride + ((size_t)h * K + kk) * V + v0 + vv] : 0.f;
+    }
+    const float* Wg = static_cast<const float*>(ws.w);
+    const float* Qg = static_cast<const float*>(ws.qd);
+    const float* Pg = static_cast<const float*>(ws.p);
+    const float* Kg = static_cast<const float*>(ws.kdt);
+    const float* Ug = static_cast<const float*>(ws.ut);
+    for (int c = 0; c < NC; c++) {
+        const long slot = slot0 + c;
+        __syncthreads();
+        for (int x = tid; x < C * K; x += F32_THREADS) {
+            w[x] = Wg[slot * C * K + x];
+            qd[x] = Qg[slot * C * K + x];
+            kdt[x] = Kg[slot * K * C + x];
+        }
+        for (int x = tid; x < C * C; x += F32_THREADS) P[x] = Pg[slot * C * C + x];
+        for (int x = tid; x < F32_VB * C; x += F32_THREADS) ut[x] = Ug[(slot * V + v0) * C + x];
+        __syncthreads();
+        // v_new[t][v] = u[t][v] - sum_k w[t][k] S[k][v]
+        for (int x = tid; x < C * F32_VB; x += F32_THREADS) {
+            const int t = x / F32_VB, vv = x % F32_VB;
+            float acc = 0.f;
+            for (int kk = 0; kk < K; kk++) acc = fmaf(w[t * K + kk], S[kk * F32_VB + vv], acc);
+            vn[x] = ut[vv * C + t] - acc;
+        }
+        __syncthreads();
+        // o[t][v] = sum_k qd[t][k] S[k][v] + sum_j P[t][j] v_new[j][v]
+        const int rows = min(C, len - c * C);
+        for (int x = tid; x < C * F32_VB; x += F32_THREADS) {
+            const int t = x / F32_VB, vv = x % F32_VB;
+            float a = 0.f, b = 0.f;
+            for (int kk = 0; kk < K; kk++) a = fmaf(qd[t * K + kk], S[kk * F32_VB + vv], a);
+            for (int j = 0; j <= t; j++) b = fmaf(P[t * C + j], vn[j * F32_VB + vv], b);
+            if (t < rows) {
+                const float val = a + b;
+                OutT* dst = o + ((size_t)(start + c * C + t) * H + h) * V + v0 + vv;
+                if constexpr (sizeof(OutT) == 4) *dst = val; else *dst = to_bf16(val);
+            }
+        }
+        __syncthreads();
+        // S = e^{last} S + kd^T v_new
+        const float dec = ws.decay[slot];
+        for (int x = tid; x < K * F32_VB; x += F32_THREADS) {
+            const int kk = x / F32_VB, vv = x % F32_VB;
+            float acc = 0.f;
+            for (int t = 0; t < C; t++) acc = fmaf(kdt[kk * C + t], vn[t * F32_VB + vv], acc);
+            S[x] = S[x] * dec + acc;
+        }
+    }
+    __syncthreads();
+    if (s_out)
+        for (int x = tid; x < K * F32_VB; x += F32_THREADS) {
+            const int kk = x / F32_VB, vv = x % F32_VB;
+            s_out[(long)seq * H * K * V + ((size_t)h * K + kk) * V + v0 + vv] = S[x];
+        }
+}
+
+int run_f32(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o, bool o_f32,
+            void* workspace, size_t workspace_bytes, const SeqTable& seqs, int H, int HK, float scale,
+            const void* s_in, long s_in_stride, void* s_out, cudaStream_t st) {
+    if (!q || !k || !v || !g || !beta || !o || !workspace || H <= 0 || HK <= 0 || H % HK) return cudaErrorInvalidValue;
+    GdnTable tab;
+    make_gdn_table(tab, seqs);
+    const long slots = tab.chunk_base[seqs.count];
+    const Layout L(slots, H, true);
+    if ((size_t)L.total > workspace_bytes) return cudaErrorInvalidValue;
+    static const cudaError_t configured = [] {
+        cudaError_t e = cudaFuncSetAttribute(gdn_prep<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gdn_scan_f32<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, F32_SMEM);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(gdn_scan_f32<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, F32_SMEM);
+        return e;
+    }();
+    if (configured != cudaSuccess) return configured;
+    uint8_t* b = static_cast<uint8_t*>(workspace);
+    Work ws{b + L.w, b + L.qd, b + L.p, b + L.kdt, b + L.ut, reinterpret_cast<float*>(b + L.decay), slots};
+    gdn_prep<true><<<dim3(tab.max_chunks, H, seqs.count), PREP_THREADS, PREP_SMEM, st>>>(
+        static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), g,
+        static_cast<const bf16*>(beta), ws, tab, H, HK, scale);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const dim3 grid(H, seqs.count, V / F32_VB);
+    if (o_f32)
+        gdn_scan_f32<float><<<grid, F32_THREADS, F32_SMEM, st>>>(ws, tab, static_cast<float*>(o), H,
+            static_cast<const float*>(s_in), s_in_stride, static_cast<float*>(s_out));
+    else
+        gdn_scan_f32<bf16><<<grid, F32_THREADS, F32_SMEM, st>>>(ws, tab, static_cast<bf16*>(o), H,
+            static_cast<const float*>(s_in), s_in_stride, static_cast<float*>(s_out));
+    return cudaGetLastError();
+}
+
+}  // namespace gdn
+}  // namespace s1
+
+using namespace s1;
+
+namespace {
+
+// Workspace pointers handed in by callers are 256-byte aligned (cudaMalloc); the
+// TMA tiles want 1024: round up inside the caller's buffer.
+void* align1k(void* p, size_t& bytes) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uintptr_t r = (a + 1023) & ~(uintptr_t)1023;
+    const size_t skip = r - a;
+    bytes = bytes > skip ? bytes - skip : 0;
+    return reinterpret_cast<void*>(r);
+}
+
+int single(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+           float* workspace, int T, int H, int HK, float scale, const void* s_in, void* s_out, void* stream) {
+    if (T < 0 || HK <= 0 || H <= 0 || H % HK != 0) return cudaErrorInvalidValue;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (T == 0) {
+        if (!s_out) return cudaSuccess;
+        const size_t bytes = (size_t)H * 128 * 128 * sizeof(float);
+        return s_in ? cudaMemcpyAsync(s_out, s_in, bytes, cudaMemcpyDeviceToDevice, st) : cudaMemsetAsync(s_out, 0, bytes, st);
+    }
+    SeqTable tab;
+    const size_t len = (size_t)T;
+    make_table(tab, &len, 1);
+    size_t bytes = gdn::workspace_bytes_for((T + 63) / 64, H, false);
+    void* ws = align1k(workspace, bytes);
+    return gdn::run(q, k, v, g, beta, o, ws, bytes, tab, H, HK, scale, s_in, 0, s_out, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t cs1_gdn_workspace_floats(int T, int H) {
+    if (T <= 0 || H <= 0) return 0;
+    return (gdn::workspace_bytes_for((T + 63) / 64, H, false) + 3) / 4;
+}
+
+int cs1_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                    float* workspace, int T, int H, int HK, float scale, void* stream) {
+    return single(q, k, v, g, beta, o, workspace, T, H, HK, scale, nullptr, nullptr, stream);
+}
+
+int cs1_gdn_prefill_wide(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                         float* workspace, int T, int H, int HK, float scale, void* stream) {
+    return single(q, k, v, g, beta, o, workspace, T, H, HK, scale, nullptr, nullptr, stream);
+}
+
+int cs1_gdn_prefill_x(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                      float* workspace, int T, int H, int HK, float scale, const void* s_in, void* s_out,
+                      void* stream) {
+    return single(q, k, v, g, beta, o, workspace, T, H, HK, scale, s_in, s_out, stream);
+}
+
+size_t cs1_gdn_batch_workspace_floats(int tokens, int H, int count) {
+    if (tokens <= 0 || H <= 0 || count <= 0 || count > MAX_SEQS || tokens > INT_MAX - count * 64) return 0;
+    const long slots = (tokens + 63) / 64 + count;
+    return (gdn::workspace_bytes_for(slots, H, false) + 3) / 4;
+}
+
+int cs1_gdn_prefill_batch_x(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                            void* o, float* workspace, size_t workspace_bytes, const size_t* lengths,
+                            size_t count, int H, int HK, float scale, const void* state_in, int state_stride,
+                            void* state_out, void* stream) {
+    SeqTable tab;
+    if (!make_table(tab, lengths, count) || (state_stride != 0 && state_stride != 1)) return cudaErrorInvalidValue;
+    size_t bytes = workspace_bytes;
+    void* ws = align1k(workspace, bytes);
+    const long stride = state_stride ? (long)H * 128 * 128 : 0;
+    return gdn::run(q, k, v, g, beta, o, ws, bytes, tab, H, HK, scale, state_in, stride, state_out,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gdn_prefill_batch_shared(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                                 void* o, float* workspace, size_t workspace_bytes, const size_t* lengths,
+                                 size_t count, int H, int HK, float scale, const void* state, void* stream) {
+    return cs1_gdn_prefill_batch_x(q, k, v, g, beta, o, workspace, workspace_bytes, lengths, count, H, HK, scale,
+                                   state, 0, nullptr, stream);
+}
+
+int cs1_gdn_prefill_batch(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                          float* workspace, size_t workspace_bytes, const size_t* lengths, size_t count, int H,
+                          int HK, float scale, void* stream) {
+    return cs1_gdn_prefill_batch_x(q, k, v, g, beta, o, workspace, workspace_bytes, lengths, count, H, HK, scale,
+                                   nullptr, 0, nullptr, stream);
+}
+
+// ---- FP32 operator (ops.h:116-121): float32 normalised q/k, recurrent state and
+// intermediates; bfloat16 output. The context records the device it was made on. ----
+struct Fp32Context {
+    int device;
+    size_t bytes;
+};
+
+void* cs1_gdn_fp32_create(size_t workspace_bytes) {
+    auto* c = new (std::nothrow) Fp32Context;
+    if (!c) return nullptr;
+    c->bytes = workspace_bytes;
+    if (cudaGetDevice(&c->device) != cudaSuccess) {
+        delete c;
+        return nullptr;
+    }
+    return c;
+}
+
+void cs1_gdn_fp32_destroy(void* context) { delete static_cast<Fp32Context*>(context); }
+
+size_t cs1_gdn_fp32_workspace_floats(int T, int H) {
+    if (T <= 0 || T > 65536 || H <= 0 || H > 256) return 0;
+    return (gdn::workspace_bytes_for((T + 63) / 64, H, true) + 3) / 4;
+}
+
+static int fp32_call(void* context, const void* q, const void* k, const void* v, const float* g, const void* beta,
+                     void* o, bool o_f32, float* workspace, int T, int H, int HK, float scale, const float* s_in,
+                     float* s_out, void* stream) {
+    if (!context || !workspace || !q || !k || !v || !g || !beta || !o || !cs1_gdn_fp32_workspace_floats(T, H) ||
+        HK <= 0 || H % HK != 0 || !(scale > 0.f) || !(scale < INFINITY))
+        return cudaErrorInvalidValue;
+    SeqTable tab;
+    const size_t len = (size_t)T;
+    make_table(tab, &len, 1);
+    size_t bytes = gdn::workspace_bytes_for((T + 63) / 64, H, true);
+    void* ws = align1k(workspace, bytes);
+    return gdn::run_f32(q, k, v, g, beta, o, o_f32, ws, bytes, tab, H, HK, scale, s_in, 0, s_out,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gdn_prefill_fp32(void* context, const void* q, const void* k, const void* v, const float* g,
+                         const void* beta, void* o, float* workspace, int T, int H, int HK, float scale,
+                         void* stream) {
+    return fp32_call(context, q, k, v, g, beta, o, false, workspace, T, H, HK, scale, nullptr, nullptr, stream);
+}
+
+int cs1_gdn_prefill_fp32_x(void* context, const void* q, const void* k, const void* v, const float* g,
+                           const void* beta, float* o, float* workspace, int T, int H, int HK, float scale,
+                           const float* s_in, float* s_out, void* stream) {
+    return fp32_call(context, q, k, v, g, beta, o, true, workspace, T, H, HK, scale, s_in, s_out, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// Declarations shared by the two Gated DeltaNet translation units (gdn.cu, gdn_fp32.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "ops_internal.h"
+
+namespace s1 {
+namespace gdn {
+
+constexpr int C = 64;   // chunk length
+constexpr int K = 128;  // key head dim
+constexpr int V = 128;  // value head dim
+
+// Packed sequences plus the first chunk slot of each (slots = chunks over the pack).
+struct GdnTable {
+    SeqTable seq;
+    int chunk_base[MAX_SEQS + 1];
+    int max_chunks;
+};
+bool make_gdn_table(GdnTable& g, const SeqTable& t);
+
+// Workspace regions; element type bf16 (scan operands) or fp32 (FP32 operator).
+// Index [head * slots + slot] selects one chunk's tile.
+struct Work {
+    void* w;       // [.., 64 t][128 k]
+    void* qd;      // [.., 64 t][128 k]
+    void* p;       // [.., 64 t][64 j]
+    void* kdt;     // [.., 128 k][64 t]
+    void* ut;      // [.., 128 v][64 t]
+    float* decay;  // [..] e^{cum_last}
+    long slots;
+};
+
+struct Layout {
+    long w, qd, p, kdt, ut, decay, total;
+    Layout(long slots, int H, bool f32);
+};
+
+size_t workspace_bytes_for(long slots, int H, bool f32);
+
+}  // namespace gdn
+}  // namespace s1

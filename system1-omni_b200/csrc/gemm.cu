@@ -1,0 +1,469 @@
+// Projection GEMMs of the Qwen3.5 prefill on Blackwell tensor cores.
+//
+//   y[M, N] = x[M, K] * w[N, K]^T     bf16 in, fp32 accumulate in tensor memory, bf16 out
+//
+// One persistent, warp-specialised kernel per (tile width, epilogue):
+//   warp 0      TMA producer: 128x64 A and BNx64 B tiles (128-byte swizzle) into a
+//               ring of shared-memory stages, completion counted on mbarriers
+//   warp 1      allocates tensor memory, one thread issues tcgen05.mma (M=128, N=BN,
+//               K=16) into one of two TMEM accumulators and commits to mbarriers
+//   warps 2..5  epilogue: tcgen05.ld of their 32 TMEM lanes (= 32 output rows),
+//               bf16 conversion and the fused epilogue, stores to global memory;
+//               the accumulator is released while the next tile's MMAs run in the
+//               other one.
+// Tiles are walked in groups of GROUP_M row blocks so that the CTAs resident at
+// one time share A rows and B rows in L2.
+//
+// Every output element's K reduction runs in the same order whatever M, the row
+// index or the tile width, so a row's result does not depend on how rows were
+// packed (the property cs1_gemm_create_fixed promises in the reference's ops.h).
+//
+// Fused epilogues (additive symbols):
+//   cs1_gemm_residual: residual = bf16(residual + bf16(x w^T))   (decoder residual add)
+//   cs1_gemm_swiglu:   out = bf16(bf16(silu(gate)) * up), with gate and up rows of w
+//                      interleaved in blocks of 128 (SwiGLU of the MLP)
+#include <algorithm>
+#include <new>
+
+#include "common.cuh"
+#include "ops_internal.h"
+#include "tc.cuh"
+
+S1_FAULT_WORD(gemm)
+
+namespace s1 {
+namespace gemm {
+
+using namespace s1::tc;
+
+constexpr int BM = 128, BK = 64, THREADS = 192, GROUP_M = 16;
+enum Epi : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2 };
+
+template <int BN>
+struct Cfg {
+    static constexpr int STAGES = BN == 256 ? 4 : 6;
+    static constexpr int A_BYTES = BM * BK * 2;
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 2 * BN;
+    static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+    static constexpr int SMEM = BAR_OFFSET + 256 + 1024;  // barriers + TMEM address + alignment slack
+};
+
+struct Params {
+    bf16* y;
+    int ldy;
+    int M, N, K;
+    int tiles_m, tiles_n;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m, int& n) {
+    const int per_group = GROUP_M * tiles_n;
+    const int group = t / per_group;
+    const int first = group * GROUP_M;
+    const int gm = min(GROUP_M, tiles_m - first);
+    const int r = t - group * per_group;
+    m = first + r % gm;
+    n = r / gm;
+}
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p) {
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + C::BAR_OFFSET;
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (C::STAGES + s); };
+    auto tfull = [&](int a) { return bars + 8u * (2 * C::STAGES + a); };
+    auto tempty = [&](int a) { return bars + 8u * (2 * C::STAGES + 2 + a); };
+    const uint32_t drain = bars + 8u * (2 * C::STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BAR_OFFSET + 8 * (2 * C::STAGES + 5));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_tiles = p.tiles_m * p.tiles_n;
+    const int KB = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 4);
+        }
+        mbar_init(drain, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                int m, n;
+                tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(empty(s), ph ^ 1)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t a_dst = base + s * C::STAGE_BYTES;
+                    mbar_expect_tx(full(s), C::STAGE_BYTES);
+                    tma_load_2d(a_dst, &map_a, full(s), kb * BK, m * BM);
+                    tma_load_2d(a_dst + C::A_BYTES, &map_b, full(s), kb * BK, n * BN);
+                    issued++;
+                    if (++s == C::STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            // Drain: every load this thread issued has landed before the CTA exits.
+            const long pending = issued < C::STAGES ? issued : C::STAGES;
+            for (long i = 0; i < pending; i++) {
+                if (--s < 0) {
+                    s = C::STAGES - 1;
+                    ph ^= 1;
+                }
+                (void)mbar_wait(full(s), ph);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t IDESC = idesc(BM, BN, AB_BF16);
+            int s = 0, acc = 0;
+            uint32_t ph = 0, acc_ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                if (!mbar_wait(tempty(acc), acc_ph ^ 1)) {
+                    atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * BN;
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(full(s), ph)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = base + s * C::STAGE_BYTES;
+                    const uint64_t ad = desc_sw128(a_addr), bd = desc_sw128(a_addr + C::A_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++)
+                        mma_bf16(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+                    mma_commit(empty(s));
+                    if (++s == C::STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(tfull(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_ph ^= 1;
+                }
+            }
+            // All MMAs of this CTA complete before tensor memory is freed.
+            mma_commit(drain);
+            (void)mbar_wait(drain, 0);
+        }
+    } else {
+        const int q = warp & 3;  // TMEM lane quadrant this warp may access
+        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+        int acc = 0;
+        uint32_t acc_ph = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            int m, n;
+            tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+            if (!mbar_wait(tfull(acc), acc_ph)) {
+                if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            const int row = m * BM + q * 32 + lane;
+            const bool row_ok = row < p.M;
+            const uint32_t tcol = lane_addr + acc * BN;
+            if constexpr (EPI == EPI_SWIGLU) {
+                // columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows
+                const int out_col0 = n * (BN / 2);
+                const int out_n = p.N / 2;
+#pragma unroll 1
+                for (int c = 0; c < BN / 64; c++) {
+                    float g[32], u[32];
+                    tmem_ld32(tcol + c * 32, g);
+                    tmem_ld32(tcol + BN / 2 + c * 32, u);
+                    tmem_ld_wait();
+                    const int col = out_col0 + c * 32;
+                    if (row_ok) {
+                        bf16* dst = p.y + (size_t)row * p.ldy + col;
+#pragma unroll
+                        for (int v = 0; v < 4; v++) {
+                            if (col + v * 8 + 8 <= out_n) {
+                                float o[8];
+#pragma unroll
+                                for (int e = 0; e < 8; e++) {
+                                    const float gg = rbf(g[v * 8 + e]), uu = rbf(u[v * 8 + e]);
+                                    o[e] = rbf(silu(gg)) * uu;
+                                }
+                                st8(dst + v * 8, pack8(o));
+                            }
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    float v[32];
+                    tmem_ld32(tcol + c * 32, v);
+                    tmem_ld_wait();
+                    const int col = n * BN + c * 32;
+                    if (row_ok) {
+                        bf16* dst = p.y + (size_t)row * p.ldy + col;
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; g8++) {
+                            if (col + g8 * 8 + 8 <= p.N) {
+                                float o[8];
+                                if constexpr (EPI == EPI_RESIDUAL) {
+                                    float r[8];
+                                    unpack8(ld8(dst + g8 * 8), r);
+#pragma unroll
+                                    for (int e = 0; e < 8; e++) o[e] = r[e] + rbf(v[g8 * 8 + e]);
+                                } else {
+#pragma unroll
+                                    for (int e = 0; e < 8; e++) o[e] = v[g8 * 8 + e];
+                                }
+                                st8(dst + g8 * 8, pack8(o));
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_ph ^= 1;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, C::TMEM_COLS);
+    }
+}
+
+// Any shape: one thread per output, fp32 accumulation in K order. Used only when
+// a shape or pointer misses the tensor-map alignment rules.
+template <int EPI>
+__global__ void gemm_simt_kernel(const bf16* __restrict__ x, const bf16* __restrict__ w, bf16* y, int ldy, int M,
+                                 int N, int K) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x, m = blockIdx.y;
+    if (m >= M) return;
+    const int out_n = EPI == EPI_SWIGLU ? N / 2 : N;
+    if (n >= out_n) return;
+    const bf16* xr = x + (size_t)m * K;
+    auto dot = [&](int row) {
+        const bf16* wr = w + (size_t)row * K;
+        float acc = 0.f;
+        for (int k = 0; k < K; k++) acc = fmaf(f32(xr[k]), f32(wr[k]), acc);
+        return acc;
+    };
+    if constexpr (EPI == EPI_SWIGLU) {
+        const int blk = n / 128, j = n % 128;
+        const float g = rbf(dot(blk * 256 + j)), u = rbf(dot(blk * 256 + 128 + j));
+        y[(size_t)m * ldy + n] = to_bf16(rbf(silu(g)) * u);
+    } else if constexpr (EPI == EPI_RESIDUAL) {
+        bf16* d = y + (size_t)m * ldy + n;
+        *d = to_bf16(f32(*d) + rbf(dot(n)));
+    } else {
+        y[(size_t)m * ldy + n] = to_bf16(dot(n));
+    }
+}
+
+struct Handle {
+    int device = 0;
+    int sms = 148;
+    int fixed_m = 0;
+};
+
+template <int BN, int EPI>
+int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy,
+              cudaStream_t st) {
+    using C = Cfg<BN>;
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (configured != cudaSuccess) return configured;
+    CUtensorMap ma, mb;
+    int e = host::make_map_2d(&ma, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, K, BM, BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    e = host::make_map_2d(&mb, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, BN, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    Params p;
+    p.y = static_cast<bf16*>(y);
+    p.ldy = ldy;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.tiles_m = (M + BM - 1) / BM;
+    p.tiles_n = (N + BN - 1) / BN;
+    const int tiles = p.tiles_m * p.tiles_n;
+    const int grid = std::min(tiles, h->sms);
+    gemm_kernel<BN, EPI><<<grid, THREADS, C::SMEM, st>>>(ma, mb, p);
+    return cudaGetLastError();
+}
+
+int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int epi,
+        cudaStream_t st) {
+    if (!h || M < 0 || N <= 0 || K <= 0 || !x || !w || !y) return cudaErrorInvalidValue;
+    const int out_n = epi == EPI_SWIGLU ? N / 2 : N;
+    if (ldy < out_n) return cudaErrorInvalidValue;
+    if (epi == EPI_SWIGLU && N % 256 != 0) return cudaErrorInvalidValue;
+    if (M == 0) return cudaSuccess;
+    const bool tc_ok = K % 8 == 0 && N % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(w) && aligned16(y);
+    if (!tc_ok) {
+        const dim3 grid((out_n + 127) / 128, M);
+        switch (epi) {
+            case EPI_SWIGLU:
+                gemm_simt_kernel<EPI_SWIGLU><<<grid, 128, 0, st>>>(static_cast<const bf16*>(x),
+                    static_cast<const bf16*>(w), static_cast<bf16*>(y), ldy, M, N, K);
+                break;
+            case EPI_RESIDUAL:
+                gemm_simt_kernel<EPI_RESIDUAL><<<grid, 128, 0, st>>>(static_cast<const bf16*>(x),
+                    static_cast<const bf16*>(w), static_cast<bf16*>(y), ldy, M, N, K);
+                break;
+            default:
+                gemm_simt_kernel<EPI_STORE><<<grid, 128, 0, st>>>(static_cast<const bf16*>(x),
+                    static_cast<const bf16*>(w), static_cast<bf16*>(y), ldy, M, N, K);
+        }
+        return cudaGetLastError();
+    }
+    // 256-wide tiles unless that leaves most SMs idle.
+    const long tiles256 = (long)((M + BM - 1) / BM) * ((N + 255) / 256);
+    const bool wide = epi == EPI_SWIGLU || tiles256 >= h->sms;
+    switch (epi) {
+        case EPI_SWIGLU:
+            return launch_tc<256, EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);
+        case EPI_RESIDUAL:
+            return wide ? launch_tc<256, EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st)
+                        : launch_tc<128, EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st);
+        default:
+            return wide ? launch_tc<256, EPI_STORE>(h, x, w, y, M, N, K, ldy, st)
+                        : launch_tc<128, EPI_STORE>(h, x, w, y, M, N, K, ldy, st);
+    }
+}
+
+}  // namespace gemm
+}  // namespace s1
+
+using namespace s1;
+
+extern "C" {
+
+void* cs1_gemm_create(size_t workspace_bytes) {
+    (void)workspace_bytes;  // the tcgen05 kernels need no library workspace
+    auto* h = new (std::nothrow) gemm::Handle;
+    if (!h) return nullptr;
+    if (cudaGetDevice(&h->device) != cudaSuccess) {
+        delete h;
+        return nullptr;
+    }
+    h->sms = host::num_sms();
+    return h;
+}
+
+void* cs1_gemm_create_fixed(size_t workspace_bytes, int reference_m) {
+    if (reference_m <= 0) return nullptr;
+    auto* h = static_cast<gemm::Handle*>(cs1_gemm_create(workspace_bytes));
+    if (h) h->fixed_m = reference_m;
+    return h;
+}
+
+void* cs1_gemm_create_matched(size_t workspace_bytes, int reference_m) {
+    return cs1_gemm_create_fixed(workspace_bytes, reference_m);
+}
+
+// Every handle runs the same M-independent kernels, so any two are compatible.
+int cs1_gemm_compatible(void* ordinary, void* matched, int M, int N, int K) {
+    (void)ordinary;
+    (void)matched;
+    return (M >= 0 && N > 0 && K > 0) ? 1 : 0;
+}
+
+void cs1_gemm_destroy(void* gemm) { delete static_cast<gemm::Handle*>(gemm); }
+
+int cs1_gemm_enable_equivalent_tiles(void* gemm) { return gemm ? 1 : -1; }
+
+int cs1_gemm(void* gemm, const void* x, const void* w, void* y, int M, int N, int K, int ldy, void* stream) {
+    return gemm::run(static_cast<const gemm::Handle*>(gemm), x, w, y, M, N, K, ldy, gemm::EPI_STORE,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gemm_packed(void* gemm, const void* x, const void* w, void* y, const size_t* lengths, size_t count, int N,
+                    int K, void* stream) {
+    if (!lengths || count == 0) return cudaErrorInvalidValue;
+    size_t rows = 0;
+    for (size_t i = 0; i < count; i++) {
+        if (lengths[i] == 0) return cudaErrorInvalidValue;
+        rows += lengths[i];
+    }
+    if (rows > 0x7FFFFFFF) return cudaErrorInvalidValue;
+    return gemm::run(static_cast<const gemm::Handle*>(gemm), x, w, y, (int)rows, N, K, N, gemm::EPI_STORE,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gemm_reuse_check(void* gemm, const size_t* original_rows, size_t originals, const size_t* target_rows,
+                         size_t targets, int N, int K) {
+    if (!gemm || N <= 0 || K <= 0) return cudaErrorInvalidValue;
+    (void)original_rows;
+    (void)originals;
+    (void)target_rows;
+    (void)targets;
+    return 0;
+}
+
+int cs1_gemm_reuse(void* gemm, const void* x, const void* w, void* y, int M, int N, int K, int original_M,
+                   void* stream) {
+    (void)original_M;
+    return gemm::run(static_cast<const gemm::Handle*>(gemm), x, w, y, M, N, K, N, gemm::EPI_STORE,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gemm_residual(void* gemm, const void* x, const void* w, void* residual, int M, int N, int K, int ldr,
+                      void* stream) {
+    return gemm::run(static_cast<const gemm::Handle*>(gemm), x, w, residual, M, N, K, ldr, gemm::EPI_RESIDUAL,
+                     static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gemm_swiglu(void* gemm, const void* x, const void* w, void* out, int M, int I, int K, int ldo,
+                    void* stream) {
+    if (I <= 0 || I % 128 != 0) return cudaErrorInvalidValue;
+    return gemm::run(static_cast<const gemm::Handle*>(gemm), x, w, out, M, 2 * I, K, ldo, gemm::EPI_SWIGLU,
+                     static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,186 @@
+// Row normalisations of the Qwen3.5 prefill (bandwidth-bound, 16-byte accesses).
+//
+//  cs1_rms_norm       out = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w))      (Qwen3_5RMSNorm)
+//  cs1_add_rms_norm   residual = bf16(residual + delta); out = rms_norm(residual)
+//  cs1_gated_rms_norm GDN output norm, rows of 128:
+//                     bf16(bf16(w * bf16(x / rms(x))) * silu(z))          (Qwen3_5RMSNormGated)
+// Rounding points follow the reference kernels (norm.cu:11-139 of the reference);
+// the fp32 sum of squares is reduced in a different order (tree over packs).
+#include "common.cuh"
+#include "ops_internal.h"
+
+namespace s1 {
+namespace {
+
+constexpr int NT = 256;       // threads per row block
+constexpr int MAXP = 4;       // packs of 8 cached per thread: D <= 8192
+
+template <bool Add>
+__global__ void __launch_bounds__(NT) rms_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
+                                                 const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                 bf16* __restrict__ out, int D, float eps) {
+    __shared__ float scratch[32];
+    const size_t row = blockIdx.x;
+    const int packs = D >> 3;
+    float v[MAXP][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < MAXP; i++) {
+        const int pk = threadIdx.x + i * NT;
+        if (pk < packs) {
+            const size_t off = row * D + (size_t)pk * 8;
+            if constexpr (Add) {
+                float a[8], b[8];
+                unpack8(ld8(res + off), a);
+                unpack8(ld8(delta + off), b);
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[i][e] = rbf(a[e] + b[e]);
+                st8(res + off, pack8(v[i]));
+            } else {
+                unpack8(ld8(x + off), v[i]);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss = fmaf(v[i][e], v[i][e], ss);
+        }
+    }
+    const float inv = rsqrtf(block_sum(ss, scratch) / D + eps);
+#pragma unroll
+    for (int i = 0; i < MAXP; i++) {
+        const int pk = threadIdx.x + i * NT;
+        if (pk < packs) {
+            float wv[8], o[8];
+            unpack8(ld8(w + (size_t)pk * 8), wv);
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = v[i][e] * inv * (1.f + wv[e]);
+            st8(out + row * D + (size_t)pk * 8, pack8(o));
+        }
+    }
+}
+
+// Any D: scalar path, two passes over the row.
+template <bool Add>
+__global__ void __launch_bounds__(NT) rms_scalar_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
+                                                        const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                        bf16* __restrict__ out, int D, float eps) {
+    __shared__ float scratch[32];
+    const size_t row = blockIdx.x;
+    const bf16* src = Add ? res : x;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < D; i += NT) {
+        float val;
+        if constexpr (Add) {
+            const bf16 r = to_bf16(f32(res[row * D + i]) + f32(delta[row * D + i]));
+            res[row * D + i] = r;
+            val = f32(r);
+        } else {
+            val = f32(src[row * D + i]);
+        }
+        ss = fmaf(val, val, ss);
+    }
+    const float inv = rsqrtf(block_sum(ss, scratch) / D + eps);
+    for (int i = threadIdx.x; i < D; i += NT) out[row * D + i] = to_bf16(f32(src[row * D + i]) * inv * (1.f + f32(w[i])));
+}
+
+// One warp per (token, head) row of 128; each lane holds 4 values (8 bytes).
+__global__ void gated_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
+                             const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const size_t base = (size_t)row * 128 + lane * 4;
+    const size_t zb = (size_t)(row / H) * ldz + (size_t)(row % H) * 128 + lane * 4;
+    const uint2 xr = *reinterpret_cast<const uint2*>(x + base);
+    const uint2 zr = *reinterpret_cast<const uint2*>(z + zb);
+    const uint2 wr = *reinterpret_cast<const uint2*>(w + lane * 4);
+    const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xr);
+    const __nv_bfloat162* zp = reinterpret_cast<const __nv_bfloat162*>(&zr);
+    const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wr);
+    float v[4], zz[4], ww[4];
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const float2 a = __bfloat1622float2(xp[i]), b = __bfloat1622float2(zp[i]), c = __bfloat1622float2(wp[i]);
+        v[2 * i] = a.x; v[2 * i + 1] = a.y;
+        zz[2 * i] = b.x; zz[2 * i + 1] = b.y;
+        ww[2 * i] = c.x; ww[2 * i + 1] = c.y;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) ss = fmaf(v[i], v[i], ss);
+    const float inv = rsqrtf(warp_sum(ss) / 128.f + eps);
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) o[i] = rbf(ww[i] * rbf(v[i] * inv)) * silu(zz[i]);
+    uint2 r;
+    r.x = pack_bf16x2(o[0], o[1]);
+    r.y = pack_bf16x2(o[2], o[3]);
+    *reinterpret_cast<uint2*>(out + base) = r;
+}
+
+__global__ void gated_scalar_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
+                                    const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
+    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const size_t base = (size_t)row * 128;
+    const size_t zb = (size_t)(row / H) * ldz + (size_t)(row % H) * 128;
+    float ss = 0.f;
+    for (int i = lane; i < 128; i += 32) ss = fmaf(f32(x[base + i]), f32(x[base + i]), ss);
+    const float inv = rsqrtf(warp_sum(ss) / 128.f + eps);
+    for (int i = lane; i < 128; i += 32)
+        out[base + i] = to_bf16(rbf(f32(w[i]) * rbf(f32(x[base + i]) * inv)) * silu(f32(z[zb + i])));
+}
+
+bool vec_ok(int D, const void* a, const void* b, const void* c, const void* d) {
+    return D % 8 == 0 && D <= 8 * NT * MAXP && aligned16(a) && aligned16(b) && aligned16(c) && aligned16(d);
+}
+
+}  // namespace
+}  // namespace s1
+
+using namespace s1;
+
+extern "C" int cs1_rms_norm(const void* x, const void* w, void* out, int rows, int D, float eps, void* stream) {
+    if (rows < 0 || D <= 0) return cudaErrorInvalidValue;
+    if (rows == 0) return cudaSuccess;
+    auto st = static_cast<cudaStream_t>(stream);
+    auto X = static_cast<const bf16*>(x);
+    auto Wt = static_cast<const bf16*>(w);
+    auto O = static_cast<bf16*>(out);
+    if (vec_ok(D, x, w, out, out))
+        rms_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
+    else
+        rms_scalar_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
+    return cudaGetLastError();
+}
+
+extern "C" int cs1_add_rms_norm(void* residual, const void* delta, const void* w, void* out, int rows, int D,
+                                float eps, void* stream) {
+    if (rows < 0 || D <= 0) return cudaErrorInvalidValue;
+    if (rows == 0) return cudaSuccess;
+    auto st = static_cast<cudaStream_t>(stream);
+    auto R = static_cast<bf16*>(residual);
+    auto Dl = static_cast<const bf16*>(delta);
+    auto Wt = static_cast<const bf16*>(w);
+    auto O = static_cast<bf16*>(out);
+    if (vec_ok(D, residual, delta, w, out))
+        rms_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
+    else
+        rms_scalar_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
+    return cudaGetLastError();
+}
+
+extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const void* w, void* out, int T, int H,
+                                  int D, float eps, void* stream) {
+    if (D != 128 || T < 0 || H <= 0 || ldz < H * D) return cudaErrorInvalidValue;
+    const int rows = T * H;
+    if (rows == 0) return cudaSuccess;
+    constexpr int WARPS = 8;
+    auto st = static_cast<cudaStream_t>(stream);
+    const bool vec = ldz % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(z) |
+                                       reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 7) == 0;
+    if (vec)
+        gated_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
+            static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
+    else
+        gated_scalar_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
+            static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
+    return cudaGetLastError();
+}

@@ -1,0 +1,16 @@
+"""Python bindings of the B200 Qwen3.5 hybrid decision-model prefill.
+
+Thin ctypes layer over the two native libraries built in-tree by
+`system1-omni_b200/build.py`:
+
+* `libqwen3_5_cuda.so` -- the cs1_* C ABI (include/qwen3_5_ops.h): every
+  operation of the prefill as a hand-written sm_100a kernel.
+* `libs1_model.so`     -- the C++ prefill host (include/s1_model.h): weights,
+  packed / shared-prefix forward, scorer head, CUDA graphs.
+
+There is no fallback: a missing library raises at import of the binding.
+"""
+from .cs1 import Cs1, Cs1Error, lib_path
+from .model import Config, Model, preset, pack_ranges, shared_prefix
+
+__all__ = ["Cs1", "Cs1Error", "lib_path", "Config", "Model", "preset", "pack_ranges", "shared_prefix"]

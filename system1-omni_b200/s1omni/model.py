@@ -1,0 +1,245 @@
+"""ctypes binding of libs1_model.so (include/s1_model.h): the decision-model prefill.
+
+`Model` mirrors the reference worker's executor interface: load weights, run a
+packed-candidate prefill, score each candidate's final token with the learned
+head (src/models/open_jev/native/src/executor.rs:237-343 for the call pattern).
+"""
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from .cs1 import lib_path
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+Z = ctypes.c_size_t
+
+
+class _Cfg(ctypes.Structure):
+    _fields_ = [("hidden", I), ("intermediate", I), ("n_layers", I), ("layer_types", ctypes.POINTER(I)),
+                ("lin_k_heads", I), ("lin_v_heads", I), ("lin_k_dim", I), ("lin_v_dim", I), ("heads", I),
+                ("kv_heads", I), ("head_dim", I), ("rotary_half", I), ("theta", ctypes.c_double),
+                ("eps", ctypes.c_float), ("vocab", I), ("labels", I)]
+
+
+@dataclass
+class Config:
+    """Qwen3.5 hybrid scorer shape (Transformers Qwen3_5TextConfig fields, renamed)."""
+    hidden: int
+    intermediate: int
+    layer_types: list            # "gdn" / "attn" per layer
+    lin_k_heads: int
+    lin_v_heads: int
+    heads: int
+    kv_heads: int
+    vocab: int
+    labels: int = 8
+    lin_k_dim: int = 128
+    lin_v_dim: int = 128
+    head_dim: int = 256
+    rotary_half: int = 32
+    theta: float = 1.0e7
+    eps: float = 1e-6
+    name: str = field(default="custom")
+
+    def weight_count(self):
+        H, I_ = self.hidden, self.intermediate
+        kd, vd, hv = self.lin_k_heads * 128, self.lin_v_heads * 128, self.lin_v_heads
+        n = self.vocab * H + H + self.labels * (H + 1)
+        for t in self.layer_types:
+            n += 2 * H + 3 * H * I_
+            if t == "gdn":
+                conv = 2 * kd + vd
+                n += (conv + vd + 2 * hv) * H + conv * 4 + 2 * hv + 128 + H * vd
+            else:
+                n += (2 * self.heads * 256 + 2 * self.kv_heads * 256) * H + 512 + H * self.heads * 256
+        return n
+
+    def projection_flops_per_token(self):
+        """2 * sum(N * K) over every projection (the tensor-core work per token)."""
+        H, I_ = self.hidden, self.intermediate
+        kd, vd, hv = self.lin_k_heads * 128, self.lin_v_heads * 128, self.lin_v_heads
+        f = 0
+        for t in self.layer_types:
+            f += 3 * H * I_
+            if t == "gdn":
+                f += (2 * kd + vd + vd + 2 * hv) * H + H * vd
+            else:
+                f += (2 * self.heads * 256 + 2 * self.kv_heads * 256) * H + H * self.heads * 256
+        return 2 * f
+
+
+def _hybrid(n, interval=4):
+    return ["attn" if (i + 1) % interval == 0 else "gdn" for i in range(n)]
+
+
+def preset(name):
+    """BASELINE shapes (4B, 9B, 27B) and small test shapes."""
+    table = {
+        "4b": (2560, 9216, 32, 16, 32, 16, 4, 151936),
+        "9b": (4096, 12288, 32, 16, 32, 16, 4, 151936),
+        "27b": (5120, 17408, 64, 16, 48, 24, 4, 151936),
+        "tiny": (256, 512, 4, 2, 4, 4, 2, 512),
+        "tiny8": (512, 1024, 8, 2, 6, 6, 2, 1024),
+    }
+    H, I_, L, hk, hv, hq, hkv, vocab = table[name]
+    return Config(H, I_, _hybrid(L), hk, hv, hq, hkv, vocab, name=name)
+
+
+def _lib():
+    lib = ctypes.CDLL(lib_path("libs1_model.so"))
+    lib.s1_model_create.restype = P
+    lib.s1_model_create.argtypes = [ctypes.c_char_p, ctypes.POINTER(_Cfg), I, I, I]
+    lib.s1_model_destroy.argtypes = [P]
+    lib.s1_model_destroy.restype = None
+    lib.s1_model_error.restype = ctypes.c_char_p
+    lib.s1_model_error.argtypes = [P]
+    lib.s1_model_set_weight.argtypes = [P, ctypes.c_char_p, P, Z]
+    lib.s1_model_init_random.argtypes = [P, ctypes.c_uint64, ctypes.c_float]
+    lib.s1_model_forward.argtypes = [P, P, P, Z, P, P]
+    lib.s1_model_forward_shared.argtypes = [P, P, Z, P, P, Z, P, P]
+    lib.s1_model_stage.argtypes = [P, P, P, Z]
+    lib.s1_model_run_staged.argtypes = [P]
+    lib.s1_model_fetch_logits.argtypes = [P, P]
+    lib.s1_model_set_graphs.argtypes = [P, I]
+    lib.s1_model_stream.restype = P
+    lib.s1_model_stream.argtypes = [P]
+    lib.s1_model_last_launches.restype = ctypes.c_long
+    lib.s1_model_last_launches.argtypes = [P]
+    lib.s1_model_fused.argtypes = [P]
+    lib.s1_pack_ranges.argtypes = [P, Z, Z, Z, P]
+    lib.s1_shared_prefix.restype = Z
+    lib.s1_shared_prefix.argtypes = [P, P, Z, Z]
+    return lib
+
+
+_LIB = None
+
+
+def _get():
+    global _LIB
+    if _LIB is None:
+        import os
+        path = lib_path("libs1_model.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} is missing: run system1-omni_b200/build.py")
+        _LIB = _lib()
+    return _LIB
+
+
+def pack_ranges(lengths, max_sequences=16, max_tokens=4096):
+    """[(start, end)] launch ranges (open_jev batching.rs:9-25), computed by the C++ host."""
+    lib = _get()
+    n = len(lengths)
+    arr = np.asarray(lengths, dtype=np.uintp)
+    starts = np.zeros(n + 1, dtype=np.uintp)
+    r = lib.s1_pack_ranges(arr.ctypes.data, n, max_sequences, max_tokens, starts.ctypes.data)
+    if r < 0:
+        raise ValueError("invalid packing arguments")
+    return [(int(starts[i]), int(starts[i + 1])) for i in range(r)]
+
+
+def shared_prefix(inputs, minimum=2049):
+    """Aligned shared prefix of 2..16 candidates (batching.rs:29-49), computed by the C++ host."""
+    lib = _get()
+    arrays = [np.ascontiguousarray(x, dtype=np.int32) for x in inputs]
+    ptrs = (ctypes.c_void_p * max(1, len(arrays)))(*[a.ctypes.data for a in arrays])
+    lens = np.asarray([len(a) for a in arrays], dtype=np.uintp)
+    return int(lib.s1_shared_prefix(ctypes.cast(ptrs, P), lens.ctypes.data, len(arrays), minimum))
+
+
+class Model:
+    """A prefill model on one GPU: `Model(cfg, device, max_tokens, max_seqs)`."""
+
+    def __init__(self, cfg, device=0, max_tokens=4096, max_seqs=64, cs1_library=None):
+        self.cfg = cfg
+        self._lib = _get()
+        self._types = (I * len(cfg.layer_types))(*[0 if t == "gdn" else 1 for t in cfg.layer_types])
+        c = _Cfg(cfg.hidden, cfg.intermediate, len(cfg.layer_types), self._types, cfg.lin_k_heads, cfg.lin_v_heads,
+                 cfg.lin_k_dim, cfg.lin_v_dim, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rotary_half,
+                 float(cfg.theta), float(cfg.eps), cfg.vocab, cfg.labels)
+        path = (cs1_library or lib_path()).encode()
+        self._h = self._lib.s1_model_create(path, ctypes.byref(c), device, max_tokens, max_seqs)
+        if not self._h:
+            raise RuntimeError("s1_model_create: " + self._lib.s1_model_error(None).decode())
+        self.max_tokens, self.max_seqs = max_tokens, max_seqs
+
+    def _check(self, rc, what):
+        if rc != 0:
+            raise RuntimeError(f"{what}: " + self._lib.s1_model_error(self._h).decode())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._lib.s1_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def set_weight(self, name, array):
+        """array: numpy float32 holding bf16 values (converted here), or float32 for the head."""
+        a = np.ascontiguousarray(array, dtype=np.float32)
+        if name in ("head_w", "head_b"):
+            data = a
+        else:
+            u = a.view(np.uint32).astype(np.uint64)
+            data = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        self._check(self._lib.s1_model_set_weight(self._h, name.encode(), data.ctypes.data, data.nbytes), name)
+
+    def load(self, weights):
+        for name, arr in weights.items():
+            self.set_weight(name, arr)
+
+    def init_random(self, seed=0, std=0.02):
+        self._check(self._lib.s1_model_init_random(self._h, seed, std), "init_random")
+
+    def forward(self, seqs, hidden=False):
+        """Packed candidates (list of int arrays) -> logits [n, labels] (and last hidden rows)."""
+        ids = np.concatenate([np.asarray(s, np.int32) for s in seqs])
+        lens = np.asarray([len(s) for s in seqs], dtype=np.uintp)
+        logits = np.zeros((len(seqs), self.cfg.labels), np.float32)
+        hid = np.zeros((len(seqs), self.cfg.hidden), np.float32) if hidden else None
+        self._check(self._lib.s1_model_forward(self._h, ids.ctypes.data, lens.ctypes.data, len(seqs),
+                                               logits.ctypes.data, hid.ctypes.data if hidden else None), "forward")
+        return (logits, hid) if hidden else logits
+
+    def forward_shared(self, prefix, suffixes, hidden=False):
+        pre = np.asarray(prefix, np.int32)
+        ids = np.concatenate([np.asarray(s, np.int32) for s in suffixes])
+        lens = np.asarray([len(s) for s in suffixes], dtype=np.uintp)
+        logits = np.zeros((len(suffixes), self.cfg.labels), np.float32)
+        hid = np.zeros((len(suffixes), self.cfg.hidden), np.float32) if hidden else None
+        self._check(self._lib.s1_model_forward_shared(self._h, pre.ctypes.data, len(pre), ids.ctypes.data,
+                                                      lens.ctypes.data, len(suffixes), logits.ctypes.data,
+                                                      hid.ctypes.data if hidden else None), "forward_shared")
+        return (logits, hid) if hidden else logits
+
+    def stage(self, seqs):
+        ids = np.concatenate([np.asarray(s, np.int32) for s in seqs])
+        lens = np.asarray([len(s) for s in seqs], dtype=np.uintp)
+        self._staged_n = len(seqs)
+        self._check(self._lib.s1_model_stage(self._h, ids.ctypes.data, lens.ctypes.data, len(seqs)), "stage")
+
+    def run_staged(self):
+        self._check(self._lib.s1_model_run_staged(self._h), "run_staged")
+
+    def fetch_logits(self):
+        out = np.zeros((self._staged_n, self.cfg.labels), np.float32)
+        self._check(self._lib.s1_model_fetch_logits(self._h, out.ctypes.data), "fetch_logits")
+        return out
+
+    def set_graphs(self, on):
+        self._check(self._lib.s1_model_set_graphs(self._h, 1 if on else 0), "set_graphs")
+
+    @property
+    def stream(self):
+        return self._lib.s1_model_stream(self._h)
+
+    @property
+    def last_launches(self):
+        return int(self._lib.s1_model_last_launches(self._h))
+
+    @property
+    def fused(self):
+        return bool(self._lib.s1_model_fused(self._h))

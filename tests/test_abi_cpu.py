@@ -1,0 +1,113 @@
+"""CPU checks of the drop-in boundary: both libraries load without a GPU, export
+every symbol their headers declare, report ABI version 9, and the host packing
+policy matches the reference's own test vectors (tests/open_jev/batching.rs)."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared(header):
+    text = open(os.path.join(ROOT, "include", header)).read()
+    text = re.sub(r"//.*", "", text)
+    return sorted(set(re.findall(r"\b((?:cs1|s1)_[a-z0-9_]+)\s*\(", text)))
+
+
+def _exported(lib):
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", lib], capture_output=True, text=True, check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if " T " in line}
+
+
+def test_cs1_library_exports_every_declared_symbol():
+    from s1omni import lib_path
+    names = _declared("qwen3_5_ops.h")
+    assert len(names) > 60
+    exported = _exported(lib_path())
+    missing = [n for n in names if n not in exported]
+    assert not missing, missing
+    # nothing else leaks out of the library
+    assert all(n.startswith("cs1_") for n in exported), sorted(n for n in exported if not n.startswith("cs1_"))
+
+
+def test_model_library_exports_every_declared_symbol():
+    from s1omni import lib_path
+    names = _declared("s1_model.h")
+    exported = _exported(lib_path("libs1_model.so"))
+    missing = [n for n in names if n not in exported]
+    assert not missing, missing
+
+
+def test_abi_version_without_gpu():
+    from s1omni import Cs1
+    lib = Cs1()
+    assert lib.cs1_abi_version() == 9
+    assert lib.cs1_gdn_fp32_workspace_floats(0, 32) == 0
+    assert lib.cs1_gdn_fp32_workspace_floats(65537, 32) == 0
+    assert lib.cs1_gdn_fp32_workspace_floats(1, 257) == 0
+    assert lib.cs1_gdn_batch_workspace_floats(100, 4, 0) == 0
+    assert lib.cs1_gdn_workspace_floats(64, 4) > 0
+
+
+def test_reference_loader_required_symbols_present():
+    """Every symbol the reference's Rust loader requires (cuda.rs api! table)."""
+    from s1omni import lib_path
+    required = """cs1_abi_version cs1_error_string cs1_set_device cs1_get_device cs1_bf16_finite cs1_malloc cs1_free
+    cs1_stream_create cs1_stream_sync cs1_stream_destroy cs1_graph_begin cs1_graph_end cs1_graph_launch
+    cs1_graph_destroy cs1_upload cs1_download cs1_copy_dd cs1_copy2d cs1_embed cs1_rms_norm cs1_add_rms_norm
+    cs1_gated_rms_norm cs1_gdn_conv cs1_gdn_gates cs1_gdn_workspace_floats cs1_gdn_prefill cs1_gdn_prefill_x
+    cs1_attn_prep cs1_attention cs1_attention_gated cs1_attention_gated_prefix cs1_sigmoid_gate cs1_silu_mul
+    cs1_gemm_create cs1_gemm_create_fixed cs1_gemm_destroy cs1_gemm cs1_vision_linear cs1_gemm_f32
+    cs1_vision_norm cs1_vision_position cs1_vision_rope cs1_vision_attention""".split()
+    exported = _exported(lib_path())
+    assert not [n for n in required if n not in exported]
+
+
+def test_pack_ranges_reference_vectors():
+    from s1omni import pack_ranges
+    from oracle.packing import ranges
+    lengths = [2048, 2048, 1, 5000, 3] + [4] * 17
+    expect = [(0, 2), (2, 3), (3, 4), (4, 20), (20, 22)]
+    assert pack_ranges(lengths) == expect
+    assert ranges(lengths) == expect
+    rng = np.random.default_rng(0)
+    for _ in range(200):
+        lens = rng.integers(1, 5000, rng.integers(1, 40)).tolist()
+        assert pack_ranges(lens) == ranges(lens)
+    assert pack_ranges([]) == []
+
+
+def test_shared_prefix_reference_vectors():
+    from s1omni import shared_prefix
+    from oracle.packing import shared_prefix as oracle_sp
+    a = np.ones(2100, np.int32)
+    b = a.copy()
+    b[2000] = 2
+    for fn in (shared_prefix, oracle_sp):
+        assert fn([a, b]) == 1984
+    b[100] = 3
+    for fn in (shared_prefix, oracle_sp):
+        assert fn([a, b]) == 0
+        assert fn([a, a]) == 2048
+        assert fn([a]) == 0
+        assert fn([a, a[:2048]]) == 0
+        assert fn([a] * 17) == 0
+    a = np.full(801, 42, np.int32)
+    b = np.full(832, 42, np.int32)
+    b[790] = 7
+    for fn in (shared_prefix, oracle_sp):
+        assert fn([a, b]) == 0
+        assert fn([a, b], 512) == 768
+        assert fn([a, b[:511]], 512) == 0
+        assert fn([a, b[:512]], 512) == 0
+        assert fn([a], 512) == 0
+        assert fn([a] * 17, 512) == 0
+
+
+def test_model_create_reports_missing_library():
+    from s1omni import Model, preset
+    with pytest.raises(RuntimeError, match="dlopen"):
+        Model(preset("tiny"), cs1_library="/nonexistent/libqwen3_5_cuda.so")
