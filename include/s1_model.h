@@ -47,7 +47,8 @@ typedef struct s1_config {
     int labels;          // scorer-head rows
 } s1_config;
 
-// Binds the cs1 library at `cs1_library_path`, selects `device`, allocates the weight
+// Binds the cs1 library at `cs1_library_path` ("lib" or "lib;aux", where aux may supply
+// cs1_fill_random for libraries without it), selects `device`, allocates the weight
 // arena and scratch for packs of up to max_tokens rows and max_seqs sequences.
 // Returns null on failure (s1_model_error(NULL) then describes it).
 void* s1_model_create(const char* cs1_library_path, const s1_config* cfg, int device, int max_tokens,

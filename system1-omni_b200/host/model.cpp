@@ -99,7 +99,16 @@ bool bind(void* h, const char* name, F& fn, bool required, std::string& err) {
     return true;
 }
 
-bool load_api(const char* path, Api& a, std::string& err) {
+// `spec` is "library" or "library;aux": symbols of this build that a library lacks
+// (the random weight fill used by benchmarks) may come from the aux library.
+bool load_api(const char* spec, Api& a, std::string& err) {
+    std::string primary(spec), aux;
+    const size_t semi = primary.find(';');
+    if (semi != std::string::npos) {
+        aux = primary.substr(semi + 1);
+        primary = primary.substr(0, semi);
+    }
+    const char* path = primary.c_str();
     a.handle = dlopen(path, RTLD_NOW | RTLD_LOCAL);
     if (!a.handle) {
         err = std::string("dlopen failed: ") + dlerror();
@@ -155,6 +164,10 @@ bool load_api(const char* path, Api& a, std::string& err) {
     bind(h, "cs1_gemm_swiglu", a.gemm_swiglu, false, err);
     bind(h, "cs1_head_score", a.head_score, false, err);
     bind(h, "cs1_fill_random", a.fill_random, false, err);
+    if (!a.fill_random && !aux.empty()) {
+        void* ah = dlopen(aux.c_str(), RTLD_NOW | RTLD_LOCAL);
+        if (ah) bind(ah, "cs1_fill_random", a.fill_random, false, err);
+    }
     return true;
 }
 
@@ -541,9 +554,37 @@ int run_layers(Model* m, const Batch& b) {
     return 0;
 }
 
+// Without cs1_head_score the head runs on the host after downloading each last row,
+// as the reference's executor does (executor.rs:59-71); logits land in host_logits.
+int host_head(Model* m, int n, float* logits) {
+    const s1_config& c = m->cfg;
+    std::vector<int32_t> rows(n);
+    CK(m->api.download(rows.data(), m->S(m->s_rows), (size_t)n * 4, m->stream), "download rows");
+    std::vector<float> W((size_t)c.labels * c.hidden), bias(c.labels);
+    CK(m->api.download(W.data(), m->W(m->head_w), W.size() * 4, m->stream), "download head");
+    CK(m->api.download(bias.data(), m->W(m->head_b), bias.size() * 4, m->stream), "download bias");
+    std::vector<uint16_t> row(c.hidden);
+    for (int i = 0; i < n; i++) {
+        CK(m->api.download(row.data(), m->S(m->s_x) + (size_t)rows[i] * c.hidden * 2, (size_t)c.hidden * 2,
+                           m->stream),
+           "download last row");
+        for (int l = 0; l < c.labels; l++) {
+            double acc = 0.0;
+            for (int d = 0; d < c.hidden; d++) {
+                const uint32_t u = (uint32_t)row[d] << 16;
+                float h;
+                std::memcpy(&h, &u, 4);
+                acc += (double)W[(size_t)l * c.hidden + d] * (double)h;
+            }
+            logits[(size_t)i * c.labels + l] = (float)acc + bias[l];
+        }
+    }
+    return 0;
+}
+
 int run_head(Model* m, int n) {
     const s1_config& c = m->cfg;
-    if (!m->api.head_score) return fail(m, -1, "library has no scorer head (cs1_head_score)");
+    if (!m->api.head_score) return 0;  // host head after the forward (host_head)
     m->launches++;
     CK(m->api.head_score(m->S(m->s_x), c.hidden, reinterpret_cast<const int32_t*>(m->S(m->s_rows)), n,
                          reinterpret_cast<const float*>(m->W(m->head_w)), reinterpret_cast<const float*>(m->W(m->head_b)),
@@ -663,8 +704,14 @@ int ensure_prefix(Model* m, int P) {
 int read_outputs(Model* m, const Batch& b, float* logits, float* hidden) {
     const s1_config& c = m->cfg;
     const int n = (int)b.lengths.size();
-    if (logits) CK(m->api.download(logits, m->S(m->s_logits), (size_t)n * c.labels * 4, m->stream), "download logits");
-    else CK(m->api.stream_sync(m->stream), "sync");
+    if (logits && !m->api.head_score) {
+        const int rc = host_head(m, n, logits);
+        if (rc) return rc;
+    } else if (logits) {
+        CK(m->api.download(logits, m->S(m->s_logits), (size_t)n * c.labels * 4, m->stream), "download logits");
+    } else {
+        CK(m->api.stream_sync(m->stream), "sync");
+    }
     if (hidden) {
         std::vector<uint16_t> row(c.hidden);
         size_t r = 0;
