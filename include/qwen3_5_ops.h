@@ -65,11 +65,11 @@ int cs1_add_rms_norm(void* residual, const void* delta, const void* w, void* out
 int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const void* w, void* out, int T, int H, int D,
                        float eps, void* stream);                  // ops.h:62
 int cs1_gdn_conv(const void* qkv, int ld, const void* w, void* q, void* k, void* v, int T, int key_dim,
-                 int value_dim, void* stream);                    // ops.h:68
+                 int value_dim, void* stream);                    // ops.h:67
 int cs1_gdn_conv_vector(const void* qkv, int ld, const void* w, void* q, void* k, void* v, int T, int key_dim,
-                        int value_dim, void* stream);             // ops.h:71
+                        int value_dim, void* stream);             // ops.h:70
 int cs1_gdn_conv_prefix(const void* qkv, const void* history, int ld, const void* w, void* q, void* k, void* v,
-                        int T, int key_dim, int value_dim, void* stream);   // ops.h:75
+                        int T, int key_dim, int value_dim, void* stream);   // ops.h:74
 // Additive: causal conv of `count` (<= 256) packed sequences in one launch. Every
 // sequence starts from zero history, or, if `history` is non-null, from the same three
 // pre-conv rows [3, ld] (the tail of a shared prefix). lengths: host array.
@@ -77,43 +77,43 @@ int cs1_gdn_conv_batch(const void* qkv, const void* history, int ld, const void*
                        const size_t* lengths, size_t count, int key_dim, int value_dim, void* stream);
 int cs1_attention_gated_shared(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
                                const void* prefix_k, const void* prefix_v, int suffix, int prefix, int Hq,
-                               int Hk, int Dh, float scale, void* stream);   // ops.h:79
+                               int Hk, int Dh, float scale, void* stream);   // ops.h:78
 int cs1_attention_gated_shared_batch(const void* q, const void* k, const void* v, int ldv, const void* gate,
                                      void* out, const void* prefix_k, const void* prefix_v,
                                      const size_t* lengths, size_t count, int prefix, int Hq, int Hk, int Dh,
-                                     float scale, void* stream);  // ops.h:86
+                                     float scale, void* stream);  // ops.h:85
 int cs1_attention_gated_batch(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
                               const size_t* lengths, size_t count, int Hq, int Hk, int Dh, float scale,
-                              void* stream);                      // ops.h:93
+                              void* stream);                      // ops.h:92
 int cs1_gdn_gates(const void* b, const void* a, int ld, const void* A_log, const void* dt_bias, void* beta,
-                  float* g, int T, int H, void* stream);          // ops.h:99
-size_t cs1_gdn_batch_workspace_floats(int tokens, int H, int count);   // ops.h:105
+                  float* g, int T, int H, void* stream);          // ops.h:98
+size_t cs1_gdn_batch_workspace_floats(int tokens, int H, int count);   // ops.h:104
 int cs1_gdn_prefill_batch(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
                           float* workspace, size_t workspace_bytes, const size_t* lengths, size_t count, int H,
-                          int HK, float scale, void* stream);     // ops.h:106
+                          int HK, float scale, void* stream);     // ops.h:105
 int cs1_gdn_prefill_batch_shared(const void* q, const void* k, const void* v, const float* g, const void* beta,
                                  void* o, float* workspace, size_t workspace_bytes, const size_t* lengths,
                                  size_t count, int H, int HK, float scale, const void* state,
-                                 void* stream);                   // ops.h:110
-size_t cs1_gdn_workspace_floats(int T, int H);                    // ops.h:113
-void* cs1_gdn_fp32_create(size_t workspace_bytes);                // ops.h:116
-void cs1_gdn_fp32_destroy(void* context);                         // ops.h:117
-size_t cs1_gdn_fp32_workspace_floats(int T, int H);               // ops.h:118
+                                 void* stream);                   // ops.h:109
+size_t cs1_gdn_workspace_floats(int T, int H);                    // ops.h:112
+void* cs1_gdn_fp32_create(size_t workspace_bytes);                // ops.h:115
+void cs1_gdn_fp32_destroy(void* context);                         // ops.h:116
+size_t cs1_gdn_fp32_workspace_floats(int T, int H);               // ops.h:117
 int cs1_gdn_prefill_fp32(void* context, const void* q, const void* k, const void* v, const float* g,
                          const void* beta, void* o, float* workspace, int T, int H, int HK, float scale,
-                         void* stream);                           // ops.h:119
+                         void* stream);                           // ops.h:118
 // Additive: the FP32 operator with float32 output o [T,H,128] and an optional
 // explicit float32 state (s_in null = zero; s_out null = skip), [H,128,128].
 int cs1_gdn_prefill_fp32_x(void* context, const void* q, const void* k, const void* v, const float* g,
                            const void* beta, float* o, float* workspace, int T, int H, int HK, float scale,
                            const float* s_in, float* s_out, void* stream);
 int cs1_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
-                    float* workspace, int T, int H, int HK, float scale, void* stream);   // ops.h:122
+                    float* workspace, int T, int H, int HK, float scale, void* stream);   // ops.h:121
 int cs1_gdn_prefill_wide(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
-                         float* workspace, int T, int H, int HK, float scale, void* stream);   // ops.h:127
+                         float* workspace, int T, int H, int HK, float scale, void* stream);   // ops.h:126
 int cs1_gdn_prefill_x(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
                       float* workspace, int T, int H, int HK, float scale, const void* s_in, void* s_out,
-                      void* stream);                              // ops.h:136
+                      void* stream);                              // ops.h:134
 // Additive: packed sequences with per-sequence initial states. state_in: null (zero),
 // or [count,H,128,128] float32 (state_stride 1) or one shared [H,128,128] (state_stride 0);
 // state_out: null or [count,H,128,128]. Workspace as cs1_gdn_batch_workspace_floats.
@@ -123,38 +123,38 @@ int cs1_gdn_prefill_batch_x(const void* q, const void* k, const void* v, const f
                             void* state_out, void* stream);
 int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const void* kw, const void* cos,
                   const void* sin, void* q, void* gate, void* k, int T, int Hq, int Hk, int Dh, int half,
-                  float eps, void* stream);                       // ops.h:143
+                  float eps, void* stream);                       // ops.h:141
 int cs1_attention(const void* q, const void* k, const void* v, int ldv, void* out, int T, int Hq, int Hk, int Dh,
-                  float scale, void* stream);                     // ops.h:149
+                  float scale, void* stream);                     // ops.h:147
 int cs1_attention_gated(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out, int T,
-                        int Hq, int Hk, int Dh, float scale, void* stream);   // ops.h:155
+                        int Hq, int Hk, int Dh, float scale, void* stream);   // ops.h:153
 int cs1_attention_gated_bidirectional(const void* q, const void* k, const void* v, int ldv, const void* gate,
                                       void* out, int T, int Hq, int Hk, int Dh, float scale,
-                                      void* stream);              // ops.h:161
+                                      void* stream);              // ops.h:159
 int cs1_attention_gated_prefix_bidirectional(const void* q, const void* k, const void* v, int ldv,
                                              const void* gate, void* out, int T, int state, int Hq, int Hk,
-                                             int Dh, float scale, void* stream);   // ops.h:170
+                                             int Dh, float scale, void* stream);   // ops.h:167
 int cs1_attention_gated_prefix(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
-                               int T, int Hq, int Hk, int Dh, float scale, int q_base, void* stream);   // ops.h:177
-int cs1_sigmoid_gate(void* x, const void* gate, size_t n, void* stream);   // ops.h:182
-int cs1_silu_mul(const void* gate_up, int ld, void* out, int T, int I, void* stream);   // ops.h:185
+                               int T, int Hq, int Hk, int Dh, float scale, int q_base, void* stream);   // ops.h:174
+int cs1_sigmoid_gate(void* x, const void* gate, size_t n, void* stream);   // ops.h:179
+int cs1_silu_mul(const void* gate_up, int ld, void* out, int T, int I, void* stream);   // ops.h:182
 
 // GEMM handles (ops.h:187-217). The tcgen05 kernels need no library workspace and
 // reduce every output in an order independent of M, the row index and the tile
 // width, so every handle kind is row-invariant and all handles are compatible.
-void* cs1_gemm_create(size_t workspace_bytes);                    // ops.h:189
-void* cs1_gemm_create_fixed(size_t workspace_bytes, int reference_m);   // ops.h:195
-void* cs1_gemm_create_matched(size_t workspace_bytes, int reference_m);   // ops.h:199
-int cs1_gemm_compatible(void* ordinary, void* matched, int M, int N, int K);   // ops.h:200
-void cs1_gemm_destroy(void* gemm);                                // ops.h:201
-int cs1_gemm_enable_equivalent_tiles(void* gemm);                 // ops.h:206
-int cs1_gemm(void* gemm, const void* x, const void* w, void* y, int M, int N, int K, int ldy, void* stream);   // ops.h:207
+void* cs1_gemm_create(size_t workspace_bytes);                    // ops.h:186
+void* cs1_gemm_create_fixed(size_t workspace_bytes, int reference_m);   // ops.h:192
+void* cs1_gemm_create_matched(size_t workspace_bytes, int reference_m);   // ops.h:196
+int cs1_gemm_compatible(void* ordinary, void* matched, int M, int N, int K);   // ops.h:197
+void cs1_gemm_destroy(void* gemm);                                // ops.h:198
+int cs1_gemm_enable_equivalent_tiles(void* gemm);                 // ops.h:203
+int cs1_gemm(void* gemm, const void* x, const void* w, void* y, int M, int N, int K, int ldy, void* stream);   // ops.h:204
 int cs1_gemm_packed(void* gemm, const void* x, const void* w, void* y, const size_t* lengths, size_t count, int N,
-                    int K, void* stream);                         // ops.h:211
+                    int K, void* stream);                         // ops.h:208
 int cs1_gemm_reuse_check(void* gemm, const size_t* original_rows, size_t originals, const size_t* target_rows,
-                         size_t targets, int N, int K);           // ops.h:217
+                         size_t targets, int N, int K);           // ops.h:214
 int cs1_gemm_reuse(void* gemm, const void* x, const void* w, void* y, int M, int N, int K, int original_M,
-                   void* stream);                                 // ops.h:219
+                   void* stream);                                 // ops.h:216
 // Additive: residual[M,N] (rows of ldr) = bf16(residual + bf16(x w^T)), the decoder
 // residual add fused into the projection epilogue.
 int cs1_gemm_residual(void* gemm, const void* x, const void* w, void* residual, int M, int N, int K, int ldr,
@@ -185,6 +185,11 @@ int cs1_vision_norm(const void* x, const void* w, const void* b, void* y, int ro
 int cs1_vision_position(void* x, const void* table, const int* indices, const float* weights, int n, void* stream);
 int cs1_vision_rope(const void* qkv, const float* co, const float* si, void* q, void* k, int n, void* stream);
 int cs1_vision_attention(const void* q, const void* k, const void* v, void* out, int n, void* stream);
+int cs1_vision_bias(void* x, const void* bias, size_t n, int d, void* stream);               // ops.h:233
+int cs1_vision_gelu(void* x, size_t n, int exact, void* stream);                             // ops.h:234
+int cs1_vision_add(void* x, const void* delta, size_t n, void* stream);                      // ops.h:235
+int cs1_vision_to_float(const void* x, float* out, size_t n, void* stream);                  // ops.h:236
+int cs1_vision_lora_add(void* x, const float* delta, size_t n, float scale, void* stream);   // ops.h:237
 
 #ifdef __cplusplus
 }

@@ -144,5 +144,10 @@ int cs1_vision_rope(const void*, const float*, const float*, void*, void*, int, 
     return cudaErrorNotSupported;
 }
 int cs1_vision_attention(const void*, const void*, const void*, void*, int, void*) { return cudaErrorNotSupported; }
+int cs1_vision_bias(void*, const void*, size_t, int, void*) { return cudaErrorNotSupported; }
+int cs1_vision_gelu(void*, size_t, int, void*) { return cudaErrorNotSupported; }
+int cs1_vision_add(void*, const void*, size_t, void*) { return cudaErrorNotSupported; }
+int cs1_vision_to_float(const void*, float*, size_t, void*) { return cudaErrorNotSupported; }
+int cs1_vision_lora_add(void*, const float*, size_t, float, void*) { return cudaErrorNotSupported; }
 
 }  // extern "C"

@@ -91,6 +91,11 @@ SIGNATURES = {
     "cs1_vision_position": (I, [P, P, P, P, I, P]),
     "cs1_vision_rope": (I, [P, P, P, P, P, I, P]),
     "cs1_vision_attention": (I, [P, P, P, P, I, P]),
+    "cs1_vision_bias": (I, [P, P, Z, I, P]),
+    "cs1_vision_gelu": (I, [P, Z, I, P]),
+    "cs1_vision_add": (I, [P, P, Z, P]),
+    "cs1_vision_to_float": (I, [P, P, Z, P]),
+    "cs1_vision_lora_add": (I, [P, P, Z, F, P]),
 }
 
 # Functions whose int return is a size or a boolean-like status, not an error code.
