@@ -128,9 +128,60 @@ def cpu_sample(tokens=256, seed=0):
     return 1.0 / (per_token_period * 16), dt, threads
 
 
+def reference_cuda(args, local):
+    """The reference's own CUDA library (built from its sources by oracle/Makefile into
+    oracle/_ref/, recompiled for sm_100a: cuBLASLt GEMMs, mma.sync attention and GDN)
+    driven by the same C++ host on the same GPU, on the same 32 requests split into
+    launches the way the reference executor packs them (<= 16 prompts, <= 4096 tokens,
+    open_jev batching.rs:9-25). Returns a dict, or None when the library is absent."""
+    ref = os.path.join(ROOT, "oracle", "_ref", "libqwen3_5_cuda.so")
+    if not os.path.exists(ref):
+        return None
+    import torch
+    from s1omni import Model, lib_path, pack_ranges, preset
+    torch.cuda.set_device(local)
+    cfg = preset("27b")
+    seqs = requests(0)
+    tokens = int(sum(len(s) for s in seqs))
+    ranges = pack_ranges([len(s) for s in seqs], 16, 4096)
+    cap = max(sum(len(s) for s in seqs[a:b]) for a, b in ranges) + 64
+    m = Model(cfg, device=local, max_tokens=cap, max_seqs=16, cs1_library=ref + ";" + lib_path())
+    m.init_random(seed=1234, std=0.02)
+    stream = torch.cuda.ExternalStream(m.stream)
+
+    def step():
+        out = []
+        for a, b in ranges:
+            out.append(m.forward(seqs[a:b]))
+        return np.concatenate(out)
+    logits = step()
+    for _ in range(max(1, args.warmup - 1)):
+        step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    n = max(1, min(args.steps, 3))
+    for _ in range(n):
+        step()
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1e3 / n
+    m.close()
+    del stream
+    return {"value": tokens / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "launch_ranges": len(ranges),
+            "library": "reference src/backends/cuda/qwen3_5 built for sm_100a (oracle/Makefile)",
+            "host": "this build's C++ host, eager, host-side scorer head (the reference's executor path)",
+            "timing": "wall clock around synchronous forward calls (host copies included)",
+            "logits_sample": logits[:4].round(4).tolist()}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
+    ref_cuda = None
+    if not args.no_ref_cuda:
+        try:
+            ref_cuda = reference_cuda(args, int(os.environ.get("LOCAL_RANK", 0)))
+        except Exception as e:  # reported, not fatal: the CPU arm is the contract
+            ref_cuda = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     vals = []
     for _ in range(args.warmup):
         cpu_sample(args.cpu_tokens)
@@ -146,6 +197,7 @@ def run_reference(args, rank, world):
         "data": "synthetic", "config": {"workload": "27b-a-batch32", "model": "qwen3.5-27b-shape", "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_cuda_same_gpu": ref_cuda,
     }), flush=True)
 
 
@@ -277,7 +329,7 @@ def run_ours(args, rank, world, local):
                              "sample": f"one {args.cpu_tokens}-token prompt, one 4-layer period of the 27B shape "
                                        f"(numpy float32 restatement), x16 periods"},
             "clocks": clocks.summary(),
-            "checks": {"finite_logits_no_fault": ok},
+            "checks": {"finite_logits_no_fault": ok, "logits_sample": logits[:4].round(4).tolist()},
         }
     if dist:
         dist.barrier()
@@ -295,6 +347,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-ref-cuda", action="store_true")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))

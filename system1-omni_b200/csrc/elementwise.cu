@@ -40,8 +40,12 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const Pack8* __res
     }
 }
 
-// Eight channels per thread. The row's position inside its sequence decides which
-// taps read the three rows of `history` (shared by every sequence) or zeros.
+// Eight channels per thread over a run of CONV_ROWS consecutive rows: the weights are
+// loaded once and the three previous input rows slide through registers, so every input
+// row is read once. A run that crosses into a new sequence restarts its window from zeros
+// (or from the three rows of `history`, shared by every sequence).
+constexpr int CONV_ROWS = 32;
+
 __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
                                 bf16* __restrict__ v, int key_packs, int value_packs, SeqTable tab) {
@@ -56,36 +60,67 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
 #pragma unroll
         for (int e = 0; e < 8; e++) wt[(i * 8 + e) / 4][(i * 8 + e) % 4] = f[e];
     }
+    bf16* dst;
+    int dst_ld;
+    if (c < key_packs) {
+        dst = q + (size_t)c * 8;
+        dst_ld = key_packs * 8;
+    } else if (c < 2 * key_packs) {
+        dst = k + (size_t)(c - key_packs) * 8;
+        dst_ld = key_packs * 8;
+    } else {
+        dst = v + (size_t)(c - 2 * key_packs) * 8;
+        dst_ld = value_packs * 8;
+    }
     const int T = tab.offset[tab.count];
-    for (int t = blockIdx.y; t < T; t += gridDim.y) {
-        const int s = seq_of(tab, t);
+    const int t_begin = blockIdx.y * CONV_ROWS;
+    const int t_end = min(T, t_begin + CONV_ROWS);
+    if (t_begin >= T) return;
+    int s = seq_of(tab, t_begin);
+    int next = tab.offset[s + 1];
+    float x1[8], x2[8], x3[8];  // rows t-3, t-2, t-1
+    auto window = [&](int t) {
+        // load the three rows before t inside its sequence (history or zeros before the start)
         const int pos = t - tab.offset[s];
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            const int back = 3 - j;
-            const bf16* src = nullptr;
-            if (pos >= back)
-                src = qkv + (size_t)(t - back) * ld + (size_t)c * 8;
-            else if (history)
-                src = history + (size_t)(3 - back + pos) * ld + (size_t)c * 8;
-            if (src) {
-                float x[8];
-                unpack8(ld8(src), x);
+        for (int back = 3; back >= 1; back--) {
+            float* dstw = back == 3 ? x1 : back == 2 ? x2 : x3;
+            if (pos >= back) {
+                unpack8(ld8(qkv + (size_t)(t - back) * ld + (size_t)c * 8), dstw);
+            } else if (history) {
+                unpack8(ld8(history + (size_t)(3 - back + pos) * ld + (size_t)c * 8), dstw);
+            } else {
 #pragma unroll
-                for (int e = 0; e < 8; e++) acc[e] = fmaf(wt[e][j], x[e], acc[e]);
+                for (int e = 0; e < 8; e++) dstw[e] = 0.f;
             }
         }
+    };
+    window(t_begin);
+    for (int t = t_begin; t < t_end; t++) {
+        if (t == next) {
+            s++;
+            next = tab.offset[s + 1];
+            window(t);
+        }
+        float x0[8];
+        unpack8(ld8(qkv + (size_t)t * ld + (size_t)c * 8), x0);
         float y[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) y[e] = silu(rbf(acc[e]));
-        const Pack8 o = pack8(y);
-        if (c < key_packs)
-            st8(q + (size_t)t * key_packs * 8 + (size_t)c * 8, o);
-        else if (c < 2 * key_packs)
-            st8(k + (size_t)t * key_packs * 8 + (size_t)(c - key_packs) * 8, o);
-        else
-            st8(v + (size_t)t * value_packs * 8 + (size_t)(c - 2 * key_packs) * 8, o);
+        for (int e = 0; e < 8; e++) {
+            float acc = 0.f;
+            acc = fmaf(wt[e][0], x1[e], acc);
+            acc = fmaf(wt[e][1], x2[e], acc);
+            acc = fmaf(wt[e][2], x3[e], acc);
+            acc = fmaf(wt[e][3], x0[e], acc);
+            y[e] = silu(rbf(acc));
+        }
+        st8(dst + (size_t)t * dst_ld, pack8(y));
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            x1[e] = x2[e];
+            x2[e] = x3[e];
+            x3[e] = x0[e];
+        }
     }
 }
 
@@ -181,7 +216,7 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
                      aligned16(q) && aligned16(k) && aligned16(v) && (!history || aligned16(history));
     if (vec) {
         const int packs = (2 * key_dim + value_dim) / 8;
-        conv_vec_kernel<<<dim3((packs + 127) / 128, rows), 128, 0, st>>>(
+        conv_vec_kernel<<<dim3((packs + 127) / 128, (T + CONV_ROWS - 1) / CONV_ROWS), 128, 0, st>>>(
             static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld, static_cast<const bf16*>(w),
             static_cast<bf16*>(q), static_cast<bf16*>(k), static_cast<bf16*>(v), key_dim / 8, value_dim / 8, tab);
     } else {

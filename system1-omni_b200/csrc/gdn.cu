@@ -242,6 +242,307 @@ __global__ void __launch_bounds__(PREP_THREADS) gdn_prep(const bf16* __restrict_
     }
 }
 
+// ------------------------------------------------------- prep on tcgen05 ----
+// One CTA (256 threads, 2 per SM) per (chunk, head, sequence):
+//  1. cum = sequential fp32 cumsum of g; kn, qn = L2-normalised k and scaled q, rounded
+//     to TF32 and written as one [128 rows = kn | qn][128] fp32 operand tile (128B swizzle).
+//  2. MMA1 (kind::tf32, M=128, N=64, K=128): D[i][j] = [kn;qn]_i . kn_j into TMEM.
+//     Lanes 0..63 give A_ij = beta_i kk_ij e^{cum_i-cum_j} (j < i) into shared memory,
+//     lanes 64..127 give P_tj = qk_tj e^{cum_t-cum_j} (j <= t), stored bf16.
+//     Meanwhile warps 4..7 write qd, kd^T (global) and the MMA2 operands
+//     (k e^cum)^T and v^T (shared, bf16).
+//  3. T = (I + A)^-1 blockwise: 16x16 diagonal inverses by substitution, then block rows
+//     T_ij = -T_ii sum_k A_ik T_kj; tb = bf16(T diag(beta)).
+//  4. MMA2 (kind::f16, M=128, N=64, K=64): u^T = v^T tb^T, w^T = (k e^cum)^T tb^T; u^T
+//     rows go out directly, w is transposed through shared memory.
+constexpr int TP_THREADS = 256;
+constexpr int TP_KQ = 0;                         // 4 x [128][32 fp32] = 64 KB
+constexpr int TP_VT = 0;                         // after MMA1: v^T      [128][64] bf16, 16 KB
+constexpr int TP_KWT = 16384;                    //              (k e^cum)^T [128][64] bf16, 16 KB
+constexpr int TP_TB = 32768;                     //              tb      [64][64] bf16, 8 KB
+constexpr int TP_WST = 40960;                    //              w staging [64][136] bf16, 17 KB
+constexpr int TP_KQ_BYTES = 65536;
+constexpr int TP_A = TP_KQ_BYTES;                // A fp32 [64][65]
+constexpr int TP_T = TP_A + C * LDC * 4;         // T fp32 [64][65]
+constexpr int TP_VEC = TP_T + C * LDC * 4;       // cum, bet, ecum, erem, gg [64] each
+constexpr int TP_BAR = TP_VEC + 5 * C * 4;
+constexpr int TP_SMEM = TP_BAR + 64 + 1024;
+constexpr int WST_LD = 136;
+
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// Byte offset of fp32 element (row, col) in the [rows][128] fp32 tile stored as four
+// [rows][32] sub-tiles of 128-byte rows with the 128B swizzle; sub-tile stride `sub`.
+__device__ __forceinline__ uint32_t kq_off(int row, int col, int sub) {
+    return (uint32_t)((col >> 5) * sub) + sw128_offset(row, (col & 31) >> 2) + (uint32_t)((col & 3) << 2);
+}
+
+__global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                              const bf16* __restrict__ v, const float* __restrict__ g,
+                                                              const bf16* __restrict__ beta, Work ws, GdnTable tab,
+                                                              int H, int HK, float scale) {
+    const int seq = blockIdx.z;
+    const int start = tab.seq.offset[seq];
+    const int len = tab.seq.offset[seq + 1] - start;
+    const int c = blockIdx.x;
+    if (c * C >= len) return;
+    const int h = blockIdx.y, hk = h / (H / HK);
+    const long slot = (long)h * ws.slots + tab.chunk_base[seq] + c;
+    const int t0 = start + c * C;
+    const int n = min(C, len - c * C);
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* sm = smem_raw + (base - raw);
+    float* A = reinterpret_cast<float*>(sm + TP_A);
+    float* Tm = reinterpret_cast<float*>(sm + TP_T);
+    float* cum = reinterpret_cast<float*>(sm + TP_VEC);
+    float* bet = cum + C;
+    float* ecum = bet + C;
+    float* erem = ecum + C;
+    float* gg = erem + C;
+    const uint32_t bar = base + TP_BAR;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + TP_BAR + 16);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tmem_alloc(smem_u32(tmem_slot), 256);
+        tmem_relinquish();
+    }
+    if (tid < C) {
+        gg[tid] = tid < n ? g[(size_t)(t0 + tid) * H + h] : 0.f;
+        bet[tid] = tid < n ? f32(beta[(size_t)(t0 + tid) * H + h]) : 0.f;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (tid == 0) {
+        float s = 0.f;
+        for (int i = 0; i < C; i++) {
+            s += gg[i];
+            cum[i] = s;
+        }
+        ws.decay[slot] = expf(s);
+    }
+    // 1. normalised rows: warp per row, lane holds dims lane + 32e
+    for (int r = warp; r < C; r += TP_THREADS / 32) {
+        float kx[4], qx[4], ks = 0.f, qs = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int d = lane + 32 * e;
+            kx[e] = r < n ? f32(k[((size_t)(t0 + r) * HK + hk) * K + d]) : 0.f;
+            qx[e] = r < n ? f32(q[((size_t)(t0 + r) * HK + hk) * K + d]) : 0.f;
+            ks = fmaf(kx[e], kx[e], ks);
+            qs = fmaf(qx[e], qx[e], qs);
+        }
+        ks = warp_sum(ks);
+        qs = warp_sum(qs);
+        const float kinv = rsqrtf(ks + 1e-6f), qinv = rsqrtf(qs + 1e-6f) * scale;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int d = lane + 32 * e;
+            *reinterpret_cast<float*>(sm + TP_KQ + kq_off(r, d, 16384)) = tf32_rna(kx[e] * kinv);
+            *reinterpret_cast<float*>(sm + TP_KQ + kq_off(C + r, d, 16384)) = tf32_rna(qx[e] * qinv);
+        }
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid < C) {
+        ecum[tid] = expf(cum[tid]);
+        erem[tid] = expf(cum[C - 1] - cum[tid]);
+    }
+    if (tid == 0) {
+        tc_fence_after();
+        constexpr uint32_t ID = idesc(128, 64, AB_TF32);
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++) {
+            const uint32_t a = base + TP_KQ + (uint32_t)(kk >> 2) * 16384 + (uint32_t)(kk & 3) * 32;
+            mma_tf32(tmem, desc_sw128(a), desc_sw128(a), ID, kk > 0);
+        }
+        mma_commit(bar);
+    }
+    __syncthreads();  // ecum / erem visible
+    bool ok = true;
+    if (warp < 4) {
+        // 2a. A rows (lanes 0..63) and P rows (lanes 64..127) from TMEM
+        if (!mbar_wait(bar, 0)) {
+            if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+            ok = false;
+        }
+        tc_fence_after();
+        const int i = tid;  // TMEM lane
+        float d[64];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), *reinterpret_cast<float(*)[32]>(d));
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + 32, *reinterpret_cast<float(*)[32]>(d + 32));
+        tmem_ld_wait();
+        if (i < C) {
+#pragma unroll
+            for (int j = 0; j < C; j++) A[i * LDC + j] = j < i ? bet[i] * d[j] * expf(cum[i] - cum[j]) : 0.f;
+        } else {
+            const int t = i - C;
+            bf16* P = static_cast<bf16*>(ws.p) + slot * C * C + (size_t)t * C;
+#pragma unroll
+            for (int j8 = 0; j8 < C / 8; j8++) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const int j = j8 * 8 + e;
+                    f[e] = j <= t ? d[j] * expf(cum[t] - cum[j]) : 0.f;
+                }
+                st8(P + j8 * 8, pack8(f));
+            }
+        }
+    } else {
+        // 2b. qd [t][d] and kd^T [d][t] to global (units of 8 consecutive elements)
+        const int w4 = tid - 128;
+        bf16* QD = static_cast<bf16*>(ws.qd) + slot * C * K;
+        bf16* KDT = static_cast<bf16*>(ws.kdt) + slot * K * C;
+        for (int u = w4; u < C * K / 8; u += 128) {
+            const int t = u / (K / 8), d0 = (u % (K / 8)) * 8;
+            float f[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) f[e] = *reinterpret_cast<const float*>(sm + TP_KQ + kq_off(C + t, d0 + e, 16384)) * ecum[t];
+            st8(QD + (size_t)t * K + d0, pack8(f));
+            const int dd = u / (C / 8), tt0 = (u % (C / 8)) * 8;
+#pragma unroll
+            for (int e = 0; e < 8; e++) f[e] = *reinterpret_cast<const float*>(sm + TP_KQ + kq_off(tt0 + e, dd, 16384)) * erem[tt0 + e];
+            st8(KDT + (size_t)dd * C + tt0, pack8(f));
+        }
+    }
+    __syncthreads();  // MMA1 done reading the KQ tile (all threads waited or fell through); A complete
+    // The KQ region is reused from here: build (k e^cum)^T and v^T in it. kn is still needed, so
+    // stage it first: each thread keeps its units in registers.
+    {
+        // (k e^cum)^T [d][j] and v^T [v][j], units of (row, 8 consecutive j): 1024 units each
+        float kw[4][8];
+        for (int i = 0; i < 4; i++) {
+            const int u = tid + i * TP_THREADS;
+            const int dd = u / (C / 8), j0 = (u % (C / 8)) * 8;
+#pragma unroll
+            for (int e = 0; e < 8; e++)
+                kw[i][e] = rbf(*reinterpret_cast<const float*>(sm + TP_KQ + kq_off(j0 + e, dd, 16384)) * ecum[j0 + e]);
+        }
+        __syncthreads();
+        for (int i = 0; i < 4; i++) {
+            const int u = tid + i * TP_THREADS;
+            const int dd = u / (C / 8), j0 = (u % (C / 8)) * 8;
+            *reinterpret_cast<Pack8*>(sm + TP_KWT + sw128_offset(dd, j0 >> 3)) = pack8(kw[i]);
+            float vv[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) vv[e] = j0 + e < n ? f32(v[((size_t)(t0 + j0 + e) * H + h) * V + dd]) : 0.f;
+            *reinterpret_cast<Pack8*>(sm + TP_VT + sw128_offset(dd, j0 >> 3)) = pack8(vv);
+        }
+    }
+    // 3. T = (I + A)^-1. Diagonal 16x16 blocks: one thread per (block, column).
+    if (tid < C) {
+        const int b = tid >> 4, col = tid & 15, o = b * 16;
+        float x[16];
+#pragma unroll
+        for (int r = 0; r < 16; r++) {
+            float acc = r == col ? 1.f : 0.f;
+#pragma unroll
+            for (int m = 0; m < r; m++) acc = fmaf(-A[(o + r) * LDC + o + m], x[m], acc);
+            x[r] = r < col ? 0.f : acc;
+        }
+#pragma unroll
+        for (int r = 0; r < 16; r++) Tm[(o + r) * LDC + o + col] = x[r];
+    }
+    // zero the strictly-upper blocks
+    for (int x = tid; x < C * C; x += TP_THREADS) {
+        const int i = x / C, j = x % C;
+        if ((j >> 4) > (i >> 4)) Tm[i * LDC + j] = 0.f;
+    }
+    __syncthreads();
+    // Block rows 1..3: S_j = sum_{k=j}^{i-1} A_ik T_kj, then T_ij = -T_ii S_j.
+    float* S = reinterpret_cast<float*>(sm + TP_WST);  // scratch [3][16][16]
+    for (int bi = 1; bi < 4; bi++) {
+        for (int x = tid; x < bi * 256; x += TP_THREADS) {
+            const int bj = x >> 8, r = (x >> 4) & 15, cc = x & 15;
+            float acc = 0.f;
+            for (int m = bj * 16; m < bi * 16; m++) acc = fmaf(A[(bi * 16 + r) * LDC + m], Tm[m * LDC + bj * 16 + cc], acc);
+            S[x] = acc;
+        }
+        __syncthreads();
+        for (int x = tid; x < bi * 256; x += TP_THREADS) {
+            const int bj = x >> 8, r = (x >> 4) & 15, cc = x & 15;
+            float acc = 0.f;
+            for (int m = 0; m <= r; m++) acc = fmaf(Tm[(bi * 16 + r) * LDC + bi * 16 + m], S[(bj << 8) + (m << 4) + cc], acc);
+            Tm[(bi * 16 + r) * LDC + bj * 16 + cc] = -acc;
+        }
+        __syncthreads();
+    }
+    // tb = bf16(T diag(beta)) as the [64 t][64 j] operand tile
+    for (int u = tid; u < C * C / 8; u += TP_THREADS) {
+        const int t = u >> 3, j0 = (u & 7) * 8;
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) f[e] = Tm[t * LDC + j0 + e] * bet[j0 + e];
+        *reinterpret_cast<Pack8*>(sm + TP_TB + sw128_offset(t, j0 >> 3)) = pack8(f);
+    }
+    fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+        tc_fence_after();
+        constexpr uint32_t ID = idesc(128, 64, AB_BF16);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            const uint32_t off = (uint32_t)kk * 32;
+            const uint64_t b = desc_sw128(base + TP_TB + off);
+            mma_bf16(tmem + 64, desc_sw128(base + TP_VT + off), b, ID, kk > 0);
+            mma_bf16(tmem + 128, desc_sw128(base + TP_KWT + off), b, ID, kk > 0);
+        }
+        mma_commit(bar);
+    }
+    __syncwarp();
+    if (!mbar_wait(bar, 1)) {
+        if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+        ok = false;
+    }
+    tc_fence_after();
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;  // TMEM lane = v (u^T) or d (w^T)
+    bf16* wst = reinterpret_cast<bf16*>(sm + TP_WST);
+    {
+        float x[64];
+        const uint32_t col = warp < 4 ? 64u : 128u;
+        tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + col, *reinterpret_cast<float(*)[32]>(x));
+        tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + col + 32, *reinterpret_cast<float(*)[32]>(x + 32));
+        tmem_ld_wait();
+        if (warp < 4) {
+            bf16* UT = static_cast<bf16*>(ws.ut) + (slot * V + row) * C;
+#pragma unroll
+            for (int j8 = 0; j8 < 8; j8++) st8(UT + j8 * 8, pack8(x + j8 * 8));
+        } else {
+#pragma unroll
+            for (int t = 0; t < C; t++) wst[t * WST_LD + row] = to_bf16(x[t]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    {
+        bf16* W = static_cast<bf16*>(ws.w) + slot * C * K;
+        for (int u = tid; u < C * K / 8; u += TP_THREADS) {
+            const int t = u >> 4, d0 = (u & 15) * 8;
+            st8(W + (size_t)t * K + d0, *reinterpret_cast<const Pack8*>(wst + t * WST_LD + d0));
+        }
+    }
+    (void)ok;
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 256);
+    }
+}
+
 // ---------------------------------------------------------------- scan ----
 // 160 threads: warps 0..3 own TMEM lanes / value columns 0..127, warp 4 lane 0
 // issues TMA and MMA. Shared memory (1024-aligned tiles, 128B swizzle):
@@ -491,7 +792,7 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     if ((size_t)L.total > workspace_bytes) return cudaErrorInvalidValue;
     if ((reinterpret_cast<uintptr_t>(workspace) & 1023) != 0) return cudaErrorInvalidValue;
     static const cudaError_t configured = [] {
-        cudaError_t e = cudaFuncSetAttribute(gdn_prep<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
+        cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(gdn_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM);
         return e;
@@ -499,7 +800,7 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     if (configured != cudaSuccess) return configured;
     uint8_t* b = static_cast<uint8_t*>(workspace);
     Work ws{b + L.w, b + L.qd, b + L.p, b + L.kdt, b + L.ut, reinterpret_cast<float*>(b + L.decay), slots};
-    gdn_prep<false><<<dim3(tab.max_chunks, H, seqs.count), PREP_THREADS, PREP_SMEM, st>>>(
+    gdn_prep_tc<<<dim3(tab.max_chunks, H, seqs.count), TP_THREADS, TP_SMEM, st>>>(
         static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), g,
         static_cast<const bf16*>(beta), ws, tab, H, HK, scale);
     cudaError_t e = cudaGetLastError();

@@ -15,6 +15,7 @@
 
 #include <dlfcn.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -887,10 +888,26 @@ __attribute__((visibility("default"))) int s1_model_init_random(void* mp, uint64
         CK(m->api.fill_random(m->W(r), r.elems, kind, k, a, b, r.f32 ? 1 : 0, m->stream), "random fill");
         return 0;
     };
+    // gate and up rows are drawn per logical 128-row block, so the stacked (gate | up) and
+    // the interleaved (fused SwiGLU) layouts hold the same logical weights
+    auto fill_gate_up = [&](const Layer& L) -> int {
+        const size_t H = m->cfg.hidden, I = m->cfg.intermediate, blk = 128;
+        const uint64_t kg = (k += 0xD1B54A32D192ED03ull), ku = (k += 0xD1B54A32D192ED03ull);
+        for (size_t b = 0; b * blk < I; b++) {
+            const size_t rows = std::min(blk, I - b * blk);
+            const size_t gate_row = m->fused ? 2 * blk * b : blk * b;
+            const size_t up_row = m->fused ? 2 * blk * b + blk : I + blk * b;
+            CK(m->api.fill_random(m->W(L.gate_up) + gate_row * H * 2, rows * H, 0, kg + b, 0.f, std_, 0, m->stream),
+               "random fill");
+            CK(m->api.fill_random(m->W(L.gate_up) + up_row * H * 2, rows * H, 0, ku + b, 0.f, std_, 0, m->stream),
+               "random fill");
+        }
+        return 0;
+    };
     int rc = fill(m->embed, 0, 0.f, std_);
     for (const Layer& L : m->layers) {
         if (rc) return rc;
-        rc = fill(L.input_norm, 0, 0.f, 0.1f) || fill(L.post_norm, 0, 0.f, 0.1f) || fill(L.gate_up, 0, 0.f, std_) ||
+        rc = fill(L.input_norm, 0, 0.f, 0.1f) || fill(L.post_norm, 0, 0.f, 0.1f) || fill_gate_up(L) ||
              fill(L.down, 0, 0.f, std_);
         if (rc) return rc;
         if (L.type == 0)

@@ -132,13 +132,18 @@ class Cs1:
             raise FileNotFoundError(f"{path} is missing: run system1-omni_b200/build.py")
         self.path = path
         self.raw = ctypes.CDLL(path)
+        self.missing = set()
         for name, (res, args) in SIGNATURES.items():
-            fn = getattr(self.raw, name)
+            try:
+                fn = getattr(self.raw, name)
+            except AttributeError:  # optional / additive symbol absent from this library
+                self.missing.add(name)
+                continue
             fn.restype = res
             fn.argtypes = args
 
     def __getattr__(self, name):
-        if name not in SIGNATURES:
+        if name not in SIGNATURES or name in self.__dict__.get("missing", ()):
             raise AttributeError(name)
         fn = getattr(self.raw, name)
         res = SIGNATURES[name][0]
