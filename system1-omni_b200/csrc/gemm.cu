@@ -23,6 +23,7 @@
 //   cs1_gemm_swiglu:   out = bf16(bf16(silu(gate)) * up), with gate and up rows of w
 //                      interleaved in blocks of 128 (SwiGLU of the MLP)
 #include <algorithm>
+#include <cstdlib>
 #include <new>
 
 #include "common.cuh"
@@ -276,6 +277,249 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cta_group::2): a cluster of two CTAs on two SMs computes a
+// 256 x 256 tile. Each CTA loads its own 128 rows of A and one half (128 rows) of B
+// per stage (32 KB instead of 48 KB for the same per-SM MMA work), the even (leader)
+// CTA issues M=256 N=256 MMAs that read both CTAs' shared memory, and each CTA holds
+// its 128 accumulator rows in its own tensor memory for its own epilogue.
+//   - TMA completions of both CTAs count on the leader's full barrier;
+//   - the leader's commits arrive on both CTAs' empty / tmem-full barriers (multicast
+//     commit, no multicast loads);
+//   - both CTAs' epilogue warps arrive on the leader's tmem-empty barrier.
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = 128 * BK * 2;
+constexpr int P_B_BYTES = 128 * BK * 2;
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_BAR_OFFSET = P_STAGES * P_STAGE_BYTES;
+constexpr int P_SMEM = P_BAR_OFFSET + 256 + 1024;
+constexpr int P_GROUP_M = 8;
+
+__device__ __forceinline__ void pair_tile_coords(int t, int tiles_m, int tiles_n, int& m, int& n) {
+    const int per_group = P_GROUP_M * tiles_n;
+    const int group = t / per_group;
+    const int first = group * P_GROUP_M;
+    const int gm = min(P_GROUP_M, tiles_m - first);
+    const int r = t - group * per_group;
+    m = first + r % gm;
+    n = r / gm;
+}
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p) {
+    constexpr int BN = 256;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + P_BAR_OFFSET;
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (P_STAGES + s); };
+    auto tfull = [&](int a) { return bars + 8u * (2 * P_STAGES + a); };
+    auto tempty = [&](int a) { return bars + 8u * (2 * P_STAGES + 2 + a); };
+    const uint32_t drain = bars + 8u * (2 * P_STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + P_BAR_OFFSET + 8 * (2 * P_STAGES + 5));
+
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_tiles = p.tiles_m * p.tiles_n;
+    const int KB = (p.K + BK - 1) / BK;
+    const int cid = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 8);
+        }
+        mbar_init(drain, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), 2 * BN);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers initialised before any remote arrive or TMA completion
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int t = cid; t < num_tiles && ok; t += nclusters) {
+                int m, n;
+                pair_tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(empty(s), ph ^ 1)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t a_dst = base + s * P_STAGE_BYTES;
+                    if (leader) mbar_expect_tx(full(s), 2 * P_STAGE_BYTES);
+                    tma_load_2d_pair(a_dst, &map_a, full(s), kb * BK, m * 256 + (int)rank * 128);
+                    tma_load_2d_pair(a_dst + P_A_BYTES, &map_b, full(s), kb * BK, n * BN + (int)rank * 128);
+                    issued++;
+                    if (++s == P_STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            if (leader) {
+                // every load of both CTAs has landed (all complete on the leader's barriers)
+                const long pending = issued < P_STAGES ? issued : P_STAGES;
+                for (long i = 0; i < pending; i++) {
+                    if (--s < 0) {
+                        s = P_STAGES - 1;
+                        ph ^= 1;
+                    }
+                    (void)mbar_wait(full(s), ph);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            if (leader) {
+                constexpr uint32_t IDESC = idesc(256, BN, AB_BF16);
+                int s = 0, acc = 0;
+                uint32_t ph = 0, acc_ph = 0;
+                bool ok = true;
+                for (int t = cid; t < num_tiles && ok; t += nclusters) {
+                    if (!mbar_wait(tempty(acc), acc_ph ^ 1)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc * BN;
+                    for (int kb = 0; kb < KB; kb++) {
+                        if (!mbar_wait(full(s), ph)) {
+                            atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = base + s * P_STAGE_BYTES;
+                        const uint64_t ad = desc_sw128(a_addr), bd = desc_sw128(a_addr + P_A_BYTES);
+#pragma unroll
+                        for (int k = 0; k < BK / 16; k++)
+                            mma_bf16_pair(d, ad + 2 * k, bd + 2 * k, IDESC, (kb | k) != 0);
+                        mma_commit_pair(empty(s), 3);
+                        if (++s == P_STAGES) {
+                            s = 0;
+                            ph ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit_pair(tfull(acc), 3);
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_ph ^= 1;
+                    }
+                }
+                mma_commit_pair(drain, 3);
+            }
+            // both CTAs: the leader's MMAs (which write this CTA's tensor memory) are done
+            (void)mbar_wait(drain, 0);
+        }
+    } else {
+        const int q = warp & 3;
+        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+        const uint32_t leader_tempty0 = map_to_rank(tempty(0), 0), leader_tempty1 = map_to_rank(tempty(1), 0);
+        int acc = 0;
+        uint32_t acc_ph = 0;
+        for (int t = cid; t < num_tiles; t += nclusters) {
+            int m, n;
+            pair_tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+            if (!mbar_wait(tfull(acc), acc_ph)) {
+                if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            const int row = m * 256 + (int)rank * 128 + q * 32 + lane;
+            const bool row_ok = row < p.M;
+            const uint32_t tcol = lane_addr + acc * BN;
+            if constexpr (EPI == EPI_SWIGLU) {
+                const int out_col0 = n * (BN / 2);
+                const int out_n = p.N / 2;
+#pragma unroll 1
+                for (int c = 0; c < BN / 64; c++) {
+                    float g[32], u[32];
+                    tmem_ld32(tcol + c * 32, g);
+                    tmem_ld32(tcol + BN / 2 + c * 32, u);
+                    tmem_ld_wait();
+                    const int col = out_col0 + c * 32;
+                    if (row_ok) {
+                        bf16* dst = p.y + (size_t)row * p.ldy + col;
+#pragma unroll
+                        for (int v = 0; v < 4; v++) {
+                            if (col + v * 8 + 8 <= out_n) {
+                                float o[8];
+#pragma unroll
+                                for (int e = 0; e < 8; e++) o[e] = rbf(silu(rbf(g[v * 8 + e]))) * rbf(u[v * 8 + e]);
+                                st8(dst + v * 8, pack8(o));
+                            }
+                        }
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    float v[32];
+                    tmem_ld32(tcol + c * 32, v);
+                    tmem_ld_wait();
+                    const int col = n * BN + c * 32;
+                    if (row_ok) {
+                        bf16* dst = p.y + (size_t)row * p.ldy + col;
+#pragma unroll
+                        for (int g8 = 0; g8 < 4; g8++) {
+                            if (col + g8 * 8 + 8 <= p.N) {
+                                float o[8];
+                                if constexpr (EPI == EPI_RESIDUAL) {
+                                    float r[8];
+                                    unpack8(ld8(dst + g8 * 8), r);
+#pragma unroll
+                                    for (int e = 0; e < 8; e++) o[e] = r[e] + rbf(v[g8 * 8 + e]);
+                                } else {
+#pragma unroll
+                                    for (int e = 0; e < 8; e++) o[e] = v[g8 * 8 + e];
+                                }
+                                st8(dst + g8 * 8, pack8(o));
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+            if (++acc == 2) {
+                acc = 0;
+                acc_ph ^= 1;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 2 * BN);
+    }
+}
+
 // Any shape: one thread per output, fp32 accumulation in K order. Used only when
 // a shape or pointer misses the tensor-map alignment rules.
 template <int EPI>
@@ -308,6 +552,7 @@ struct Handle {
     int device = 0;
     int sms = 148;
     int fixed_m = 0;
+    bool pairs = true;  // CTA-pair kernels for large M (S1_GEMM_PAIRS=0 selects the single-CTA kernels)
 };
 
 template <int BN, int EPI>
@@ -337,6 +582,32 @@ int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int
     return cudaGetLastError();
 }
 
+template <int EPI>
+int launch_pair(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy,
+                cudaStream_t st) {
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    if (configured != cudaSuccess) return configured;
+    CUtensorMap ma, mb;
+    int e = host::make_map_2d(&ma, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, K, 128, BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    e = host::make_map_2d(&mb, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, 128, BK, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    Params p;
+    p.y = static_cast<bf16*>(y);
+    p.ldy = ldy;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.tiles_m = (M + 255) / 256;
+    p.tiles_n = (N + 255) / 256;
+    const int tiles = p.tiles_m * p.tiles_n;
+    const int grid = 2 * std::min(tiles, h->sms / 2);
+    gemm_pair_kernel<EPI><<<grid, THREADS, P_SMEM, st>>>(ma, mb, p);
+    return cudaGetLastError();
+}
+
 int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int epi,
         cudaStream_t st) {
     if (!h || M < 0 || N <= 0 || K <= 0 || !x || !w || !y) return cudaErrorInvalidValue;
@@ -361,6 +632,18 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
                     static_cast<const bf16*>(w), static_cast<bf16*>(y), ldy, M, N, K);
         }
         return cudaGetLastError();
+    }
+    // CTA pairs (256 x 256 tiles) when there are enough tiles to fill the SMs in pairs.
+    const long pair_tiles = (long)((M + 255) / 256) * ((N + 255) / 256);
+    if (h->pairs && pair_tiles >= h->sms / 2) {
+        switch (epi) {
+            case EPI_SWIGLU:
+                return launch_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);
+            case EPI_RESIDUAL:
+                return launch_pair<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st);
+            default:
+                return launch_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, st);
+        }
     }
     // 256-wide tiles unless that leaves most SMs idle.
     const long tiles256 = (long)((M + BM - 1) / BM) * ((N + 255) / 256);
@@ -393,6 +676,8 @@ void* cs1_gemm_create(size_t workspace_bytes) {
         return nullptr;
     }
     h->sms = host::num_sms();
+    const char* env = getenv("S1_GEMM_PAIRS");
+    h->pairs = !(env && env[0] == '0');
     return h;
 }
 

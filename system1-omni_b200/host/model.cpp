@@ -82,6 +82,10 @@ struct Api {
     int (*attention_gated_shared_batch)(const void*, const void*, const void*, int, const void*, void*, const void*,
                                         const void*, const size_t*, size_t, int, int, int, int, float,
                                         void*) = nullptr;
+    int (*attention_gated_batch)(const void*, const void*, const void*, int, const void*, void*, const size_t*,
+                                 size_t, int, int, int, float, void*) = nullptr;
+    // most sequences one batched launch takes: 256 in this build, 16 in the reference (ops.h:83-94)
+    int max_batch = 16;
     int (*gemm_residual)(void*, const void*, const void*, void*, int, int, int, int, void*) = nullptr;
     int (*gemm_swiglu)(void*, const void*, const void*, void*, int, int, int, int, void*) = nullptr;
     int (*head_score)(const void*, int, const int32_t*, int, const float*, const float*, int, int, float*,
@@ -161,10 +165,12 @@ bool load_api(const char* spec, Api& a, std::string& err) {
     bind(h, "cs1_gdn_conv_batch", a.gdn_conv_batch, false, err);
     bind(h, "cs1_gdn_prefill_batch_x", a.gdn_prefill_batch_x, false, err);
     bind(h, "cs1_attention_gated_shared_batch", a.attention_gated_shared_batch, false, err);
+    bind(h, "cs1_attention_gated_batch", a.attention_gated_batch, false, err);
     bind(h, "cs1_gemm_residual", a.gemm_residual, false, err);
     bind(h, "cs1_gemm_swiglu", a.gemm_swiglu, false, err);
     bind(h, "cs1_head_score", a.head_score, false, err);
     bind(h, "cs1_fill_random", a.fill_random, false, err);
+    a.max_batch = a.gdn_prefill_batch_x ? 256 : 16;
     if (!a.fill_random && !aux.empty()) {
         void* ah = dlopen(aux.c_str(), RTLD_NOW | RTLD_LOCAL);
         if (ah) bind(ah, "cs1_fill_random", a.fill_random, false, err);
@@ -412,7 +418,7 @@ int run_layers(Model* m, const Batch& b) {
             const int ld = m->gdn_in;
             uint8_t* gin = m->S(m->s_gdn_in);
             const void* hist = suffix ? m->prefix_buf + m->p_tail[gi] : nullptr;
-            if (m->api.gdn_conv_batch) {
+            if (m->api.gdn_conv_batch && n <= m->api.max_batch) {
                 m->launches++;
                 CK(m->api.gdn_conv_batch(gin, hist, ld, m->W(L.conv), m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
                                          b.lengths.data(), n, m->kd, m->vd, m->stream),
@@ -444,7 +450,7 @@ int run_layers(Model* m, const Batch& b) {
             float* ws = reinterpret_cast<float*>(m->S(m->s_ws));
             const void* s_in = suffix ? m->prefix_buf + m->p_state[gi] : nullptr;
             void* s_out = b.capture ? m->prefix_buf + m->p_state[gi] : nullptr;
-            if (m->api.gdn_prefill_batch_x) {
+            if (m->api.gdn_prefill_batch_x && n <= m->api.max_batch) {
                 m->launches += 2;
                 CK(m->api.gdn_prefill_batch_x(m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
                                               reinterpret_cast<const float*>(m->S(m->s_g)), m->S(m->s_beta),
@@ -498,13 +504,18 @@ int run_layers(Model* m, const Batch& b) {
                "attention prep");
             const void* pk = suffix ? m->prefix_buf + m->p_k[ai] : nullptr;
             const void* pv = suffix ? m->prefix_buf + m->p_v[ai] : nullptr;
-            if (m->api.attention_gated_shared_batch) {
+            if (suffix && m->api.attention_gated_shared_batch && n <= m->api.max_batch) {
                 m->launches++;
                 CK(m->api.attention_gated_shared_batch(m->S(m->s_aq), m->S(m->s_ak), vptr, ld, m->S(m->s_agate),
-                                                       m->S(m->s_ao), pk, pv, b.lengths.data(), n,
-                                                       suffix ? b.prefix : 0, c.heads, c.kv_heads, c.head_dim,
-                                                       attn_scale, m->stream),
-                   "attention");
+                                                       m->S(m->s_ao), pk, pv, b.lengths.data(), n, b.prefix,
+                                                       c.heads, c.kv_heads, c.head_dim, attn_scale, m->stream),
+                   "shared attention batch");
+            } else if (!suffix && m->api.attention_gated_batch && n >= 2 && n <= m->api.max_batch) {
+                m->launches++;
+                CK(m->api.attention_gated_batch(m->S(m->s_aq), m->S(m->s_ak), vptr, ld, m->S(m->s_agate),
+                                                m->S(m->s_ao), b.lengths.data(), n, c.heads, c.kv_heads, c.head_dim,
+                                                attn_scale, m->stream),
+                   "attention batch");
             } else {
                 for (int s = 0; s < n; s++) {
                     const size_t o = offs[s];

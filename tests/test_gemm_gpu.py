@@ -81,9 +81,28 @@ def test_gemm_packed_equals_per_sequence(cs1, gemm, stream):
         off += n
 
 
-@pytest.mark.parametrize("M", [1, 200, 1500])
-def test_gemm_residual_epilogue(cs1, gemm, stream, M):
-    N, K = 2560, 512
+def test_cta_pair_kernel_equals_single_cta_kernel(cs1, stream, monkeypatch):
+    """The 256x256 CTA-pair kernel and the 128-row single-CTA kernels give identical bits."""
+    M, N, K = 1100, 16480, 1024
+    x, w = _rand((M, K), 15), _rand((N, K), 16, 0.05)
+    out = []
+    for pairs in ("1", "0"):
+        monkeypatch.setenv("S1_GEMM_PAIRS", pairs)
+        h = cs1.cs1_gemm_create(0)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        cs1.cs1_gemm(h, x, w, y, M, N, K, N, stream)
+        torch.cuda.synchronize()
+        cs1.cs1_gemm_destroy(h)
+        out.append(y)
+    assert cs1.cs1_fault_status(1) == 0
+    ref = (x.float() @ w.float().T).cpu().numpy()
+    assert max_rel(out[0].float().cpu().numpy(), ref) <= 1e-2
+    assert torch.equal(out[0], out[1])
+
+
+@pytest.mark.parametrize("M,N", [(1, 2560), (200, 2560), (1500, 2560), (4000, 5120)])
+def test_gemm_residual_epilogue(cs1, gemm, stream, M, N):
+    K = 512
     x, w = _rand((M, K), 9), _rand((N, K), 10, 0.05)
     res = _rand((M, N), 11)
     expect = (res.float() + (x.float() @ w.float().T).to(torch.bfloat16).float()).to(torch.bfloat16)
@@ -98,7 +117,7 @@ def test_gemm_residual_epilogue(cs1, gemm, stream, M):
     assert torch.equal(out, (res.float() + y.float()).to(torch.bfloat16))
 
 
-@pytest.mark.parametrize("M,I", [(1, 128), (77, 512), (1000, 1024)])
+@pytest.mark.parametrize("M,I", [(1, 128), (77, 512), (1000, 1024), (2048, 2560)])
 def test_gemm_swiglu_epilogue(cs1, gemm, stream, M, I):
     K = 384
     x = _rand((M, K), 12)
