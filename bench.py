@@ -155,6 +155,10 @@ def reference_cuda(args, local):
             out.append(m.forward(seqs[a:b]))
         return np.concatenate(out)
     logits = step()
+    # run-to-run sensitivity of the reference itself: the same requests one by one
+    # (different GEMM row counts, hence possibly different cuBLASLt algorithms)
+    single = np.concatenate([m.forward(seqs[i:i + 1]) for i in range(len(seqs))])
+    self_diff = float(np.abs(single - logits).max())
     for _ in range(max(1, args.warmup - 1)):
         step()
     torch.cuda.synchronize()
@@ -170,7 +174,8 @@ def reference_cuda(args, local):
             "library": "reference src/backends/cuda/qwen3_5 built for sm_100a (oracle/Makefile)",
             "host": "this build's C++ host, eager, host-side scorer head (the reference's executor path)",
             "timing": "wall clock around synchronous forward calls (host copies included)",
-            "logits_sample": logits[:4].round(4).tolist()}
+            "logits_sample": logits[:4].round(4).tolist(),
+            "self_max_abs_diff_packed_vs_single": self_diff}
 
 
 def run_reference(args, rank, world):

@@ -62,6 +62,8 @@ const char* s1_model_error(void* model);
 // attention: q, k, v, q_norm, k_norm, o. Data are host bf16 (f32 for the head),
 // row-major in the Transformers shapes; `bytes` must match.
 int s1_model_set_weight(void* model, const char* name, const void* host_data, size_t bytes);
+// The inverse: copy a parameter, in the same layout, back to host memory.
+int s1_model_get_weight(void* model, const char* name, void* host_data, size_t bytes);
 // Fill every parameter on the device from a counter-based generator (benchmarks):
 // matrices ~ N(0, std), zero-centred norms ~ N(0, 0.1), gated-norm weight ~ 1 + N(0, 0.1),
 // conv ~ U(-0.5, 0.5), A_log = log U(1, 16), dt_bias ~ 1 + N(0, 0.1).

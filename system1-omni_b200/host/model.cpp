@@ -829,17 +829,18 @@ __attribute__((visibility("default"))) const char* s1_model_error(void* mp) {
     return m ? m->err.c_str() : g_create_error.c_str();
 }
 
-__attribute__((visibility("default"))) int s1_model_set_weight(void* mp, const char* name, const void* data,
-                                                              size_t bytes) {
-    auto* m = static_cast<Model*>(mp);
-    if (!m || !name || !data) return -1;
+// Copies one named parameter between the host and the arena (to_device: upload).
+static int weight_io(Model* m, const char* name, void* data, size_t bytes, bool to_device) {
     const s1_config& c = m->cfg;
     const size_t H = c.hidden, I = c.intermediate;
     std::string n(name);
     auto put = [&](const Region& r, size_t row0, size_t rows, size_t cols) -> int {
         const size_t eb = r.f32 ? 4 : 2;
         if (bytes != rows * cols * eb) return fail(m, -1, "size mismatch for " + n);
-        CK(m->api.upload(m->W(r) + row0 * cols * eb, data, bytes, m->stream), "upload " + n);
+        if (to_device)
+            CK(m->api.upload(m->W(r) + row0 * cols * eb, data, bytes, m->stream), "upload " + n);
+        else
+            CK(m->api.download(data, m->W(r) + row0 * cols * eb, bytes, m->stream), "download " + n);
         return 0;
     };
     if (n == "embed") return put(m->embed, 0, c.vocab, H);
@@ -859,11 +860,15 @@ __attribute__((visibility("default"))) int s1_model_set_weight(void* mp, const c
         if (bytes != I * H * 2) return fail(m, -1, "size mismatch for " + n);
         if (!m->fused) return put(L.gate_up, f == "gate" ? 0 : I, I, H);
         // interleave in blocks of 128 rows: [gate b | up b] for b = 0, 1, ...
-        const uint8_t* src = static_cast<const uint8_t*>(data);
+        uint8_t* host = static_cast<uint8_t*>(data);
         for (size_t b = 0; b < I / 128; b++) {
             const size_t dst_row = 256 * b + (f == "gate" ? 0 : 128);
-            CK(m->api.upload(m->W(L.gate_up) + dst_row * H * 2, src + b * 128 * H * 2, 128 * H * 2, m->stream),
-               "upload " + n);
+            if (to_device)
+                CK(m->api.upload(m->W(L.gate_up) + dst_row * H * 2, host + b * 128 * H * 2, 128 * H * 2, m->stream),
+                   "upload " + n);
+            else
+                CK(m->api.download(host + b * 128 * H * 2, m->W(L.gate_up) + dst_row * H * 2, 128 * H * 2, m->stream),
+                   "download " + n);
         }
         return 0;
     }
@@ -887,6 +892,20 @@ __attribute__((visibility("default"))) int s1_model_set_weight(void* mp, const c
         if (f == "o") return put(L.o, 0, H, m->qd);
     }
     return fail(m, -1, "unknown parameter " + n);
+}
+
+__attribute__((visibility("default"))) int s1_model_set_weight(void* mp, const char* name, const void* data,
+                                                              size_t bytes) {
+    auto* m = static_cast<Model*>(mp);
+    if (!m || !name || !data) return -1;
+    return weight_io(m, name, const_cast<void*>(data), bytes, true);
+}
+
+__attribute__((visibility("default"))) int s1_model_get_weight(void* mp, const char* name, void* data,
+                                                              size_t bytes) {
+    auto* m = static_cast<Model*>(mp);
+    if (!m || !name || !data) return -1;
+    return weight_io(m, name, data, bytes, false);
 }
 
 __attribute__((visibility("default"))) int s1_model_init_random(void* mp, uint64_t seed, float std_) {

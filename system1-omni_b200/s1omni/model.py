@@ -96,6 +96,7 @@ def _lib():
     lib.s1_model_error.restype = ctypes.c_char_p
     lib.s1_model_error.argtypes = [P]
     lib.s1_model_set_weight.argtypes = [P, ctypes.c_char_p, P, Z]
+    lib.s1_model_get_weight.argtypes = [P, ctypes.c_char_p, P, Z]
     lib.s1_model_init_random.argtypes = [P, ctypes.c_uint64, ctypes.c_float]
     lib.s1_model_forward.argtypes = [P, P, P, Z, P, P]
     lib.s1_model_forward_shared.argtypes = [P, P, Z, P, P, Z, P, P]
@@ -186,6 +187,17 @@ class Model:
             u = a.view(np.uint32).astype(np.uint64)
             data = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
         self._check(self._lib.s1_model_set_weight(self._h, name.encode(), data.ctypes.data, data.nbytes), name)
+
+    def get_weight(self, name, shape):
+        """Read a parameter back as float32 (bf16 values; float32 for the head)."""
+        if name in ("head_w", "head_b"):
+            out = np.zeros(shape, np.float32)
+        else:
+            out = np.zeros(shape, np.uint16)
+        self._check(self._lib.s1_model_get_weight(self._h, name.encode(), out.ctypes.data, out.nbytes), name)
+        if out.dtype == np.uint16:
+            out = (out.astype(np.uint32) << 16).view(np.float32)
+        return out
 
     def load(self, weights):
         for name, arr in weights.items():

@@ -1,0 +1,68 @@
+"""Whole-forward parity at the 27B layer widths (hidden 5120, SwiGLU 17408, GDN 16/48
+heads, attention 24/4 heads x 256) over one 4-layer period (3 GDN + 1 attention).
+
+The weights are drawn on the device by s1_model_init_random and read back with
+s1_model_get_weight, so the numpy oracle runs on exactly the weights the kernels use.
+Gates: logits within 2e-2 absolute of the oracle (BASELINE's bf16 tolerance) and of the
+reference's own CUDA library driven by the same host with the same weights.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import model as OM
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF = os.path.join(ROOT, "oracle", "_ref", "libqwen3_5_cuda.so")
+
+
+def _cfgs():
+    from s1omni import Config
+    layers = ["gdn", "gdn", "gdn", "attn"]
+    ours = Config(5120, 17408, layers, 16, 48, 24, 4, 4096, name="27b-period")
+    oracle = OM.Config(5120, 17408, layers, 16, 48, 24, 4, 4096, name="27b-period")
+    return ours, oracle
+
+
+@pytest.fixture(scope="module")
+def period(cs1):
+    from s1omni import Model
+    cfg, ocfg = _cfgs()
+    m = Model(cfg, device=0, max_tokens=1024, max_seqs=8)
+    m.init_random(seed=99, std=0.02)
+    W = {name: m.get_weight(name, shape) for name, shape, _ in OM.weight_shapes(ocfg)}
+    yield cfg, ocfg, m, W
+    m.close()
+
+
+def _prompts(vocab):
+    rng = np.random.default_rng(5)
+    return [rng.integers(0, vocab, n).astype(np.int32) for n in (100, 65, 1)]
+
+
+def test_fullwidth_period_matches_oracle(period):
+    cfg, ocfg, m, W = period
+    seqs = _prompts(cfg.vocab)
+    logits = m.forward(seqs)
+    _, ref = OM.forward_batch(ocfg, W, seqs, gdn_mode="bf16")
+    err = float(np.abs(logits - ref).max())
+    assert err <= 2e-2, (err, float(np.abs(ref).max()))
+
+
+def test_fullwidth_period_matches_reference_library(period):
+    if not os.path.exists(REF):
+        pytest.skip("reference library not built (make -C oracle)")
+    from s1omni import Model, lib_path
+    cfg, _, m, _ = period
+    seqs = _prompts(cfg.vocab)
+    ours = m.forward(seqs)
+    r = Model(cfg, device=0, max_tokens=1024, max_seqs=8, cs1_library=REF + ";" + lib_path())
+    try:
+        r.init_random(seed=99, std=0.02)
+        theirs = r.forward(seqs)
+    finally:
+        r.close()
+    err = float(np.abs(ours - theirs).max())
+    assert err <= 2e-2, (err, float(np.abs(theirs).max()))
