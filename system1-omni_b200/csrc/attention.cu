@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(THREADS, 1) flash_kernel(Args a, SeqTable tab)
     bf16* qs = reinterpret_cast<bf16*>(smem_raw);
     bf16* ks = qs + TILE_Q;  // [2][BN][LDS]
     bf16* vs = ks + 2 * TILE_KV;
-    const int seq = blockIdx.z, h = blockIdx.y, hk = h / (a.Hq / a.Hk);
+    const int seq = tab.order[blockIdx.z], h = blockIdx.y, hk = h / (a.Hq / a.Hk);
     const int off = tab.offset[seq];
     const int len = tab.offset[seq + 1] - off;
     const int qrows = len - a.q_base;

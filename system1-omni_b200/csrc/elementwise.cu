@@ -25,6 +25,15 @@ bool make_table(SeqTable& t, const size_t* lengths, size_t count) {
         t.offset[i + 1] = (int)rows;
         if ((int)lengths[i] > t.max_len) t.max_len = (int)lengths[i];
     }
+    // stable insertion sort by decreasing length (count <= 256)
+    for (size_t i = 0; i < count; i++) {
+        int j = (int)i;
+        while (j > 0 && lengths[t.order[j - 1]] < lengths[i]) {
+            t.order[j] = t.order[j - 1];
+            j--;
+        }
+        t.order[j] = (int)i;
+    }
     return true;
 }
 

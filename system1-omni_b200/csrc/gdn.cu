@@ -579,7 +579,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     const uint32_t drain = bars + 64;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 72);
 
-    const int h = blockIdx.x, seq = blockIdx.y;
+    const int h = blockIdx.x, seq = tab.seq.order[blockIdx.y];
     const int start = tab.seq.offset[seq];
     const int len = tab.seq.offset[seq + 1] - start;
     const int NC = (len + C - 1) / C;

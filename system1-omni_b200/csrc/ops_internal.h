@@ -16,6 +16,7 @@ struct SeqTable {
     int count;
     int max_len;
     int offset[MAX_SEQS + 1];
+    int order[MAX_SEQS];  // sequence indices by decreasing length (longest work scheduled first)
 };
 
 // Build a table from host lengths; false if count is 0 or above MAX_SEQS, a length is
