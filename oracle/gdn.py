@@ -102,6 +102,14 @@ def chunk_fp32(q, k, v, g, beta, scale, state=None, l2norm=True):
     return o.astype(np.float32), S.astype(np.float32)
 
 
+def tf32(x):
+    """Round float32 to TF32 (10-bit mantissa), nearest with ties away from zero: the
+    operand rounding of the reference's pair products (gdn_prefill.cu:197-198)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = ((u.astype(np.uint64) + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    return r.view(np.float32)
+
+
 def _inverse_unit_lower(A):
     """(I + A)^-1 for strictly lower-triangular A [.., C, C], float32."""
     n = A.shape[-1]
@@ -117,7 +125,8 @@ def chunk_bf16(q, k, v, g, beta, scale, state=None):
     """The reference's bfloat16-intermediate chunk kernel (`gdn_prefill.cu:113-547`).
 
     Per chunk and head: cum = sequential fp32 cumsum of g; kn, qn = L2-normalised k, q
-    (q also scaled); A[i,j] = beta_i kn_i.kn_j exp(cum_i - cum_j) for j < i;
+    (q also scaled); A[i,j] = beta_i kn_i.kn_j exp(cum_i - cum_j) for j < i, with the
+    pair products on TF32-rounded operands as the reference computes them;
     T = (I + A)^-1; u = bf16(bf16(T diag(beta)) v); w = bf16(bf16(T diag(beta)) bf16(kn e^cum));
     qd = bf16(qn e^cum); kd = bf16(kn e^(last - cum)); P = bf16(qn.kn e^(cum_i - cum_j)), j <= i.
     Scan: S_b = bf16(S); v_new = bf16(u - w S_b); o = bf16(qd S_b + P v_new);
@@ -151,7 +160,8 @@ def chunk_bf16(q, k, v, g, beta, scale, state=None):
             qn = qq * qinv[:, None]
             dec = np.exp(np.minimum(cum[:, None] - cum[None, :], 0)).astype(np.float32)
             lower = np.tril(np.ones((C, C), bool), -1)
-            A = np.where(lower, bb[:, None] * (kn @ kn.T) * dec, 0).astype(np.float32)
+            kt, qt = tf32(kn), tf32(qn)  # pair products take TF32 operands
+            A = np.where(lower, bb[:, None] * (kt @ kt.T) * dec, 0).astype(np.float32)
             Tm = _inverse_unit_lower(A)
             tb = rnd(Tm * bb[None, :])
             vb = np.zeros((C, D), np.float32)
@@ -160,7 +170,7 @@ def chunk_bf16(q, k, v, g, beta, scale, state=None):
             w = rnd(tb @ rnd(kn * ecum[:, None]))
             qd = rnd(qn * ecum[:, None])
             kd = rnd(kn * erem[:, None])
-            P = rnd(np.where(np.tril(np.ones((C, C), bool)), (qn @ kn.T) * dec, 0))
+            P = rnd(np.where(np.tril(np.ones((C, C), bool)), (qt @ kt.T) * dec, 0))
             Sb = rnd(S)
             v_new = rnd(u - w @ Sb)
             oc = rnd(qd @ Sb + P @ v_new)

@@ -9,10 +9,11 @@
 //   scan:      v_new = u - w S;  o = qd S + P v_new;  S = e^{last} S + kd^T v_new
 //
 // Two kernels:
-//  1. gdn_prep (parallel over chunk x head x sequence): everything that does not
+//  1. gdn_prep_tc (parallel over chunk x head x sequence): everything that does not
 //     depend on the state, written to the workspace in the layouts the scan's
-//     tensor-core operands want (w and qd [64 t][128 k], P [64 t][64 j], kd^T
-//     [128 k][64 t], u^T [128 v][64 t]) as bfloat16, plus e^{last} per chunk.
+//     tensor-core operands want (qd [64 t][128 k] K-major, w^T [128 k][64 t] and
+//     kd [64 t][128 k] read MN-major, P [64 t][64 j], u^T [128 v][64 t]) as bfloat16,
+//     plus e^{last} per chunk.
 //  2. gdn_scan (one CTA per head x sequence, serial over chunks) on tcgen05:
 //     the state is kept transposed, S^T [v][k], so that TMEM lane = value column v
 //     and every contraction is an M = 128, K-major MMA:
@@ -26,8 +27,8 @@
 // u, w, qd, kd, P, the per-chunk state copy and v_new in bfloat16, state and
 // accumulations in fp32.
 //
-// The FP32 operator (cs1_gdn_prefill_fp32, gdn_fp32.cu) shares the prep kernel
-// with float32 outputs and runs its own float32 scan.
+// The FP32 operator (cs1_gdn_prefill_fp32) runs a float32 CUDA-core prep
+// (gdn_prep<true>, w [t][k] and kd^T [k][t] layouts) and its own float32 scan.
 #include <algorithm>
 #include <climits>
 #include <cmath>
@@ -243,31 +244,34 @@ __global__ void __launch_bounds__(PREP_THREADS) gdn_prep(const bf16* __restrict_
 }
 
 // ------------------------------------------------------- prep on tcgen05 ----
-// One CTA (256 threads, 2 per SM) per (chunk, head, sequence):
-//  1. cum = sequential fp32 cumsum of g; kn, qn = L2-normalised k and scaled q, rounded
-//     to TF32 and written as one [128 rows = kn | qn][128] fp32 operand tile (128B swizzle).
-//  2. MMA1 (kind::tf32, M=128, N=64, K=128): D[i][j] = [kn;qn]_i . kn_j into TMEM.
-//     Lanes 0..63 give A_ij = beta_i kk_ij e^{cum_i-cum_j} (j < i) into shared memory,
-//     lanes 64..127 give P_tj = qk_tj e^{cum_t-cum_j} (j <= t), stored bf16.
-//     Meanwhile warps 4..7 write qd, kd^T (global) and the MMA2 operands
-//     (k e^cum)^T and v^T (shared, bf16).
-//  3. T = (I + A)^-1 blockwise: 16x16 diagonal inverses by substitution, then block rows
-//     T_ij = -T_ii sum_k A_ik T_kj; tb = bf16(T diag(beta)).
-//  4. MMA2 (kind::f16, M=128, N=64, K=64): u^T = v^T tb^T, w^T = (k e^cum)^T tb^T; u^T
-//     rows go out directly, w is transposed through shared memory.
+// One CTA (256 threads, 2 per SM) per (chunk, head, sequence); every operand is used in
+// the layout it is produced in (no transposes):
+//  1. cum = sequential fp32 cumsum of g. Each warp loads 8 rows of q and k with 8-byte
+//     lane accesses, normalises them (k / |k|, q / |q| * scale) and writes
+//       - the TF32-rounded [kn ; qn] rows into a K-major fp32 operand tile (128B swizzle),
+//       - qd = bf16(qn e^cum) and kd = bf16(kn e^(last-cum)) rows straight to the workspace,
+//       - kw = bf16(kn e^cum) rows into an MN-major bf16 operand tile (rows = token j).
+//  2. MMA1 (kind::tf32, M=128, N=64, K=128): D[i][j] = [kn;qn]_i . kn_j in TMEM. Lanes
+//     0..63 give A_ij = beta_i kk_ij e^(cum_i-cum_j) (j < i); lanes 64..127 give
+//     P_tj = qk_tj e^(cum_t-cum_j) (j <= t), stored bf16. v rows go (16-byte loads) into
+//     an MN-major bf16 tile meanwhile.
+//  3. T = (I + A)^-1 blockwise on CUDA cores (16x16 diagonal substitutions, then block
+//     rows T_ij = -T_ii sum_k A_ik T_kj); tb = bf16(T diag(beta)) as a K-major tile.
+//  4. MMA2 (kind::f16, A MN-major, M=128, N=64, K=64): u^T = v^T tb^T and
+//     w^T = kw^T tb^T; each thread stores its TMEM row (128 contiguous bytes).
+// Workspace layouts written: qd [t][k], kd [t][k], P [t][j], u^T [v][t], w^T [k][t].
 constexpr int TP_THREADS = 256;
-constexpr int TP_KQ = 0;                         // 4 x [128][32 fp32] = 64 KB
-constexpr int TP_VT = 0;                         // after MMA1: v^T      [128][64] bf16, 16 KB
-constexpr int TP_KWT = 16384;                    //              (k e^cum)^T [128][64] bf16, 16 KB
-constexpr int TP_TB = 32768;                     //              tb      [64][64] bf16, 8 KB
-constexpr int TP_WST = 40960;                    //              w staging [64][136] bf16, 17 KB
-constexpr int TP_KQ_BYTES = 65536;
-constexpr int TP_A = TP_KQ_BYTES;                // A fp32 [64][65]
-constexpr int TP_T = TP_A + C * LDC * 4;         // T fp32 [64][65]
-constexpr int TP_VEC = TP_T + C * LDC * 4;       // cum, bet, ecum, erem, gg [64] each
+constexpr int TP_KQ = 0;                         // 4 x [128][32 fp32] = 64 KB; after MMA1: A, T, scratch
+constexpr int TP_KW = 65536;                     // kw, MN-major: 2 blocks x [64 j][64 d] bf16 = 16 KB
+constexpr int TP_VB = TP_KW + 16384;             // v,  MN-major: 2 blocks x [64 j][64 v] bf16 = 16 KB
+constexpr int TP_TB = TP_VB + 16384;             // tb, K-major [64 t][64 j] bf16 = 8 KB
+constexpr int TP_VEC = TP_TB + 8192;             // cum, bet, ecum, erem, gg [64] each
 constexpr int TP_BAR = TP_VEC + 5 * C * 4;
 constexpr int TP_SMEM = TP_BAR + 64 + 1024;
-constexpr int WST_LD = 136;
+constexpr int TP_A = 0;                          // inside the KQ region once MMA1 is done
+constexpr int TP_T = TP_A + C * LDC * 4;
+constexpr int TP_S = TP_T + C * LDC * 4;         // inverse scratch [3][16][16] fp32
+constexpr uint32_t MN_BLOCK = 8192;              // 64 K-rows x 128 B: stride between 64-wide MN blocks
 
 __device__ __forceinline__ float tf32_rna(float x) {
     uint32_t r;
@@ -275,10 +279,10 @@ __device__ __forceinline__ float tf32_rna(float x) {
     return __uint_as_float(r);
 }
 
-// Byte offset of fp32 element (row, col) in the [rows][128] fp32 tile stored as four
-// [rows][32] sub-tiles of 128-byte rows with the 128B swizzle; sub-tile stride `sub`.
-__device__ __forceinline__ uint32_t kq_off(int row, int col, int sub) {
-    return (uint32_t)((col >> 5) * sub) + sw128_offset(row, (col & 31) >> 2) + (uint32_t)((col & 3) << 2);
+// Byte offset of bf16 element (k_row, mn) in an MN-major 128B-swizzled tile made of
+// 64-wide MN blocks of [64 K-rows][128 B].
+__device__ __forceinline__ uint32_t mn_off(int krow, int mn) {
+    return (uint32_t)(mn >> 6) * MN_BLOCK + sw128_offset(krow, (mn & 63) >> 3) + (uint32_t)((mn & 7) << 1);
 }
 
 __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restrict__ q, const bf16* __restrict__ k,
@@ -301,6 +305,7 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
     uint8_t* sm = smem_raw + (base - raw);
     float* A = reinterpret_cast<float*>(sm + TP_A);
     float* Tm = reinterpret_cast<float*>(sm + TP_T);
+    float* S = reinterpret_cast<float*>(sm + TP_S);
     float* cum = reinterpret_cast<float*>(sm + TP_VEC);
     float* bet = cum + C;
     float* ecum = bet + C;
@@ -334,33 +339,75 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         }
         ws.decay[slot] = expf(s);
     }
-    // 1. normalised rows: warp per row, lane holds dims lane + 32e
-    for (int r = warp; r < C; r += TP_THREADS / 32) {
-        float kx[4], qx[4], ks = 0.f, qs = 0.f;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int d = lane + 32 * e;
-            kx[e] = r < n ? f32(k[((size_t)(t0 + r) * HK + hk) * K + d]) : 0.f;
-            qx[e] = r < n ? f32(q[((size_t)(t0 + r) * HK + hk) * K + d]) : 0.f;
-            ks = fmaf(kx[e], kx[e], ks);
-            qs = fmaf(qx[e], qx[e], qs);
-        }
-        ks = warp_sum(ks);
-        qs = warp_sum(qs);
-        const float kinv = rsqrtf(ks + 1e-6f), qinv = rsqrtf(qs + 1e-6f) * scale;
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int d = lane + 32 * e;
-            *reinterpret_cast<float*>(sm + TP_KQ + kq_off(r, d, 16384)) = tf32_rna(kx[e] * kinv);
-            *reinterpret_cast<float*>(sm + TP_KQ + kq_off(C + r, d, 16384)) = tf32_rna(qx[e] * qinv);
-        }
-    }
-    fence_async_smem();
     __syncthreads();
     if (tid < C) {
         ecum[tid] = expf(cum[tid]);
         erem[tid] = expf(cum[C - 1] - cum[tid]);
     }
+    __syncthreads();
+
+    // 1. rows r = warp*8 .. warp*8+7; lane holds dims d0 = 4*lane .. +3
+    {
+        const int d0 = lane * 4;
+        uint2 kr[8], qr[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = warp * 8 + i;
+            if (r < n) {
+                kr[i] = *reinterpret_cast<const uint2*>(k + ((size_t)(t0 + r) * HK + hk) * K + d0);
+                qr[i] = *reinterpret_cast<const uint2*>(q + ((size_t)(t0 + r) * HK + hk) * K + d0);
+            } else {
+                kr[i] = make_uint2(0u, 0u);
+                qr[i] = make_uint2(0u, 0u);
+            }
+        }
+        bf16* QD = static_cast<bf16*>(ws.qd) + slot * C * K;
+        bf16* KD = static_cast<bf16*>(ws.kdt) + slot * C * K;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = warp * 8 + i;
+            float kx[4], qx[4];
+            const __nv_bfloat162* kp = reinterpret_cast<const __nv_bfloat162*>(&kr[i]);
+            const __nv_bfloat162* qp = reinterpret_cast<const __nv_bfloat162*>(&qr[i]);
+            const float2 k01 = __bfloat1622float2(kp[0]), k23 = __bfloat1622float2(kp[1]);
+            const float2 q01 = __bfloat1622float2(qp[0]), q23 = __bfloat1622float2(qp[1]);
+            kx[0] = k01.x; kx[1] = k01.y; kx[2] = k23.x; kx[3] = k23.y;
+            qx[0] = q01.x; qx[1] = q01.y; qx[2] = q23.x; qx[3] = q23.y;
+            float ks = 0.f, qs = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                ks = fmaf(kx[e], kx[e], ks);
+                qs = fmaf(qx[e], qx[e], qs);
+            }
+            ks = warp_sum(ks);
+            qs = warp_sum(qs);
+            const float kinv = rsqrtf(ks + 1e-6f), qinv = rsqrtf(qs + 1e-6f) * scale;
+            float kn[4], qn[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                kn[e] = kx[e] * kinv;
+                qn[e] = qx[e] * qinv;
+            }
+            // TF32 operand rows: dims d0..d0+3 = one 16-byte chunk of sub-tile d0 / 32
+            const uint32_t chunk = (uint32_t)((d0 & 31) >> 2);
+            *reinterpret_cast<float4*>(sm + TP_KQ + (d0 >> 5) * 16384 + sw128_offset(r, chunk)) =
+                make_float4(tf32_rna(kn[0]), tf32_rna(kn[1]), tf32_rna(kn[2]), tf32_rna(kn[3]));
+            *reinterpret_cast<float4*>(sm + TP_KQ + (d0 >> 5) * 16384 + sw128_offset(C + r, chunk)) =
+                make_float4(tf32_rna(qn[0]), tf32_rna(qn[1]), tf32_rna(qn[2]), tf32_rna(qn[3]));
+            uint2 o;
+            o.x = pack_bf16x2(qn[0] * ecum[r], qn[1] * ecum[r]);
+            o.y = pack_bf16x2(qn[2] * ecum[r], qn[3] * ecum[r]);
+            *reinterpret_cast<uint2*>(QD + (size_t)r * K + d0) = o;
+            o.x = pack_bf16x2(kn[0] * erem[r], kn[1] * erem[r]);
+            o.y = pack_bf16x2(kn[2] * erem[r], kn[3] * erem[r]);
+            *reinterpret_cast<uint2*>(KD + (size_t)r * K + d0) = o;
+            o.x = pack_bf16x2(kn[0] * ecum[r], kn[1] * ecum[r]);
+            o.y = pack_bf16x2(kn[2] * ecum[r], kn[3] * ecum[r]);
+            *reinterpret_cast<uint2*>(sm + TP_KW + mn_off(r, d0)) = o;
+        }
+    }
+    fence_async_smem();
+    __syncthreads();
     if (tid == 0) {
         tc_fence_after();
         constexpr uint32_t ID = idesc(128, 64, AB_TF32);
@@ -371,16 +418,25 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         }
         mma_commit(bar);
     }
-    __syncthreads();  // ecum / erem visible
-    bool ok = true;
-    if (warp < 4) {
-        // 2a. A rows (lanes 0..63) and P rows (lanes 64..127) from TMEM
-        if (!mbar_wait(bar, 0)) {
-            if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
-            ok = false;
+    // v rows into the MN-major tile (16-byte units: row j, dims 8u..8u+7), zero past the end
+    for (int u = tid; u < C * V / 8; u += TP_THREADS) {
+        const int j = u >> 4, d8 = (u & 15) * 8;
+        Pack8 val;
+        if (j < n) {
+            val = ld8(v + ((size_t)(t0 + j) * H + h) * V + d8);
+        } else {
+            const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            val = pack8(z);
         }
-        tc_fence_after();
-        const int i = tid;  // TMEM lane
+        *reinterpret_cast<Pack8*>(sm + TP_VB + (d8 >> 6) * MN_BLOCK + sw128_offset(j, (d8 & 63) >> 3)) = val;
+    }
+    bool ok = mbar_wait(bar, 0);  // every thread: MMA1 done, the KQ region is free
+    if (!ok && lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+    tc_fence_after();
+    __syncthreads();
+    if (warp < 4) {
+        // 2. A rows (lanes 0..63) and P rows (lanes 64..127) from TMEM
+        const int i = tid;
         float d[64];
         tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), *reinterpret_cast<float(*)[32]>(d));
         tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + 32, *reinterpret_cast<float(*)[32]>(d + 32));
@@ -402,47 +458,8 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
                 st8(P + j8 * 8, pack8(f));
             }
         }
-    } else {
-        // 2b. qd [t][d] and kd^T [d][t] to global (units of 8 consecutive elements)
-        const int w4 = tid - 128;
-        bf16* QD = static_cast<bf16*>(ws.qd) + slot * C * K;
-        bf16* KDT = static_cast<bf16*>(ws.kdt) + slot * K * C;
-        for (int u = w4; u < C * K / 8; u += 128) {
-            const int t = u / (K / 8), d0 = (u % (K / 8)) * 8;
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) f[e] = *reinterpret_cast<const float*>(sm + TP_KQ + kq_off(C + t, d0 + e, 16384)) * ecum[t];
-            st8(QD + (size_t)t * K + d0, pack8(f));
-            const int dd = u / (C / 8), tt0 = (u % (C / 8)) * 8;
-#pragma unroll
-            for (int e = 0; e < 8; e++) f[e] = *reinterpret_cast<const float*>(sm + TP_KQ + kq_off(tt0 + e, dd, 16384)) * erem[tt0 + e];
-            st8(KDT + (size_t)dd * C + tt0, pack8(f));
-        }
     }
-    __syncthreads();  // MMA1 done reading the KQ tile (all threads waited or fell through); A complete
-    // The KQ region is reused from here: build (k e^cum)^T and v^T in it. kn is still needed, so
-    // stage it first: each thread keeps its units in registers.
-    {
-        // (k e^cum)^T [d][j] and v^T [v][j], units of (row, 8 consecutive j): 1024 units each
-        float kw[4][8];
-        for (int i = 0; i < 4; i++) {
-            const int u = tid + i * TP_THREADS;
-            const int dd = u / (C / 8), j0 = (u % (C / 8)) * 8;
-#pragma unroll
-            for (int e = 0; e < 8; e++)
-                kw[i][e] = rbf(*reinterpret_cast<const float*>(sm + TP_KQ + kq_off(j0 + e, dd, 16384)) * ecum[j0 + e]);
-        }
-        __syncthreads();
-        for (int i = 0; i < 4; i++) {
-            const int u = tid + i * TP_THREADS;
-            const int dd = u / (C / 8), j0 = (u % (C / 8)) * 8;
-            *reinterpret_cast<Pack8*>(sm + TP_KWT + sw128_offset(dd, j0 >> 3)) = pack8(kw[i]);
-            float vv[8];
-#pragma unroll
-            for (int e = 0; e < 8; e++) vv[e] = j0 + e < n ? f32(v[((size_t)(t0 + j0 + e) * H + h) * V + dd]) : 0.f;
-            *reinterpret_cast<Pack8*>(sm + TP_VT + sw128_offset(dd, j0 >> 3)) = pack8(vv);
-        }
-    }
+    __syncthreads();
     // 3. T = (I + A)^-1. Diagonal 16x16 blocks: one thread per (block, column).
     if (tid < C) {
         const int b = tid >> 4, col = tid & 15, o = b * 16;
@@ -457,14 +474,11 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
 #pragma unroll
         for (int r = 0; r < 16; r++) Tm[(o + r) * LDC + o + col] = x[r];
     }
-    // zero the strictly-upper blocks
     for (int x = tid; x < C * C; x += TP_THREADS) {
         const int i = x / C, j = x % C;
         if ((j >> 4) > (i >> 4)) Tm[i * LDC + j] = 0.f;
     }
     __syncthreads();
-    // Block rows 1..3: S_j = sum_{k=j}^{i-1} A_ik T_kj, then T_ij = -T_ii S_j.
-    float* S = reinterpret_cast<float*>(sm + TP_WST);  // scratch [3][16][16]
     for (int bi = 1; bi < 4; bi++) {
         for (int x = tid; x < bi * 256; x += TP_THREADS) {
             const int bj = x >> 8, r = (x >> 4) & 15, cc = x & 15;
@@ -481,7 +495,7 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         }
         __syncthreads();
     }
-    // tb = bf16(T diag(beta)) as the [64 t][64 j] operand tile
+    // tb = bf16(T diag(beta)), K-major [64 t][64 j]
     for (int u = tid; u < C * C / 8; u += TP_THREADS) {
         const int t = u >> 3, j0 = (u & 7) * 8;
         float f[8];
@@ -493,50 +507,35 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
     __syncthreads();
     if (tid == 0) {
         tc_fence_after();
-        constexpr uint32_t ID = idesc(128, 64, AB_BF16);
+        constexpr uint32_t ID = idesc_major(128, 64, AB_BF16, 1, 0);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
-            const uint32_t off = (uint32_t)kk * 32;
-            const uint64_t b = desc_sw128(base + TP_TB + off);
-            mma_bf16(tmem + 64, desc_sw128(base + TP_VT + off), b, ID, kk > 0);
-            mma_bf16(tmem + 128, desc_sw128(base + TP_KWT + off), b, ID, kk > 0);
+            const uint64_t bdesc = desc_sw128(base + TP_TB + (uint32_t)kk * 32);
+            const uint32_t koff = (uint32_t)kk * 2048;
+            mma_bf16(tmem + 64, desc_sw128_mn(base + TP_VB + koff, MN_BLOCK, 1024), bdesc, ID, kk > 0);
+            mma_bf16(tmem + 128, desc_sw128_mn(base + TP_KW + koff, MN_BLOCK, 1024), bdesc, ID, kk > 0);
         }
         mma_commit(bar);
     }
     __syncwarp();
     if (!mbar_wait(bar, 1)) {
         if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
-        ok = false;
     }
     tc_fence_after();
-    const int q4 = warp & 3;
-    const int row = q4 * 32 + lane;  // TMEM lane = v (u^T) or d (w^T)
-    bf16* wst = reinterpret_cast<bf16*>(sm + TP_WST);
     {
+        const int q4 = warp & 3;
+        const int row = q4 * 32 + lane;  // TMEM lane = v (u^T) or k (w^T)
         float x[64];
         const uint32_t col = warp < 4 ? 64u : 128u;
         tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + col, *reinterpret_cast<float(*)[32]>(x));
         tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + col + 32, *reinterpret_cast<float(*)[32]>(x + 32));
         tmem_ld_wait();
-        if (warp < 4) {
-            bf16* UT = static_cast<bf16*>(ws.ut) + (slot * V + row) * C;
+        bf16* dst = static_cast<bf16*>(warp < 4 ? ws.ut : ws.w) + (slot * V + row) * C;
 #pragma unroll
-            for (int j8 = 0; j8 < 8; j8++) st8(UT + j8 * 8, pack8(x + j8 * 8));
-        } else {
-#pragma unroll
-            for (int t = 0; t < C; t++) wst[t * WST_LD + row] = to_bf16(x[t]);
-        }
+        for (int j8 = 0; j8 < 8; j8++) st8(dst + j8 * 8, pack8(x + j8 * 8));
     }
     tc_fence_before();
     __syncthreads();
-    {
-        bf16* W = static_cast<bf16*>(ws.w) + slot * C * K;
-        for (int u = tid; u < C * K / 8; u += TP_THREADS) {
-            const int t = u >> 4, d0 = (u & 15) * 8;
-            st8(W + (size_t)t * K + d0, *reinterpret_cast<const Pack8*>(wst + t * WST_LD + d0));
-        }
-    }
-    (void)ok;
     if (warp == 0) {
         tc_fence_after();
         tmem_dealloc(tmem, 256);
@@ -611,18 +610,19 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     if (warp == 4) {
         if (lane == 0) {
             constexpr uint32_t ID64 = idesc(128, 64, AB_BF16);
-            constexpr uint32_t ID128 = idesc(128, 128, AB_BF16);
+            constexpr uint32_t ID64_BMN = idesc_major(128, 64, AB_BF16, 0, 1);
+            constexpr uint32_t ID128_BMN = idesc_major(128, 128, AB_BF16, 0, 1);
             auto issue_load = [&](int c) {
                 const int b = c & 1;
                 const uint32_t dst = base + OFF_BUF + b * BUF_BYTES;
                 const int row = (int)((slot0 + c) * C);
                 mbar_expect_tx(full(b), TX_BYTES);
-                tma_load_2d(dst + BUF_W, &maps.w, full(b), 0, row);
-                tma_load_2d(dst + BUF_W + SUB64, &maps.w, full(b), 64, row);
+                tma_load_2d(dst + BUF_W, &maps.w, full(b), 0, (int)((slot0 + c) * K));  // w^T [128 k][64 t]
                 tma_load_2d(dst + BUF_QD, &maps.qd, full(b), 0, row);
                 tma_load_2d(dst + BUF_QD + SUB64, &maps.qd, full(b), 64, row);
                 tma_load_2d(dst + BUF_P, &maps.p, full(b), 0, row);
-                tma_load_2d(dst + BUF_KDT, &maps.kdt, full(b), 0, (int)((slot0 + c) * K));
+                tma_load_2d(dst + BUF_KDT, &maps.kdt, full(b), 0, row);  // kd [64 t][128 k], two 64-wide blocks
+                tma_load_2d(dst + BUF_KDT + SUB64, &maps.kdt, full(b), 64, row);
             };
             int issued = 0;
             if (NC > 0) issue_load(0), issued++;
@@ -643,7 +643,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t sub = (uint32_t)(kk >> 2), off = (uint32_t)(kk & 3) * 32;
                     const uint64_t a = desc_sw128(base + OFF_ST + sub * SUB128 + off);
-                    mma_bf16(tmem + 0, a, desc_sw128(buf + BUF_W + sub * SUB64 + off), ID64, kk > 0);
+                    mma_bf16(tmem + 0, a, desc_sw128_mn(buf + BUF_W + (uint32_t)kk * 2048, SUB64, 1024), ID64_BMN,
+                             kk > 0);
                     mma_bf16(tmem + 64, a, desc_sw128(buf + BUF_QD + sub * SUB64 + off), ID64, kk > 0);
                 }
                 mma_commit(ws_done);
@@ -658,7 +659,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
                     const uint32_t off = (uint32_t)kk * 32;
                     const uint64_t a = desc_sw128(base + OFF_VN + off);
                     mma_bf16(tmem + 64, a, desc_sw128(buf + BUF_P + off), ID64, 1);
-                    mma_bf16(tmem + 128, a, desc_sw128(buf + BUF_KDT + off), ID128, kk > 0);
+                    mma_bf16(tmem + 128, a, desc_sw128_mn(buf + BUF_KDT + (uint32_t)kk * 2048, SUB64, 1024),
+                             ID128_BMN, kk > 0);
                 }
                 mma_commit(upd_done);
                 mma_commit(empty(b));
@@ -807,13 +809,13 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     if (e != cudaSuccess) return e;
     ScanMaps maps;
     const uint64_t rows64 = (uint64_t)H * slots * C, rows128 = (uint64_t)H * slots * K;
-    int r = host::make_map_2d(&maps.w, ws.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, K, K, 64, 64,
+    int r = host::make_map_2d(&maps.w, ws.w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows128, C, C, 128, 64,
                               CU_TENSOR_MAP_SWIZZLE_128B);
     if (!r) r = host::make_map_2d(&maps.qd, ws.qd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, K, K, 64, 64,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (!r) r = host::make_map_2d(&maps.p, ws.p, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, C, C, 64, 64,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
-    if (!r) r = host::make_map_2d(&maps.kdt, ws.kdt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows128, C, C, 128, 64,
+    if (!r) r = host::make_map_2d(&maps.kdt, ws.kdt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, K, K, 64, 64,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (r) return r;
     gdn_scan<<<dim3(H, seqs.count), SCAN_THREADS, SCAN_SMEM, st>>>(maps, ws, tab, static_cast<bf16*>(o), H,

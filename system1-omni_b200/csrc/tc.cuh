@@ -224,6 +224,27 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t smem_addr) {
     return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major operand stored with the 128-byte
+// swizzle: each 128-byte row holds 64 consecutive M (or N) elements (bf16) of one K index;
+// 8 K-rows form a 1024-byte atom; consecutive K-atoms are `sbo` bytes apart and
+// consecutive 64-element MN blocks `lbo` bytes apart. One MMA with K = 16 reads two
+// K-atoms, so the next K step starts 2 * sbo bytes further.
+__device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor with the operand majors: a_mn / b_mn = 1 for MN-major.
+__host__ __device__ constexpr uint32_t idesc_major(int M, int N, uint32_t ab, uint32_t a_mn, uint32_t b_mn) {
+    return (1u << 4) | (ab << 7) | (ab << 10) | (a_mn << 15) | (b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
 // Instruction descriptor: fp32 accumulate, A and B K-major, of type `ab`
 // (kind::f16: 0 = f16, 1 = bf16; kind::tf32: 2 = tf32), tile M x N.
 __host__ __device__ constexpr uint32_t idesc(int M, int N, uint32_t ab) {
