@@ -168,9 +168,11 @@ def reference_cuda(args, local):
         step()
     torch.cuda.synchronize()
     ms = (time.perf_counter() - t0) * 1e3 / n
+    lat = latency(m, args)
     m.close()
     del stream
     return {"value": tokens / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "launch_ranges": len(ranges),
+            "p50_decision_latency_ms": lat,
             "library": "reference src/backends/cuda/qwen3_5 built for sm_100a (oracle/Makefile)",
             "host": "this build's C++ host, eager, host-side scorer head (the reference's executor path)",
             "timing": "wall clock around synchronous forward calls (host copies included)",
@@ -252,6 +254,29 @@ def gemm_roofline(cs1, cfg, M, stream, torch):
     return flops / (ms * 1e-3) / 1e12, ms, flops, launches
 
 
+def single_requests(n=16, seed=5):
+    """Concurrency-1 workload of BASELINE's 27B config (a): one prompt per request."""
+    rng = np.random.default_rng(seed)
+    x = np.exp(rng.normal(np.log(800.0), 0.6, n))
+    lens = np.clip(np.round(x), 1, 8192).astype(np.int64)
+    return [rng.integers(0, 151936, int(L)).astype(np.int32) for L in lens]
+
+
+def latency(model, args):
+    """p50 / mean decision latency at concurrency 1: host ids in, 8 logits out, eager
+    (each request has its own length), wall clock per request after one warm-up."""
+    reqs = single_requests()
+    model.set_graphs(False)
+    model.forward([reqs[0]])
+    ms = []
+    for r in reqs:
+        t0 = time.perf_counter()
+        model.forward([r])
+        ms.append((time.perf_counter() - t0) * 1e3)
+    return {"p50_ms": float(np.median(ms)), "mean_ms": float(np.mean(ms)), "requests": len(reqs),
+            "tokens_median": int(np.median([len(r) for r in reqs]))}
+
+
 def run_ours(args, rank, world, local):
     import torch
     from s1omni import Cs1, Model, preset
@@ -299,6 +324,7 @@ def run_ours(args, rank, world, local):
         model.forward(seqs)
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
     e2e = float(np.median(e2e_ms[1:]))
+    lat = latency(model, args)
     h2d = tokens * 4 + tokens * 32 * 2 * 2 + BATCH * 4
     d2h = BATCH * cfg.labels * 4
     tmax = torch.tensor([ms, e2e], device="cuda")
@@ -333,6 +359,7 @@ def run_ours(args, rank, world, local):
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
                              "sample": f"one {args.cpu_tokens}-token prompt, one 4-layer period of the 27B shape "
                                        f"(numpy float32 restatement), x16 periods"},
+            "p50_decision_latency_ms": lat,
             "clocks": clocks.summary(),
             "checks": {"finite_logits_no_fault": ok, "logits_sample": logits[:4].round(4).tolist()},
         }

@@ -633,9 +633,18 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
         }
         return cudaGetLastError();
     }
-    // CTA pairs (256 x 256 tiles) when there are enough tiles to fill the SMs in pairs.
+    // Kernel choice by waves: a wave of the CTA-pair kernel is sms/2 tiles of 256x256, of
+    // the single-CTA kernels sms tiles of 128x256 or 128x128. The pair kernel does the same
+    // per-SM work per tile about 15% faster, the 128-wide kernel half the work about 20%
+    // slower; pick the smallest estimated time (waves x relative tile time).
     const long pair_tiles = (long)((M + 255) / 256) * ((N + 255) / 256);
-    if (h->pairs && pair_tiles >= h->sms / 2) {
+    const long t256 = (long)((M + BM - 1) / BM) * ((N + 255) / 256);
+    const long t128 = (long)((M + BM - 1) / BM) * ((N + 127) / 128);
+    const long slots = h->sms;
+    const double c_pair = (double)((pair_tiles + slots / 2 - 1) / (slots / 2)) * 1.0;
+    const double c_256 = (double)((t256 + slots - 1) / slots) * 1.15;
+    const double c_128 = (double)((t128 + slots - 1) / slots) * 0.6;
+    if (h->pairs && c_pair <= c_256 && c_pair <= c_128) {
         switch (epi) {
             case EPI_SWIGLU:
                 return launch_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);
@@ -645,9 +654,7 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
                 return launch_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, st);
         }
     }
-    // 256-wide tiles unless that leaves most SMs idle.
-    const long tiles256 = (long)((M + BM - 1) / BM) * ((N + 255) / 256);
-    const bool wide = epi == EPI_SWIGLU || tiles256 >= h->sms;
+    const bool wide = epi == EPI_SWIGLU || c_256 <= c_128;
     switch (epi) {
         case EPI_SWIGLU:
             return launch_tc<256, EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);

@@ -3,8 +3,15 @@ heads, attention 24/4 heads x 256) over one 4-layer period (3 GDN + 1 attention)
 
 The weights are drawn on the device by s1_model_init_random and read back with
 s1_model_get_weight, so the numpy oracle runs on exactly the weights the kernels use.
-Gates: logits within 2e-2 absolute of the oracle (BASELINE's bf16 tolerance) and of the
-reference's own CUDA library driven by the same host with the same weights.
+
+Gates. At these widths the bf16 forward has a noise floor of the same size as BASELINE's
+2e-2 logit tolerance: the numpy restatement itself moves by up to 0.028 when only its
+GEMM accumulation changes from float32 to float64 (same weights and prompts, logits up
+to 3.8), and the reference's own CUDA library differs from it by about 0.044. So:
+* logits within 2e-2 absolute of the reference's own CUDA library (built from its sources
+  by oracle/Makefile) driven by the same host with the same weights -- the north-star gate;
+* logits no further from the numpy restatement than the reference library is, plus 1e-2
+  (or within 6e-2 when the reference library was not built).
 """
 import os
 
@@ -60,4 +67,8 @@ def test_fullwidth_period_matches_oracle_and_reference(period):
         report["ours_vs_reference"] = float(np.abs(ours - theirs).max())
         report["reference_vs_oracle"] = float(np.abs(theirs - oracle).max())
     print(report)
-    assert d_oracle <= 2e-2, report
+    if "ours_vs_reference" in report:
+        assert report["ours_vs_reference"] <= 2e-2, report
+        assert d_oracle <= report["reference_vs_oracle"] + 1e-2, report
+    else:
+        assert d_oracle <= 6e-2, report
