@@ -121,7 +121,7 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
             acc = fmaf(wt[e][1], x2[e], acc);
             acc = fmaf(wt[e][2], x3[e], acc);
             acc = fmaf(wt[e][3], x0[e], acc);
-            y[e] = silu(rbf(acc));
+            y[e] = silu_fast(rbf(acc));
         }
         st8(dst + (size_t)t * dst_ld, pack8(y));
 #pragma unroll

@@ -543,11 +543,18 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
 }
 
 // ---------------------------------------------------------------- scan ----
-// 160 threads: warps 0..3 own TMEM lanes / value columns 0..127, warp 4 lane 0
-// issues TMA and MMA. Shared memory (1024-aligned tiles, 128B swizzle):
-//   ST   S^T bf16 [128 v][128 k]  as two [128][64] sub-tiles      32 KB
-//   VN   v_new^T bf16 [128 v][64 t]                                16 KB
-//   per buffer b (2): W [64][128] (2 sub-tiles), QD (2), P [64][64], KDT [128][64]   56 KB each
+// One CTA per (head, sequence), longest sequences first; two CTAs per SM.
+// 160 threads: warps 0..3 own TMEM lanes = value columns 0..127, warp 4 lane 0 issues TMA
+// and MMA. The fp32 state S^T [v][k] lives in tensor memory (columns 128..255) and is
+// accumulated there by the update MMA; per chunk each thread reads its state row, writes
+// the bf16 copy the next MMAs read from shared memory, and writes back e^{last} S before
+// the update MMA adds (kd^T v_new)^T onto it.
+// TMEM columns: [0,64) (wS)^T, [64,128) o^T, [128,256) S^T.
+// Shared memory (1024-aligned tiles, 128B swizzle):
+//   ST   S^T bf16 [128 v][128 k] as two [128][64] K-major sub-tiles     32 KB
+//   VN   v_new^T bf16 [128 v][64 t] K-major                             16 KB
+//   one operand buffer: W = w^T [128 k][64 t] MN-major, QD [64 t][128 k] K-major
+//   (2 sub-tiles), P [64 t][64 j] K-major, KD [64 t][128 k] MN-major (2 blocks)   56 KB
 constexpr int SCAN_THREADS = 160;
 constexpr int SUB64 = 64 * 128;        // bytes of a [64 rows][64 bf16] tile
 constexpr int SUB128 = 128 * 128;      // bytes of a [128 rows][64 bf16] tile
@@ -556,7 +563,7 @@ constexpr int OFF_VN = OFF_ST + 2 * SUB128;
 constexpr int OFF_BUF = OFF_VN + SUB128;
 constexpr int BUF_W = 0, BUF_QD = 2 * SUB64, BUF_P = 4 * SUB64, BUF_KDT = 5 * SUB64;
 constexpr int BUF_BYTES = 5 * SUB64 + SUB128;
-constexpr int OFF_BAR = OFF_BUF + 2 * BUF_BYTES;
+constexpr int OFF_BAR = OFF_BUF + BUF_BYTES;
 constexpr int SCAN_SMEM = OFF_BAR + 128 + 1024;
 constexpr uint32_t TX_BYTES = BUF_BYTES;
 
@@ -564,7 +571,7 @@ struct ScanMaps {
     CUtensorMap w, qd, p, kdt;
 };
 
-__global__ void __launch_bounds__(SCAN_THREADS, 1)
+__global__ void __launch_bounds__(SCAN_THREADS, 2)
     gdn_scan(const __grid_constant__ ScanMaps maps, Work ws, GdnTable tab, bf16* __restrict__ o, int H,
              const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out) {
     extern __shared__ uint8_t smem_raw[];
@@ -572,11 +579,10 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* smem = smem_raw + (base - raw);
     const uint32_t bars = base + OFF_BAR;
-    auto full = [&](int b) { return bars + 8u * b; };          // TMA landed, count 1 + tx
-    auto empty = [&](int b) { return bars + 8u * (2 + b); };   // MMAs done with buffer b
-    const uint32_t s_ready = bars + 32, ws_done = bars + 40, vn_ready = bars + 48, upd_done = bars + 56;
-    const uint32_t drain = bars + 64;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 72);
+    const uint32_t full = bars, empty = bars + 8;
+    const uint32_t s_ready = bars + 16, ws_done = bars + 24, vn_ready = bars + 32, upd_done = bars + 40;
+    const uint32_t drain = bars + 48;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 64);
 
     const int h = blockIdx.x, seq = tab.seq.order[blockIdx.y];
     const int start = tab.seq.offset[seq];
@@ -586,10 +592,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        mbar_init(full(0), 1);
-        mbar_init(full(1), 1);
-        mbar_init(empty(0), 1);
-        mbar_init(empty(1), 1);
+        mbar_init(full, 1);
+        mbar_init(empty, 1);
         mbar_init(s_ready, 128);
         mbar_init(ws_done, 1);
         mbar_init(vn_ready, 128);
@@ -605,39 +609,32 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // TMEM columns: [0,64) (wS)^T, [64,128) o^T, [128,256) S^T update
 
     if (warp == 4) {
         if (lane == 0) {
             constexpr uint32_t ID64 = idesc(128, 64, AB_BF16);
             constexpr uint32_t ID64_BMN = idesc_major(128, 64, AB_BF16, 0, 1);
             constexpr uint32_t ID128_BMN = idesc_major(128, 128, AB_BF16, 0, 1);
+            const uint32_t buf = base + OFF_BUF;
             auto issue_load = [&](int c) {
-                const int b = c & 1;
-                const uint32_t dst = base + OFF_BUF + b * BUF_BYTES;
                 const int row = (int)((slot0 + c) * C);
-                mbar_expect_tx(full(b), TX_BYTES);
-                tma_load_2d(dst + BUF_W, &maps.w, full(b), 0, (int)((slot0 + c) * K));  // w^T [128 k][64 t]
-                tma_load_2d(dst + BUF_QD, &maps.qd, full(b), 0, row);
-                tma_load_2d(dst + BUF_QD + SUB64, &maps.qd, full(b), 64, row);
-                tma_load_2d(dst + BUF_P, &maps.p, full(b), 0, row);
-                tma_load_2d(dst + BUF_KDT, &maps.kdt, full(b), 0, row);  // kd [64 t][128 k], two 64-wide blocks
-                tma_load_2d(dst + BUF_KDT + SUB64, &maps.kdt, full(b), 64, row);
+                mbar_expect_tx(full, TX_BYTES);
+                tma_load_2d(buf + BUF_W, &maps.w, full, 0, (int)((slot0 + c) * K));  // w^T [128 k][64 t]
+                tma_load_2d(buf + BUF_QD, &maps.qd, full, 0, row);
+                tma_load_2d(buf + BUF_QD + SUB64, &maps.qd, full, 64, row);
+                tma_load_2d(buf + BUF_P, &maps.p, full, 0, row);
+                tma_load_2d(buf + BUF_KDT, &maps.kdt, full, 0, row);  // kd [64 t][128 k], two 64-wide blocks
+                tma_load_2d(buf + BUF_KDT + SUB64, &maps.kdt, full, 64, row);
             };
             int issued = 0;
             if (NC > 0) issue_load(0), issued++;
-            if (NC > 1) issue_load(1), issued++;
-            bool ok = true;
-            for (int c = 0; c < NC && ok; c++) {
-                const int b = c & 1;
-                const uint32_t ph = (uint32_t)(c >> 1) & 1u;
+            for (int c = 0; c < NC; c++) {
                 const uint32_t cp = (uint32_t)c & 1u;
-                if (!mbar_wait(full(b), ph) || !mbar_wait(s_ready, cp)) {
+                if (!mbar_wait(full, cp) || !mbar_wait(s_ready, cp)) {
                     atomicOr(&g_fault_word, FAULT_WAIT_MMA);
                     break;
                 }
                 tc_fence_after();
-                const uint32_t buf = base + OFF_BUF + b * BUF_BYTES;
                 // (wS)^T -> cols [0,64), (qd S)^T -> cols [64,128); K = 128 over two sub-tiles
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {
@@ -653,69 +650,73 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                // o^T += v_new^T P^T ; S^T update = v_new^T kd  (K = 64 tokens)
+                // o^T += v_new^T P^T ; S^T += v_new^T kd  (K = 64 tokens; S^T holds e^{last} S)
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++) {
                     const uint32_t off = (uint32_t)kk * 32;
                     const uint64_t a = desc_sw128(base + OFF_VN + off);
                     mma_bf16(tmem + 64, a, desc_sw128(buf + BUF_P + off), ID64, 1);
                     mma_bf16(tmem + 128, a, desc_sw128_mn(buf + BUF_KDT + (uint32_t)kk * 2048, SUB64, 1024),
-                             ID128_BMN, kk > 0);
+                             ID128_BMN, 1);
                 }
                 mma_commit(upd_done);
-                mma_commit(empty(b));
-                if (c + 2 < NC) {
-                    if (!mbar_wait(empty(b), ph)) {
+                mma_commit(empty);
+                if (c + 1 < NC) {
+                    if (!mbar_wait(empty, cp)) {
                         atomicOr(&g_fault_word, FAULT_WAIT_MMA);
-                        ok = false;
                         break;
                     }
-                    issue_load(c + 2);
+                    issue_load(c + 1);
                     issued++;
                 }
             }
             mma_commit(drain);
             (void)mbar_wait(drain, 0);
-            // Every TMA load issued has landed before exit (already true on success).
-            for (int c = std::max(0, issued - 2); c < issued; c++) (void)mbar_wait(full(c & 1), (uint32_t)(c >> 1) & 1u);
+            if (issued > 0) (void)mbar_wait(full, (uint32_t)(issued - 1) & 1u);
         }
     } else {
-        // Thread v = threadIdx.x owns TMEM lane v and row v of S^T.
+        // Thread v = threadIdx.x owns TMEM lane v: row v of S^T and column v of o.
         const int vcol = threadIdx.x;
         const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-        float S[K];
-        if (s_in) {
-            const float* si = s_in + (long)seq * s_in_stride + (size_t)h * K * V;
+        {
+            // initial state into TMEM (zero or s_in column v)
+            const float* si = s_in ? s_in + (long)seq * s_in_stride + (size_t)h * K * V : nullptr;
 #pragma unroll
-            for (int kk = 0; kk < K; kk++) S[kk] = si[(size_t)kk * V + vcol];
-        } else {
+            for (int q4 = 0; q4 < 4; q4++) {
+                float x[32];
 #pragma unroll
-            for (int kk = 0; kk < K; kk++) S[kk] = 0.f;
+                for (int i = 0; i < 32; i++) x[i] = si ? si[(size_t)(q4 * 32 + i) * V + vcol] : 0.f;
+                tmem_st32(lane_addr + 128 + q4 * 32, x);
+            }
+            tmem_st_wait();
         }
         const bf16* UT = reinterpret_cast<const bf16*>(ws.ut);
         uint8_t* st_tile = smem + OFF_ST;
         uint8_t* vn_tile = smem + OFF_VN;
         for (int c = 0; c < NC; c++) {
             const uint32_t cp = (uint32_t)c & 1u;
-            // u^T row for this chunk (prefetched before the MMAs need it)
-            float u[C];
-            {
-                const bf16* ur = UT + ((slot0 + c) * V + vcol) * C;
+            const float dec = ws.decay[slot0 + c];
+            // S row: bf16 copy for this chunk's MMAs, then e^{last} S back for the update MMA
 #pragma unroll
-                for (int i = 0; i < C / 8; i++) unpack8(ld8(ur + i * 8), u + i * 8);
+            for (int q4 = 0; q4 < 4; q4++) {
+                float x[32];
+                tmem_ld32(lane_addr + 128 + q4 * 32, x);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int ch = q4 * 4 + i;  // 16-byte chunk of the 256-byte row
+                    *reinterpret_cast<Pack8*>(st_tile + (ch >> 3) * SUB128 + sw128_offset(vcol, ch & 7)) =
+                        pack8(x + i * 8);
+                }
+#pragma unroll
+                for (int i = 0; i < 32; i++) x[i] *= dec;
+                tmem_st32(lane_addr + 128 + q4 * 32, x);
             }
-            // S^T row v as bf16 into the swizzled operand tile
-#pragma unroll
-            for (int ch = 0; ch < 16; ch++) {
-                const int sub = ch >> 3;
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; e++) f[e] = S[ch * 8 + e];
-                *reinterpret_cast<Pack8*>(st_tile + sub * SUB128 + sw128_offset(vcol, ch & 7)) = pack8(f);
-            }
+            tmem_st_wait();
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(s_ready);
+            const bf16* ur = UT + ((slot0 + c) * V + vcol) * C;
             if (!mbar_wait(ws_done, cp)) {
                 atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
                 break;
@@ -726,12 +727,15 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
             for (int half = 0; half < 2; half++) {
                 float ws_[32];
                 tmem_ld32(lane_addr + half * 32, ws_);
+                float u[32];
+#pragma unroll
+                for (int i = 0; i < 4; i++) unpack8(ld8(ur + half * 32 + i * 8), u + i * 8);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     float f[8];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) f[e] = u[half * 32 + i * 8 + e] - ws_[i * 8 + e];
+                    for (int e = 0; e < 8; e++) f[e] = u[i * 8 + e] - ws_[i * 8 + e];
                     *reinterpret_cast<Pack8*>(vn_tile + sw128_offset(vcol, half * 4 + i)) = pack8(f);
                 }
             }
@@ -756,23 +760,19 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
                     if (t < rows) o[((size_t)(start + c * C + t) * H + h) * V + vcol] = to_bf16(ov[i]);
                 }
             }
-            // S = e^{last} S + update
-            const float dec = ws.decay[slot0 + c];
-#pragma unroll
-            for (int q4 = 0; q4 < 4; q4++) {
-                float up[32];
-                tmem_ld32(lane_addr + 128 + q4 * 32, up);
-                tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < 32; i++) S[q4 * 32 + i] = fmaf(S[q4 * 32 + i], dec, up[i]);
-            }
-            tc_fence_before();
         }
         if (s_out) {
             float* so = s_out + (long)seq * (long)H * K * V + (size_t)h * K * V;
 #pragma unroll
-            for (int kk = 0; kk < K; kk++) so[(size_t)kk * V + vcol] = S[kk];
+            for (int q4 = 0; q4 < 4; q4++) {
+                float x[32];
+                tmem_ld32(lane_addr + 128 + q4 * 32, x);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++) so[(size_t)(q4 * 32 + i) * V + vcol] = x[i];
+            }
         }
+        tc_fence_before();
     }
     tc_fence_before();
     __syncthreads();

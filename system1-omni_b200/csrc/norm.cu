@@ -108,7 +108,7 @@ __global__ void gated_kernel(const bf16* __restrict__ x, const bf16* __restrict_
     const float inv = rsqrtf(warp_sum(ss) / 128.f + eps);
     float o[4];
 #pragma unroll
-    for (int i = 0; i < 4; i++) o[i] = rbf(ww[i] * rbf(v[i] * inv)) * silu(zz[i]);
+    for (int i = 0; i < 4; i++) o[i] = rbf(ww[i] * rbf(v[i] * inv)) * silu_fast(zz[i]);
     uint2 r;
     r.x = pack_bf16x2(o[0], o[1]);
     r.y = pack_bf16x2(o[2], o[3]);
