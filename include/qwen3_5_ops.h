@@ -109,6 +109,17 @@ int cs1_gdn_prefill_fp32_x(void* context, const void* q, const void* k, const vo
                            const float* s_in, float* s_out, void* stream);
 int cs1_gdn_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
                     float* workspace, int T, int H, int HK, float scale, void* stream);   // ops.h:121
+// Additive, no counterpart in the reference: cs1_gdn_prefill for callers that cannot
+// allocate device memory (a host that may not call cudaMalloc on the path where it runs
+// the prefill). The workspace is a fixed 64 MiB device array inside this library, held by
+// every GPU that loads it until exit, so T x H is limited: roughly
+// ceil(T / 64) * H <= 910 (T <= 1152 at 48 heads, 1792 at 32, 3584 at 16); larger
+// sizes return cudaErrorInvalidValue before any launch. The first call on a device looks
+// up the array's device address (make it before any stream capture). The array keeps the
+// last call's contents; nothing needs clearing, but calls that overlap on the GPU (other
+// streams, other host threads) race on it. Allocates nothing.
+int cs1_gdn_prefill_noalloc(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                            int T, int H, int HK, float scale, void* stream);
 int cs1_gdn_prefill_wide(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
                          float* workspace, int T, int H, int HK, float scale, void* stream);   // ops.h:126
 int cs1_gdn_prefill_x(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,

@@ -61,6 +61,7 @@ SIGNATURES = {
     "cs1_gdn_prefill_fp32_x": (I, [P, P, P, P, P, P, P, P, I, I, I, F, P, P, P]),
     "cs1_gdn_prefill": (I, [P, P, P, P, P, P, P, I, I, I, F, P]),
     "cs1_gdn_prefill_wide": (I, [P, P, P, P, P, P, P, I, I, I, F, P]),
+    "cs1_gdn_prefill_noalloc": (I, [P, P, P, P, P, P, I, I, I, F, P]),
     "cs1_gdn_prefill_x": (I, [P, P, P, P, P, P, P, I, I, I, F, P, P, P]),
     "cs1_gdn_prefill_batch_x": (I, [P, P, P, P, P, P, P, Z, P, Z, I, I, F, P, I, P, P]),
     "cs1_attn_prep": (I, [P, P, I, P, P, P, P, P, P, P, I, I, I, I, I, F, P]),

@@ -1,0 +1,56 @@
+"""cs1_gdn_prefill_noalloc: the chunked GDN prefill with its workspace in the library's
+own fixed device array, for callers that cannot allocate device memory on the path where
+they run the prefill.
+
+Called through the C ABI twice in a row (a different input each time, so the second
+call runs over the first call's leftover scratch) and checked against cs1_gdn_prefill
+with a caller-owned workspace, within the GDN gate used by test_gdn_gpu.py
+(max |err| <= 2e-2 * max |ref|). Also: a size beyond the fixed scratch is rejected
+before any launch. This file is collected last so that a failure here stops a `-x` run
+only after every other test has run; it also passes alone in a fresh process.
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import dev_bf16, dev_f32, empty_bf16, host
+from oracle import fixtures
+
+pytestmark = pytest.mark.gpu
+SCALE = 128 ** -0.5
+
+
+def _inputs(T, H, HK, seed):
+    return fixtures.grouped_inputs(seed, T, H, HK)
+
+
+def _with_workspace(cs1, stream, q, k, v, g, beta, H, HK):
+    T = v.shape[0]
+    ws = torch.empty(cs1.cs1_gdn_workspace_floats(T, H), dtype=torch.float32, device="cuda")
+    o = empty_bf16(T, H, 128)
+    cs1.cs1_gdn_prefill(dev_bf16(q), dev_bf16(k), dev_bf16(v), dev_f32(g), dev_bf16(beta), o, ws, T, H, HK, SCALE,
+                        stream)
+    return host(o)
+
+
+def test_noalloc_matches_caller_workspace_twice(cs1, stream):
+    H, HK = 48, 16
+    for T, seed in ((700, 1), (333, 2)):
+        q, k, v, g, beta = _inputs(T, H, HK, seed)
+        ref = _with_workspace(cs1, stream, q, k, v, g, beta, H, HK)
+        o = empty_bf16(T, H, 128)
+        # keep the device inputs alive until the call has run on the stream
+        dq, dk, dv, dg, db = dev_bf16(q), dev_bf16(k), dev_bf16(v), dev_f32(g), dev_bf16(beta)
+        rc = cs1.raw.cs1_gdn_prefill_noalloc(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(),
+                                             db.data_ptr(), o.data_ptr(), T, H, HK, SCALE, stream)
+        assert rc == 0
+        got = host(o)
+        assert cs1.cs1_fault_status(1) == 0
+        assert np.abs(got - ref).max() <= 2e-2 * np.abs(ref).max(), (T, np.abs(got - ref).max())
+
+
+def test_noalloc_rejects_sizes_beyond_its_scratch(cs1, stream):
+    p = torch.empty(16, dtype=torch.bfloat16, device="cuda").data_ptr()
+    # 48 heads x 64 chunks needs about 226 MB of workspace, above the 64 MiB scratch
+    assert cs1.raw.cs1_gdn_prefill_noalloc(p, p, p, p, p, p, 4096, 48, 16, SCALE, stream) != 0
+    assert cs1.raw.cs1_gdn_prefill_noalloc(p, p, p, p, p, p, 64, 48, 5, SCALE, stream) != 0
