@@ -289,13 +289,22 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
                                                               const bf16* __restrict__ v, const float* __restrict__ g,
                                                               const bf16* __restrict__ beta, Work ws, GdnTable tab,
                                                               int H, int HK, float scale) {
-    const int seq = blockIdx.z;
+    // blockIdx.x enumerates the chunk slots of all packed sequences (no idle CTAs)
+    const int slot_in_pack = blockIdx.x;
+    int seq = 0;
+    {
+        int lo = 0, hi = tab.seq.count - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (tab.chunk_base[mid] <= slot_in_pack) lo = mid; else hi = mid - 1;
+        }
+        seq = lo;
+    }
     const int start = tab.seq.offset[seq];
     const int len = tab.seq.offset[seq + 1] - start;
-    const int c = blockIdx.x;
-    if (c * C >= len) return;
+    const int c = slot_in_pack - tab.chunk_base[seq];
     const int h = blockIdx.y, hk = h / (H / HK);
-    const long slot = (long)h * ws.slots + tab.chunk_base[seq] + c;
+    const long slot = (long)h * ws.slots + slot_in_pack;
     const int t0 = start + c * C;
     const int n = min(C, len - c * C);
 
@@ -332,9 +341,14 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (tid == 0) {
+        // sequential fp32 sum (the reference's order), from registers
+        float gv[C];
+#pragma unroll
+        for (int i = 0; i < C; i++) gv[i] = gg[i];
         float s = 0.f;
+#pragma unroll
         for (int i = 0; i < C; i++) {
-            s += gg[i];
+            s += gv[i];
             cum[i] = s;
         }
         ws.decay[slot] = expf(s);
@@ -443,7 +457,7 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         tmem_ld_wait();
         if (i < C) {
 #pragma unroll
-            for (int j = 0; j < C; j++) A[i * LDC + j] = j < i ? bet[i] * d[j] * expf(cum[i] - cum[j]) : 0.f;
+            for (int j = 0; j < C; j++) A[i * LDC + j] = j < i ? bet[i] * d[j] * __expf(cum[i] - cum[j]) : 0.f;
         } else {
             const int t = i - C;
             bf16* P = static_cast<bf16*>(ws.p) + slot * C * C + (size_t)t * C;
@@ -453,7 +467,7 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
                     const int j = j8 * 8 + e;
-                    f[e] = j <= t ? d[j] * expf(cum[t] - cum[j]) : 0.f;
+                    f[e] = j <= t ? d[j] * __expf(cum[t] - cum[j]) : 0.f;
                 }
                 st8(P + j8 * 8, pack8(f));
             }
@@ -693,9 +707,18 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
         const bf16* UT = reinterpret_cast<const bf16*>(ws.ut);
         uint8_t* st_tile = smem + OFF_ST;
         uint8_t* vn_tile = smem + OFF_VN;
+        float dec_next = NC > 0 ? ws.decay[slot0] : 1.f;
         for (int c = 0; c < NC; c++) {
             const uint32_t cp = (uint32_t)c & 1u;
-            const float dec = ws.decay[slot0 + c];
+            const float dec = dec_next;
+            // this chunk's u^T row (128 bytes) and the next chunk's decay, ahead of their use
+            uint4 ur4[8];
+            {
+                const uint4* ur = reinterpret_cast<const uint4*>(UT + ((slot0 + c) * V + vcol) * C);
+#pragma unroll
+                for (int i = 0; i < 8; i++) ur4[i] = ur[i];
+            }
+            if (c + 1 < NC) dec_next = ws.decay[slot0 + c + 1];
             // S row: bf16 copy for this chunk's MMAs, then e^{last} S back for the update MMA
 #pragma unroll
             for (int q4 = 0; q4 < 4; q4++) {
@@ -716,20 +739,18 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(s_ready);
-            const bf16* ur = UT + ((slot0 + c) * V + vcol) * C;
-            if (!mbar_wait(ws_done, cp)) {
-                atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
-                break;
-            }
+            // A wait that gives up does not leave the loop on its own: the group decides
+            // together at the named barrier below, so no thread waits there for one that left.
+            bool ok = mbar_wait(ws_done, cp);
             tc_fence_after();
             // v_new = bf16(u - wS)
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
+            for (int half = 0; ok && half < 2; half++) {
                 float ws_[32];
                 tmem_ld32(lane_addr + half * 32, ws_);
                 float u[32];
 #pragma unroll
-                for (int i = 0; i < 4; i++) unpack8(ld8(ur + half * 32 + i * 8), u + i * 8);
+                for (int i = 0; i < 4; i++) unpack8(*reinterpret_cast<const Pack8*>(&ur4[half * 4 + i]), u + i * 8);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -742,24 +763,33 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(vn_ready);
-            if (!mbar_wait(upd_done, cp)) {
-                atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
-                break;
-            }
+            ok = ok && mbar_wait(upd_done, cp);
             tc_fence_after();
-            // o rows of this chunk, column v
+            // o rows of this chunk: column v into a [64 t][128 v] staging tile (the v_new
+            // tile is free once the update MMAs are done), then 16-byte row stores
             const int rows = min(C, len - c * C);
+            bf16* ost = reinterpret_cast<bf16*>(vn_tile);
 #pragma unroll
-            for (int half = 0; half < 2; half++) {
+            for (int half = 0; ok && half < 2; half++) {
                 float ov[32];
                 tmem_ld32(lane_addr + 64 + half * 32, ov);
                 tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i++) {
-                    const int t = half * 32 + i;
-                    if (t < rows) o[((size_t)(start + c * C + t) * H + h) * V + vcol] = to_bf16(ov[i]);
-                }
+                for (int i = 0; i < 32; i++) ost[(half * 32 + i) * V + vcol] = to_bf16(ov[i]);
             }
+            if (bar_any(1, 128, !ok)) {
+                atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+                break;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int u = vcol + i * 128;  // 16-byte unit: row u / 16, columns (u % 16) * 8
+                const int t = u >> 4, v8 = (u & 15) * 8;
+                if (t < rows)
+                    st8(o + ((size_t)(start + c * C + t) * H + h) * V + v8,
+                        *reinterpret_cast<const Pack8*>(ost + t * V + v8));
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
         }
         if (s_out) {
             float* so = s_out + (long)seq * (long)H * K * V + (size_t)h * K * V;
@@ -802,7 +832,7 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     if (configured != cudaSuccess) return configured;
     uint8_t* b = static_cast<uint8_t*>(workspace);
     Work ws{b + L.w, b + L.qd, b + L.p, b + L.kdt, b + L.ut, reinterpret_cast<float*>(b + L.decay), slots};
-    gdn_prep_tc<<<dim3(tab.max_chunks, H, seqs.count), TP_THREADS, TP_SMEM, st>>>(
+    gdn_prep_tc<<<dim3((unsigned)slots, H), TP_THREADS, TP_SMEM, st>>>(
         static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), g,
         static_cast<const bf16*>(beta), ws, tab, H, HK, scale);
     cudaError_t e = cudaGetLastError();

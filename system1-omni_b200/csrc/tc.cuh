@@ -115,6 +115,16 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Named barrier `id` over `n` threads that also returns whether any of them passed true.
+__device__ __forceinline__ bool bar_any(int id, int n, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred a, b;\n setp.ne.u32 a, %1, 0;\n bar.red.or.pred b, %2, %3, a;\n selp.u32 %0, 1, 0, b;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)p), "r"(id), "r"(n)
+        : "memory");
+    return r != 0;
+}
 
 // ---- tcgen05: tensor memory ----
 // Allocate `cols` columns (a power of two >= 32); the whole warp executes this.
