@@ -17,6 +17,8 @@
 // rows (positions continue after it), a windowed first query row, and the
 // bidirectional / prefix-bidirectional masks.
 #include <climits>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "ops_internal.h"
@@ -290,14 +292,404 @@ __global__ void __launch_bounds__(THREADS, 1) flash_kernel(Args a, SeqTable tab)
     }
 }
 
+// ------------------------------------------------------- flash (tcgen05) ----
+// A CTA takes 128 queries of one head. Per 128-key tile j:
+//   S_j = Q K_j^T   tcgen05.mma M=128 N=128 K=256 into one of two TMEM buffers
+//   softmax         4 warps, thread = query row = TMEM lane: masked row max, exp2,
+//                   bf16 P_j into shared memory (the A operand of the next MMA)
+//   O += P_j V_j    tcgen05.mma M=128 N=256 K=128 into TMEM (V as an MN-major B operand)
+// The MMA thread issues S_{j+1} before PV_j, so the tensor pipe computes the next
+// scores while the softmax warps work. O is rescaled only when a row's maximum grows
+// by more than 2^8 over the base its probabilities were taken against (the sum l uses
+// the same base, so the quotient is unchanged; p <= 2^8 loses nothing in bf16).
+// Q, K and V arrive by TMA (128-byte swizzle, one head per box, prefix K/V from their
+// own tensor maps); K is released per 64-dim block as soon as its MMAs have completed.
+// Warp 0: TMA producer; warp 1: TMEM allocation and MMA issue; warps 2-5: softmax and
+// the epilogue (O / l staged through shared memory, gate applied on coalesced rows).
+namespace tca {
+
+constexpr int BM = 128, BN = 128, THREADS = 192;
+constexpr int SUB = 128 * 128;  // one [128 rows][64 bf16] swizzled tile, 16 KB
+constexpr int OFF_Q = 0, OFF_K = 4 * SUB, OFF_V = 8 * SUB, OFF_P = 12 * SUB, OFF_BAR = 14 * SUB;
+constexpr int SMEM = OFF_BAR + 256 + 1024;
+constexpr uint32_t ID_S = tc::idesc(128, BN, tc::AB_BF16);
+constexpr uint32_t ID_O = tc::idesc_major(128, DH, tc::AB_BF16, 0, 1);
+constexpr float RESCALE_LOG2 = 8.f;
+
+struct Maps {
+    CUtensorMap q, k, v, pk, pv;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ int query_blocks(const SeqTable& tab, int i, int q_base) {
+    const int rows = tab.offset[i + 1] - tab.offset[i] - q_base;
+    return rows > 0 ? (rows + BM - 1) / BM : 0;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    flash_tc(const __grid_constant__ Maps maps, Args a, SeqTable tab) {
+    using namespace tc;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + OFF_BAR;
+    const uint32_t q_full = bars, k_full = bars + 8, k_empty = bars + 40, v_full = bars + 72, v_empty = bars + 80;
+    const uint32_t s_full = bars + 88, s_free = bars + 104, p_full = bars + 120, pv_done = bars + 128;
+    const uint32_t drain = bars + 136;
+    int* info = reinterpret_cast<int*>(smem + OFF_BAR + 160);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 192);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (warp == 0) {
+        // blockIdx.y -> (sequence, query block): sequences in the table's order (longest
+        // first), the blocks of one sequence last-first (the most key tiles first)
+        const int target = blockIdx.y;
+        int cnt[8], local = 0;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const int pos = lane * 8 + e;
+            cnt[e] = pos < tab.count ? query_blocks(tab, tab.order[pos], a.q_base) : 0;
+            local += cnt[e];
+        }
+        int incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int first = incl - local;
+        if (target >= first && target < incl) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                if (target >= first && target < first + cnt[e]) {
+                    info[0] = tab.order[lane * 8 + e];
+                    info[1] = cnt[e] - 1 - (target - first);
+                }
+                first += cnt[e];
+            }
+        }
+    }
+    if (threadIdx.x == 32) {
+        mbar_init(q_full, 1);
+        for (int d = 0; d < 4; d++) {
+            mbar_init(k_full + 8 * d, 1);
+            mbar_init(k_empty + 8 * d, 1);
+        }
+        mbar_init(v_full, 1);
+        mbar_init(v_empty, 1);
+        mbar_init(s_full, 1);
+        mbar_init(s_full + 8, 1);
+        mbar_init(s_free, 128);
+        mbar_init(s_free + 8, 128);
+        mbar_init(p_full, 128);
+        mbar_init(pv_done, 1);
+        mbar_init(drain, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int seq = info[0], qb = info[1];
+    const int h = blockIdx.x, hk = h / (a.Hq / a.Hk);
+    const int off = tab.offset[seq];
+    const int len = tab.offset[seq + 1] - off;
+    const int q0 = a.q_base + qb * BM;  // first own query row of this block
+    const int P = a.P;
+    const int total = P + len;          // keys visible to this sequence
+    const int qpos0 = P + q0;           // position of the block's first query
+    const int kv_end = a.causal ? min(total, qpos0 + BM) : total;
+    const int n = (kv_end + BN - 1) / BN;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int kc[4] = {0, 0, 0, 0}, vc = 0;
+            bool ok = true;
+            mbar_expect_tx(q_full, 4 * SUB);
+#pragma unroll
+            for (int d = 0; d < 4; d++) tma_load_3d(base + OFF_Q + d * SUB, &maps.q, q_full, d * 64, h, off + q0);
+            auto load_kv = [&](uint32_t dst, const CUtensorMap* own, const CUtensorMap* pre, uint32_t bar, int d,
+                               int j) {
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    const int key0 = j * BN + hf * 64;  // P is a multiple of 64: a half is all prefix or all own
+                    if (key0 < P)
+                        tma_load_3d(dst + hf * (SUB / 2), pre, bar, d * 64, hk, key0);
+                    else
+                        tma_load_3d(dst + hf * (SUB / 2), own, bar, d * 64, hk, off + key0 - P);
+                }
+            };
+            // order of use: K_0, K_1, V_0, K_2, V_1, ... (S_{j+1} is issued before PV_j)
+            for (int j = 0; ok && j <= n; j++) {
+                if (j < n) {
+                    for (int d = 0; d < 4 && ok; d++) {
+                        if (j > 0 && !mbar_wait(k_empty + 8 * d, (uint32_t)(j - 1) & 1u)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(k_full + 8 * d, SUB);
+                        load_kv(base + OFF_K + d * SUB, &maps.k, &maps.pk, k_full + 8 * d, d, j);
+                        kc[d]++;
+                    }
+                }
+                if (ok && j > 0) {
+                    const int t = j - 1;
+                    if (t > 0 && !mbar_wait(v_empty, (uint32_t)(t - 1) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(v_full, 4 * SUB);
+#pragma unroll
+                    for (int d = 0; d < 4; d++) load_kv(base + OFF_V + d * SUB, &maps.v, &maps.pv, v_full, d, t);
+                    vc++;
+                }
+            }
+            if (!ok) atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
+            // the copies still in flight land before this CTA can leave
+            (void)mbar_wait(q_full, 0);
+            for (int d = 0; d < 4; d++)
+                if (kc[d] > 0) (void)mbar_wait(k_full + 8 * d, (uint32_t)(kc[d] - 1) & 1u);
+            if (vc > 0) (void)mbar_wait(v_full, (uint32_t)(vc - 1) & 1u);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = mbar_wait(q_full, 0);
+            tc_fence_after();
+            auto pv = [&](int i) -> bool {
+                if (!mbar_wait(p_full, (uint32_t)i & 1u) || !mbar_wait(v_full, (uint32_t)i & 1u)) return false;
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; kk++)
+                    mma_bf16(tmem + 256, desc_sw128(base + OFF_P + (kk >> 2) * SUB + (kk & 3) * 32),
+                             desc_sw128_mn(base + OFF_V + kk * 2048, SUB, 1024), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(v_empty);
+                mma_commit(pv_done);
+                return true;
+            };
+            for (int j = 0; ok && j < n; j++) {
+                const int b = j & 1;
+                if (j >= 2 && !mbar_wait(s_free + 8 * b, (uint32_t)((j - 2) >> 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int d = 0; d < 4; d++) {
+                    if (!mbar_wait(k_full + 8 * d, (uint32_t)j & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)
+                        mma_bf16(tmem + b * BN, desc_sw128(base + OFF_Q + d * SUB + kk * 32),
+                                 desc_sw128(base + OFF_K + d * SUB + kk * 32), ID_S, (d | kk) ? 1u : 0u);
+                    mma_commit(k_empty + 8 * d);
+                }
+                if (!ok) break;
+                mma_commit(s_full + 8 * b);
+                if (j >= 1) ok = pv(j - 1);
+            }
+            if (ok && n > 0) ok = pv(n - 1);
+            if (!ok) atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+            mma_commit(drain);
+            (void)mbar_wait(drain, 0);
+        }
+    } else {
+        const int wq = warp & 3;  // this warp's quarter of the TMEM lanes
+        const int r = wq * 32 + lane;
+        const uint32_t lane_addr = tmem + ((uint32_t)(wq * 32) << 16);
+        const int qpos = qpos0 + r;
+        const float sl2 = a.scale_log2;
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n; j++) {
+            const int b = j & 1;
+            // tcgen05.ld/st are warp-collective: every wait outcome is made warp-uniform
+            if (!__all_sync(0xffffffffu, mbar_wait(s_full + 8 * b, (uint32_t)(j >> 1) & 1u))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            float s[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; c++) tmem_ld32(lane_addr + b * BN + c * 32, s[c]);
+            tmem_ld_wait();
+            tc_fence_before();
+            mbar_arrive(s_free + 8 * b);
+            const int k0 = j * BN;
+            bool full = k0 + BN <= total;
+            if (a.causal)
+                full = full && k0 + BN - 1 <= qpos;
+            else if (a.state > 0 && qpos < a.state)
+                full = full && k0 + BN <= a.state;
+            float mx = -INFINITY;
+            if (full) {
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+#pragma unroll
+                    for (int e = 0; e < 32; e++) mx = fmaxf(mx, s[c][e]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; c++)
+#pragma unroll
+                    for (int e = 0; e < 32; e++) {
+                        const int key = k0 + c * 32 + e;
+                        bool vis = key < total;
+                        if (a.causal)
+                            vis = vis && key <= qpos;
+                        else if (a.state > 0 && qpos < a.state)
+                            vis = vis && key < a.state;
+                        s[c][e] = vis ? s[c][e] : -INFINITY;
+                        mx = fmaxf(mx, s[c][e]);
+                    }
+            }
+            mx *= sl2;
+            // PV_{j-1} must be complete before P is overwritten or O rescaled
+            if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (uint32_t)(j - 1) & 1u))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const bool grow = mx > m + RESCALE_LOG2;
+            const float alpha = grow ? ex2(m - mx) : 1.f;
+            l *= alpha;
+            if (grow) m = mx;
+            // the warp rescales its 32 rows of O together (factor 1 for rows that keep their base)
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+#pragma unroll 1
+                for (int c = 0; c < DH / 32; c++) {
+                    float o[32];
+                    tmem_ld32(lane_addr + 256 + c * 32, o);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; e++) o[e] *= alpha;
+                    tmem_st32(lane_addr + 256 + c * 32, o);
+                }
+                tmem_st_wait();
+            }
+            const float nm = m == -INFINITY ? 0.f : -m;
+            uint8_t* prow = smem + OFF_P;
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+#pragma unroll
+                for (int g8 = 0; g8 < 4; g8++) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        f[e] = ex2(fmaf(s[c][g8 * 8 + e], sl2, nm));
+                        l += f[e];
+                    }
+                    const int chunk = c * 4 + g8;  // 16-byte chunk of the 128-key row
+                    *reinterpret_cast<Pack8*>(prow + (chunk >> 3) * SUB + sw128_offset(r, chunk & 7)) = pack8(f);
+                }
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (ok && n > 0) ok = mbar_wait(pv_done, (uint32_t)(n - 1) & 1u);
+        tc_fence_after();
+        if (bar_any(1, 128, !ok)) {  // uniform over the four warps: the loads below are collective
+            if (r == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+        } else {
+            // bf16(O / l) into the Q tile (free: every MMA has completed), row r with its
+            // 16-byte chunks rotated by r so that the row-per-thread writes spread over banks
+            const float inv = 1.f / l;
+            bf16* stage = reinterpret_cast<bf16*>(smem + OFF_Q);
+#pragma unroll 1
+            for (int c = 0; c < DH / 32; c++) {
+                float o[32];
+                tmem_ld32(lane_addr + 256 + c * 32, o);
+                tmem_ld_wait();
+#pragma unroll
+                for (int g8 = 0; g8 < 4; g8++) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) f[e] = o[g8 * 8 + e] * inv;
+                    const int chunk = c * 4 + g8;
+                    st8(stage + r * DH + ((chunk ^ r) & 31) * 8, pack8(f));
+                }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const int t = threadIdx.x - 64, chunk = t & 31;
+#pragma unroll 4
+            for (int i = 0; i < BM / 4; i++) {
+                const int row = (t >> 5) + 4 * i;
+                const int lrow = q0 + row;
+                if (lrow >= len) break;
+                float x[8];
+                unpack8(ld8(stage + row * DH + ((chunk ^ row) & 31) * 8), x);
+                const size_t o_off = ((size_t)(off + lrow) * a.Hq + h) * DH + chunk * 8;
+                if (a.gated) {
+                    float gv[8];
+                    unpack8(ld8(a.gate + o_off), gv);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) x[e] = x[e] * rbf(sigmoid(gv[e]));
+                }
+                st8(a.out + o_off, pack8(x));
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+bool use_tc() {
+    static const bool on = [] {
+        const char* e = getenv("S1_ATTN_TC");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(flash_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (configured != cudaSuccess) return configured;
+    const int rows = tab.offset[tab.count];
+    Maps maps;
+    memset(&maps, 0, sizeof(maps));
+    int e = host::make_map_3d_bf16(&maps.q, a.q, DH, a.Hq, rows, DH, (uint64_t)a.Hq * DH, 64, BM);
+    if (!e) e = host::make_map_3d_bf16(&maps.k, a.k, DH, a.Hk, rows, DH, (uint64_t)a.Hk * DH, 64, 64);
+    if (!e) e = host::make_map_3d_bf16(&maps.v, a.v, DH, a.Hk, rows, DH, (uint64_t)a.ldv, 64, 64);
+    if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pk, a.pk, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
+    if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pv, a.pv, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
+    if (e) return e;
+    flash_tc<<<dim3(a.Hq, blocks), THREADS, SMEM, st>>>(maps, a, tab);
+    return cudaGetLastError();
+}
+
+}  // namespace tca
+
 int launch(Args a, const SeqTable& tab, cudaStream_t st) {
     if (a.Hq <= 0 || a.Hk <= 0 || a.Hq % a.Hk || a.ldv % 8 || a.ldv < a.Hk * DH) return cudaErrorInvalidValue;
+    int max_rows = 0, blocks = 0;
+    for (int i = 0; i < tab.count; i++) {
+        const int rows = tab.offset[i + 1] - tab.offset[i] - a.q_base;
+        max_rows = max(max_rows, rows);
+        if (rows > 0) blocks += (rows + BM - 1) / BM;
+    }
+    if (max_rows <= 0) return cudaSuccess;
+    const bool aligned = aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.out) &&
+                         (!a.gated || aligned16(a.gate)) &&
+                         (a.P == 0 || (a.P % 64 == 0 && aligned16(a.pk) && aligned16(a.pv)));
+    if (aligned && tca::use_tc()) return tca::launch_tc(a, tab, blocks, st);
     static const cudaError_t configured =
         cudaFuncSetAttribute(flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (configured != cudaSuccess) return configured;
-    int max_rows = 0;
-    for (int i = 0; i < tab.count; i++) max_rows = max(max_rows, tab.offset[i + 1] - tab.offset[i] - a.q_base);
-    if (max_rows <= 0) return cudaSuccess;
     const dim3 grid((max_rows + BM - 1) / BM, a.Hq, tab.count);
     flash_kernel<<<grid, THREADS, SMEM, st>>>(a, tab);
     return cudaGetLastError();

@@ -741,7 +741,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
             mbar_arrive(s_ready);
             // A wait that gives up does not leave the loop on its own: the group decides
             // together at the named barrier below, so no thread waits there for one that left.
-            bool ok = mbar_wait(ws_done, cp);
+            // tcgen05.ld is warp-collective: the wait outcome is made warp-uniform
+            bool ok = __all_sync(0xffffffffu, mbar_wait(ws_done, cp));
             tc_fence_after();
             // v_new = bf16(u - wS)
 #pragma unroll
@@ -763,7 +764,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
             fence_async_smem();
             tc_fence_before();
             mbar_arrive(vn_ready);
-            ok = ok && mbar_wait(upd_done, cp);
+            ok = __all_sync(0xffffffffu, ok && mbar_wait(upd_done, cp));
             tc_fence_after();
             // o rows of this chunk: column v into a [64 t][128 v] staging tile (the v_new
             // tile is free once the update MMAs are done), then 16-byte row stores

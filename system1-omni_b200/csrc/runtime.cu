@@ -41,6 +41,20 @@ int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type, in
     return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
 }
 
+int make_map_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t mid, uint64_t rows,
+                     uint64_t mid_pitch, uint64_t row_pitch, uint32_t box_inner, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_tiled();
+    if (!fn) return cudaErrorNotSupported;
+    const cuuint64_t dims[3] = {inner, mid, rows};
+    const cuuint64_t strides[2] = {mid_pitch * 2, row_pitch * 2};
+    const cuuint32_t box[3] = {box_inner, 1, box_rows};
+    const cuuint32_t elem_strides[3] = {1, 1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                          elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
+}
+
 int num_sms() {
     static int cache[64] = {0};
     int dev = 0;

@@ -295,6 +295,12 @@ EncodeTiledFn encode_tiled();
 int make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType type, int elem_bytes, uint64_t rows,
                 uint64_t cols, uint64_t ld, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle);
 
+// bf16 tensor [rows][mid][inner] with pitches in elements (mid_pitch between the middle
+// index, row_pitch between rows), boxes of box_rows x 1 x box_inner, 128B swizzle: one
+// head's [box_rows][box_inner] tile per load.
+int make_map_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t mid, uint64_t rows,
+                     uint64_t mid_pitch, uint64_t row_pitch, uint32_t box_inner, uint32_t box_rows);
+
 int num_sms();
 
 }  // namespace host

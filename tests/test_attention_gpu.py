@@ -141,3 +141,28 @@ def test_attention_prefix_bidirectional(cs1, stream):
     got = host(out)
     assert np.array_equal(got[state:], host(bid)[state:])
     assert np.array_equal(got[:state], host(st))
+
+
+def test_attention_growing_scores_rescale(cs1, stream):
+    """Keys whose norm grows along the sequence: each row's running maximum keeps rising
+    over the key tiles, so the deferred rescale of the output accumulator is exercised."""
+    T, Hq, Hk = 700, 4, 2
+    q, k, vfull, ldv, gate = _qkv(T, Hq, Hk, 51)
+    k = rnd((k * np.linspace(0.1, 4.0, T, dtype=np.float32)[:, None, None]).astype(np.float32))
+    out = empty_bf16(T, Hq, 256)
+    cs1.cs1_attention_gated(dev_bf16(q), dev_bf16(k), dev_bf16(vfull), ldv, dev_bf16(gate), out, T, Hq, Hk, 256, SCALE,
+                            stream)
+    v = vfull[:, :Hk * 256].reshape(T, Hk, 256)
+    assert _row_rel(host(out), ops.attention_gated(q, k, v, gate, SCALE)) <= 1.6e-2
+
+
+def test_attention_long_gqa6(cs1, stream):
+    """27B head grouping (6 query heads per key head) over 12 key tiles."""
+    T, Hq, Hk = 1500, 6, 1
+    q, k, vfull, ldv, gate = _qkv(T, Hq, Hk, 61)
+    out = empty_bf16(T, Hq, 256)
+    cs1.cs1_attention_gated(dev_bf16(q), dev_bf16(k), dev_bf16(vfull), ldv, dev_bf16(gate), out, T, Hq, Hk, 256, SCALE,
+                            stream)
+    v = vfull[:, :Hk * 256].reshape(T, Hk, 256)
+    assert _row_rel(host(out), ops.attention_gated(q, k, v, gate, SCALE)) <= 1.6e-2
+    assert cs1.cs1_fault_status(1) == 0
