@@ -7,7 +7,9 @@ of BASELINE's 27B config: prompt lengths log-normal, median 800, sigma 0.6, clip
 1..8192; synthetic uniform token ids; random-init bf16 weights of the 27B shape) through
 the C++ host and the sm_100a kernels, scored by the 8-label head on each final token.
 Weak scaling: every rank processes its own batch of 32 requests with a full weight
-replica; no collective on the hot path. Prints one JSON line on rank 0.
+replica; no collective on the hot path. Prints one JSON line on rank 0. Rank 0 also
+times workload (b), one 32,768-token prefill (`long_prefill` in the line; `--no-long`
+skips it).
 
 `--impl reference` times the reference's CPU path on the host cores instead: the numpy
 restatement of the same forward (the reference's prefill exists only as GPU code; its CPU
@@ -30,6 +32,14 @@ import numpy as np  # noqa: E402
 METRIC = "prefill tokens/s (27B-shape hybrid scorer, batch of 32 requests per GPU)"
 UNIT = "tokens/s"
 BATCH = 32
+
+
+LONG = 32768  # workload (b) of BASELINE's 27B config: one 32,768-token prefill
+
+
+def long_request(seed=5):
+    rng = np.random.default_rng(seed)
+    return rng.integers(0, 151936, LONG).astype(np.int32)
 
 
 def requests(rank, n=BATCH, seed=4):
@@ -209,9 +219,16 @@ def run_reference(args, rank, world):
 
 
 # ------------------------------------------------------------------ GPU arm ----
+# DRAM traffic of one gemm_pair_kernel<SWIGLU> launch at M = 29,122 (N = 34,816, K = 5,120),
+# dram__bytes_read.sum + dram__bytes_write.sum from the ncu capture summarised in
+# profiles/gemm_swiglu_29122x34816x5120.md; scaled by rows for another M.
+SWIGLU_TRAFFIC = {"m": 29122, "bytes": None}
+
+
 def gemm_roofline(cs1, cfg, M, stream, torch):
     """Time the projection GEMMs of one GDN layer, one attention layer and the MLP at the
-    workload's M with CUDA events on the launching stream; return TFLOP/s and ms."""
+    workload's M with CUDA events on the launching stream; return the set's TFLOP/s, ms,
+    FLOPs and, per shape, (kind, N, K, ms)."""
     H, I_ = cfg.hidden, cfg.intermediate
     kd, vd, hv = cfg.lin_k_heads * 128, cfg.lin_v_heads * 128, cfg.lin_v_heads
     shapes = [((2 * kd + vd) + vd + 2 * hv, H, "store"), (H, vd, "residual"),
@@ -221,7 +238,7 @@ def gemm_roofline(cs1, cfg, M, stream, torch):
     x = torch.randn(M, max(I_, H), device="cuda").to(torch.bfloat16) * 0.5
     flops = 0.0
     ms = 0.0
-    launches = 0
+    per_shape = []
     for N, K, kind in shapes:
         w = (torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16)
         out_n = N // 2 if kind == "swiglu" else N
@@ -246,12 +263,35 @@ def gemm_roofline(cs1, cfg, M, stream, torch):
             call()
         e.record(torch.cuda.current_stream())
         torch.cuda.synchronize()
-        ms += s.elapsed_time(e) / reps
+        t = s.elapsed_time(e) / reps
+        ms += t
         flops += 2.0 * M * N * K
-        launches += 1
+        per_shape.append((kind, N, K, t))
         del w, y, xs
     cs1.cs1_gemm_destroy(h)
-    return flops / (ms * 1e-3) / 1e12, ms, flops, launches
+    return flops / (ms * 1e-3) / 1e12, ms, flops, per_shape
+
+
+def long_prefill(model, torch, stream, steps=3):
+    """Workload (b): one 32,768-token prefill, staged in HBM, CUDA-graph replay timed with
+    CUDA events on the model's stream."""
+    seq = long_request()
+    model.set_graphs(True)
+    model.stage([seq])
+    for _ in range(3):
+        model.run_staged()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record(stream)
+    for _ in range(steps):
+        model.run_staged()
+    e.record(stream)
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    logits = model.fetch_logits()
+    return {"workload": "27b-b-32k", "tokens": LONG, "value": LONG / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
+            "steps": steps, "warmup": 3, "seed": 5, "finite": bool(np.isfinite(logits).all()),
+            "logits": logits[0].round(4).tolist()}
 
 
 def single_requests(n=16, seed=5):
@@ -289,7 +329,7 @@ def run_ours(args, rank, world, local):
     cfg = preset("27b")
     seqs = requests(rank)
     tokens = int(sum(len(s) for s in seqs))
-    cap = max(tokens, 1) + 64
+    cap = max(tokens, 0 if args.no_long else LONG) + 64
     model = Model(cfg, device=local, max_tokens=cap, max_seqs=BATCH)
     model.init_random(seed=1234, std=0.02)
     cs1 = Cs1()
@@ -327,6 +367,7 @@ def run_ours(args, rank, world, local):
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
     e2e = float(np.median(e2e_ms[1:]))
     lat = latency(model, args)
+    long = long_prefill(model, torch, stream) if rank == 0 and not args.no_long else None
     h2d = tokens * 4 + tokens * 32 * 2 * 2 + BATCH * 4
     d2h = BATCH * cfg.labels * 4
     tmax = torch.tensor([ms, e2e], device="cuda")
@@ -338,8 +379,13 @@ def run_ours(args, rank, world, local):
     total_tokens = float(tok[0])
     result = None
     if rank == 0:
-        tflops, gms, gflops, _ = gemm_roofline(cs1, cfg, tokens, torch.cuda.current_stream().cuda_stream, torch)
+        tflops, gms, gflops, per_shape = gemm_roofline(cs1, cfg, tokens, torch.cuda.current_stream().cuda_stream,
+                                                       torch)
         peak_tf, peak_bw, peak_kind = measured_peaks()
+        _, sw_n, sw_k, sw_ms = next(x for x in per_shape if x[0] == "swiglu")
+        sw_flops = 2.0 * tokens * sw_n * sw_k
+        sw_tf = sw_flops / (sw_ms * 1e-3) / 1e12
+        sw_traffic = (SWIGLU_TRAFFIC["bytes"] * tokens / SWIGLU_TRAFFIC["m"]) if SWIGLU_TRAFFIC["bytes"] else None
         value = total_tokens / (ms_max * 1e-3)
         proj = cfg.projection_flops_per_token() * tokens
         cpu_v, cpu_dt, cpu_threads = cpu_sample(args.cpu_tokens) if not args.no_cpu else (None, 0.0, 0)
@@ -354,14 +400,19 @@ def run_ours(args, rank, world, local):
             "e2e": {"value": total_tokens / (e2e_max * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches_per_step * args.steps),
-            "roofline": {"bound": "tensor", "kernel": "tcgen05 projection GEMM (6 shapes of a layer set)",
-                         "achieved": tflops, "peak": peak_tf, "unit": "TFLOP/s", "frac": tflops / peak_tf,
-                         "peak_kind": peak_kind + " burst bf16", "traffic": None,
+            "roofline": {"bound": "tensor",
+                         "kernel": f"gemm_pair_kernel<SWIGLU> (MLP gate/up + SwiGLU), M={tokens} N={sw_n} K={sw_k}",
+                         "achieved": sw_tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": sw_tf / peak_tf,
+                         "peak_kind": peak_kind + " burst bf16", "ms_per_launch": sw_ms,
+                         "algorithmic_flops_per_launch": sw_flops, "traffic": sw_traffic,
+                         "traffic_unit": "bytes per launch (ncu dram read + write)",
+                         "projection_set": {"shapes": len(per_shape), "tflops": tflops, "frac": tflops / peak_tf},
                          "forward_projection_tflops": proj / (ms_max * 1e-3) / 1e12},
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
                              "sample": f"one {args.cpu_tokens}-token prompt, one 4-layer period of the 27B shape "
                                        f"(numpy float32 restatement), x16 periods"},
             "p50_decision_latency_ms": lat,
+            "long_prefill": long,
             "clocks": clocks.summary(),
             "checks": {"finite_logits_no_fault": ok, "logits_sample": logits[:4].round(4).tolist()},
         }
@@ -382,6 +433,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ref-cuda", action="store_true")
+    ap.add_argument("--no-long", action="store_true", help="skip workload (b), the 32,768-token prefill")
     args = ap.parse_args()
     if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
         # one process per GPU: relaunch under torch.distributed.run on this node

@@ -244,33 +244,38 @@ __global__ void __launch_bounds__(PREP_THREADS) gdn_prep(const bf16* __restrict_
 }
 
 // ------------------------------------------------------- prep on tcgen05 ----
-// One CTA (256 threads, 2 per SM) per (chunk, head, sequence); every operand is used in
-// the layout it is produced in (no transposes):
-//  1. cum = sequential fp32 cumsum of g. Each warp loads 8 rows of q and k with 8-byte
-//     lane accesses, normalises them (k / |k|, q / |q| * scale) and writes
-//       - the TF32-rounded [kn ; qn] rows into a K-major fp32 operand tile (128B swizzle),
-//       - qd = bf16(qn e^cum) and kd = bf16(kn e^(last-cum)) rows straight to the workspace,
-//       - kw = bf16(kn e^cum) rows into an MN-major bf16 operand tile (rows = token j).
-//  2. MMA1 (kind::tf32, M=128, N=64, K=128): D[i][j] = [kn;qn]_i . kn_j in TMEM. Lanes
-//     0..63 give A_ij = beta_i kk_ij e^(cum_i-cum_j) (j < i); lanes 64..127 give
-//     P_tj = qk_tj e^(cum_t-cum_j) (j <= t), stored bf16. v rows go (16-byte loads) into
-//     an MN-major bf16 tile meanwhile.
-//  3. T = (I + A)^-1 blockwise on CUDA cores (16x16 diagonal substitutions, then block
-//     rows T_ij = -T_ii sum_k A_ik T_kj); tb = bf16(T diag(beta)) as a K-major tile.
-//  4. MMA2 (kind::f16, A MN-major, M=128, N=64, K=64): u^T = v^T tb^T and
-//     w^T = kw^T tb^T; each thread stores its TMEM row (128 contiguous bytes).
+// One CTA (256 threads, 2 per SM) per (chunk slot, head) over all packed sequences;
+// every operand is used in the layout it is produced in (no transposes):
+//  1. v arrives by TMA in an MN-major bf16 tile (rows = token j). Each warp loads 8 rows
+//     of q and k (8-byte lane accesses) and normalises them (k / |k|, q / |q| * scale)
+//     into a K-major TF32 operand tile (128B swizzle) while one thread forms the
+//     sequential fp32 cumsum of g. MMA1 is issued, then qd = bf16(qn e^cum) and
+//     kd = bf16(kn e^(last-cum)) go to the workspace and kw = bf16(kn e^cum) into an
+//     MN-major operand tile.
+//  2. MMA1 (kind::tf32, M=128, N=64, K=128): D[i][j] = [kn;qn]_i . kn_j in TMEM, read by
+//     all 8 warps (one column half each): lanes 0..63 give A_ij = beta_i kk_ij
+//     e^(cum_i-cum_j) (j < i); lanes 64..127 give P_tj = qk_tj e^(cum_t-cum_j) (j <= t),
+//     staged as bf16 and stored as one contiguous 8 KB tile.
+//  3. T = (I + A)^-1 blockwise on CUDA cores in fp32: 16x16 diagonal substitutions, then
+//     block rows T_ij = -T_ii sum_k A_ik T_kj in 4-column register tiles (each sum in the
+//     order of the plain loops); tb = bf16(T diag(beta)) as a K-major tile.
+//  4. MMA2 (kind::f16, A MN-major, M=128, N=64, K=64): u^T = v^T tb^T and w^T = kw^T tb^T;
+//     the TMEM rows are staged in shared memory and stored as contiguous 16 KB tiles.
+// Rows past a sequence's end have beta = 0, so their tb columns are zero and whatever v
+// rows the TMA brings there (the next sequence's, or zero fill) do not reach u.
 // Workspace layouts written: qd [t][k], kd [t][k], P [t][j], u^T [v][t], w^T [k][t].
 constexpr int TP_THREADS = 256;
-constexpr int TP_KQ = 0;                         // 4 x [128][32 fp32] = 64 KB; after MMA1: A, T, scratch
+constexpr int LDT = C + 4;                       // fp32 row stride of A and T (16-byte aligned rows)
+constexpr int TP_KQ = 0;                         // 4 x [128][32 fp32] = 64 KB; then A, T, scratch; then u^T / w^T staging
 constexpr int TP_KW = 65536;                     // kw, MN-major: 2 blocks x [64 j][64 d] bf16 = 16 KB
 constexpr int TP_VB = TP_KW + 16384;             // v,  MN-major: 2 blocks x [64 j][64 v] bf16 = 16 KB
-constexpr int TP_TB = TP_VB + 16384;             // tb, K-major [64 t][64 j] bf16 = 8 KB
+constexpr int TP_TB = TP_VB + 16384;             // P staging, then tb K-major [64 t][64 j] bf16 = 8 KB
 constexpr int TP_VEC = TP_TB + 8192;             // cum, bet, ecum, erem, gg [64] each
 constexpr int TP_BAR = TP_VEC + 5 * C * 4;
 constexpr int TP_SMEM = TP_BAR + 64 + 1024;
 constexpr int TP_A = 0;                          // inside the KQ region once MMA1 is done
-constexpr int TP_T = TP_A + C * LDC * 4;
-constexpr int TP_S = TP_T + C * LDC * 4;         // inverse scratch [3][16][16] fp32
+constexpr int TP_T = TP_A + C * LDT * 4;
+constexpr int TP_S = TP_T + C * LDT * 4;         // inverse scratch [3][16][16] fp32
 constexpr uint32_t MN_BLOCK = 8192;              // 64 K-rows x 128 B: stride between 64-wide MN blocks
 
 __device__ __forceinline__ float tf32_rna(float x) {
@@ -285,10 +290,10 @@ __device__ __forceinline__ uint32_t mn_off(int krow, int mn) {
     return (uint32_t)(mn >> 6) * MN_BLOCK + sw128_offset(krow, (mn & 63) >> 3) + (uint32_t)((mn & 7) << 1);
 }
 
-__global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restrict__ q, const bf16* __restrict__ k,
-                                                              const bf16* __restrict__ v, const float* __restrict__ g,
-                                                              const bf16* __restrict__ beta, Work ws, GdnTable tab,
-                                                              int H, int HK, float scale) {
+__global__ void __launch_bounds__(TP_THREADS, 2)
+    gdn_prep_tc(const __grid_constant__ CUtensorMap vmap, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                const float* __restrict__ g, const bf16* __restrict__ beta, Work ws, GdnTable tab, int H, int HK,
+                float scale) {
     // blockIdx.x enumerates the chunk slots of all packed sequences (no idle CTAs)
     const int slot_in_pack = blockIdx.x;
     int seq = 0;
@@ -320,12 +325,32 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
     float* ecum = bet + C;
     float* erem = ecum + C;
     float* gg = erem + C;
-    const uint32_t bar = base + TP_BAR;
+    const uint32_t bar = base + TP_BAR, vbar = base + TP_BAR + 8;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + TP_BAR + 16);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+    // global loads first: g and beta of the chunk, this warp's 8 rows of k and q
+    float gval = 0.f, bval = 0.f;
+    if (tid < n) {
+        gval = g[(size_t)(t0 + tid) * H + h];
+        bval = f32(beta[(size_t)(t0 + tid) * H + h]);
+    }
+    const int d0 = lane * 4;
+    uint2 kr[8], qr[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int r = warp * 8 + i;
+        if (r < n) {
+            kr[i] = *reinterpret_cast<const uint2*>(k + ((size_t)(t0 + r) * HK + hk) * K + d0);
+            qr[i] = *reinterpret_cast<const uint2*>(q + ((size_t)(t0 + r) * HK + hk) * K + d0);
+        } else {
+            kr[i] = make_uint2(0u, 0u);
+            qr[i] = make_uint2(0u, 0u);
+        }
+    }
     if (tid == 0) {
         mbar_init(bar, 1);
+        mbar_init(vbar, 1);
         mbar_fence_init();
     }
     if (warp == 0) {
@@ -333,14 +358,18 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         tmem_relinquish();
     }
     if (tid < C) {
-        gg[tid] = tid < n ? g[(size_t)(t0 + tid) * H + h] : 0.f;
-        bet[tid] = tid < n ? f32(beta[(size_t)(t0 + tid) * H + h]) : 0.f;
+        gg[tid] = gval;
+        bet[tid] = bval;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     if (tid == 0) {
+        // v rows t0..t0+63 of head h into the MN-major tile
+        mbar_expect_tx(vbar, 2 * MN_BLOCK);
+        tma_load_3d(base + TP_VB, &vmap, vbar, 0, h, t0);
+        tma_load_3d(base + TP_VB + MN_BLOCK, &vmap, vbar, 64, h, t0);
         // sequential fp32 sum (the reference's order), from registers
         float gv[C];
 #pragma unroll
@@ -353,75 +382,38 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         }
         ws.decay[slot] = expf(s);
     }
-    __syncthreads();
-    if (tid < C) {
-        ecum[tid] = expf(cum[tid]);
-        erem[tid] = expf(cum[C - 1] - cum[tid]);
-    }
-    __syncthreads();
-
-    // 1. rows r = warp*8 .. warp*8+7; lane holds dims d0 = 4*lane .. +3
-    {
-        const int d0 = lane * 4;
-        uint2 kr[8], qr[8];
+    // 1. norms and the TF32 operand rows: dims d0..d0+3 = one 16-byte chunk of sub-tile d0 / 32
+    float kinv[8], qinv[8];
+    const uint32_t chunk = (uint32_t)((d0 & 31) >> 2);
 #pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int r = warp * 8 + i;
-            if (r < n) {
-                kr[i] = *reinterpret_cast<const uint2*>(k + ((size_t)(t0 + r) * HK + hk) * K + d0);
-                qr[i] = *reinterpret_cast<const uint2*>(q + ((size_t)(t0 + r) * HK + hk) * K + d0);
-            } else {
-                kr[i] = make_uint2(0u, 0u);
-                qr[i] = make_uint2(0u, 0u);
-            }
+    for (int i = 0; i < 8; i++) {
+        const int r = warp * 8 + i;
+        float kx[4], qx[4];
+        const __nv_bfloat162* kp = reinterpret_cast<const __nv_bfloat162*>(&kr[i]);
+        const __nv_bfloat162* qp = reinterpret_cast<const __nv_bfloat162*>(&qr[i]);
+        const float2 k01 = __bfloat1622float2(kp[0]), k23 = __bfloat1622float2(kp[1]);
+        const float2 q01 = __bfloat1622float2(qp[0]), q23 = __bfloat1622float2(qp[1]);
+        kx[0] = k01.x; kx[1] = k01.y; kx[2] = k23.x; kx[3] = k23.y;
+        qx[0] = q01.x; qx[1] = q01.y; qx[2] = q23.x; qx[3] = q23.y;
+        float ks = 0.f, qs = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            ks = fmaf(kx[e], kx[e], ks);
+            qs = fmaf(qx[e], qx[e], qs);
         }
-        bf16* QD = static_cast<bf16*>(ws.qd) + slot * C * K;
-        bf16* KD = static_cast<bf16*>(ws.kdt) + slot * C * K;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int r = warp * 8 + i;
-            float kx[4], qx[4];
-            const __nv_bfloat162* kp = reinterpret_cast<const __nv_bfloat162*>(&kr[i]);
-            const __nv_bfloat162* qp = reinterpret_cast<const __nv_bfloat162*>(&qr[i]);
-            const float2 k01 = __bfloat1622float2(kp[0]), k23 = __bfloat1622float2(kp[1]);
-            const float2 q01 = __bfloat1622float2(qp[0]), q23 = __bfloat1622float2(qp[1]);
-            kx[0] = k01.x; kx[1] = k01.y; kx[2] = k23.x; kx[3] = k23.y;
-            qx[0] = q01.x; qx[1] = q01.y; qx[2] = q23.x; qx[3] = q23.y;
-            float ks = 0.f, qs = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                ks = fmaf(kx[e], kx[e], ks);
-                qs = fmaf(qx[e], qx[e], qs);
-            }
-            ks = warp_sum(ks);
-            qs = warp_sum(qs);
-            const float kinv = rsqrtf(ks + 1e-6f), qinv = rsqrtf(qs + 1e-6f) * scale;
-            float kn[4], qn[4];
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                kn[e] = kx[e] * kinv;
-                qn[e] = qx[e] * qinv;
-            }
-            // TF32 operand rows: dims d0..d0+3 = one 16-byte chunk of sub-tile d0 / 32
-            const uint32_t chunk = (uint32_t)((d0 & 31) >> 2);
-            *reinterpret_cast<float4*>(sm + TP_KQ + (d0 >> 5) * 16384 + sw128_offset(r, chunk)) =
-                make_float4(tf32_rna(kn[0]), tf32_rna(kn[1]), tf32_rna(kn[2]), tf32_rna(kn[3]));
-            *reinterpret_cast<float4*>(sm + TP_KQ + (d0 >> 5) * 16384 + sw128_offset(C + r, chunk)) =
-                make_float4(tf32_rna(qn[0]), tf32_rna(qn[1]), tf32_rna(qn[2]), tf32_rna(qn[3]));
-            uint2 o;
-            o.x = pack_bf16x2(qn[0] * ecum[r], qn[1] * ecum[r]);
-            o.y = pack_bf16x2(qn[2] * ecum[r], qn[3] * ecum[r]);
-            *reinterpret_cast<uint2*>(QD + (size_t)r * K + d0) = o;
-            o.x = pack_bf16x2(kn[0] * erem[r], kn[1] * erem[r]);
-            o.y = pack_bf16x2(kn[2] * erem[r], kn[3] * erem[r]);
-            *reinterpret_cast<uint2*>(KD + (size_t)r * K + d0) = o;
-            o.x = pack_bf16x2(kn[0] * ecum[r], kn[1] * ecum[r]);
-            o.y = pack_bf16x2(kn[2] * ecum[r], kn[3] * ecum[r]);
-            *reinterpret_cast<uint2*>(sm + TP_KW + mn_off(r, d0)) = o;
-        }
+        ks = warp_sum(ks);
+        qs = warp_sum(qs);
+        kinv[i] = rsqrtf(ks + 1e-6f);
+        qinv[i] = rsqrtf(qs + 1e-6f) * scale;
+        *reinterpret_cast<float4*>(sm + TP_KQ + (d0 >> 5) * 16384 + sw128_offset(r, chunk)) =
+            make_float4(tf32_rna(kx[0] * kinv[i]), tf32_rna(kx[1] * kinv[i]), tf32_rna(kx[2] * kinv[i]),
+                        tf32_rna(kx[3] * kinv[i]));
+        *reinterpret_cast<float4*>(sm + TP_KQ + (d0 >> 5) * 16384 + sw128_offset(C + r, chunk)) =
+            make_float4(tf32_rna(qx[0] * qinv[i]), tf32_rna(qx[1] * qinv[i]), tf32_rna(qx[2] * qinv[i]),
+                        tf32_rna(qx[3] * qinv[i]));
     }
     fence_async_smem();
-    __syncthreads();
+    __syncthreads();  // cum and the TF32 tile are complete
     if (tid == 0) {
         tc_fence_after();
         constexpr uint32_t ID = idesc(128, 64, AB_TF32);
@@ -432,48 +424,87 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         }
         mma_commit(bar);
     }
-    // v rows into the MN-major tile (16-byte units: row j, dims 8u..8u+7), zero past the end
-    for (int u = tid; u < C * V / 8; u += TP_THREADS) {
-        const int j = u >> 4, d8 = (u & 15) * 8;
-        Pack8 val;
-        if (j < n) {
-            val = ld8(v + ((size_t)(t0 + j) * H + h) * V + d8);
-        } else {
-            const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            val = pack8(z);
-        }
-        *reinterpret_cast<Pack8*>(sm + TP_VB + (d8 >> 6) * MN_BLOCK + sw128_offset(j, (d8 & 63) >> 3)) = val;
+    if (tid < C) {
+        ecum[tid] = expf(cum[tid]);
+        erem[tid] = expf(cum[C - 1] - cum[tid]);
     }
+    __syncthreads();
+    {
+        bf16* QD = static_cast<bf16*>(ws.qd) + slot * C * K;
+        bf16* KD = static_cast<bf16*>(ws.kdt) + slot * C * K;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int r = warp * 8 + i;
+            float kn[4], qn[4];
+            const __nv_bfloat162* kp = reinterpret_cast<const __nv_bfloat162*>(&kr[i]);
+            const __nv_bfloat162* qp = reinterpret_cast<const __nv_bfloat162*>(&qr[i]);
+            const float2 k01 = __bfloat1622float2(kp[0]), k23 = __bfloat1622float2(kp[1]);
+            const float2 q01 = __bfloat1622float2(qp[0]), q23 = __bfloat1622float2(qp[1]);
+            kn[0] = k01.x * kinv[i]; kn[1] = k01.y * kinv[i]; kn[2] = k23.x * kinv[i]; kn[3] = k23.y * kinv[i];
+            qn[0] = q01.x * qinv[i]; qn[1] = q01.y * qinv[i]; qn[2] = q23.x * qinv[i]; qn[3] = q23.y * qinv[i];
+            const float ec = ecum[r], er = erem[r];
+            uint2 o;
+            o.x = pack_bf16x2(qn[0] * ec, qn[1] * ec);
+            o.y = pack_bf16x2(qn[2] * ec, qn[3] * ec);
+            *reinterpret_cast<uint2*>(QD + (size_t)r * K + d0) = o;
+            o.x = pack_bf16x2(kn[0] * er, kn[1] * er);
+            o.y = pack_bf16x2(kn[2] * er, kn[3] * er);
+            *reinterpret_cast<uint2*>(KD + (size_t)r * K + d0) = o;
+            o.x = pack_bf16x2(kn[0] * ec, kn[1] * ec);
+            o.y = pack_bf16x2(kn[2] * ec, kn[3] * ec);
+            *reinterpret_cast<uint2*>(sm + TP_KW + mn_off(r, d0)) = o;
+        }
+    }
+    fence_async_smem();  // kw is read by MMA2
     bool ok = mbar_wait(bar, 0);  // every thread: MMA1 done, the KQ region is free
     if (!ok && lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
     tc_fence_after();
-    __syncthreads();
-    if (warp < 4) {
-        // 2. A rows (lanes 0..63) and P rows (lanes 64..127) from TMEM
-        const int i = tid;
-        float d[64];
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), *reinterpret_cast<float(*)[32]>(d));
-        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + 32, *reinterpret_cast<float(*)[32]>(d + 32));
+    // 2. A rows (TMEM lanes 0..63) and P rows (lanes 64..127); warp w reads lane quarter
+    //    w % 4, columns 32 * (w / 4) .. +31
+    {
+        const int q4 = warp & 3, j0 = (warp >> 2) * 32;
+        const int row = q4 * 32 + lane;
+        float d[32];
+        tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)j0, d);
         tmem_ld_wait();
-        if (i < C) {
+        if (row < C) {
+            const int i = row;
+            const float ci = cum[i], bi = bet[i];
+            float* arow = A + i * LDT + j0;
 #pragma unroll
-            for (int j = 0; j < C; j++) A[i * LDC + j] = j < i ? bet[i] * d[j] * __expf(cum[i] - cum[j]) : 0.f;
+            for (int j4 = 0; j4 < 8; j4++) {
+                float f[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int j = j0 + j4 * 4 + e;
+                    f[e] = j < i ? bi * d[j4 * 4 + e] * __expf(ci - cum[j]) : 0.f;
+                }
+                *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(f[0], f[1], f[2], f[3]);
+            }
         } else {
-            const int t = i - C;
-            bf16* P = static_cast<bf16*>(ws.p) + slot * C * C + (size_t)t * C;
+            const int t = row - C;
+            const float ct = cum[t];
 #pragma unroll
-            for (int j8 = 0; j8 < C / 8; j8++) {
+            for (int c8 = 0; c8 < 4; c8++) {
                 float f[8];
 #pragma unroll
                 for (int e = 0; e < 8; e++) {
-                    const int j = j8 * 8 + e;
-                    f[e] = j <= t ? d[j] * __expf(cum[t] - cum[j]) : 0.f;
+                    const int j = j0 + c8 * 8 + e;
+                    f[e] = j <= t ? d[c8 * 8 + e] * __expf(ct - cum[j]) : 0.f;
                 }
-                st8(P + j8 * 8, pack8(f));
+                const int ch = (j0 >> 3) + c8;  // 16-byte chunk of the 128-byte P row
+                *reinterpret_cast<Pack8*>(sm + TP_TB + t * 128 + ((ch ^ (t & 7)) << 4)) = pack8(f);
             }
         }
     }
     __syncthreads();
+    {
+        bf16* P = static_cast<bf16*>(ws.p) + slot * C * C;
+        for (int u = tid; u < C * C / 8; u += TP_THREADS) {
+            const int t = u >> 3, c8 = u & 7;
+            st8(P + t * C + c8 * 8, *reinterpret_cast<const Pack8*>(sm + TP_TB + t * 128 + ((c8 ^ (t & 7)) << 4)));
+        }
+    }
     // 3. T = (I + A)^-1. Diagonal 16x16 blocks: one thread per (block, column).
     if (tid < C) {
         const int b = tid >> 4, col = tid & 15, o = b * 16;
@@ -482,30 +513,54 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         for (int r = 0; r < 16; r++) {
             float acc = r == col ? 1.f : 0.f;
 #pragma unroll
-            for (int m = 0; m < r; m++) acc = fmaf(-A[(o + r) * LDC + o + m], x[m], acc);
+            for (int m = 0; m < r; m++) acc = fmaf(-A[(o + r) * LDT + o + m], x[m], acc);
             x[r] = r < col ? 0.f : acc;
         }
 #pragma unroll
-        for (int r = 0; r < 16; r++) Tm[(o + r) * LDC + o + col] = x[r];
+        for (int r = 0; r < 16; r++) Tm[(o + r) * LDT + o + col] = x[r];
     }
     for (int x = tid; x < C * C; x += TP_THREADS) {
         const int i = x / C, j = x % C;
-        if ((j >> 4) > (i >> 4)) Tm[i * LDC + j] = 0.f;
+        if ((j >> 4) > (i >> 4)) Tm[i * LDT + j] = 0.f;
     }
     __syncthreads();
+    // block rows bi = 1..3: S_bj = sum_{kb = bj}^{bi-1} A_(bi,kb) T_(kb,bj), then
+    // T_(bi,bj) = -T_(bi,bi) S_bj; thread = (bj, row r, 4 columns)
+#pragma unroll
     for (int bi = 1; bi < 4; bi++) {
-        for (int x = tid; x < bi * 256; x += TP_THREADS) {
-            const int bj = x >> 8, r = (x >> 4) & 15, cc = x & 15;
-            float acc = 0.f;
-            for (int m = bj * 16; m < bi * 16; m++) acc = fmaf(A[(bi * 16 + r) * LDC + m], Tm[m * LDC + bj * 16 + cc], acc);
-            S[x] = acc;
+        const int bj = tid >> 6, r = (tid >> 2) & 15, c4 = (tid & 3) * 4;
+        if (tid < bi * 64) {
+            const float* arow = A + (16 * bi + r) * LDT;
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            for (int kb = bj; kb < bi; kb++) {
+#pragma unroll
+                for (int m = 0; m < 16; m++) {
+                    const float av = arow[16 * kb + m];
+                    const float4 tv = *reinterpret_cast<const float4*>(Tm + (16 * kb + m) * LDT + 16 * bj + c4);
+                    a0 = fmaf(av, tv.x, a0);
+                    a1 = fmaf(av, tv.y, a1);
+                    a2 = fmaf(av, tv.z, a2);
+                    a3 = fmaf(av, tv.w, a3);
+                }
+            }
+            *reinterpret_cast<float4*>(S + (bj * 16 + r) * 16 + c4) = make_float4(a0, a1, a2, a3);
         }
         __syncthreads();
-        for (int x = tid; x < bi * 256; x += TP_THREADS) {
-            const int bj = x >> 8, r = (x >> 4) & 15, cc = x & 15;
-            float acc = 0.f;
-            for (int m = 0; m <= r; m++) acc = fmaf(Tm[(bi * 16 + r) * LDC + bi * 16 + m], S[(bj << 8) + (m << 4) + cc], acc);
-            Tm[(bi * 16 + r) * LDC + bj * 16 + cc] = -acc;
+        if (tid < bi * 64) {
+            const float* trow = Tm + (16 * bi + r) * LDT + 16 * bi;
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+            for (int m = 0; m < 16; m++) {
+                if (m <= r) {
+                    const float tv = trow[m];
+                    const float4 sv = *reinterpret_cast<const float4*>(S + (bj * 16 + m) * 16 + c4);
+                    a0 = fmaf(tv, sv.x, a0);
+                    a1 = fmaf(tv, sv.y, a1);
+                    a2 = fmaf(tv, sv.z, a2);
+                    a3 = fmaf(tv, sv.w, a3);
+                }
+            }
+            *reinterpret_cast<float4*>(Tm + (16 * bi + r) * LDT + 16 * bj + c4) = make_float4(-a0, -a1, -a2, -a3);
         }
         __syncthreads();
     }
@@ -514,13 +569,14 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         const int t = u >> 3, j0 = (u & 7) * 8;
         float f[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) f[e] = Tm[t * LDC + j0 + e] * bet[j0 + e];
+        for (int e = 0; e < 8; e++) f[e] = Tm[t * LDT + j0 + e] * bet[j0 + e];
         *reinterpret_cast<Pack8*>(sm + TP_TB + sw128_offset(t, j0 >> 3)) = pack8(f);
     }
     fence_async_smem();
     __syncthreads();
     if (tid == 0) {
         tc_fence_after();
+        if (!mbar_wait(vbar, 0)) atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
         constexpr uint32_t ID = idesc_major(128, 64, AB_BF16, 1, 0);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
@@ -536,6 +592,7 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
     }
     tc_fence_after();
+    // 4. u^T rows (warps 0-3) and w^T rows (warps 4-7) staged in the free KQ region
     {
         const int q4 = warp & 3;
         const int row = q4 * 32 + lane;  // TMEM lane = v (u^T) or k (w^T)
@@ -544,9 +601,16 @@ __global__ void __launch_bounds__(TP_THREADS, 2) gdn_prep_tc(const bf16* __restr
         tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + col, *reinterpret_cast<float(*)[32]>(x));
         tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + col + 32, *reinterpret_cast<float(*)[32]>(x + 32));
         tmem_ld_wait();
-        bf16* dst = static_cast<bf16*>(warp < 4 ? ws.ut : ws.w) + (slot * V + row) * C;
+        uint8_t* stg = sm + TP_KQ + (warp < 4 ? 0 : 16384) + row * 128;
 #pragma unroll
-        for (int j8 = 0; j8 < 8; j8++) st8(dst + j8 * 8, pack8(x + j8 * 8));
+        for (int c8 = 0; c8 < 8; c8++) *reinterpret_cast<Pack8*>(stg + ((c8 ^ (row & 7)) << 4)) = pack8(x + c8 * 8);
+    }
+    __syncthreads();
+    // one contiguous 16 KB tile each: u^T [128 v][64 t] and w^T [128 k][64 t]
+    for (int u = tid; u < 2 * V * C / 8; u += TP_THREADS) {
+        const int which = u >> 10, row = (u >> 3) & 127, c8 = u & 7;
+        bf16* dst = static_cast<bf16*>(which ? ws.w : ws.ut) + (slot * V + row) * C + c8 * 8;
+        st8(dst, *reinterpret_cast<const Pack8*>(sm + TP_KQ + which * 16384 + row * 128 + ((c8 ^ (row & 7)) << 4)));
     }
     tc_fence_before();
     __syncthreads();
@@ -833,9 +897,12 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     if (configured != cudaSuccess) return configured;
     uint8_t* b = static_cast<uint8_t*>(workspace);
     Work ws{b + L.w, b + L.qd, b + L.p, b + L.kdt, b + L.ut, reinterpret_cast<float*>(b + L.decay), slots};
+    CUtensorMap vmap;
+    if (int e = host::make_map_3d_bf16(&vmap, v, V, H, (uint64_t)seqs.offset[seqs.count], V, (uint64_t)H * V, 64, 64))
+        return e;
     gdn_prep_tc<<<dim3((unsigned)slots, H), TP_THREADS, TP_SMEM, st>>>(
-        static_cast<const bf16*>(q), static_cast<const bf16*>(k), static_cast<const bf16*>(v), g,
-        static_cast<const bf16*>(beta), ws, tab, H, HK, scale);
+        vmap, static_cast<const bf16*>(q), static_cast<const bf16*>(k), g, static_cast<const bf16*>(beta), ws, tab,
+        H, HK, scale);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     ScanMaps maps;

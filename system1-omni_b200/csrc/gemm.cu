@@ -56,16 +56,31 @@ struct Params {
     int ldy;
     int M, N, K;
     int tiles_m, tiles_n;
+    int group;  // > 0: tiles walked in groups of `group` row blocks; < 0: groups of -group column blocks
 };
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& m, int& n) {
-    const int per_group = GROUP_M * tiles_n;
-    const int group = t / per_group;
-    const int first = group * GROUP_M;
-    const int gm = min(GROUP_M, tiles_m - first);
-    const int r = t - group * per_group;
-    m = first + r % gm;
-    n = r / gm;
+// Tile t -> (row block m, column block n). With group g > 0 the CTAs resident at one time
+// share g row blocks of A and sweep the columns; with g < 0 they share -g column blocks
+// of B and sweep the rows.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group, int& m, int& n) {
+    if (group > 0) {
+        const int per_group = group * tiles_n;
+        const int gi = t / per_group;
+        const int first = gi * group;
+        const int gm = min(group, tiles_m - first);
+        const int r = t - gi * per_group;
+        m = first + r % gm;
+        n = r / gm;
+    } else {
+        const int g = -group;
+        const int per_group = g * tiles_m;
+        const int gi = t / per_group;
+        const int first = gi * g;
+        const int gn = min(g, tiles_n - first);
+        const int r = t - gi * per_group;
+        n = first + r % gn;
+        m = r / gn;
+    }
 }
 
 template <int BN, int EPI>
@@ -119,7 +134,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
                 int m, n;
-                tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+                tile_coords(t, p.tiles_m, p.tiles_n, p.group, m, n);
                 for (int kb = 0; kb < KB; kb++) {
                     if (!mbar_wait(empty(s), ph ^ 1)) {
                         atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
@@ -196,7 +211,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t acc_ph = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
             int m, n;
-            tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+            tile_coords(t, p.tiles_m, p.tiles_n, p.group, m, n);
             if (!mbar_wait(tfull(acc), acc_ph)) {
                 if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
                 break;
@@ -293,17 +308,8 @@ constexpr int P_B_BYTES = 128 * BK * 2;
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
 constexpr int P_BAR_OFFSET = P_STAGES * P_STAGE_BYTES;
 constexpr int P_SMEM = P_BAR_OFFSET + 256 + 1024;
-constexpr int P_GROUP_M = 8;
+constexpr int P_GROUP_M = 16;
 
-__device__ __forceinline__ void pair_tile_coords(int t, int tiles_m, int tiles_n, int& m, int& n) {
-    const int per_group = P_GROUP_M * tiles_n;
-    const int group = t / per_group;
-    const int first = group * P_GROUP_M;
-    const int gm = min(P_GROUP_M, tiles_m - first);
-    const int r = t - group * per_group;
-    m = first + r % gm;
-    n = r / gm;
-}
 
 template <int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
@@ -360,7 +366,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             bool ok = true;
             for (int t = cid; t < num_tiles && ok; t += nclusters) {
                 int m, n;
-                pair_tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+                tile_coords(t, p.tiles_m, p.tiles_n, p.group, m, n);
                 for (int kb = 0; kb < KB; kb++) {
                     if (!mbar_wait(empty(s), ph ^ 1)) {
                         atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
@@ -442,7 +448,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         uint32_t acc_ph = 0;
         for (int t = cid; t < num_tiles; t += nclusters) {
             int m, n;
-            pair_tile_coords(t, p.tiles_m, p.tiles_n, m, n);
+            tile_coords(t, p.tiles_m, p.tiles_n, p.group, m, n);
             if (!mbar_wait(tfull(acc), acc_ph)) {
                 if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
                 break;
@@ -553,6 +559,7 @@ struct Handle {
     int sms = 148;
     int fixed_m = 0;
     bool pairs = true;  // CTA-pair kernels for large M (S1_GEMM_PAIRS=0 selects the single-CTA kernels)
+    int group = 0;      // tile grouping (0: the kernels' defaults; S1_GEMM_GROUP overrides, for tuning)
 };
 
 template <int BN, int EPI>
@@ -576,6 +583,7 @@ int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int
     p.K = K;
     p.tiles_m = (M + BM - 1) / BM;
     p.tiles_n = (N + BN - 1) / BN;
+    p.group = h->group ? h->group : GROUP_M;
     const int tiles = p.tiles_m * p.tiles_n;
     const int grid = std::min(tiles, h->sms);
     gemm_kernel<BN, EPI><<<grid, THREADS, C::SMEM, st>>>(ma, mb, p);
@@ -602,6 +610,7 @@ int launch_pair(const Handle* h, const void* x, const void* w, void* y, int M, i
     p.K = K;
     p.tiles_m = (M + 255) / 256;
     p.tiles_n = (N + 255) / 256;
+    p.group = h->group ? h->group : P_GROUP_M;
     const int tiles = p.tiles_m * p.tiles_n;
     const int grid = 2 * std::min(tiles, h->sms / 2);
     gemm_pair_kernel<EPI><<<grid, THREADS, P_SMEM, st>>>(ma, mb, p);
@@ -685,6 +694,8 @@ void* cs1_gemm_create(size_t workspace_bytes) {
     h->sms = host::num_sms();
     const char* env = getenv("S1_GEMM_PAIRS");
     h->pairs = !(env && env[0] == '0');
+    const char* grp = getenv("S1_GEMM_GROUP");
+    if (grp) h->group = atoi(grp);
     return h;
 }
 

@@ -1,5 +1,8 @@
-"""Whole-forward parity at the 27B layer widths (hidden 5120, SwiGLU 17408, GDN 16/48
-heads, attention 24/4 heads x 256) over one 4-layer period (3 GDN + 1 attention).
+"""Whole-forward parity at the layer widths of the three BASELINE models over one 4-layer
+period (3 GDN + 1 attention): 27B (hidden 5120, SwiGLU 17408, GDN 16/48 heads, attention
+24/4 heads x 256), 9B (4096, 12288, 16/32, 16/4) and 4B (2560, 9216, 16/32, 16/4).
+Config C2's shape (a 2,048-token shared prefix and 8 candidates of 32 tokens) is run at
+the 4B widths through the shared-prefix path.
 
 The weights are drawn on the device by s1_model_init_random and read back with
 s1_model_get_weight, so the numpy oracle runs on exactly the weights the kernels use.
@@ -25,18 +28,22 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 REF = os.path.join(ROOT, "oracle", "_ref", "libqwen3_5_cuda.so")
 
 
-def _cfgs():
+WIDTHS = {"27b": (5120, 17408, 16, 48, 24, 4), "9b": (4096, 12288, 16, 32, 16, 4), "4b": (2560, 9216, 16, 32, 16, 4)}
+
+
+def _cfgs(name):
     from s1omni import Config
     layers = ["gdn", "gdn", "gdn", "attn"]
-    ours = Config(5120, 17408, layers, 16, 48, 24, 4, 4096, name="27b-period")
-    oracle = OM.Config(5120, 17408, layers, 16, 48, 24, 4, 4096, name="27b-period")
+    H, I, hk, hv, hq, hkv = WIDTHS[name]
+    ours = Config(H, I, layers, hk, hv, hq, hkv, 4096, name=name + "-period")
+    oracle = OM.Config(H, I, layers, hk, hv, hq, hkv, 4096, name=name + "-period")
     return ours, oracle
 
 
-@pytest.fixture(scope="module")
-def period(cs1):
+@pytest.fixture(scope="module", params=["27b", "9b", "4b"])
+def period(cs1, request):
     from s1omni import Model
-    cfg, ocfg = _cfgs()
+    cfg, ocfg = _cfgs(request.param)
     m = Model(cfg, device=0, max_tokens=1024, max_seqs=8)
     m.init_random(seed=99, std=0.02)
     W = {name: m.get_weight(name, shape) for name, shape, _ in OM.weight_shapes(ocfg)}
@@ -72,3 +79,29 @@ def test_fullwidth_period_matches_oracle_and_reference(period):
         assert d_oracle <= report["reference_vs_oracle"] + 1e-2, report
     else:
         assert d_oracle <= 6e-2, report
+
+
+def test_c2_shared_prefix_candidates_at_4b_width(cs1):
+    """C2's shape at the 4B widths: 8 candidates of 32 tokens after one 2,048-token
+    prefix. The shared-prefix pass (prefix once, GDN state / conv rows / K-V forked) must
+    equal each full prompt run on its own, bit for bit, and stay within the noise floor of
+    the oracle's shared-prefix forward."""
+    from s1omni import Model
+    cfg, ocfg = _cfgs("4b")
+    rng = np.random.default_rng(2)
+    prefix = rng.integers(0, cfg.vocab, 2048).astype(np.int32)
+    suffixes = [rng.integers(0, cfg.vocab, 32).astype(np.int32) for _ in range(8)]
+    m = Model(cfg, device=0, max_tokens=2048 + 8 * 32 + 64, max_seqs=16)
+    try:
+        m.init_random(seed=7, std=0.02)
+        shared = m.forward_shared(prefix, suffixes)
+        for i, sfx in enumerate(suffixes):
+            full = m.forward([np.concatenate([prefix, sfx])])[0]
+            assert np.array_equal(shared[i], full), (i, np.abs(shared[i] - full).max())
+        W = {name: m.get_weight(name, shape) for name, shape, _ in OM.weight_shapes(ocfg)}
+    finally:
+        m.close()
+    ref = OM.forward_shared_prefix(ocfg, W, prefix, suffixes)[1]
+    d = float(np.abs(shared - ref).max())
+    print({"c2_ours_vs_oracle": d, "logit_max": float(np.abs(ref).max())})
+    assert d <= 6e-2
