@@ -222,7 +222,7 @@ def run_reference(args, rank, world):
 # DRAM traffic of one gemm_pair_kernel<SWIGLU> launch at M = 29,122 (N = 34,816, K = 5,120),
 # dram__bytes_read.sum + dram__bytes_write.sum from the ncu capture summarised in
 # profiles/gemm_swiglu_29122x34816x5120.md; scaled by rows for another M.
-SWIGLU_TRAFFIC = {"m": 29122, "bytes": None}
+SWIGLU_TRAFFIC = {"m": 29122, "bytes": 8526523904 + 1024200192}
 
 
 def gemm_roofline(cs1, cfg, M, stream, torch):

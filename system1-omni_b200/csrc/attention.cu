@@ -32,46 +32,88 @@ namespace attn {
 constexpr int DH = 256;
 
 // ---------------------------------------------------------------- prep ----
+constexpr int PREP_UNITS = 4;  // (token, head) units per warp, loads of all issued first
 __global__ void prep_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
                             const bf16* __restrict__ qw, const bf16* __restrict__ kw, const bf16* __restrict__ cosb,
                             const bf16* __restrict__ sinb, bf16* __restrict__ q, bf16* __restrict__ gate,
-                            bf16* __restrict__ k, int T, int Hq, int Hk, int half, float eps) {
-    const int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+                            bf16* __restrict__ k, int T, int Hq, int Hk, int half, float eps, bool cs_vec) {
+    // 32-bit unit indices (T * heads < 2^31 is checked on the host)
+    const int unit0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * PREP_UNITS;
+    const int lane = threadIdx.x & 31;
     const int heads = Hq + Hk;
-    if (warp >= T * heads) return;
-    const int t = warp / heads, hh = warp % heads;
-    const bool is_q = hh < Hq;
-    const int h = is_q ? hh : hh - Hq;
-    const bf16* src = is_q ? qg + (size_t)t * ld + (size_t)h * 2 * DH : kr + (size_t)t * ld + (size_t)h * DH;
+    const int units = T * heads;
     const int d0 = lane * 8;
-    float x[8], w[8];
-    unpack8(ld8(src + d0), x);
-    unpack8(ld8((is_q ? qw : kw) + d0), w);
-    float ss = 0.f;
+    const int rot = 2 * half;  // a lane's 8 dims are all rotated or all passed through (half % 8 == 0)
+    Pack8 xr[PREP_UNITS], gr[PREP_UNITS];
 #pragma unroll
-    for (int i = 0; i < 8; i++) ss = fmaf(x[i], x[i], ss);
-    const float inv = rsqrtf(warp_sum(ss) / DH + eps);
-#pragma unroll
-    for (int i = 0; i < 8; i++) x[i] = rbf(x[i] * inv * (1.f + w[i]));
-    const int rot = 2 * half;
-    float y[8];
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const float partner = __shfl_xor_sync(0xffffffffu, x[i], half / 8);
-        const int d = d0 + i;
-        y[i] = x[i];
-        if (d < rot) {
-            const int fi = d % half;
-            const float c = f32(cosb[(size_t)t * half + fi]), s = f32(sinb[(size_t)t * half + fi]);
-            const float r = d < half ? -partner : partner;
-            y[i] = rbf(rbf(x[i] * c) + rbf(r * s));
+    for (int i = 0; i < PREP_UNITS; i++) {
+        const int u = unit0 + i;
+        if (u < units) {
+            const int t = u / heads, hh = u - t * heads;
+            if (hh < Hq) {
+                const bf16* src = qg + (size_t)t * ld + (size_t)hh * 2 * DH;
+                xr[i] = ld8(src + d0);
+                gr[i] = ld8(src + DH + d0);
+            } else {
+                xr[i] = ld8(kr + (size_t)t * ld + (size_t)(hh - Hq) * DH + d0);
+            }
         }
     }
-    if (is_q) {
-        st8(q + ((size_t)t * Hq + h) * DH + d0, pack8(y));
-        st8(gate + ((size_t)t * Hq + h) * DH + d0, ld8(src + DH + d0));
-    } else {
-        st8(k + ((size_t)t * Hk + h) * DH + d0, pack8(y));
+    float wq[8], wk[8];
+    unpack8(ld8(qw + d0), wq);
+    unpack8(ld8(kw + d0), wk);
+#pragma unroll
+    for (int i = 0; i < PREP_UNITS; i++) {
+        const int u = unit0 + i;
+        if (u >= units) break;  // uniform over the warp
+        const int t = u / heads, hh = u - t * heads;
+        const bool is_q = hh < Hq;
+        const int h = is_q ? hh : hh - Hq;
+        float x[8];
+        unpack8(xr[i], x);
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss = fmaf(x[e], x[e], ss);
+        const float inv = rsqrtf(warp_sum(ss) / DH + eps);
+#pragma unroll
+        for (int e = 0; e < 8; e++) x[e] = x[e] * inv * (1.f + (is_q ? wq[e] : wk[e]));
+        rbf8(x);
+        float cs[8], sn[8];
+        if (d0 < rot) {
+            const size_t f0 = (size_t)t * half + d0 % half;
+            if (cs_vec) {
+                unpack8(ld8(cosb + f0), cs);
+                unpack8(ld8(sinb + f0), sn);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    cs[e] = f32(cosb[f0 + e]);
+                    sn[e] = f32(sinb[f0 + e]);
+                }
+            }
+        }
+        float y[8], ps[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float partner = __shfl_xor_sync(0xffffffffu, x[e], half / 8);
+            y[e] = x[e] * cs[e];
+            ps[e] = (d0 < half ? -partner : partner) * sn[e];
+        }
+        if (d0 < rot) {
+            rbf8(y);
+            rbf8(ps);
+#pragma unroll
+            for (int e = 0; e < 8; e++) y[e] += ps[e];  // rounded by the pack below
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) y[e] = x[e];
+        }
+        if (is_q) {
+            st8(q + ((size_t)t * Hq + h) * DH + d0, pack8(y));
+            st8(gate + ((size_t)t * Hq + h) * DH + d0, gr[i]);
+        } else {
+            st8(k + ((size_t)t * Hk + h) * DH + d0, pack8(y));
+        }
     }
 }
 
@@ -739,8 +781,10 @@ int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const 
     if (ld % 8 != 0 || T < 0 || Hq < 0 || Hk < 0) return cudaErrorInvalidValue;
     if (Dh != attn::DH || half <= 0 || half % 8 != 0 || 2 * half > Dh || ((half / 8) & (half / 8 - 1)))
         return cudaErrorInvalidValue;
-    const long warps = (long)T * (Hq + Hk);
-    if (warps == 0) return cudaSuccess;
+    const long units = (long)T * (Hq + Hk);
+    if (units == 0) return cudaSuccess;
+    if (units > INT_MAX - 64) return cudaErrorInvalidValue;
+    const long warps = (units + attn::PREP_UNITS - 1) / attn::PREP_UNITS;
     if (!aligned16(qg) || !aligned16(kr) || !aligned16(qw) || !aligned16(kw) || !aligned16(q) || !aligned16(gate) ||
         !aligned16(k))
         return cudaErrorInvalidValue;
@@ -748,7 +792,8 @@ int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const 
     attn::prep_kernel<<<(unsigned)((warps + WPB - 1) / WPB), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
         static_cast<const bf16*>(qg), static_cast<const bf16*>(kr), ld, static_cast<const bf16*>(qw),
         static_cast<const bf16*>(kw), static_cast<const bf16*>(cos), static_cast<const bf16*>(sin),
-        static_cast<bf16*>(q), static_cast<bf16*>(gate), static_cast<bf16*>(k), T, Hq, Hk, half, eps);
+        static_cast<bf16*>(q), static_cast<bf16*>(gate), static_cast<bf16*>(k), T, Hq, Hk, half, eps,
+        aligned16(cos) && aligned16(sin));
     return cudaGetLastError();
 }
 

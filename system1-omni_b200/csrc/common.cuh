@@ -14,6 +14,17 @@ __device__ __forceinline__ bf16 to_bf16(float x) { return __float2bfloat16_rn(x)
 // A float rounded through bfloat16, the value PyTorch keeps after a bfloat16 op.
 __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 
+// Eight floats rounded through bfloat16 in pairs: one cvt.rn.bf16x2.f32 per two values
+// (the scalar conversion issues at half that rate), same values as rbf on each.
+__device__ __forceinline__ void rbf8(float (&v)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const float2 f = __bfloat1622float2(__floats2bfloat162_rn(v[i], v[i + 1]));
+        v[i] = f.x;
+        v[i + 1] = f.y;
+    }
+}
+
 __device__ __forceinline__ float warp_sum(float x) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
@@ -44,6 +55,7 @@ __device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
 // accurate expf and IEEE division would make them instruction-bound.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
+
 
 // Eight bfloat16 values moved as one 16-byte access.
 struct alignas(16) Pack8 {

@@ -53,7 +53,7 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const Pack8* __res
 // loaded once and the three previous input rows slide through registers, so every input
 // row is read once. A run that crosses into a new sequence restarts its window from zeros
 // (or from the three rows of `history`, shared by every sequence).
-constexpr int CONV_ROWS = 32;
+constexpr int CONV_ROWS = 64;
 
 __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
@@ -105,30 +105,43 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
         }
     };
     window(t_begin);
-    for (int t = t_begin; t < t_end; t++) {
-        if (t == next) {
-            s++;
-            next = tab.offset[s + 1];
-            window(t);
-        }
-        float x0[8];
-        unpack8(ld8(qkv + (size_t)t * ld + (size_t)c * 8), x0);
-        float y[8];
+    // rows in batches of 8: all loads of a batch are in flight before the first is used
+    for (int tb = t_begin; tb < t_end; tb += 8) {
+        Pack8 raw[8];
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            float acc = 0.f;
-            acc = fmaf(wt[e][0], x1[e], acc);
-            acc = fmaf(wt[e][1], x2[e], acc);
-            acc = fmaf(wt[e][2], x3[e], acc);
-            acc = fmaf(wt[e][3], x0[e], acc);
-            y[e] = silu_fast(rbf(acc));
-        }
-        st8(dst + (size_t)t * dst_ld, pack8(y));
+        for (int i = 0; i < 8; i++)
+            if (tb + i < t_end) raw[i] = ld8(qkv + (size_t)(tb + i) * ld + (size_t)c * 8);
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            x1[e] = x2[e];
-            x2[e] = x3[e];
-            x3[e] = x0[e];
+        for (int i = 0; i < 8; i++) {
+            const int t = tb + i;
+            if (t >= t_end) break;
+            if (t == next) {
+                s++;
+                next = tab.offset[s + 1];
+                window(t);
+            }
+            float x0[8];
+            unpack8(raw[i], x0);
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                float acc = 0.f;
+                acc = fmaf(wt[e][0], x1[e], acc);
+                acc = fmaf(wt[e][1], x2[e], acc);
+                acc = fmaf(wt[e][2], x3[e], acc);
+                acc = fmaf(wt[e][3], x0[e], acc);
+                y[e] = acc;
+            }
+            rbf8(y);
+#pragma unroll
+            for (int e = 0; e < 8; e++) y[e] = silu_fast(y[e]);
+            st8(dst + (size_t)t * dst_ld, pack8(y));
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                x1[e] = x2[e];
+                x2[e] = x3[e];
+                x3[e] = x0[e];
+            }
         }
     }
 }
@@ -181,18 +194,32 @@ __global__ void sigmoid_gate_kernel(bf16* __restrict__ x, const bf16* __restrict
         x[i] = to_bf16(f32(x[i]) * rbf(sigmoid(f32(gate[i]))));
 }
 
+// Grid (column packs / blockDim.x, row pairs): a thread takes one 8-column pack of two
+// rows, with the four loads in flight together.
 __global__ void silu_mul_vec_kernel(const bf16* __restrict__ gu, int ld, bf16* __restrict__ out, int I, long T) {
-    const int packs = I / 8;
-    const long n = T * packs;
-    for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-        const long t = i / packs;
-        const int j = (int)(i % packs) * 8;
-        float g[8], u[8], o[8];
-        unpack8(ld8(gu + t * ld + j), g);
-        unpack8(ld8(gu + t * ld + I + j), u);
+    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (j >= I) return;
+    for (long t0 = 2 * (long)blockIdx.y; t0 < T; t0 += 2 * (long)gridDim.y) {
+        Pack8 gp[2], up[2];
 #pragma unroll
-        for (int e = 0; e < 8; e++) o[e] = rbf(silu(g[e])) * u[e];
-        st8(out + t * I + j, pack8(o));
+        for (int r = 0; r < 2; r++)
+            if (t0 + r < T) {
+                gp[r] = ld8(gu + (t0 + r) * ld + j);
+                up[r] = ld8(gu + (t0 + r) * ld + I + j);
+            }
+#pragma unroll
+        for (int r = 0; r < 2; r++)
+            if (t0 + r < T) {
+                float g[8], u[8], o[8];
+                unpack8(gp[r], g);
+                unpack8(up[r], u);
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] = silu(g[e]);
+                rbf8(o);
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] *= u[e];
+                st8(out + (t0 + r) * I + j, pack8(o));
+            }
     }
 }
 
@@ -312,8 +339,13 @@ extern "C" int cs1_silu_mul(const void* gate_up, int ld, void* out, int T, int I
     if (n == 0) return cudaSuccess;
     auto st = static_cast<cudaStream_t>(stream);
     if (I % 8 == 0 && ld % 8 == 0 && aligned16(gate_up) && aligned16(out))
-        silu_mul_vec_kernel<<<grid_for(n / 8), THREADS, 0, st>>>(static_cast<const bf16*>(gate_up), ld,
+    {
+        const unsigned cols = (unsigned)((I / 8 + THREADS - 1) / THREADS);
+        const long pairs = ((long)T + 1) / 2;
+        const unsigned rows = (unsigned)(pairs < 65535 ? pairs : 65535);
+        silu_mul_vec_kernel<<<dim3(cols, rows), THREADS, 0, st>>>(static_cast<const bf16*>(gate_up), ld,
                                                                   static_cast<bf16*>(out), I, T);
+    }
     else
         silu_mul_scalar_kernel<<<grid_for(n), THREADS, 0, st>>>(static_cast<const bf16*>(gate_up), ld,
                                                                  static_cast<bf16*>(out), I, T);

@@ -22,6 +22,13 @@ __global__ void __launch_bounds__(NT) rms_kernel(bf16* __restrict__ res, const b
     __shared__ float scratch[32];
     const size_t row = blockIdx.x;
     const int packs = D >> 3;
+    // the weights are loaded with the row, ahead of the reduction
+    Pack8 wp[MAXP];
+#pragma unroll
+    for (int i = 0; i < MAXP; i++) {
+        const int pk = threadIdx.x + i * NT;
+        if (pk < packs) wp[i] = ld8(w + (size_t)pk * 8);
+    }
     float v[MAXP][8];
     float ss = 0.f;
 #pragma unroll
@@ -49,12 +56,99 @@ __global__ void __launch_bounds__(NT) rms_kernel(bf16* __restrict__ res, const b
         const int pk = threadIdx.x + i * NT;
         if (pk < packs) {
             float wv[8], o[8];
-            unpack8(ld8(w + (size_t)pk * 8), wv);
+            unpack8(wp[i], wv);
 #pragma unroll
             for (int e = 0; e < 8; e++) o[e] = v[i][e] * inv * (1.f + wv[e]);
             st8(out + row * D + (size_t)pk * 8, pack8(o));
         }
     }
+}
+
+// One warp per row for D <= 32 * 8 * PPL: every 16-byte pack of the row is loaded before
+// the warp reduces it (no block barrier), the weights sit in shared memory, and each warp
+// walks rows with a grid stride. The add variant keeps the bf16 sums packed in registers.
+constexpr int PPL = 20;  // packs per lane: D <= 5120
+constexpr int RW_WARPS = 8;
+template <bool Add>
+__global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
+                                                                 const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                                 bf16* __restrict__ out, int rows, int D, float eps) {
+    __shared__ Pack8 wsm[32 * PPL];
+    const int packs = D >> 3, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < packs; i += blockDim.x) wsm[i] = ld8(w + (size_t)i * 8);
+    __syncthreads();
+    const int warps = gridDim.x * RW_WARPS;
+    for (int row = blockIdx.x * RW_WARPS + (threadIdx.x >> 5); row < rows; row += warps) {
+        const size_t off = (size_t)row * D;
+        Pack8 v[PPL];
+        if constexpr (Add) {
+            Pack8 b[PPL];
+#pragma unroll
+            for (int i = 0; i < PPL; i++) {
+                const int pk = lane + 32 * i;
+                if (pk < packs) {
+                    v[i] = ld8(res + off + (size_t)pk * 8);
+                    b[i] = ld8(delta + off + (size_t)pk * 8);
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < PPL; i++) {
+                const int pk = lane + 32 * i;
+                if (pk < packs) {
+                    float fa[8], fb[8];
+                    unpack8(v[i], fa);
+                    unpack8(b[i], fb);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) fa[e] += fb[e];
+                    v[i] = pack8(fa);
+                    st8(res + off + (size_t)pk * 8, v[i]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < PPL; i++) {
+                const int pk = lane + 32 * i;
+                if (pk < packs) v[i] = ld8(x + off + (size_t)pk * 8);
+            }
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < PPL; i++) {
+            if (lane + 32 * i < packs) {
+                float f[8];
+                unpack8(v[i], f);
+#pragma unroll
+                for (int e = 0; e < 8; e++) ss = fmaf(f[e], f[e], ss);
+            }
+        }
+        const float inv = rsqrtf(warp_sum(ss) / D + eps);
+#pragma unroll
+        for (int i = 0; i < PPL; i++) {
+            const int pk = lane + 32 * i;
+            if (pk < packs) {
+                float f[8], wv[8], o[8];
+                unpack8(v[i], f);
+                unpack8(wsm[pk], wv);
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] = f[e] * inv * (1.f + wv[e]);
+                st8(out + off + (size_t)pk * 8, pack8(o));
+            }
+        }
+    }
+}
+
+int rms_warp_grid(int rows) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0, n = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) ==
+                                                      cudaSuccess && n > 0)
+            sms = n;
+        else
+            sms = 148;
+    }
+    const int need = (rows + RW_WARPS - 1) / RW_WARPS;
+    return need < sms * 8 ? need : sms * 8;
 }
 
 // Any D: scalar path, two passes over the row.
@@ -115,6 +209,53 @@ __global__ void gated_kernel(const bf16* __restrict__ x, const bf16* __restrict_
     *reinterpret_cast<uint2*>(out + base) = r;
 }
 
+// Half a warp per (token, head) row of 128 (16-byte lane accesses), G_ROWS rows per
+// warp with every load issued before the first row is reduced.
+constexpr int G_ROWS = 8;
+__global__ void gated16_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
+                               const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
+    const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
+    const int row0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * G_ROWS;
+    if (row0 >= rows) return;
+    Pack8 xr[G_ROWS / 2], zr[G_ROWS / 2];
+#pragma unroll
+    for (int i = 0; i < G_ROWS / 2; i++) {
+        const int row = row0 + 2 * i + half;
+        if (row < rows) {
+            xr[i] = ld8(x + (size_t)row * 128 + hl * 8);
+            zr[i] = ld8(z + (size_t)(row / H) * ldz + (size_t)(row % H) * 128 + hl * 8);
+        } else {
+            const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            xr[i] = zr[i] = pack8(zero);
+        }
+    }
+    float wv[8];
+    unpack8(ld8(w + hl * 8), wv);
+#pragma unroll
+    for (int i = 0; i < G_ROWS / 2; i++) {
+        const int row = row0 + 2 * i + half;
+        float v[8], zz[8];
+        unpack8(xr[i], v);
+        unpack8(zr[i], zz);
+        float ss = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(ss / 128.f + eps);
+        float o8[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) o8[e] = v[e] * inv;
+        rbf8(o8);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o8[e] *= wv[e];
+        rbf8(o8);
+#pragma unroll
+        for (int e = 0; e < 8; e++) o8[e] *= silu_fast(zz[e]);
+        if (row < rows) st8(out + (size_t)row * 128 + hl * 8, pack8(o8));
+    }
+}
+
 __global__ void gated_scalar_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
                                     const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -144,7 +285,9 @@ extern "C" int cs1_rms_norm(const void* x, const void* w, void* out, int rows, i
     auto X = static_cast<const bf16*>(x);
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
-    if (vec_ok(D, x, w, out, out))
+    if (vec_ok(D, x, w, out, out) && D <= 256 * PPL)
+        rms_warp_kernel<false><<<rms_warp_grid(rows), RW_WARPS * 32, 0, st>>>(nullptr, nullptr, X, Wt, O, rows, D, eps);
+    else if (vec_ok(D, x, w, out, out))
         rms_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
     else
         rms_scalar_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
@@ -160,7 +303,9 @@ extern "C" int cs1_add_rms_norm(void* residual, const void* delta, const void* w
     auto Dl = static_cast<const bf16*>(delta);
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
-    if (vec_ok(D, residual, delta, w, out))
+    if (vec_ok(D, residual, delta, w, out) && D <= 256 * PPL)
+        rms_warp_kernel<true><<<rms_warp_grid(rows), RW_WARPS * 32, 0, st>>>(R, Dl, nullptr, Wt, O, rows, D, eps);
+    else if (vec_ok(D, residual, delta, w, out))
         rms_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
     else
         rms_scalar_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
@@ -174,9 +319,14 @@ extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const v
     if (rows == 0) return cudaSuccess;
     constexpr int WARPS = 8;
     auto st = static_cast<cudaStream_t>(stream);
-    const bool vec = ldz % 4 == 0 && ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(z) |
-                                       reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out)) & 7) == 0;
-    if (vec)
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(z) |
+                           reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out);
+    const bool vec = ldz % 4 == 0 && (bits & 7) == 0;
+    if (ldz % 8 == 0 && (bits & 15) == 0) {
+        const int per_block = WARPS * G_ROWS;
+        gated16_kernel<<<(rows + per_block - 1) / per_block, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
+            static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
+    } else if (vec)
         gated_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
             static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
     else
