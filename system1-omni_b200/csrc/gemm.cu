@@ -526,6 +526,230 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Swapped-operand variant for few rows of x (short prompts): the MMA's M side is 128
+// rows of w (output columns) and its N side NT rows of x (a multiple of 16 up to 256),
+// D^T[128 w rows][NT rows of x], so the rows of x are covered at a granularity of 16
+// instead of 128 and the tile count can be matched to the SMs. The K reduction of each
+// output element has the same order as in the other kernels. Epilogue warps own TMEM
+// lanes = output columns; each stages 32 rows x 32 columns in shared memory and stores
+// 64-byte row segments. A SwiGLU tile holds a gate block of w and its up block (two
+// accumulators; NT <= 128).
+constexpr int S_STAGES = 4;
+constexpr int S_STAGE_BYTES = 48 * 1024;
+constexpr int S_STG_OFFSET = S_STAGES * S_STAGE_BYTES;  // 4 warps x [32][32] bf16 staging
+constexpr int S_BAR_OFFSET = S_STG_OFFSET + 4 * 2048;
+constexpr int S_SMEM = S_BAR_OFFSET + 256 + 1024;
+
+struct SwapParams {
+    bf16* y;
+    int ldy;
+    int M, N, K;  // M rows of x, N rows of w (both halves for SwiGLU)
+    int nt;       // rows of x per tile
+    int tiles_w, tiles_t;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_swap_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                     SwapParams p) {
+    constexpr bool SW = EPI == EPI_SWIGLU;
+    constexpr int A_BYTES = BM * BK * 2;
+    constexpr uint32_t B_OFF = SW ? 2 * A_BYTES : A_BYTES;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + S_BAR_OFFSET;
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (S_STAGES + s); };
+    auto tfull = [&](int a) { return bars + 8u * (2 * S_STAGES + a); };
+    auto tempty = [&](int a) { return bars + 8u * (2 * S_STAGES + 2 + a); };
+    const uint32_t drain = bars + 8u * (2 * S_STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S_BAR_OFFSET + 8 * (2 * S_STAGES + 5));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_tiles = p.tiles_w * p.tiles_t;
+    const int KB = (p.K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S_STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 4);
+        }
+        mbar_init(drain, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&map_w);
+        tma_prefetch_desc(&map_x);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            long issued = 0;
+            bool ok = true;
+            const uint32_t tx = B_OFF + (uint32_t)p.nt * BK * 2;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                const int wt = t / p.tiles_t, tt = t - wt * p.tiles_t;
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(empty(s), ph ^ 1)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = base + s * S_STAGE_BYTES;
+                    mbar_expect_tx(full(s), tx);
+                    tma_load_2d(dst, &map_w, full(s), kb * BK, SW ? wt * 256 : wt * BM);
+                    if constexpr (SW) tma_load_2d(dst + A_BYTES, &map_w, full(s), kb * BK, wt * 256 + BM);
+                    tma_load_2d(dst + B_OFF, &map_x, full(s), kb * BK, tt * p.nt);
+                    issued++;
+                    if (++s == S_STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            const long pending = issued < S_STAGES ? issued : S_STAGES;
+            for (long i = 0; i < pending; i++) {
+                if (--s < 0) {
+                    s = S_STAGES - 1;
+                    ph ^= 1;
+                }
+                (void)mbar_wait(full(s), ph);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            int s = 0, acc = 0;
+            uint32_t ph = 0, acc_ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+                const int wt = t / p.tiles_t, tt = t - wt * p.tiles_t;
+                (void)wt;
+                const int rows = min(p.nt, p.M - tt * p.nt);
+                const uint32_t id = idesc(BM, (rows + 15) & ~15, AB_BF16);
+                if (!mbar_wait(tempty(acc), acc_ph ^ 1)) {
+                    atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + acc * 256;
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(full(s), ph)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = base + s * S_STAGE_BYTES;
+                    const uint64_t ad = desc_sw128(a_addr), bd = desc_sw128(a_addr + B_OFF);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++) {
+                        mma_bf16(d, ad + 2 * k, bd + 2 * k, id, (kb | k) != 0);
+                        if constexpr (SW) mma_bf16(d + 128, desc_sw128(a_addr + A_BYTES) + 2 * k, bd + 2 * k, id,
+                                                   (kb | k) != 0);
+                    }
+                    mma_commit(empty(s));
+                    if (++s == S_STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(tfull(acc));
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_ph ^= 1;
+                }
+            }
+            mma_commit(drain);
+            (void)mbar_wait(drain, 0);
+        }
+    } else {
+        const int q = warp & 3;
+        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+        bf16* stg = reinterpret_cast<bf16*>(smem + S_STG_OFFSET + q * 2048);  // [32 rows of x][32 columns]
+        const int out_n = SW ? p.N / 2 : p.N;
+        int acc = 0;
+        uint32_t acc_ph = 0;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            const int wt = t / p.tiles_t, tt = t - wt * p.tiles_t;
+            if (!mbar_wait(tfull(acc), acc_ph)) {
+                if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            const int col0 = wt * BM + q * 32;  // this warp's 32 output columns
+            const int row0 = tt * p.nt;
+            const int rows = min(p.nt, p.M - row0);
+#pragma unroll 1
+            for (int c = 0; c * 32 < rows; c++) {
+                float v[32];
+                tmem_ld32(lane_addr + acc * 256 + c * 32, v);
+                if constexpr (SW) {
+                    float u[32];
+                    tmem_ld32(lane_addr + acc * 256 + 128 + c * 32, u);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = rbf(silu(rbf(v[i]))) * rbf(u[i]);
+                } else {
+                    tmem_ld_wait();
+                }
+                // STORE: bf16(acc); RESIDUAL: bf16(acc), added to the residual below; SwiGLU: the output
+#pragma unroll
+                for (int i = 0; i < 32; i++) stg[i * 32 + lane] = to_bf16(v[i]);
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int ch = lane + 32 * j, i = ch >> 2, part = ch & 3;
+                    const int r = c * 32 + i, row = row0 + r, col = col0 + part * 8;
+                    if (r < rows && col + 8 <= out_n) {  // rows of this tile only (r < rows implies row < M)
+                        const Pack8 val = *reinterpret_cast<const Pack8*>(stg + i * 32 + part * 8);
+                        bf16* dst = p.y + (size_t)row * p.ldy + col;
+                        if constexpr (EPI == EPI_RESIDUAL) {
+                            float r[8], a[8];
+                            unpack8(ld8(dst), r);
+                            unpack8(val, a);
+#pragma unroll
+                            for (int e = 0; e < 8; e++) r[e] += a[e];
+                            st8(dst, pack8(r));
+                        } else {
+                            st8(dst, val);
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty(acc));
+            if (++acc == 2) {
+                acc = 0;
+                acc_ph ^= 1;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 // Any shape: one thread per output, fp32 accumulation in K order. Used only when
 // a shape or pointer misses the tensor-map alignment rules.
 template <int EPI>
@@ -560,6 +784,7 @@ struct Handle {
     int fixed_m = 0;
     bool pairs = true;  // CTA-pair kernels for large M (S1_GEMM_PAIRS=0 selects the single-CTA kernels)
     int group = 0;      // tile grouping (0: the kernels' defaults; S1_GEMM_GROUP overrides, for tuning)
+    bool swap = true;   // swapped-operand kernel for few rows (S1_GEMM_SWAP=0 disables)
 };
 
 template <int BN, int EPI>
@@ -617,6 +842,57 @@ int launch_pair(const Handle* h, const void* x, const void* w, void* y, int M, i
     return cudaGetLastError();
 }
 
+template <int EPI>
+int launch_swap(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int nt,
+                cudaStream_t st) {
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(gemm_swap_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM);
+    if (configured != cudaSuccess) return configured;
+    CUtensorMap mw, mx;
+    int e = host::make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, BM, BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    e = host::make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, K, (uint32_t)nt, BK,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    SwapParams p;
+    p.y = static_cast<bf16*>(y);
+    p.ldy = ldy;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.nt = nt;
+    p.tiles_w = EPI == EPI_SWIGLU ? N / 256 : (N + BM - 1) / BM;
+    p.tiles_t = (M + nt - 1) / nt;
+    const int tiles = p.tiles_w * p.tiles_t;
+    gemm_swap_kernel<EPI><<<std::min(tiles, h->sms), THREADS, S_SMEM, st>>>(mw, mx, p);
+    return cudaGetLastError();
+}
+
+// Best token tile of the swapped kernel and its estimated time in the units of the
+// kernel choice below (waves x per-tile time relative to a 256 x 256 CTA-pair tile).
+// A tile of 128 w rows x nt rows costs nt / 256 of a 128 x 256 single-CTA tile, scaled up
+// where its operand bytes per MMA cycle (8192 / nt + 64; SwiGLU 8192 / nt + 32) exceed
+// what the 128 x 256 tiles sustain (~100 B / cycle / SM).
+double swap_cost(int M, int N, int epi, int sms, int& best_nt) {
+    const bool sw = epi == EPI_SWIGLU;
+    const long tiles_w = sw ? N / 256 : (N + BM - 1) / BM;
+    double best = 1e30;
+    best_nt = 0;
+    for (int nt = 32; nt <= (sw ? 128 : 256); nt += 16) {
+        const long tiles = tiles_w * ((M + nt - 1) / nt);
+        const long waves = (tiles + sms - 1) / sms;
+        const double rate = 8192.0 / nt + (sw ? 32.0 : 64.0);
+        const double eff = rate > 100.0 ? rate / 100.0 : 1.0;
+        const double c = (double)waves * 1.15 * (sw ? 2.0 : 1.0) * nt / 256.0 * eff;
+        if (c < best) {
+            best = c;
+            best_nt = nt;
+        }
+    }
+    return best;
+}
+
 int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int epi,
         cudaStream_t st) {
     if (!h || M < 0 || N <= 0 || K <= 0 || !x || !w || !y) return cudaErrorInvalidValue;
@@ -653,6 +929,18 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
     const double c_pair = (double)((pair_tiles + slots / 2 - 1) / (slots / 2)) * 1.0;
     const double c_256 = (double)((t256 + slots - 1) / slots) * 1.15;
     const double c_128 = (double)((t128 + slots - 1) / slots) * 0.6;
+    int nt = 0;
+    const double c_swap = h->swap ? swap_cost(M, N, epi, (int)slots, nt) : 1e30;
+    if (nt > 0 && c_swap < c_pair && c_swap < c_256 && c_swap < c_128) {
+        switch (epi) {
+            case EPI_SWIGLU:
+                return launch_swap<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, nt, st);
+            case EPI_RESIDUAL:
+                return launch_swap<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, nt, st);
+            default:
+                return launch_swap<EPI_STORE>(h, x, w, y, M, N, K, ldy, nt, st);
+        }
+    }
     if (h->pairs && c_pair <= c_256 && c_pair <= c_128) {
         switch (epi) {
             case EPI_SWIGLU:
@@ -696,6 +984,8 @@ void* cs1_gemm_create(size_t workspace_bytes) {
     h->pairs = !(env && env[0] == '0');
     const char* grp = getenv("S1_GEMM_GROUP");
     if (grp) h->group = atoi(grp);
+    const char* sw = getenv("S1_GEMM_SWAP");
+    h->swap = !(sw && sw[0] == '0');
     return h;
 }
 

@@ -144,3 +144,35 @@ def test_gemm_invalid_arguments(cs1, gemm, stream):
     assert cs1.raw.cs1_gemm(gemm, x.data_ptr(), x.data_ptr(), y.data_ptr(), 4, 64, 64, 32, stream) != 0
     assert cs1.raw.cs1_gemm(gemm, x.data_ptr(), x.data_ptr(), y.data_ptr(), -1, 64, 64, 64, stream) != 0
     assert cs1.raw.cs1_gemm(gemm, x.data_ptr(), x.data_ptr(), y.data_ptr(), 0, 64, 64, 64, stream) == 0
+
+
+@pytest.mark.parametrize("M,N,epi", [(771, 16480, "store"), (300, 5120, "residual"), (771, 2560, "swiglu"),
+                                     (17, 1544, "store"), (1, 5120, "residual")])
+def test_swapped_operand_kernel_equals_row_kernels(cs1, stream, monkeypatch, M, N, epi):
+    """Short inputs go through the swapped-operand kernel (rows of w as the MMA's M side,
+    rows of x as its N side); its bits equal those of the 128-row kernels."""
+    K = 1024
+    x = _rand((M, K), 17)
+    w = _rand((2 * N if epi == "swiglu" else N, K), 18, 0.05)
+    res = _rand((M, N), 19)
+    out = []
+    for swap in ("1", "0"):
+        monkeypatch.setenv("S1_GEMM_SWAP", swap)
+        h = cs1.cs1_gemm_create(0)
+        if epi == "swiglu":
+            y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            cs1.cs1_gemm_swiglu(h, x, w, y, M, N, K, N, stream)
+        elif epi == "residual":
+            y = res.clone()
+            cs1.cs1_gemm_residual(h, x, w, y, M, N, K, N, stream)
+        else:
+            y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            cs1.cs1_gemm(h, x, w, y, M, N, K, N, stream)
+        torch.cuda.synchronize()
+        cs1.cs1_gemm_destroy(h)
+        out.append(y)
+    assert cs1.cs1_fault_status(1) == 0
+    if epi == "store":
+        ref = (x.float() @ w.float().T).cpu().numpy()
+        assert max_rel(out[0].float().cpu().numpy(), ref) <= 1e-2
+    assert torch.equal(out[0], out[1])
