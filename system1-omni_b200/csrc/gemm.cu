@@ -25,6 +25,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <new>
+#include <string>
 
 #include "common.cuh"
 #include "ops_internal.h"
@@ -47,7 +48,8 @@ struct Cfg {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = 2 * BN;
-    static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+    static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;   // epilogue staging, 4 warps x 32 rows x 80 B
+    static constexpr int BAR_OFFSET = STG_OFFSET + 4 * 32 * 80;
     static constexpr int SMEM = BAR_OFFSET + 256 + 1024;  // barriers + TMEM address + alignment slack
 };
 
@@ -81,6 +83,45 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
         n = first + r % gn;
         m = r / gn;
     }
+}
+
+// Epilogue store of one warp's 32 rows x 32 columns: lane i holds row row0 + i (v: its
+// 32 columns, the STORE / RESIDUAL accumulator or the finished SwiGLU output). The block
+// goes through a private shared-memory tile (rows 80 bytes apart: the 16-byte chunks of
+// any 8 rows fall in distinct bank groups) and leaves as 64-byte row segments, so a warp
+// store writes whole 32-byte sectors of 8 rows instead of 16 bytes of 32 rows. The
+// residual is read the same way; numerics as before: bf16(acc), bf16(res + bf16(acc)).
+template <int EPI>
+__device__ __forceinline__ void store_block(uint8_t* stg, const float (&v)[32], bf16* y, int ldy, int row0,
+                                            int M, int col, int out_n, int lane) {
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) f[e] = v[j * 8 + e];
+        *reinterpret_cast<Pack8*>(stg + lane * 80 + j * 16) = pack8(f);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int ch = lane + 32 * j, i = ch >> 2, part = ch & 3;
+        const int row = row0 + i, c = col + part * 8;
+        if (row < M && c + 8 <= out_n) {
+            const Pack8 val = *reinterpret_cast<const Pack8*>(stg + i * 80 + part * 16);
+            bf16* dst = y + (size_t)row * ldy + c;
+            if constexpr (EPI == EPI_RESIDUAL) {
+                float r[8], a[8];
+                unpack8(ld8(dst), r);
+                unpack8(val, a);
+#pragma unroll
+                for (int e = 0; e < 8; e++) r[e] += a[e];
+                st8(dst, pack8(r));
+            } else {
+                st8(dst, val);
+            }
+        }
+    }
+    __syncwarp();
 }
 
 template <int BN, int EPI>
@@ -217,35 +258,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const int row = m * BM + q * 32 + lane;
-            const bool row_ok = row < p.M;
+            const int row0 = m * BM + q * 32;  // this warp's 32 rows
             const uint32_t tcol = lane_addr + acc * BN;
+            uint8_t* stg = smem + C::STG_OFFSET + q * 32 * 80;
             if constexpr (EPI == EPI_SWIGLU) {
                 // columns [0, BN/2) are gate rows, [BN/2, BN) the matching up rows
                 const int out_col0 = n * (BN / 2);
-                const int out_n = p.N / 2;
 #pragma unroll 1
                 for (int c = 0; c < BN / 64; c++) {
                     float g[32], u[32];
                     tmem_ld32(tcol + c * 32, g);
                     tmem_ld32(tcol + BN / 2 + c * 32, u);
                     tmem_ld_wait();
-                    const int col = out_col0 + c * 32;
-                    if (row_ok) {
-                        bf16* dst = p.y + (size_t)row * p.ldy + col;
 #pragma unroll
-                        for (int v = 0; v < 4; v++) {
-                            if (col + v * 8 + 8 <= out_n) {
-                                float o[8];
-#pragma unroll
-                                for (int e = 0; e < 8; e++) {
-                                    const float gg = rbf(g[v * 8 + e]), uu = rbf(u[v * 8 + e]);
-                                    o[e] = rbf(silu(gg)) * uu;
-                                }
-                                st8(dst + v * 8, pack8(o));
-                            }
-                        }
-                    }
+                    for (int e = 0; e < 32; e++) g[e] = rbf(silu(rbf(g[e]))) * rbf(u[e]);
+                    store_block<EPI>(stg, g, p.y, p.ldy, row0, p.M, out_col0 + c * 32, p.N / 2, lane);
                 }
             } else {
 #pragma unroll 1
@@ -253,26 +280,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     float v[32];
                     tmem_ld32(tcol + c * 32, v);
                     tmem_ld_wait();
-                    const int col = n * BN + c * 32;
-                    if (row_ok) {
-                        bf16* dst = p.y + (size_t)row * p.ldy + col;
-#pragma unroll
-                        for (int g8 = 0; g8 < 4; g8++) {
-                            if (col + g8 * 8 + 8 <= p.N) {
-                                float o[8];
-                                if constexpr (EPI == EPI_RESIDUAL) {
-                                    float r[8];
-                                    unpack8(ld8(dst + g8 * 8), r);
-#pragma unroll
-                                    for (int e = 0; e < 8; e++) o[e] = r[e] + rbf(v[g8 * 8 + e]);
-                                } else {
-#pragma unroll
-                                    for (int e = 0; e < 8; e++) o[e] = v[g8 * 8 + e];
-                                }
-                                st8(dst + g8 * 8, pack8(o));
-                            }
-                        }
-                    }
+                    store_block<EPI>(stg, v, p.y, p.ldy, row0, p.M, n * BN + c * 32, p.N, lane);
                 }
             }
             tc_fence_before();
@@ -306,7 +314,8 @@ constexpr int P_STAGES = 6;
 constexpr int P_A_BYTES = 128 * BK * 2;
 constexpr int P_B_BYTES = 128 * BK * 2;
 constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
-constexpr int P_BAR_OFFSET = P_STAGES * P_STAGE_BYTES;
+constexpr int P_STG_OFFSET = P_STAGES * P_STAGE_BYTES;  // epilogue staging, 4 warps x 32 rows x 80 B
+constexpr int P_BAR_OFFSET = P_STG_OFFSET + 4 * 32 * 80;
 constexpr int P_SMEM = P_BAR_OFFSET + 256 + 1024;
 constexpr int P_GROUP_M = 16;
 
@@ -454,31 +463,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const int row = m * 256 + (int)rank * 128 + q * 32 + lane;
-            const bool row_ok = row < p.M;
+            const int row0 = m * 256 + (int)rank * 128 + q * 32;  // this warp's 32 rows
             const uint32_t tcol = lane_addr + acc * BN;
+            uint8_t* stg = smem + P_STG_OFFSET + q * 32 * 80;
             if constexpr (EPI == EPI_SWIGLU) {
                 const int out_col0 = n * (BN / 2);
-                const int out_n = p.N / 2;
 #pragma unroll 1
                 for (int c = 0; c < BN / 64; c++) {
                     float g[32], u[32];
                     tmem_ld32(tcol + c * 32, g);
                     tmem_ld32(tcol + BN / 2 + c * 32, u);
                     tmem_ld_wait();
-                    const int col = out_col0 + c * 32;
-                    if (row_ok) {
-                        bf16* dst = p.y + (size_t)row * p.ldy + col;
 #pragma unroll
-                        for (int v = 0; v < 4; v++) {
-                            if (col + v * 8 + 8 <= out_n) {
-                                float o[8];
-#pragma unroll
-                                for (int e = 0; e < 8; e++) o[e] = rbf(silu(rbf(g[v * 8 + e]))) * rbf(u[v * 8 + e]);
-                                st8(dst + v * 8, pack8(o));
-                            }
-                        }
-                    }
+                    for (int e = 0; e < 32; e++) g[e] = rbf(silu(rbf(g[e]))) * rbf(u[e]);
+                    store_block<EPI>(stg, g, p.y, p.ldy, row0, p.M, out_col0 + c * 32, p.N / 2, lane);
                 }
             } else {
 #pragma unroll 1
@@ -486,26 +484,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     float v[32];
                     tmem_ld32(tcol + c * 32, v);
                     tmem_ld_wait();
-                    const int col = n * BN + c * 32;
-                    if (row_ok) {
-                        bf16* dst = p.y + (size_t)row * p.ldy + col;
-#pragma unroll
-                        for (int g8 = 0; g8 < 4; g8++) {
-                            if (col + g8 * 8 + 8 <= p.N) {
-                                float o[8];
-                                if constexpr (EPI == EPI_RESIDUAL) {
-                                    float r[8];
-                                    unpack8(ld8(dst + g8 * 8), r);
-#pragma unroll
-                                    for (int e = 0; e < 8; e++) o[e] = r[e] + rbf(v[g8 * 8 + e]);
-                                } else {
-#pragma unroll
-                                    for (int e = 0; e < 8; e++) o[e] = v[g8 * 8 + e];
-                                }
-                                st8(dst + g8 * 8, pack8(o));
-                            }
-                        }
-                    }
+                    store_block<EPI>(stg, v, p.y, p.ldy, row0, p.M, n * BN + c * 32, p.N, lane);
                 }
             }
             tc_fence_before();
@@ -547,7 +526,27 @@ struct SwapParams {
     int M, N, K;  // M rows of x, N rows of w (both halves for SwiGLU)
     int nt;       // rows of x per tile
     int tiles_w, tiles_t;
+    int full;     // tiles done whole (whole waves); the rest are split along x
+    int split;    // parts per remaining tile, of `sub` rows of x each
+    int sub;
+    int items;    // full + (tiles_w * tiles_t - full) * split
 };
+
+// Work item -> (w tile, first row of x, rows of x). Items past `full` are parts of the
+// last partial wave's tiles, so that wave spreads over every SM; a part can be empty.
+__device__ __forceinline__ void swap_item(const SwapParams& p, int t, int& wt, int& x0, int& rows) {
+    int tile = t, part = 0, span = p.nt;
+    if (t >= p.full) {
+        const int u = t - p.full;
+        tile = p.full + u / p.split;
+        part = u - (u / p.split) * p.split;
+        span = p.sub;
+    }
+    wt = tile / p.tiles_t;
+    const int tt = tile - wt * p.tiles_t;
+    x0 = tt * p.nt + part * span;
+    rows = min(min(span, p.nt - part * span), p.M - x0);
+}
 
 template <int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -569,7 +568,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S_BAR_OFFSET + 8 * (2 * S_STAGES + 5));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int num_tiles = p.tiles_w * p.tiles_t;
+    const int num_tiles = p.items;
     const int KB = (p.K + BK - 1) / BK;
 
     if (threadIdx.x == 0) {
@@ -603,7 +602,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = true;
             const uint32_t tx = B_OFF + (uint32_t)p.nt * BK * 2;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int wt = t / p.tiles_t, tt = t - wt * p.tiles_t;
+                int wt, x0, rows;
+                swap_item(p, t, wt, x0, rows);
+                if (rows <= 0) continue;
                 for (int kb = 0; kb < KB; kb++) {
                     if (!mbar_wait(empty(s), ph ^ 1)) {
                         atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
@@ -614,7 +615,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mbar_expect_tx(full(s), tx);
                     tma_load_2d(dst, &map_w, full(s), kb * BK, SW ? wt * 256 : wt * BM);
                     if constexpr (SW) tma_load_2d(dst + A_BYTES, &map_w, full(s), kb * BK, wt * 256 + BM);
-                    tma_load_2d(dst + B_OFF, &map_x, full(s), kb * BK, tt * p.nt);
+                    tma_load_2d(dst + B_OFF, &map_x, full(s), kb * BK, x0);
                     issued++;
                     if (++s == S_STAGES) {
                         s = 0;
@@ -637,9 +638,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t ph = 0, acc_ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-                const int wt = t / p.tiles_t, tt = t - wt * p.tiles_t;
-                (void)wt;
-                const int rows = min(p.nt, p.M - tt * p.nt);
+                int wt, x0, rows;
+                swap_item(p, t, wt, x0, rows);
+                if (rows <= 0) continue;
                 const uint32_t id = idesc(BM, (rows + 15) & ~15, AB_BF16);
                 if (!mbar_wait(tempty(acc), acc_ph ^ 1)) {
                     atomicOr(&g_fault_word, FAULT_WAIT_MMA);
@@ -686,15 +687,15 @@ __global__ void __launch_bounds__(THREADS, 1)
         int acc = 0;
         uint32_t acc_ph = 0;
         for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-            const int wt = t / p.tiles_t, tt = t - wt * p.tiles_t;
+            int wt, row0, rows;
+            swap_item(p, t, wt, row0, rows);
+            if (rows <= 0) continue;
             if (!mbar_wait(tfull(acc), acc_ph)) {
                 if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
                 break;
             }
             tc_fence_after();
             const int col0 = wt * BM + q * 32;  // this warp's 32 output columns
-            const int row0 = tt * p.nt;
-            const int rows = min(p.nt, p.M - row0);
 #pragma unroll 1
             for (int c = 0; c * 32 < rows; c++) {
                 float v[32];
@@ -785,7 +786,12 @@ struct Handle {
     bool pairs = true;  // CTA-pair kernels for large M (S1_GEMM_PAIRS=0 selects the single-CTA kernels)
     int group = 0;      // tile grouping (0: the kernels' defaults; S1_GEMM_GROUP overrides, for tuning)
     bool swap = true;   // swapped-operand kernel for few rows (S1_GEMM_SWAP=0 disables)
+    // Tuning override (S1_GEMM_KERNEL = pair | row256 | row128 | swap, S1_GEMM_NT = the
+    // swapped kernel's rows of x per tile): every call of the handle uses that kernel
+    // where the shape allows it. 0 = the wave model's choice.
+    int force = 0, force_nt = 0;
 };
+enum Force : int { FORCE_NONE = 0, FORCE_PAIR, FORCE_ROW256, FORCE_ROW128, FORCE_SWAP };
 
 template <int BN, int EPI>
 int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy,
@@ -842,6 +848,22 @@ int launch_pair(const Handle* h, const void* x, const void* w, void* y, int M, i
     return cudaGetLastError();
 }
 
+// Whole waves of tiles stay whole; the tiles of a last partial wave are split along x
+// into parts of at least 64 rows so that they spread over the idle SMs.
+void swap_split(int tiles, int sms, int nt, int& full, int& split, int& sub) {
+    full = tiles / sms * sms;
+    const int rem = tiles - full;
+    split = 1;
+    if (rem > 0) {
+        const int by_sms = (sms + rem - 1) / rem;
+        const int by_rows = nt / 64 > 1 ? nt / 64 : 1;
+        split = by_sms < by_rows ? by_sms : by_rows;
+        while (split > 1 && rem * split > sms) split--;
+    }
+    sub = ((nt + split - 1) / split + 15) & ~15;
+    if (split == 1) full = tiles;
+}
+
 template <int EPI>
 int launch_swap(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int nt,
                 cudaStream_t st) {
@@ -865,7 +887,9 @@ int launch_swap(const Handle* h, const void* x, const void* w, void* y, int M, i
     p.tiles_w = EPI == EPI_SWIGLU ? N / 256 : (N + BM - 1) / BM;
     p.tiles_t = (M + nt - 1) / nt;
     const int tiles = p.tiles_w * p.tiles_t;
-    gemm_swap_kernel<EPI><<<std::min(tiles, h->sms), THREADS, S_SMEM, st>>>(mw, mx, p);
+    swap_split(tiles, h->sms, nt, p.full, p.split, p.sub);
+    p.items = p.full + (tiles - p.full) * p.split;
+    gemm_swap_kernel<EPI><<<std::min(p.items, h->sms), THREADS, S_SMEM, st>>>(mw, mx, p);
     return cudaGetLastError();
 }
 
@@ -881,10 +905,13 @@ double swap_cost(int M, int N, int epi, int sms, int& best_nt) {
     best_nt = 0;
     for (int nt = 32; nt <= (sw ? 128 : 256); nt += 16) {
         const long tiles = tiles_w * ((M + nt - 1) / nt);
-        const long waves = (tiles + sms - 1) / sms;
+        int full, split, sub;
+        swap_split((int)tiles, sms, nt, full, split, sub);
+        const long whole = tiles / sms;  // whole waves; a partial one costs sub / nt of a wave
+        const double waves = (double)whole + (tiles > whole * sms ? (double)sub / nt : 0.0);
         const double rate = 8192.0 / nt + (sw ? 32.0 : 64.0);
         const double eff = rate > 100.0 ? rate / 100.0 : 1.0;
-        const double c = (double)waves * 1.15 * (sw ? 2.0 : 1.0) * nt / 256.0 * eff;
+        const double c = waves * 1.15 * (sw ? 2.0 : 1.0) * nt / 256.0 * eff;
         if (c < best) {
             best = c;
             best_nt = nt;
@@ -930,8 +957,22 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
     const double c_256 = (double)((t256 + slots - 1) / slots) * 1.15;
     const double c_128 = (double)((t128 + slots - 1) / slots) * 0.6;
     int nt = 0;
-    const double c_swap = h->swap ? swap_cost(M, N, epi, (int)slots, nt) : 1e30;
-    if (nt > 0 && c_swap < c_pair && c_swap < c_256 && c_swap < c_128) {
+    double c_swap = h->swap ? swap_cost(M, N, epi, (int)slots, nt) : 1e30;
+    double cp = c_pair, c2 = c_256, c1 = epi == EPI_SWIGLU ? 1e30 : c_128;
+    if (h->force != FORCE_NONE) {  // tuning override: make the forced kernel the cheapest
+        cp = h->force == FORCE_PAIR ? 0.0 : 1e30;
+        c2 = h->force == FORCE_ROW256 ? 0.0 : 1e30;
+        c1 = h->force == FORCE_ROW128 && epi != EPI_SWIGLU ? 0.0 : 1e30;
+        c_swap = h->force == FORCE_SWAP ? 0.0 : 1e30;
+        if (h->force == FORCE_SWAP) {
+            const int cap = epi == EPI_SWIGLU ? 128 : 256;
+            if (h->force_nt >= 16 && h->force_nt <= cap && h->force_nt % 16 == 0) nt = h->force_nt;
+            if (nt == 0) nt = 128;
+        }
+        if (h->force == FORCE_PAIR && !h->pairs) cp = 1e30;
+        if (cp != 0.0 && c2 != 0.0 && c1 != 0.0 && c_swap != 0.0) c2 = 0.0;  // not applicable: 128 x 256
+    }
+    if (nt > 0 && c_swap < cp && c_swap < c2 && c_swap < c1) {
         switch (epi) {
             case EPI_SWIGLU:
                 return launch_swap<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, nt, st);
@@ -941,7 +982,7 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
                 return launch_swap<EPI_STORE>(h, x, w, y, M, N, K, ldy, nt, st);
         }
     }
-    if (h->pairs && c_pair <= c_256 && c_pair <= c_128) {
+    if (h->pairs && cp <= c2 && cp <= c1) {
         switch (epi) {
             case EPI_SWIGLU:
                 return launch_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);
@@ -951,7 +992,7 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
                 return launch_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, st);
         }
     }
-    const bool wide = epi == EPI_SWIGLU || c_256 <= c_128;
+    const bool wide = epi == EPI_SWIGLU || c2 <= c1;
     switch (epi) {
         case EPI_SWIGLU:
             return launch_tc<256, EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);
@@ -986,6 +1027,12 @@ void* cs1_gemm_create(size_t workspace_bytes) {
     if (grp) h->group = atoi(grp);
     const char* sw = getenv("S1_GEMM_SWAP");
     h->swap = !(sw && sw[0] == '0');
+    if (const char* f = getenv("S1_GEMM_KERNEL")) {
+        const std::string k(f);
+        h->force = k == "pair" ? gemm::FORCE_PAIR : k == "row256" ? gemm::FORCE_ROW256
+                 : k == "row128" ? gemm::FORCE_ROW128 : k == "swap" ? gemm::FORCE_SWAP : gemm::FORCE_NONE;
+    }
+    if (const char* nt = getenv("S1_GEMM_NT")) h->force_nt = atoi(nt);
     return h;
 }
 

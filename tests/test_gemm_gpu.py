@@ -176,3 +176,21 @@ def test_swapped_operand_kernel_equals_row_kernels(cs1, stream, monkeypatch, M, 
         ref = (x.float() @ w.float().T).cpu().numpy()
         assert max_rel(out[0].float().cpu().numpy(), ref) <= 1e-2
     assert torch.equal(out[0], out[1])
+
+
+@pytest.mark.parametrize("M,N", [(700, 16480), (1500, 14336), (400, 34816)])
+def test_swapped_kernel_split_tail_equals_row_kernels(cs1, stream, monkeypatch, M, N):
+    """Tile counts whose last wave is split along x (parts of the last tiles on idle SMs)."""
+    K = 512
+    x, w = _rand((M, K), 20), _rand((N, K), 21, 0.05)
+    out = []
+    for swap in ("1", "0"):
+        monkeypatch.setenv("S1_GEMM_SWAP", swap)
+        h = cs1.cs1_gemm_create(0)
+        y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        cs1.cs1_gemm(h, x, w, y, M, N, K, N, stream)
+        torch.cuda.synchronize()
+        cs1.cs1_gemm_destroy(h)
+        out.append(y)
+    assert cs1.cs1_fault_status(1) == 0
+    assert torch.equal(out[0], out[1])
