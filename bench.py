@@ -154,7 +154,7 @@ def reference_cuda(args, local):
     seqs = requests(0)
     tokens = int(sum(len(s) for s in seqs))
     ranges = pack_ranges([len(s) for s in seqs], 16, 4096)
-    cap = max(sum(len(s) for s in seqs[a:b]) for a, b in ranges) + 64
+    cap = max(max(sum(len(s) for s in seqs[a:b]) for a, b in ranges), 0 if args.no_long else LONG) + 64
     m = Model(cfg, device=local, max_tokens=cap, max_seqs=16, cs1_library=ref + ";" + lib_path())
     m.init_random(seed=1234, std=0.02)
     stream = torch.cuda.ExternalStream(m.stream)
@@ -179,10 +179,23 @@ def reference_cuda(args, local):
     torch.cuda.synchronize()
     ms = (time.perf_counter() - t0) * 1e3 / n
     lat = latency(m, args)
+    long = None
+    if not args.no_long:
+        # workload (b): the reference executor sends a prompt this long alone (one launch)
+        seq = long_request()
+        m.forward([seq])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(2):
+            m.forward([seq])
+        torch.cuda.synchronize()
+        lms = (time.perf_counter() - t0) * 1e3 / 2
+        long = {"workload": "27b-b-32k", "tokens": LONG, "value": LONG / (lms * 1e-3), "unit": UNIT,
+                "ms_per_step": lms, "timing": "wall clock around synchronous forward calls"}
     m.close()
     del stream
     return {"value": tokens / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "launch_ranges": len(ranges),
-            "p50_decision_latency_ms": lat,
+            "p50_decision_latency_ms": lat, "long_prefill": long,
             "library": "reference src/backends/cuda/qwen3_5 built for sm_100a (oracle/Makefile)",
             "host": "this build's C++ host, eager, host-side scorer head (the reference's executor path)",
             "timing": "wall clock around synchronous forward calls (host copies included)",

@@ -427,9 +427,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(v_empty, 1);
         mbar_init(s_full, 1);
         mbar_init(s_full + 8, 1);
-        mbar_init(s_free, 128);
-        mbar_init(s_free + 8, 128);
-        mbar_init(p_full, 128);
+        mbar_init(s_free, 4);  // one arrive per softmax warp
+        mbar_init(s_free + 8, 4);
+        mbar_init(p_full, 4);
         mbar_init(pv_done, 1);
         mbar_init(drain, 1);
         mbar_fence_init();
@@ -567,19 +567,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int c = 0; c < 4; c++) tmem_ld32(lane_addr + b * BN + c * 32, s[c]);
             tmem_ld_wait();
             tc_fence_before();
-            mbar_arrive(s_free + 8 * b);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free + 8 * b);
             const int k0 = j * BN;
             bool full = k0 + BN <= total;
             if (a.causal)
                 full = full && k0 + BN - 1 <= qpos;
             else if (a.state > 0 && qpos < a.state)
                 full = full && k0 + BN <= a.state;
-            float mx = -INFINITY;
+            // row maximum over 8 independent chains (one warp per SMSP: no other warp hides
+            // the latency of a 128-long dependent chain)
+            float m8[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) m8[i] = -INFINITY;
             if (full) {
 #pragma unroll
                 for (int c = 0; c < 4; c++)
 #pragma unroll
-                    for (int e = 0; e < 32; e++) mx = fmaxf(mx, s[c][e]);
+                    for (int e = 0; e < 32; e++) m8[e & 7] = fmaxf(m8[e & 7], s[c][e]);
             } else {
 #pragma unroll
                 for (int c = 0; c < 4; c++)
@@ -592,9 +597,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                         else if (a.state > 0 && qpos < a.state)
                             vis = vis && key < a.state;
                         s[c][e] = vis ? s[c][e] : -INFINITY;
-                        mx = fmaxf(mx, s[c][e]);
+                        m8[e & 7] = fmaxf(m8[e & 7], s[c][e]);
                     }
             }
+            float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             mx *= sl2;
             // PV_{j-1} must be complete before P is overwritten or O rescaled
             if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (uint32_t)(j - 1) & 1u))) {
@@ -621,6 +628,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             const float nm = m == -INFINITY ? 0.f : -m;
             uint8_t* prow = smem + OFF_P;
+            float l8[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) l8[i] = 0.f;
 #pragma unroll
             for (int c = 0; c < 4; c++)
 #pragma unroll
@@ -629,14 +639,16 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
                         f[e] = ex2(fmaf(s[c][g8 * 8 + e], sl2, nm));
-                        l += f[e];
+                        l8[e] += f[e];
                     }
                     const int chunk = c * 4 + g8;  // 16-byte chunk of the 128-key row
                     *reinterpret_cast<Pack8*>(prow + (chunk >> 3) * SUB + sw128_offset(r, chunk & 7)) = pack8(f);
                 }
+            l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
             fence_async_smem();
             tc_fence_before();
-            mbar_arrive(p_full);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
         }
         if (ok && n > 0) ok = mbar_wait(pv_done, (uint32_t)(n - 1) & 1u);
         tc_fence_after();

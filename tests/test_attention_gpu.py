@@ -33,7 +33,8 @@ def _row_rel(a, b):
     return float((np.abs(a - b).max(1) / np.maximum(np.abs(b).max(1), 1e-30)).max())
 
 
-@pytest.mark.parametrize("T,Hq,Hk", [(1, 4, 2), (63, 4, 2), (65, 16, 4), (139, 4, 1), (700, 24, 4), (2048, 4, 2)])
+@pytest.mark.parametrize("T,Hq,Hk", [(1, 4, 2), (63, 4, 2), (65, 16, 4), (139, 4, 1), (700, 24, 4), (2048, 4, 2),
+                                     (300, 6, 2), (130, 3, 3)])
 def test_attention_gated_matches_oracle(cs1, stream, T, Hq, Hk):
     q, k, vfull, ldv, gate = _qkv(T, Hq, Hk, T)
     out = empty_bf16(T, Hq, 256)
