@@ -672,9 +672,9 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
     if (threadIdx.x == 0) {
         mbar_init(full, 1);
         mbar_init(empty, 1);
-        mbar_init(s_ready, 128);
+        mbar_init(s_ready, 4);  // one arrive per epilogue warp
         mbar_init(ws_done, 1);
-        mbar_init(vn_ready, 128);
+        mbar_init(vn_ready, 4);
         mbar_init(upd_done, 1);
         mbar_init(drain, 1);
         mbar_fence_init();
@@ -771,19 +771,16 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
         const bf16* UT = reinterpret_cast<const bf16*>(ws.ut);
         uint8_t* st_tile = smem + OFF_ST;
         uint8_t* vn_tile = smem + OFF_VN;
-        float dec_next = NC > 0 ? ws.decay[slot0] : 1.f;
-        for (int c = 0; c < NC; c++) {
-            const uint32_t cp = (uint32_t)c & 1u;
-            const float dec = dec_next;
-            // this chunk's u^T row (128 bytes) and the next chunk's decay, ahead of their use
-            uint4 ur4[8];
-            {
-                const uint4* ur = reinterpret_cast<const uint4*>(UT + ((slot0 + c) * V + vcol) * C);
+        uint4 ur4[8];  // this chunk's u^T row (128 bytes)
+        auto load_u = [&](int c) {
+            const uint4* ur = reinterpret_cast<const uint4*>(UT + ((slot0 + c) * V + vcol) * C);
 #pragma unroll
-                for (int i = 0; i < 8; i++) ur4[i] = ur[i];
-            }
-            if (c + 1 < NC) dec_next = ws.decay[slot0 + c + 1];
-            // S row: bf16 copy for this chunk's MMAs, then e^{last} S back for the update MMA
+            for (int i = 0; i < 8; i++) ur4[i] = ur[i];
+        };
+        // Chunk c's pass over the state row: the bf16 copy the first MMAs read, then e^{last} S
+        // written back for the update MMA; one arrive per warp on s_ready.
+        auto state_pass = [&](int c) {
+            const float dec = ws.decay[slot0 + c];
 #pragma unroll
             for (int q4 = 0; q4 < 4; q4++) {
                 float x[32];
@@ -802,7 +799,15 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
             tmem_st_wait();
             fence_async_smem();
             tc_fence_before();
-            mbar_arrive(s_ready);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_ready);
+        };
+        if (NC > 0) {
+            load_u(0);
+            state_pass(0);
+        }
+        for (int c = 0; c < NC; c++) {
+            const uint32_t cp = (uint32_t)c & 1u;
             // A wait that gives up does not leave the loop on its own: the group decides
             // together at the named barrier below, so no thread waits there for one that left.
             // tcgen05.ld is warp-collective: the wait outcome is made warp-uniform
@@ -810,7 +815,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
             tc_fence_after();
             // v_new = bf16(u - wS)
 #pragma unroll
-            for (int half = 0; ok && half < 2; half++) {
+            for (int half = 0; half < 2; half++) {
+                if (!ok) break;  // warp-uniform
                 float ws_[32];
                 tmem_ld32(lane_addr + half * 32, ws_);
                 float u[32];
@@ -827,20 +833,29 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
             }
             fence_async_smem();
             tc_fence_before();
-            mbar_arrive(vn_ready);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(vn_ready);
             ok = __all_sync(0xffffffffu, ok && mbar_wait(upd_done, cp));
             tc_fence_after();
-            // o rows of this chunk: column v into a [64 t][128 v] staging tile (the v_new
-            // tile is free once the update MMAs are done), then 16-byte row stores
+            // o rows of this chunk into the v_new tile (free: the update MMAs have read it) right
+            // away -- the next chunk's first MMAs rewrite these TMEM columns -- then the next
+            // chunk's state pass (it gates those MMAs); the o rows leave as 16-byte row segments
+            // while the MMAs run
             const int rows = min(C, len - c * C);
             bf16* ost = reinterpret_cast<bf16*>(vn_tile);
+            if (ok) {  // warp-uniform
 #pragma unroll
-            for (int half = 0; ok && half < 2; half++) {
-                float ov[32];
-                tmem_ld32(lane_addr + 64 + half * 32, ov);
-                tmem_ld_wait();
+                for (int half = 0; half < 2; half++) {
+                    float ov[32];
+                    tmem_ld32(lane_addr + 64 + half * 32, ov);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 32; i++) ost[(half * 32 + i) * V + vcol] = to_bf16(ov[i]);
+                    for (int i = 0; i < 32; i++) ost[(half * 32 + i) * V + vcol] = to_bf16(ov[i]);
+                }
+            }
+            if (ok && c + 1 < NC) {
+                load_u(c + 1);
+                state_pass(c + 1);
             }
             if (bar_any(1, 128, !ok)) {
                 atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
@@ -854,7 +869,7 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
                     st8(o + ((size_t)(start + c * C + t) * H + h) * V + v8,
                         *reinterpret_cast<const Pack8*>(ost + t * V + v8));
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the tile takes the next v_new
         }
         if (s_out) {
             float* so = s_out + (long)seq * (long)H * K * V + (size_t)h * K * V;
