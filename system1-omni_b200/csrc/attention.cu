@@ -37,6 +37,8 @@ __global__ void prep_kernel(const bf16* __restrict__ qg, const bf16* __restrict_
                             const bf16* __restrict__ qw, const bf16* __restrict__ kw, const bf16* __restrict__ cosb,
                             const bf16* __restrict__ sinb, bf16* __restrict__ q, bf16* __restrict__ gate,
                             bf16* __restrict__ k, int T, int Hq, int Hk, int half, float eps, bool cs_vec) {
+    grid_dep_wait();
+    grid_dep_launch();
     // 32-bit unit indices (T * heads < 2^31 is checked on the host)
     const int unit0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * PREP_UNITS;
     const int lane = threadIdx.x & 31;
@@ -442,6 +444,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
     const int seq = info[0], qb = info[1];
     const int h = blockIdx.x, hk = h / (a.Hq / a.Hk);
     const int off = tab.offset[seq];
@@ -722,8 +726,7 @@ int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pk, a.pk, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pv, a.pv, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (e) return e;
-    flash_tc<<<dim3(a.Hq, blocks), THREADS, SMEM, st>>>(maps, a, tab);
-    return cudaGetLastError();
+    return launch_pdl(flash_tc, dim3(a.Hq, blocks), dim3(THREADS), SMEM, st, maps, a, tab);
 }
 
 }  // namespace tca
@@ -801,12 +804,11 @@ int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const 
         !aligned16(k))
         return cudaErrorInvalidValue;
     constexpr int WPB = 8;
-    attn::prep_kernel<<<(unsigned)((warps + WPB - 1) / WPB), WPB * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const bf16*>(qg), static_cast<const bf16*>(kr), ld, static_cast<const bf16*>(qw),
-        static_cast<const bf16*>(kw), static_cast<const bf16*>(cos), static_cast<const bf16*>(sin),
-        static_cast<bf16*>(q), static_cast<bf16*>(gate), static_cast<bf16*>(k), T, Hq, Hk, half, eps,
-        aligned16(cos) && aligned16(sin));
-    return cudaGetLastError();
+    return launch_pdl(attn::prep_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
+                      static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg), static_cast<const bf16*>(kr),
+                      ld, static_cast<const bf16*>(qw), static_cast<const bf16*>(kw), static_cast<const bf16*>(cos),
+                      static_cast<const bf16*>(sin), static_cast<bf16*>(q), static_cast<bf16*>(gate),
+                      static_cast<bf16*>(k), T, Hq, Hk, half, eps, aligned16(cos) && aligned16(sin));
 }
 
 int cs1_attention(const void* q, const void* k, const void* v, int ldv, void* out, int T, int Hq, int Hk, int Dh,

@@ -43,6 +43,8 @@ constexpr int THREADS = 256;
 
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const Pack8* __restrict__ table,
                              Pack8* __restrict__ out, int packs, int T) {
+    grid_dep_wait();
+    grid_dep_launch();
     for (int t = blockIdx.x; t < T; t += gridDim.x) {
         const size_t id = (size_t)ids[t];
         for (int i = threadIdx.x; i < packs; i += blockDim.x) out[(size_t)t * packs + i] = table[id * packs + i];
@@ -58,6 +60,8 @@ constexpr int CONV_ROWS = 64;
 __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
                                 bf16* __restrict__ v, int key_packs, int value_packs, SeqTable tab) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     const int packs = 2 * key_packs + value_packs;
     if (c >= packs) return;
@@ -179,6 +183,8 @@ __global__ void conv_scalar_kernel(const bf16* __restrict__ qkv, const bf16* __r
 __global__ void gates_kernel(const bf16* __restrict__ b, const bf16* __restrict__ a, int ld,
                              const bf16* __restrict__ A_log, const bf16* __restrict__ dt_bias,
                              bf16* __restrict__ beta, float* __restrict__ g, long n, int H) {
+    grid_dep_wait();
+    grid_dep_launch();
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
         const int h = (int)(i % H);
         const size_t src = (size_t)(i / H) * ld + h;
@@ -252,9 +258,10 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
                      aligned16(q) && aligned16(k) && aligned16(v) && (!history || aligned16(history));
     if (vec) {
         const int packs = (2 * key_dim + value_dim) / 8;
-        conv_vec_kernel<<<dim3((packs + 127) / 128, (T + CONV_ROWS - 1) / CONV_ROWS), 128, 0, st>>>(
-            static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld, static_cast<const bf16*>(w),
-            static_cast<bf16*>(q), static_cast<bf16*>(k), static_cast<bf16*>(v), key_dim / 8, value_dim / 8, tab);
+        return launch_pdl(conv_vec_kernel, dim3((packs + 127) / 128, (T + CONV_ROWS - 1) / CONV_ROWS), dim3(128), 0,
+                          st, static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
+                          static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
+                          static_cast<bf16*>(v), key_dim / 8, value_dim / 8, tab);
     } else {
         const int ch = 2 * key_dim + value_dim;
         conv_scalar_kernel<<<dim3((ch + 127) / 128, rows), 128, 0, st>>>(
@@ -274,9 +281,8 @@ extern "C" int cs1_embed(const int32_t* ids, const void* table, void* out, int T
     if (T == 0) return cudaSuccess;
     if (!aligned16(table) || !aligned16(out)) return cudaErrorInvalidValue;
     const int grid = T < 65535 ? T : 65535;
-    embed_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(ids, static_cast<const Pack8*>(table),
-                                                                      static_cast<Pack8*>(out), D / 8, T);
-    return cudaGetLastError();
+    return launch_pdl(embed_kernel, dim3(grid), dim3(128), 0, static_cast<cudaStream_t>(stream), ids,
+                      static_cast<const Pack8*>(table), static_cast<Pack8*>(out), D / 8, T);
 }
 
 extern "C" int cs1_gdn_conv(const void* qkv, int ld, const void* w, void* q, void* k, void* v, int T, int key_dim,
@@ -320,10 +326,9 @@ extern "C" int cs1_gdn_gates(const void* b, const void* a, int ld, const void* A
     if (T < 0 || H < 0 || ld < H) return cudaErrorInvalidValue;
     const long n = (long)T * H;
     if (n == 0) return cudaSuccess;
-    gates_kernel<<<grid_for(n), THREADS, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const bf16*>(b), static_cast<const bf16*>(a), ld, static_cast<const bf16*>(A_log),
-        static_cast<const bf16*>(dt_bias), static_cast<bf16*>(beta), g, n, H);
-    return cudaGetLastError();
+    return launch_pdl(gates_kernel, dim3(grid_for(n)), dim3(THREADS), 0, static_cast<cudaStream_t>(stream),
+                      static_cast<const bf16*>(b), static_cast<const bf16*>(a), ld, static_cast<const bf16*>(A_log),
+                      static_cast<const bf16*>(dt_bias), static_cast<bf16*>(beta), g, n, H);
 }
 
 extern "C" int cs1_sigmoid_gate(void* x, const void* gate, size_t n, void* stream) {

@@ -329,6 +329,8 @@ __global__ void __launch_bounds__(TP_THREADS, 2)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + TP_BAR + 16);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
+    grid_dep_wait();
+    grid_dep_launch();
     // global loads first: g and beta of the chunk, this warp's 8 rows of k and q
     float gval = 0.f, bval = 0.f;
     if (tid < n) {
@@ -687,6 +689,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 4) {
         if (lane == 0) {
@@ -915,10 +919,9 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     CUtensorMap vmap;
     if (int e = host::make_map_3d_bf16(&vmap, v, V, H, (uint64_t)seqs.offset[seqs.count], V, (uint64_t)H * V, 64, 64))
         return e;
-    gdn_prep_tc<<<dim3((unsigned)slots, H), TP_THREADS, TP_SMEM, st>>>(
-        vmap, static_cast<const bf16*>(q), static_cast<const bf16*>(k), g, static_cast<const bf16*>(beta), ws, tab,
-        H, HK, scale);
-    cudaError_t e = cudaGetLastError();
+    cudaError_t e = launch_pdl(gdn_prep_tc, dim3((unsigned)slots, H), dim3(TP_THREADS), TP_SMEM, st, vmap,
+                               static_cast<const bf16*>(q), static_cast<const bf16*>(k), g,
+                               static_cast<const bf16*>(beta), ws, tab, H, HK, scale);
     if (e != cudaSuccess) return e;
     ScanMaps maps;
     const uint64_t rows64 = (uint64_t)H * slots * C, rows128 = (uint64_t)H * slots * K;
@@ -931,10 +934,9 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     if (!r) r = host::make_map_2d(&maps.kdt, ws.kdt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, K, K, 64, 64,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (r) return r;
-    gdn_scan<<<dim3(H, seqs.count), SCAN_THREADS, SCAN_SMEM, st>>>(maps, ws, tab, static_cast<bf16*>(o), H,
-                                                                   static_cast<const float*>(s_in), s_in_stride,
-                                                                   static_cast<float*>(s_out));
-    return cudaGetLastError();
+    return launch_pdl(gdn_scan, dim3(H, seqs.count), dim3(SCAN_THREADS), SCAN_SMEM, st, maps, ws, tab,
+                      static_cast<bf16*>(o), H, static_cast<const float*>(s_in), s_in_stride,
+                      static_cast<float*>(s_out));
 }
 
 size_t workspace_bytes_for(long slots, int H, bool f32) { return (size_t)Layout(slots, H, f32).total + 1024; }

@@ -166,6 +166,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -366,6 +368,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     cluster_sync();  // both CTAs' barriers initialised before any remote arrive or TMA completion
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -593,6 +597,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (lane == 0) {
@@ -817,8 +823,7 @@ int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int
     p.group = h->group ? h->group : GROUP_M;
     const int tiles = p.tiles_m * p.tiles_n;
     const int grid = std::min(tiles, h->sms);
-    gemm_kernel<BN, EPI><<<grid, THREADS, C::SMEM, st>>>(ma, mb, p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_kernel<BN, EPI>, dim3(grid), dim3(THREADS), C::SMEM, st, ma, mb, p);
 }
 
 template <int EPI>
@@ -844,8 +849,7 @@ int launch_pair(const Handle* h, const void* x, const void* w, void* y, int M, i
     p.group = h->group ? h->group : P_GROUP_M;
     const int tiles = p.tiles_m * p.tiles_n;
     const int grid = 2 * std::min(tiles, h->sms / 2);
-    gemm_pair_kernel<EPI><<<grid, THREADS, P_SMEM, st>>>(ma, mb, p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_pair_kernel<EPI>, dim3(grid), dim3(THREADS), P_SMEM, st, ma, mb, p);
 }
 
 // Whole waves of tiles stay whole; the tiles of a last partial wave are split along x
@@ -889,8 +893,7 @@ int launch_swap(const Handle* h, const void* x, const void* w, void* y, int M, i
     const int tiles = p.tiles_w * p.tiles_t;
     swap_split(tiles, h->sms, nt, p.full, p.split, p.sub);
     p.items = p.full + (tiles - p.full) * p.split;
-    gemm_swap_kernel<EPI><<<std::min(p.items, h->sms), THREADS, S_SMEM, st>>>(mw, mx, p);
-    return cudaGetLastError();
+    return launch_pdl(gemm_swap_kernel<EPI>, dim3(std::min(p.items, h->sms)), dim3(THREADS), S_SMEM, st, mw, mx, p);
 }
 
 // Best token tile of the swapped kernel and its estimated time in the units of the

@@ -15,6 +15,8 @@ namespace {
 __global__ void head_kernel(const bf16* __restrict__ hidden, int ldh, const int32_t* __restrict__ rows, int n,
                             const float* __restrict__ W, const float* __restrict__ bias, int L, int D,
                             float* __restrict__ logits) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (w >= n * L) return;
     const int i = w / L, l = w % L;
@@ -37,7 +39,6 @@ extern "C" int cs1_head_score(const void* hidden, int ldh, const int32_t* rows, 
     if (!hidden || !rows || !W || !bias || !logits || n < 0 || L <= 0 || D <= 0 || ldh < D) return cudaErrorInvalidValue;
     if (n == 0) return cudaSuccess;
     const long warps = (long)n * L;
-    head_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        static_cast<const bf16*>(hidden), ldh, rows, n, W, bias, L, D, logits);
-    return cudaGetLastError();
+    return launch_pdl(head_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                      static_cast<const bf16*>(hidden), ldh, rows, n, W, bias, L, D, logits);
 }

@@ -74,6 +74,8 @@ __global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restric
                                                                  const bf16* __restrict__ x, const bf16* __restrict__ w,
                                                                  bf16* __restrict__ out, int rows, int D, float eps) {
     __shared__ Pack8 wsm[32 * PPL];
+    grid_dep_wait();
+    grid_dep_launch();
     const int packs = D >> 3, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < packs; i += blockDim.x) wsm[i] = ld8(w + (size_t)i * 8);
     __syncthreads();
@@ -214,6 +216,8 @@ __global__ void gated_kernel(const bf16* __restrict__ x, const bf16* __restrict_
 constexpr int G_ROWS = 8;
 __global__ void gated16_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
                                const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
+    grid_dep_wait();
+    grid_dep_launch();
     const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
     const int row0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * G_ROWS;
     if (row0 >= rows) return;
@@ -286,7 +290,8 @@ extern "C" int cs1_rms_norm(const void* x, const void* w, void* out, int rows, i
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
     if (vec_ok(D, x, w, out, out) && D <= 256 * PPL)
-        rms_warp_kernel<false><<<rms_warp_grid(rows), RW_WARPS * 32, 0, st>>>(nullptr, nullptr, X, Wt, O, rows, D, eps);
+        return launch_pdl(rms_warp_kernel<false>, dim3(rms_warp_grid(rows)), dim3(RW_WARPS * 32), 0, st,
+                          static_cast<bf16*>(nullptr), static_cast<const bf16*>(nullptr), X, Wt, O, rows, D, eps);
     else if (vec_ok(D, x, w, out, out))
         rms_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
     else
@@ -304,7 +309,8 @@ extern "C" int cs1_add_rms_norm(void* residual, const void* delta, const void* w
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
     if (vec_ok(D, residual, delta, w, out) && D <= 256 * PPL)
-        rms_warp_kernel<true><<<rms_warp_grid(rows), RW_WARPS * 32, 0, st>>>(R, Dl, nullptr, Wt, O, rows, D, eps);
+        return launch_pdl(rms_warp_kernel<true>, dim3(rms_warp_grid(rows)), dim3(RW_WARPS * 32), 0, st, R, Dl,
+                          static_cast<const bf16*>(nullptr), Wt, O, rows, D, eps);
     else if (vec_ok(D, residual, delta, w, out))
         rms_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
     else
@@ -324,8 +330,9 @@ extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const v
     const bool vec = ldz % 4 == 0 && (bits & 7) == 0;
     if (ldz % 8 == 0 && (bits & 15) == 0) {
         const int per_block = WARPS * G_ROWS;
-        gated16_kernel<<<(rows + per_block - 1) / per_block, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
-            static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
+        return launch_pdl(gated16_kernel, dim3((rows + per_block - 1) / per_block), dim3(WARPS * 32), 0, st,
+                          static_cast<const bf16*>(x), static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w),
+                          static_cast<bf16*>(out), rows, H, eps);
     } else if (vec)
         gated_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
             static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);

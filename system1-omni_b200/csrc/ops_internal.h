@@ -5,6 +5,10 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#ifdef __CUDACC__
+#include <cuda_runtime.h>
+#endif
+
 #include "../../include/qwen3_5_ops.h"
 
 namespace s1 {
@@ -24,6 +28,39 @@ struct SeqTable {
 bool make_table(SeqTable& t, const size_t* lengths, size_t count);
 
 #ifdef __CUDACC__
+// Programmatic dependent launch. The forward's kernels are launched with programmatic
+// stream serialisation, so a kernel's CTAs may start while the previous kernel's last
+// CTAs still run: everything before grid_dep_wait() (barrier set-up, tensor-memory
+// allocation, descriptor prefetch) overlaps that tail, and nothing before it touches
+// global memory. grid_dep_wait() returns once the previous kernel has completed and its
+// writes are visible; grid_dep_launch() lets the next kernel's CTAs be scheduled.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();  // S1_PDL=0 turns the attribute off (plain stream order)
+
+// Launch with the programmatic-serialisation attribute (see grid_dep_wait); the kernel
+// must call grid_dep_wait() before its first global-memory access. The attribute is set
+// for eager launches only: inside a captured CUDA graph it measured slower (the graph
+// already removes the launch gaps it hides), so captured launches keep plain order.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const bool capturing = cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() && !capturing ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Sequence index of row `row` (binary search over the offsets).
 __device__ __forceinline__ int seq_of(const SeqTable& t, int row) {
     int lo = 0, hi = t.count - 1;

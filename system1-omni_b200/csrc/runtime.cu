@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <mutex>
 
 #include "ops_internal.h"
@@ -54,6 +55,18 @@ int make_map_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : cudaErrorInvalidValue;
 }
+
+}  // namespace host
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("S1_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+namespace host {
 
 int num_sms() {
     static int cache[64] = {0};
