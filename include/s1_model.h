@@ -93,6 +93,30 @@ void* s1_model_stream(void* model);
 long s1_model_last_launches(void* model);
 // Fused projections (cs1_gemm_residual / cs1_gemm_swiglu) in use: 1 yes, 0 no.
 int s1_model_fused(void* model);
+// The model's configuration (layer_types points into the model; valid while it lives).
+int s1_model_get_config(void* model, s1_config* out);
+
+// ---- checkpoints (src/models/qwen3_5/native/src/model.rs:96-226, 267-397) ----
+// A Hugging Face Qwen3.5 config.json (or its text_config) as an s1_config; layer_types
+// receives the per-layer kinds (capacity max_layers). labels is set to 1 (the Open-Jev
+// scalar head); change it for another head. Returns 0, or -1 (s1_checkpoint_error()).
+int s1_config_from_hf(const char* config_json, s1_config* out, int* layer_types, int max_layers);
+// Load every language-model weight of a checkpoint folder (model.safetensors, or the
+// shards of model.safetensors.index.json; tensors under "model.language_model.",
+// "model." or no prefix) into the model; fp32 A_log and GDN-norm weights are rounded
+// once to bf16, any other non-bf16 tensor is an error, and so is a weight of the model's
+// configuration that the folder lacks or a tensor whose shape differs from the model's.
+int s1_model_load_checkpoint(void* model, const char* dir);
+// The scorer head of an export manifest (open_jev_export.json: head_weight, head_bias;
+// a flat list for one label or [labels][hidden]).
+int s1_model_load_head(void* model, const char* manifest_json, int labels, int hidden);
+// The tensors a checkpoint folder maps to ("<name> <hf name> <dtype> <shape>" lines; no
+// GPU needed). Returns the bytes of the full text, or -1.
+long s1_checkpoint_list(const char* dir, char* out, size_t cap);
+// The checks s1_model_load_checkpoint makes before reading any payload (tensor set,
+// shapes, dtypes, payload sizes) against a configuration, without a model or a GPU.
+int s1_checkpoint_check(const char* dir, const s1_config* cfg);
+const char* s1_checkpoint_error(void);
 
 // ---- packing policy (host integer logic, no GPU) ----
 // Launch ranges of candidates (src/models/open_jev/native/src/batching.rs:9-25): writes

@@ -1045,6 +1045,13 @@ __attribute__((visibility("default"))) int s1_model_fused(void* mp) {
     return m ? (m->fused ? 1 : 0) : -1;
 }
 
+__attribute__((visibility("default"))) int s1_model_get_config(void* mp, s1_config* out) {
+    auto* m = static_cast<Model*>(mp);
+    if (!m || !out) return -1;
+    *out = m->cfg;
+    return 0;
+}
+
 }  // extern "C"
 
 // ===================================================== packing policy (host) ====

@@ -109,6 +109,15 @@ def _lib():
     lib.s1_model_last_launches.restype = ctypes.c_long
     lib.s1_model_last_launches.argtypes = [P]
     lib.s1_model_fused.argtypes = [P]
+    lib.s1_config_from_hf.argtypes = [ctypes.c_char_p, ctypes.POINTER(_Cfg), P, I]
+    lib.s1_model_load_checkpoint.argtypes = [P, ctypes.c_char_p]
+    lib.s1_model_load_head.argtypes = [P, ctypes.c_char_p, I, I]
+    lib.s1_checkpoint_list.restype = ctypes.c_long
+    lib.s1_checkpoint_list.argtypes = [ctypes.c_char_p, P, Z]
+    lib.s1_checkpoint_check.argtypes = [ctypes.c_char_p, ctypes.POINTER(_Cfg)]
+    lib.s1_model_get_config.argtypes = [P, ctypes.POINTER(_Cfg)]
+    lib.s1_checkpoint_error.restype = ctypes.c_char_p
+    lib.s1_checkpoint_error.argtypes = []
     lib.s1_pack_ranges.argtypes = [P, Z, Z, Z, P]
     lib.s1_shared_prefix.restype = Z
     lib.s1_shared_prefix.argtypes = [P, P, Z, Z]
@@ -148,6 +157,47 @@ def shared_prefix(inputs, minimum=2049):
     ptrs = (ctypes.c_void_p * max(1, len(arrays)))(*[a.ctypes.data for a in arrays])
     lens = np.asarray([len(a) for a in arrays], dtype=np.uintp)
     return int(lib.s1_shared_prefix(ctypes.cast(ptrs, P), lens.ctypes.data, len(arrays), minimum))
+
+
+def config_from_hf(config_json, labels=1, name="checkpoint"):
+    """The Config of a Hugging Face Qwen3.5 config.json (or its text_config), read by the
+    C++ host (model.rs:96-226 of the reference). labels: rows of the scorer head."""
+    lib = _get()
+    types = (I * 4096)()
+    c = _Cfg()
+    if lib.s1_config_from_hf(str(config_json).encode(), ctypes.byref(c), ctypes.cast(types, P), 4096) != 0:
+        raise ValueError("config.json: " + lib.s1_checkpoint_error().decode())
+    return Config(c.hidden, c.intermediate, ["gdn" if types[i] == 0 else "attn" for i in range(c.n_layers)],
+                  c.lin_k_heads, c.lin_v_heads, c.heads, c.kv_heads, c.vocab, labels=labels, lin_k_dim=c.lin_k_dim,
+                  lin_v_dim=c.lin_v_dim, head_dim=c.head_dim, rotary_half=c.rotary_half, theta=c.theta, eps=c.eps,
+                  name=name)
+
+
+def checkpoint_list(folder):
+    """[(name, hf_name, dtype, shape)] of the language-model tensors of a checkpoint folder."""
+    lib = _get()
+    n = lib.s1_checkpoint_list(str(folder).encode(), None, 0)
+    if n < 0:
+        raise ValueError("checkpoint: " + lib.s1_checkpoint_error().decode())
+    buf = ctypes.create_string_buffer(n)
+    lib.s1_checkpoint_list(str(folder).encode(), buf, n)
+    out = []
+    for line in buf.value.decode().splitlines():
+        name, hf, dtype, shape = line.split(" ")
+        out.append((name, hf, dtype, tuple(int(x) for x in shape.split("x"))))
+    return out
+
+
+def checkpoint_check(folder, cfg):
+    """Check a checkpoint folder against a Config (tensor set, shapes, dtypes, sizes) on
+    the host, as Model.load_checkpoint does before it reads any payload. Raises ValueError."""
+    lib = _get()
+    types = (I * len(cfg.layer_types))(*[0 if t == "gdn" else 1 for t in cfg.layer_types])
+    c = _Cfg(cfg.hidden, cfg.intermediate, len(cfg.layer_types), types, cfg.lin_k_heads, cfg.lin_v_heads,
+             cfg.lin_k_dim, cfg.lin_v_dim, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rotary_half,
+             float(cfg.theta), float(cfg.eps), cfg.vocab, cfg.labels)
+    if lib.s1_checkpoint_check(str(folder).encode(), ctypes.byref(c)) != 0:
+        raise ValueError("checkpoint: " + lib.s1_checkpoint_error().decode())
 
 
 class Model:
@@ -202,6 +252,16 @@ class Model:
     def load(self, weights):
         for name, arr in weights.items():
             self.set_weight(name, arr)
+
+    def load_checkpoint(self, folder):
+        """Every language-model weight of a Hugging Face Qwen3.5 checkpoint folder."""
+        if self._lib.s1_model_load_checkpoint(self._h, str(folder).encode()) != 0:
+            raise RuntimeError("load_checkpoint: " + self._lib.s1_checkpoint_error().decode())
+
+    def load_head(self, manifest_json):
+        """The scorer head of an export manifest (open_jev_export.json)."""
+        if self._lib.s1_model_load_head(self._h, str(manifest_json).encode(), self.cfg.labels, self.cfg.hidden) != 0:
+            raise RuntimeError("load_head: " + self._lib.s1_checkpoint_error().decode())
 
     def init_random(self, seed=0, std=0.02):
         self._check(self._lib.s1_model_init_random(self._h, seed, std), "init_random")
