@@ -757,6 +757,273 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair swapped-operand variant: a cluster of two CTAs computes 256 rows of w (the
+// MMA's M side, 128 per CTA) x N rows of x (N a multiple of 16, at most NT <= 256; each
+// CTA loads N/2 of them, cta_group::2 splits the MMA's N side in halves). Per SM and
+// MMA cycle it reads 8192 / N + 32 bytes of operands from shared memory, against
+// 8192 / N + 64 for the single-CTA swapped kernel, and its tile of x is twice as wide.
+// Work items, the split of the last partial wave and the epilogue follow the swapped
+// kernel. SwiGLU: CTA r of a pair takes, from the 256-row block (gate 128 | up 128) of
+// w, gate rows 64r .. 64r+63 into its A rows 0..63 and the up rows of the same output
+// columns into A rows 64..127, so TMEM lanes l and l + 64 hold gate and up of one output
+// column; the epilogue warps holding them (q and q + 2) pass rounded values through
+// shared memory, each computing the outputs of every other 32-row chunk of x.
+constexpr int SP_A_BYTES = BM * BK * 2;  // 128 rows of w
+constexpr int SP_B_MAX = 128 * BK * 2;   // up to 128 rows of x (N <= 256)
+constexpr int SP_STAGE_BYTES = SP_A_BYTES + SP_B_MAX;
+template <int EPI>
+struct SPCfg {
+    static constexpr bool SW = EPI == EPI_SWIGLU;
+    static constexpr int STAGES = SW ? 5 : 6;
+    static constexpr int STG_OFFSET = STAGES * SP_STAGE_BYTES;  // 4 warps x [32][32] bf16 staging
+    // SwiGLU exchange: per warp up to 4 chunks x [32 rows of x][32 lanes] bf16 for its partner
+    static constexpr int XCH_OFFSET = STG_OFFSET + 4 * 2048;
+    static constexpr int BAR_OFFSET = XCH_OFFSET + (SW ? 4 * 8192 : 0);
+    static constexpr int SMEM = BAR_OFFSET + 256 + 1024;
+};
+
+template <int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_swap_pair_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                          SwapParams p) {
+    using C = SPCfg<EPI>;
+    constexpr bool SW = C::SW;
+    constexpr int SP_STAGES = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* smem = smem_raw + (base - raw);
+    const uint32_t bars = base + C::BAR_OFFSET;
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (SP_STAGES + s); };
+    auto tfull = [&](int a) { return bars + 8u * (2 * SP_STAGES + a); };
+    auto tempty = [&](int a) { return bars + 8u * (2 * SP_STAGES + 2 + a); };
+    const uint32_t drain = bars + 8u * (2 * SP_STAGES + 4);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BAR_OFFSET + 8 * (2 * SP_STAGES + 5));
+
+    const uint32_t rank = cluster_rank();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int num_items = p.items;
+    const int KB = (p.K + BK - 1) / BK;
+    const int cid = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SP_STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull(a), 1);
+            mbar_init(tempty(a), 8);
+        }
+        mbar_init(drain, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&map_w);
+        tma_prefetch_desc(&map_x);
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(smem_u32(tmem_slot), 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers initialised before any remote arrive or TMA completion
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
+
+    if (warp == 0) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            long issued = 0;
+            bool ok = true;
+            const uint32_t tx = 2u * (SP_A_BYTES + (uint32_t)(p.nt / 2) * BK * 2);
+            for (int t = cid; t < num_items && ok; t += nclusters) {
+                int wt, x0, rows;
+                swap_item(p, t, wt, x0, rows);
+                if (rows <= 0) continue;
+                const int n_half = ((rows + 15) & ~15) / 2;
+                // rows of w: SwiGLU gate 64r.. and up 128+64r.. of block wt; else 128r.. of tile wt
+                const int w0 = SW ? wt * 256 + 64 * (int)rank : wt * 256 + 128 * (int)rank;
+                const int w1 = SW ? w0 + 128 : w0 + 64;
+                for (int kb = 0; kb < KB; kb++) {
+                    if (!mbar_wait(empty(s), ph ^ 1)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = base + s * SP_STAGE_BYTES;
+                    if (leader) mbar_expect_tx(full(s), tx);
+                    tma_load_2d_pair(dst, &map_w, full(s), kb * BK, w0);
+                    tma_load_2d_pair(dst + SP_A_BYTES / 2, &map_w, full(s), kb * BK, w1);
+                    tma_load_2d_pair(dst + SP_A_BYTES, &map_x, full(s), kb * BK, x0 + (int)rank * n_half);
+                    issued++;
+                    if (++s == SP_STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            if (leader) {
+                // every load of both CTAs has landed (all complete on the leader's barriers)
+                const long pending = issued < SP_STAGES ? issued : SP_STAGES;
+                for (long i = 0; i < pending; i++) {
+                    if (--s < 0) {
+                        s = SP_STAGES - 1;
+                        ph ^= 1;
+                    }
+                    (void)mbar_wait(full(s), ph);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            if (leader) {
+                int s = 0, acc = 0;
+                uint32_t ph = 0, acc_ph = 0;
+                bool ok = true;
+                for (int t = cid; t < num_items && ok; t += nclusters) {
+                    int wt, x0, rows;
+                    swap_item(p, t, wt, x0, rows);
+                    if (rows <= 0) continue;
+                    const uint32_t id = idesc(256, (rows + 15) & ~15, AB_BF16);
+                    if (!mbar_wait(tempty(acc), acc_ph ^ 1)) {
+                        atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem + acc * 256;
+                    for (int kb = 0; kb < KB; kb++) {
+                        if (!mbar_wait(full(s), ph)) {
+                            atomicOr(&g_fault_word, FAULT_WAIT_MMA);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = base + s * SP_STAGE_BYTES;
+                        const uint64_t ad = desc_sw128(a_addr), bd = desc_sw128(a_addr + SP_A_BYTES);
+#pragma unroll
+                        for (int k = 0; k < BK / 16; k++) mma_bf16_pair(d, ad + 2 * k, bd + 2 * k, id, (kb | k) != 0);
+                        mma_commit_pair(empty(s), 3);
+                        if (++s == SP_STAGES) {
+                            s = 0;
+                            ph ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    mma_commit_pair(tfull(acc), 3);
+                    if (++acc == 2) {
+                        acc = 0;
+                        acc_ph ^= 1;
+                    }
+                }
+                mma_commit_pair(drain, 3);
+            }
+            // both CTAs: the leader's MMAs (which write this CTA's tensor memory) are done
+            (void)mbar_wait(drain, 0);
+        }
+    } else {
+        const int q = warp & 3;
+        const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+        bf16* stg = reinterpret_cast<bf16*>(smem + C::STG_OFFSET + q * 2048);  // [32 rows of x][32 columns]
+        // SwiGLU partners: warps q and q ^ 2 (gate lanes 32q.., up lanes 64 + 32q..)
+        bf16* xsend = reinterpret_cast<bf16*>(smem + C::XCH_OFFSET + q * 8192);
+        const bf16* xrecv = reinterpret_cast<const bf16*>(smem + C::XCH_OFFSET + (q ^ 2) * 8192);
+        const uint32_t leader_tempty0 = map_to_rank(tempty(0), 0), leader_tempty1 = map_to_rank(tempty(1), 0);
+        const int out_n = SW ? p.N / 2 : p.N;
+        int acc = 0;
+        uint32_t acc_ph = 0;
+        for (int t = cid; t < num_items; t += nclusters) {
+            int wt, row0, rows;
+            swap_item(p, t, wt, row0, rows);
+            if (rows <= 0) continue;
+            bool bad = !__all_sync(0xffffffffu, mbar_wait(tfull(acc), acc_ph));
+            if (SW) bad = bar_any(1 + (q & 1), 64, bad);  // the exchange partners leave together
+            if (bad) {
+                if (lane == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            // this warp's 32 output columns
+            const int col0 = SW ? wt * 128 + 64 * (int)rank + (q & 1) * 32 : wt * 256 + 128 * (int)rank + q * 32;
+            const uint32_t tacc = lane_addr + acc * 256;
+            const int chunks = (rows + 31) / 32;
+            // SwiGLU: the gate warp finishes the even chunks of 32 rows of x, the up warp the
+            // odd ones; each first hands its partner the bf16-rounded values of the others
+            const int own = SW ? (q < 2 ? 0 : 1) : 0, step = SW ? 2 : 1;
+            if constexpr (SW) {
+#pragma unroll 1
+                for (int c = 1 - own; c < chunks; c += 2) {
+                    float v[32];
+                    tmem_ld32(tacc + c * 32, v);
+                    tmem_ld_wait();
+                    bf16* dst = xsend + (c >> 1) * 1024;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) dst[i * 32 + lane] = to_bf16(v[i]);
+                }
+                named_bar_sync(1 + (q & 1), 64);
+            }
+#pragma unroll 1
+            for (int c = own; c < chunks; c += step) {
+                float v[32];
+                tmem_ld32(tacc + c * 32, v);
+                tmem_ld_wait();
+                if constexpr (SW) {
+                    const bf16* src = xrecv + (c >> 1) * 1024;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const float o = f32(src[i * 32 + lane]);
+                        v[i] = q < 2 ? rbf(silu(rbf(v[i]))) * o : rbf(silu(o)) * rbf(v[i]);
+                    }
+                }
+                // STORE: bf16(acc); RESIDUAL: bf16(acc), added to the residual below; SwiGLU: the output
+#pragma unroll
+                for (int i = 0; i < 32; i++) stg[i * 32 + lane] = to_bf16(v[i]);
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int ch = lane + 32 * j, i = ch >> 2, part = ch & 3;
+                    const int r = c * 32 + i, row = row0 + r, col = col0 + part * 8;
+                    if (r < rows && col + 8 <= out_n) {  // rows of this item only (r < rows implies row < M)
+                        const Pack8 val = *reinterpret_cast<const Pack8*>(stg + i * 32 + part * 8);
+                        bf16* dst = p.y + (size_t)row * p.ldy + col;
+                        if constexpr (EPI == EPI_RESIDUAL) {
+                            float r8[8], a8[8];
+                            unpack8(ld8(dst), r8);
+                            unpack8(val, a8);
+#pragma unroll
+                            for (int e = 0; e < 8; e++) r8[e] += a8[e];
+                            st8(dst, pack8(r8));
+                        } else {
+                            st8(dst, val);
+                        }
+                    }
+                }
+                __syncwarp();
+            }
+            if constexpr (SW) named_bar_sync(1 + (q & 1), 64);  // partner done reading before the next item's writes
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc ? leader_tempty1 : leader_tempty0);
+            if (++acc == 2) {
+                acc = 0;
+                acc_ph ^= 1;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
 // Any shape: one thread per output, fp32 accumulation in K order. Used only when
 // a shape or pointer misses the tensor-map alignment rules.
 template <int EPI>
@@ -792,12 +1059,12 @@ struct Handle {
     bool pairs = true;  // CTA-pair kernels for large M (S1_GEMM_PAIRS=0 selects the single-CTA kernels)
     int group = 0;      // tile grouping (0: the kernels' defaults; S1_GEMM_GROUP overrides, for tuning)
     bool swap = true;   // swapped-operand kernel for few rows (S1_GEMM_SWAP=0 disables)
-    // Tuning override (S1_GEMM_KERNEL = pair | row256 | row128 | swap, S1_GEMM_NT = the
-    // swapped kernel's rows of x per tile): every call of the handle uses that kernel
+    // Tuning override (S1_GEMM_KERNEL = pair | row256 | row128 | swap | swap2, S1_GEMM_NT =
+    // the swapped kernels' rows of x per tile): every call of the handle uses that kernel
     // where the shape allows it. 0 = the wave model's choice.
     int force = 0, force_nt = 0;
 };
-enum Force : int { FORCE_NONE = 0, FORCE_PAIR, FORCE_ROW256, FORCE_ROW128, FORCE_SWAP };
+enum Force : int { FORCE_NONE = 0, FORCE_PAIR, FORCE_ROW256, FORCE_ROW128, FORCE_SWAP, FORCE_SWAP2 };
 
 template <int BN, int EPI>
 int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy,
@@ -896,11 +1163,41 @@ int launch_swap(const Handle* h, const void* x, const void* w, void* y, int M, i
     return launch_pdl(gemm_swap_kernel<EPI>, dim3(std::min(p.items, h->sms)), dim3(THREADS), S_SMEM, st, mw, mx, p);
 }
 
+template <int EPI>
+int launch_swap_pair(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int nt,
+                     cudaStream_t st) {
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(gemm_swap_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SPCfg<EPI>::SMEM);
+    if (configured != cudaSuccess) return configured;
+    CUtensorMap mw, mx;
+    int e = host::make_map_2d(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, K, K, 64, BK,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    e = host::make_map_2d(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, K, (uint32_t)(nt / 2), BK,
+                          CU_TENSOR_MAP_SWIZZLE_128B);
+    if (e) return e;
+    SwapParams p;
+    p.y = static_cast<bf16*>(y);
+    p.ldy = ldy;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.nt = nt;
+    p.tiles_w = EPI == EPI_SWIGLU ? N / 256 : (N + 255) / 256;
+    p.tiles_t = (M + nt - 1) / nt;
+    const int tiles = p.tiles_w * p.tiles_t, pairs = h->sms / 2;
+    swap_split(tiles, pairs, nt, p.full, p.split, p.sub);
+    p.items = p.full + (tiles - p.full) * p.split;
+    return launch_pdl(gemm_swap_pair_kernel<EPI>, dim3(2 * std::min(p.items, pairs)), dim3(THREADS), SPCfg<EPI>::SMEM, st,
+                      mw, mx, p);
+}
+
 // Best token tile of the swapped kernel and its estimated time in the units of the
 // kernel choice below (waves x per-tile time relative to a 256 x 256 CTA-pair tile).
 // A tile of 128 w rows x nt rows costs nt / 256 of a 128 x 256 single-CTA tile, scaled up
 // where its operand bytes per MMA cycle (8192 / nt + 64; SwiGLU 8192 / nt + 32) exceed
-// what the 128 x 256 tiles sustain (~100 B / cycle / SM).
+// what the 128 x 256 tiles sustain (~90 B / cycle / SM). Constants fitted to
+// `python -m s1omni.gemm_tune` sweeps of the 27B shapes.
 double swap_cost(int M, int N, int epi, int sms, int& best_nt) {
     const bool sw = epi == EPI_SWIGLU;
     const long tiles_w = sw ? N / 256 : (N + BM - 1) / BM;
@@ -913,8 +1210,32 @@ double swap_cost(int M, int N, int epi, int sms, int& best_nt) {
         const long whole = tiles / sms;  // whole waves; a partial one costs sub / nt of a wave
         const double waves = (double)whole + (tiles > whole * sms ? (double)sub / nt : 0.0);
         const double rate = 8192.0 / nt + (sw ? 32.0 : 64.0);
-        const double eff = rate > 100.0 ? rate / 100.0 : 1.0;
-        const double c = waves * 1.15 * (sw ? 2.0 : 1.0) * nt / 256.0 * eff;
+        const double eff = rate > 90.0 ? rate / 90.0 : 1.0;
+        const double c = waves * 1.2 * (sw ? 2.0 : 1.0) * nt / 256.0 * eff;
+        if (c < best) {
+            best = c;
+            best_nt = nt;
+        }
+    }
+    return best;
+}
+
+// The same for the CTA-pair swapped kernel: a pair tile of 256 w rows x nt rows of x is
+// nt / 256 of a 256 x 256 pair tile; operand bytes per MMA cycle and SM 8192 / nt + 32.
+double swap_pair_cost(int M, int N, int epi, int sms, int& best_nt) {
+    const long tiles_w = epi == EPI_SWIGLU ? N / 256 : (N + 255) / 256;
+    const int pairs = sms / 2;
+    double best = 1e30;
+    best_nt = 0;
+    for (int nt = 32; nt <= 256; nt += 16) {
+        const long tiles = tiles_w * ((M + nt - 1) / nt);
+        int full, split, sub;
+        swap_split((int)tiles, pairs, nt, full, split, sub);
+        const long whole = tiles / pairs;
+        const double waves = (double)whole + (tiles > whole * pairs ? (double)sub / nt : 0.0);
+        const double rate = 8192.0 / nt + 32.0;
+        const double eff = rate > 70.0 ? rate / 70.0 : 1.0;
+        const double c = waves * 1.15 * nt / 256.0 * eff;
         if (c < best) {
             best = c;
             best_nt = nt;
@@ -959,21 +1280,40 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
     const double c_pair = (double)((pair_tiles + slots / 2 - 1) / (slots / 2)) * 1.0;
     const double c_256 = (double)((t256 + slots - 1) / slots) * 1.15;
     const double c_128 = (double)((t128 + slots - 1) / slots) * 0.6;
-    int nt = 0;
+    int nt = 0, nt2 = 0;
     double c_swap = h->swap ? swap_cost(M, N, epi, (int)slots, nt) : 1e30;
+    double c_swap2 = h->swap && h->pairs ? swap_pair_cost(M, N, epi, (int)slots, nt2) : 1e30;
     double cp = c_pair, c2 = c_256, c1 = epi == EPI_SWIGLU ? 1e30 : c_128;
     if (h->force != FORCE_NONE) {  // tuning override: make the forced kernel the cheapest
         cp = h->force == FORCE_PAIR ? 0.0 : 1e30;
         c2 = h->force == FORCE_ROW256 ? 0.0 : 1e30;
         c1 = h->force == FORCE_ROW128 && epi != EPI_SWIGLU ? 0.0 : 1e30;
         c_swap = h->force == FORCE_SWAP ? 0.0 : 1e30;
+        c_swap2 = h->force == FORCE_SWAP2 ? 0.0 : 1e30;
         if (h->force == FORCE_SWAP) {
             const int cap = epi == EPI_SWIGLU ? 128 : 256;
+            nt = 0;
             if (h->force_nt >= 16 && h->force_nt <= cap && h->force_nt % 16 == 0) nt = h->force_nt;
             if (nt == 0) nt = 128;
         }
-        if (h->force == FORCE_PAIR && !h->pairs) cp = 1e30;
-        if (cp != 0.0 && c2 != 0.0 && c1 != 0.0 && c_swap != 0.0) c2 = 0.0;  // not applicable: 128 x 256
+        if (h->force == FORCE_SWAP2) {
+            nt2 = 0;
+            if (h->force_nt >= 32 && h->force_nt <= 256 && h->force_nt % 16 == 0) nt2 = h->force_nt;
+            if (nt2 == 0) nt2 = 256;
+        }
+        if ((h->force == FORCE_PAIR || h->force == FORCE_SWAP2) && !h->pairs) cp = c_swap2 = 1e30;
+        if (cp != 0.0 && c2 != 0.0 && c1 != 0.0 && c_swap != 0.0 && c_swap2 != 0.0)
+            c2 = 0.0;  // not applicable: 128 x 256
+    }
+    if (nt2 > 0 && c_swap2 < cp && c_swap2 < c2 && c_swap2 < c1 && c_swap2 <= c_swap) {
+        switch (epi) {
+            case EPI_SWIGLU:
+                return launch_swap_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, nt2, st);
+            case EPI_RESIDUAL:
+                return launch_swap_pair<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, nt2, st);
+            default:
+                return launch_swap_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, nt2, st);
+        }
     }
     if (nt > 0 && c_swap < cp && c_swap < c2 && c_swap < c1) {
         switch (epi) {
@@ -1033,7 +1373,8 @@ void* cs1_gemm_create(size_t workspace_bytes) {
     if (const char* f = getenv("S1_GEMM_KERNEL")) {
         const std::string k(f);
         h->force = k == "pair" ? gemm::FORCE_PAIR : k == "row256" ? gemm::FORCE_ROW256
-                 : k == "row128" ? gemm::FORCE_ROW128 : k == "swap" ? gemm::FORCE_SWAP : gemm::FORCE_NONE;
+                 : k == "row128" ? gemm::FORCE_ROW128 : k == "swap" ? gemm::FORCE_SWAP
+                 : k == "swap2" ? gemm::FORCE_SWAP2 : gemm::FORCE_NONE;
     }
     if (const char* nt = getenv("S1_GEMM_NT")) h->force_nt = atoi(nt);
     return h;

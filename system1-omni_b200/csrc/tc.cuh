@@ -115,6 +115,10 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Named barrier `id` over `n` threads (whole warps).
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 // Named barrier `id` over `n` threads that also returns whether any of them passed true.
 __device__ __forceinline__ bool bar_any(int id, int n, bool p) {
     uint32_t r;

@@ -3,7 +3,7 @@
     cd system1-omni_b200 && python -m s1omni.gemm_tune [--m 300,771,2048] [--reps 10]
 
 For each M and shape, one handle per kernel option (S1_GEMM_KERNEL = pair | row256 |
-row128 | swap with S1_GEMM_NT = 64..256, set before cs1_gemm_create) and the default
+row128 | swap | swap2 with S1_GEMM_NT = 64..256, set before cs1_gemm_create) and the default
 handle (the library's wave model); CUDA-event time per call after three warm-up calls.
 Prints one JSON line per (M, shape) with every option's milliseconds, the fastest
 option and the model's time. Used to calibrate the kernel choice.
@@ -31,6 +31,8 @@ def main():
     opts = [("model", {}), ("pair", {"S1_GEMM_KERNEL": "pair"}), ("row256", {"S1_GEMM_KERNEL": "row256"}),
             ("row128", {"S1_GEMM_KERNEL": "row128"})]
     opts += [(f"swap{nt}", {"S1_GEMM_KERNEL": "swap", "S1_GEMM_NT": str(nt)}) for nt in (64, 96, 128, 160, 192, 224, 256)]
+    opts += [(f"pswap{nt}", {"S1_GEMM_KERNEL": "swap2", "S1_GEMM_NT": str(nt)})
+             for nt in range(64, 257, 16)]
     for M in [int(x) for x in a.m.split(",")]:
         for epi, N, K in SHAPES:
             x = (torch.randn(M, K, device="cuda", generator=g) * 0.5).to(torch.bfloat16)

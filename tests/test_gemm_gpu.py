@@ -194,3 +194,41 @@ def test_swapped_kernel_split_tail_equals_row_kernels(cs1, stream, monkeypatch, 
         out.append(y)
     assert cs1.cs1_fault_status(1) == 0
     assert torch.equal(out[0], out[1])
+
+
+@pytest.mark.parametrize("M,N,epi,nt", [(771, 16480, "store", 208), (771, 17408, "swiglu", 208),
+                                        (771, 5120, "residual", 256), (17, 1544, "store", 32),
+                                        (1, 5120, "residual", 32), (300, 2560, "swiglu", 96),
+                                        (1500, 14336, "store", 256), (700, 16480, "store", 208),
+                                        (130, 1000, "residual", 144)])
+def test_swapped_pair_kernel_equals_row_kernels(cs1, stream, monkeypatch, M, N, epi, nt):
+    """The CTA-pair swapped kernel (256 rows of w over two SMs as the MMA's M side, nt rows
+    of x as its N side, split in halves between the CTAs), forced, against the 128 x 256
+    kernel: identical bits for every epilogue, partial tiles of w and x, and the split last
+    wave (700 x 16480 at nt = 208: 260 pair tiles over 74 pairs)."""
+    K = 640
+    x = _rand((M, K), 22)
+    w = _rand((2 * N if epi == "swiglu" else N, K), 23, 0.05)
+    res = _rand((M, N), 24)
+    out = []
+    for kernel in ("swap2", "row256"):
+        monkeypatch.setenv("S1_GEMM_KERNEL", kernel)
+        monkeypatch.setenv("S1_GEMM_NT", str(nt))
+        h = cs1.cs1_gemm_create(0)
+        if epi == "swiglu":
+            y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            cs1.cs1_gemm_swiglu(h, x, w, y, M, N, K, N, stream)
+        elif epi == "residual":
+            y = res.clone()
+            cs1.cs1_gemm_residual(h, x, w, y, M, N, K, N, stream)
+        else:
+            y = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            cs1.cs1_gemm(h, x, w, y, M, N, K, N, stream)
+        torch.cuda.synchronize()
+        cs1.cs1_gemm_destroy(h)
+        out.append(y)
+    assert cs1.cs1_fault_status(1) == 0
+    if epi == "store":
+        ref = (x.float() @ w.float().T).cpu().numpy()
+        assert max_rel(out[0].float().cpu().numpy(), ref) <= 1e-2
+    assert torch.equal(out[0], out[1])
