@@ -119,6 +119,126 @@ __global__ void prep_kernel(const bf16* __restrict__ qg, const bf16* __restrict_
     }
 }
 
+// The same prep with fewer instructions per unit (the kernel is issue-bound): one
+// division per warp (the units' tokens and heads follow by increments), the rotary rows
+// loaded with the inputs and unpacked once when the warp's units share a token (always
+// when PREP_UNITS divides Hq + Hk), the rotate-half sign folded into the sine, and the
+// norm and rotary products in packed f32x2 (lane-for-lane the scalar roundings).
+// Needs 16-byte aligned rotary tables and Hq + Hk >= 2.
+__global__ void prep_fast_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
+                                 const bf16* __restrict__ qw, const bf16* __restrict__ kw,
+                                 const bf16* __restrict__ cosb, const bf16* __restrict__ sinb, bf16* __restrict__ q,
+                                 bf16* __restrict__ gate, bf16* __restrict__ k, int T, int Hq, int Hk, int half,
+                                 float eps) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int unit0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * PREP_UNITS;
+    const int lane = threadIdx.x & 31;
+    const int heads = Hq + Hk;
+    const int units = T * heads;
+    if (unit0 >= units) return;
+    const int d0 = lane * 8;
+    const bool rotated = d0 < 2 * half;  // a lane's 8 dims are all rotated or all passed through
+    int ti[PREP_UNITS], hi[PREP_UNITS];
+    {
+        int t = unit0 / heads, hh = unit0 - t * heads;
+#pragma unroll
+        for (int i = 0; i < PREP_UNITS; i++) {
+            ti[i] = t;
+            hi[i] = hh;
+            if (++hh == heads) {
+                hh = 0;
+                t++;
+            }
+        }
+    }
+    const int n = min(PREP_UNITS, units - unit0);
+    Pack8 xr[PREP_UNITS], gr[PREP_UNITS];
+#pragma unroll
+    for (int i = 0; i < PREP_UNITS; i++) {
+        if (i < n) {
+            const bf16* row = qg + (size_t)ti[i] * ld;
+            if (hi[i] < Hq) {
+                const bf16* src = row + hi[i] * 2 * DH;
+                xr[i] = ld8(src + d0);
+                gr[i] = ld8(src + DH + d0);
+            } else {
+                xr[i] = ld8(kr + (size_t)ti[i] * ld + (hi[i] - Hq) * DH + d0);
+            }
+        }
+    }
+    const int t_a = ti[0], t_b = ti[n - 1];
+    const int f = d0 & (half - 1);  // half is a power of two (checked on the host)
+    Pack8 ca, sa, cb, sb;
+    if (rotated) {
+        ca = ld8(cosb + (size_t)t_a * half + f);
+        sa = ld8(sinb + (size_t)t_a * half + f);
+        if (t_b != t_a) {
+            cb = ld8(cosb + (size_t)t_b * half + f);
+            sb = ld8(sinb + (size_t)t_b * half + f);
+        }
+    }
+    float2 wq[4], wk[4];  // 1 + w
+    {
+        float a[8], b[8];
+        unpack8(ld8(qw + d0), a);
+        unpack8(ld8(kw + d0), b);
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            wq[p] = make_float2(1.f + a[2 * p], 1.f + a[2 * p + 1]);
+            wk[p] = make_float2(1.f + b[2 * p], 1.f + b[2 * p + 1]);
+        }
+    }
+    const float sgn = d0 < half ? -1.f : 1.f;  // rotate-half: -x2 for the first half, +x1 for the second
+    float2 cs[4], sn[4];
+    auto rot_rows = [&](const Pack8& c8, const Pack8& s8) {
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            cs[p] = __bfloat1622float2(c8.h[p]);
+            const float2 sv = __bfloat1622float2(s8.h[p]);
+            sn[p] = make_float2(sgn * sv.x, sgn * sv.y);
+        }
+    };
+    if (rotated) rot_rows(ca, sa);
+#pragma unroll
+    for (int i = 0; i < PREP_UNITS; i++) {
+        if (i >= n) break;  // uniform over the warp
+        const bool is_q = hi[i] < Hq;
+        float2 x[4];
+        float ss = 0.f;
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            x[p] = __bfloat1622float2(xr[i].h[p]);
+            ss = fmaf(x[p].x, x[p].x, ss);
+            ss = fmaf(x[p].y, x[p].y, ss);
+        }
+        const float inv = rsqrtf(warp_sum(ss) / DH + eps);
+        const float2 inv2 = make_float2(inv, inv);
+#pragma unroll
+        for (int p = 0; p < 4; p++) x[p] = rbf2(mul2(mul2(x[p], inv2), is_q ? wq[p] : wk[p]));
+        if (rotated && i > 0 && ti[i] != ti[i - 1]) rot_rows(cb, sb);  // the warp's second token
+        Pack8 out;
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            const float2 partner = make_float2(__shfl_xor_sync(0xffffffffu, x[p].x, half / 8),
+                                               __shfl_xor_sync(0xffffffffu, x[p].y, half / 8));
+            if (rotated) {
+                // bf16(x cos) + bf16(rotate_half(x) sin), rounded once more by the pack
+                const float2 y = add2(rbf2(mul2(x[p], cs[p])), rbf2(mul2(partner, sn[p])));
+                out.h[p] = __floats2bfloat162_rn(y.x, y.y);
+            } else {
+                out.h[p] = __floats2bfloat162_rn(x[p].x, x[p].y);
+            }
+        }
+        if (is_q) {
+            st8(q + ((size_t)ti[i] * Hq + hi[i]) * DH + d0, out);
+            st8(gate + ((size_t)ti[i] * Hq + hi[i]) * DH + d0, gr[i]);
+        } else {
+            st8(k + ((size_t)ti[i] * Hk + hi[i] - Hq) * DH + d0, out);
+        }
+    }
+}
+
 // ---------------------------------------------------------------- flash ----
 constexpr int BM = 128, BN = 64, WARPS = 8, THREADS = WARPS * 32;
 constexpr int LDS = DH + 8;  // padded smem row (528 B): ldmatrix rows hit distinct banks
@@ -804,6 +924,15 @@ int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const 
         !aligned16(k))
         return cudaErrorInvalidValue;
     constexpr int WPB = 8;
+    const bool cs_vec = aligned16(cos) && aligned16(sin);
+    // (with Hq + Hk >= 2 the PREP_UNITS = 4 units of a warp fall in at most two tokens)
+    if (cs_vec && Hq + Hk >= 2 && !legacy_elementwise())
+        return launch_pdl(attn::prep_fast_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
+                          static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg),
+                          static_cast<const bf16*>(kr), ld, static_cast<const bf16*>(qw),
+                          static_cast<const bf16*>(kw), static_cast<const bf16*>(cos), static_cast<const bf16*>(sin),
+                          static_cast<bf16*>(q), static_cast<bf16*>(gate), static_cast<bf16*>(k), T, Hq, Hk, half,
+                          eps);
     return launch_pdl(attn::prep_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
                       static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg), static_cast<const bf16*>(kr),
                       ld, static_cast<const bf16*>(qw), static_cast<const bf16*>(kw), static_cast<const bf16*>(cos),

@@ -65,13 +65,14 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     const int packs = 2 * key_packs + value_packs;
     if (c >= packs) return;
-    float wt[8][4];
+    // channel pairs (2p, 2p + 1) in f32x2 lanes: wt[p][j] = tap j of both channels
+    float2 wt[4][4];
 #pragma unroll
     for (int i = 0; i < 4; i++) {
         float f[8];
-        unpack8(ld8(w + (size_t)c * 32 + i * 8), f);
+        unpack8(ld8(w + (size_t)c * 32 + i * 8), f);  // channels 2i, 2i + 1, four taps each
 #pragma unroll
-        for (int e = 0; e < 8; e++) wt[(i * 8 + e) / 4][(i * 8 + e) % 4] = f[e];
+        for (int j = 0; j < 4; j++) wt[i][j] = make_float2(f[j], f[4 + j]);
     }
     bf16* dst;
     int dst_ld;
@@ -91,20 +92,24 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
     if (t_begin >= T) return;
     int s = seq_of(tab, t_begin);
     int next = tab.offset[s + 1];
-    float x1[8], x2[8], x3[8];  // rows t-3, t-2, t-1
+    float2 x1[4], x2[4], x3[4];  // rows t-3, t-2, t-1
+    auto unpack = [](const Pack8& p, float2 (&o)[4]) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[i] = __bfloat1622float2(p.h[i]);
+    };
     auto window = [&](int t) {
         // load the three rows before t inside its sequence (history or zeros before the start)
         const int pos = t - tab.offset[s];
 #pragma unroll
         for (int back = 3; back >= 1; back--) {
-            float* dstw = back == 3 ? x1 : back == 2 ? x2 : x3;
+            float2(&dw)[4] = back == 3 ? x1 : back == 2 ? x2 : x3;
             if (pos >= back) {
-                unpack8(ld8(qkv + (size_t)(t - back) * ld + (size_t)c * 8), dstw);
+                unpack(ld8(qkv + (size_t)(t - back) * ld + (size_t)c * 8), dw);
             } else if (history) {
-                unpack8(ld8(history + (size_t)(3 - back + pos) * ld + (size_t)c * 8), dstw);
+                unpack(ld8(history + (size_t)(3 - back + pos) * ld + (size_t)c * 8), dw);
             } else {
 #pragma unroll
-                for (int e = 0; e < 8; e++) dstw[e] = 0.f;
+                for (int i = 0; i < 4; i++) dw[i] = make_float2(0.f, 0.f);
             }
         }
     };
@@ -124,27 +129,25 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
                 next = tab.offset[s + 1];
                 window(t);
             }
-            float x0[8];
-            unpack8(raw[i], x0);
-            float y[8];
+            float2 x0[4];
+            unpack(raw[i], x0);
+            Pack8 out;
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                float acc = 0.f;
-                acc = fmaf(wt[e][0], x1[e], acc);
-                acc = fmaf(wt[e][1], x2[e], acc);
-                acc = fmaf(wt[e][2], x3[e], acc);
-                acc = fmaf(wt[e][3], x0[e], acc);
-                y[e] = acc;
+            for (int p = 0; p < 4; p++) {
+                // the reference's tap order: w0 x[t-3] + w1 x[t-2] + w2 x[t-1] + w3 x[t], fp32
+                float2 acc = mul2(wt[p][0], x1[p]);
+                acc = fma2(wt[p][1], x2[p], acc);
+                acc = fma2(wt[p][2], x3[p], acc);
+                acc = fma2(wt[p][3], x0[p], acc);
+                const float2 y = silu2_fast(rbf2(acc));
+                out.h[p] = __floats2bfloat162_rn(y.x, y.y);
             }
-            rbf8(y);
+            st8(dst + (size_t)t * dst_ld, out);
 #pragma unroll
-            for (int e = 0; e < 8; e++) y[e] = silu_fast(y[e]);
-            st8(dst + (size_t)t * dst_ld, pack8(y));
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                x1[e] = x2[e];
-                x2[e] = x3[e];
-                x3[e] = x0[e];
+            for (int p = 0; p < 4; p++) {
+                x1[p] = x2[p];
+                x2[p] = x3[p];
+                x3[p] = x0[p];
             }
         }
     }

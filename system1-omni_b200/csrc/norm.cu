@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restric
     }
 }
 
-int rms_warp_grid(int rows) {
+int sm_count() {
     static int sms = 0;
     if (!sms) {
         int dev = 0, n = 0;
@@ -149,8 +149,12 @@ int rms_warp_grid(int rows) {
         else
             sms = 148;
     }
+    return sms;
+}
+
+int rms_warp_grid(int rows) {
     const int need = (rows + RW_WARPS - 1) / RW_WARPS;
-    return need < sms * 8 ? need : sms * 8;
+    return need < sm_count() * 8 ? need : sm_count() * 8;
 }
 
 // Any D: scalar path, two passes over the row.
@@ -260,6 +264,75 @@ __global__ void gated16_kernel(const bf16* __restrict__ x, const bf16* __restric
     }
 }
 
+// The gated norm over a grid-stride loop of G_ROWS-row groups per warp, with each lane's
+// x and z chunks of the next two groups fetched by cp.async into a per-lane ring of
+// shared memory while the current group is computed (each lane reads back only its own
+// slots, so no barrier).
+constexpr int GA_WARPS = 8, GA_STAGES = 3;
+constexpr int GA_SLOTS = G_ROWS;  // per lane and stage: G_ROWS / 2 x chunks, then as many z chunks
+constexpr int GA_SMEM = GA_WARPS * GA_STAGES * GA_SLOTS * 32 * 16;
+
+__global__ void __launch_bounds__(GA_WARPS * 32) gated_async_kernel(const bf16* __restrict__ x,
+                                                                  const bf16* __restrict__ z, int ldz,
+                                                                  const bf16* __restrict__ w, bf16* __restrict__ out,
+                                                                  int rows, int H, float eps) {
+    extern __shared__ Pack8 gring[];  // [GA_WARPS][GA_STAGES][GA_SLOTS][32]
+    grid_dep_wait();
+    grid_dep_launch();
+    const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4, wib = threadIdx.x >> 5;
+    const int groups = (rows + G_ROWS - 1) / G_ROWS;
+    const int g0 = blockIdx.x * GA_WARPS + wib, gstep = gridDim.x * GA_WARPS;
+    Pack8* ring = gring + (size_t)wib * GA_STAGES * GA_SLOTS * 32 + lane;
+    auto issue = [&](int k) {  // the k-th group of this warp into stage k % GA_STAGES
+        const int g = g0 + k * gstep;
+        Pack8* dst = ring + (k % GA_STAGES) * GA_SLOTS * 32;
+#pragma unroll
+        for (int i = 0; i < G_ROWS / 2; i++) {
+            const int row = g * G_ROWS + 2 * i + half;
+            const bool ok = g < groups && row < rows;
+            const int r = ok ? row : 0;
+            cp_async16_zfill(dst + i * 32, x + (size_t)r * 128 + hl * 8, ok);
+            cp_async16_zfill(dst + (G_ROWS / 2 + i) * 32, z + (size_t)(r / H) * ldz + (size_t)(r % H) * 128 + hl * 8,
+                             ok);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    issue(1);
+    float wv[8];
+    unpack8(ld8(w + hl * 8), wv);
+    for (int k = 0; g0 + k * gstep < groups; k++) {
+        cp_async_wait1();
+        issue(k + 2);  // past the end it only commits zero-filled slots of a later stage
+        const Pack8* src = ring + (k % GA_STAGES) * GA_SLOTS * 32;
+        const int row0 = (g0 + k * gstep) * G_ROWS;
+#pragma unroll
+        for (int i = 0; i < G_ROWS / 2; i++) {
+            const int row = row0 + 2 * i + half;
+            float v[8], zz[8];
+            unpack8(src[i * 32], v);
+            unpack8(src[(G_ROWS / 2 + i) * 32], zz);
+            float ss = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            const float inv = rsqrtf(ss / 128.f + eps);
+            float o8[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) o8[e] = v[e] * inv;
+            rbf8(o8);
+#pragma unroll
+            for (int e = 0; e < 8; e++) o8[e] *= wv[e];
+            rbf8(o8);
+#pragma unroll
+            for (int e = 0; e < 8; e++) o8[e] *= silu_fast(zz[e]);
+            if (row < rows) st8(out + (size_t)row * 128 + hl * 8, pack8(o8));
+        }
+    }
+    cp_async_wait_all();
+}
+
 __global__ void gated_scalar_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
                                     const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
     const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
@@ -328,6 +401,17 @@ extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const v
     const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(z) |
                            reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out);
     const bool vec = ldz % 4 == 0 && (bits & 7) == 0;
+    if (ldz % 8 == 0 && (bits & 15) == 0 && !legacy_elementwise()) {
+        static const cudaError_t configured =
+            cudaFuncSetAttribute(gated_async_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GA_SMEM);
+        if (configured != cudaSuccess) return configured;
+        const int groups = (rows + G_ROWS - 1) / G_ROWS;
+        const int need = (groups + GA_WARPS - 1) / GA_WARPS;
+        const int grid = need < sm_count() * 2 ? need : sm_count() * 2;  // two resident per SM
+        return launch_pdl(gated_async_kernel, dim3(grid), dim3(GA_WARPS * 32), GA_SMEM, st,
+                          static_cast<const bf16*>(x), static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w),
+                          static_cast<bf16*>(out), rows, H, eps);
+    }
     if (ldz % 8 == 0 && (bits & 15) == 0) {
         const int per_block = WARPS * G_ROWS;
         return launch_pdl(gated16_kernel, dim3((rows + per_block - 1) / per_block), dim3(WARPS * 32), 0, st,

@@ -38,6 +38,9 @@ __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.w
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 bool pdl_enabled();  // S1_PDL=0 turns the attribute off (plain stream order)
+// S1_ELEM_LEGACY=1 selects the previous versions of the conv, gated-norm and attention-prep
+// kernels (register-staged loads), for timing the two against each other.
+bool legacy_elementwise();
 
 // Launch with the programmatic-serialisation attribute (see grid_dep_wait); the kernel
 // must call grid_dep_wait() before its first global-memory access. The attribute is set

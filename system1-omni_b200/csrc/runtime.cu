@@ -66,6 +66,14 @@ bool pdl_enabled() {
     return on;
 }
 
+bool legacy_elementwise() {
+    static const bool on = [] {
+        const char* e = getenv("S1_ELEM_LEGACY");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
+
 namespace host {
 
 int num_sms() {
