@@ -41,6 +41,8 @@ bool pdl_enabled();  // S1_PDL=0 turns the attribute off (plain stream order)
 // S1_ELEM_LEGACY=1 selects the previous versions of the conv, gated-norm and attention-prep
 // kernels (register-staged loads), for timing the two against each other.
 bool legacy_elementwise();
+// S1_SCAN_WIDE=0 keeps the GDN scan at four epilogue warps for every launch size.
+bool scan_wide_enabled();
 
 // Launch with the programmatic-serialisation attribute (see grid_dep_wait); the kernel
 // must call grid_dep_wait() before its first global-memory access. The attribute is set

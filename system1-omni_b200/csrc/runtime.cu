@@ -66,6 +66,14 @@ bool pdl_enabled() {
     return on;
 }
 
+bool scan_wide_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("S1_SCAN_WIDE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 bool legacy_elementwise() {
     static const bool on = [] {
         const char* e = getenv("S1_ELEM_LEGACY");
