@@ -495,6 +495,12 @@ __device__ __forceinline__ int query_blocks(const SeqTable& tab, int i, int q_ba
     return rows > 0 ? (rows + BM - 1) / BM : 0;
 }
 
+// PT: P in tensor memory. The softmax warps write bf16 P_j over the first 64 columns of
+// its own S buffer (two keys per 32-bit column) and PV_j reads its A operand from there, so
+// P is double-buffered with S: the softmax of tile j + 1 no longer waits for PV_j (only a
+// rescale of O does), and S_{j+2} is issued into a buffer once PV_j, its last reader, is
+// complete. Without PT, P goes through one shared-memory tile.
+template <bool PT>
 __global__ void __launch_bounds__(THREADS, 1)
     flash_tc(const __grid_constant__ Maps maps, Args a, SeqTable tab) {
     using namespace tc;
@@ -505,7 +511,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t bars = base + OFF_BAR;
     const uint32_t q_full = bars, k_full = bars + 8, k_empty = bars + 40, v_full = bars + 72, v_empty = bars + 80;
     const uint32_t s_full = bars + 88, s_free = bars + 104, p_full = bars + 120, pv_done = bars + 128;
-    const uint32_t drain = bars + 136;
+    const uint32_t drain = bars + 136, pv_done1 = bars + 144;
+    // PV_i completion: one barrier (parity i & 1), or with PT one per S/P buffer (parity (i >> 1) & 1),
+    // so that a waiter is never two phases behind: with PT the softmax does not wait for every PV
+    auto pv_bar = [&](int i) { return PT && (i & 1) ? pv_done1 : pv_done; };
+    auto pv_par = [&](int i) { return (uint32_t)(PT ? i >> 1 : i) & 1u; };
     int* info = reinterpret_cast<int*>(smem + OFF_BAR + 160);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 192);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -553,6 +563,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(s_free + 8, 4);
         mbar_init(p_full, 4);
         mbar_init(pv_done, 1);
+        mbar_init(pv_done1, 1);
         mbar_init(drain, 1);
         mbar_fence_init();
     }
@@ -632,19 +643,32 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = mbar_wait(q_full, 0);
             tc_fence_after();
             auto pv = [&](int i) -> bool {
-                if (!mbar_wait(p_full, (uint32_t)i & 1u) || !mbar_wait(v_full, (uint32_t)i & 1u)) return false;
+                // PT: P_i is announced on its buffer's own barrier (s_free is unused then), so the
+                // softmax running a tile ahead cannot complete a second phase before this wait
+                const bool p_ok = PT ? mbar_wait(s_free + 8 * (i & 1), (uint32_t)(i >> 1) & 1u)
+                                     : mbar_wait(p_full, (uint32_t)i & 1u);
+                if (!p_ok || !mbar_wait(v_full, (uint32_t)i & 1u)) return false;
                 tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; kk++)
-                    mma_bf16(tmem + 256, desc_sw128(base + OFF_P + (kk >> 2) * SUB + (kk & 3) * 32),
-                             desc_sw128_mn(base + OFF_V + kk * 2048, SUB, 1024), ID_O, (i > 0 || kk > 0) ? 1u : 0u);
+                for (int kk = 0; kk < BN / 16; kk++) {
+                    const uint64_t vd = desc_sw128_mn(base + OFF_V + kk * 2048, SUB, 1024);
+                    const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+                    if constexpr (PT)  // 16 keys = 8 packed columns of P_i
+                        mma_bf16_ts(tmem + 256, tmem + (uint32_t)((i & 1) * BN + kk * 8), vd, ID_O, acc);
+                    else
+                        mma_bf16(tmem + 256, desc_sw128(base + OFF_P + (kk >> 2) * SUB + (kk & 3) * 32), vd, ID_O,
+                                 acc);
+                }
                 mma_commit(v_empty);
-                mma_commit(pv_done);
+                mma_commit(pv_bar(i));
                 return true;
             };
             for (int j = 0; ok && j < n; j++) {
                 const int b = j & 1;
-                if (j >= 2 && !mbar_wait(s_free + 8 * b, (uint32_t)((j - 2) >> 1) & 1u)) {
+                // buffer b is free once the softmax has read S_{j-2} (and, with P in it, PV_{j-2}
+                // has completed; PV_{j-1} is not issued yet, so the parity names PV_{j-2})
+                if (j >= 2 && !(PT ? mbar_wait(pv_bar(j - 2), pv_par(j - 2))
+                                   : mbar_wait(s_free + 8 * b, (uint32_t)((j - 2) >> 1) & 1u))) {
                     ok = false;
                     break;
                 }
@@ -690,9 +714,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int c = 0; c < 4; c++) tmem_ld32(lane_addr + b * BN + c * 32, s[c]);
             tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(s_free + 8 * b);
+            if constexpr (!PT) {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(s_free + 8 * b);
+            }
             const int k0 = j * BN;
             bool full = k0 + BN <= total;
             if (a.causal)
@@ -727,13 +753,15 @@ __global__ void __launch_bounds__(THREADS, 1)
             float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             mx *= sl2;
-            // PV_{j-1} must be complete before P is overwritten or O rescaled
-            if (j > 0 && !__all_sync(0xffffffffu, mbar_wait(pv_done, (uint32_t)(j - 1) & 1u))) {
+            const bool grow = mx > m + RESCALE_LOG2;
+            // PV_{j-1} must be complete before O is rescaled (and, with P in shared memory,
+            // before P is overwritten); PV_{j-2} is, since S_j was issued after it
+            if (j > 0 && (!PT || __any_sync(0xffffffffu, grow)) &&
+                !__all_sync(0xffffffffu, mbar_wait(pv_bar(j - 1), pv_par(j - 1)))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const bool grow = mx > m + RESCALE_LOG2;
             const float alpha = grow ? ex2(m - mx) : 1.f;
             l *= alpha;
             if (grow) m = mx;
@@ -755,8 +783,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             float l8[8];
 #pragma unroll
             for (int i = 0; i < 8; i++) l8[i] = 0.f;
+            uint32_t pk[32];  // PT: 64 keys of P as bf16 pairs (one tcgen05.st of 32 columns)
 #pragma unroll
-            for (int c = 0; c < 4; c++)
+            for (int c = 0; c < 4; c++) {
 #pragma unroll
                 for (int g8 = 0; g8 < 4; g8++) {
                     float f[8];
@@ -765,16 +794,31 @@ __global__ void __launch_bounds__(THREADS, 1)
                         f[e] = ex2(fmaf(s[c][g8 * 8 + e], sl2, nm));
                         l8[e] += f[e];
                     }
-                    const int chunk = c * 4 + g8;  // 16-byte chunk of the 128-key row
-                    *reinterpret_cast<Pack8*>(prow + (chunk >> 3) * SUB + sw128_offset(r, chunk & 7)) = pack8(f);
+                    if constexpr (PT) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+                            pk[(c & 1) * 16 + g8 * 4 + e] = *reinterpret_cast<const uint32_t*>(&h2);
+                        }
+                    } else {
+                        const int chunk = c * 4 + g8;  // 16-byte chunk of the 128-key row
+                        *reinterpret_cast<Pack8*>(prow + (chunk >> 3) * SUB + sw128_offset(r, chunk & 7)) = pack8(f);
+                    }
                 }
+                if constexpr (PT) {
+                    if (c & 1) tmem_st32(lane_addr + b * BN + (c >> 1) * 32, *reinterpret_cast<const float(*)[32]>(pk));
+                }
+            }
             l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
-            fence_async_smem();
+            if constexpr (PT)
+                tmem_st_wait();
+            else
+                fence_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(PT ? s_free + 8 * b : p_full);
         }
-        if (ok && n > 0) ok = mbar_wait(pv_done, (uint32_t)(n - 1) & 1u);
+        if (ok && n > 0) ok = mbar_wait(pv_bar(n - 1), pv_par(n - 1));
         tc_fence_after();
         if (bar_any(1, 128, !ok)) {  // uniform over the four warps: the loads below are collective
             if (r == 0) atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
@@ -833,9 +877,21 @@ bool use_tc() {
     return on;
 }
 
+bool p_in_tmem() {
+    static const bool on = [] {
+        const char* e = getenv("S1_ATTN_PT");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
-    static const cudaError_t configured =
-        cudaFuncSetAttribute(flash_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    static const cudaError_t configured = [] {
+        cudaError_t e = cudaFuncSetAttribute(flash_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        return e == cudaSuccess
+                   ? cudaFuncSetAttribute(flash_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM)
+                   : e;
+    }();
     if (configured != cudaSuccess) return configured;
     const int rows = tab.offset[tab.count];
     Maps maps;
@@ -846,7 +902,8 @@ int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pk, a.pk, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pv, a.pv, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (e) return e;
-    return launch_pdl(flash_tc, dim3(a.Hq, blocks), dim3(THREADS), SMEM, st, maps, a, tab);
+    return launch_pdl(p_in_tmem() ? flash_tc<true> : flash_tc<false>, dim3(a.Hq, blocks), dim3(THREADS), SMEM, st,
+                      maps, a, tab);
 }
 
 }  // namespace tca
