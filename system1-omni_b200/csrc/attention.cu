@@ -710,6 +710,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                 break;
             }
             tc_fence_after();
+            if (j == n - 1 && a.gated) {
+                // S_{n-1} is complete, so no MMA reads the K tile any more: fetch this thread's
+                // gate units of the output pass into it, behind the last softmax and PV
+                const int t = threadIdx.x - 64, chunk = t & 31;
+                bf16* gs = reinterpret_cast<bf16*>(smem + OFF_K);
+#pragma unroll 8
+                for (int i = 0; i < BM / 4; i++) {
+                    const int row = (t >> 5) + 4 * i, lrow = min(q0 + row, len - 1);
+                    cp_async16_zfill(gs + row * DH + chunk * 8, a.gate + ((size_t)(off + lrow) * a.Hq + h) * DH + chunk * 8,
+                                     q0 + row < len);
+                }
+                cp_async_commit();
+            }
             float s[4][32];
 #pragma unroll
             for (int c = 0; c < 4; c++) tmem_ld32(lane_addr + b * BN + c * 32, s[c]);
@@ -843,21 +856,29 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             asm volatile("bar.sync 1, 128;" ::: "memory");
             const int t = threadIdx.x - 64, chunk = t & 31;
+            const bf16* gs = reinterpret_cast<const bf16*>(smem + OFF_K);
+            if (a.gated) cp_async_wait_all();  // this thread's own gate units (fetched at the last tile)
 #pragma unroll 4
             for (int i = 0; i < BM / 4; i++) {
                 const int row = (t >> 5) + 4 * i;
                 const int lrow = q0 + row;
                 if (lrow >= len) break;
-                float x[8];
-                unpack8(ld8(stage + row * DH + ((chunk ^ row) & 31) * 8), x);
+                const Pack8 xv = ld8(stage + row * DH + ((chunk ^ row) & 31) * 8);
                 const size_t o_off = ((size_t)(off + lrow) * a.Hq + h) * DH + chunk * 8;
                 if (a.gated) {
-                    float gv[8];
-                    unpack8(ld8(a.gate + o_off), gv);
+                    const Pack8 gv = ld8(gs + row * DH + chunk * 8);
+                    Pack8 y;
 #pragma unroll
-                    for (int e = 0; e < 8; e++) x[e] = x[e] * rbf(sigmoid(gv[e]));
+                    for (int p2 = 0; p2 < 4; p2++) {
+                        // out = x * bf16(sigmoid(gate))
+                        const float2 sg = rbf2(sigmoid2_fast(__bfloat1622float2(gv.h[p2])));
+                        const float2 o2 = mul2(__bfloat1622float2(xv.h[p2]), sg);
+                        y.h[p2] = __floats2bfloat162_rn(o2.x, o2.y);
+                    }
+                    st8(a.out + o_off, y);
+                } else {
+                    st8(a.out + o_off, xv);
                 }
-                st8(a.out + o_off, pack8(x));
             }
         }
     }

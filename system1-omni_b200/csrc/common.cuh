@@ -132,6 +132,20 @@ __device__ __forceinline__ float2 rbf2(float2 v) { return __bfloat1622float2(__f
 // exponential and reciprocal (relative error ~1e-7, far below the bf16 rounding that
 // follows): one packed multiply, add and multiply and two special-function operations
 // per lane.
+// Sigmoid of a pair from 1 / (1 + 2^(-y log2 e)) with the hardware base-2 exponential and
+// reciprocal (relative error ~1e-7).
+__device__ __forceinline__ float2 sigmoid2_fast(float2 y) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    const float2 t = mul2(y, make_float2(-kLog2e, -kLog2e));
+    float2 e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(t.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(t.y));
+    const float2 d = add2(e, make_float2(1.f, 1.f));
+    float2 r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
+    return r;
+}
 __device__ __forceinline__ float2 silu2_fast(float2 y) {
     constexpr float kLog2e = 1.4426950408889634f;
     const float2 t = mul2(y, make_float2(-kLog2e, -kLog2e));
