@@ -1,6 +1,6 @@
 """Time every projection-GEMM kernel of libqwen3_5_cuda.so on the 27B projection shapes.
 
-    cd system1-omni_b200 && python -m s1omni.gemm_tune [--m 300,771,2048] [--reps 10]
+    cd system1-omni_b200 && python -m s1omni.gemm_tune [--m 300,771,2048] [--reps 10] [--lib PATH]
 
 For each M and shape, one handle per kernel option (S1_GEMM_KERNEL = pair | row256 |
 row128 | swap | swap2 with S1_GEMM_NT = 64..256, set before cs1_gemm_create) and the default
@@ -24,8 +24,9 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--m", default="300,771,2048")
     ap.add_argument("--reps", type=int, default=10)
+    ap.add_argument("--lib", default=None, help="another build of the library (default: this package's)")
     a = ap.parse_args()
-    lib = Cs1()
+    lib = Cs1(a.lib)
     st = torch.cuda.current_stream().cuda_stream
     g = torch.Generator(device="cuda").manual_seed(0)
     opts = [("model", {}), ("pair", {"S1_GEMM_KERNEL": "pair"}), ("row256", {"S1_GEMM_KERNEL": "row256"}),
