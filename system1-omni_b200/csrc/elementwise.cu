@@ -57,34 +57,44 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const Pack8* __res
 // (or from the three rows of `history`, shared by every sequence).
 constexpr int CONV_ROWS = 64;
 
-__global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld,
+// NP channel pairs per thread: 4 (16-byte accesses) or 2 (8-byte accesses, about half the
+// registers, so more warps per SM keep loads in flight).
+template <int NP>
+struct alignas(4 * NP) PackN {
+    __nv_bfloat162 h[NP];
+};
+
+template <int NP>
+__global__ void __launch_bounds__(128, NP == 2 ? 8 : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
                                 bf16* __restrict__ v, int key_packs, int value_packs, SeqTable tab) {
+    using P = PackN<NP>;
+    constexpr int CH = 2 * NP;  // channels per thread
     grid_dep_wait();
     grid_dep_launch();
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;  // pack of CH channels
     const int packs = 2 * key_packs + value_packs;
     if (c >= packs) return;
     // channel pairs (2p, 2p + 1) in f32x2 lanes: wt[p][j] = tap j of both channels
-    float2 wt[4][4];
+    float2 wt[NP][4];
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
+    for (int i = 0; i < NP; i++) {
         float f[8];
-        unpack8(ld8(w + (size_t)c * 32 + i * 8), f);  // channels 2i, 2i + 1, four taps each
+        unpack8(ld8(w + (size_t)c * CH * 4 + i * 8), f);  // channels 2i, 2i + 1, four taps each
 #pragma unroll
         for (int j = 0; j < 4; j++) wt[i][j] = make_float2(f[j], f[4 + j]);
     }
     bf16* dst;
     int dst_ld;
     if (c < key_packs) {
-        dst = q + (size_t)c * 8;
-        dst_ld = key_packs * 8;
+        dst = q + (size_t)c * CH;
+        dst_ld = key_packs * CH;
     } else if (c < 2 * key_packs) {
-        dst = k + (size_t)(c - key_packs) * 8;
-        dst_ld = key_packs * 8;
+        dst = k + (size_t)(c - key_packs) * CH;
+        dst_ld = key_packs * CH;
     } else {
-        dst = v + (size_t)(c - 2 * key_packs) * 8;
-        dst_ld = value_packs * 8;
+        dst = v + (size_t)(c - 2 * key_packs) * CH;
+        dst_ld = value_packs * CH;
     }
     const int T = tab.offset[tab.count];
     const int t_begin = blockIdx.y * CONV_ROWS;
@@ -92,34 +102,36 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
     if (t_begin >= T) return;
     int s = seq_of(tab, t_begin);
     int next = tab.offset[s + 1];
-    float2 x1[4], x2[4], x3[4];  // rows t-3, t-2, t-1
-    auto unpack = [](const Pack8& p, float2 (&o)[4]) {
+    const bf16* col = qkv + (size_t)c * CH;
+    auto ld = [&](const bf16* p) { return *reinterpret_cast<const P*>(p); };
+    float2 x1[NP], x2[NP], x3[NP];  // rows t-3, t-2, t-1
+    auto unpack = [](const P& p, float2 (&o)[NP]) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) o[i] = __bfloat1622float2(p.h[i]);
+        for (int i = 0; i < NP; i++) o[i] = __bfloat1622float2(p.h[i]);
     };
     auto window = [&](int t) {
         // load the three rows before t inside its sequence (history or zeros before the start)
         const int pos = t - tab.offset[s];
 #pragma unroll
         for (int back = 3; back >= 1; back--) {
-            float2(&dw)[4] = back == 3 ? x1 : back == 2 ? x2 : x3;
+            float2(&dw)[NP] = back == 3 ? x1 : back == 2 ? x2 : x3;
             if (pos >= back) {
-                unpack(ld8(qkv + (size_t)(t - back) * ld + (size_t)c * 8), dw);
+                unpack(ld(col + (size_t)(t - back) * ld_), dw);
             } else if (history) {
-                unpack(ld8(history + (size_t)(3 - back + pos) * ld + (size_t)c * 8), dw);
+                unpack(ld(history + (size_t)(3 - back + pos) * ld_ + (size_t)c * CH), dw);
             } else {
 #pragma unroll
-                for (int i = 0; i < 4; i++) dw[i] = make_float2(0.f, 0.f);
+                for (int i = 0; i < NP; i++) dw[i] = make_float2(0.f, 0.f);
             }
         }
     };
     window(t_begin);
     // rows in batches of 8: all loads of a batch are in flight before the first is used
     for (int tb = t_begin; tb < t_end; tb += 8) {
-        Pack8 raw[8];
+        P raw[8];
 #pragma unroll
         for (int i = 0; i < 8; i++)
-            if (tb + i < t_end) raw[i] = ld8(qkv + (size_t)(tb + i) * ld + (size_t)c * 8);
+            if (tb + i < t_end) raw[i] = ld(col + (size_t)(tb + i) * ld_);
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const int t = tb + i;
@@ -129,11 +141,11 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
                 next = tab.offset[s + 1];
                 window(t);
             }
-            float2 x0[4];
+            float2 x0[NP];
             unpack(raw[i], x0);
-            Pack8 out;
+            P out;
 #pragma unroll
-            for (int p = 0; p < 4; p++) {
+            for (int p = 0; p < NP; p++) {
                 // the reference's tap order: w0 x[t-3] + w1 x[t-2] + w2 x[t-1] + w3 x[t], fp32
                 float2 acc = mul2(wt[p][0], x1[p]);
                 acc = fma2(wt[p][1], x2[p], acc);
@@ -142,9 +154,9 @@ __global__ void conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __rest
                 const float2 y = silu2_fast(rbf2(acc));
                 out.h[p] = __floats2bfloat162_rn(y.x, y.y);
             }
-            st8(dst + (size_t)t * dst_ld, out);
+            *reinterpret_cast<P*>(dst + (size_t)t * dst_ld) = out;
 #pragma unroll
-            for (int p = 0; p < 4; p++) {
+            for (int p = 0; p < NP; p++) {
                 x1[p] = x2[p];
                 x2[p] = x3[p];
                 x3[p] = x0[p];
@@ -260,11 +272,15 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
     const bool vec = key_dim % 8 == 0 && value_dim % 8 == 0 && ld % 8 == 0 && aligned16(qkv) && aligned16(w) &&
                      aligned16(q) && aligned16(k) && aligned16(v) && (!history || aligned16(history));
     if (vec) {
-        const int packs = (2 * key_dim + value_dim) / 8;
-        return launch_pdl(conv_vec_kernel, dim3((packs + 127) / 128, (T + CONV_ROWS - 1) / CONV_ROWS), dim3(128), 0,
-                          st, static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
+        // 4 channels per thread: twice the threads at half the registers each (64: 8 CTAs of 128
+        // threads per SM instead of 4), which keeps more rows in flight
+        const bool narrow = conv_narrow() && key_dim % 4 == 0;
+        const int cpt = narrow ? 4 : 8, tpacks = (2 * key_dim + value_dim) / cpt;
+        return launch_pdl(narrow ? conv_vec_kernel<2> : conv_vec_kernel<4>,
+                          dim3((tpacks + 127) / 128, (T + CONV_ROWS - 1) / CONV_ROWS), dim3(128), 0, st,
+                          static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
                           static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
-                          static_cast<bf16*>(v), key_dim / 8, value_dim / 8, tab);
+                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, tab);
     } else {
         const int ch = 2 * key_dim + value_dim;
         conv_scalar_kernel<<<dim3((ch + 127) / 128, rows), 128, 0, st>>>(

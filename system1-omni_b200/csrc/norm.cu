@@ -299,8 +299,12 @@ __global__ void __launch_bounds__(GA_WARPS * 32) gated_async_kernel(const bf16* 
     };
     issue(0);
     issue(1);
-    float wv[8];
-    unpack8(ld8(w + hl * 8), wv);
+    float2 w2[4];
+    {
+        const Pack8 wp = ld8(w + hl * 8);
+#pragma unroll
+        for (int p = 0; p < 4; p++) w2[p] = __bfloat1622float2(wp.h[p]);
+    }
     for (int k = 0; g0 + k * gstep < groups; k++) {
         cp_async_wait1();
         issue(k + 2);  // past the end it only commits zero-filled slots of a later stage
@@ -309,25 +313,28 @@ __global__ void __launch_bounds__(GA_WARPS * 32) gated_async_kernel(const bf16* 
 #pragma unroll
         for (int i = 0; i < G_ROWS / 2; i++) {
             const int row = row0 + 2 * i + half;
-            float v[8], zz[8];
-            unpack8(src[i * 32], v);
-            unpack8(src[(G_ROWS / 2 + i) * 32], zz);
+            const Pack8 xv = src[i * 32], zv = src[(G_ROWS / 2 + i) * 32];
+            float2 v[4];
             float ss = 0.f;
 #pragma unroll
-            for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
+            for (int p = 0; p < 4; p++) {
+                v[p] = __bfloat1622float2(xv.h[p]);
+                ss = fmaf(v[p].x, v[p].x, ss);
+                ss = fmaf(v[p].y, v[p].y, ss);
+            }
 #pragma unroll
             for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
             const float inv = rsqrtf(ss / 128.f + eps);
-            float o8[8];
+            const float2 inv2 = make_float2(inv, inv);
+            Pack8 o8;
 #pragma unroll
-            for (int e = 0; e < 8; e++) o8[e] = v[e] * inv;
-            rbf8(o8);
-#pragma unroll
-            for (int e = 0; e < 8; e++) o8[e] *= wv[e];
-            rbf8(o8);
-#pragma unroll
-            for (int e = 0; e < 8; e++) o8[e] *= silu_fast(zz[e]);
-            if (row < rows) st8(out + (size_t)row * 128 + hl * 8, pack8(o8));
+            for (int p = 0; p < 4; p++) {
+                // bf16(bf16(w * bf16(x * inv)) * silu(z)), lane for lane the scalar roundings
+                const float2 y = mul2(rbf2(mul2(rbf2(mul2(v[p], inv2)), w2[p])),
+                                      silu2_fast(__bfloat1622float2(zv.h[p])));
+                o8.h[p] = __floats2bfloat162_rn(y.x, y.y);
+            }
+            if (row < rows) st8(out + (size_t)row * 128 + hl * 8, o8);
         }
     }
     cp_async_wait_all();

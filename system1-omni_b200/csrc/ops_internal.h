@@ -41,6 +41,8 @@ bool pdl_enabled();  // S1_PDL=0 turns the attribute off (plain stream order)
 // S1_ELEM_LEGACY=1 selects the previous versions of the conv, gated-norm and attention-prep
 // kernels (register-staged loads), for timing the two against each other.
 bool legacy_elementwise();
+// S1_CONV_NARROW=0 runs the GDN conv with 8 channels per thread instead of 4.
+bool conv_narrow();
 // S1_SCAN_WIDE=0 keeps the GDN scan at four epilogue warps for every launch size.
 bool scan_wide_enabled();
 

@@ -66,6 +66,14 @@ bool pdl_enabled() {
     return on;
 }
 
+bool conv_narrow() {
+    static const bool on = [] {
+        const char* e = getenv("S1_CONV_NARROW");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 bool scan_wide_enabled() {
     static const bool on = [] {
         const char* e = getenv("S1_SCAN_WIDE");
