@@ -96,6 +96,21 @@ int s1_model_fused(void* model);
 // The model's configuration (layer_types points into the model; valid while it lives).
 int s1_model_get_config(void* model, s1_config* out);
 
+// ---- context-parallel prefill of one prompt over several GPUs (one process each) ----
+// The prompt is split in order into one piece per rank; rank r runs every layer on its
+// piece and receives from rank r - 1, per layer, what a shared prefix would hand it (the
+// GDN layer's final fp32 state and last three pre-conv rows, the attention layer's K and V
+// of all earlier pieces), sending its own on to rank r + 1 (NCCL point-to-point on the
+// model stream, so the ranks pipeline layer by layer). With pieces on 64-token boundaries
+// the last rank's logits equal those of the whole prompt on one GPU, bit for bit.
+// NCCL is bound at run time: nccl_library null or "" means "libnccl.so.2".
+int s1_cp_unique_id(const char* nccl_library, void* id_out);  // 128 bytes, made on one rank
+int s1_model_cp_init(void* model, const char* nccl_library, const void* id, int rank, int world);
+// ids[len]: this rank's piece, starting at prompt position `start` (0 on rank 0, a multiple
+// of 64; every piece but the last a multiple of 64 long). logits [labels] and hidden [H]
+// are written on the last rank only.
+int s1_model_forward_cp(void* model, const int32_t* ids, size_t len, size_t start, float* logits, float* hidden);
+
 // ---- checkpoints (src/models/qwen3_5/native/src/model.rs:96-226, 267-397) ----
 // A Hugging Face Qwen3.5 config.json (or its text_config) as an s1_config; layer_types
 // receives the per-layer kinds (capacity max_layers). labels is set to 1 (the Open-Jev

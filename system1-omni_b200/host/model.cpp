@@ -14,6 +14,7 @@
 #include "s1_model.h"
 
 #include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -22,6 +23,7 @@
 #include <deque>
 #include <map>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 namespace {
@@ -200,8 +202,48 @@ struct Batch {
     std::vector<size_t> lengths;
     int prefix = 0;        // shared prefix length for suffix passes (positions start there)
     bool capture = false;  // capture prefix state (prefix pass)
+    bool cp = false;       // context-parallel piece: prefix state from rank - 1, own state to rank + 1
     size_t rows = 0;
 };
+
+// NCCL, bound at run time (the library torch or the system provides) for the
+// context-parallel prefill.
+struct Nccl {
+    void* lib = nullptr;
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*group_start)() = nullptr;
+    ncclResult_t (*group_end)() = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+bool load_nccl(const char* path, Nccl& n, std::string& err) {
+    n.lib = dlopen(path && *path ? path : "libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!n.lib) {
+        err = std::string("cannot load NCCL: ") + dlerror();
+        return false;
+    }
+    bool ok = true;
+    auto sym = [&](const char* name, auto& fn) {
+        fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(n.lib, name));
+        if (!fn) {
+            ok = false;
+            err = std::string("NCCL has no ") + name;
+        }
+    };
+    sym("ncclGetUniqueId", n.get_unique_id);
+    sym("ncclCommInitRank", n.comm_init_rank);
+    sym("ncclCommDestroy", n.comm_destroy);
+    sym("ncclSend", n.send);
+    sym("ncclRecv", n.recv);
+    sym("ncclGroupStart", n.group_start);
+    sym("ncclGroupEnd", n.group_end);
+    sym("ncclGetErrorString", n.error_string);
+    return ok;
+}
 
 struct Model {
     Api api;
@@ -234,6 +276,11 @@ struct Model {
     bool graphs = false;
     std::map<std::vector<size_t>, void*> graph_cache;
     std::deque<std::vector<size_t>> graph_order;
+    // context parallelism: rank of `cp_world` processes that split one prompt in order
+    Nccl nccl;
+    ncclComm_t comm = nullptr;
+    int cp_rank = 0, cp_world = 1;
+    uint8_t* cp_state = nullptr;  // this rank's final GDN state of the current layer, sent on
     // staged batch for run_staged
     Batch staged;
     bool have_staged = false;
@@ -394,6 +441,20 @@ int project_residual(Model* m, size_t x, const Region& w, int M, int K, const Re
     return 0;
 }
 
+// One NCCL group on the model stream: `send` to rank + 1 and / or receive into `recv`
+// from rank - 1 (either may be null).
+int cp_xfer(Model* m, const void* send, size_t send_bytes, void* recv, size_t recv_bytes, const char* what) {
+    Nccl& n = m->nccl;
+    const auto st = static_cast<cudaStream_t>(m->stream);
+    ncclResult_t r = n.group_start();
+    if (r == ncclSuccess && send) r = n.send(send, send_bytes, ncclUint8, m->cp_rank + 1, m->comm, st);
+    if (r == ncclSuccess && recv) r = n.recv(recv, recv_bytes, ncclUint8, m->cp_rank - 1, m->comm, st);
+    const ncclResult_t e = n.group_end();
+    if (r == ncclSuccess) r = e;
+    if (r != ncclSuccess) return fail(m, -1, std::string(what) + ": " + n.error_string(r));
+    return 0;
+}
+
 int run_layers(Model* m, const Batch& b) {
     const s1_config& c = m->cfg;
     const int T = (int)b.rows;
@@ -403,6 +464,7 @@ int run_layers(Model* m, const Batch& b) {
     const float gdn_scale = 1.0f / std::sqrt((float)c.lin_k_dim);
     const float attn_scale = 1.0f / std::sqrt((float)c.head_dim);
     const bool suffix = b.prefix > 0 && !b.capture;
+    const bool cp_send = b.cp && m->cp_rank + 1 < m->cp_world, cp_recv = b.cp && m->cp_rank > 0;
     m->launches++;
     CK(m->api.embed(static_cast<const int32_t*>((const void*)m->S(m->s_ids)), m->W(m->embed), m->S(m->s_res), T,
                     c.hidden, m->stream),
@@ -417,6 +479,12 @@ int run_layers(Model* m, const Batch& b) {
             CK(gemm_store(m, m->s_x, L.in_proj, m->s_gdn_in, T, m->gdn_in, c.hidden), "gdn input projection");
             const int ld = m->gdn_in;
             uint8_t* gin = m->S(m->s_gdn_in);
+            if (cp_send || cp_recv) {  // the last three pre-conv rows go to the next piece's conv
+                const int rc = cp_xfer(m, cp_send ? gin + (size_t)(T - 3) * ld * 2 : nullptr, (size_t)3 * ld * 2,
+                                       cp_recv ? m->prefix_buf + m->p_tail[gi] : nullptr, (size_t)3 * ld * 2,
+                                       "conv history exchange");
+                if (rc) return rc;
+            }
             const void* hist = suffix ? m->prefix_buf + m->p_tail[gi] : nullptr;
             if (m->api.gdn_conv_batch && n <= m->api.max_batch) {
                 m->launches++;
@@ -448,8 +516,13 @@ int run_layers(Model* m, const Batch& b) {
                                 reinterpret_cast<float*>(m->S(m->s_g)), T, c.lin_v_heads, m->stream),
                "gdn gates");
             float* ws = reinterpret_cast<float*>(m->S(m->s_ws));
+            const size_t state_bytes = (size_t)c.lin_v_heads * c.lin_k_dim * c.lin_v_dim * 4;
+            if (cp_recv) {  // the previous piece's final state of this layer
+                const int rc = cp_xfer(m, nullptr, 0, m->prefix_buf + m->p_state[gi], state_bytes, "state receive");
+                if (rc) return rc;
+            }
             const void* s_in = suffix ? m->prefix_buf + m->p_state[gi] : nullptr;
-            void* s_out = b.capture ? m->prefix_buf + m->p_state[gi] : nullptr;
+            void* s_out = b.capture ? m->prefix_buf + m->p_state[gi] : cp_send ? m->cp_state : nullptr;
             if (m->api.gdn_prefill_batch_x && n <= m->api.max_batch) {
                 m->launches += 2;
                 CK(m->api.gdn_prefill_batch_x(m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
@@ -477,6 +550,10 @@ int run_layers(Model* m, const Batch& b) {
                        "gdn prefill");
                 }
             }
+            if (cp_send) {
+                const int rc = cp_xfer(m, m->cp_state, state_bytes, nullptr, 0, "state send");
+                if (rc) return rc;
+            }
             m->launches++;
             CK(m->api.gated_rms_norm(m->S(m->s_lo), gin + zoff, ld, m->W(L.norm), m->S(m->s_ln), T, c.lin_v_heads,
                                      c.lin_v_dim, c.eps, m->stream),
@@ -502,6 +579,12 @@ int run_layers(Model* m, const Batch& b) {
                                 m->S(m->s_aq), m->S(m->s_agate), m->S(m->s_ak), T, c.heads, c.kv_heads, c.head_dim,
                                 c.rotary_half, c.eps, m->stream),
                "attention prep");
+            const size_t kv_prefix = (size_t)b.prefix * m->kvd * 2;
+            if (cp_recv) {  // K (normed, rotated) and V of every earlier piece
+                int rc = cp_xfer(m, nullptr, 0, m->prefix_buf + m->p_k[ai], kv_prefix, "prefix K receive");
+                if (!rc) rc = cp_xfer(m, nullptr, 0, m->prefix_buf + m->p_v[ai], kv_prefix, "prefix V receive");
+                if (rc) return rc;
+            }
             const void* pk = suffix ? m->prefix_buf + m->p_k[ai] : nullptr;
             const void* pv = suffix ? m->prefix_buf + m->p_v[ai] : nullptr;
             if (suffix && m->api.attention_gated_shared_batch && n <= m->api.max_batch) {
@@ -545,6 +628,19 @@ int run_layers(Model* m, const Batch& b) {
                 CK(m->api.copy2d(m->prefix_buf + m->p_v[ai], (size_t)m->kvd * 2, vptr, (size_t)ld * 2,
                                  (size_t)m->kvd * 2, P, m->stream),
                    "capture prefix V");
+            }
+            if (cp_send) {  // this piece's K and V after the received ones, all to the next piece
+                m->launches += 2;
+                CK(m->api.copy_dd(m->prefix_buf + m->p_k[ai] + kv_prefix, m->S(m->s_ak), (size_t)T * m->kvd * 2,
+                                  m->stream),
+                   "append K");
+                CK(m->api.copy2d(m->prefix_buf + m->p_v[ai] + kv_prefix, (size_t)m->kvd * 2, vptr, (size_t)ld * 2,
+                                 (size_t)m->kvd * 2, T, m->stream),
+                   "append V");
+                const size_t bytes = kv_prefix + (size_t)T * m->kvd * 2;
+                int rc = cp_xfer(m, m->prefix_buf + m->p_k[ai], bytes, nullptr, 0, "prefix K send");
+                if (!rc) rc = cp_xfer(m, m->prefix_buf + m->p_v[ai], bytes, nullptr, 0, "prefix V send");
+                if (rc) return rc;
             }
             CK(project_residual(m, m->s_ao, L.o, T, m->qd, L.post_norm), "attention output projection");
             ai++;
@@ -819,6 +915,8 @@ __attribute__((visibility("default"))) void s1_model_destroy(void* mp) {
     if (m->arena) m->api.free_(m->arena);
     if (m->scratch) m->api.free_(m->scratch);
     if (m->prefix_buf) m->api.free_(m->prefix_buf);
+    if (m->cp_state) m->api.free_(m->cp_state);
+    if (m->comm) m->nccl.comm_destroy(m->comm);
     if (m->stream) m->api.stream_destroy(m->stream);
     // the library stays loaded: CUDA state it owns must outlive this model
     delete m;
@@ -1043,6 +1141,73 @@ __attribute__((visibility("default"))) long s1_model_last_launches(void* mp) {
 __attribute__((visibility("default"))) int s1_model_fused(void* mp) {
     auto* m = static_cast<Model*>(mp);
     return m ? (m->fused ? 1 : 0) : -1;
+}
+
+__attribute__((visibility("default"))) int s1_cp_unique_id(const char* nccl_library, void* id_out) {
+    if (!id_out) return -1;
+    Nccl n;
+    std::string err;
+    if (!load_nccl(nccl_library, n, err)) {
+        g_create_error = err;
+        return -1;
+    }
+    ncclUniqueId id;
+    if (n.get_unique_id(&id) != ncclSuccess) {
+        g_create_error = "ncclGetUniqueId failed";
+        return -1;
+    }
+    std::memcpy(id_out, &id, sizeof(id));
+    return 0;
+}
+
+__attribute__((visibility("default"))) int s1_model_cp_init(void* mp, const char* nccl_library, const void* id,
+                                                           int rank, int world) {
+    auto* m = static_cast<Model*>(mp);
+    if (!m || !id || world < 2 || rank < 0 || rank >= world) return -1;
+    if (m->comm) return fail(m, -1, "context parallelism is already initialised");
+    std::string err;
+    if (!load_nccl(nccl_library, m->nccl, err)) return fail(m, -1, err);
+    CK(m->api.set_device(m->device), "set device");
+    ncclUniqueId uid;
+    std::memcpy(&uid, id, sizeof(uid));
+    const ncclResult_t r = m->nccl.comm_init_rank(&m->comm, world, uid, rank);
+    if (r != ncclSuccess) {
+        m->comm = nullptr;
+        return fail(m, -1, std::string("ncclCommInitRank: ") + m->nccl.error_string(r));
+    }
+    void* p = nullptr;
+    const s1_config& c = m->cfg;
+    CK(m->api.malloc_(&p, (size_t)c.lin_v_heads * c.lin_k_dim * c.lin_v_dim * 4), "state buffer");
+    m->cp_state = static_cast<uint8_t*>(p);
+    m->cp_rank = rank;
+    m->cp_world = world;
+    return 0;
+}
+
+__attribute__((visibility("default"))) int s1_model_forward_cp(void* mp, const int32_t* ids, size_t len, size_t start,
+                                                              float* logits, float* hidden) {
+    auto* m = static_cast<Model*>(mp);
+    if (!m || !ids) return -1;
+    if (!m->comm) return fail(m, -1, "context parallelism is not initialised");
+    const bool last = m->cp_rank + 1 == m->cp_world;
+    if (len < 64 || len > (size_t)m->cap_tokens) return fail(m, -1, "piece length out of range");
+    if (start % 64 != 0 || (!last && len % 64 != 0))
+        return fail(m, -1, "pieces must start on multiples of 64 tokens (all but the last of 64k tokens)");
+    if ((start == 0) != (m->cp_rank == 0)) return fail(m, -1, "rank 0 holds the first piece");
+    int rc = ensure_prefix(m, (int)(start + len));
+    if (rc) return rc;
+    Batch b;
+    b.lengths = {len};
+    b.rows = len;
+    b.prefix = (int)start;
+    b.cp = true;
+    rc = stage_inputs(m, ids, b);
+    if (rc) return rc;
+    m->launches = 0;
+    rc = run_layers(m, b);
+    if (!rc && last) rc = run_head(m, 1);
+    if (rc) return rc;
+    return read_outputs(m, b, last ? logits : nullptr, last ? hidden : nullptr);
 }
 
 __attribute__((visibility("default"))) int s1_model_get_config(void* mp, s1_config* out) {

@@ -114,6 +114,9 @@ def _lib():
     lib.s1_model_load_head.argtypes = [P, ctypes.c_char_p, I, I]
     lib.s1_checkpoint_list.restype = ctypes.c_long
     lib.s1_checkpoint_list.argtypes = [ctypes.c_char_p, P, Z]
+    lib.s1_cp_unique_id.argtypes = [ctypes.c_char_p, P]
+    lib.s1_model_cp_init.argtypes = [P, ctypes.c_char_p, P, I, I]
+    lib.s1_model_forward_cp.argtypes = [P, P, Z, Z, P, P]
     lib.s1_checkpoint_check.argtypes = [ctypes.c_char_p, ctypes.POINTER(_Cfg)]
     lib.s1_model_get_config.argtypes = [P, ctypes.POINTER(_Cfg)]
     lib.s1_checkpoint_error.restype = ctypes.c_char_p
@@ -200,6 +203,16 @@ def checkpoint_check(folder, cfg):
         raise ValueError("checkpoint: " + lib.s1_checkpoint_error().decode())
 
 
+def cp_unique_id(nccl_library=None):
+    """The 128-byte NCCL id of a context-parallel group, made on one rank and handed to
+    every rank (for instance with torch.distributed.broadcast_object_list)."""
+    lib = _get()
+    buf = ctypes.create_string_buffer(128)
+    if lib.s1_cp_unique_id((nccl_library or "").encode(), buf) != 0:
+        raise RuntimeError("s1_cp_unique_id: " + lib.s1_model_error(None).decode())
+    return buf.raw
+
+
 class Model:
     """A prefill model on one GPU: `Model(cfg, device, max_tokens, max_seqs)`."""
 
@@ -262,6 +275,21 @@ class Model:
         """The scorer head of an export manifest (open_jev_export.json)."""
         if self._lib.s1_model_load_head(self._h, str(manifest_json).encode(), self.cfg.labels, self.cfg.hidden) != 0:
             raise RuntimeError("load_head: " + self._lib.s1_checkpoint_error().decode())
+
+    def cp_init(self, rank, world, uid, nccl_library=None):
+        """Join a context-parallel group of `world` processes (one per GPU) as `rank`."""
+        self._check(self._lib.s1_model_cp_init(self._h, (nccl_library or "").encode(), ctypes.c_char_p(uid), rank,
+                                               world), "cp_init")
+
+    def forward_cp(self, ids, start, hidden=False):
+        """This rank's piece of one prompt (positions from `start`): logits [labels] (and the
+        last hidden row) on the last rank, None on the others."""
+        a = np.ascontiguousarray(ids, np.int32)
+        logits = np.zeros(self.cfg.labels, np.float32)
+        hid = np.zeros(self.cfg.hidden, np.float32) if hidden else None
+        self._check(self._lib.s1_model_forward_cp(self._h, a.ctypes.data, len(a), start, logits.ctypes.data,
+                                                  hid.ctypes.data if hidden else None), "forward_cp")
+        return (logits, hid) if hidden else logits
 
     def init_random(self, seed=0, std=0.02):
         self._check(self._lib.s1_model_init_random(self._h, seed, std), "init_random")
