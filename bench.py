@@ -9,7 +9,9 @@ the C++ host and the sm_100a kernels, scored by the 8-label head on each final t
 Weak scaling: every rank processes its own batch of 32 requests with a full weight
 replica; no collective on the hot path. Prints one JSON line on rank 0. Rank 0 also
 times workload (b), one 32,768-token prefill (`long_prefill` in the line; `--no-long`
-skips it).
+skips it); with N > 1 GPUs every rank then runs the same prompt context-parallel, one
+piece per GPU with the per-layer state passed rank to rank over NCCL
+(`long_prefill_cp`).
 
 `--impl reference` times the reference's CPU path on the host cores instead: the numpy
 restatement of the same forward (the reference's prefill exists only as GPU code; its CPU
@@ -307,6 +309,43 @@ def long_prefill(model, torch, stream, steps=3):
             "logits": logits[0].round(4).tolist()}
 
 
+def long_prefill_cp(model, torch, dist, rank, world, stream, steps=3):
+    """Workload (b) over every rank of a multi-GPU run: the same 32,768-token prompt split in
+    order into one piece per GPU (64-token boundaries), context-parallel (per-layer GDN
+    state, conv history and attention K/V passed rank to rank over NCCL). Host ids in, the
+    last rank's logits out; CUDA events on each model stream, max over ranks."""
+    from s1omni import cp_unique_id
+    seq = long_request()
+    base = (LONG // world) // 64 * 64
+    lengths = [base] * (world - 1) + [LONG - base * (world - 1)]
+    start = base * rank
+    piece = seq[start:start + lengths[rank]]
+    uid = [cp_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(uid, src=0)
+    model.cp_init(rank, world, uid[0])
+    model.forward_cp(piece, start)  # warm-up
+    times, out = [], None
+    for _ in range(steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        out = model.forward_cp(piece, start)
+        e.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times.append(float(t))
+    logits = torch.tensor(out if rank == world - 1 else np.zeros(8, np.float32), device="cuda")
+    dist.broadcast(logits, src=world - 1)
+    ms = float(np.median(times))
+    lg = logits.cpu().numpy()
+    return {"workload": "27b-b-32k", "parallelism": f"context-parallel x{world}", "tokens": LONG,
+            "pieces": lengths, "value": LONG / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+            "warmup": 1, "seed": 5, "timing": "CUDA events on each rank's model stream, max over ranks, median",
+            "finite": bool(np.isfinite(lg).all()), "logits": lg.round(4).tolist()}
+
+
 def single_requests(n=16, seed=5):
     """Concurrency-1 workload of BASELINE's 27B config (a): one prompt per request."""
     rng = np.random.default_rng(seed)
@@ -386,6 +425,7 @@ def run_ours(args, rank, world, local):
     e2e = float(np.median(e2e_ms[1:]))
     lat = latency(model, args)
     long = long_prefill(model, torch, stream) if rank == 0 and not args.no_long else None
+    long_cp = long_prefill_cp(model, torch, dist, rank, world, stream) if dist and not args.no_long else None
     h2d = tokens * 4 + tokens * 32 * 2 * 2 + BATCH * 4
     d2h = BATCH * cfg.labels * 4
     tmax = torch.tensor([ms, e2e], device="cuda")
@@ -431,6 +471,7 @@ def run_ours(args, rank, world, local):
                                        f"(numpy float32 restatement), x16 periods"},
             "p50_decision_latency_ms": lat,
             "long_prefill": long,
+            "long_prefill_cp": long_cp,
             "clocks": clocks.summary(),
             "checks": {"finite_logits_no_fault": ok, "logits_sample": logits[:4].round(4).tolist()},
         }
