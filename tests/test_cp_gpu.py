@@ -1,8 +1,8 @@
-"""Context-parallel prefill on two GPUs (s1_model_forward_cp): a prompt split into two
-pieces on a 64-token boundary, per-layer GDN states, conv history and attention K/V
-passed from rank 0 to rank 1 over NCCL. The last rank's logits and final hidden row
-equal, bit for bit, those of the whole prompt on one GPU, and are within 2e-2 of the
-oracle. Skipped with fewer than two GPUs."""
+"""Context-parallel prefill (s1_model_forward_cp): a prompt split into pieces on 64-token
+boundaries, one rank per piece, per-layer GDN states, conv history and attention K/V
+passed rank to rank over NCCL. The last rank's logits and final hidden row equal, bit for
+bit, those of the whole prompt on one GPU, and are within 2e-2 of the oracle. Each case
+is skipped with fewer GPUs than pieces."""
 import json
 import os
 import socket
@@ -20,14 +20,16 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("pieces", ["256,192", "64,321"])
+@pytest.mark.parametrize("pieces", ["256,192", "64,321", "128,64,192,100"])
 def test_context_parallel_equals_one_gpu(pieces):
+    """Two ranks (first and last only), and four (middle ranks receive, append and send)."""
     import torch
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    world = len(pieces.split(","))
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     worker = os.path.join(os.path.dirname(os.path.abspath(__file__)), "cp_worker.py")
     env = dict(os.environ, CP_PIECES=pieces, NCCL_NVLS_ENABLE="0")
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2", "--master-addr",
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", str(world), "--master-addr",
            "127.0.0.1", "--master-port", str(_free_port()), worker]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
