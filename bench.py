@@ -311,14 +311,14 @@ def long_prefill(model, torch, stream, steps=3):
 
 def long_prefill_cp(model, torch, dist, rank, world, stream, steps=3):
     """Workload (b) over every rank of a multi-GPU run: the same 32,768-token prompt split in
-    order into one piece per GPU (64-token boundaries), context-parallel (per-layer GDN
+    order into one piece per GPU (64-token boundaries, sized for equal estimated work per
+    rank), context-parallel (per-layer GDN
     state, conv history and attention K/V passed rank to rank over NCCL). Host ids in, the
     last rank's logits out; CUDA events on each model stream, max over ranks."""
-    from s1omni import cp_unique_id
+    from s1omni import cp_pieces, cp_unique_id, preset
     seq = long_request()
-    base = (LONG // world) // 64 * 64
-    lengths = [base] * (world - 1) + [LONG - base * (world - 1)]
-    start = base * rank
+    lengths = cp_pieces(preset("27b"), LONG, world)  # work-balanced pieces on 64-token boundaries
+    start = sum(lengths[:rank])
     piece = seq[start:start + lengths[rank]]
     uid = [cp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)

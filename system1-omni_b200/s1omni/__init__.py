@@ -11,7 +11,7 @@ Thin ctypes layer over the two native libraries built in-tree by
 There is no fallback: a missing library raises at import of the binding.
 """
 from .cs1 import Cs1, Cs1Error, lib_path
-from .model import Config, Model, checkpoint_check, cp_unique_id, checkpoint_list, config_from_hf, preset, pack_ranges, shared_prefix
+from .model import Config, Model, checkpoint_check, cp_pieces, cp_unique_id, checkpoint_list, config_from_hf, preset, pack_ranges, shared_prefix
 
-__all__ = ["Cs1", "Cs1Error", "lib_path", "Config", "Model", "checkpoint_check", "checkpoint_list", "cp_unique_id", "config_from_hf", "preset",
+__all__ = ["Cs1", "Cs1Error", "lib_path", "Config", "Model", "checkpoint_check", "checkpoint_list", "cp_pieces", "cp_unique_id", "config_from_hf", "preset",
            "pack_ranges", "shared_prefix"]

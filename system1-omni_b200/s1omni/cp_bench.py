@@ -4,7 +4,9 @@ launch (one GPU each), 27B shape, random-init weights.
     python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 \\
         --master-port P -m s1omni.cp_bench [--tokens 32768] [--steps 3]
 
-The prompt is split into equal pieces on 64-token boundaries (rank order = prompt order);
+The prompt is split into pieces on 64-token boundaries (rank order = prompt order), sized
+so that every rank's estimated work is about the same (`cp_pieces`; `--equal` for equal
+pieces);
 each step is one forward_cp on every rank, timed by wall clock between barriers (host
 ids in, the last rank's logits out), max over ranks. Prints one JSON line on rank 0.
 """
@@ -18,7 +20,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from .model import Model, cp_unique_id, preset
+from .model import Model, cp_pieces, cp_unique_id, preset
 
 
 def main():
@@ -26,15 +28,16 @@ def main():
     ap.add_argument("--tokens", type=int, default=32768)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--preset", default="27b")
+    ap.add_argument("--equal", action="store_true", help="equal pieces instead of work-balanced ones")
     a = ap.parse_args()
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dist.init_process_group("gloo", timeout=timedelta(seconds=300))
     cfg = preset(a.preset)
-    base = (a.tokens // world) // 64 * 64
-    lengths = [base] * (world - 1) + [a.tokens - base * (world - 1)]
-    start = base * rank
+    lengths = cp_pieces(cfg, a.tokens, world) if not a.equal else \
+        [(a.tokens // world) // 64 * 64] * (world - 1) + [a.tokens - (a.tokens // world) // 64 * 64 * (world - 1)]
+    start = sum(lengths[:rank])
     ids = np.random.default_rng(5).integers(0, cfg.vocab, a.tokens).astype(np.int32)
     m = Model(cfg, device=local, max_tokens=lengths[rank] + 64, max_seqs=4)
     m.init_random(seed=1234, std=0.02)

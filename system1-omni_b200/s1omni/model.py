@@ -203,6 +203,39 @@ def checkpoint_check(folder, cfg):
         raise ValueError("checkpoint: " + lib.s1_checkpoint_error().decode())
 
 
+def cp_pieces(cfg, tokens, world, align=64):
+    """Piece lengths of a context-parallel split of one `tokens`-long prompt over `world`
+    ranks (in prompt order), on `align`-token boundaries, sized so that every rank's
+    estimated work is about the same: projection FLOPs in proportion to its tokens plus
+    causal attention FLOPs in proportion to its queries times the keys they see (all
+    earlier pieces and half of its own). The last rank takes the remainder."""
+    lin = cfg.projection_flops_per_token()
+    att = 4.0 * cfg.heads * cfg.head_dim * sum(1 for t in cfg.layer_types if t != "gdn")
+
+    def cost(start, n):
+        return lin * n + att * n * (start + n / 2.0)
+
+    total = cost(0, tokens)
+    lengths, start = [], 0
+    for r in range(world - 1):
+        left = world - r
+        target = cost(start, tokens - start) / left if r else total / world
+        lo, hi = 0, tokens - start
+        while lo < hi:  # largest aligned n with cost(start, n) <= target
+            mid = (lo + hi + 1) // 2
+            if cost(start, mid) <= target:
+                lo = mid
+            else:
+                hi = mid - 1
+        n = max(align, lo // align * align)
+        lengths.append(n)
+        start += n
+    lengths.append(tokens - start)
+    if lengths[-1] < align:
+        raise ValueError("prompt too short for this many pieces")
+    return lengths
+
+
 def cp_unique_id(nccl_library=None):
     """The 128-byte NCCL id of a context-parallel group, made on one rank and handed to
     every rank (for instance with torch.distributed.broadcast_object_list)."""
