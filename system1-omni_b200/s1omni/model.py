@@ -227,7 +227,10 @@ def cp_pieces(cfg, tokens, world, align=64):
                 lo = mid
             else:
                 hi = mid - 1
-        n = max(align, lo // align * align)
+        down = lo // align * align  # the aligned length whose cost is nearer the target
+        up = min(down + align, tokens - start - align)
+        n = up if up > down and abs(cost(start, up) - target) < abs(cost(start, down) - target) else down
+        n = max(align, n)
         lengths.append(n)
         start += n
     lengths.append(tokens - start)

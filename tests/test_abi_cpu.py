@@ -113,3 +113,23 @@ def test_model_create_reports_missing_library():
     from s1omni import Model, preset
     with pytest.raises(RuntimeError, match="dlopen"):
         Model(preset("tiny"), cs1_library="/nonexistent/libqwen3_5_cuda.so")
+
+
+def test_cp_pieces_balance_and_alignment():
+    """Context-parallel piece sizes: in order, on 64-token boundaries, summing to the prompt,
+    and each rank's estimated work (projections + causal attention) within one 64-token step
+    of the mean (2% at 32k tokens)."""
+    from s1omni import cp_pieces, preset
+    cfg = preset("27b")
+    lin = cfg.projection_flops_per_token()
+    att = 4.0 * cfg.heads * cfg.head_dim * sum(1 for t in cfg.layer_types if t != "gdn")
+    for tokens, world in ((32768, 2), (32768, 4), (32768, 8), (8192, 3)):
+        lengths = cp_pieces(cfg, tokens, world)
+        assert len(lengths) == world and sum(lengths) == tokens
+        assert all(n % 64 == 0 for n in lengths[:-1]) and lengths[-1] >= 64
+        starts = np.concatenate([[0], np.cumsum(lengths)[:-1]])
+        cost = [lin * n + att * n * (s + n / 2) for s, n in zip(starts, lengths)]
+        step = 64 / (tokens / world)  # relative size of one alignment step
+        assert max(cost) / np.mean(cost) < 1 + max(0.02, step), (tokens, world, lengths)
+    with pytest.raises(ValueError):
+        cp_pieces(cfg, 200, 4)
