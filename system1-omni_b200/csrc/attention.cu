@@ -743,11 +743,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             float m8[8];
 #pragma unroll
             for (int i = 0; i < 8; i++) m8[i] = -INFINITY;
-            if (full) {
+            if (full) {  // three-input max: 16 per chain instead of 32
 #pragma unroll
                 for (int c = 0; c < 4; c++)
 #pragma unroll
-                    for (int e = 0; e < 32; e++) m8[e & 7] = fmaxf(m8[e & 7], s[c][e]);
+                    for (int e = 0; e < 32; e += 16)
+#pragma unroll
+                        for (int i = 0; i < 8; i++) m8[i] = max3(m8[i], s[c][e + i], s[c][e + 8 + i]);
             } else {
 #pragma unroll
                 for (int c = 0; c < 4; c++)
@@ -793,9 +795,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             const float nm = m == -INFINITY ? 0.f : -m;
             uint8_t* prow = smem + OFF_P;
-            float l8[8];
+            float2 l2[4];  // row-sum chains of keys e = 2p, 2p + 1 (mod 8), in f32x2 pairs
 #pragma unroll
-            for (int i = 0; i < 8; i++) l8[i] = 0.f;
+            for (int i = 0; i < 4; i++) l2[i] = make_float2(0.f, 0.f);
+            const float2 sl22 = make_float2(sl2, sl2), nm2 = make_float2(nm, nm);
             uint32_t pk[32];  // PT: 64 keys of P as bf16 pairs (one tcgen05.st of 32 columns)
 #pragma unroll
             for (int c = 0; c < 4; c++) {
@@ -803,9 +806,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int g8 = 0; g8 < 4; g8++) {
                     float f[8];
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        f[e] = ex2(fmaf(s[c][g8 * 8 + e], sl2, nm));
-                        l8[e] += f[e];
+                    for (int e = 0; e < 8; e += 2) {
+                        const float2 t = fma2(make_float2(s[c][g8 * 8 + e], s[c][g8 * 8 + e + 1]), sl22, nm2);
+                        f[e] = ex2(t.x);
+                        f[e + 1] = ex2(t.y);
+                        l2[e >> 1] = add2(l2[e >> 1], make_float2(f[e], f[e + 1]));
                     }
                     if constexpr (PT) {
 #pragma unroll
@@ -822,7 +827,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (c & 1) tmem_st32(lane_addr + b * BN + (c >> 1) * 32, *reinterpret_cast<const float(*)[32]>(pk));
                 }
             }
-            l += ((l8[0] + l8[1]) + (l8[2] + l8[3])) + ((l8[4] + l8[5]) + (l8[6] + l8[7]));
+            l += ((l2[0].x + l2[0].y) + (l2[1].x + l2[1].y)) + ((l2[2].x + l2[2].y) + (l2[3].x + l2[3].y));
             if constexpr (PT)
                 tmem_st_wait();
             else

@@ -126,6 +126,12 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
         : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
     return d;
 }
+// Maximum of three (one instruction on sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
 // bf16 rounding of a pair (one paired conversion), back in fp32.
 __device__ __forceinline__ float2 rbf2(float2 v) { return __bfloat1622float2(__floats2bfloat162_rn(v.x, v.y)); }
 // SiLU of a pair from the identity y / (1 + 2^(-y log2 e)) with the hardware base-2
