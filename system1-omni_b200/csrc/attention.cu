@@ -125,7 +125,7 @@ __global__ void prep_kernel(const bf16* __restrict__ qg, const bf16* __restrict_
 // when PREP_UNITS divides Hq + Hk), the rotate-half sign folded into the sine, and the
 // norm and rotary products in packed f32x2 (lane-for-lane the scalar roundings).
 // Needs 16-byte aligned rotary tables and Hq + Hk >= 2.
-__global__ void prep_fast_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
+__global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
                                  const bf16* __restrict__ qw, const bf16* __restrict__ kw,
                                  const bf16* __restrict__ cosb, const bf16* __restrict__ sinb, bf16* __restrict__ q,
                                  bf16* __restrict__ gate, bf16* __restrict__ k, int T, int Hq, int Hk, int half,
@@ -167,27 +167,11 @@ __global__ void prep_fast_kernel(const bf16* __restrict__ qg, const bf16* __rest
             }
         }
     }
-    const int t_a = ti[0], t_b = ti[n - 1];
     const int f = d0 & (half - 1);  // half is a power of two (checked on the host)
-    Pack8 ca, sa, cb, sb;
+    Pack8 ca, sa;
     if (rotated) {
-        ca = ld8(cosb + (size_t)t_a * half + f);
-        sa = ld8(sinb + (size_t)t_a * half + f);
-        if (t_b != t_a) {
-            cb = ld8(cosb + (size_t)t_b * half + f);
-            sb = ld8(sinb + (size_t)t_b * half + f);
-        }
-    }
-    float2 wq[4], wk[4];  // 1 + w
-    {
-        float a[8], b[8];
-        unpack8(ld8(qw + d0), a);
-        unpack8(ld8(kw + d0), b);
-#pragma unroll
-        for (int p = 0; p < 4; p++) {
-            wq[p] = make_float2(1.f + a[2 * p], 1.f + a[2 * p + 1]);
-            wk[p] = make_float2(1.f + b[2 * p], 1.f + b[2 * p + 1]);
-        }
+        ca = ld8(cosb + (size_t)ti[0] * half + f);
+        sa = ld8(sinb + (size_t)ti[0] * half + f);
     }
     const float sgn = d0 < half ? -1.f : 1.f;  // rotate-half: -x2 for the first half, +x1 for the second
     float2 cs[4], sn[4];
@@ -214,9 +198,14 @@ __global__ void prep_fast_kernel(const bf16* __restrict__ qg, const bf16* __rest
         }
         const float inv = rsqrtf(warp_sum(ss) / DH + eps);
         const float2 inv2 = make_float2(inv, inv);
+        const Pack8 wv = ld8((is_q ? qw : kw) + d0);  // this unit's norm weight (L1-resident, 512 bytes)
 #pragma unroll
-        for (int p = 0; p < 4; p++) x[p] = rbf2(mul2(mul2(x[p], inv2), is_q ? wq[p] : wk[p]));
-        if (rotated && i > 0 && ti[i] != ti[i - 1]) rot_rows(cb, sb);  // the warp's second token
+        for (int p = 0; p < 4; p++) {
+            const float2 w = __bfloat1622float2(wv.h[p]);
+            x[p] = rbf2(mul2(mul2(x[p], inv2), make_float2(1.f + w.x, 1.f + w.y)));
+        }
+        if (rotated && i > 0 && ti[i] != ti[i - 1])  // the warp's second token: its rotary rows, on demand
+            rot_rows(ld8(cosb + (size_t)ti[i] * half + f), ld8(sinb + (size_t)ti[i] * half + f));
         Pack8 out;
 #pragma unroll
         for (int p = 0; p < 4; p++) {
