@@ -635,12 +635,7 @@ __global__ void __launch_bounds__(TP_THREADS, 2)
 //   VN   v_new^T bf16 [128 v][64 t] K-major                             16 KB
 //   one operand buffer: W = w^T [128 k][64 t] MN-major, QD [64 t][128 k] K-major
 //   (2 sub-tiles), P [64 t][64 j] K-major, KD [64 t][128 k] MN-major (2 blocks)   56 KB
-// EW = 4 epilogue warps (one thread per state row, two CTAs per SM) or EW = 8 (warps q and
-// q + 4 share lane quarter q: each takes half of a row's k columns in the state pass and
-// half of the chunk's tokens for v_new and o), which halves the per-thread work on the
-// chunk-serial path, for launches with fewer (head, sequence) CTAs than SMs.
-template <int EW>
-constexpr int scan_threads() { return EW * 32 + 32; }
+constexpr int SCAN_THREADS = 160;
 constexpr int SUB64 = 64 * 128;        // bytes of a [64 rows][64 bf16] tile
 constexpr int SUB128 = 128 * 128;      // bytes of a [128 rows][64 bf16] tile
 constexpr int OFF_ST = 0;
@@ -656,13 +651,9 @@ struct ScanMaps {
     CUtensorMap w, qd, p, kdt;
 };
 
-template <int EW>
-__global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
+__global__ void __launch_bounds__(SCAN_THREADS, 2)
     gdn_scan(const __grid_constant__ ScanMaps maps, Work ws, GdnTable tab, bf16* __restrict__ o, int H,
              const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out) {
-    constexpr int MW = EW;          // the TMA / MMA warp
-    constexpr int ET = EW * 32;     // epilogue threads
-    constexpr int QH = EW / 4;      // threads per state row (column halves)
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -683,14 +674,14 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
     if (threadIdx.x == 0) {
         mbar_init(full, 1);
         mbar_init(empty, 1);
-        mbar_init(s_ready, EW);  // one arrive per epilogue warp
+        mbar_init(s_ready, 4);  // one arrive per epilogue warp
         mbar_init(ws_done, 1);
-        mbar_init(vn_ready, EW);
+        mbar_init(vn_ready, 4);
         mbar_init(upd_done, 1);
         mbar_init(drain, 1);
         mbar_fence_init();
     }
-    if (warp == MW) {
+    if (warp == 4) {
         tmem_alloc(smem_u32(tmem_slot), 256);
         tmem_relinquish();
     }
@@ -701,7 +692,7 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
     grid_dep_wait();
     grid_dep_launch();
 
-    if (warp == MW) {
+    if (warp == 4) {
         if (lane == 0) {
             constexpr uint32_t ID64 = idesc(128, 64, AB_BF16);
             constexpr uint32_t ID64_BMN = idesc_major(128, 64, AB_BF16, 0, 1);
@@ -766,17 +757,14 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
             if (issued > 0) (void)mbar_wait(full, (uint32_t)(issued - 1) & 1u);
         }
     } else {
-        // Thread (v, hf): v = TMEM lane = row v of S^T and column v of o; hf = the half of the
-        // k columns (state pass) and of the chunk's tokens (v_new, o) it handles when EW = 8.
-        const int vcol = (warp & 3) * 32 + lane;
-        const int hf = QH == 2 ? warp >> 2 : 0;
-        const uint32_t lane_addr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        // Thread v = threadIdx.x owns TMEM lane v: row v of S^T and column v of o.
+        const int vcol = threadIdx.x;
+        const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
         {
             // initial state into TMEM (zero or s_in column v)
             const float* si = s_in ? s_in + (long)seq * s_in_stride + (size_t)h * K * V : nullptr;
 #pragma unroll
-            for (int qq = 0; qq < 4 / QH; qq++) {
-                const int q4 = hf * (4 / QH) + qq;
+            for (int q4 = 0; q4 < 4; q4++) {
                 float x[32];
 #pragma unroll
                 for (int i = 0; i < 32; i++) x[i] = si ? si[(size_t)(q4 * 32 + i) * V + vcol] : 0.f;
@@ -787,20 +775,18 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
         const bf16* UT = reinterpret_cast<const bf16*>(ws.ut);
         uint8_t* st_tile = smem + OFF_ST;
         uint8_t* vn_tile = smem + OFF_VN;
-        constexpr int UQ = 8 / QH;  // 16-byte pieces of this thread's part of the u^T row
-        uint4 ur4[UQ];
+        uint4 ur4[8];  // this chunk's u^T row (128 bytes)
         auto load_u = [&](int c) {
-            const uint4* ur = reinterpret_cast<const uint4*>(UT + ((slot0 + c) * V + vcol) * C) + hf * UQ;
+            const uint4* ur = reinterpret_cast<const uint4*>(UT + ((slot0 + c) * V + vcol) * C);
 #pragma unroll
-            for (int i = 0; i < UQ; i++) ur4[i] = ur[i];
+            for (int i = 0; i < 8; i++) ur4[i] = ur[i];
         };
         // Chunk c's pass over the state row: the bf16 copy the first MMAs read, then e^{last} S
         // written back for the update MMA; one arrive per warp on s_ready.
         auto state_pass = [&](int c) {
             const float dec = ws.decay[slot0 + c];
 #pragma unroll
-            for (int qq = 0; qq < 4 / QH; qq++) {
-                const int q4 = hf * (4 / QH) + qq;
+            for (int q4 = 0; q4 < 4; q4++) {
                 float x[32];
                 tmem_ld32(lane_addr + 128 + q4 * 32, x);
                 tmem_ld_wait();
@@ -831,16 +817,15 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
             // tcgen05.ld is warp-collective: the wait outcome is made warp-uniform
             bool ok = __all_sync(0xffffffffu, mbar_wait(ws_done, cp));
             tc_fence_after();
-            // v_new = bf16(u - wS), tokens [32 half, 32 half + 32)
+            // v_new = bf16(u - wS)
 #pragma unroll
-            for (int hh = 0; hh < 2 / QH; hh++) {
+            for (int half = 0; half < 2; half++) {
                 if (!ok) break;  // warp-uniform
-                const int half = hf + hh;
                 float ws_[32];
                 tmem_ld32(lane_addr + half * 32, ws_);
                 float u[32];
 #pragma unroll
-                for (int i = 0; i < 4; i++) unpack8(*reinterpret_cast<const Pack8*>(&ur4[hh * 4 + i]), u + i * 8);
+                for (int i = 0; i < 4; i++) unpack8(*reinterpret_cast<const Pack8*>(&ur4[half * 4 + i]), u + i * 8);
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -864,8 +849,7 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
             bf16* ost = reinterpret_cast<bf16*>(vn_tile);
             if (ok) {  // warp-uniform
 #pragma unroll
-                for (int hh = 0; hh < 2 / QH; hh++) {
-                    const int half = hf + hh;
+                for (int half = 0; half < 2; half++) {
                     float ov[32];
                     tmem_ld32(lane_addr + 64 + half * 32, ov);
                     tmem_ld_wait();
@@ -877,25 +861,24 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
                 load_u(c + 1);
                 state_pass(c + 1);
             }
-            if (bar_any(1, ET, !ok)) {
+            if (bar_any(1, 128, !ok)) {
                 atomicOr(&g_fault_word, FAULT_WAIT_EPILOGUE);
                 break;
             }
 #pragma unroll
-            for (int i = 0; i < 1024 / ET; i++) {
-                const int u = (int)threadIdx.x + i * ET;  // 16-byte unit: row u / 16, columns (u % 16) * 8
+            for (int i = 0; i < 8; i++) {
+                const int u = vcol + i * 128;  // 16-byte unit: row u / 16, columns (u % 16) * 8
                 const int t = u >> 4, v8 = (u & 15) * 8;
                 if (t < rows)
                     st8(o + ((size_t)(start + c * C + t) * H + h) * V + v8,
                         *reinterpret_cast<const Pack8*>(ost + t * V + v8));
             }
-            named_bar_sync(1, ET);  // the tile takes the next v_new
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the tile takes the next v_new
         }
         if (s_out) {
             float* so = s_out + (long)seq * (long)H * K * V + (size_t)h * K * V;
 #pragma unroll
-            for (int qq = 0; qq < 4 / QH; qq++) {
-                const int q4 = hf * (4 / QH) + qq;
+            for (int q4 = 0; q4 < 4; q4++) {
                 float x[32];
                 tmem_ld32(lane_addr + 128 + q4 * 32, x);
                 tmem_ld_wait();
@@ -907,7 +890,7 @@ __global__ void __launch_bounds__(EW * 32 + 32, EW == 4 ? 2 : 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == MW) {
+    if (warp == 4) {
         tc_fence_after();
         tmem_dealloc(tmem, 256);
     }
@@ -927,9 +910,7 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     static const cudaError_t configured = [] {
         cudaError_t e = cudaFuncSetAttribute(gdn_prep_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM);
         if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gdn_scan<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(gdn_scan<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM);
+            e = cudaFuncSetAttribute(gdn_scan, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM);
         return e;
     }();
     if (configured != cudaSuccess) return configured;
@@ -953,10 +934,7 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
     if (!r) r = host::make_map_2d(&maps.kdt, ws.kdt, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows64, K, K, 64, 64,
                                   CU_TENSOR_MAP_SWIZZLE_128B);
     if (r) return r;
-    // few (head, sequence) CTAs: one per SM with twice the epilogue threads
-    const bool wide = (long)H * seqs.count <= host::num_sms() && scan_wide_enabled();
-    return launch_pdl(wide ? gdn_scan<8> : gdn_scan<4>, dim3(H, seqs.count),
-                      dim3(wide ? scan_threads<8>() : scan_threads<4>()), SCAN_SMEM, st, maps, ws, tab,
+    return launch_pdl(gdn_scan, dim3(H, seqs.count), dim3(SCAN_THREADS), SCAN_SMEM, st, maps, ws, tab,
                       static_cast<bf16*>(o), H, static_cast<const float*>(s_in), s_in_stride,
                       static_cast<float*>(s_out));
 }

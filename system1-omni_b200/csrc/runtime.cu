@@ -74,14 +74,6 @@ bool conv_narrow() {
     return on;
 }
 
-bool scan_wide_enabled() {
-    static const bool on = [] {
-        const char* e = getenv("S1_SCAN_WIDE");
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
-
 bool legacy_elementwise() {
     static const bool on = [] {
         const char* e = getenv("S1_ELEM_LEGACY");
