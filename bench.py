@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 A step is one packed prefill of a batch of 32 single-candidate requests (workload (a)
-of BASELINE's 27B config: prompt lengths log-normal, median 800, sigma 0.6, clipped to
+of the 27B benchmark configuration: prompt lengths log-normal, median 800, sigma 0.6, clipped to
 1..8192; synthetic uniform token ids; random-init bf16 weights of the 27B shape) through
 the C++ host and the sm_100a kernels, scored by the 8-label head on each final token.
 Weak scaling: every rank processes its own batch of 32 requests with a full weight
@@ -36,7 +36,7 @@ UNIT = "tokens/s"
 BATCH = 32
 
 
-LONG = 32768  # workload (b) of BASELINE's 27B config: one 32,768-token prefill
+LONG = 32768  # workload (b) of the 27B benchmark configuration: one 32,768-token prefill
 
 
 def long_request(seed=5):
@@ -347,7 +347,7 @@ def long_prefill_cp(model, torch, dist, rank, world, stream, steps=3):
 
 
 def single_requests(n=16, seed=5):
-    """Concurrency-1 workload of BASELINE's 27B config (a): one prompt per request."""
+    """Concurrency-1 workload (a) of the 27B benchmark configuration: one prompt per request."""
     rng = np.random.default_rng(seed)
     x = np.exp(rng.normal(np.log(800.0), 0.6, n))
     lens = np.clip(np.round(x), 1, 8192).astype(np.int64)

@@ -1,5 +1,5 @@
 """Seeded synthetic inputs shared by the golden generator, the tests and the
-bench (test infrastructure only). BASELINE's workloads name no public suite;
+bench (test infrastructure only). The benchmark workloads name no public suite;
 these seeded generators stand in with its shapes and value distributions.
 """
 import numpy as np

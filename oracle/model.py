@@ -71,7 +71,7 @@ def hybrid_layers(n, interval=4):
 
 
 def preset(name):
-    """Named shapes: the three BASELINE model sizes and small test models."""
+    """Named shapes: the three benchmark model sizes (4B, 9B, 27B) and small test models."""
     if name == "4b":
         return Config(2560, 9216, hybrid_layers(32), 16, 32, 16, 4, 151936, name=name)
     if name == "9b":

@@ -75,7 +75,7 @@ def _hybrid(n, interval=4):
 
 
 def preset(name):
-    """BASELINE shapes (4B, 9B, 27B) and small test shapes."""
+    """The benchmark shapes (4B, 9B, 27B) and small test shapes."""
     table = {
         "4b": (2560, 9216, 32, 16, 32, 16, 4, 151936),
         "9b": (4096, 12288, 32, 16, 32, 16, 4, 151936),

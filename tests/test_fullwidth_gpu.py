@@ -1,4 +1,4 @@
-"""Whole-forward parity at the layer widths of the three BASELINE models over one 4-layer
+"""Whole-forward parity at the layer widths of the three benchmark models (4B, 9B, 27B) over one 4-layer
 period (3 GDN + 1 attention): 27B (hidden 5120, SwiGLU 17408, GDN 16/48 heads, attention
 24/4 heads x 256), 9B (4096, 12288, 16/32, 16/4) and 4B (2560, 9216, 16/32, 16/4).
 Config C2's shape (a 2,048-token shared prefix and 8 candidates of 32 tokens) is run at
@@ -7,7 +7,7 @@ the 4B widths through the shared-prefix path.
 The weights are drawn on the device by s1_model_init_random and read back with
 s1_model_get_weight, so the numpy oracle runs on exactly the weights the kernels use.
 
-Gates. At these widths the bf16 forward has a noise floor of the same size as BASELINE's
+Gates. At these widths the bf16 forward has a noise floor of the same size as the benchmark's
 2e-2 logit tolerance: the numpy restatement itself moves by up to 0.028 when only its
 GEMM accumulation changes from float32 to float64 (same weights and prompts, logits up
 to 3.8), and the reference's own CUDA library differs from it by 0.039 (9B widths) to
@@ -17,7 +17,7 @@ library and the restatement -- two faithful implementations of the same bf16 rou
 points -- is therefore measured in every run and used as the floor:
 * logits within max(2e-2, floor + 5e-3) absolute of the reference's own CUDA library
   (built from its sources by oracle/Makefile) driven by the same host with the same
-  weights -- BASELINE's 2e-2 wherever the forward itself is that stable;
+  weights -- the benchmark's 2e-2 wherever the forward itself is that stable;
 * logits no further from the numpy restatement than the reference library is, plus 1e-2
   (or within 6e-2 when the reference library was not built).
 """

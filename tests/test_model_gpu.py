@@ -1,7 +1,7 @@
 """Whole-forward parity of the B200 prefill host + kernels against the oracle.
 
 * logits of the seeded tiny hybrid model (3 GDN + 1 attention layer) within 2e-2
-  absolute of the numpy oracle (BASELINE's bf16 logit tolerance) and of Transformers'
+  absolute of the numpy oracle (the benchmark's bf16 logit tolerance) and of Transformers'
   own forward (golden hidden rows through the same head);
 * packed candidates == each candidate alone, bit for bit (per-sequence state isolation);
 * shared-prefix suffixes == the full prompt, bit for bit at a 64-aligned prefix;
