@@ -336,7 +336,7 @@ def long_prefill_cp(model, torch, dist, rank, world, stream, steps=3):
         t = torch.tensor([s.elapsed_time(e)], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         times.append(float(t))
-    logits = torch.tensor(out if rank == world - 1 else np.zeros(8, np.float32), device="cuda")
+    logits = torch.tensor(out if out is not None else np.zeros(8, np.float32), device="cuda")
     dist.broadcast(logits, src=world - 1)
     ms = float(np.median(times))
     lg = logits.cpu().numpy()

@@ -58,7 +58,7 @@ def main():
         t = torch.tensor([dt])
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         times.append(float(t))
-    logits = torch.tensor(out if rank == world - 1 else np.zeros(cfg.labels, np.float32))
+    logits = torch.tensor(out if out is not None else np.zeros(cfg.labels, np.float32))
     dist.broadcast(logits, src=world - 1)
     if rank == 0:
         ms = float(np.median(times)) * 1e3

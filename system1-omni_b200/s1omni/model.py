@@ -316,6 +316,7 @@ class Model:
         """Join a context-parallel group of `world` processes (one per GPU) as `rank`."""
         self._check(self._lib.s1_model_cp_init(self._h, (nccl_library or "").encode(), ctypes.c_char_p(uid), rank,
                                                world), "cp_init")
+        self._cp_last = rank == world - 1
 
     def forward_cp(self, ids, start, hidden=False):
         """This rank's piece of one prompt (positions from `start`): logits [labels] (and the
@@ -325,6 +326,8 @@ class Model:
         hid = np.zeros(self.cfg.hidden, np.float32) if hidden else None
         self._check(self._lib.s1_model_forward_cp(self._h, a.ctypes.data, len(a), start, logits.ctypes.data,
                                                   hid.ctypes.data if hidden else None), "forward_cp")
+        if not getattr(self, "_cp_last", False):
+            return (None, None) if hidden else None
         return (logits, hid) if hidden else logits
 
     def init_random(self, seed=0, std=0.02):
