@@ -48,12 +48,11 @@ __device__ __forceinline__ float block_sum(float x, float* scratch) {
     return t;
 }
 
-// PyTorch's float32 SiLU and sigmoid.
-__device__ __forceinline__ float silu(float x) { return x / (1.f + expf(-x)); }
 // SiLU with the hardware exp2 / reciprocal approximations (relative error ~1e-7, far
 // below the bf16 rounding that follows it) for the bandwidth-bound kernels, where the
 // accurate expf and IEEE division would make them instruction-bound.
 __device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.f + __expf(-x)); }
+// PyTorch's float32 sigmoid.
 __device__ __forceinline__ float sigmoid(float x) { return 1.f / (1.f + expf(-x)); }
 
 
@@ -151,6 +150,16 @@ __device__ __forceinline__ float2 sigmoid2_fast(float2 y) {
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(d.x));
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
     return r;
+}
+// The same SiLU for one value, operation for operation (so a scalar and a packed caller
+// round identically): the SwiGLU of the GEMM epilogues and of cs1_silu_mul.
+__device__ __forceinline__ float silu_hw(float y) {
+    constexpr float kLog2e = 1.4426950408889634f;
+    float e, r;
+    const float t = y * -kLog2e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(t));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.f));
+    return y * r;
 }
 __device__ __forceinline__ float2 silu2_fast(float2 y) {
     constexpr float kLog2e = 1.4426950408889634f;

@@ -185,7 +185,7 @@ __global__ void conv_scalar_kernel(const bf16* __restrict__ qkv, const bf16* __r
                 x = f32(history[(size_t)(3 - back + pos) * ld + c]);
             acc = fmaf(f32(w[c * 4 + j]), x, acc);
         }
-        const bf16 y = to_bf16(silu(rbf(acc)));
+        const bf16 y = to_bf16(silu_hw(rbf(acc)));
         if (c < key_dim)
             q[(size_t)t * key_dim + c] = y;
         else if (c < 2 * key_dim)
@@ -231,15 +231,14 @@ __global__ void silu_mul_vec_kernel(const bf16* __restrict__ gu, int ld, bf16* _
 #pragma unroll
         for (int r = 0; r < 2; r++)
             if (t0 + r < T) {
-                float g[8], u[8], o[8];
-                unpack8(gp[r], g);
-                unpack8(up[r], u);
+                Pack8 o;
 #pragma unroll
-                for (int e = 0; e < 8; e++) o[e] = silu(g[e]);
-                rbf8(o);
-#pragma unroll
-                for (int e = 0; e < 8; e++) o[e] *= u[e];
-                st8(out + (t0 + r) * I + j, pack8(o));
+                for (int p = 0; p < 4; p++) {  // bf16(bf16(silu(g)) * u), in f32x2 pairs
+                    const float2 y = mul2(rbf2(silu2_fast(__bfloat1622float2(gp[r].h[p]))),
+                                          __bfloat1622float2(up[r].h[p]));
+                    o.h[p] = __floats2bfloat162_rn(y.x, y.y);
+                }
+                st8(out + (t0 + r) * I + j, o);
             }
     }
 }
@@ -249,7 +248,7 @@ __global__ void silu_mul_scalar_kernel(const bf16* __restrict__ gu, int ld, bf16
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
         const long t = i / I;
         const int j = (int)(i % I);
-        out[i] = to_bf16(rbf(silu(f32(gu[t * ld + j]))) * f32(gu[t * ld + I + j]));
+        out[i] = to_bf16(rbf(silu_hw(f32(gu[t * ld + j]))) * f32(gu[t * ld + I + j]));
     }
 }
 

@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tmem_ld32(tcol + BN / 2 + c * 32, u);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; e++) g[e] = rbf(silu(rbf(g[e]))) * rbf(u[e]);
+                    for (int e = 0; e < 32; e++) g[e] = rbf(silu_hw(rbf(g[e]))) * rbf(u[e]);
                     store_block<EPI>(stg, g, p.y, p.ldy, row0, p.M, out_col0 + c * 32, p.N / 2, lane);
                 }
             } else {
@@ -479,7 +479,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     tmem_ld32(tcol + BN / 2 + c * 32, u);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; e++) g[e] = rbf(silu(rbf(g[e]))) * rbf(u[e]);
+                    for (int e = 0; e < 32; e++) g[e] = rbf(silu_hw(rbf(g[e]))) * rbf(u[e]);
                     store_block<EPI>(stg, g, p.y, p.ldy, row0, p.M, out_col0 + c * 32, p.N / 2, lane);
                 }
             } else {
@@ -711,7 +711,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tmem_ld32(lane_addr + acc * 256 + 128 + c * 32, u);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) v[i] = rbf(silu(rbf(v[i]))) * rbf(u[i]);
+                    for (int i = 0; i < 32; i++) v[i] = rbf(silu_hw(rbf(v[i]))) * rbf(u[i]);
                 } else {
                     tmem_ld_wait();
                 }
@@ -977,7 +977,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
                         const float o = f32(src[i * 32 + lane]);
-                        v[i] = q < 2 ? rbf(silu(rbf(v[i]))) * o : rbf(silu(o)) * rbf(v[i]);
+                        v[i] = q < 2 ? rbf(silu_hw(rbf(v[i]))) * o : rbf(silu_hw(o)) * rbf(v[i]);
                     }
                 }
                 // STORE: bf16(acc); RESIDUAL: bf16(acc), added to the residual below; SwiGLU: the output
@@ -1043,7 +1043,7 @@ __global__ void gemm_simt_kernel(const bf16* __restrict__ x, const bf16* __restr
     if constexpr (EPI == EPI_SWIGLU) {
         const int blk = n / 128, j = n % 128;
         const float g = rbf(dot(blk * 256 + j)), u = rbf(dot(blk * 256 + 128 + j));
-        y[(size_t)m * ldy + n] = to_bf16(rbf(silu(g)) * u);
+        y[(size_t)m * ldy + n] = to_bf16(rbf(silu_hw(g)) * u);
     } else if constexpr (EPI == EPI_RESIDUAL) {
         bf16* d = y + (size_t)m * ldy + n;
         *d = to_bf16(f32(*d) + rbf(dot(n)));

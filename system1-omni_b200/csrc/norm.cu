@@ -350,7 +350,7 @@ __global__ void gated_scalar_kernel(const bf16* __restrict__ x, const bf16* __re
     for (int i = lane; i < 128; i += 32) ss = fmaf(f32(x[base + i]), f32(x[base + i]), ss);
     const float inv = rsqrtf(warp_sum(ss) / 128.f + eps);
     for (int i = lane; i < 128; i += 32)
-        out[base + i] = to_bf16(rbf(f32(w[i]) * rbf(f32(x[base + i]) * inv)) * silu(f32(z[zb + i])));
+        out[base + i] = to_bf16(rbf(f32(w[i]) * rbf(f32(x[base + i]) * inv)) * silu_hw(f32(z[zb + i])));
 }
 
 bool vec_ok(int D, const void* a, const void* b, const void* c, const void* d) {
