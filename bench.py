@@ -464,7 +464,10 @@ def run_ours(args, rank, world, local):
                          "peak_kind": peak_kind + " burst bf16", "ms_per_launch": sw_ms,
                          "algorithmic_flops_per_launch": sw_flops, "traffic": sw_traffic,
                          "traffic_unit": "bytes per launch (ncu dram read + write)",
-                         "projection_set": {"shapes": len(per_shape), "tflops": tflops, "frac": tflops / peak_tf},
+                         "projection_set": {"shapes": len(per_shape), "tflops": tflops, "frac": tflops / peak_tf,
+                                            "per_shape": [{"epilogue": k, "n": n_, "k": k_, "ms": round(t_, 4),
+                                                           "tflops": round(2.0 * tokens * n_ * k_ / (t_ * 1e-3) / 1e12, 1)}
+                                                          for k, n_, k_, t_ in per_shape]},
                          "forward_projection_tflops": proj / (ms_max * 1e-3) / 1e12},
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
                              "sample": f"one {args.cpu_tokens}-token prompt, one 4-layer period of the 27B shape "
