@@ -120,6 +120,42 @@ def test_silu_mul_and_sigmoid_gate(cs1, stream):
     assert max_rel(host(xd), ops.sigmoid_gate(x, gate)) <= ULP
 
 
+def _ordered(b):
+    """bf16 bit patterns -> integers in value order (+0 and -0 both 0), so that the
+    difference of two is their distance in bf16 ulps."""
+    b = b.astype(np.int32)
+    return np.where(b & 0x8000, -(b & 0x7FFF), b)
+
+
+def test_silu_every_bf16_value(cs1, stream):
+    """cs1_silu_mul with up = 1 over every finite bf16 gate value, element by element,
+    against PyTorch's float32 SiLU rounded to bf16. The kernels' SiLU, x * rcp(1 + 2^(-x
+    log2 e)) on the hardware exp2 / reciprocal approximations, is within one bf16 ulp
+    everywhere except below -87.34, where 1 + e^-x exceeds 2^126, the flush-to-zero
+    reciprocal returns 0 and the result is a signed zero in place of a value of magnitude
+    below 1.1e-36."""
+    bits = np.arange(65536, dtype=np.uint32)
+    g = (bits << 16).view(np.float32)
+    g = g[np.isfinite(g)]
+    I = 256
+    T = (g.size + I - 1) // I
+    gate = np.zeros(T * I, np.float32)
+    gate[:g.size] = g
+    gu = np.concatenate([gate.reshape(T, I), np.ones((T, I), np.float32)], axis=1)
+    out = empty_bf16(T, I)
+    cs1.cs1_silu_mul(dev_bf16(gu), 2 * I, out, T, I, stream)
+    torch.cuda.synchronize()
+    got = out.reshape(-1)[:g.size].cpu().view(torch.int16).numpy().view(np.uint16)
+    want = torch.nn.functional.silu(torch.from_numpy(g)).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    dist = np.abs(_ordered(got) - _ordered(want))
+    tail = g < -87.34
+    assert dist[~tail].max() <= 1
+    assert np.all((got[tail] & 0x7FFF) == 0)
+    wv = (want[tail].astype(np.uint32) << 16).view(np.float32)
+    assert np.abs(wv).max() < 1.1e-36
+    assert np.mean(dist[~tail] == 0) > 0.99
+
+
 @pytest.mark.parametrize("T,Hq,Hk", [(1, 4, 2), (70, 24, 4), (300, 16, 4)])
 def test_attn_prep(cs1, stream, T, Hq, Hk):
     ld = Hq * 512 + 2 * Hk * 256
