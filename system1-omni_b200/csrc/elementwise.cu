@@ -51,11 +51,11 @@ __global__ void embed_kernel(const int32_t* __restrict__ ids, const Pack8* __res
     }
 }
 
-// Eight channels per thread over a run of CONV_ROWS consecutive rows: the weights are
-// loaded once and the three previous input rows slide through registers, so every input
-// row is read once. A run that crosses into a new sequence restarts its window from zeros
-// (or from the three rows of `history`, shared by every sequence).
-constexpr int CONV_ROWS = 64;
+// Channels per thread over a run of `run` consecutive rows: the weights are loaded once and
+// the three previous input rows slide through registers, so every input row is read once
+// (plus three rows of window per run). A run that crosses into a new sequence restarts its
+// window from zeros (or from the three rows of `history`, shared by every sequence). The
+// split into runs does not change any output bit.
 
 // NP channel pairs per thread: 4 (16-byte accesses) or 2 (8-byte accesses, about half the
 // registers, so more warps per SM keep loads in flight).
@@ -67,7 +67,7 @@ struct alignas(4 * NP) PackN {
 template <int NP>
 __global__ void __launch_bounds__(128, NP == 2 ? 8 : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
-                                bf16* __restrict__ v, int key_packs, int value_packs, SeqTable tab) {
+                                bf16* __restrict__ v, int key_packs, int value_packs, int run, SeqTable tab) {
     using P = PackN<NP>;
     constexpr int CH = 2 * NP;  // channels per thread
     grid_dep_wait();
@@ -97,8 +97,8 @@ __global__ void __launch_bounds__(128, NP == 2 ? 8 : 4) conv_vec_kernel(const bf
         dst_ld = value_packs * CH;
     }
     const int T = tab.offset[tab.count];
-    const int t_begin = blockIdx.y * CONV_ROWS;
-    const int t_end = min(T, t_begin + CONV_ROWS);
+    const int t_begin = blockIdx.y * run;
+    const int t_end = min(T, t_begin + run);
     if (t_begin >= T) return;
     int s = seq_of(tab, t_begin);
     int next = tab.offset[s + 1];
@@ -275,11 +275,20 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
         // threads per SM instead of 4), which keeps more rows in flight
         const bool narrow = conv_narrow() && key_dim % 4 == 0;
         const int cpt = narrow ? 4 : 8, tpacks = (2 * key_dim + value_dim) / cpt;
+        const long groups = (tpacks + 127) / 128;
+        // Runs of 64 rows, shortened (to 32, then 16) while the grid is below two waves of
+        // resident CTAs: a short prompt's CTAs each wait on a few batches of loads in series,
+        // so more and shorter runs finish sooner.
+        const long waves2 = 2L * sm_count() * (narrow ? 8 : 4);
+        int run = 64;
+        while (run > 16 && groups * ((T + run - 1) / run) < waves2 && (T + run / 2 - 1) / (run / 2) <= 65535)
+            run /= 2;
+        if ((T + run - 1) / run > 65535) return cudaErrorInvalidValue;
         return launch_pdl(narrow ? conv_vec_kernel<2> : conv_vec_kernel<4>,
-                          dim3((tpacks + 127) / 128, (T + CONV_ROWS - 1) / CONV_ROWS), dim3(128), 0, st,
+                          dim3((unsigned)groups, (T + run - 1) / run), dim3(128), 0, st,
                           static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
                           static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
-                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, tab);
+                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, run, tab);
     } else {
         const int ch = 2 * key_dim + value_dim;
         conv_scalar_kernel<<<dim3((ch + 127) / 128, rows), 128, 0, st>>>(

@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(NT) rms_kernel(bf16* __restrict__ res, const b
 // One warp per row for D <= 32 * 8 * PPL: every 16-byte pack of the row is loaded before
 // the warp reduces it (no block barrier), the weights sit in shared memory, and each warp
 // walks rows with a grid stride. The add variant keeps the bf16 sums packed in registers.
+// Up to RW_WARPS warps per CTA; fewer when the rows do not fill every SM (rms_warp_shape).
 constexpr int PPL = 20;  // packs per lane: D <= 5120
 constexpr int RW_WARPS = 8;
 template <bool Add>
@@ -79,8 +80,8 @@ __global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restric
     const int packs = D >> 3, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < packs; i += blockDim.x) wsm[i] = ld8(w + (size_t)i * 8);
     __syncthreads();
-    const int warps = gridDim.x * RW_WARPS;
-    for (int row = blockIdx.x * RW_WARPS + (threadIdx.x >> 5); row < rows; row += warps) {
+    const int cta_warps = blockDim.x >> 5, warps = gridDim.x * cta_warps;
+    for (int row = blockIdx.x * cta_warps + (threadIdx.x >> 5); row < rows; row += warps) {
         const size_t off = (size_t)row * D;
         Pack8 v[PPL];
         if constexpr (Add) {
@@ -139,22 +140,16 @@ __global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restric
     }
 }
 
-int sm_count() {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0, n = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) ==
-                                                      cudaSuccess && n > 0)
-            sms = n;
-        else
-            sms = 148;
-    }
-    return sms;
-}
-
-int rms_warp_grid(int rows) {
-    const int need = (rows + RW_WARPS - 1) / RW_WARPS;
-    return need < sm_count() * 8 ? need : sm_count() * 8;
+// Grid and block of rms_warp_kernel: RW_WARPS warps per CTA and at most 8 CTAs per SM
+// (grid stride beyond), or, when the rows are fewer than RW_WARPS per SM, ceil(rows / SMs)
+// warps per CTA, so that every SM takes a share instead of a few SMs taking 8 rows each.
+void rms_warp_shape(int rows, dim3& grid, dim3& block) {
+    const int sms = sm_count();
+    int w = (rows + sms - 1) / sms;
+    w = w < 1 ? 1 : w > RW_WARPS ? RW_WARPS : w;
+    const int need = (rows + w - 1) / w;
+    grid = dim3(need < sms * 8 ? need : sms * 8);
+    block = dim3(32 * w);
 }
 
 // Any D: scalar path, two passes over the row.
@@ -369,10 +364,12 @@ extern "C" int cs1_rms_norm(const void* x, const void* w, void* out, int rows, i
     auto X = static_cast<const bf16*>(x);
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
-    if (vec_ok(D, x, w, out, out) && D <= 256 * PPL)
-        return launch_pdl(rms_warp_kernel<false>, dim3(rms_warp_grid(rows)), dim3(RW_WARPS * 32), 0, st,
-                          static_cast<bf16*>(nullptr), static_cast<const bf16*>(nullptr), X, Wt, O, rows, D, eps);
-    else if (vec_ok(D, x, w, out, out))
+    if (vec_ok(D, x, w, out, out) && D <= 256 * PPL) {
+        dim3 grid, block;
+        rms_warp_shape(rows, grid, block);
+        return launch_pdl(rms_warp_kernel<false>, grid, block, 0, st, static_cast<bf16*>(nullptr),
+                          static_cast<const bf16*>(nullptr), X, Wt, O, rows, D, eps);
+    } else if (vec_ok(D, x, w, out, out))
         rms_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
     else
         rms_scalar_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
@@ -388,10 +385,12 @@ extern "C" int cs1_add_rms_norm(void* residual, const void* delta, const void* w
     auto Dl = static_cast<const bf16*>(delta);
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
-    if (vec_ok(D, residual, delta, w, out) && D <= 256 * PPL)
-        return launch_pdl(rms_warp_kernel<true>, dim3(rms_warp_grid(rows)), dim3(RW_WARPS * 32), 0, st, R, Dl,
-                          static_cast<const bf16*>(nullptr), Wt, O, rows, D, eps);
-    else if (vec_ok(D, residual, delta, w, out))
+    if (vec_ok(D, residual, delta, w, out) && D <= 256 * PPL) {
+        dim3 grid, block;
+        rms_warp_shape(rows, grid, block);
+        return launch_pdl(rms_warp_kernel<true>, grid, block, 0, st, R, Dl, static_cast<const bf16*>(nullptr), Wt,
+                          O, rows, D, eps);
+    } else if (vec_ok(D, residual, delta, w, out))
         rms_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
     else
         rms_scalar_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);

@@ -43,6 +43,7 @@ bool pdl_enabled();  // S1_PDL=0 turns the attribute off (plain stream order)
 bool legacy_elementwise();
 // S1_CONV_NARROW=0 runs the GDN conv with 8 channels per thread instead of 4.
 bool conv_narrow();
+int sm_count();  // multiprocessors of the current device (148 when the query fails)
 
 // Launch with the programmatic-serialisation attribute (see grid_dep_wait); the kernel
 // must call grid_dep_wait() before its first global-memory access. The attribute is set

@@ -74,6 +74,19 @@ bool conv_narrow() {
     return on;
 }
 
+int sm_count() {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0, n = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) ==
+                                                      cudaSuccess && n > 0)
+            sms = n;
+        else
+            sms = 148;
+    }
+    return sms;
+}
+
 bool legacy_elementwise() {
     static const bool on = [] {
         const char* e = getenv("S1_ELEM_LEGACY");

@@ -2,13 +2,14 @@
 profiler capture).
 
     cd system1-omni_b200 && python -m s1omni.forward_bench --preset 27b --lengths 771 \
-        [--graphs] [--steps 5] [--once]
+        [--graphs] [--steps 5] [--once] [--lib PATH]
 
 `--lengths` lists the prompt lengths packed into the one forward (uniform token ids,
 seed 0). Without `--graphs` every step is an eager forward through the C++ host (host ids
 in, host logits out), the concurrency-1 serving path; with `--graphs` the staged batch is
 replayed from a CUDA graph. Prints one JSON line (ms per forward, tokens/s, launches per
-forward). `--once` runs exactly one eager forward after the weight fill.
+forward). `--once` runs exactly one eager forward after the weight fill. `--lib` loads another
+build of libqwen3_5_cuda.so under the same host (A/B timing of two kernel builds).
 """
 import argparse
 import json
@@ -27,12 +28,13 @@ def main():
     ap.add_argument("--graphs", action="store_true")
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--once", action="store_true")
+    ap.add_argument("--lib", default=None)
     a = ap.parse_args()
     cfg = preset(a.preset)
     lengths = [int(x) for x in a.lengths.split(",")]
     rng = np.random.default_rng(0)
     seqs = [rng.integers(0, cfg.vocab, n).astype(np.int32) for n in lengths]
-    m = Model(cfg, device=0, max_tokens=sum(lengths) + 64, max_seqs=max(len(seqs), 1))
+    m = Model(cfg, device=0, max_tokens=sum(lengths) + 64, max_seqs=max(len(seqs), 1), cs1_library=a.lib)
     try:
         m.init_random(seed=1234, std=0.02)
         if a.once:
