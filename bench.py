@@ -107,11 +107,14 @@ def measured_peaks():
 
 
 # ------------------------------------------------------------------ CPU arm ----
-def cpu_sample(tokens=256, seed=0):
-    """Time the numpy restatement of one 4-layer period (3 GDN + 1 attention + MLPs) of
-    the 27B shape on one prompt of `tokens` tokens; return (tokens/s extrapolated to 64
-    layers, seconds, threads)."""
-    from threadpoolctl import threadpool_info
+_CPU_PERIOD = {}
+
+
+def cpu_period(seed=0):
+    """The 27B shape's 4-layer period (3 GDN + 1 attention + MLPs) for the numpy
+    restatement, with its random weights; built once per process."""
+    if seed in _CPU_PERIOD:
+        return _CPU_PERIOD[seed]
     from oracle import model as OM
     from oracle.bf16 import rnd
     cfg = OM.preset("27b")
@@ -131,7 +134,18 @@ def cpu_sample(tokens=256, seed=0):
                 x = x + np.float32(1)
             shared[key] = x if kind == "f32" else rnd(x)
         W[name] = shared[key]
-    ids = rng.integers(0, cfg.vocab, tokens)
+    _CPU_PERIOD[seed] = (cfg, W)
+    return _CPU_PERIOD[seed]
+
+
+def cpu_sample(tokens=256, seed=0):
+    """Time the numpy restatement of one 4-layer period (3 GDN + 1 attention + MLPs) of
+    the 27B shape on one prompt of `tokens` tokens (weights built beforehand, outside the
+    timed call); return (tokens/s extrapolated to 64 layers, seconds, threads)."""
+    from threadpoolctl import threadpool_info
+    from oracle import model as OM
+    cfg, W = cpu_period(seed)
+    ids = np.random.default_rng(seed + 1).integers(0, cfg.vocab, tokens)
     t0 = time.perf_counter()
     OM.run_sequence(cfg, W, ids, gdn_mode="fp32")
     dt = time.perf_counter() - t0
