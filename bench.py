@@ -460,7 +460,9 @@ def run_ours(args, rank, world, local):
         sw_traffic = (SWIGLU_TRAFFIC["bytes"] * tokens / SWIGLU_TRAFFIC["m"]) if SWIGLU_TRAFFIC["bytes"] else None
         value = total_tokens / (ms_max * 1e-3)
         proj = cfg.projection_flops_per_token() * tokens
-        cpu_v, cpu_dt, cpu_threads = cpu_sample(args.cpu_tokens) if not args.no_cpu else (None, 0.0, 0)
+        # the CPU baseline is timed at N = 1 only (rank 0 of a multi-GPU job skips it)
+        use_cpu = world == 1 and not args.no_cpu
+        cpu_v, cpu_dt, cpu_threads = cpu_sample(args.cpu_tokens) if use_cpu else (None, 0.0, 0)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
@@ -485,7 +487,7 @@ def run_ours(args, rank, world, local):
                          "forward_projection_tflops": proj / (ms_max * 1e-3) / 1e12},
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
                              "sample": f"one {args.cpu_tokens}-token prompt, one 4-layer period of the 27B shape "
-                                       f"(numpy float32 restatement), x16 periods"},
+                                       f"(numpy float32 restatement), x16 periods"} if use_cpu else None,
             "p50_decision_latency_ms": lat,
             "long_prefill": long,
             "long_prefill_cp": long_cp,
