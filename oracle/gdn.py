@@ -51,7 +51,9 @@ def _expand(q, k, H):
 
 def chunk_fp32(q, k, v, g, beta, scale, state=None, l2norm=True):
     """torch_chunk_gated_delta_rule restated (float32), with an optional initial
-    state [H,K,V]; returns float32 o and the final float32 state."""
+    state [H,K,V]; returns float32 o and the final float32 state. Third-party source:
+    transformers `models/qwen3_5/modeling_qwen3_5.py:234-311` (5.5.0 here; the reference
+    pins 5.17.0, `tests/qwen3_5/test_gdn_fp32.py:3,24`)."""
     T, H, D = v.shape
     q, k = _expand(q, k, H)
     if l2norm:

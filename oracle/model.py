@@ -157,7 +157,8 @@ class PrefixState:
 
 
 def run_sequence(cfg, W, ids, prefix=None, capture=False, gdn_mode="bf16"):
-    """Forward one sequence (optionally continuing a PrefixState).
+    """Forward one sequence (optionally continuing a PrefixState), in the layer order of
+    `run_with_attention` (`src/models/qwen3_5/native/src/model.rs:3178-3727`).
 
     gdn_mode: "bf16" -- the reference kernel's bf16 intermediates (the CUDA path's
     arithmetic); "fp32" -- float32 chunk form with float32 L2 norms (the FP32
@@ -245,8 +246,9 @@ def head(cfg, W, h):
 
 
 def forward_batch(cfg, W, seqs, gdn_mode="bf16"):
-    """Packed independent candidates: each sequence's positions restart at 0 and
-    its state starts at zero, so the packed result is the per-sequence result.
+    """Packed independent candidates (`model.rs:1548-1632`, `forward_batch_layout`):
+    each sequence's positions restart at 0 and its state starts at zero, so the packed
+    result is the per-sequence result.
     Returns (last hidden rows [n, H], logits [n, labels])."""
     last = np.stack([run_sequence(cfg, W, s, gdn_mode=gdn_mode)[0][-1] for s in seqs])
     return last, head(cfg, W, last)

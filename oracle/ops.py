@@ -11,11 +11,13 @@ from .bf16 import rnd
 
 
 def silu(x):
+    """PyTorch's float32 SiLU, x / (1 + e^-x) (`src/backends/cuda/qwen3_5/common.cuh:41`)."""
     x = np.asarray(x, dtype=np.float32)
     return (x / (np.float32(1) + np.exp(-x))).astype(np.float32)
 
 
 def sigmoid(x):
+    """PyTorch's float32 sigmoid, 1 / (1 + e^-x) (`common.cuh:42`)."""
     x = np.asarray(x, dtype=np.float32)
     return (np.float32(1) / (np.float32(1) + np.exp(-x))).astype(np.float32)
 
@@ -141,7 +143,7 @@ def attention_gated(q, k, v, gate, scale, prefix_k=None, prefix_v=None):
 
 
 def gemm(x, w):
-    """y = bf16(x @ w^T) with fp32 accumulation (`gemm.cu`, cs1_gemm)."""
+    """y = bf16(x @ w^T) with fp32 accumulation (`gemm.cu:318-463`, cs1_gemm)."""
     return rnd(np.asarray(x, np.float32) @ np.asarray(w, np.float32).T)
 
 

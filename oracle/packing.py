@@ -54,7 +54,9 @@ def shared_prefix(inputs, minimum=MAX_TOKENS // 2 + 1):
 
 
 def layout(lengths, prefix=0):
-    """Packed rows: offsets [n], positions [sum], last-token rows [n] (int64)."""
+    """Packed rows: offsets [n], positions [sum], last-token rows [n] (int64), as
+    `forward_batch_layout` builds them (`src/models/qwen3_5/native/src/model.rs:1548-1632`);
+    with a prefix, positions continue at its length (`model.rs:3240`)."""
     lengths = [int(x) for x in lengths]
     offsets = np.zeros(len(lengths), np.int64)
     if lengths:
