@@ -703,6 +703,12 @@ int run_head(Model* m, int n) {
 
 // Upload ids, per-row rotary tables and the last-token rows of a batch.
 int stage_inputs(Model* m, const int32_t* ids, const Batch& b) {
+    // Every id indexes the embedding table, so one out of range would read past it on the
+    // device: the batch is refused before anything is copied or launched.
+    for (size_t i = 0; i < b.rows; i++)
+        if (ids[i] < 0 || ids[i] >= m->cfg.vocab)
+            return fail(m, -1, "token id " + std::to_string(ids[i]) + " at row " + std::to_string(i) +
+                                   " is outside [0, vocab = " + std::to_string(m->cfg.vocab) + ")");
     const int half = m->cfg.rotary_half;
     const int n = (int)b.lengths.size();
     size_t maxpos = 0;

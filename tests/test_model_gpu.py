@@ -75,3 +75,23 @@ def test_graph_replay_equals_eager(tiny):
         m.set_graphs(False)
     assert np.array_equal(first, eager) and np.array_equal(second, eager)
     assert np.array_equal(replay_other, m.forward(other))
+
+
+def test_out_of_range_token_ids_are_refused(tiny):
+    """An id outside [0, vocab) would index past the embedding table on the device: the
+    host refuses the batch before any copy or launch, on every entry point, and the model
+    stays usable."""
+    cfg, W, m = tiny
+    rng = np.random.default_rng(6)
+    good = rng.integers(0, cfg.vocab, 40).astype(np.int32)
+    before = m.forward([good])
+    for bad_id in (cfg.vocab, -1):
+        bad = good.copy()
+        bad[17] = bad_id
+        with pytest.raises(RuntimeError, match="outside"):
+            m.forward([good, bad])
+        with pytest.raises(RuntimeError, match="outside"):
+            m.forward_shared(bad, [good])
+    from s1omni import Cs1
+    assert Cs1().cs1_fault_status(1) == 0
+    assert np.array_equal(m.forward([good]), before)
