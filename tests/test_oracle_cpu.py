@@ -63,6 +63,25 @@ def test_gdn_chunk_state_continuation():
     assert rel(np.concatenate([oa, ob]), o) <= 1e-6 and rel(sb, s) <= 1e-6
 
 
+def test_gdn_output_and_state_are_affine_in_the_initial_state():
+    """The chunked recurrence is affine in its initial state: with f(S) = (o, S_end) from
+    initial state S, f(a Sa + b Sb) - f(0) = a (f(Sa) - f(0)) + b (f(Sb) - f(0)). This is
+    the property that lets a piece of a prompt run before its initial state is known
+    (segments of one sequence corrected afterwards)."""
+    # weak decay, so that the initial state still shapes the final one after 193 tokens
+    q, k, v, g, beta = fixtures.grouped_inputs(9, T=193, H=4, HK=2, decay=0.02)
+    rng = np.random.default_rng(10)
+    sa, sb = (rng.standard_normal((4, 128, 128)).astype(np.float32) * np.float32(0.3) for _ in range(2))
+    a, b = np.float32(0.7), np.float32(-1.3)
+    f = {key: G.chunk_fp32(q, k, v, g, beta, SCALE, state=s) for key, s in
+         (("0", None), ("a", sa), ("b", sb), ("ab", a * sa + b * sb))}
+    for i in range(2):  # output rows, then the final state
+        base = f["0"][i].astype(np.float64)
+        lhs = f["ab"][i] - base
+        rhs = a * (f["a"][i] - base) + b * (f["b"][i] - base)
+        assert rel(lhs, rhs) <= 1e-5, (i, rel(lhs, rhs))
+
+
 def test_tiny_model_matches_transformers():
     gold = np.load(os.path.join(GOLD, "tiny_model.npz"))
     cfg = OM.preset("tiny")
