@@ -85,6 +85,14 @@ int s1_model_stage(void* model, const int32_t* ids, const size_t* lengths, size_
 int s1_model_run_staged(void* model);
 int s1_model_fetch_logits(void* model, float* logits);
 
+// Layers [first, last) of a packed batch, eagerly, starting from a given residual stream
+// instead of the embedding (layer-by-layer comparisons of two cs1 libraries or against an
+// oracle). residual: host bf16 bits [sum lengths, H], the stream entering layer `first`;
+// overwritten with the stream leaving layer last - 1. ids give the positions' rotary rows
+// and are range-checked as in s1_model_forward.
+int s1_model_run_layers(void* model, const int32_t* ids, const size_t* lengths, size_t count, int first, int last,
+                        uint16_t* residual);
+
 // CUDA graphs for repeated length vectors (default off): 0 = eager, 1 = capture/replay.
 int s1_model_set_graphs(void* model, int enabled);
 // The model's cudaStream_t (for timing with events on the launching stream).
@@ -110,6 +118,19 @@ int s1_model_cp_init(void* model, const char* nccl_library, const void* id, int 
 // of 64; every piece but the last a multiple of 64 long). logits [labels] and hidden [H]
 // are written on the last rank only.
 int s1_model_forward_cp(void* model, const int32_t* ids, size_t len, size_t start, float* logits, float* hidden);
+
+// Before any transfer, forward_cp has every rank check its own piece and exchange
+// (status, start, len) with the others (one NCCL all-gather); if any rank refuses, or the
+// pieces do not follow one another, every rank returns the same error. The two steps,
+// callable without a GPU:
+// the checks on one rank's piece: 0, or a negative code (-1 no ids, -2 length outside
+// [64, cap_tokens], -3 start not a multiple of 64, -4 a piece before the last not a
+// multiple of 64 long, -5 rank 0 not at position 0, -6 a token id outside [0, vocab));
+int s1_cp_piece_status(const int32_t* ids, size_t len, size_t start, int rank, int world, int vocab,
+                       size_t cap_tokens);
+// the verdict on all ranks' rows (status, start, len, 0) in rank order: 0, or -1 with the
+// reason written to msg (capacity cap).
+int s1_cp_agree(const int64_t* table, int world, char* msg, size_t cap);
 
 // ---- checkpoints (src/models/qwen3_5/native/src/model.rs:96-226, 267-397) ----
 // A Hugging Face Qwen3.5 config.json (or its text_config) as an s1_config; layer_types
@@ -141,6 +162,17 @@ int s1_pack_ranges(const size_t* lengths, size_t count, size_t max_sequences, si
 // Shared prefix of 2..16 candidates (batching.rs:29-49): the common prefix floored to a
 // multiple of 64, or 0 if under 512 or if any candidate is shorter than `minimum`.
 size_t s1_shared_prefix(const int32_t* const* ids, const size_t* lengths, size_t count, size_t minimum);
+
+// ---- request dispatch over GPUs (host integer/float logic, no GPU) ----
+// Each GPU holds a full weight replica and serves the requests given to it; requests go
+// to ranks longest processing time first by token cost (s1omni.request_cost): requests
+// in decreasing cost, each to the least-loaded rank (ties: lower index / lower rank).
+// Writes rank_of[n] and, if non-null, the per-rank cost totals loads[ranks]. Returns 0,
+// or -1 for ranks < 1 or a negative / non-finite cost. Replaces the reference's
+// per-worker grouping of queued requests (src/runtime/src/batching.rs:94-125,
+// src/models/open_jev/native/src/executor/batched.rs:28-31) one level up: across
+// the per-GPU workers.
+int s1_dispatch_lpt(const double* costs, size_t n, int ranks, int* rank_of, double* loads);
 
 #ifdef __cplusplus
 }

@@ -156,85 +156,141 @@ class PrefixState:
         self.length = 0
 
 
-def run_sequence(cfg, W, ids, prefix=None, capture=False, gdn_mode="bf16"):
+def _attention_f64(q, k, v, gate, scale, prefix_k=None, prefix_v=None):
+    """Causal GQA attention in float64 with unrounded probabilities (the op's exact value;
+    only its output is rounded): the `precise` variant of `ops.attention_gated`."""
+    S, Hq, Dh = q.shape
+    if prefix_k is not None:
+        k = np.concatenate([prefix_k, k], 0)
+        v = np.concatenate([prefix_v, v], 0)
+    P = k.shape[0] - S
+    group = Hq // k.shape[1]
+    mask = np.arange(P + S)[None, :] <= (P + np.arange(S))[:, None]
+    out = np.zeros((S, Hq, Dh))
+    for h in range(Hq):
+        kh = h // group
+        s = (q[:, h, :].astype(np.float64) @ k[:, kh, :].astype(np.float64).T) * float(scale)
+        s = np.where(mask, s, -np.inf)
+        e = np.exp(s - s.max(-1, keepdims=True))
+        out[:, h, :] = (e / e.sum(-1, keepdims=True)) @ v[:, kh, :].astype(np.float64)
+    att = rnd(out.astype(np.float32))
+    return rnd(att * rnd(ops.sigmoid(gate.reshape(S, Hq, Dh))))
+
+
+def _gemm64(x, w):
+    """y = bf16(x @ w^T) accumulated in float64 (the `precise` variant of `ops.gemm`)."""
+    return rnd((np.asarray(x, np.float64) @ np.asarray(w, np.float64).T).astype(np.float32))
+
+
+def _layer(cfg, W, i, res, x, cos, sin, prefix, cap, gi, ai, gdn_mode, precise):
+    """Layer i of `run_with_attention` (`model.rs:3308-3723`): the token mixer (GDN or
+    gated attention), its residual add, the SwiGLU MLP and its residual add, each
+    residual add followed by the next RMSNorm. Returns (res, x)."""
+    T = res.shape[0]
+    gemm = _gemm64 if precise else ops.gemm
+    scale_gdn = np.float32(cfg.lin_k_dim ** -0.5)
+    scale_attn = np.float32(cfg.head_dim ** -0.5)
+    p = f"l{i}."
+    if cfg.layer_types[i] == "gdn":
+        w_in = np.concatenate([W[p + "in_qkv"], W[p + "in_z"], W[p + "in_b"], W[p + "in_a"]], 0)
+        y = gemm(x, w_in)
+        qkv = y[:, :cfg.conv_dim]
+        z = y[:, cfg.conv_dim:cfg.conv_dim + cfg.value_dim]
+        b = y[:, cfg.conv_dim + cfg.value_dim:cfg.conv_dim + cfg.value_dim + cfg.lin_v_heads]
+        a = y[:, cfg.conv_dim + cfg.value_dim + cfg.lin_v_heads:]
+        hist = prefix.conv_tail[gi] if prefix is not None else None
+        q, k, v = ops.gdn_conv(qkv, W[p + "conv"], cfg.key_dim, cfg.value_dim, history=hist)
+        beta, g = ops.gdn_gates(b, a, W[p + "A_log"], W[p + "dt_bias"])
+        q = q.reshape(T, cfg.lin_k_heads, cfg.lin_k_dim)
+        k = k.reshape(T, cfg.lin_k_heads, cfg.lin_k_dim)
+        v = v.reshape(T, cfg.lin_v_heads, cfg.lin_v_dim)
+        s_in = prefix.gdn_state[gi] if prefix is not None else None
+        if precise:
+            o, s_out = G.recurrent_f64(q, k, v, g, beta, float(scale_gdn), state=s_in)
+            o = o.astype(np.float32)
+        elif gdn_mode == "bf16":
+            o, s_out = G.chunk_bf16(q, k, v, g, beta, scale_gdn, state=s_in)
+        elif gdn_mode == "hf":
+            o, s_out = G.chunk_fp32(G.l2norm_bf16(q), G.l2norm_bf16(k), v, g, beta, scale_gdn,
+                                    state=s_in, l2norm=False)
+        else:
+            o, s_out = G.chunk_fp32(q, k, v, g, beta, scale_gdn, state=s_in)
+        o = rnd(o)
+        ln = ops.gated_rms_norm(o, z, W[p + "norm"], cfg.eps)
+        delta = gemm(ln, W[p + "out"])
+        if cap is not None:
+            cap.gdn_state.append(s_out)
+            full = qkv if hist is None else np.concatenate([hist, qkv], 0)
+            tail = np.zeros((3, cfg.conv_dim), np.float32)
+            n = min(3, full.shape[0])
+            tail[3 - n:] = full[full.shape[0] - n:]
+            cap.conv_tail.append(tail)
+    else:
+        w_in = np.concatenate([W[p + "q"], W[p + "k"], W[p + "v"]], 0)
+        y = gemm(x, w_in)
+        qg = y[:, :cfg.attn_q]
+        kr = y[:, cfg.attn_q:cfg.attn_q + cfg.kv_heads * cfg.head_dim]
+        vr = y[:, cfg.attn_q + cfg.kv_heads * cfg.head_dim:].reshape(T, cfg.kv_heads, cfg.head_dim)
+        q, gate, k = ops.attn_prep(qg, kr, W[p + "q_norm"], W[p + "k_norm"], cos, sin,
+                                   cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rotary_half, cfg.eps)
+        pk = prefix.k[ai] if prefix is not None else None
+        pv = prefix.v[ai] if prefix is not None else None
+        if precise:
+            att = _attention_f64(q, k, vr, gate, scale_attn, pk, pv)
+        else:
+            att = ops.attention_gated(q, k, vr, gate, scale_attn, pk, pv)
+        delta = gemm(att.reshape(T, -1), W[p + "o"])
+        if cap is not None:
+            cap.k.append(k if pk is None else np.concatenate([pk, k], 0))
+            cap.v.append(vr if pv is None else np.concatenate([pv, vr], 0))
+    res, x = ops.add_rms_norm(res, delta, W[p + "post_norm"], cfg.eps)
+    gu = gemm(x, np.concatenate([W[p + "gate"], W[p + "up"]], 0))
+    act = ops.silu_mul(gu, cfg.intermediate)
+    delta = gemm(act, W[p + "down"])
+    nxt = W[f"l{i + 1}.input_norm"] if i + 1 < len(cfg.layer_types) else W["final_norm"]
+    return ops.add_rms_norm(res, delta, nxt, cfg.eps)
+
+
+def run_sequence(cfg, W, ids, prefix=None, capture=False, gdn_mode="bf16", precise=False):
     """Forward one sequence (optionally continuing a PrefixState), in the layer order of
     `run_with_attention` (`src/models/qwen3_5/native/src/model.rs:3178-3727`).
 
     gdn_mode: "bf16" -- the reference kernel's bf16 intermediates (the CUDA path's
     arithmetic); "fp32" -- float32 chunk form with float32 L2 norms (the FP32
     operator); "hf" -- float32 chunk form after Transformers' bfloat16 L2 norm.
+    precise: every projection accumulated in float64, the GDN as the float64 token
+    recurrence and attention in float64 with unrounded probabilities; each op's output
+    is rounded to bf16 at the same points as in the kernels (the exact value of every
+    op, so the distance of a kernel from it is that kernel's own arithmetic error).
 
     Returns (final-norm hidden rows [T, H], PrefixState or None). Positions start
     at prefix.length (0 without a prefix)."""
     T = len(ids)
-    H = cfg.hidden
     P = prefix.length if prefix is not None else 0
     cos, sin = rotary_tables(np.arange(P, P + T), cfg.rotary_half, cfg.theta)
-    scale_gdn = np.float32(cfg.lin_k_dim ** -0.5)
-    scale_attn = np.float32(cfg.head_dim ** -0.5)
     cap = PrefixState() if capture else None
     res = ops.embed(ids, W["embed"])
     x = ops.rms_norm(res, W["l0.input_norm"], cfg.eps)
     gi = ai = 0
     for i, t in enumerate(cfg.layer_types):
-        p = f"l{i}."
-        if t == "gdn":
-            w_in = np.concatenate([W[p + "in_qkv"], W[p + "in_z"], W[p + "in_b"], W[p + "in_a"]], 0)
-            y = ops.gemm(x, w_in)
-            qkv = y[:, :cfg.conv_dim]
-            z = y[:, cfg.conv_dim:cfg.conv_dim + cfg.value_dim]
-            b = y[:, cfg.conv_dim + cfg.value_dim:cfg.conv_dim + cfg.value_dim + cfg.lin_v_heads]
-            a = y[:, cfg.conv_dim + cfg.value_dim + cfg.lin_v_heads:]
-            hist = prefix.conv_tail[gi] if prefix is not None else None
-            q, k, v = ops.gdn_conv(qkv, W[p + "conv"], cfg.key_dim, cfg.value_dim, history=hist)
-            beta, g = ops.gdn_gates(b, a, W[p + "A_log"], W[p + "dt_bias"])
-            q = q.reshape(T, cfg.lin_k_heads, cfg.lin_k_dim)
-            k = k.reshape(T, cfg.lin_k_heads, cfg.lin_k_dim)
-            v = v.reshape(T, cfg.lin_v_heads, cfg.lin_v_dim)
-            s_in = prefix.gdn_state[gi] if prefix is not None else None
-            if gdn_mode == "bf16":
-                o, s_out = G.chunk_bf16(q, k, v, g, beta, scale_gdn, state=s_in)
-            elif gdn_mode == "hf":
-                o, s_out = G.chunk_fp32(G.l2norm_bf16(q), G.l2norm_bf16(k), v, g, beta, scale_gdn,
-                                        state=s_in, l2norm=False)
-            else:
-                o, s_out = G.chunk_fp32(q, k, v, g, beta, scale_gdn, state=s_in)
-            o = rnd(o)
-            ln = ops.gated_rms_norm(o, z, W[p + "norm"], cfg.eps)
-            delta = ops.gemm(ln, W[p + "out"])
-            if cap is not None:
-                cap.gdn_state.append(s_out)
-                full = qkv if hist is None else np.concatenate([hist, qkv], 0)
-                tail = np.zeros((3, cfg.conv_dim), np.float32)
-                n = min(3, full.shape[0])
-                tail[3 - n:] = full[full.shape[0] - n:]
-                cap.conv_tail.append(tail)
-            gi += 1
-        else:
-            w_in = np.concatenate([W[p + "q"], W[p + "k"], W[p + "v"]], 0)
-            y = ops.gemm(x, w_in)
-            qg = y[:, :cfg.attn_q]
-            kr = y[:, cfg.attn_q:cfg.attn_q + cfg.kv_heads * cfg.head_dim]
-            vr = y[:, cfg.attn_q + cfg.kv_heads * cfg.head_dim:].reshape(T, cfg.kv_heads, cfg.head_dim)
-            q, gate, k = ops.attn_prep(qg, kr, W[p + "q_norm"], W[p + "k_norm"], cos, sin,
-                                       cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.rotary_half, cfg.eps)
-            pk = prefix.k[ai] if prefix is not None else None
-            pv = prefix.v[ai] if prefix is not None else None
-            att = ops.attention_gated(q, k, vr, gate, scale_attn, pk, pv)
-            delta = ops.gemm(att.reshape(T, -1), W[p + "o"])
-            if cap is not None:
-                cap.k.append(k if pk is None else np.concatenate([pk, k], 0))
-                cap.v.append(vr if pv is None else np.concatenate([pv, vr], 0))
-            ai += 1
-        res, x = ops.add_rms_norm(res, delta, W[p + "post_norm"], cfg.eps)
-        gu = ops.gemm(x, np.concatenate([W[p + "gate"], W[p + "up"]], 0))
-        act = ops.silu_mul(gu, cfg.intermediate)
-        delta = ops.gemm(act, W[p + "down"])
-        nxt = W[f"l{i + 1}.input_norm"] if i + 1 < len(cfg.layer_types) else W["final_norm"]
-        res, x = ops.add_rms_norm(res, delta, nxt, cfg.eps)
+        res, x = _layer(cfg, W, i, res, x, cos, sin, prefix, cap, gi, ai, gdn_mode, precise)
+        gi, ai = (gi + 1, ai) if t == "gdn" else (gi, ai + 1)
     if cap is not None:
         cap.length = P + T
     return x, cap
+
+
+def run_layers(cfg, W, ids, first, last, res, gdn_mode="bf16", precise=False):
+    """Layers [first, last) of one sequence (positions from 0) from the residual stream
+    `res` [T, H] entering layer `first`; returns the stream leaving layer last - 1 (the
+    counterpart of the host's s1_model_run_layers, for layer-by-layer comparisons).
+    W needs only the parameters of those layers (and the next input norm)."""
+    cos, sin = rotary_tables(np.arange(len(ids)), cfg.rotary_half, cfg.theta)
+    res = np.asarray(res, np.float32)
+    x = ops.rms_norm(res, W[f"l{first}.input_norm"], cfg.eps)
+    for i in range(first, last):
+        res, x = _layer(cfg, W, i, res, x, cos, sin, None, None, 0, 0, gdn_mode, precise)
+    return res
 
 
 def head(cfg, W, h):

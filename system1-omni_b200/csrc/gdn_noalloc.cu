@@ -13,6 +13,9 @@
 // code the array's name is only a host-side stand-in, so the device address comes from
 // cudaGetSymbolAddress, once per device, with that device current, on the first call
 // on that device (that first call should therefore come before any stream capture).
+// The address is kept for the life of the process: a cudaDeviceReset of a device while
+// this library is loaded leaves it stale, so a process that resets a device must not call
+// this entry point on it again.
 #include <mutex>
 
 #include "gdn.cuh"

@@ -215,6 +215,7 @@ struct Nccl {
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     ncclResult_t (*send)(const void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*recv)(void*, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
     ncclResult_t (*group_start)() = nullptr;
     ncclResult_t (*group_end)() = nullptr;
     const char* (*error_string)(ncclResult_t) = nullptr;
@@ -239,6 +240,7 @@ bool load_nccl(const char* path, Nccl& n, std::string& err) {
     sym("ncclCommDestroy", n.comm_destroy);
     sym("ncclSend", n.send);
     sym("ncclRecv", n.recv);
+    sym("ncclAllGather", n.all_gather);
     sym("ncclGroupStart", n.group_start);
     sym("ncclGroupEnd", n.group_end);
     sym("ncclGetErrorString", n.error_string);
@@ -281,6 +283,7 @@ struct Model {
     ncclComm_t comm = nullptr;
     int cp_rank = 0, cp_world = 1;
     uint8_t* cp_state = nullptr;  // this rank's final GDN state of the current layer, sent on
+    int64_t* cp_table = nullptr;  // (status, start, len, 0) of every rank, then this rank's own row
     // staged batch for run_staged
     Batch staged;
     bool have_staged = false;
@@ -455,8 +458,12 @@ int cp_xfer(Model* m, const void* send, size_t send_bytes, void* recv, size_t re
     return 0;
 }
 
-int run_layers(Model* m, const Batch& b) {
+// Layers [first, last) of a staged batch. From layer 0 the residual stream starts at the
+// embedding of the staged ids; from a later layer it is whatever s_res holds (a
+// residual stream handed in by s1_model_run_layers).
+int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
     const s1_config& c = m->cfg;
+    if (last < 0) last = c.n_layers;
     const int T = (int)b.rows;
     const int n = (int)b.lengths.size();
     std::vector<size_t> offs(n + 1, 0);
@@ -465,15 +472,19 @@ int run_layers(Model* m, const Batch& b) {
     const float attn_scale = 1.0f / std::sqrt((float)c.head_dim);
     const bool suffix = b.prefix > 0 && !b.capture;
     const bool cp_send = b.cp && m->cp_rank + 1 < m->cp_world, cp_recv = b.cp && m->cp_rank > 0;
+    if (first == 0) {
+        m->launches++;
+        CK(m->api.embed(static_cast<const int32_t*>((const void*)m->S(m->s_ids)), m->W(m->embed), m->S(m->s_res), T,
+                        c.hidden, m->stream),
+           "embed");
+    }
     m->launches++;
-    CK(m->api.embed(static_cast<const int32_t*>((const void*)m->S(m->s_ids)), m->W(m->embed), m->S(m->s_res), T,
-                    c.hidden, m->stream),
-       "embed");
-    m->launches++;
-    CK(m->api.rms_norm(m->S(m->s_res), m->W(m->layers[0].input_norm), m->S(m->s_x), T, c.hidden, c.eps, m->stream),
+    CK(m->api.rms_norm(m->S(m->s_res), m->W(m->layers[first].input_norm), m->S(m->s_x), T, c.hidden, c.eps,
+                       m->stream),
        "input norm");
-    int gi = 0, ai = 0;
-    for (int li = 0; li < c.n_layers; li++) {
+    int gi = 0, ai = 0;  // index of the layer among the GDN / attention layers (prefix buffers)
+    for (int li = 0; li < first; li++) (m->types[li] == 0 ? gi : ai)++;
+    for (int li = first; li < last; li++) {
         const Layer& L = m->layers[li];
         if (L.type == 0) {
             CK(gemm_store(m, m->s_x, L.in_proj, m->s_gdn_in, T, m->gdn_in, c.hidden), "gdn input projection");
@@ -785,9 +796,22 @@ int execute(Model* m, const Batch& b, bool head) {
     return 0;
 }
 
+// Destroy every cached graph: a captured graph holds the device addresses it ran on.
+void drop_graphs(Model* m) {
+    for (auto& kv : m->graph_cache) m->api.graph_destroy(kv.second);
+    m->graph_cache.clear();
+    m->graph_order.clear();
+}
+
 int ensure_prefix(Model* m, int P) {
     if (m->prefix_buf && P <= m->prefix_len) return 0;
-    if (m->prefix_buf) m->api.free_(m->prefix_buf);
+    if (m->prefix_buf) {
+        // Graphs of suffix passes read the prefix buffer being freed: replaying one would
+        // touch freed device memory, so they go with it (after the stream has drained).
+        CK(m->api.stream_sync(m->stream), "sync before prefix reallocation");
+        drop_graphs(m);
+        m->api.free_(m->prefix_buf);
+    }
     m->prefix_buf = nullptr;
     const s1_config& c = m->cfg;
     size_t at = 0;
@@ -916,12 +940,13 @@ __attribute__((visibility("default"))) void s1_model_destroy(void* mp) {
     auto* m = static_cast<Model*>(mp);
     if (!m) return;
     if (m->stream) m->api.stream_sync(m->stream);
-    for (auto& kv : m->graph_cache) m->api.graph_destroy(kv.second);
+    drop_graphs(m);
     if (m->gemm) m->api.gemm_destroy(m->gemm);
     if (m->arena) m->api.free_(m->arena);
     if (m->scratch) m->api.free_(m->scratch);
     if (m->prefix_buf) m->api.free_(m->prefix_buf);
     if (m->cp_state) m->api.free_(m->cp_state);
+    if (m->cp_table) m->api.free_(m->cp_table);
     if (m->comm) m->nccl.comm_destroy(m->comm);
     if (m->stream) m->api.stream_destroy(m->stream);
     // the library stays loaded: CUDA state it owns must outlive this model
@@ -1072,6 +1097,25 @@ __attribute__((visibility("default"))) int s1_model_forward(void* mp, const int3
     return read_outputs(m, b, logits, hidden);
 }
 
+__attribute__((visibility("default"))) int s1_model_run_layers(void* mp, const int32_t* ids, const size_t* lengths,
+                                                              size_t count, int first, int last, uint16_t* residual) {
+    auto* m = static_cast<Model*>(mp);
+    if (!m || !ids || !residual) return -1;
+    if (first < 0 || last <= first || last > m->cfg.n_layers) return fail(m, -1, "layer range out of bounds");
+    Batch b;
+    int rc = check_batch(m, lengths, count, b);
+    if (rc) return rc;
+    rc = stage_inputs(m, ids, b);
+    if (rc) return rc;
+    const size_t bytes = b.rows * (size_t)m->cfg.hidden * 2;
+    CK(m->api.upload(m->S(m->s_res), residual, bytes, m->stream), "upload residual");
+    m->launches = 0;
+    rc = run_layers(m, b, first, last);
+    if (rc) return rc;
+    CK(m->api.download(residual, m->S(m->s_res), bytes, m->stream), "download residual");
+    return 0;
+}
+
 __attribute__((visibility("default"))) int s1_model_forward_shared(void* mp, const int32_t* prefix_ids,
                                                                   size_t prefix_len, const int32_t* suffix_ids,
                                                                   const size_t* suffix_lengths, size_t count,
@@ -1185,6 +1229,8 @@ __attribute__((visibility("default"))) int s1_model_cp_init(void* mp, const char
     const s1_config& c = m->cfg;
     CK(m->api.malloc_(&p, (size_t)c.lin_v_heads * c.lin_k_dim * c.lin_v_dim * 4), "state buffer");
     m->cp_state = static_cast<uint8_t*>(p);
+    CK(m->api.malloc_(&p, (size_t)(world + 1) * 4 * sizeof(int64_t)), "piece table");
+    m->cp_table = static_cast<int64_t*>(p);
     m->cp_rank = rank;
     m->cp_world = world;
     return 0;
@@ -1193,13 +1239,24 @@ __attribute__((visibility("default"))) int s1_model_cp_init(void* mp, const char
 __attribute__((visibility("default"))) int s1_model_forward_cp(void* mp, const int32_t* ids, size_t len, size_t start,
                                                               float* logits, float* hidden) {
     auto* m = static_cast<Model*>(mp);
-    if (!m || !ids) return -1;
+    if (!m) return -1;
     if (!m->comm) return fail(m, -1, "context parallelism is not initialised");
     const bool last = m->cp_rank + 1 == m->cp_world;
-    if (len < 64 || len > (size_t)m->cap_tokens) return fail(m, -1, "piece length out of range");
-    if (start % 64 != 0 || (!last && len % 64 != 0))
-        return fail(m, -1, "pieces must start on multiples of 64 tokens (all but the last of 64k tokens)");
-    if ((start == 0) != (m->cp_rank == 0)) return fail(m, -1, "rank 0 holds the first piece");
+    // Every rank checks its own piece, then all ranks exchange (status, start, len) and
+    // apply the same verdict before any transfer: a rank that refused alone would leave
+    // its peers waiting in NCCL sends and receives that have no timeout.
+    const int status = s1_cp_piece_status(ids, len, start, m->cp_rank, m->cp_world, m->cfg.vocab,
+                                          (size_t)m->cap_tokens);
+    const int64_t mine[4] = {status, (int64_t)start, (int64_t)len, 0};
+    int64_t* own = m->cp_table + (size_t)m->cp_world * 4;
+    CK(m->api.upload(own, mine, sizeof(mine), m->stream), "upload piece row");
+    const ncclResult_t r = m->nccl.all_gather(own, m->cp_table, 4, ncclInt64, m->comm,
+                                              static_cast<cudaStream_t>(m->stream));
+    if (r != ncclSuccess) return fail(m, -1, std::string("piece exchange: ") + m->nccl.error_string(r));
+    std::vector<int64_t> table((size_t)m->cp_world * 4);
+    CK(m->api.download(table.data(), m->cp_table, table.size() * sizeof(int64_t), m->stream), "download pieces");
+    char why[256];
+    if (s1_cp_agree(table.data(), m->cp_world, why, sizeof(why)) != 0) return fail(m, -1, why);
     int rc = ensure_prefix(m, (int)(start + len));
     if (rc) return rc;
     Batch b;
@@ -1269,4 +1326,84 @@ extern "C" __attribute__((visibility("default"))) size_t s1_shared_prefix(const 
     }
     const size_t aligned = common / 64 * 64;
     return aligned >= 512 ? aligned : 0;
+}
+
+// ============================================== context-parallel agreement (host) ====
+// The checks one rank makes on its own piece of a context-parallel prompt: 0, or
+// -1 no ids, -2 piece length outside [64, cap_tokens], -3 start not a multiple of 64,
+// -4 length of a piece before the last not a multiple of 64, -5 rank 0 not at position 0
+// (or another rank at 0), -6 a token id outside [0, vocab).
+extern "C" __attribute__((visibility("default"))) int s1_cp_piece_status(const int32_t* ids, size_t len,
+                                                                        size_t start, int rank, int world,
+                                                                        int vocab, size_t cap_tokens) {
+    if (!ids) return -1;
+    if (len < 64 || len > cap_tokens) return -2;
+    if (start % 64 != 0) return -3;
+    if (rank + 1 < world && len % 64 != 0) return -4;
+    if ((start == 0) != (rank == 0)) return -5;
+    for (size_t i = 0; i < len; i++)
+        if (ids[i] < 0 || ids[i] >= vocab) return -6;
+    return 0;
+}
+
+// Every rank's (status, start, len, unused) row, in rank order: 0 when every rank's
+// status is 0 and the pieces follow one another (rank r starts where rank r - 1 ends, so
+// what rank r - 1 sends is what rank r expects), else -1 with the reason in msg. Every
+// rank evaluates the same table and so reaches the same verdict.
+extern "C" __attribute__((visibility("default"))) int s1_cp_agree(const int64_t* table, int world, char* msg,
+                                                                 size_t cap) {
+    auto say = [&](const std::string& s) {
+        if (msg && cap) {
+            std::strncpy(msg, s.c_str(), cap - 1);
+            msg[cap - 1] = 0;
+        }
+        return -1;
+    };
+    if (!table || world < 1) return say("no piece table");
+    static const char* what[] = {"", "no ids", "piece length out of range", "start not a multiple of 64",
+                                 "piece before the last not a multiple of 64 tokens", "rank 0 must hold position 0",
+                                 "token id outside [0, vocab)"};
+    for (int r = 0; r < world; r++) {
+        const int64_t st = table[4 * r];
+        if (st != 0) {
+            const int k = (st <= -1 && st >= -6) ? (int)-st : 0;
+            return say("rank " + std::to_string(r) + " refused its piece: " +
+                       (k ? what[k] : ("status " + std::to_string(st))));
+        }
+    }
+    for (int r = 1; r < world; r++) {
+        const int64_t want = table[4 * (r - 1) + 1] + table[4 * (r - 1) + 2];
+        if (table[4 * r + 1] != want)
+            return say("rank " + std::to_string(r) + " starts at " + std::to_string(table[4 * r + 1]) +
+                       " but rank " + std::to_string(r - 1) + " ends at " + std::to_string(want));
+    }
+    if (msg && cap) msg[0] = 0;
+    return 0;
+}
+
+// ========================================================= request dispatch (host) ====
+// Requests over ranks (one process per GPU, each with a full weight replica), longest
+// processing time first: requests in decreasing cost (ties: lower index first), each to
+// the rank with the least cost assigned so far (ties: lower rank). The greedy's makespan
+// is within 4/3 of the optimum. Writes rank_of[n] and, if non-null, loads[ranks]; returns
+// 0, or -1 on invalid arguments (a negative or non-finite cost, ranks < 1).
+extern "C" __attribute__((visibility("default"))) int s1_dispatch_lpt(const double* costs, size_t n, int ranks,
+                                                                     int* rank_of, double* loads) {
+    if (ranks < 1 || (n && (!costs || !rank_of))) return -1;
+    for (size_t i = 0; i < n; i++)
+        if (!(costs[i] >= 0.0) || !std::isfinite(costs[i])) return -1;
+    std::vector<size_t> order(n);
+    for (size_t i = 0; i < n; i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](size_t a, size_t b) { return costs[a] > costs[b]; });
+    std::vector<double> load(ranks, 0.0);
+    for (size_t i : order) {
+        int best = 0;
+        for (int r = 1; r < ranks; r++)
+            if (load[r] < load[best]) best = r;
+        rank_of[i] = best;
+        load[best] += costs[i];
+    }
+    if (loads)
+        for (int r = 0; r < ranks; r++) loads[r] = load[r];
+    return 0;
 }

@@ -11,7 +11,10 @@ Thin ctypes layer over the two native libraries built in-tree by
 There is no fallback: a missing library raises at import of the binding.
 """
 from .cs1 import Cs1, Cs1Error, lib_path
-from .model import Config, Model, checkpoint_check, cp_pieces, cp_unique_id, checkpoint_list, config_from_hf, preset, pack_ranges, shared_prefix
+from .dispatch import dispatch, request_cost, shard
+from .model import (Config, Model, checkpoint_check, checkpoint_list, config_from_hf, cp_agree, cp_piece_status,
+                    cp_pieces, cp_unique_id, pack_ranges, preset, shared_prefix)
 
-__all__ = ["Cs1", "Cs1Error", "lib_path", "Config", "Model", "checkpoint_check", "checkpoint_list", "cp_pieces", "cp_unique_id", "config_from_hf", "preset",
-           "pack_ranges", "shared_prefix"]
+__all__ = ["Cs1", "Cs1Error", "lib_path", "Config", "Model", "checkpoint_check", "checkpoint_list", "config_from_hf",
+           "cp_agree", "cp_piece_status", "cp_pieces", "cp_unique_id", "dispatch", "pack_ranges", "preset",
+           "request_cost", "shard", "shared_prefix"]

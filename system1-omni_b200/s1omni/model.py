@@ -100,6 +100,7 @@ def _lib():
     lib.s1_model_init_random.argtypes = [P, ctypes.c_uint64, ctypes.c_float]
     lib.s1_model_forward.argtypes = [P, P, P, Z, P, P]
     lib.s1_model_forward_shared.argtypes = [P, P, Z, P, P, Z, P, P]
+    lib.s1_model_run_layers.argtypes = [P, P, P, Z, I, I, P]
     lib.s1_model_stage.argtypes = [P, P, P, Z]
     lib.s1_model_run_staged.argtypes = [P]
     lib.s1_model_fetch_logits.argtypes = [P, P]
@@ -121,6 +122,8 @@ def _lib():
     lib.s1_model_get_config.argtypes = [P, ctypes.POINTER(_Cfg)]
     lib.s1_checkpoint_error.restype = ctypes.c_char_p
     lib.s1_checkpoint_error.argtypes = []
+    lib.s1_cp_piece_status.argtypes = [P, Z, Z, I, I, I, Z]
+    lib.s1_cp_agree.argtypes = [P, I, ctypes.c_char_p, Z]
     lib.s1_pack_ranges.argtypes = [P, Z, Z, Z, P]
     lib.s1_shared_prefix.restype = Z
     lib.s1_shared_prefix.argtypes = [P, P, Z, Z]
@@ -239,6 +242,22 @@ def cp_pieces(cfg, tokens, world, align=64):
     return lengths
 
 
+def cp_piece_status(ids, start, rank, world, vocab, cap_tokens):
+    """The checks forward_cp makes on one rank's piece (host only): 0 or a negative code."""
+    a = np.ascontiguousarray(ids, np.int32)
+    return int(_get().s1_cp_piece_status(a.ctypes.data if len(a) else None, len(a), start, rank, world, vocab,
+                                         cap_tokens))
+
+
+def cp_agree(table):
+    """The verdict every rank reaches on all ranks' (status, start, len, 0) rows before a
+    context-parallel forward: (0, "") or (-1, reason)."""
+    t = np.ascontiguousarray(table, np.int64).reshape(-1, 4)
+    msg = ctypes.create_string_buffer(256)
+    rc = _get().s1_cp_agree(t.ctypes.data, len(t), msg, 256)
+    return int(rc), msg.value.decode()
+
+
 def cp_unique_id(nccl_library=None):
     """The 128-byte NCCL id of a context-parallel group, made on one rank and handed to
     every rank (for instance with torch.distributed.broadcast_object_list)."""
@@ -354,11 +373,24 @@ class Model:
                                                       hid.ctypes.data if hidden else None), "forward_shared")
         return (logits, hid) if hidden else logits
 
+    def run_layers(self, seqs, first, last, residual):
+        """Layers [first, last) of packed candidates from a residual stream (bf16 bit
+        patterns, uint16 [sum lengths, H], the stream entering layer `first`); returns the
+        stream leaving layer last - 1 in the same form."""
+        ids = np.concatenate([np.asarray(s, np.int32) for s in seqs])
+        lens = np.asarray([len(s) for s in seqs], dtype=np.uintp)
+        res = np.ascontiguousarray(residual, dtype=np.uint16).copy()
+        if res.shape != (len(ids), self.cfg.hidden):
+            raise ValueError(f"residual must be [{len(ids)}, {self.cfg.hidden}] bf16 bits")
+        self._check(self._lib.s1_model_run_layers(self._h, ids.ctypes.data, lens.ctypes.data, len(seqs), first, last,
+                                                  res.ctypes.data), "run_layers")
+        return res
+
     def stage(self, seqs):
         ids = np.concatenate([np.asarray(s, np.int32) for s in seqs])
         lens = np.asarray([len(s) for s in seqs], dtype=np.uintp)
-        self._staged_n = len(seqs)
         self._check(self._lib.s1_model_stage(self._h, ids.ctypes.data, lens.ctypes.data, len(seqs)), "stage")
+        self._staged_n = len(seqs)  # a refused batch leaves the previous one staged
 
     def run_staged(self):
         self._check(self._lib.s1_model_run_staged(self._h), "run_staged")

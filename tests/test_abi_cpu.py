@@ -133,3 +133,38 @@ def test_cp_pieces_balance_and_alignment():
         assert max(cost) / np.mean(cost) < 1 + max(0.02, step), (tokens, world, lengths)
     with pytest.raises(ValueError):
         cp_pieces(cfg, 200, 4)
+
+
+def test_dispatch_lpt_balances_and_matches_restatement():
+    """s1_dispatch_lpt (C++ host) against a plain restatement of longest-processing-time
+    first, and its makespan against the 4/3 bound of the greedy, on log-normal costs."""
+    from s1omni import dispatch, request_cost, preset
+    rng = np.random.default_rng(0)
+    cfg = preset("27b")
+    lens = np.clip(np.round(np.exp(rng.normal(np.log(800.0), 0.6, 256))), 1, 8192).astype(int)
+    costs = [request_cost(cfg, int(n)) for n in lens]
+    for ranks in (1, 2, 3, 8):
+        rank_of, loads = dispatch(costs, ranks)
+        # restatement: decreasing cost (stable on index), least-loaded rank (lowest index on ties)
+        order = sorted(range(len(costs)), key=lambda i: -costs[i])
+        want, load = [0] * len(costs), [0.0] * ranks
+        for i in order:
+            r = min(range(ranks), key=lambda j: (load[j], j))
+            want[i] = r
+            load[r] += costs[i]
+        assert rank_of == want
+        assert np.allclose(loads, load)
+        assert max(loads) <= (4.0 / 3.0) * max(sum(costs) / ranks, max(costs)) + 1e-6
+    assert dispatch([], 4) == ([], [0.0] * 4)
+    with pytest.raises(ValueError):
+        dispatch([1.0, -1.0], 2)
+    with pytest.raises(ValueError):
+        dispatch([1.0], 0)
+
+
+def test_request_cost_counts_candidates_over_the_prompt():
+    from s1omni import request_cost, preset
+    cfg = preset("9b")
+    lin = cfg.projection_flops_per_token()
+    assert request_cost(cfg, 100, [10, 20]) > request_cost(cfg, 100) + lin * 30
+    assert request_cost(cfg, 0, [64]) == request_cost(cfg, 64)

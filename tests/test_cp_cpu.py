@@ -86,3 +86,81 @@ def test_context_parallel_chain_on_gloo(pieces):
     assert res["ids_equal"] and res["id_len"] == 128
     assert res["pieces_equal"] and sum(res["pieces"]) == 32768 and len(res["pieces"]) == world
     assert all(x % 64 == 0 for x in res["pieces"][:-1])
+
+
+def _agree_rank(rank, world, port, case, out):
+    import sys
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "system1-omni_b200"))
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    from s1omni import cp_agree, cp_piece_status
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    vocab, pieces = 1000, [128, 64, 100]
+    starts = [0, 128, 192]
+    ids = np.random.default_rng(rank).integers(0, vocab, pieces[rank]).astype(np.int32)
+    start = starts[rank]
+    if case == "bad_id" and rank == 1:
+        ids[7] = vocab
+    if case == "gap" and rank == 2:
+        start = 256
+    status = cp_piece_status(ids, start, rank, world, vocab, 4096)
+    # the same exchange forward_cp makes over NCCL, here over gloo
+    mine = torch.tensor([status, start, len(ids), 0], dtype=torch.int64)
+    rows = [torch.zeros(4, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(rows, mine)
+    rc, why = cp_agree(torch.stack(rows).numpy())
+    out.put((rank, status, rc, why))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", ["good", "bad_id", "gap"])
+def test_context_parallel_ranks_refuse_together(case):
+    """forward_cp's agreement step on three gloo ranks: each rank checks its own piece,
+    the (status, start, len) rows are all-gathered, and every rank reaches the same verdict,
+    so a rank with a bad token id, or pieces that do not follow one another, make every rank
+    return the same error before any transfer (none is left waiting in a send or receive)."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    out = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_agree_rank, args=(r, world, port, case, out)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted(out.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    verdicts = {(rc, why) for _, _, rc, why in res}
+    assert len(verdicts) == 1, res
+    rc, why = verdicts.pop()
+    if case == "good":
+        assert rc == 0 and all(st == 0 for _, st, _, _ in res)
+    elif case == "bad_id":
+        assert rc == -1 and "rank 1" in why and "token id" in why
+        assert [st for _, st, _, _ in res] == [0, -6, 0]
+    else:
+        assert rc == -1 and "rank 2 starts at 256" in why
+
+
+def test_piece_status_codes():
+    from s1omni import cp_piece_status
+    ok = np.zeros(64, np.int32)
+    assert cp_piece_status(ok, 0, 0, 2, 10, 4096) == 0
+    assert cp_piece_status(np.zeros(0, np.int32), 0, 0, 2, 10, 4096) == -1
+    assert cp_piece_status(np.zeros(32, np.int32), 0, 0, 2, 10, 4096) == -2
+    assert cp_piece_status(ok, 64, 1, 2, 10, 32) == -2
+    assert cp_piece_status(ok, 65, 1, 2, 10, 4096) == -3
+    assert cp_piece_status(np.zeros(65, np.int32), 0, 0, 2, 10, 4096) == -4
+    assert cp_piece_status(np.zeros(65, np.int32), 64, 1, 2, 10, 4096) == 0
+    assert cp_piece_status(ok, 64, 0, 2, 10, 4096) == -5
+    assert cp_piece_status(ok, 0, 1, 2, 10, 4096) == -5
+    bad = ok.copy()
+    bad[3] = -1
+    assert cp_piece_status(bad, 0, 0, 2, 10, 4096) == -6

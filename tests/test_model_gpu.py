@@ -95,3 +95,73 @@ def test_out_of_range_token_ids_are_refused(tiny):
     from s1omni import Cs1
     assert Cs1().cs1_fault_status(1) == 0
     assert np.array_equal(m.forward([good]), before)
+
+
+def test_refused_stage_keeps_the_staged_batch(tiny):
+    """s1_model_stage refuses a batch with an out-of-range id before any copy, so the batch
+    staged before it still runs and gives the same logits."""
+    cfg, W, m = tiny
+    rng = np.random.default_rng(8)
+    good = [rng.integers(0, cfg.vocab, n).astype(np.int32) for n in (33, 70)]
+    m.stage(good)
+    m.run_staged()
+    before = m.fetch_logits()
+    bad = good[1].copy()
+    bad[5] = cfg.vocab
+    with pytest.raises(RuntimeError, match="outside"):
+        m.stage([good[0], bad])
+    m.run_staged()
+    assert np.array_equal(m.fetch_logits(), before)
+    assert np.array_equal(before, m.forward(good))
+
+
+def test_graphs_survive_prefix_reallocation(tiny):
+    """A longer shared prefix reallocates the prefix buffers; graphs captured for suffix
+    passes on the old buffers are dropped with them, so a later suffix pass with the
+    earlier prefix length captures afresh and equals eager (prefix 128 -> 256 -> 128)."""
+    cfg, W, m = tiny
+    rng = np.random.default_rng(9)
+    suffixes = [rng.integers(0, cfg.vocab, n).astype(np.int32) for n in (20, 45)]
+    p1 = rng.integers(0, cfg.vocab, 128).astype(np.int32)
+    p2 = rng.integers(0, cfg.vocab, 256).astype(np.int32)
+    eager1 = m.forward_shared(p1, suffixes)
+    eager2 = m.forward_shared(p2, suffixes)
+    m.set_graphs(True)
+    try:
+        got = []
+        for p in (p1, p1, p2, p2, p1, p1):
+            got.append(m.forward_shared(p, suffixes))
+    finally:
+        m.set_graphs(False)
+    for i, p in enumerate((p1, p1, p2, p2, p1, p1)):
+        assert np.array_equal(got[i], eager1 if p is p1 else eager2), i
+    from s1omni import Cs1
+    assert Cs1().cs1_fault_status(1) == 0
+
+
+def test_run_layers_composes_to_the_forward(tiny):
+    """s1_model_run_layers from the embedding through every layer, one layer at a time,
+    gives the forward's final hidden rows bit for bit, and one layer from a given residual
+    stream matches the oracle's layer within the bf16 tolerance."""
+    cfg, W, m = tiny
+    from oracle.bf16 import bits, from_bits
+    from oracle import ops
+    rng = np.random.default_rng(10)
+    seqs = [rng.integers(0, cfg.vocab, n).astype(np.int32) for n in (65, 30)]
+    _, hidden = m.forward(seqs, hidden=True)
+    ids = np.concatenate(seqs)
+    res = bits(W["embed"][ids])
+    whole = m.run_layers(seqs, 0, len(cfg.layer_types), res)
+    for layer in range(len(cfg.layer_types)):
+        res = m.run_layers(seqs, layer, layer + 1, res)
+    assert np.array_equal(res, whole)
+    last = np.cumsum([len(s) for s in seqs]) - 1
+    final = ops.rms_norm(from_bits(res)[last], W["final_norm"], cfg.eps)
+    # the final RMSNorm restated on the host: within one bf16 ulp of the kernel's
+    assert (np.abs(final - hidden) <= np.abs(hidden) * 2.0 ** -7 + 1e-30).all()
+    # one layer, teacher-forced, against the oracle's layer on the first sequence
+    h = bits(W["embed"][seqs[0]])
+    got = from_bits(m.run_layers([seqs[0]], 0, 2, h))
+    want = OM.run_layers(cfg, W, seqs[0], 0, 2, from_bits(h))
+    upd = np.abs(want - from_bits(h)).max()
+    assert np.abs(got - want).max() <= 2e-2 * upd, np.abs(got - want).max() / upd

@@ -149,3 +149,26 @@ def test_presets_have_baseline_shapes(name):
     assert (a.hidden, a.intermediate, a.lin_v_heads, a.heads) == (b.hidden, b.intermediate, b.lin_v_heads, b.heads)
     assert a.layer_types == b.layer_types
     assert a.layer_types.count("attn") * 4 == len(a.layer_types)
+
+
+def test_precise_forward_is_the_float32_forward_to_bf16_noise():
+    """The precise oracle (float64 ops, bf16 rounding at op outputs) and the float32 one
+    on the tiny model: the same forward up to bf16 rounding flips, and the shared-prefix
+    continuation of the precise form equals its full prompt up to the same noise."""
+    cfg = OM.preset("tiny")
+    W = OM.make_weights(cfg, seed=7)
+    rng = np.random.default_rng(3)
+    prefix = rng.integers(0, cfg.vocab, 128)
+    sfx = rng.integers(0, cfg.vocab, 20)
+    full = np.concatenate([prefix, sfx])
+    a = OM.run_sequence(cfg, W, full, precise=True)[0][-1]
+    b = OM.run_sequence(cfg, W, full)[0][-1]
+    assert np.abs(a - b).max() <= 0.05 * np.abs(b).max()
+    _, st = OM.run_sequence(cfg, W, prefix, capture=True, precise=True)
+    c = OM.run_sequence(cfg, W, sfx, prefix=st, precise=True)[0][-1]
+    assert np.abs(c - a).max() <= 0.05 * np.abs(a).max()
+    # layer by layer from the embedding equals the whole forward's residual stream
+    from oracle import ops
+    res = OM.run_layers(cfg, W, full, 0, len(cfg.layer_types), ops.embed(full, W["embed"]))
+    x = ops.rms_norm(res, W["final_norm"], cfg.eps)
+    assert np.array_equal(x[-1], b)

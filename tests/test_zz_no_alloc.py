@@ -4,9 +4,9 @@ they run the prefill.
 
 Called through the C ABI twice in a row (a different input each time, so the second
 call runs over the first call's leftover scratch) and checked against cs1_gdn_prefill
-with a caller-owned workspace, within the GDN gate used by test_gdn_gpu.py
-(max |err| <= 2e-2 * max |ref|). Also: a size beyond the fixed scratch is rejected
-before any launch. This file is collected last so that a failure here stops a `-x` run
+with a caller-owned workspace: the same kernels on the same inputs, so the outputs are
+equal bit for bit. Also: the largest size the fixed scratch holds (48 heads x 1,152
+tokens) runs and matches, one token more is rejected before any launch. This file is collected last so that a failure here stops a `-x` run
 only after every other test has run; it also passes alone in a fresh process.
 """
 import numpy as np
@@ -46,7 +46,30 @@ def test_noalloc_matches_caller_workspace_twice(cs1, stream):
         assert rc == 0
         got = host(o)
         assert cs1.cs1_fault_status(1) == 0
-        assert np.abs(got - ref).max() <= 2e-2 * np.abs(ref).max(), (T, np.abs(got - ref).max())
+        assert np.array_equal(got, ref), (T, np.abs(got - ref).max())
+
+
+def test_noalloc_largest_size_runs_and_one_token_more_is_rejected(cs1, stream):
+    """ceil(T / 64) * H <= 910 fits the 64 MiB scratch: T = 1,152 at 48 heads (18 chunks)
+    runs and equals cs1_gdn_prefill; T = 1,153 (19 chunks) is refused before any launch."""
+    H, HK, T = 48, 16, 1152
+    q, k, v, g, beta = _inputs(T, H, HK, 3)
+    ref = _with_workspace(cs1, stream, q, k, v, g, beta, H, HK)
+    dq, dk, dv, dg, db = dev_bf16(q), dev_bf16(k), dev_bf16(v), dev_f32(g), dev_bf16(beta)
+    o = empty_bf16(T, H, 128)
+    assert cs1.raw.cs1_gdn_prefill_noalloc(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
+                                           o.data_ptr(), T, H, HK, SCALE, stream) == 0
+    assert np.array_equal(host(o), ref)
+    sentinel = torch.full((T + 1, H, 128), 7.0, dtype=torch.bfloat16, device="cuda")
+    big = [torch.zeros((T + 1) * n, dtype=dt, device="cuda") for n, dt in
+           ((HK * 128, torch.bfloat16), (HK * 128, torch.bfloat16), (H * 128, torch.bfloat16), (H, torch.float32),
+            (H, torch.bfloat16))]
+    rc = cs1.raw.cs1_gdn_prefill_noalloc(*[b.data_ptr() for b in big], sentinel.data_ptr(), T + 1, H, HK, SCALE,
+                                         stream)
+    assert rc != 0
+    torch.cuda.synchronize()
+    assert bool((sentinel == 7.0).all())  # nothing was launched
+    assert cs1.cs1_fault_status(1) == 0
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch(cs1, stream):
