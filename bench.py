@@ -1,21 +1,28 @@
 """Prefill benchmark of the 27B-shaped Qwen3.5 hybrid decision scorer on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--ref-cuda]
 
-A step is one packed prefill of a batch of 32 single-candidate requests (workload (a)
-of the 27B benchmark configuration: prompt lengths log-normal, median 800, sigma 0.6, clipped to
+A step is one packed prefill of 32 single-candidate requests per GPU (workload (a) of the
+27B benchmark configuration: prompt lengths log-normal, median 800, sigma 0.6, clipped to
 1..8192; synthetic uniform token ids; random-init bf16 weights of the 27B shape) through
 the C++ host and the sm_100a kernels, scored by the 8-label head on each final token.
-Weak scaling: every rank processes its own batch of 32 requests with a full weight
-replica; no collective on the hot path. Prints one JSON line on rank 0. Rank 0 also
-times workload (b), one 32,768-token prefill (`long_prefill` in the line; `--no-long`
-skips it); with N > 1 GPUs every rank then runs the same prompt context-parallel, one
-piece per GPU with the per-layer state passed rank to rank over NCCL
-(`long_prefill_cp`).
+Weak scaling: one pool of 32 x N requests is drawn from one seed and dispatched over the
+N ranks longest-processing-time first by token cost (s1omni.dispatch); every rank holds a
+full weight replica and no collective sits on the hot path. Prints one JSON line on rank 0.
+Rank 0 also times workload (b), one 32,768-token prefill (`long_prefill`; `--no-long`
+skips it); with N > 1 GPUs every rank then runs the same prompt context-parallel, one piece
+per GPU with the per-layer state passed rank to rank over NCCL (`long_prefill_cp`, with
+`cp_bit_exact`: its logits equal the one-GPU logits bit for bit). `c3` is configuration C3
+(9B shape, 256 requests of a log-normal prompt and 4 candidates each, the candidates
+continuing from the shared prompt), the 256 requests dispatched over the N ranks (strong
+scaling; `--no-c3` skips it).
 
-`--impl reference` times the reference's CPU path on the host cores instead: the numpy
-restatement of the same forward (the reference's prefill exists only as GPU code; its CPU
-parity anchor is Transformers' PyTorch forward) on a bounded sample of the workload.
+`--impl reference` times the reference's CPU path on the host cores instead: Transformers'
+own Qwen3.5 decoder layers (the reference's CPU parity anchor, FLA and causal-conv1d off,
+float32) on one 771-token prompt (the median of the concurrency-1 workload) through one
+4-layer period of the 27B shape, extrapolated x16 to 64 layers; every host thread is used.
+`--ref-cuda` times the reference's own CUDA library (built from its sources by
+oracle/Makefile) through the same C++ host on the same GPU instead, and prints its own line.
 """
 import argparse
 import json
@@ -44,11 +51,36 @@ def long_request(seed=5):
     return rng.integers(0, 151936, LONG).astype(np.int32)
 
 
-def requests(rank, n=BATCH, seed=4):
-    rng = np.random.default_rng(seed + 1000 * rank)
+def pool(n, seed=4):
+    """n requests of workload (a): log-normal lengths (median 800, sigma 0.6, 1..8192)."""
+    rng = np.random.default_rng(seed)
     x = np.exp(rng.normal(np.log(800.0), 0.6, n))
     lens = np.clip(np.round(x), 1, 8192).astype(np.int64)
     return [rng.integers(0, 151936, int(L)).astype(np.int32) for L in lens]
+
+
+def requests(rank, world=1):
+    """This rank's share of one pool of 32 x world requests, dispatched over the ranks
+    longest processing time first by token cost (s1omni.dispatch)."""
+    from s1omni import preset, request_cost, shard
+    reqs = pool(BATCH * world)
+    if world == 1:
+        return reqs
+    cfg = preset("27b")
+    return shard(reqs, [request_cost(cfg, len(r)) for r in reqs], world, rank)
+
+
+C3_REQUESTS = 256
+
+
+def c3_pool(seed=3):
+    """Configuration C3: 256 requests, prompt lengths clip(round(exp(N(ln 600, 0.6))), 64,
+    4096), 4 candidates of U{16..64} tokens each; uniform token ids."""
+    rng = np.random.default_rng(seed)
+    lens = np.clip(np.round(np.exp(rng.normal(np.log(600.0), 0.6, C3_REQUESTS))), 64, 4096).astype(np.int64)
+    cands = rng.integers(16, 65, (C3_REQUESTS, 4))
+    return [(rng.integers(0, 151936, int(L)).astype(np.int32),
+             [rng.integers(0, 151936, int(c)).astype(np.int32) for c in cands[i]]) for i, L in enumerate(lens)]
 
 
 class Clocks:
@@ -107,62 +139,121 @@ def measured_peaks():
 
 
 # ------------------------------------------------------------------ CPU arm ----
-_CPU_PERIOD = {}
+CPU_TOKENS = 771  # median prompt of the concurrency-1 workload (single_requests)
+_HF = {}
 
 
-def cpu_period(seed=0):
-    """The 27B shape's 4-layer period (3 GDN + 1 attention + MLPs) for the numpy
-    restatement, with its random weights; built once per process."""
-    if seed in _CPU_PERIOD:
-        return _CPU_PERIOD[seed]
-    from oracle import model as OM
-    from oracle.bf16 import rnd
-    cfg = OM.preset("27b")
-    cfg = OM.Config(cfg.hidden, cfg.intermediate, ["gdn", "gdn", "gdn", "attn"], cfg.lin_k_heads, cfg.lin_v_heads,
-                    cfg.heads, cfg.kv_heads, 4096, name="27b-period")
-    rng = np.random.default_rng(seed)
-    W = {}
-    shared = {}
-    for name, shape, kind in OM.weight_shapes(cfg):
-        leaf = name.split(".")[-1]
-        key = (leaf, shape)
-        if key not in shared:  # one draw per distinct tensor shape: timing, not accuracy
-            x = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
-            if leaf == "A_log":
-                x = np.log(rng.uniform(1, 16, shape)).astype(np.float32)
-            if leaf in ("norm", "dt_bias"):
-                x = x + np.float32(1)
-            shared[key] = x if kind == "f32" else rnd(x)
-        W[name] = shared[key]
-    _CPU_PERIOD[seed] = (cfg, W)
-    return _CPU_PERIOD[seed]
+def host_threads():
+    """Every host thread this process may run on (torchrun sets OMP_NUM_THREADS=1; the
+    CPU arm overrides it explicitly)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
-def cpu_sample(tokens=256, seed=0):
-    """Time the numpy restatement of one 4-layer period (3 GDN + 1 attention + MLPs) of
-    the 27B shape on one prompt of `tokens` tokens (weights built beforehand, outside the
-    timed call); return (tokens/s extrapolated to 64 layers, seconds, threads)."""
-    from threadpoolctl import threadpool_info
-    from oracle import model as OM
-    cfg, W = cpu_period(seed)
-    ids = np.random.default_rng(seed + 1).integers(0, cfg.vocab, tokens)
-    t0 = time.perf_counter()
-    OM.run_sequence(cfg, W, ids, gdn_mode="fp32")
-    dt = time.perf_counter() - t0
-    threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
-    per_token_period = dt / tokens
-    return 1.0 / (per_token_period * 16), dt, threads
+def hf_period():
+    """Transformers' own Qwen3.5 text model with one 4-layer period of the 27B shape (3
+    Gated DeltaNet + 1 gated attention layer, SwiGLU 17,408), float32, FLA and
+    causal-conv1d forced off as the reference's HF baseline does. Weights are filled from
+    a seeded block of N(0, 0.02) values (A_log = log U(1, 16), dt_bias 1, norms at their
+    identity values): a timing model, built once per process."""
+    if "m" in _HF:
+        return _HF["m"]
+    import torch
+    import transformers.utils.import_utils as iu
+    iu.is_flash_linear_attention_available = lambda *a, **k: False
+    iu.is_causal_conv1d_available = lambda *a, **k: False
+    from transformers import Qwen3_5TextConfig
+    from transformers.models.qwen3_5 import modeling_qwen3_5 as M
+    config = Qwen3_5TextConfig(
+        vocab_size=16, hidden_size=5120, intermediate_size=17408, num_hidden_layers=4, num_attention_heads=24,
+        num_key_value_heads=4, head_dim=256, linear_num_key_heads=16, linear_num_value_heads=48,
+        linear_key_head_dim=128, linear_value_head_dim=128, linear_conv_kernel_dim=4,
+        layer_types=["linear_attention"] * 3 + ["full_attention"], rms_norm_eps=1e-6, max_position_embeddings=40000,
+        rope_parameters={"rope_type": "default", "rope_theta": 1e7, "partial_rotary_factor": 0.25,
+                         "mrope_section": [11, 11, 10], "mrope_interleaved": True})
+    config._attn_implementation = "eager"
+    with torch.device("meta"):
+        model = M.Qwen3_5TextModel(config)
+    model = model.to_empty(device="cpu").eval()
+    g = torch.Generator().manual_seed(0)
+    block = torch.randn(1 << 20, generator=g) * 0.02
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("A_log"):
+                p.uniform_(1.0, 16.0, generator=g).log_()
+            elif name.endswith("dt_bias") or name.endswith("linear_attn.norm.weight"):
+                p.fill_(1.0)
+            elif name.endswith("norm.weight") or name.endswith("layernorm.weight"):
+                p.zero_()  # zero-centred RMSNorm: scale 1 + w
+            elif "conv1d" in name:
+                p.uniform_(-0.5, 0.5, generator=g)
+            else:
+                flat = p.view(-1)
+                for i in range(0, flat.numel(), block.numel()):
+                    n = min(block.numel(), flat.numel() - i)
+                    flat[i:i + n].copy_(block[:n])
+    model.rotary_emb = M.Qwen3_5TextRotaryEmbedding(config=config)  # its buffers, computed on the host
+    _HF["m"] = model
+    _HF["versions"] = f"transformers {__import__('transformers').__version__}, torch {torch.__version__}"
+    return model
 
 
-def reference_cuda(args, local):
+def cpu_sample(tokens=CPU_TOKENS, seed=0):
+    """Time one `tokens`-token prompt through the 27B-shape period of Transformers' model on
+    every host thread; return (tokens/s extrapolated to 64 layers, seconds, threads)."""
+    import torch
+    threads = host_threads()
+    torch.set_num_threads(threads)
+    model = hf_period()
+    x = torch.randn(1, tokens, 5120, generator=torch.Generator().manual_seed(seed)) * 0.02
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        model(inputs_embeds=x)
+        dt = time.perf_counter() - t0
+    return tokens / (dt * 16), dt, threads
+
+
+def cpu_sample_desc(tokens=CPU_TOKENS):
+    return (f"one {tokens}-token prompt through one 4-layer period (3 GDN + 1 attention + MLPs) of the 27B shape, "
+            f"Transformers Qwen3_5TextModel float32 eager (FLA off; {_HF.get('versions', '')}), "
+            f"x16 periods (extrapolated to 64 layers)")
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample()
+    threads = host_threads()
+    for _ in range(args.steps):
+        v, dt, threads = cpu_sample()
+        vals.append(v)
+    value = float(np.median(vals))
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "27b-a-batch32", "model": "qwen3.5-27b-shape", "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                         "sample": cpu_sample_desc()},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_reference_cuda(args, rank, world, local):
     """The reference's own CUDA library (built from its sources by oracle/Makefile into
     oracle/_ref/, recompiled for sm_100a: cuBLASLt GEMMs, mma.sync attention and GDN)
-    driven by the same C++ host on the same GPU, on the same 32 requests split into
-    launches the way the reference executor packs them (<= 16 prompts, <= 4096 tokens,
-    open_jev batching.rs:9-25). Returns a dict, or None when the library is absent."""
+    driven by the same C++ host on the same GPU, on rank 0's requests split into launches
+    the way the reference executor packs them (<= 16 prompts, <= 4096 tokens,
+    open_jev batching.rs:9-25), eager, wall clock around synchronous calls."""
+    if rank != 0:
+        return
     ref = os.path.join(ROOT, "oracle", "_ref", "libqwen3_5_cuda.so")
     if not os.path.exists(ref):
-        return None
+        print(json.dumps({"impl": "reference-cuda-same-gpu", "unavailable": "oracle/_ref not built"}), flush=True)
+        return
     import torch
     from s1omni import Model, lib_path, pack_ranges, preset
     torch.cuda.set_device(local)
@@ -173,18 +264,10 @@ def reference_cuda(args, local):
     cap = max(max(sum(len(s) for s in seqs[a:b]) for a, b in ranges), 0 if args.no_long else LONG) + 64
     m = Model(cfg, device=local, max_tokens=cap, max_seqs=16, cs1_library=ref + ";" + lib_path())
     m.init_random(seed=1234, std=0.02)
-    stream = torch.cuda.ExternalStream(m.stream)
 
     def step():
-        out = []
-        for a, b in ranges:
-            out.append(m.forward(seqs[a:b]))
-        return np.concatenate(out)
+        return np.concatenate([m.forward(seqs[a:b]) for a, b in ranges])
     logits = step()
-    # run-to-run sensitivity of the reference itself: the same requests one by one
-    # (different GEMM row counts, hence possibly different cuBLASLt algorithms)
-    single = np.concatenate([m.forward(seqs[i:i + 1]) for i in range(len(seqs))])
-    self_diff = float(np.abs(single - logits).max())
     for _ in range(max(1, args.warmup - 1)):
         step()
     torch.cuda.synchronize()
@@ -197,7 +280,6 @@ def reference_cuda(args, local):
     lat = latency(m, args)
     long = None
     if not args.no_long:
-        # workload (b): the reference executor sends a prompt this long alone (one launch)
         seq = long_request()
         m.forward([seq])
         torch.cuda.synchronize()
@@ -209,42 +291,13 @@ def reference_cuda(args, local):
         long = {"workload": "27b-b-32k", "tokens": LONG, "value": LONG / (lms * 1e-3), "unit": UNIT,
                 "ms_per_step": lms, "timing": "wall clock around synchronous forward calls"}
     m.close()
-    del stream
-    return {"value": tokens / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "launch_ranges": len(ranges),
-            "p50_decision_latency_ms": lat, "long_prefill": long,
-            "library": "reference src/backends/cuda/qwen3_5 built for sm_100a (oracle/Makefile)",
-            "host": "this build's C++ host, eager, host-side scorer head (the reference's executor path)",
-            "timing": "wall clock around synchronous forward calls (host copies included)",
-            "logits_sample": logits[:4].round(4).tolist(),
-            "self_max_abs_diff_packed_vs_single": self_diff}
-
-
-def run_reference(args, rank, world):
-    if rank != 0:
-        return
-    ref_cuda = None
-    if not args.no_ref_cuda:
-        try:
-            ref_cuda = reference_cuda(args, int(os.environ.get("LOCAL_RANK", 0)))
-        except Exception as e:  # reported, not fatal: the CPU arm is the contract
-            ref_cuda = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
-    vals = []
-    for _ in range(args.warmup):
-        cpu_sample(args.cpu_tokens)
-    for _ in range(args.steps):
-        v, dt, threads = cpu_sample(args.cpu_tokens)
-        vals.append(v)
-    value = float(np.median(vals))
-    sample = (f"one {args.cpu_tokens}-token prompt through one 4-layer period (3 GDN + 1 attention + MLPs) of the "
-              f"27B shape, numpy float32 restatement, x16 periods (extrapolated to 64 layers)")
     print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": "27b-a-batch32", "model": "qwen3.5-27b-shape", "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "reference_cuda_same_gpu": ref_cuda,
-    }), flush=True)
+        "impl": "reference-cuda-same-gpu", "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": UNIT,
+        "ms_per_step": ms, "launch_ranges": len(ranges), "p50_decision_latency_ms": lat, "long_prefill": long,
+        "library": "reference src/backends/cuda/qwen3_5 built for sm_100a (oracle/Makefile)",
+        "host": "this build's C++ host, eager, host-side scorer head (the reference's executor path)",
+        "timing": "wall clock around synchronous forward calls (host copies included)",
+        "logits_sample": logits[:4].round(4).tolist()}), flush=True)
 
 
 # ------------------------------------------------------------------ GPU arm ----
@@ -320,15 +373,18 @@ def long_prefill(model, torch, stream, steps=3):
     logits = model.fetch_logits()
     return {"workload": "27b-b-32k", "tokens": LONG, "value": LONG / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms,
             "steps": steps, "warmup": 3, "seed": 5, "finite": bool(np.isfinite(logits).all()),
-            "logits": logits[0].round(4).tolist()}
+            "logits": logits[0].round(4).tolist(), "_raw": logits[0].copy()}
 
 
-def long_prefill_cp(model, torch, dist, rank, world, stream, steps=3):
+def long_prefill_cp(model, torch, dist, rank, world, stream, one_gpu=None, steps=3):
     """Workload (b) over every rank of a multi-GPU run: the same 32,768-token prompt split in
     order into one piece per GPU (64-token boundaries, sized for equal estimated work per
     rank), context-parallel (per-layer GDN
     state, conv history and attention K/V passed rank to rank over NCCL). Host ids in, the
-    last rank's logits out; CUDA events on each model stream, max over ranks."""
+    last rank's logits out; CUDA events on each model stream, max over ranks. On rank 0,
+    `one_gpu` holds the one-GPU logits of the same prompt: `cp_bit_exact` says whether the
+    context-parallel logits equal them bit for bit (they should: pieces start on 64-token
+    boundaries, where the chunked GDN restarts)."""
     from s1omni import cp_pieces, cp_unique_id, preset
     seq = long_request()
     lengths = cp_pieces(preset("27b"), LONG, world)  # work-balanced pieces on 64-token boundaries
@@ -354,10 +410,67 @@ def long_prefill_cp(model, torch, dist, rank, world, stream, steps=3):
     dist.broadcast(logits, src=world - 1)
     ms = float(np.median(times))
     lg = logits.cpu().numpy()
-    return {"workload": "27b-b-32k", "parallelism": f"context-parallel x{world}", "tokens": LONG,
-            "pieces": lengths, "value": LONG / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
-            "warmup": 1, "seed": 5, "timing": "CUDA events on each rank's model stream, max over ranks, median",
-            "finite": bool(np.isfinite(lg).all()), "logits": lg.round(4).tolist()}
+    out = {"workload": "27b-b-32k", "parallelism": f"context-parallel x{world}", "tokens": LONG,
+           "pieces": lengths, "value": LONG / (ms * 1e-3), "unit": UNIT, "ms_per_step": ms, "steps": steps,
+           "warmup": 1, "seed": 5, "timing": "CUDA events on each rank's model stream, max over ranks, median",
+           "finite": bool(np.isfinite(lg).all()), "logits": lg.round(4).tolist()}
+    if one_gpu is not None:
+        out["cp_bit_exact"] = bool(np.array_equal(lg, one_gpu))
+        out["max_abs_diff_vs_one_gpu"] = float(np.abs(lg - one_gpu).max())
+    return out
+
+
+def c3_step(model, reqs):
+    """One pass over this rank's C3 requests: each request's prompt runs once as a shared
+    prefix and its 4 candidates continue from it in one packed pass (host ids in, logits
+    out). Returns (tokens, logits of the first request)."""
+    tokens, first = 0, None
+    for prompt, cands in reqs:
+        lg = model.forward_shared(prompt, cands)
+        first = lg if first is None else first
+        tokens += len(prompt) + sum(len(c) for c in cands)
+    return tokens, first
+
+
+def run_c3(torch, dist, rank, world, local, steps=2):
+    """Configuration C3 (9B shape, random-init weights seed 1234): the 256 requests of
+    c3_pool dispatched over the ranks longest-processing-time first by token cost; each
+    rank serves its share request by request (eager, wall clock around synchronous calls,
+    max over ranks). Strong scaling: the 256 requests are the whole job at every N."""
+    from s1omni import Model, preset, request_cost, shard
+    cfg = preset("9b")
+    reqs = c3_pool()
+    costs = [request_cost(cfg, len(p), [len(c) for c in cs]) for p, cs in reqs]
+    mine = shard(reqs, costs, world, rank)
+    total = sum(len(p) + sum(len(c) for c in cs) for p, cs in reqs)
+    cap = max(len(p) for p, _ in reqs) + 4 * 64 + 64
+    m = Model(cfg, device=local, max_tokens=cap, max_seqs=8)
+    try:
+        m.init_random(seed=1234, std=0.02)
+        c3_step(m, mine[:4])  # warm-up
+        times = []
+        logits = None
+        for _ in range(steps):
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            _, lg = c3_step(m, mine)
+            torch.cuda.synchronize()
+            t = torch.tensor([time.perf_counter() - t0], device="cuda")
+            if dist:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            times.append(float(t))
+            logits = lg if rank == 0 else logits
+    finally:
+        m.close()
+    sec = float(np.median(times))
+    return {"workload": "c3-9b-256x4", "model": "qwen3.5-9b-shape hybrid scorer (24 GDN + 8 attn)",
+            "requests": C3_REQUESTS, "candidates_per_request": 4, "tokens": int(total),
+            "requests_on_rank0": len(mine), "value": total / sec, "unit": UNIT, "seconds_per_step": sec,
+            "steps": steps, "warmup": 1, "scaling": "strong", "dispatch": "longest processing time first by token cost",
+            "timing": "wall clock around synchronous forward_shared calls (host ids in, logits out), max over ranks",
+            "logits_first_request": None if logits is None else logits.round(4).tolist()}
 
 
 def single_requests(n=16, seed=5):
@@ -398,7 +511,7 @@ def run_ours(args, rank, world, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
     cfg = preset("27b")
-    seqs = requests(rank)
+    seqs = requests(rank, world)
     tokens = int(sum(len(s) for s in seqs))
     cap = max(tokens, 0 if args.no_long else LONG) + 64
     model = Model(cfg, device=local, max_tokens=cap, max_seqs=BATCH)
@@ -439,9 +552,15 @@ def run_ours(args, rank, world, local):
     e2e = float(np.median(e2e_ms[1:]))
     lat = latency(model, args)
     long = long_prefill(model, torch, stream) if rank == 0 and not args.no_long else None
-    long_cp = long_prefill_cp(model, torch, dist, rank, world, stream) if dist and not args.no_long else None
-    h2d = tokens * 4 + tokens * 32 * 2 * 2 + BATCH * 4
-    d2h = BATCH * cfg.labels * 4
+    one_gpu = long.pop("_raw") if long else None
+    long_cp = long_prefill_cp(model, torch, dist, rank, world, stream, one_gpu) if dist and not args.no_long else None
+    c3 = None
+    if not args.no_c3:
+        model.close()  # the 9B replica of C3 takes its place
+        model = None
+        c3 = run_c3(torch, dist, rank, world, local)
+    h2d = tokens * 4 + tokens * 32 * 2 * 2 + len(seqs) * 4  # ids, rotary rows, last-row indices
+    d2h = len(seqs) * cfg.labels * 4
     tmax = torch.tensor([ms, e2e], device="cuda")
     tok = torch.tensor([float(tokens)], device="cuda")
     if dist:
@@ -462,13 +581,15 @@ def run_ours(args, rank, world, local):
         proj = cfg.projection_flops_per_token() * tokens
         # the CPU baseline is timed at N = 1 only (rank 0 of a multi-GPU job skips it)
         use_cpu = world == 1 and not args.no_cpu
-        cpu_v, cpu_dt, cpu_threads = cpu_sample(args.cpu_tokens) if use_cpu else (None, 0.0, 0)
+        cpu_v, cpu_dt, cpu_threads = cpu_sample() if use_cpu else (None, 0.0, 0)
         result = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform token ids, random-init weights)",
             "config": {"workload": "27b-a-batch32", "model": "qwen3.5-27b-shape hybrid scorer (48 GDN + 16 attn)",
-                       "requests_per_gpu": BATCH, "tokens_per_gpu": tokens, "global_batch": BATCH * world,
+                       "requests_per_gpu": BATCH, "tokens_rank0": tokens, "tokens_total": int(total_tokens),
+                       "global_batch": BATCH * world, "dispatch": "one pool of 32 x N requests, longest processing "
+                       "time first by token cost (s1omni.dispatch)",
                        "seq_len": "log-normal median 800 sigma 0.6 clip 1..8192", "parallelism": f"replica x{world}",
                        "l2": "weights (54 GB) and activations exceed L2 every step", "cuda_graphs": True},
             "e2e": {"value": total_tokens / (e2e_max * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
@@ -485,19 +606,20 @@ def run_ours(args, rank, world, local):
                                                            "tflops": round(2.0 * tokens * n_ * k_ / (t_ * 1e-3) / 1e12, 1)}
                                                           for k, n_, k_, t_ in per_shape]},
                          "forward_projection_tflops": proj / (ms_max * 1e-3) / 1e12},
-            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
-                             "sample": f"one {args.cpu_tokens}-token prompt, one 4-layer period of the 27B shape "
-                                       f"(numpy float32 restatement), x16 periods"} if use_cpu else None,
+            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "reference",
+                             "sample": cpu_sample_desc()} if use_cpu else None,
             "p50_decision_latency_ms": lat,
             "long_prefill": long,
             "long_prefill_cp": long_cp,
+            "c3": c3,
             "clocks": clocks.summary(),
             "checks": {"finite_logits_no_fault": ok, "logits_sample": logits[:4].round(4).tolist()},
         }
     if dist:
         dist.barrier()
         dist.destroy_process_group()
-    model.close()
+    if model is not None:
+        model.close()
     if result:
         print(json.dumps(result), flush=True)
 
@@ -508,10 +630,11 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=256)
+    ap.add_argument("--ref-cuda", action="store_true",
+                    help="time the reference's own CUDA library (oracle/_ref) through the same host, same GPU")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-ref-cuda", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip workload (b), the 32,768-token prefill")
+    ap.add_argument("--no-c3", action="store_true", help="skip configuration C3 (9B, 256 requests x 4 candidates)")
     args = ap.parse_args()
     if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
         # one process per GPU: relaunch under torch.distributed.run on this node
@@ -525,7 +648,9 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
-    if args.impl == "reference":
+    if args.ref_cuda:
+        run_reference_cuda(args, rank, world, local)
+    elif args.impl == "reference":
         run_reference(args, rank, world)
     else:
         run_ours(args, rank, world, local)

@@ -56,6 +56,10 @@ int cs1_copy2d(void* dst, size_t dpitch, const void* src, size_t spitch, size_t 
 // 4 epilogue, 8 other) since the last clear; a set bit means a kernel abandoned its
 // work and its outputs are not valid.
 uint32_t cs1_fault_status(int clear);
+// Additive, no counterpart in the reference: a self-test of that reporting. One thread
+// waits, with the kernels' bounded wait cut to `cycles` (1e3 .. 4e9), on a barrier nothing
+// completes, gives up and sets bit 8; no copy or MMA is in flight. Returns the launch status.
+int cs1_wait_selftest(long long cycles, void* stream);
 
 // ---- operations ----
 int cs1_embed(const int32_t* ids, const void* table, void* out, int T, int D, void* stream);   // ops.h:51

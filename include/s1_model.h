@@ -75,7 +75,10 @@ int s1_model_init_random(void* model, uint64_t seed, float std);
 int s1_model_forward(void* model, const int32_t* ids, const size_t* lengths, size_t count, float* logits,
                      float* hidden);
 // One shared prefix, computed once, then `count` suffixes continued from its GDN
-// states, conv history and attention K/V (positions continue at prefix_len).
+// states, conv history and attention K/V. The shared part is the prefix floored to a
+// multiple of 64 tokens (the reference floors shared prefixes the same way); the rest of
+// the prefix is prepended to every suffix, so each candidate's logits are those of its
+// full prompt (prefix + suffix) run alone. A prefix under 64 tokens is not shared at all.
 int s1_model_forward_shared(void* model, const int32_t* prefix_ids, size_t prefix_len, const int32_t* suffix_ids,
                             const size_t* suffix_lengths, size_t count, float* logits, float* hidden);
 

@@ -41,30 +41,39 @@ def _headers(d):
         [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include"))]
 
 
-def compile_cu(src, force):
+def compile_cu(src, force, tuning=False):
     obj = os.path.join(OBJ, os.path.basename(src) + ".o")
     if not force and not _newer(obj, [src] + _headers(CSRC)):
         return obj, None
-    cmd = [NVCC, *ARCH, *CUDA_FLAGS, "-c", src, "-o", obj]
+    cmd = [NVCC, *ARCH, *CUDA_FLAGS, *(["-DS1_TUNING"] if tuning else []), "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode:
         return obj, r.stderr + r.stdout
     return obj, None
 
 
-def build(jobs=8, force=False, verbose=False):
+def build(jobs=8, force=False, verbose=False, tuning=False):
+    """tuning: compile with -DS1_TUNING (kernel-choice overrides read from the environment,
+    for calibration runs only); forces a full rebuild, as does the next product build."""
+    stamp = os.path.join(OBJ, "tuning.stamp")
+    if tuning != os.path.exists(stamp):
+        force = True
     os.makedirs(OUT, exist_ok=True)
     os.makedirs(OBJ, exist_ok=True)
     srcs = [os.path.join(CSRC, s) for s in CU_SOURCES]
     errors = []
     objs = []
     with cf.ThreadPoolExecutor(jobs) as ex:
-        for obj, err in ex.map(lambda s: compile_cu(s, force), srcs):
+        for obj, err in ex.map(lambda s: compile_cu(s, force, tuning), srcs):
             objs.append(obj)
             if err:
                 errors.append(err)
     if errors:
         raise RuntimeError("nvcc failed:\n" + "\n".join(errors))
+    if tuning:
+        open(stamp, "w").close()
+    elif os.path.exists(stamp):
+        os.remove(stamp)
     lib = os.path.join(OUT, "libqwen3_5_cuda.so")
     if force or _newer(lib, objs):
         cmd = [NVCC, *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", lib, *objs, "-lcudart_static", "-lrt",
@@ -90,9 +99,10 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--jobs", type=int, default=8)
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--tuning", action="store_true", help="kernel-choice overrides from the environment")
     a = ap.parse_args()
     try:
-        build(a.jobs, a.force, verbose=True)
+        build(a.jobs, a.force, verbose=True, tuning=a.tuning)
     except RuntimeError as e:
         print(e, file=sys.stderr)
         sys.exit(1)

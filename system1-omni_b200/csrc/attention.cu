@@ -1,21 +1,19 @@
 // Full-attention layers of the Qwen3.5 prefill: q/k preparation and gated GQA
 // flash attention (head dim 256).
 //
-// attn_prep: one warp per (token, head); each lane holds 8 consecutive dims (one
-// 16-byte load). Per-head zero-centred RMSNorm (one bf16 rounding), then partial
-// rotary embedding on the first 2*half dims (rotate_half; each product and the
-// sum rounded to bf16 as Transformers does in bf16); the partner of dim d < half
+// attn_prep (prep_fast_kernel): one warp per 4 (token, head) units; each lane holds 8
+// consecutive dims (one 16-byte load). Per-head zero-centred RMSNorm (one bf16 rounding),
+// then partial rotary embedding on the first 2*half dims (rotate_half; each product and
+// the sum rounded to bf16 as Transformers does in bf16); the partner of dim d < half
 // (dim d + half) sits in lane ^ (half / 8). The gate half of each q row is copied out.
 //
-// flash attention: a CTA takes 128 queries of one head (8 warps x 16 rows) and
-// walks 64-key tiles up to its last query; K/V tiles are double-buffered with
-// cp.async; QK^T and PV run on mma.sync m16n8k16 (bf16 in, fp32 accumulate);
-// online softmax in base 2 with fp32 running max/sum; probabilities rounded to
-// bf16 for PV; the gated epilogue is bf16(bf16(att) * bf16(sigmoid(gate))).
-// One kernel serves every entry point through its arguments: packed sequences
-// (a SeqTable), an immutable shared prefix K/V read before each sequence's own
-// rows (positions continue after it), a windowed first query row, and the
-// bidirectional / prefix-bidirectional masks.
+// flash attention (flash_tc): tcgen05 MMAs with S, P and O in tensor memory, fed by TMA;
+// see the comment above the kernel. One kernel serves every entry point through its
+// arguments: packed sequences (a SeqTable), an immutable shared prefix K/V read before
+// each sequence's own rows (positions continue after it), a windowed first query row,
+// and the bidirectional / prefix-bidirectional masks. Operands must start on 16-byte
+// boundaries and a shared prefix must be whole 64-key tiles; other calls are refused
+// with cudaErrorInvalidValue before any launch.
 #include <climits>
 #include <cstdlib>
 #include <cstring>
@@ -33,98 +31,6 @@ constexpr int DH = 256;
 
 // ---------------------------------------------------------------- prep ----
 constexpr int PREP_UNITS = 4;  // (token, head) units per warp, loads of all issued first
-__global__ void prep_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
-                            const bf16* __restrict__ qw, const bf16* __restrict__ kw, const bf16* __restrict__ cosb,
-                            const bf16* __restrict__ sinb, bf16* __restrict__ q, bf16* __restrict__ gate,
-                            bf16* __restrict__ k, int T, int Hq, int Hk, int half, float eps, bool cs_vec) {
-    grid_dep_wait();
-    grid_dep_launch();
-    // 32-bit unit indices (T * heads < 2^31 is checked on the host)
-    const int unit0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * PREP_UNITS;
-    const int lane = threadIdx.x & 31;
-    const int heads = Hq + Hk;
-    const int units = T * heads;
-    const int d0 = lane * 8;
-    const int rot = 2 * half;  // a lane's 8 dims are all rotated or all passed through (half % 8 == 0)
-    Pack8 xr[PREP_UNITS], gr[PREP_UNITS];
-#pragma unroll
-    for (int i = 0; i < PREP_UNITS; i++) {
-        const int u = unit0 + i;
-        if (u < units) {
-            const int t = u / heads, hh = u - t * heads;
-            if (hh < Hq) {
-                const bf16* src = qg + (size_t)t * ld + (size_t)hh * 2 * DH;
-                xr[i] = ld8(src + d0);
-                gr[i] = ld8(src + DH + d0);
-            } else {
-                xr[i] = ld8(kr + (size_t)t * ld + (size_t)(hh - Hq) * DH + d0);
-            }
-        }
-    }
-    float wq[8], wk[8];
-    unpack8(ld8(qw + d0), wq);
-    unpack8(ld8(kw + d0), wk);
-#pragma unroll
-    for (int i = 0; i < PREP_UNITS; i++) {
-        const int u = unit0 + i;
-        if (u >= units) break;  // uniform over the warp
-        const int t = u / heads, hh = u - t * heads;
-        const bool is_q = hh < Hq;
-        const int h = is_q ? hh : hh - Hq;
-        float x[8];
-        unpack8(xr[i], x);
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; e++) ss = fmaf(x[e], x[e], ss);
-        const float inv = rsqrtf(warp_sum(ss) / DH + eps);
-#pragma unroll
-        for (int e = 0; e < 8; e++) x[e] = x[e] * inv * (1.f + (is_q ? wq[e] : wk[e]));
-        rbf8(x);
-        float cs[8], sn[8];
-        if (d0 < rot) {
-            const size_t f0 = (size_t)t * half + d0 % half;
-            if (cs_vec) {
-                unpack8(ld8(cosb + f0), cs);
-                unpack8(ld8(sinb + f0), sn);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    cs[e] = f32(cosb[f0 + e]);
-                    sn[e] = f32(sinb[f0 + e]);
-                }
-            }
-        }
-        float y[8], ps[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const float partner = __shfl_xor_sync(0xffffffffu, x[e], half / 8);
-            y[e] = x[e] * cs[e];
-            ps[e] = (d0 < half ? -partner : partner) * sn[e];
-        }
-        if (d0 < rot) {
-            rbf8(y);
-            rbf8(ps);
-#pragma unroll
-            for (int e = 0; e < 8; e++) y[e] += ps[e];  // rounded by the pack below
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; e++) y[e] = x[e];
-        }
-        if (is_q) {
-            st8(q + ((size_t)t * Hq + h) * DH + d0, pack8(y));
-            st8(gate + ((size_t)t * Hq + h) * DH + d0, gr[i]);
-        } else {
-            st8(k + ((size_t)t * Hk + h) * DH + d0, pack8(y));
-        }
-    }
-}
-
-// The same prep with fewer instructions per unit (the kernel is issue-bound): one
-// division per warp (the units' tokens and heads follow by increments), the rotary rows
-// loaded with the inputs and unpacked once when the warp's units share a token (always
-// when PREP_UNITS divides Hq + Hk), the rotate-half sign folded into the sine, and the
-// norm and rotary products in packed f32x2 (lane-for-lane the scalar roundings).
-// Needs 16-byte aligned rotary tables and Hq + Hk >= 2.
 __global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
                                  const bf16* __restrict__ qw, const bf16* __restrict__ kw,
                                  const bf16* __restrict__ cosb, const bf16* __restrict__ sinb, bf16* __restrict__ q,
@@ -229,11 +135,6 @@ __global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restric
 }
 
 // ---------------------------------------------------------------- flash ----
-constexpr int BM = 128, BN = 64, WARPS = 8, THREADS = WARPS * 32;
-constexpr int LDS = DH + 8;  // padded smem row (528 B): ldmatrix rows hit distinct banks
-constexpr int TILE_Q = BM * LDS, TILE_KV = BN * LDS;
-constexpr int SMEM = (TILE_Q + 4 * TILE_KV) * 2;
-
 struct Args {
     const bf16* q;
     const bf16* k;
@@ -250,200 +151,6 @@ struct Args {
     float scale_log2;
     int gated, causal;
 };
-
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-    const uint32_t s = tc::smem_u32(smem);
-    const int n = valid ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const bf16* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(tc::smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const bf16* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(tc::smem_u32(p)));
-}
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-__global__ void __launch_bounds__(THREADS, 1) flash_kernel(Args a, SeqTable tab) {
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    bf16* qs = reinterpret_cast<bf16*>(smem_raw);
-    bf16* ks = qs + TILE_Q;  // [2][BN][LDS]
-    bf16* vs = ks + 2 * TILE_KV;
-    const int seq = tab.order[blockIdx.z], h = blockIdx.y, hk = h / (a.Hq / a.Hk);
-    const int off = tab.offset[seq];
-    const int len = tab.offset[seq + 1] - off;
-    const int qrows = len - a.q_base;
-    const int nblocks = (qrows + BM - 1) / BM;
-    if ((int)blockIdx.x >= nblocks) return;
-    const int qb = nblocks - 1 - (int)blockIdx.x;   // longest causal blocks first
-    const int q0 = a.q_base + qb * BM;               // first own query row of this block
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = lane >> 2, t4 = lane & 3;
-    const int P = a.P;
-    const int total = P + len;                        // keys visible to this sequence
-    const int qpos0 = P + q0;                         // absolute position of the block's first query
-    // keys needed: causal -> up to the block's last query; otherwise all
-    const int kv_end = a.causal ? min(total, qpos0 + BM) : total;
-
-    for (int c = tid; c < BM * (DH / 8); c += THREADS) {
-        const int r = c / (DH / 8), col = (c % (DH / 8)) * 8;
-        const int row = min(q0 + r, len - 1);
-        cp_async16(qs + r * LDS + col, a.q + ((size_t)(off + row) * a.Hq + h) * DH + col, q0 + r < len);
-    }
-    auto load_kv = [&](int tile, int buf) {
-        const int k0 = tile * BN;
-        for (int c = tid; c < BN * (DH / 8); c += THREADS) {
-            const int r = c / (DH / 8), col = (c % (DH / 8)) * 8;
-            const int key = min(k0 + r, total - 1);
-            const bool valid = k0 + r < total;
-            const bf16* ksrc;
-            const bf16* vsrc;
-            if (key < P) {
-                ksrc = a.pk + ((size_t)key * a.Hk + hk) * DH + col;
-                vsrc = a.pv + ((size_t)key * a.Hk + hk) * DH + col;
-            } else {
-                const size_t row = (size_t)(off + key - P);
-                ksrc = a.k + (row * a.Hk + hk) * DH + col;
-                vsrc = a.v + row * a.ldv + (size_t)hk * DH + col;
-            }
-            cp_async16(ks + buf * TILE_KV + r * LDS + col, ksrc, valid);
-            cp_async16(vs + buf * TILE_KV + r * LDS + col, vsrc, valid);
-        }
-    };
-    const int ntiles = (kv_end + BN - 1) / BN;
-    load_kv(0, 0);
-    cp_commit();
-
-    float o[DH / 8][4];
-#pragma unroll
-    for (int n = 0; n < DH / 8; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-    const int wrow0 = qpos0 + warp * 16;  // absolute position of this warp's first row
-    const int rows_valid = len - (q0 + warp * 16);
-
-    for (int tile = 0; tile < ntiles; tile++) {
-        const int buf = tile & 1;
-        if (tile + 1 < ntiles) load_kv(tile + 1, buf ^ 1);
-        cp_commit();
-        cp_wait<1>();
-        __syncthreads();
-        const int k0 = tile * BN;
-        const bf16* kb = ks + buf * TILE_KV;
-        const bf16* vb = vs + buf * TILE_KV;
-        // does this warp see any key of the tile?
-        bool active = rows_valid > 0;
-        if (a.causal) active = active && k0 <= wrow0 + 15;
-        if (active) {
-            float sc[BN / 8][4];
-#pragma unroll
-            for (int n = 0; n < BN / 8; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-#pragma unroll
-            for (int kk = 0; kk < DH; kk += 16) {
-                uint32_t af[4];
-                ldsm_x4(af, qs + (warp * 16 + (lane & 15)) * LDS + kk + (lane >> 4) * 8);
-#pragma unroll
-                for (int n = 0; n < BN / 8; n += 2) {
-                    uint32_t bfr[4];
-                    ldsm_x4(bfr, kb + (n * 8 + (lane & 7) + (lane >> 4) * 8) * LDS + kk + ((lane >> 3) & 1) * 8);
-                    mma16816(sc[n], af, bfr[0], bfr[1]);
-                    mma16816(sc[n + 1], af, bfr[2], bfr[3]);
-                }
-            }
-            float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-            for (int n = 0; n < BN / 8; n++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const int key = k0 + n * 8 + 2 * t4 + (e & 1);
-                    const int qpos = wrow0 + g + (e >> 1) * 8;
-                    bool vis = key < total;
-                    if (a.causal) vis = vis && key <= qpos;
-                    else if (a.state > 0 && qpos < a.state) vis = vis && key < a.state;
-                    sc[n][e] = vis ? sc[n][e] * a.scale_log2 : -INFINITY;
-                    mx[e >> 1] = fmaxf(mx[e >> 1], sc[n][e]);
-                }
-            float alpha[2], base2[2];
-#pragma unroll
-            for (int r = 0; r < 2; r++) {
-                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-                const float mn = fmaxf(m[r], mx[r]);
-                base2[r] = mn == -INFINITY ? 0.f : mn;
-                alpha[r] = exp2f(m[r] - base2[r]);
-                m[r] = mn;
-                l[r] *= alpha[r];
-            }
-#pragma unroll
-            for (int n = 0; n < BN / 8; n++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    sc[n][e] = exp2f(sc[n][e] - base2[e >> 1]);
-                    l[e >> 1] += sc[n][e];
-                }
-#pragma unroll
-            for (int n = 0; n < DH / 8; n++) {
-                o[n][0] *= alpha[0];
-                o[n][1] *= alpha[0];
-                o[n][2] *= alpha[1];
-                o[n][3] *= alpha[1];
-            }
-#pragma unroll
-            for (int j = 0; j < BN / 16; j++) {
-                uint32_t pa[4];
-                pa[0] = pack_bf16x2(sc[2 * j][0], sc[2 * j][1]);
-                pa[1] = pack_bf16x2(sc[2 * j][2], sc[2 * j][3]);
-                pa[2] = pack_bf16x2(sc[2 * j + 1][0], sc[2 * j + 1][1]);
-                pa[3] = pack_bf16x2(sc[2 * j + 1][2], sc[2 * j + 1][3]);
-#pragma unroll
-                for (int n = 0; n < DH / 8; n += 2) {
-                    uint32_t bfr[4];
-                    ldsm_x4_t(bfr, vb + (j * 16 + (lane & 7) + ((lane >> 3) & 1) * 8) * LDS + n * 8 + (lane >> 4) * 8);
-                    mma16816(o[n], pa, bfr[0], bfr[1]);
-                    mma16816(o[n + 1], pa, bfr[2], bfr[3]);
-                }
-            }
-        }
-        __syncthreads();  // the next prefetch overwrites this buffer
-    }
-    cp_wait<0>();
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
-        l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
-    }
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        const int lrow = q0 + warp * 16 + g + r * 8;  // own row index
-        if (lrow >= len) continue;
-        const float inv = 1.f / l[r];
-        const size_t orow = ((size_t)(off + lrow) * a.Hq + h) * DH;
-#pragma unroll
-        for (int n = 0; n < DH / 8; n++) {
-            const int col = n * 8 + 2 * t4;
-            float x0 = o[n][2 * r] * inv, x1 = o[n][2 * r + 1] * inv;
-            if (a.gated) {
-                const __nv_bfloat162 gv = *reinterpret_cast<const __nv_bfloat162*>(a.gate + orow + col);
-                x0 = rbf(x0) * rbf(sigmoid(__low2float(gv)));
-                x1 = rbf(x1) * rbf(sigmoid(__high2float(gv)));
-            }
-            *reinterpret_cast<uint32_t*>(a.out + orow + col) = pack_bf16x2(x0, x1);
-        }
-    }
-}
 
 // ------------------------------------------------------- flash (tcgen05) ----
 // A CTA takes 128 queries of one head. Per 128-key tile j:
@@ -463,7 +170,7 @@ namespace tca {
 
 constexpr int BM = 128, BN = 128, THREADS = 192;
 constexpr int SUB = 128 * 128;  // one [128 rows][64 bf16] swizzled tile, 16 KB
-constexpr int OFF_Q = 0, OFF_K = 4 * SUB, OFF_V = 8 * SUB, OFF_P = 12 * SUB, OFF_BAR = 14 * SUB;
+constexpr int OFF_Q = 0, OFF_K = 4 * SUB, OFF_V = 8 * SUB, OFF_BAR = 12 * SUB;
 constexpr int SMEM = OFF_BAR + 256 + 1024;
 constexpr uint32_t ID_S = tc::idesc(128, BN, tc::AB_BF16);
 constexpr uint32_t ID_O = tc::idesc_major(128, DH, tc::AB_BF16, 0, 1);
@@ -484,12 +191,11 @@ __device__ __forceinline__ int query_blocks(const SeqTable& tab, int i, int q_ba
     return rows > 0 ? (rows + BM - 1) / BM : 0;
 }
 
-// PT: P in tensor memory. The softmax warps write bf16 P_j over the first 64 columns of
+// P lives in tensor memory. The softmax warps write bf16 P_j over the first 64 columns of
 // its own S buffer (two keys per 32-bit column) and PV_j reads its A operand from there, so
-// P is double-buffered with S: the softmax of tile j + 1 no longer waits for PV_j (only a
+// P is double-buffered with S: the softmax of tile j + 1 does not wait for PV_j (only a
 // rescale of O does), and S_{j+2} is issued into a buffer once PV_j, its last reader, is
-// complete. Without PT, P goes through one shared-memory tile.
-template <bool PT>
+// complete.
 __global__ void __launch_bounds__(THREADS, 1)
     flash_tc(const __grid_constant__ Maps maps, Args a, SeqTable tab) {
     using namespace tc;
@@ -499,12 +205,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* smem = smem_raw + (base - raw);
     const uint32_t bars = base + OFF_BAR;
     const uint32_t q_full = bars, k_full = bars + 8, k_empty = bars + 40, v_full = bars + 72, v_empty = bars + 80;
-    const uint32_t s_full = bars + 88, s_free = bars + 104, p_full = bars + 120, pv_done = bars + 128;
+    const uint32_t s_full = bars + 88, s_free = bars + 104, pv_done = bars + 128;
     const uint32_t drain = bars + 136, pv_done1 = bars + 144;
-    // PV_i completion: one barrier (parity i & 1), or with PT one per S/P buffer (parity (i >> 1) & 1),
-    // so that a waiter is never two phases behind: with PT the softmax does not wait for every PV
-    auto pv_bar = [&](int i) { return PT && (i & 1) ? pv_done1 : pv_done; };
-    auto pv_par = [&](int i) { return (uint32_t)(PT ? i >> 1 : i) & 1u; };
+    // PV_i completion: one barrier per S/P buffer (parity (i >> 1) & 1), so that a waiter is
+    // never two phases behind (the softmax does not wait for every PV)
+    auto pv_bar = [&](int i) { return (i & 1) ? pv_done1 : pv_done; };
+    auto pv_par = [&](int i) { return (uint32_t)(i >> 1) & 1u; };
     int* info = reinterpret_cast<int*>(smem + OFF_BAR + 160);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 192);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -550,7 +256,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(s_full + 8, 1);
         mbar_init(s_free, 4);  // one arrive per softmax warp
         mbar_init(s_free + 8, 4);
-        mbar_init(p_full, 4);
         mbar_init(pv_done, 1);
         mbar_init(pv_done1, 1);
         mbar_init(drain, 1);
@@ -632,21 +337,17 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = mbar_wait(q_full, 0);
             tc_fence_after();
             auto pv = [&](int i) -> bool {
-                // PT: P_i is announced on its buffer's own barrier (s_free is unused then), so the
-                // softmax running a tile ahead cannot complete a second phase before this wait
-                const bool p_ok = PT ? mbar_wait(s_free + 8 * (i & 1), (uint32_t)(i >> 1) & 1u)
-                                     : mbar_wait(p_full, (uint32_t)i & 1u);
+                // P_i is announced on its buffer's own barrier, so the softmax running a tile
+                // ahead cannot complete a second phase before this wait
+                const bool p_ok = mbar_wait(s_free + 8 * (i & 1), (uint32_t)(i >> 1) & 1u);
                 if (!p_ok || !mbar_wait(v_full, (uint32_t)i & 1u)) return false;
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; kk++) {
                     const uint64_t vd = desc_sw128_mn(base + OFF_V + kk * 2048, SUB, 1024);
                     const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-                    if constexpr (PT)  // 16 keys = 8 packed columns of P_i
-                        mma_bf16_ts(tmem + 256, tmem + (uint32_t)((i & 1) * BN + kk * 8), vd, ID_O, acc);
-                    else
-                        mma_bf16(tmem + 256, desc_sw128(base + OFF_P + (kk >> 2) * SUB + (kk & 3) * 32), vd, ID_O,
-                                 acc);
+                    // 16 keys = 8 packed columns of P_i
+                    mma_bf16_ts(tmem + 256, tmem + (uint32_t)((i & 1) * BN + kk * 8), vd, ID_O, acc);
                 }
                 mma_commit(v_empty);
                 mma_commit(pv_bar(i));
@@ -654,10 +355,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             };
             for (int j = 0; ok && j < n; j++) {
                 const int b = j & 1;
-                // buffer b is free once the softmax has read S_{j-2} (and, with P in it, PV_{j-2}
-                // has completed; PV_{j-1} is not issued yet, so the parity names PV_{j-2})
-                if (j >= 2 && !(PT ? mbar_wait(pv_bar(j - 2), pv_par(j - 2))
-                                   : mbar_wait(s_free + 8 * b, (uint32_t)((j - 2) >> 1) & 1u))) {
+                // buffer b is free once PV_{j-2}, the last reader of P_{j-2} in it, has completed
+                // (PV_{j-1} is not issued yet, so the parity names PV_{j-2})
+                if (j >= 2 && !mbar_wait(pv_bar(j - 2), pv_par(j - 2))) {
                     ok = false;
                     break;
                 }
@@ -716,11 +416,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int c = 0; c < 4; c++) tmem_ld32(lane_addr + b * BN + c * 32, s[c]);
             tmem_ld_wait();
-            if constexpr (!PT) {
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(s_free + 8 * b);
-            }
             const int k0 = j * BN;
             bool full = k0 + BN <= total;
             if (a.causal)
@@ -758,9 +453,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             mx *= sl2;
             const bool grow = mx > m + RESCALE_LOG2;
-            // PV_{j-1} must be complete before O is rescaled (and, with P in shared memory,
-            // before P is overwritten); PV_{j-2} is, since S_j was issued after it
-            if (j > 0 && (!PT || __any_sync(0xffffffffu, grow)) &&
+            // PV_{j-1} must be complete before O is rescaled; PV_{j-2} is, since S_j was issued
+            // after it
+            if (j > 0 && __any_sync(0xffffffffu, grow) &&
                 !__all_sync(0xffffffffu, mbar_wait(pv_bar(j - 1), pv_par(j - 1)))) {
                 ok = false;
                 break;
@@ -783,12 +478,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_st_wait();
             }
             const float nm = m == -INFINITY ? 0.f : -m;
-            uint8_t* prow = smem + OFF_P;
             float2 l2[4];  // row-sum chains of keys e = 2p, 2p + 1 (mod 8), in f32x2 pairs
 #pragma unroll
             for (int i = 0; i < 4; i++) l2[i] = make_float2(0.f, 0.f);
             const float2 sl22 = make_float2(sl2, sl2), nm2 = make_float2(nm, nm);
-            uint32_t pk[32];  // PT: 64 keys of P as bf16 pairs (one tcgen05.st of 32 columns)
+            uint32_t pk[32];  // 64 keys of P as bf16 pairs (one tcgen05.st of 32 columns)
 #pragma unroll
             for (int c = 0; c < 4; c++) {
 #pragma unroll
@@ -801,29 +495,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                         f[e + 1] = ex2(t.y);
                         l2[e >> 1] = add2(l2[e >> 1], make_float2(f[e], f[e + 1]));
                     }
-                    if constexpr (PT) {
 #pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
-                            pk[(c & 1) * 16 + g8 * 4 + e] = *reinterpret_cast<const uint32_t*>(&h2);
-                        }
-                    } else {
-                        const int chunk = c * 4 + g8;  // 16-byte chunk of the 128-key row
-                        *reinterpret_cast<Pack8*>(prow + (chunk >> 3) * SUB + sw128_offset(r, chunk & 7)) = pack8(f);
+                    for (int e = 0; e < 4; e++) {
+                        const __nv_bfloat162 h2 = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+                        pk[(c & 1) * 16 + g8 * 4 + e] = *reinterpret_cast<const uint32_t*>(&h2);
                     }
                 }
-                if constexpr (PT) {
-                    if (c & 1) tmem_st32(lane_addr + b * BN + (c >> 1) * 32, *reinterpret_cast<const float(*)[32]>(pk));
-                }
+                if (c & 1) tmem_st32(lane_addr + b * BN + (c >> 1) * 32, *reinterpret_cast<const float(*)[32]>(pk));
             }
             l += ((l2[0].x + l2[0].y) + (l2[1].x + l2[1].y)) + ((l2[2].x + l2[2].y) + (l2[3].x + l2[3].y));
-            if constexpr (PT)
-                tmem_st_wait();
-            else
-                fence_async_smem();
+            tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(PT ? s_free + 8 * b : p_full);
+            if (lane == 0) mbar_arrive(s_free + 8 * b);
         }
         if (ok && n > 0) ok = mbar_wait(pv_bar(n - 1), pv_par(n - 1));
         tc_fence_after();
@@ -884,29 +568,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-bool use_tc() {
-    static const bool on = [] {
-        const char* e = getenv("S1_ATTN_TC");
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
-
-bool p_in_tmem() {
-    static const bool on = [] {
-        const char* e = getenv("S1_ATTN_PT");
-        return !(e && e[0] == '0');
-    }();
-    return on;
-}
-
 int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
-    static const cudaError_t configured = [] {
-        cudaError_t e = cudaFuncSetAttribute(flash_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-        return e == cudaSuccess
-                   ? cudaFuncSetAttribute(flash_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM)
-                   : e;
-    }();
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(flash_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (configured != cudaSuccess) return configured;
     const int rows = tab.offset[tab.count];
     Maps maps;
@@ -917,7 +581,7 @@ int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pk, a.pk, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pv, a.pv, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (e) return e;
-    return launch_pdl(p_in_tmem() ? flash_tc<true> : flash_tc<false>, dim3(a.Hq, blocks), dim3(THREADS), SMEM, st,
+    return launch_pdl(flash_tc, dim3(a.Hq, blocks), dim3(THREADS), SMEM, st,
                       maps, a, tab);
 }
 
@@ -929,19 +593,16 @@ int launch(Args a, const SeqTable& tab, cudaStream_t st) {
     for (int i = 0; i < tab.count; i++) {
         const int rows = tab.offset[i + 1] - tab.offset[i] - a.q_base;
         max_rows = max(max_rows, rows);
-        if (rows > 0) blocks += (rows + BM - 1) / BM;
+        if (rows > 0) blocks += (rows + tca::BM - 1) / tca::BM;
     }
     if (max_rows <= 0) return cudaSuccess;
+    // TMA tiles: every operand starts on a 16-byte boundary and the shared prefix is whole
+    // 64-key tiles (the reference's own shared-prefix entry point asks the same of it)
     const bool aligned = aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.out) &&
                          (!a.gated || aligned16(a.gate)) &&
                          (a.P == 0 || (a.P % 64 == 0 && aligned16(a.pk) && aligned16(a.pv)));
-    if (aligned && tca::use_tc()) return tca::launch_tc(a, tab, blocks, st);
-    static const cudaError_t configured =
-        cudaFuncSetAttribute(flash_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
-    if (configured != cudaSuccess) return configured;
-    const dim3 grid((max_rows + BM - 1) / BM, a.Hq, tab.count);
-    flash_kernel<<<grid, THREADS, SMEM, st>>>(a, tab);
-    return cudaGetLastError();
+    if (!aligned) return cudaErrorInvalidValue;
+    return tca::launch_tc(a, tab, blocks, st);
 }
 
 Args make_args(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out, int Hq, int Hk,
@@ -985,7 +646,7 @@ extern "C" {
 int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const void* kw, const void* cos,
                   const void* sin, void* q, void* gate, void* k, int T, int Hq, int Hk, int Dh, int half, float eps,
                   void* stream) {
-    if (ld % 8 != 0 || T < 0 || Hq < 0 || Hk < 0) return cudaErrorInvalidValue;
+    if (ld % 8 != 0 || T < 0 || Hq < 1 || Hk < 1) return cudaErrorInvalidValue;
     if (Dh != attn::DH || half <= 0 || half % 8 != 0 || 2 * half > Dh || ((half / 8) & (half / 8 - 1)))
         return cudaErrorInvalidValue;
     const long units = (long)T * (Hq + Hk);
@@ -995,21 +656,14 @@ int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const 
     if (!aligned16(qg) || !aligned16(kr) || !aligned16(qw) || !aligned16(kw) || !aligned16(q) || !aligned16(gate) ||
         !aligned16(k))
         return cudaErrorInvalidValue;
+    if (!aligned16(cos) || !aligned16(sin)) return cudaErrorInvalidValue;
     constexpr int WPB = 8;
-    const bool cs_vec = aligned16(cos) && aligned16(sin);
-    // (with Hq + Hk >= 2 the PREP_UNITS = 4 units of a warp fall in at most two tokens)
-    if (cs_vec && Hq + Hk >= 2 && !legacy_elementwise())
-        return launch_pdl(attn::prep_fast_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
-                          static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg),
-                          static_cast<const bf16*>(kr), ld, static_cast<const bf16*>(qw),
-                          static_cast<const bf16*>(kw), static_cast<const bf16*>(cos), static_cast<const bf16*>(sin),
-                          static_cast<bf16*>(q), static_cast<bf16*>(gate), static_cast<bf16*>(k), T, Hq, Hk, half,
-                          eps);
-    return launch_pdl(attn::prep_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
+    // (Hq >= Hk >= 1, so Hq + Hk >= 2: the PREP_UNITS = 4 units of a warp fall in at most two tokens)
+    return launch_pdl(attn::prep_fast_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
                       static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg), static_cast<const bf16*>(kr),
                       ld, static_cast<const bf16*>(qw), static_cast<const bf16*>(kw), static_cast<const bf16*>(cos),
                       static_cast<const bf16*>(sin), static_cast<bf16*>(q), static_cast<bf16*>(gate),
-                      static_cast<bf16*>(k), T, Hq, Hk, half, eps, aligned16(cos) && aligned16(sin));
+                      static_cast<bf16*>(k), T, Hq, Hk, half, eps);
 }
 
 int cs1_attention(const void* q, const void* k, const void* v, int ldv, void* out, int T, int Hq, int Hk, int Dh,

@@ -273,7 +273,7 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
     if (vec) {
         // 4 channels per thread: twice the threads at half the registers each (64: 8 CTAs of 128
         // threads per SM instead of 4), which keeps more rows in flight
-        const bool narrow = conv_narrow() && key_dim % 4 == 0;
+        const bool narrow = key_dim % 4 == 0;  // 4 channels per thread (8 per thread otherwise)
         const int cpt = narrow ? 4 : 8, tpacks = (2 * key_dim + value_dim) / cpt;
         const long groups = (tpacks + 127) / 128;
         // Runs of 64 rows, shortened (to 32, then 16) while the grid is below two waves of

@@ -1056,12 +1056,13 @@ struct Handle {
     int device = 0;
     int sms = 148;
     int fixed_m = 0;
-    bool pairs = true;  // CTA-pair kernels for large M (S1_GEMM_PAIRS=0 selects the single-CTA kernels)
-    int group = 0;      // tile grouping (0: the kernels' defaults; S1_GEMM_GROUP overrides, for tuning)
-    bool swap = true;   // swapped-operand kernel for few rows (S1_GEMM_SWAP=0 disables)
-    // Tuning override (S1_GEMM_KERNEL = pair | row256 | row128 | swap | swap2, S1_GEMM_NT =
-    // the swapped kernels' rows of x per tile): every call of the handle uses that kernel
-    // where the shape allows it. 0 = the wave model's choice.
+    // The fields below are fixed in product builds; a build with -DS1_TUNING (build.py
+    // --tuning) reads them from S1_GEMM_PAIRS, S1_GEMM_GROUP, S1_GEMM_SWAP, S1_GEMM_KERNEL
+    // (pair | row256 | row128 | swap | swap2) and S1_GEMM_NT to calibrate the kernel choice.
+    bool pairs = true;  // CTA-pair kernels for large M
+    int group = 0;      // tile grouping (0: the kernels' defaults)
+    bool swap = true;   // swapped-operand kernel for few rows
+    // forced kernel (0 = the wave model's choice) and the swapped kernels' rows of x per tile
     int force = 0, force_nt = 0;
 };
 enum Force : int { FORCE_NONE = 0, FORCE_PAIR, FORCE_ROW256, FORCE_ROW128, FORCE_SWAP, FORCE_SWAP2 };
@@ -1196,8 +1197,8 @@ int launch_swap_pair(const Handle* h, const void* x, const void* w, void* y, int
 // kernel choice below (waves x per-tile time relative to a 256 x 256 CTA-pair tile).
 // A tile of 128 w rows x nt rows costs nt / 256 of a 128 x 256 single-CTA tile, scaled up
 // where its operand bytes per MMA cycle (8192 / nt + 64; SwiGLU 8192 / nt + 32) exceed
-// what the 128 x 256 tiles sustain (~90 B / cycle / SM). Constants fitted to
-// `python -m s1omni.gemm_tune` sweeps of the 27B shapes.
+// what the 128 x 256 tiles sustain (~90 B / cycle / SM). Constants fitted to sweeps of the
+// 27B shapes with each kernel forced in turn (a -DS1_TUNING build).
 double swap_cost(int M, int N, int epi, int sms, int& best_nt) {
     const bool sw = epi == EPI_SWIGLU;
     const long tiles_w = sw ? N / 256 : (N + BM - 1) / BM;
@@ -1364,6 +1365,8 @@ void* cs1_gemm_create(size_t workspace_bytes) {
         return nullptr;
     }
     h->sms = host::num_sms();
+#ifdef S1_TUNING
+    // tuning builds only (build.py --tuning): kernel overrides for calibrating the wave model
     const char* env = getenv("S1_GEMM_PAIRS");
     h->pairs = !(env && env[0] == '0');
     const char* grp = getenv("S1_GEMM_GROUP");
@@ -1377,6 +1380,7 @@ void* cs1_gemm_create(size_t workspace_bytes) {
                  : k == "swap2" ? gemm::FORCE_SWAP2 : gemm::FORCE_NONE;
     }
     if (const char* nt = getenv("S1_GEMM_NT")) h->force_nt = atoi(nt);
+#endif
     return h;
 }
 

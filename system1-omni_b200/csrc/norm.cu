@@ -15,6 +15,7 @@ namespace {
 constexpr int NT = 256;       // threads per row block
 constexpr int MAXP = 4;       // packs of 8 cached per thread: D <= 8192
 
+// Rows wider than the warp kernel takes (5,120 < D <= 8,192): a CTA per row.
 template <bool Add>
 __global__ void __launch_bounds__(NT) rms_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
                                                  const bf16* __restrict__ x, const bf16* __restrict__ w,
@@ -176,88 +177,7 @@ __global__ void __launch_bounds__(NT) rms_scalar_kernel(bf16* __restrict__ res, 
     for (int i = threadIdx.x; i < D; i += NT) out[row * D + i] = to_bf16(f32(src[row * D + i]) * inv * (1.f + f32(w[i])));
 }
 
-// One warp per (token, head) row of 128; each lane holds 4 values (8 bytes).
-__global__ void gated_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
-                             const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    const size_t base = (size_t)row * 128 + lane * 4;
-    const size_t zb = (size_t)(row / H) * ldz + (size_t)(row % H) * 128 + lane * 4;
-    const uint2 xr = *reinterpret_cast<const uint2*>(x + base);
-    const uint2 zr = *reinterpret_cast<const uint2*>(z + zb);
-    const uint2 wr = *reinterpret_cast<const uint2*>(w + lane * 4);
-    const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xr);
-    const __nv_bfloat162* zp = reinterpret_cast<const __nv_bfloat162*>(&zr);
-    const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wr);
-    float v[4], zz[4], ww[4];
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-        const float2 a = __bfloat1622float2(xp[i]), b = __bfloat1622float2(zp[i]), c = __bfloat1622float2(wp[i]);
-        v[2 * i] = a.x; v[2 * i + 1] = a.y;
-        zz[2 * i] = b.x; zz[2 * i + 1] = b.y;
-        ww[2 * i] = c.x; ww[2 * i + 1] = c.y;
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; i++) ss = fmaf(v[i], v[i], ss);
-    const float inv = rsqrtf(warp_sum(ss) / 128.f + eps);
-    float o[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) o[i] = rbf(ww[i] * rbf(v[i] * inv)) * silu_fast(zz[i]);
-    uint2 r;
-    r.x = pack_bf16x2(o[0], o[1]);
-    r.y = pack_bf16x2(o[2], o[3]);
-    *reinterpret_cast<uint2*>(out + base) = r;
-}
-
-// Half a warp per (token, head) row of 128 (16-byte lane accesses), G_ROWS rows per
-// warp with every load issued before the first row is reduced.
-constexpr int G_ROWS = 8;
-__global__ void gated16_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z, int ldz,
-                               const bf16* __restrict__ w, bf16* __restrict__ out, int rows, int H, float eps) {
-    grid_dep_wait();
-    grid_dep_launch();
-    const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
-    const int row0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * G_ROWS;
-    if (row0 >= rows) return;
-    Pack8 xr[G_ROWS / 2], zr[G_ROWS / 2];
-#pragma unroll
-    for (int i = 0; i < G_ROWS / 2; i++) {
-        const int row = row0 + 2 * i + half;
-        if (row < rows) {
-            xr[i] = ld8(x + (size_t)row * 128 + hl * 8);
-            zr[i] = ld8(z + (size_t)(row / H) * ldz + (size_t)(row % H) * 128 + hl * 8);
-        } else {
-            const float zero[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            xr[i] = zr[i] = pack8(zero);
-        }
-    }
-    float wv[8];
-    unpack8(ld8(w + hl * 8), wv);
-#pragma unroll
-    for (int i = 0; i < G_ROWS / 2; i++) {
-        const int row = row0 + 2 * i + half;
-        float v[8], zz[8];
-        unpack8(xr[i], v);
-        unpack8(zr[i], zz);
-        float ss = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; e++) ss = fmaf(v[e], v[e], ss);
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float inv = rsqrtf(ss / 128.f + eps);
-        float o8[8];
-#pragma unroll
-        for (int e = 0; e < 8; e++) o8[e] = v[e] * inv;
-        rbf8(o8);
-#pragma unroll
-        for (int e = 0; e < 8; e++) o8[e] *= wv[e];
-        rbf8(o8);
-#pragma unroll
-        for (int e = 0; e < 8; e++) o8[e] *= silu_fast(zz[e]);
-        if (row < rows) st8(out + (size_t)row * 128 + hl * 8, pack8(o8));
-    }
-}
+constexpr int G_ROWS = 8;  // (token, head) rows per warp and group: half a warp per row of 128
 
 // The gated norm over a grid-stride loop of G_ROWS-row groups per warp, with each lane's
 // x and z chunks of the next two groups fetched by cp.async into a per-lane ring of
@@ -406,8 +326,7 @@ extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const v
     auto st = static_cast<cudaStream_t>(stream);
     const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(z) |
                            reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(out);
-    const bool vec = ldz % 4 == 0 && (bits & 7) == 0;
-    if (ldz % 8 == 0 && (bits & 15) == 0 && !legacy_elementwise()) {
+    if (ldz % 8 == 0 && (bits & 15) == 0) {
         static const cudaError_t configured =
             cudaFuncSetAttribute(gated_async_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, GA_SMEM);
         if (configured != cudaSuccess) return configured;
@@ -418,16 +337,8 @@ extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const v
                           static_cast<const bf16*>(x), static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w),
                           static_cast<bf16*>(out), rows, H, eps);
     }
-    if (ldz % 8 == 0 && (bits & 15) == 0) {
-        const int per_block = WARPS * G_ROWS;
-        return launch_pdl(gated16_kernel, dim3((rows + per_block - 1) / per_block), dim3(WARPS * 32), 0, st,
-                          static_cast<const bf16*>(x), static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w),
-                          static_cast<bf16*>(out), rows, H, eps);
-    } else if (vec)
-        gated_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
-            static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
-    else
-        gated_scalar_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
-            static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
+    // operands not on 16-byte boundaries: one warp per row, scalar accesses
+    gated_scalar_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
+        static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
     return cudaGetLastError();
 }

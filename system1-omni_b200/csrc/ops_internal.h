@@ -37,12 +37,7 @@ bool make_table(SeqTable& t, const size_t* lengths, size_t count);
 __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-bool pdl_enabled();  // S1_PDL=0 turns the attribute off (plain stream order)
-// S1_ELEM_LEGACY=1 selects the previous versions of the conv, gated-norm and attention-prep
-// kernels (register-staged loads), for timing the two against each other.
-bool legacy_elementwise();
-// S1_CONV_NARROW=0 runs the GDN conv with 8 channels per thread instead of 4.
-bool conv_narrow();
+bool pdl_enabled();  // always on (a build with -DS1_TUNING reads S1_PDL=0 to turn it off)
 int sm_count();  // multiprocessors of the current device (148 when the query fails)
 
 // Launch with the programmatic-serialisation attribute (see grid_dep_wait); the kernel

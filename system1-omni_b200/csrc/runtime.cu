@@ -59,19 +59,16 @@ int make_map_3d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_
 }  // namespace host
 
 bool pdl_enabled() {
+#ifdef S1_TUNING
+    // tuning builds only: S1_PDL=0 launches in plain stream order, for A/B timing
     static const bool on = [] {
         const char* e = getenv("S1_PDL");
         return !(e && e[0] == '0');
     }();
     return on;
-}
-
-bool conv_narrow() {
-    static const bool on = [] {
-        const char* e = getenv("S1_CONV_NARROW");
-        return !(e && e[0] == '0');
-    }();
-    return on;
+#else
+    return true;
+#endif
 }
 
 int sm_count() {
@@ -85,14 +82,6 @@ int sm_count() {
             sms = 148;
     }
     return sms;
-}
-
-bool legacy_elementwise() {
-    static const bool on = [] {
-        const char* e = getenv("S1_ELEM_LEGACY");
-        return e && e[0] == '1';
-    }();
-    return on;
 }
 
 namespace host {
@@ -111,6 +100,21 @@ int num_sms() {
 
 }  // namespace host
 }  // namespace s1
+
+S1_FAULT_WORD(selftest)
+
+namespace {
+// One thread waits, through the same bounded wait as the kernels' pipelines, on an
+// mbarrier that nothing arrives on; when the wait gives up it records FAULT_WAIT_OTHER in
+// this file's fault word and returns. No copy or MMA is in flight, so giving up is safe.
+__global__ void wait_selftest_kernel(long long limit) {
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t b = s1::tc::smem_u32(&bar);
+    s1::tc::mbar_init(b, 1);
+    s1::tc::mbar_fence_init();
+    if (!s1::tc::mbar_wait_for(b, 0, limit)) atomicOr(&g_fault_word, s1::tc::FAULT_WAIT_OTHER);
+}
+}  // namespace
 
 extern "C" uint32_t s1_fault_read_gemm(int clear);
 extern "C" uint32_t s1_fault_read_gdn(int clear);
@@ -184,8 +188,15 @@ int cs1_graph_destroy(void* exec) { return cudaGraphExecDestroy(static_cast<cuda
 
 // Bit mask of the bounded device waits that gave up since the last clear
 // (1 producer, 2 MMA issuer, 4 epilogue, 8 other), OR-ed over the kernel files.
+int cs1_wait_selftest(long long cycles, void* stream) {
+    if (cycles < 1000 || cycles > 4000000000ll) return cudaErrorInvalidValue;
+    wait_selftest_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(cycles);
+    return cudaGetLastError();
+}
+
 uint32_t cs1_fault_status(int clear) {
-    return s1_fault_read_gemm(clear) | s1_fault_read_gdn(clear) | s1_fault_read_attention(clear);
+    return s1_fault_read_gemm(clear) | s1_fault_read_gdn(clear) | s1_fault_read_attention(clear) |
+           s1_fault_read_selftest(clear);
 }
 
 // ---- vision entry points: required symbols of the loader; the vision path is

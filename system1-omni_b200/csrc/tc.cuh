@@ -54,14 +54,18 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Wait for the phase of `parity` to complete; false after about a second.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Wait for the phase of `parity` to complete; false after `limit` cycles.
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, long long limit) {
     if (mbar_try(bar, parity)) return true;
     const long long t0 = clock64();
     while (true) {
         if (mbar_try(bar, parity)) return true;
-        if (clock64() - t0 > S1_WAIT_CYCLES) return false;
+        if (clock64() - t0 > limit) return false;
     }
+}
+// Wait for the phase of `parity` to complete; false after about a second.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, S1_WAIT_CYCLES);
 }
 
 // ---- clusters (CTA pairs for cta_group::2) ----

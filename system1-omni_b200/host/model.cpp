@@ -1122,27 +1122,50 @@ __attribute__((visibility("default"))) int s1_model_forward_shared(void* mp, con
                                                                   float* logits, float* hidden) {
     auto* m = static_cast<Model*>(mp);
     if (!m || !prefix_ids || !suffix_ids) return -1;
-    if (prefix_len < 3 || prefix_len > (size_t)m->cap_tokens) return fail(m, -1, "prefix length out of range");
-    int rc = ensure_prefix(m, (int)prefix_len);
+    if (prefix_len < 1 || prefix_len > (size_t)m->cap_tokens) return fail(m, -1, "prefix length out of range");
+    Batch b;
+    int rc = check_batch(m, suffix_lengths, count, b);
+    if (rc) return rc;
+    // The shared part is the prefix floored to a multiple of 64 tokens (the chunk of the
+    // GDN scan and the key tile of the attention kernels), as the reference floors its
+    // shared prefixes (batching.rs:29-49); the rest of the prefix is prepended to every
+    // suffix, so each candidate's result is that of its full prompt.
+    const size_t shared = prefix_len / 64 * 64, rest = prefix_len - shared;
+    std::vector<int32_t> ids;
+    std::vector<size_t> lens(count);
+    ids.reserve(count * rest + b.rows);
+    size_t at = 0;
+    for (size_t i = 0; i < count; i++) {
+        ids.insert(ids.end(), prefix_ids + shared, prefix_ids + prefix_len);
+        ids.insert(ids.end(), suffix_ids + at, suffix_ids + at + suffix_lengths[i]);
+        at += suffix_lengths[i];
+        lens[i] = rest + suffix_lengths[i];
+    }
+    Batch s;
+    rc = check_batch(m, lens.data(), count, s);
+    if (rc) return rc;
+    if (shared == 0) {  // nothing to share: the full prompts, packed
+        rc = stage_inputs(m, ids.data(), s);
+        if (!rc) rc = execute(m, s, true);
+        return rc ? rc : read_outputs(m, s, logits, hidden);
+    }
+    rc = ensure_prefix(m, (int)shared);
     if (rc) return rc;
     Batch pre;
-    pre.lengths = {prefix_len};
-    pre.rows = prefix_len;
-    pre.prefix = (int)prefix_len;
+    pre.lengths = {shared};
+    pre.rows = shared;
+    pre.prefix = (int)shared;
     pre.capture = true;
     rc = stage_inputs(m, prefix_ids, pre);
     if (rc) return rc;
     rc = execute(m, pre, false);
     if (rc) return rc;
-    Batch b;
-    rc = check_batch(m, suffix_lengths, count, b);
+    s.prefix = (int)shared;
+    rc = stage_inputs(m, ids.data(), s);
     if (rc) return rc;
-    b.prefix = (int)prefix_len;
-    rc = stage_inputs(m, suffix_ids, b);
+    rc = execute(m, s, true);
     if (rc) return rc;
-    rc = execute(m, b, true);
-    if (rc) return rc;
-    return read_outputs(m, b, logits, hidden);
+    return read_outputs(m, s, logits, hidden);
 }
 
 __attribute__((visibility("default"))) int s1_model_stage(void* mp, const int32_t* ids, const size_t* lengths,

@@ -38,6 +38,7 @@ SIGNATURES = {
     "cs1_copy_dd": (I, [P, P, Z, P]),
     "cs1_copy2d": (I, [P, Z, P, Z, Z, Z, P]),
     "cs1_fault_status": (U32, [I]),
+    "cs1_wait_selftest": (I, [ctypes.c_longlong, P]),
     "cs1_embed": (I, [P, P, P, I, I, P]),
     "cs1_rms_norm": (I, [P, P, P, I, I, F, P]),
     "cs1_add_rms_norm": (I, [P, P, P, P, I, I, F, P]),

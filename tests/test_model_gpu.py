@@ -165,3 +165,18 @@ def test_run_layers_composes_to_the_forward(tiny):
     want = OM.run_layers(cfg, W, seqs[0], 0, 2, from_bits(h))
     upd = np.abs(want - from_bits(h)).max()
     assert np.abs(got - want).max() <= 2e-2 * upd, np.abs(got - want).max() / upd
+
+
+def test_shared_prefix_off_the_64_grid_equals_full_prompt(tiny):
+    """A prefix that is not a multiple of 64 tokens: the host shares its first 64k tokens
+    and prepends the rest to every suffix, so each candidate equals its full prompt bit for
+    bit; a prefix under 64 tokens is not shared at all."""
+    cfg, W, m = tiny
+    rng = np.random.default_rng(11)
+    for plen in (100, 30):
+        prefix = rng.integers(0, cfg.vocab, plen).astype(np.int32)
+        suffixes = [rng.integers(0, cfg.vocab, n).astype(np.int32) for n in (5, 64, 17)]
+        shared = m.forward_shared(prefix, suffixes)
+        for i, s in enumerate(suffixes):
+            full = m.forward([np.concatenate([prefix, s])])[0]
+            assert np.array_equal(shared[i], full), (plen, i)

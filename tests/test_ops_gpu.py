@@ -203,3 +203,19 @@ def test_invalid_shapes_are_rejected_before_launch(cs1, stream):
     assert cs1.raw.cs1_attn_prep(p, p, 512, p, p, p, p, p, p, p, 4, 1, 1, 128, 32, 1e-6, stream) != 0
     assert cs1.raw.cs1_embed(p, p, p, 4, 7, stream) != 0
     assert cs1.raw.cs1_silu_mul(p, 4, p, 2, 8, stream) != 0
+
+
+def test_bounded_wait_gives_up_and_reports(cs1, stream):
+    """The kernels' bounded mbarrier wait, cut to ~1 ms and made to run out on a barrier
+    that nothing completes (no copy or MMA in flight): the kernel returns, the fault word
+    reports bit 8, clearing it works, and the context stays usable."""
+    import torch
+    assert cs1.cs1_fault_status(1) == 0
+    cs1.cs1_wait_selftest(2_000_000, stream)
+    torch.cuda.synchronize()
+    assert cs1.cs1_fault_status(0) == 8
+    assert cs1.cs1_fault_status(1) == 8  # read and clear
+    assert cs1.cs1_fault_status(0) == 0
+    x = torch.arange(8, dtype=torch.float32, device="cuda")
+    assert float((x * 2).sum()) == 56.0
+    assert cs1.raw.cs1_wait_selftest(10, stream) != 0  # limits outside 1e3 .. 4e9 are refused
