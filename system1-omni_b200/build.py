@@ -25,7 +25,7 @@ CUDA_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompil
               "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include")]
 
 CU_SOURCES = ["runtime.cu", "norm.cu", "elementwise.cu", "gemm.cu", "attention.cu", "gdn.cu",
-              "head.cu", "gdn_noalloc.cu"]
+              "head.cu", "gdn_noalloc.cu", "gdn_fused.cu"]
 CPP_SOURCES = ["model.cpp", "checkpoint.cpp"]
 
 

@@ -896,10 +896,20 @@ __global__ void __launch_bounds__(SCAN_THREADS, 2)
     }
 }
 
-// Zero-token sequences never reach the kernels; s_out for an empty call is a copy.
+// The bf16 prefill: the fused kernel (gdn_fused.cu), which needs no workspace.
 int run(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o, void* workspace,
         size_t workspace_bytes, const SeqTable& seqs, int H, int HK, float scale, const void* s_in,
         long s_in_stride, void* s_out, cudaStream_t st) {
+    (void)workspace;
+    (void)workspace_bytes;
+    return run_fused(q, k, v, g, beta, o, seqs, H, HK, scale, s_in, s_in_stride, s_out, st);
+}
+
+// The two-kernel form (gdn_prep_tc, then gdn_scan) with its tiles in a caller-provided
+// workspace. Zero-token sequences never reach the kernels; s_out for an empty call is a copy.
+int run_two_pass(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                 void* workspace, size_t workspace_bytes, const SeqTable& seqs, int H, int HK, float scale,
+                 const void* s_in, long s_in_stride, void* s_out, cudaStream_t st) {
     if (!q || !k || !v || !g || !beta || !o || !workspace || H <= 0 || HK <= 0 || H % HK) return cudaErrorInvalidValue;
     GdnTable tab;
     make_gdn_table(tab, seqs);

@@ -41,11 +41,20 @@ struct Layout {
 
 size_t workspace_bytes_for(long slots, int H, bool f32);
 
-// The bf16 chunked prefill over packed sequences with a caller-provided (1024-byte
-// aligned) workspace of workspace_bytes; defined in gdn.cu.
+// The bf16 chunked prefill over packed sequences (gdn.cu): the fused kernel, which
+// ignores the workspace arguments.
 int run(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o, void* workspace,
         size_t workspace_bytes, const SeqTable& seqs, int H, int HK, float scale, const void* s_in,
         long s_in_stride, void* s_out, cudaStream_t st);
+// The fused kernel: preparation and scan of a (head, sequence) in one CTA (gdn_fused.cu).
+int run_fused(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+              const SeqTable& seqs, int H, int HK, float scale, const void* s_in, long s_in_stride, void* s_out,
+              cudaStream_t st);
+// The two-kernel form with its tiles in a caller-provided (1024-byte aligned) workspace of
+// workspace_bytes (gdn.cu).
+int run_two_pass(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                 void* workspace, size_t workspace_bytes, const SeqTable& seqs, int H, int HK, float scale,
+                 const void* s_in, long s_in_stride, void* s_out, cudaStream_t st);
 
 }  // namespace gdn
 }  // namespace s1

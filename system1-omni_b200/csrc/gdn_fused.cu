@@ -1,0 +1,702 @@
+// Chunked Gated DeltaNet prefill in one kernel: the per-chunk preparation and the state
+// scan of a (value head, sequence) run in the same CTA, warp-specialised, so nothing of a
+// chunk goes through global memory between them.
+//
+// Recurrence and chunk form as in gdn.cu (Transformers' torch_chunk_gated_delta_rule,
+// chunks of 64): per chunk, with cum = cumsum(g), k^ = k / |k|, q^ = q / |q| * scale,
+//   A_ij = beta_i k^_i.k^_j e^{cum_i - cum_j} (j < i),  T = (I + A)^-1,
+//   tb = bf16(T diag(beta)),  u = bf16(tb v),  w = bf16(tb bf16(k^ e^cum)),
+//   qd = bf16(q^ e^cum),  kd = bf16(k^ e^{last - cum}),  P_tj = bf16(q^_t.k^_j e^{cum_t - cum_j}),
+//   v_new = bf16(u - w S),  o = qd S + P v_new,  S = e^{last} S + kd^T v_new.
+// The bf16 rounding points are those of the reference kernel (gdn_prefill.cu:1-15 of the
+// reference). The pair products k.k and q.k are taken on the raw bf16 rows (exact
+// products, fp32 sums) and scaled by the inverse norms afterwards, instead of on
+// TF32-rounded normalised rows: the same quantities, with fewer rounding steps.
+//
+// One CTA (512 threads, one per SM: ~210 KB of shared memory, all 512 TMEM columns) per
+// (value head, sequence), longest sequences first, walking the chunks in order:
+//   warp 0       TMA producer: q and k rows of the key head (double-buffered), v rows of
+//                the value head (single buffer, refilled as soon as its MMA has read it)
+//   warp 1       scan MMA issuer:  (wS)^T, (qd S)^T = S^T [w^T | qd^T]   (A = S^T in TMEM)
+//                                  o^T += v_new^T P^T,  S^T += v_new^T kd  (A = v_new^T in TMEM)
+//   warp 2       prep MMA issuer:  D1 = [k; q] k^T                         (raw bf16, K = 128)
+//                                  u^T = v^T tb^T,  w^T = kw^T tb^T        (K = 64)
+//   warps 4-7    scan epilogue, thread = value column v = TMEM lane: per chunk the bf16
+//                copy of S^T (the next MMA's A operand, written to TMEM) and e^{last} S^T,
+//                v_new^T = bf16(bf16(u) - wS) (TMEM), o rows out through shared memory
+//   warps 8-15   preparation of the next chunk while the scan runs: norms, cumsum and
+//                decays, A and P from D1, the 64 x 64 inverse, tb and kw tiles, then the
+//                scan operands w (from TMEM), qd and kd
+// TMEM columns: [0,128) S^T fp32 | [128,192) S^T bf16 pairs | [192,256) wS fp32, then
+// v_new^T bf16 pairs | [256,320) o^T fp32 | [320,384) D1 fp32, then w^T fp32 |
+// [384,512) u^T fp32, two chunk buffers.
+// Every wait is bounded (tc.cuh); a wait that gives up records a fault bit and sets an
+// abort flag that stops every role at its next chunk, after which the CTA drains its
+// copies and MMAs and frees its tensor memory.
+#include <algorithm>
+
+#include "common.cuh"
+#include "gdn.cuh"
+#include "ops_internal.h"
+#include "tc.cuh"
+
+S1_FAULT_WORD(gdn_fused)
+
+namespace s1 {
+namespace gdnf {
+
+using namespace s1::tc;
+using gdn::C;
+using gdn::K;
+using gdn::V;
+
+constexpr int THREADS = 512;
+constexpr int PREP0 = 8;        // first preparation warp
+constexpr int NPREP = 256;      // preparation threads (warps 8-15)
+constexpr int BAR_SCAN = 1, BAR_PREP = 2;  // named barriers (0 is __syncthreads)
+constexpr int LDT = C + 4;      // fp32 row stride of A and T
+
+// shared memory (offsets from a 1024-byte aligned base)
+constexpr int BOX = 64 * 128;                 // one [64 rows][64 bf16] swizzled box, 8 KB
+constexpr int KQ_TILE = 4 * BOX;              // [k box0 | q box0 | k box1 | q box1]: two [128][64] A tiles
+constexpr int OFF_KQ = 0;                     // two slots
+constexpr int OFF_V = OFF_KQ + 2 * KQ_TILE;   // v [64 j][128 v] as two MN blocks
+constexpr int OFF_KW = OFF_V + 2 * BOX;       // k^ e^cum [64 j][128 k] as two MN blocks
+constexpr int OFF_TB = OFF_KW + 2 * BOX;      // tb [64 t][64 j] K-major
+constexpr int OFF_W = OFF_TB + BOX;           // w^T [128 k][64 t]: the MN-major B operand of (wS)^T
+constexpr int OFF_QD = OFF_W + 2 * BOX;       // qd [64 t][128 k] K-major (two sub-tiles)
+constexpr int OFF_KD = OFF_QD + 2 * BOX;      // kd [64 t][128 k] MN-major (two blocks)
+constexpr int OFF_P = OFF_KD + 2 * BOX;       // P [64 t][64 j] K-major, two chunk buffers
+constexpr int OFF_O = OFF_P + 2 * BOX;        // o rows [64 t][128 v] bf16 staging
+constexpr int OFF_A = OFF_O + 2 * BOX;        // A fp32 [64][LDT]
+constexpr int OFF_T = OFF_A + C * LDT * 4;    // T fp32 [64][LDT]
+constexpr int OFF_X = OFF_T + C * LDT * 4;    // inverse scratch [3][16][16] fp32
+constexpr int OFF_VEC = OFF_X + 3 * 256 * 4;  // per-chunk vectors
+constexpr int VEC_CUM = 0, VEC_BET = 64, VEC_ECUM = 128, VEC_EREM = 192, VEC_KINV = 256, VEC_QINV = 320,
+              VEC_G = 384, VEC_DECAY = 448;   // floats; decay: two chunk slots
+constexpr int OFF_BAR = OFF_VEC + 512 * 4;
+constexpr int NBAR = 32;
+constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
+
+// TMEM columns
+constexpr uint32_t TM_S = 0, TM_ST = 128, TM_WS = 192, TM_O = 256, TM_D1 = 320, TM_U = 384;
+
+// barrier indices (8 bytes each)
+enum Bar : int {
+    B_IN_FULL = 0,      // [2] q, k (slot) and v landed
+    B_IN_KQ_FREE = 2,   // [2] prep done with the q, k slot (count 8)
+    B_IN_V_FREE = 4,    // MMA2 read v
+    B_D1_FULL = 5,      // MMA1 done
+    B_D1W_FREE = 6,     // prep read w^T out of the D1 columns (count 8)
+    B_TB_READY = 7,     // tb and kw tiles written (count 8)
+    B_MMA2_DONE = 8,    // u^T and w^T in TMEM
+    B_U_FREE = 9,       // [2] scan read u^T of the slot (count 4)
+    B_OPS_READY = 11,   // w, qd, kd, P and the decay of the chunk written (count 8)
+    B_OPS_W_FREE = 12,  // the first scan MMAs read w and qd
+    B_OPS_KD_FREE = 13, // the second scan MMAs read kd and P
+    B_S_READY = 14,     // S^T bf16 copy and e^{last} S^T written (count 4)
+    B_WS_DONE = 15,     // (wS)^T and (qd S)^T in TMEM
+    B_VN_READY = 16,    // v_new^T written (count 4)
+    B_UPD_DONE = 17,    // o^T and S^T updated
+    B_DRAIN_SCAN = 18,
+    B_DRAIN_PREP = 19,
+};
+
+struct Maps {
+    CUtensorMap q, k, v;
+};
+
+// Byte offset of bf16 element (row, col) in a [rows][64] 128B-swizzled box.
+__device__ __forceinline__ uint32_t box_off(int row, int col) {
+    return sw128_offset(row, col >> 3) + (uint32_t)((col & 7) << 1);
+}
+
+__device__ __forceinline__ void fail(uint32_t bit, volatile int* abort_flag) {
+    atomicOr(&g_fault_word, bit);
+    *abort_flag = 1;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gdn_fused(const __grid_constant__ Maps maps, const float* __restrict__ g, const bf16* __restrict__ beta,
+              const __grid_constant__ SeqTable tab, bf16* __restrict__ o, int H, int HK, float scale,
+              const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* sm = smem_raw + (base - raw);
+    float* vec = reinterpret_cast<float*>(sm + OFF_VEC);
+    const uint32_t bars = base + OFF_BAR;
+    auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + NBAR * 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + OFF_BAR + NBAR * 8 + 16);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int h = blockIdx.x, seq = tab.order[blockIdx.y];
+    const int hk = h / (H / HK);
+    const int start = tab.offset[seq];
+    const int len = tab.offset[seq + 1] - start;
+    const int NC = (len + C - 1) / C;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 2; i++) {
+            mbar_init(bar(B_IN_FULL + i), 1);
+            mbar_init(bar(B_IN_KQ_FREE + i), 8);
+            mbar_init(bar(B_U_FREE + i), 4);
+        }
+        mbar_init(bar(B_IN_V_FREE), 1);
+        mbar_init(bar(B_D1_FULL), 1);
+        mbar_init(bar(B_D1W_FREE), 8);
+        mbar_init(bar(B_TB_READY), 8);
+        mbar_init(bar(B_MMA2_DONE), 1);
+        mbar_init(bar(B_OPS_READY), 8);
+        mbar_init(bar(B_OPS_W_FREE), 1);
+        mbar_init(bar(B_OPS_KD_FREE), 1);
+        mbar_init(bar(B_S_READY), 4);
+        mbar_init(bar(B_WS_DONE), 1);
+        mbar_init(bar(B_VN_READY), 4);
+        mbar_init(bar(B_UPD_DONE), 1);
+        mbar_init(bar(B_DRAIN_SCAN), 1);
+        mbar_init(bar(B_DRAIN_PREP), 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    grid_dep_wait();
+    grid_dep_launch();
+
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&maps.q);
+            tma_prefetch_desc(&maps.k);
+            tma_prefetch_desc(&maps.v);
+            int issued = 0;
+            for (int c = 0; c < NC; c++) {
+                if (*abort_flag) break;
+                const int slot = c & 1;
+                if (!mbar_wait(bar(B_IN_KQ_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u) ||
+                    !mbar_wait(bar(B_IN_V_FREE), (uint32_t)(c + 1) & 1u)) {
+                    fail(FAULT_WAIT_PRODUCER, abort_flag);
+                    break;
+                }
+                const uint32_t kq = base + OFF_KQ + slot * KQ_TILE, full = bar(B_IN_FULL + slot);
+                const int t0 = start + c * C;
+                mbar_expect_tx(full, 6 * BOX);
+#pragma unroll
+                for (int b = 0; b < 2; b++) {
+                    tma_load_3d(kq + b * 2 * BOX, &maps.k, full, 64 * b, hk, t0);
+                    tma_load_3d(kq + b * 2 * BOX + BOX, &maps.q, full, 64 * b, hk, t0);
+                    tma_load_3d(base + OFF_V + b * BOX, &maps.v, full, 64 * b, h, t0);
+                }
+                issued++;
+            }
+            // the copies in flight land before the CTA can leave
+            for (int c = issued > 2 ? issued - 2 : 0; c < issued; c++)
+                (void)mbar_wait(bar(B_IN_FULL + (c & 1)), (uint32_t)(c >> 1) & 1u);
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- scan MMAs
+        if (lane == 0) {
+            constexpr uint32_t ID_W = idesc_major(128, 64, AB_BF16, 0, 1);    // B = w^T, MN-major
+            constexpr uint32_t ID_K64 = idesc(128, 64, AB_BF16);              // B = qd or P, K-major
+            constexpr uint32_t ID_KD = idesc_major(128, 128, AB_BF16, 0, 1);  // B = kd, MN-major, N = 128
+            bool ok = true;
+            for (int c = 0; c < NC; c++) {
+                if (*abort_flag) break;
+                const uint32_t par = (uint32_t)c & 1u;
+                if (!mbar_wait(bar(B_OPS_READY), par) || !mbar_wait(bar(B_S_READY), par)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t a = tmem + TM_ST + (uint32_t)kk * 8;
+                    mma_bf16_ts(tmem + TM_WS, a, desc_sw128_mn(base + OFF_W + kk * 2048, BOX, 1024), ID_W, kk > 0);
+                    mma_bf16_ts(tmem + TM_O, a, desc_sw128(base + OFF_QD + (kk >> 2) * BOX + (kk & 3) * 32), ID_K64,
+                                kk > 0);
+                }
+                mma_commit(bar(B_WS_DONE));
+                mma_commit(bar(B_OPS_W_FREE));
+                if (!mbar_wait(bar(B_VN_READY), par)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t pt = base + OFF_P + (uint32_t)(c & 1) * BOX;
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint32_t a = tmem + TM_WS + (uint32_t)kk * 8;
+                    mma_bf16_ts(tmem + TM_O, a, desc_sw128(pt + kk * 32), ID_K64, 1);
+                    mma_bf16_ts(tmem + TM_S, a, desc_sw128_mn(base + OFF_KD + kk * 2048, BOX, 1024), ID_KD, 1);
+                }
+                mma_commit(bar(B_UPD_DONE));
+                mma_commit(bar(B_OPS_KD_FREE));
+            }
+            if (!ok) fail(FAULT_WAIT_MMA, abort_flag);
+            mma_commit(bar(B_DRAIN_SCAN));
+            (void)mbar_wait(bar(B_DRAIN_SCAN), 0);
+        }
+    } else if (warp == 2) {
+        // ---------------------------------------------------------------- preparation MMAs
+        if (lane == 0) {
+            constexpr uint32_t ID_D1 = idesc(128, 64, AB_BF16);
+            constexpr uint32_t ID_2 = idesc_major(128, 64, AB_BF16, 1, 0);  // A MN-major (v, kw), B = tb K-major
+            bool ok = true;
+            for (int c = 0; c < NC; c++) {
+                if (*abort_flag) break;
+                const int slot = c & 1;
+                const uint32_t kq = base + OFF_KQ + slot * KQ_TILE;
+                if (!mbar_wait(bar(B_IN_FULL + slot), (uint32_t)(c >> 1) & 1u) ||
+                    !mbar_wait(bar(B_D1W_FREE), (uint32_t)(c + 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // D1 = [k; q] k^T on the raw rows: A = [k box | q box] (128 rows), B = its k box
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    const uint32_t t = kq + (kk >> 2) * 2 * BOX + (kk & 3) * 32;
+                    mma_bf16(tmem + TM_D1, desc_sw128(t), desc_sw128(t), ID_D1, kk > 0);
+                }
+                mma_commit(bar(B_D1_FULL));
+                if (!mbar_wait(bar(B_TB_READY), (uint32_t)c & 1u) ||
+                    !mbar_wait(bar(B_U_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // u^T = v^T tb^T into this chunk's u buffer; w^T = kw^T tb^T over the D1 columns
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) {
+                    const uint64_t b = desc_sw128(base + OFF_TB + kk * 32);
+                    mma_bf16(tmem + TM_U + (uint32_t)slot * 64, desc_sw128_mn(base + OFF_V + kk * 2048, BOX, 1024), b,
+                             ID_2, kk > 0);
+                    mma_bf16(tmem + TM_D1, desc_sw128_mn(base + OFF_KW + kk * 2048, BOX, 1024), b, ID_2, kk > 0);
+                }
+                mma_commit(bar(B_MMA2_DONE));
+                mma_commit(bar(B_IN_V_FREE));
+            }
+            if (!ok) fail(FAULT_WAIT_MMA, abort_flag);
+            mma_commit(bar(B_DRAIN_PREP));
+            (void)mbar_wait(bar(B_DRAIN_PREP), 0);
+        }
+    } else if (warp >= 4 && warp < PREP0) {
+        // ---------------------------------------------------------------- scan epilogue
+        const int v = threadIdx.x - 128;
+        const uint32_t lrow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        {
+            const float* si = s_in ? s_in + (long)seq * s_in_stride + (size_t)h * K * V : nullptr;
+#pragma unroll 1
+            for (int q4 = 0; q4 < 4; q4++) {
+                float x[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) x[i] = si ? si[(size_t)(q4 * 32 + i) * V + v] : 0.f;
+                tmem_st32(lrow + TM_S + q4 * 32, x);
+            }
+            tmem_st_wait();
+        }
+        // Chunk c's pass over the state row: its bf16 copy (the first MMAs' A operand) and
+        // e^{last} S written back for the update MMA to accumulate onto.
+        auto state_pass = [&](int c) -> bool {
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_OPS_READY), (uint32_t)c & 1u))) return false;
+            const float dec = vec[VEC_DECAY + (c & 1)];
+#pragma unroll 1
+            for (int q4 = 0; q4 < 4; q4++) {
+                float x[32];
+                uint32_t pk[16];
+                tmem_ld32(lrow + TM_S + q4 * 32, x);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 16; i++) pk[i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
+                tmem_st16(lrow + TM_ST + q4 * 16, pk);
+#pragma unroll
+                for (int i = 0; i < 32; i++) x[i] *= dec;
+                tmem_st32(lrow + TM_S + q4 * 32, x);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_S_READY));
+            return true;
+        };
+        bf16* ost = reinterpret_cast<bf16*>(sm + OFF_O);
+        bool ok = state_pass(0);
+        for (int c = 0; c < NC; c++) {
+            if (bar_any(BAR_SCAN, 128, !ok || *abort_flag != 0)) {
+                if (!ok && v == 0) fail(FAULT_WAIT_EPILOGUE, abort_flag);
+                break;
+            }
+            const uint32_t par = (uint32_t)c & 1u;
+            // v_new^T = bf16(bf16(u) - (wS)^T), written as bf16 pairs over the (wS)^T columns
+            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_WS_DONE), par));
+            uint32_t pk[32];
+            if (ok) {
+                tc_fence_after();
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    float w16[16], u16[16];
+                    tmem_ld16(lrow + TM_WS + q * 16, w16);
+                    tmem_ld16(lrow + TM_U + (uint32_t)(c & 1) * 64 + q * 16, u16);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 8; i++)
+                        pk[q * 8 + i] = pack_bf16x2(rbf(u16[2 * i]) - w16[2 * i], rbf(u16[2 * i + 1]) - w16[2 * i + 1]);
+                }
+                tmem_st32(lrow + TM_WS, *reinterpret_cast<const float(*)[32]>(pk));
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(bar(B_VN_READY));
+                    mbar_arrive(bar(B_U_FREE + (c & 1)));
+                }
+                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_UPD_DONE), par));
+            }
+            // o^T of this chunk out of TMEM before the next chunk's first MMAs rewrite it, then
+            // the next chunk's state pass (it gates those MMAs), then the o rows go out
+            if (ok) {
+                tc_fence_after();
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    float ov[32];
+                    tmem_ld32(lrow + TM_O + half * 32, ov);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 16; i++) pk[half * 16 + i] = pack_bf16x2(ov[2 * i], ov[2 * i + 1]);
+                }
+                if (c + 1 < NC) ok = state_pass(c + 1);
+            }
+            if (bar_any(BAR_SCAN, 128, !ok)) {
+                if (v == 0) fail(FAULT_WAIT_EPILOGUE, abort_flag);
+                break;
+            }
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(&pk[i]);
+                ost[(2 * i) * V + v] = p2.x;
+                ost[(2 * i + 1) * V + v] = p2.y;
+            }
+            named_bar_sync(BAR_SCAN, 128);
+            const int rows = min(C, len - c * C);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int unit = v + i * 128;  // 16-byte unit: row unit / 16, columns (unit % 16) * 8
+                const int t = unit >> 4, v8 = (unit & 15) * 8;
+                if (t < rows)
+                    st8(o + ((size_t)(start + c * C + t) * H + h) * V + v8,
+                        *reinterpret_cast<const Pack8*>(ost + t * V + v8));
+            }
+            named_bar_sync(BAR_SCAN, 128);  // the staging tile takes the next chunk's rows
+        }
+        if (s_out && ok && !*abort_flag) {
+            float* so = s_out + (long)seq * (long)H * K * V + (size_t)h * K * V;
+#pragma unroll 1
+            for (int q4 = 0; q4 < 4; q4++) {
+                float x[32];
+                tmem_ld32(lrow + TM_S + q4 * 32, x);
+                tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < 32; i++) so[(size_t)(q4 * 32 + i) * V + v] = x[i];
+            }
+        }
+        tc_fence_before();
+    } else if (warp >= PREP0) {
+        // ---------------------------------------------------------------- preparation
+        const int pt = threadIdx.x - PREP0 * 32, pw = warp - PREP0, wq = warp & 3;
+        const uint32_t lrow = tmem + ((uint32_t)(wq * 32) << 16);
+        float* cum = vec + VEC_CUM;
+        float* bet = vec + VEC_BET;
+        float* ecum = vec + VEC_ECUM;
+        float* erem = vec + VEC_EREM;
+        float* kinv = vec + VEC_KINV;
+        float* qinv = vec + VEC_QINV;
+        float* gg = vec + VEC_G;
+        float* A = reinterpret_cast<float*>(sm + OFF_A);
+        float* Tm = reinterpret_cast<float*>(sm + OFF_T);
+        float* X = reinterpret_cast<float*>(sm + OFF_X);
+        float g_next = 0.f, b_next = 0.f;  // this thread's g and beta of the next chunk (rows pt < 64)
+        if (pt < C && pt < len) {
+            g_next = g[(size_t)(start + pt) * H + h];
+            b_next = f32(beta[(size_t)(start + pt) * H + h]);
+        }
+        bool ok = true;
+        for (int c = 0; c < NC; c++) {
+            if (bar_any(BAR_PREP, NPREP, !ok || *abort_flag != 0)) {
+                if (!ok && pt == 0) fail(FAULT_WAIT_OTHER, abort_flag);
+                break;
+            }
+            const int slot = c & 1;
+            const int n = min(C, len - c * C);
+            const uint8_t* kqp = sm + OFF_KQ + slot * KQ_TILE;
+            if (pt < C) {
+                gg[pt] = pt < n ? g_next : 0.f;
+                bet[pt] = pt < n ? b_next : 0.f;
+                const int row = (c + 1) * C + pt;
+                if (row < len) {  // the next chunk's, in flight behind this one
+                    g_next = g[(size_t)(start + row) * H + h];
+                    b_next = f32(beta[(size_t)(start + row) * H + h]);
+                }
+            }
+            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_IN_FULL + slot), (uint32_t)(c >> 1) & 1u));
+            named_bar_sync(BAR_PREP, NPREP);  // g and beta of the chunk are in
+            // norms: warp pw takes rows 8 pw .. 8 pw + 7 of k and q; lane l holds dims 4l .. 4l + 3
+            if (ok) {
+                const int b = lane >> 4, col = (lane & 15) * 4;
+#pragma unroll 2
+                for (int i = 0; i < 8; i++) {
+                    const int r = pw * 8 + i;
+                    const uint2 kr = *reinterpret_cast<const uint2*>(kqp + b * 2 * BOX + box_off(r, col));
+                    const uint2 qr = *reinterpret_cast<const uint2*>(kqp + b * 2 * BOX + BOX + box_off(r, col));
+                    const __nv_bfloat162* kp = reinterpret_cast<const __nv_bfloat162*>(&kr);
+                    const __nv_bfloat162* qp = reinterpret_cast<const __nv_bfloat162*>(&qr);
+                    const float2 k01 = __bfloat1622float2(kp[0]), k23 = __bfloat1622float2(kp[1]);
+                    const float2 q01 = __bfloat1622float2(qp[0]), q23 = __bfloat1622float2(qp[1]);
+                    float ks = 0.f, qs = 0.f;
+                    ks = fmaf(k01.x, k01.x, ks);
+                    ks = fmaf(k01.y, k01.y, ks);
+                    ks = fmaf(k23.x, k23.x, ks);
+                    ks = fmaf(k23.y, k23.y, ks);
+                    qs = fmaf(q01.x, q01.x, qs);
+                    qs = fmaf(q01.y, q01.y, qs);
+                    qs = fmaf(q23.x, q23.x, qs);
+                    qs = fmaf(q23.y, q23.y, qs);
+                    ks = warp_sum(ks);
+                    qs = warp_sum(qs);
+                    if (lane == 0) {
+                        kinv[r] = rsqrtf(ks + 1e-6f);
+                        qinv[r] = rsqrtf(qs + 1e-6f) * scale;
+                    }
+                }
+                if (pt == 0) {
+                    // sequential fp32 sum (the reference's order), from registers
+                    float gv[C];
+#pragma unroll
+                    for (int i = 0; i < C; i++) gv[i] = gg[i];
+                    float s = 0.f;
+#pragma unroll
+                    for (int i = 0; i < C; i++) {
+                        s += gv[i];
+                        cum[i] = s;
+                    }
+                    vec[VEC_DECAY + slot] = expf(s);
+                }
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            if (pt < C) {
+                ecum[pt] = expf(cum[pt]);
+                erem[pt] = expf(cum[C - 1] - cum[pt]);
+            }
+            // A (rows of k, TMEM lanes 0..63) and P (rows of q, lanes 64..127) from D1;
+            // warp pw reads lane quarter pw % 4, columns 32 (pw / 4) .. + 31
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_D1_FULL), (uint32_t)c & 1u));
+            if (ok) {
+                tc_fence_after();
+                const int j0 = (pw >> 2) * 32, row = wq * 32 + lane;
+                float d[32];
+                tmem_ld32(lrow + TM_D1 + (uint32_t)j0, d);
+                tmem_ld_wait();
+                if (row < C) {
+                    const int i = row;
+                    const float ci = cum[i], si = bet[i] * kinv[i];
+                    float* arow = A + i * LDT + j0;
+#pragma unroll
+                    for (int j4 = 0; j4 < 8; j4++) {
+                        float f[4];
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int j = j0 + j4 * 4 + e;
+                            f[e] = j < i ? si * (d[j4 * 4 + e] * kinv[j]) * __expf(ci - cum[j]) : 0.f;
+                        }
+                        *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(f[0], f[1], f[2], f[3]);
+                    }
+                } else {
+                    const int t = row - C;
+                    const float ct = cum[t], st_ = qinv[t];
+                    uint8_t* pt_tile = sm + OFF_P + slot * BOX;
+#pragma unroll
+                    for (int c8 = 0; c8 < 4; c8++) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            const int j = j0 + c8 * 8 + e;
+                            f[e] = j <= t ? (d[c8 * 8 + e] * st_) * kinv[j] * __expf(ct - cum[j]) : 0.f;
+                        }
+                        *reinterpret_cast<Pack8*>(pt_tile + sw128_offset(t, (j0 >> 3) + c8)) = pack8(f);
+                    }
+                }
+            }
+            named_bar_sync(BAR_PREP, NPREP);  // A complete
+            // T = (I + A)^-1. Diagonal 16x16 blocks: one thread per (block, column).
+            if (ok && pt < C) {
+                const int b = pt >> 4, col = pt & 15, o16 = b * 16;
+                float x[16];
+#pragma unroll
+                for (int r = 0; r < 16; r++) {
+                    float acc = r == col ? 1.f : 0.f;
+#pragma unroll
+                    for (int m = 0; m < r; m++) acc = fmaf(-A[(o16 + r) * LDT + o16 + m], x[m], acc);
+                    x[r] = r < col ? 0.f : acc;
+                }
+#pragma unroll
+                for (int r = 0; r < 16; r++) Tm[(o16 + r) * LDT + o16 + col] = x[r];
+            }
+            for (int x = pt; x < C * C; x += NPREP) {
+                const int i = x / C, j = x % C;
+                if ((j >> 4) > (i >> 4)) Tm[i * LDT + j] = 0.f;
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            // block rows bi = 1..3: X_bj = sum_{kb = bj}^{bi-1} A_(bi,kb) T_(kb,bj), then
+            // T_(bi,bj) = -T_(bi,bi) X_bj; thread = (bj, row r, 4 columns)
+#pragma unroll 1
+            for (int bi = 1; bi < 4; bi++) {
+                const int bj = pt >> 6, r = (pt >> 2) & 15, c4 = (pt & 3) * 4;
+                if (pt < bi * 64) {
+                    const float* arow = A + (16 * bi + r) * LDT;
+                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+                    for (int kb = bj; kb < bi; kb++) {
+#pragma unroll
+                        for (int m = 0; m < 16; m++) {
+                            const float av = arow[16 * kb + m];
+                            const float4 tv = *reinterpret_cast<const float4*>(Tm + (16 * kb + m) * LDT + 16 * bj + c4);
+                            a0 = fmaf(av, tv.x, a0);
+                            a1 = fmaf(av, tv.y, a1);
+                            a2 = fmaf(av, tv.z, a2);
+                            a3 = fmaf(av, tv.w, a3);
+                        }
+                    }
+                    *reinterpret_cast<float4*>(X + (bj * 16 + r) * 16 + c4) = make_float4(a0, a1, a2, a3);
+                }
+                named_bar_sync(BAR_PREP, NPREP);
+                if (pt < bi * 64) {
+                    const float* trow = Tm + (16 * bi + r) * LDT + 16 * bi;
+                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+                    for (int m = 0; m < 16; m++) {
+                        if (m <= r) {
+                            const float tv = trow[m];
+                            const float4 sv = *reinterpret_cast<const float4*>(X + (bj * 16 + m) * 16 + c4);
+                            a0 = fmaf(tv, sv.x, a0);
+                            a1 = fmaf(tv, sv.y, a1);
+                            a2 = fmaf(tv, sv.z, a2);
+                            a3 = fmaf(tv, sv.w, a3);
+                        }
+                    }
+                    *reinterpret_cast<float4*>(Tm + (16 * bi + r) * LDT + 16 * bj + c4) =
+                        make_float4(-a0, -a1, -a2, -a3);
+                }
+                named_bar_sync(BAR_PREP, NPREP);
+            }
+            // tb = bf16(T diag(beta)) K-major [64 t][64 j]; kw = bf16(k^ e^cum) MN-major [j][k]
+            if (ok) {
+                for (int u = pt; u < C * C / 8; u += NPREP) {
+                    const int t = u >> 3, j0 = (u & 7) * 8;
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) f[e] = Tm[t * LDT + j0 + e] * bet[j0 + e];
+                    *reinterpret_cast<Pack8*>(sm + OFF_TB + sw128_offset(t, j0 >> 3)) = pack8(f);
+                }
+                for (int u = pt; u < C * 16; u += NPREP) {
+                    const int j = u >> 4, b = (u >> 3) & 1, ch = u & 7;
+                    float f[8];
+                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(j, ch)), f);
+                    const float kv = kinv[j], ec = ecum[j];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) f[e] = (f[e] * kv) * ec;
+                    *reinterpret_cast<Pack8*>(sm + OFF_KW + b * BOX + sw128_offset(j, ch)) = pack8(f);
+                }
+                fence_async_smem();
+            }
+            tc_fence_before();  // the D1 loads are complete before MMA2 rewrites those columns
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(bar(B_TB_READY));
+            // w^T from TMEM (lane = k) into the MN-major [128 k][64 t] operand tile, once the
+            // previous chunk's first scan MMAs have read the tile
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_MMA2_DONE), (uint32_t)c & 1u) &&
+                                                   mbar_wait(bar(B_OPS_W_FREE), (uint32_t)(c + 1) & 1u));
+            if (ok) {
+                tc_fence_after();
+                const int t0w = (pw >> 2) * 32, kr = wq * 32 + lane;
+                float x[32];
+                tmem_ld32(lrow + TM_D1 + (uint32_t)t0w, x);
+                tmem_ld_wait();
+#pragma unroll
+                for (int c4 = 0; c4 < 4; c4++)
+                    *reinterpret_cast<Pack8*>(sm + OFF_W + sw128_offset(kr, (t0w >> 3) + c4)) = pack8(x + 8 * c4);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar(B_D1W_FREE));
+            }
+            // qd and kd, once the previous chunk's update MMAs have read kd
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_OPS_KD_FREE), (uint32_t)(c + 1) & 1u));
+            if (ok) {
+                for (int u = pt; u < C * 16; u += NPREP) {
+                    const int t = u >> 4, b = (u >> 3) & 1, ch = u & 7;
+                    float kx[8], qx[8];
+                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(t, ch)), kx);
+                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + BOX + sw128_offset(t, ch)), qx);
+                    const float kv = kinv[t], qv = qinv[t], ec = ecum[t], er = erem[t];
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        qx[e] = (qx[e] * qv) * ec;
+                        kx[e] = (kx[e] * kv) * er;
+                    }
+                    *reinterpret_cast<Pack8*>(sm + OFF_QD + b * BOX + sw128_offset(t, ch)) = pack8(qx);
+                    *reinterpret_cast<Pack8*>(sm + OFF_KD + b * BOX + sw128_offset(t, ch)) = pack8(kx);
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(bar(B_OPS_READY));
+                    mbar_arrive(bar(B_IN_KQ_FREE + slot));
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace gdnf
+
+namespace gdn {
+
+// The fused prefill over packed sequences (no workspace). Defined for the layouts of
+// cs1_gdn_prefill: q, k [rows][HK][128], v, o [rows][H][128] bf16, g [rows][H] fp32,
+// beta [rows][H] bf16; s_in / s_out [count][H][128][128] fp32 (s_in_stride 0: one state
+// for every sequence).
+int run_fused(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+              const SeqTable& seqs, int H, int HK, float scale, const void* s_in, long s_in_stride, void* s_out,
+              cudaStream_t st) {
+    using namespace gdnf;
+    if (!q || !k || !v || !g || !beta || !o || H <= 0 || HK <= 0 || H % HK || H > 65535 || seqs.count > 65535)
+        return cudaErrorInvalidValue;
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return cudaErrorInvalidValue;
+    static const cudaError_t configured =
+        cudaFuncSetAttribute(gdn_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (configured != cudaSuccess) return configured;
+    const uint64_t rows = (uint64_t)seqs.offset[seqs.count];
+    Maps maps;
+    int e = host::make_map_3d_bf16(&maps.q, q, K, HK, rows, K, (uint64_t)HK * K, 64, 64);
+    if (!e) e = host::make_map_3d_bf16(&maps.k, k, K, HK, rows, K, (uint64_t)HK * K, 64, 64);
+    if (!e) e = host::make_map_3d_bf16(&maps.v, v, V, H, rows, V, (uint64_t)H * V, 64, 64);
+    if (e) return e;
+    return launch_pdl(gdn_fused, dim3(H, seqs.count), dim3(THREADS), SMEM, st, maps, g,
+                      static_cast<const bf16*>(beta), seqs, static_cast<bf16*>(o), H, HK, scale,
+                      static_cast<const float*>(s_in), s_in_stride, static_cast<float*>(s_out));
+}
+
+}  // namespace gdn
+}  // namespace s1

@@ -68,6 +68,6 @@ extern "C" __attribute__((visibility("default"))) int cs1_gdn_prefill_noalloc(co
     s1::make_table(tab, &len, 1);
     // Every workspace byte the scan reads is written by the prep kernel of the same call,
     // so nothing needs clearing between calls.
-    return s1::gdn::run(q, k, v, g, beta, o, ws, kScratchBytes, tab, H, HK, scale, nullptr, 0, nullptr,
+    return s1::gdn::run_two_pass(q, k, v, g, beta, o, ws, kScratchBytes, tab, H, HK, scale, nullptr, 0, nullptr,
                         static_cast<cudaStream_t>(stream));
 }

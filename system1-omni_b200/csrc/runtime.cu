@@ -118,6 +118,7 @@ __global__ void wait_selftest_kernel(long long limit) {
 
 extern "C" uint32_t s1_fault_read_gemm(int clear);
 extern "C" uint32_t s1_fault_read_gdn(int clear);
+extern "C" uint32_t s1_fault_read_gdn_fused(int clear);
 extern "C" uint32_t s1_fault_read_attention(int clear);
 
 extern "C" {
@@ -195,8 +196,8 @@ int cs1_wait_selftest(long long cycles, void* stream) {
 }
 
 uint32_t cs1_fault_status(int clear) {
-    return s1_fault_read_gemm(clear) | s1_fault_read_gdn(clear) | s1_fault_read_attention(clear) |
-           s1_fault_read_selftest(clear);
+    return s1_fault_read_gemm(clear) | s1_fault_read_gdn(clear) | s1_fault_read_gdn_fused(clear) |
+           s1_fault_read_attention(clear) | s1_fault_read_selftest(clear);
 }
 
 // ---- vision entry points: required symbols of the loader; the vision path is
