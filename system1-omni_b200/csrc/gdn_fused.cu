@@ -13,7 +13,7 @@
 // products, fp32 sums) and scaled by the inverse norms afterwards, instead of on
 // TF32-rounded normalised rows: the same quantities, with fewer rounding steps.
 //
-// One CTA (512 threads, one per SM: ~210 KB of shared memory, all 512 TMEM columns) per
+// One CTA (512 threads, one per SM: ~205 KB of shared memory, all 512 TMEM columns) per
 // (value head, sequence), longest sequences first, walking the chunks in order:
 //   warp 0       TMA producer: q and k rows of the key head (double-buffered), v rows of
 //                the value head (single buffer, refilled as soon as its MMA has read it)
@@ -21,18 +21,25 @@
 //                                  o^T += v_new^T P^T,  S^T += v_new^T kd  (A = v_new^T in TMEM)
 //   warp 2       prep MMA issuer:  D1 = [k; q] k^T                         (raw bf16, K = 128)
 //                                  u^T = v^T tb^T,  w^T = kw^T tb^T        (K = 64)
+//   warp 3       vector warp, ahead of the preparation: g and beta of the chunk, the
+//                sequential cumsum of g, e^cum, e^{last - cum} and the decay e^{last}
 //   warps 4-7    scan epilogue, thread = value column v = TMEM lane: per chunk the bf16
 //                copy of S^T (the next MMA's A operand, written to TMEM) and e^{last} S^T,
-//                v_new^T = bf16(bf16(u) - wS) (TMEM), o rows out through shared memory
-//   warps 8-15   preparation of the next chunk while the scan runs: norms, cumsum and
-//                decays, A and P from D1, the 64 x 64 inverse, tb and kw tiles, then the
-//                scan operands w (from TMEM), qd and kd
+//                v_new^T = bf16(bf16(u) - wS) (TMEM), the next chunk's qd and kd operand
+//                tiles, o rows straight to global memory
+//   warps 8-15   preparation of the next chunk while the scan runs: norms, kw, A and P from
+//                D1, the 64 x 64 inverse (two 32 x 32 diagonal blocks by right-looking
+//                substitution, then the block below them) written out as tb, then w (from
+//                TMEM)
 // TMEM columns: [0,128) S^T fp32 | [128,192) S^T bf16 pairs | [192,256) wS fp32, then
 // v_new^T bf16 pairs | [256,320) o^T fp32 | [320,384) D1 fp32, then w^T fp32 |
 // [384,512) u^T fp32, two chunk buffers.
 // Every wait is bounded (tc.cuh); a wait that gives up records a fault bit and sets an
 // abort flag that stops every role at its next chunk, after which the CTA drains its
-// copies and MMAs and frees its tensor memory.
+// copies and MMAs and frees its tensor memory. Each mbarrier has one producing role whose
+// arrivals are ordered behind the waits of its consumers, so no waiter can fall two phases
+// behind (which a parity wait would misread); the one hand-off without that order, the
+// norms of the next chunk read by the scan warps, is a monotonic counter.
 #include <algorithm>
 
 #include "common.cuh"
@@ -67,14 +74,17 @@ constexpr int OFF_W = OFF_TB + BOX;           // w^T [128 k][64 t]: the MN-major
 constexpr int OFF_QD = OFF_W + 2 * BOX;       // qd [64 t][128 k] K-major (two sub-tiles)
 constexpr int OFF_KD = OFF_QD + 2 * BOX;      // kd [64 t][128 k] MN-major (two blocks)
 constexpr int OFF_P = OFF_KD + 2 * BOX;       // P [64 t][64 j] K-major, two chunk buffers
-constexpr int OFF_O = OFF_P + 2 * BOX;        // o rows [64 t][128 v] bf16 staging
-constexpr int OFF_A = OFF_O + 2 * BOX;        // A fp32 [64][LDT]
-constexpr int OFF_T = OFF_A + C * LDT * 4;    // T fp32 [64][LDT]
-constexpr int OFF_X = OFF_T + C * LDT * 4;    // inverse scratch [3][16][16] fp32
-constexpr int OFF_VEC = OFF_X + 3 * 256 * 4;  // per-chunk vectors
-constexpr int VEC_CUM = 0, VEC_BET = 64, VEC_ECUM = 128, VEC_EREM = 192, VEC_KINV = 256, VEC_QINV = 320,
-              VEC_G = 384, VEC_DECAY = 448;   // floats; decay: two chunk slots
-constexpr int OFF_BAR = OFF_VEC + 512 * 4;
+constexpr int OFF_A = OFF_P + 2 * BOX;        // A fp32 [64][LDT]
+constexpr int OFF_T = OFF_A + C * LDT * 4;    // T fp32 [64][LDT] (its two diagonal 32 x 32 blocks)
+constexpr int OFF_X = OFF_T + C * LDT * 4;    // inverse scratch [32][32] fp32
+constexpr int OFF_VEC = OFF_X + 32 * 32 * 4;  // per-chunk vectors (floats)
+// two chunk slots of VEC_SLOT floats: cum * log2(e), beta, e^cum, e^{last - cum}, g
+// (scratch), written by the vector warp, and the inverse norms of k and q (q's times the
+// scale), written by the preparation; the decay e^{last} in a ring of four chunks
+constexpr int VEC_CUM2 = 0, VEC_BET = 64, VEC_ECUM = 128, VEC_EREM = 192, VEC_G = 256, VEC_KINV = 320,
+              VEC_QINV = 384, VEC_SLOT = 448;
+constexpr int VEC_DECAY = 2 * VEC_SLOT;
+constexpr int OFF_BAR = OFF_VEC + (VEC_DECAY + 8) * 4;
 constexpr int NBAR = 32;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
 
@@ -84,14 +94,14 @@ constexpr uint32_t TM_S = 0, TM_ST = 128, TM_WS = 192, TM_O = 256, TM_D1 = 320, 
 // barrier indices (8 bytes each)
 enum Bar : int {
     B_IN_FULL = 0,      // [2] q, k (slot) and v landed
-    B_IN_KQ_FREE = 2,   // [2] prep done with the q, k slot (count 8)
+    B_IN_KQ_FREE = 2,   // [2] preparation and scan warps done with the q, k slot (count 12)
     B_IN_V_FREE = 4,    // MMA2 read v
     B_D1_FULL = 5,      // MMA1 done
     B_D1W_FREE = 6,     // prep read w^T out of the D1 columns (count 8)
     B_TB_READY = 7,     // tb and kw tiles written (count 8)
     B_MMA2_DONE = 8,    // u^T and w^T in TMEM
     B_U_FREE = 9,       // [2] scan read u^T of the slot (count 4)
-    B_OPS_READY = 11,   // w, qd, kd, P and the decay of the chunk written (count 8)
+    B_OPS_READY = 11,   // w of the chunk written by the preparation (count 8)
     B_OPS_W_FREE = 12,  // the first scan MMAs read w and qd
     B_OPS_KD_FREE = 13, // the second scan MMAs read kd and P
     B_S_READY = 14,     // S^T bf16 copy and e^{last} S^T written (count 4)
@@ -100,15 +110,22 @@ enum Bar : int {
     B_UPD_DONE = 17,    // o^T and S^T updated
     B_DRAIN_SCAN = 18,
     B_DRAIN_PREP = 19,
+    B_VEC_READY = 20,   // [2] the vector warp wrote the slot's vectors (count 1)
+    B_VEC_FREE = 22,    // [2] preparation and scan warps are done with the slot (count 12)
+    B_DEC_READY = 24,   // [4] the chunk's decay is in the ring (count 1)
+    B_OPS2_READY = 28,  // P of the chunk written by the preparation (count 8)
+    B_QD_READY = 29,    // qd of the chunk written by the scan warps (count 4)
+    B_KD_READY = 30,    // kd of the chunk written by the scan warps (count 4)
 };
 
 struct Maps {
     CUtensorMap q, k, v;
 };
 
-// Byte offset of bf16 element (row, col) in a [rows][64] 128B-swizzled box.
-__device__ __forceinline__ uint32_t box_off(int row, int col) {
-    return sw128_offset(row, col >> 3) + (uint32_t)((col & 7) << 1);
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 __device__ __forceinline__ void fail(uint32_t bit, volatile int* abort_flag) {
@@ -129,6 +146,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     auto bar = [&](int i) { return bars + 8u * (uint32_t)i; };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + OFF_BAR + NBAR * 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + OFF_BAR + NBAR * 8 + 16);
+    // chunks whose norms are in (monotonic; the scan warps read them to form qd and kd)
+    volatile int* norms_done = reinterpret_cast<volatile int*>(sm + OFF_BAR + NBAR * 8 + 20);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const int h = blockIdx.x, seq = tab.order[blockIdx.y];
@@ -140,9 +159,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < 2; i++) {
             mbar_init(bar(B_IN_FULL + i), 1);
-            mbar_init(bar(B_IN_KQ_FREE + i), 8);
+            mbar_init(bar(B_IN_KQ_FREE + i), 12);
             mbar_init(bar(B_U_FREE + i), 4);
+            mbar_init(bar(B_VEC_READY + i), 1);
+            mbar_init(bar(B_VEC_FREE + i), 12);
         }
+        for (int i = 0; i < 4; i++) mbar_init(bar(B_DEC_READY + i), 1);
         mbar_init(bar(B_IN_V_FREE), 1);
         mbar_init(bar(B_D1_FULL), 1);
         mbar_init(bar(B_D1W_FREE), 8);
@@ -157,7 +179,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(bar(B_UPD_DONE), 1);
         mbar_init(bar(B_DRAIN_SCAN), 1);
         mbar_init(bar(B_DRAIN_PREP), 1);
+        mbar_init(bar(B_OPS2_READY), 8);
+        mbar_init(bar(B_QD_READY), 4);
+        mbar_init(bar(B_KD_READY), 4);
         *abort_flag = 0;
+        *norms_done = 0;
         mbar_fence_init();
     }
     if (warp == 1) {
@@ -211,7 +237,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int c = 0; c < NC; c++) {
                 if (*abort_flag) break;
                 const uint32_t par = (uint32_t)c & 1u;
-                if (!mbar_wait(bar(B_OPS_READY), par) || !mbar_wait(bar(B_S_READY), par)) {
+                if (!mbar_wait(bar(B_OPS_READY), par) || !mbar_wait(bar(B_QD_READY), par) ||
+                    !mbar_wait(bar(B_S_READY), par)) {
                     ok = false;
                     break;
                 }
@@ -225,7 +252,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 mma_commit(bar(B_WS_DONE));
                 mma_commit(bar(B_OPS_W_FREE));
-                if (!mbar_wait(bar(B_VN_READY), par)) {
+                if (!mbar_wait(bar(B_VN_READY), par) || !mbar_wait(bar(B_OPS2_READY), par) ||
+                    !mbar_wait(bar(B_KD_READY), par)) {
                     ok = false;
                     break;
                 }
@@ -288,6 +316,65 @@ __global__ void __launch_bounds__(THREADS, 1)
             mma_commit(bar(B_DRAIN_PREP));
             (void)mbar_wait(bar(B_DRAIN_PREP), 0);
         }
+    } else if (warp == 3) {
+        // ---------------------------------------------------------------- vector warp
+        // Per chunk, ahead of the preparation: g and beta of the chunk (rows past the
+        // sequence's end: 0), the sequential fp32 cumsum of g (the reference's order),
+        // cum * log2(e), e^cum, e^{last - cum} and the decay e^{last}.
+        float gn[2] = {0.f, 0.f}, bn[2] = {0.f, 0.f};  // this lane's rows lane, lane + 32 of the next chunk
+        auto fetch = [&](int c) {
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int row = c * C + lane + 32 * i;
+                gn[i] = row < len ? g[(size_t)(start + row) * H + h] : 0.f;
+                bn[i] = row < len ? f32(beta[(size_t)(start + row) * H + h]) : 0.f;
+            }
+        };
+        fetch(0);
+        for (int c = 0; c < NC; c++) {
+            if (*abort_flag) break;
+            const int slot = c & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_VEC_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u))) {
+                if (lane == 0) fail(FAULT_WAIT_OTHER, abort_flag);
+                break;
+            }
+            float* vs = vec + slot * VEC_SLOT;
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                vs[VEC_G + lane + 32 * i] = gn[i];
+                vs[VEC_BET + lane + 32 * i] = bn[i];
+            }
+            if (c + 1 < NC) fetch(c + 1);  // in flight behind this chunk's arithmetic
+            __syncwarp();
+            if (lane == 0) {
+                float gv[C];
+#pragma unroll
+                for (int i = 0; i < C; i++) gv[i] = vs[VEC_G + i];
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < C; i++) {
+                    acc += gv[i];
+                    gv[i] = acc;
+                }
+#pragma unroll
+                for (int i = 0; i < C; i++) vs[VEC_G + i] = gv[i];  // cum
+                vec[VEC_DECAY + (c & 3)] = expf(acc);
+            }
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int t = lane + 32 * i;
+                const float ct = vs[VEC_G + t];
+                vs[VEC_CUM2 + t] = ct * 1.4426950408889634f;
+                vs[VEC_ECUM + t] = expf(ct);
+                vs[VEC_EREM + t] = expf(vs[VEC_G + C - 1] - ct);
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(bar(B_VEC_READY + slot));
+                mbar_arrive(bar(B_DEC_READY + (c & 3)));
+            }
+        }
     } else if (warp >= 4 && warp < PREP0) {
         // ---------------------------------------------------------------- scan epilogue
         const int v = threadIdx.x - 128;
@@ -306,8 +393,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Chunk c's pass over the state row: its bf16 copy (the first MMAs' A operand) and
         // e^{last} S written back for the update MMA to accumulate onto.
         auto state_pass = [&](int c) -> bool {
-            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_OPS_READY), (uint32_t)c & 1u))) return false;
-            const float dec = vec[VEC_DECAY + (c & 1)];
+            if (!__all_sync(0xffffffffu, mbar_wait(bar(B_DEC_READY + (c & 3)), (uint32_t)(c >> 2) & 1u))) return false;
+            const float dec = vec[VEC_DECAY + (c & 3)];
 #pragma unroll 1
             for (int q4 = 0; q4 < 4; q4++) {
                 float x[32];
@@ -327,19 +414,89 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (lane == 0) mbar_arrive(bar(B_S_READY));
             return true;
         };
-        bf16* ost = reinterpret_cast<bf16*>(sm + OFF_O);
-        bool ok = state_pass(0);
+        // The o rows of chunk c: this thread's column v of each row, 2-byte stores (a warp
+        // writes 64 contiguous bytes of a row per store).
+        auto write_o = [&](int c, const uint32_t (&opk)[32]) {
+            const int rows = min(C, len - c * C);
+            bf16* dst = o + ((size_t)(start + c * C) * H + h) * V + v;
+            const size_t pitch = (size_t)H * V;
+#pragma unroll
+            for (int i = 0; i < 32; i++) {
+                const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(&opk[i]);
+                if (2 * i < rows) dst[(size_t)(2 * i) * pitch] = p2.x;
+                if (2 * i + 1 < rows) dst[(size_t)(2 * i + 1) * pitch] = p2.y;
+            }
+        };
+        // qd = bf16(q^ e^cum) and kd = bf16(k^ e^{last - cum}) of chunk c from its q, k rows, once
+        // the preparation has their norms (a monotonic count, so no barrier phase can alias)
+        auto norms_in = [&](int c) -> bool {
+            if (*norms_done <= c) {
+                const long long t0 = clock64();
+                while (*norms_done <= c)
+                    if (clock64() - t0 > S1_WAIT_CYCLES) return false;
+            }
+            __threadfence_block();
+            return true;
+        };
+        auto form_qd = [&](int c) {
+            const int slot = c & 1;
+            const uint8_t* kqp = sm + OFF_KQ + slot * KQ_TILE;
+            const float* vs = vec + slot * VEC_SLOT;
+#pragma unroll 2
+            for (int u = v; u < C * 16; u += 128) {
+                const int t = u >> 4, b = (u >> 3) & 1, ch = u & 7;
+                float qx[8];
+                unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + BOX + sw128_offset(t, ch)), qx);
+                const float sc = vs[VEC_QINV + t], ec = vs[VEC_ECUM + t];
+#pragma unroll
+                for (int e = 0; e < 8; e++) qx[e] = (qx[e] * sc) * ec;
+                *reinterpret_cast<Pack8*>(sm + OFF_QD + b * BOX + sw128_offset(t, ch)) = pack8(qx);
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(B_QD_READY));
+        };
+        auto form_kd = [&](int c) {
+            const int slot = c & 1;
+            const uint8_t* kqp = sm + OFF_KQ + slot * KQ_TILE;
+            const float* vs = vec + slot * VEC_SLOT;
+#pragma unroll 2
+            for (int u = v; u < C * 16; u += 128) {
+                const int t = u >> 4, b = (u >> 3) & 1, ch = u & 7;
+                float kx[8];
+                unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(t, ch)), kx);
+                const float sc = vs[VEC_KINV + t], er = vs[VEC_EREM + t];
+#pragma unroll
+                for (int e = 0; e < 8; e++) kx[e] = (kx[e] * sc) * er;
+                *reinterpret_cast<Pack8*>(sm + OFF_KD + b * BOX + sw128_offset(t, ch)) = pack8(kx);
+            }
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(bar(B_KD_READY));
+                mbar_arrive(bar(B_IN_KQ_FREE + slot));
+                mbar_arrive(bar(B_VEC_FREE + slot));
+            }
+        };
+        uint32_t opk[32];  // o^T row of the previous chunk, written out behind this chunk's update MMAs
+        bool ok = __all_sync(0xffffffffu, norms_in(0));
+        if (ok) {
+            form_qd(0);
+            form_kd(0);
+            ok = state_pass(0);
+        }
         for (int c = 0; c < NC; c++) {
             if (bar_any(BAR_SCAN, 128, !ok || *abort_flag != 0)) {
                 if (!ok && v == 0) fail(FAULT_WAIT_EPILOGUE, abort_flag);
+                ok = false;
                 break;
             }
             const uint32_t par = (uint32_t)c & 1u;
             // v_new^T = bf16(bf16(u) - (wS)^T), written as bf16 pairs over the (wS)^T columns
             ok = __all_sync(0xffffffffu, mbar_wait(bar(B_WS_DONE), par));
-            uint32_t pk[32];
             if (ok) {
                 tc_fence_after();
+                uint32_t pk[32];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     float w16[16], u16[16];
@@ -358,10 +515,17 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mbar_arrive(bar(B_VN_READY));
                     mbar_arrive(bar(B_U_FREE + (c & 1)));
                 }
-                ok = __all_sync(0xffffffffu, mbar_wait(bar(B_UPD_DONE), par));
             }
+            // the next chunk's qd (the first scan MMAs of this chunk have read the tile), then
+            // the previous chunk's o rows, both behind this chunk's update MMAs
+            if (ok && c + 1 < NC) {
+                ok = __all_sync(0xffffffffu, norms_in(c + 1));
+                if (ok) form_qd(c + 1);
+            }
+            if (c > 0) write_o(c - 1, opk);
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_UPD_DONE), par));
             // o^T of this chunk out of TMEM before the next chunk's first MMAs rewrite it, then
-            // the next chunk's state pass (it gates those MMAs), then the o rows go out
+            // the next chunk's state pass (it gates those MMAs) and its kd
             if (ok) {
                 tc_fence_after();
 #pragma unroll
@@ -370,31 +534,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                     tmem_ld32(lrow + TM_O + half * 32, ov);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 16; i++) pk[half * 16 + i] = pack_bf16x2(ov[2 * i], ov[2 * i + 1]);
+                    for (int i = 0; i < 16; i++) opk[half * 16 + i] = pack_bf16x2(ov[2 * i], ov[2 * i + 1]);
                 }
-                if (c + 1 < NC) ok = state_pass(c + 1);
+                if (c + 1 < NC) {
+                    ok = state_pass(c + 1);
+                    if (ok) form_kd(c + 1);
+                }
             }
-            if (bar_any(BAR_SCAN, 128, !ok)) {
-                if (v == 0) fail(FAULT_WAIT_EPILOGUE, abort_flag);
-                break;
-            }
-#pragma unroll
-            for (int i = 0; i < 32; i++) {
-                const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(&pk[i]);
-                ost[(2 * i) * V + v] = p2.x;
-                ost[(2 * i + 1) * V + v] = p2.y;
-            }
-            named_bar_sync(BAR_SCAN, 128);
-            const int rows = min(C, len - c * C);
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int unit = v + i * 128;  // 16-byte unit: row unit / 16, columns (unit % 16) * 8
-                const int t = unit >> 4, v8 = (unit & 15) * 8;
-                if (t < rows)
-                    st8(o + ((size_t)(start + c * C + t) * H + h) * V + v8,
-                        *reinterpret_cast<const Pack8*>(ost + t * V + v8));
-            }
-            named_bar_sync(BAR_SCAN, 128);  // the staging tile takes the next chunk's rows
+        }
+        if (bar_any(BAR_SCAN, 128, !ok)) {
+            if (v == 0 && !*abort_flag) fail(FAULT_WAIT_EPILOGUE, abort_flag);
+            ok = false;
+        } else {
+            write_o(NC - 1, opk);
         }
         if (s_out && ok && !*abort_flag) {
             float* so = s_out + (long)seq * (long)H * K * V + (size_t)h * K * V;
@@ -412,21 +564,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         // ---------------------------------------------------------------- preparation
         const int pt = threadIdx.x - PREP0 * 32, pw = warp - PREP0, wq = warp & 3;
         const uint32_t lrow = tmem + ((uint32_t)(wq * 32) << 16);
-        float* cum = vec + VEC_CUM;
-        float* bet = vec + VEC_BET;
-        float* ecum = vec + VEC_ECUM;
-        float* erem = vec + VEC_EREM;
-        float* kinv = vec + VEC_KINV;
-        float* qinv = vec + VEC_QINV;
-        float* gg = vec + VEC_G;
         float* A = reinterpret_cast<float*>(sm + OFF_A);
         float* Tm = reinterpret_cast<float*>(sm + OFF_T);
         float* X = reinterpret_cast<float*>(sm + OFF_X);
-        float g_next = 0.f, b_next = 0.f;  // this thread's g and beta of the next chunk (rows pt < 64)
-        if (pt < C && pt < len) {
-            g_next = g[(size_t)(start + pt) * H + h];
-            b_next = f32(beta[(size_t)(start + pt) * H + h]);
-        }
         bool ok = true;
         for (int c = 0; c < NC; c++) {
             if (bar_any(BAR_PREP, NPREP, !ok || *abort_flag != 0)) {
@@ -434,175 +574,47 @@ __global__ void __launch_bounds__(THREADS, 1)
                 break;
             }
             const int slot = c & 1;
-            const int n = min(C, len - c * C);
             const uint8_t* kqp = sm + OFF_KQ + slot * KQ_TILE;
-            if (pt < C) {
-                gg[pt] = pt < n ? g_next : 0.f;
-                bet[pt] = pt < n ? b_next : 0.f;
-                const int row = (c + 1) * C + pt;
-                if (row < len) {  // the next chunk's, in flight behind this one
-                    g_next = g[(size_t)(start + row) * H + h];
-                    b_next = f32(beta[(size_t)(start + row) * H + h]);
-                }
-            }
+            float* vs = vec + slot * VEC_SLOT;
+            const float* cum2 = vs + VEC_CUM2;
+            const float* bet = vs + VEC_BET;
+            const float* ecum = vs + VEC_ECUM;
+            float* kinv = vs + VEC_KINV;
+            float* qinv = vs + VEC_QINV;
             ok = __all_sync(0xffffffffu, mbar_wait(bar(B_IN_FULL + slot), (uint32_t)(c >> 1) & 1u));
-            named_bar_sync(BAR_PREP, NPREP);  // g and beta of the chunk are in
-            // norms: warp pw takes rows 8 pw .. 8 pw + 7 of k and q; lane l holds dims 4l .. 4l + 3
+            // norms: four threads per row (32 dims each: two 16-byte chunks of each box half),
+            // rows pt / 4 of k and of q
             if (ok) {
-                const int b = lane >> 4, col = (lane & 15) * 4;
-#pragma unroll 2
-                for (int i = 0; i < 8; i++) {
-                    const int r = pw * 8 + i;
-                    const uint2 kr = *reinterpret_cast<const uint2*>(kqp + b * 2 * BOX + box_off(r, col));
-                    const uint2 qr = *reinterpret_cast<const uint2*>(kqp + b * 2 * BOX + BOX + box_off(r, col));
-                    const __nv_bfloat162* kp = reinterpret_cast<const __nv_bfloat162*>(&kr);
-                    const __nv_bfloat162* qp = reinterpret_cast<const __nv_bfloat162*>(&qr);
-                    const float2 k01 = __bfloat1622float2(kp[0]), k23 = __bfloat1622float2(kp[1]);
-                    const float2 q01 = __bfloat1622float2(qp[0]), q23 = __bfloat1622float2(qp[1]);
-                    float ks = 0.f, qs = 0.f;
-                    ks = fmaf(k01.x, k01.x, ks);
-                    ks = fmaf(k01.y, k01.y, ks);
-                    ks = fmaf(k23.x, k23.x, ks);
-                    ks = fmaf(k23.y, k23.y, ks);
-                    qs = fmaf(q01.x, q01.x, qs);
-                    qs = fmaf(q01.y, q01.y, qs);
-                    qs = fmaf(q23.x, q23.x, qs);
-                    qs = fmaf(q23.y, q23.y, qs);
-                    ks = warp_sum(ks);
-                    qs = warp_sum(qs);
-                    if (lane == 0) {
-                        kinv[r] = rsqrtf(ks + 1e-6f);
-                        qinv[r] = rsqrtf(qs + 1e-6f) * scale;
+                const int r = pt >> 2, qq = pt & 3, b = qq >> 1, ch0 = (qq & 1) * 4;
+                float ks = 0.f, qs = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    float kx[8], qx[8];
+                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(r, ch0 + i)), kx);
+                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + BOX + sw128_offset(r, ch0 + i)), qx);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) {
+                        ks = fmaf(kx[e], kx[e], ks);
+                        qs = fmaf(qx[e], qx[e], qs);
                     }
                 }
-                if (pt == 0) {
-                    // sequential fp32 sum (the reference's order), from registers
-                    float gv[C];
-#pragma unroll
-                    for (int i = 0; i < C; i++) gv[i] = gg[i];
-                    float s = 0.f;
-#pragma unroll
-                    for (int i = 0; i < C; i++) {
-                        s += gv[i];
-                        cum[i] = s;
-                    }
-                    vec[VEC_DECAY + slot] = expf(s);
+                ks += __shfl_xor_sync(0xffffffffu, ks, 1);
+                qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+                ks += __shfl_xor_sync(0xffffffffu, ks, 2);
+                qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+                if (qq == 0) {
+                    kinv[r] = rsqrtf(ks + 1e-6f);
+                    qinv[r] = rsqrtf(qs + 1e-6f) * scale;
                 }
             }
-            named_bar_sync(BAR_PREP, NPREP);
-            if (pt < C) {
-                ecum[pt] = expf(cum[pt]);
-                erem[pt] = expf(cum[C - 1] - cum[pt]);
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_VEC_READY + slot), (uint32_t)(c >> 1) & 1u));
+            named_bar_sync(BAR_PREP, NPREP);  // norms and the chunk's vectors are in
+            if (pt == 0) {
+                __threadfence_block();
+                *norms_done = c + 1;
             }
-            // A (rows of k, TMEM lanes 0..63) and P (rows of q, lanes 64..127) from D1;
-            // warp pw reads lane quarter pw % 4, columns 32 (pw / 4) .. + 31
-            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_D1_FULL), (uint32_t)c & 1u));
+            // kw = bf16(k^ e^cum), the MN-major A operand of w^T = kw^T tb^T, while MMA1 runs
             if (ok) {
-                tc_fence_after();
-                const int j0 = (pw >> 2) * 32, row = wq * 32 + lane;
-                float d[32];
-                tmem_ld32(lrow + TM_D1 + (uint32_t)j0, d);
-                tmem_ld_wait();
-                if (row < C) {
-                    const int i = row;
-                    const float ci = cum[i], si = bet[i] * kinv[i];
-                    float* arow = A + i * LDT + j0;
-#pragma unroll
-                    for (int j4 = 0; j4 < 8; j4++) {
-                        float f[4];
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const int j = j0 + j4 * 4 + e;
-                            f[e] = j < i ? si * (d[j4 * 4 + e] * kinv[j]) * __expf(ci - cum[j]) : 0.f;
-                        }
-                        *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(f[0], f[1], f[2], f[3]);
-                    }
-                } else {
-                    const int t = row - C;
-                    const float ct = cum[t], st_ = qinv[t];
-                    uint8_t* pt_tile = sm + OFF_P + slot * BOX;
-#pragma unroll
-                    for (int c8 = 0; c8 < 4; c8++) {
-                        float f[8];
-#pragma unroll
-                        for (int e = 0; e < 8; e++) {
-                            const int j = j0 + c8 * 8 + e;
-                            f[e] = j <= t ? (d[c8 * 8 + e] * st_) * kinv[j] * __expf(ct - cum[j]) : 0.f;
-                        }
-                        *reinterpret_cast<Pack8*>(pt_tile + sw128_offset(t, (j0 >> 3) + c8)) = pack8(f);
-                    }
-                }
-            }
-            named_bar_sync(BAR_PREP, NPREP);  // A complete
-            // T = (I + A)^-1. Diagonal 16x16 blocks: one thread per (block, column).
-            if (ok && pt < C) {
-                const int b = pt >> 4, col = pt & 15, o16 = b * 16;
-                float x[16];
-#pragma unroll
-                for (int r = 0; r < 16; r++) {
-                    float acc = r == col ? 1.f : 0.f;
-#pragma unroll
-                    for (int m = 0; m < r; m++) acc = fmaf(-A[(o16 + r) * LDT + o16 + m], x[m], acc);
-                    x[r] = r < col ? 0.f : acc;
-                }
-#pragma unroll
-                for (int r = 0; r < 16; r++) Tm[(o16 + r) * LDT + o16 + col] = x[r];
-            }
-            for (int x = pt; x < C * C; x += NPREP) {
-                const int i = x / C, j = x % C;
-                if ((j >> 4) > (i >> 4)) Tm[i * LDT + j] = 0.f;
-            }
-            named_bar_sync(BAR_PREP, NPREP);
-            // block rows bi = 1..3: X_bj = sum_{kb = bj}^{bi-1} A_(bi,kb) T_(kb,bj), then
-            // T_(bi,bj) = -T_(bi,bi) X_bj; thread = (bj, row r, 4 columns)
-#pragma unroll 1
-            for (int bi = 1; bi < 4; bi++) {
-                const int bj = pt >> 6, r = (pt >> 2) & 15, c4 = (pt & 3) * 4;
-                if (pt < bi * 64) {
-                    const float* arow = A + (16 * bi + r) * LDT;
-                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-                    for (int kb = bj; kb < bi; kb++) {
-#pragma unroll
-                        for (int m = 0; m < 16; m++) {
-                            const float av = arow[16 * kb + m];
-                            const float4 tv = *reinterpret_cast<const float4*>(Tm + (16 * kb + m) * LDT + 16 * bj + c4);
-                            a0 = fmaf(av, tv.x, a0);
-                            a1 = fmaf(av, tv.y, a1);
-                            a2 = fmaf(av, tv.z, a2);
-                            a3 = fmaf(av, tv.w, a3);
-                        }
-                    }
-                    *reinterpret_cast<float4*>(X + (bj * 16 + r) * 16 + c4) = make_float4(a0, a1, a2, a3);
-                }
-                named_bar_sync(BAR_PREP, NPREP);
-                if (pt < bi * 64) {
-                    const float* trow = Tm + (16 * bi + r) * LDT + 16 * bi;
-                    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll
-                    for (int m = 0; m < 16; m++) {
-                        if (m <= r) {
-                            const float tv = trow[m];
-                            const float4 sv = *reinterpret_cast<const float4*>(X + (bj * 16 + m) * 16 + c4);
-                            a0 = fmaf(tv, sv.x, a0);
-                            a1 = fmaf(tv, sv.y, a1);
-                            a2 = fmaf(tv, sv.z, a2);
-                            a3 = fmaf(tv, sv.w, a3);
-                        }
-                    }
-                    *reinterpret_cast<float4*>(Tm + (16 * bi + r) * LDT + 16 * bj + c4) =
-                        make_float4(-a0, -a1, -a2, -a3);
-                }
-                named_bar_sync(BAR_PREP, NPREP);
-            }
-            // tb = bf16(T diag(beta)) K-major [64 t][64 j]; kw = bf16(k^ e^cum) MN-major [j][k]
-            if (ok) {
-                for (int u = pt; u < C * C / 8; u += NPREP) {
-                    const int t = u >> 3, j0 = (u & 7) * 8;
-                    float f[8];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) f[e] = Tm[t * LDT + j0 + e] * bet[j0 + e];
-                    *reinterpret_cast<Pack8*>(sm + OFF_TB + sw128_offset(t, j0 >> 3)) = pack8(f);
-                }
                 for (int u = pt; u < C * 16; u += NPREP) {
                     const int j = u >> 4, b = (u >> 3) & 1, ch = u & 7;
                     float f[8];
@@ -612,13 +624,136 @@ __global__ void __launch_bounds__(THREADS, 1)
                     for (int e = 0; e < 8; e++) f[e] = (f[e] * kv) * ec;
                     *reinterpret_cast<Pack8*>(sm + OFF_KW + b * BOX + sw128_offset(j, ch)) = pack8(f);
                 }
-                fence_async_smem();
             }
+            // A (rows of k, TMEM lanes 0..63) and P (rows of q, lanes 64..127) from D1;
+            // warp pw reads lane quarter pw % 4, columns 32 (pw / 4) .. + 31. P goes into this
+            // chunk's buffer once the previous chunk's update MMAs have read it.
+            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_D1_FULL), (uint32_t)c & 1u) &&
+                                                   mbar_wait(bar(B_OPS_KD_FREE), (uint32_t)(c + 1) & 1u));
+            if (ok) {
+                tc_fence_after();
+                const int j0 = (pw >> 2) * 32, row = wq * 32 + lane;
+                // the lane quarters of rows 0..31 (k) and 0..31 (q) have nothing left of the
+                // diagonal in columns 32..63
+                const bool live = (wq & 1) || j0 == 0;
+                float d[32];
+                tmem_ld32(lrow + TM_D1 + (uint32_t)j0, d);
+                tmem_ld_wait();
+                if (row < C) {
+                    const int i = row;
+                    float* arow = A + i * LDT + j0;
+                    if (live) {
+                        const float ci = cum2[i], si = bet[i] * kinv[i];
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; j4++) {
+                            float f[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const int j = j0 + j4 * 4 + e;
+                                f[e] = j < i ? si * (d[j4 * 4 + e] * kinv[j]) * ex2(ci - cum2[j]) : 0.f;
+                            }
+                            *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(f[0], f[1], f[2], f[3]);
+                        }
+                    }
+                } else {
+                    const int t = row - C;
+                    uint8_t* pt_tile = sm + OFF_P + slot * BOX;
+                    const float ct = cum2[t], st_ = qinv[t];
+#pragma unroll
+                    for (int c8 = 0; c8 < 4; c8++) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            const int j = j0 + c8 * 8 + e;
+                            f[e] = (live && j <= t) ? (d[c8 * 8 + e] * st_) * kinv[j] * ex2(ct - cum2[j]) : 0.f;
+                        }
+                        *reinterpret_cast<Pack8*>(pt_tile + sw128_offset(t, (j0 >> 3) + c8)) = pack8(f);
+                    }
+                }
+                fence_async_smem();  // P (and kw) are read by MMAs
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(bar(B_OPS2_READY));
+                    mbar_arrive(bar(B_IN_KQ_FREE + slot));  // MMA1 is done and kw is formed
+                }
+            }
+            named_bar_sync(BAR_PREP, NPREP);  // A complete
+            // T = (I + A)^-1 in two diagonal 32 x 32 blocks and the block below them, written out
+            // as tb = bf16(T diag(beta)) (K-major [64 t][64 j]) as the entries become final.
+            // Diagonal blocks: one thread per (block, column), right-looking substitution (each
+            // solved entry updates the later rows at once: a chain 32 steps deep, the terms of
+            // every entry added in the order of the plain forward substitution).
+            uint8_t* tb = sm + OFF_TB;
+            if (ok && pt < C) {
+                const int b = pt >> 5, col = pt & 31, o32 = b * 32;
+                float x[32];
+#pragma unroll
+                for (int r = 0; r < 32; r++) x[r] = r == col ? 1.f : 0.f;
+#pragma unroll
+                for (int m = 0; m < 31; m++) {
+                    const float xm = x[m];
+#pragma unroll
+                    for (int r = m + 1; r < 32; r++) x[r] = fmaf(-A[(o32 + r) * LDT + o32 + m], xm, x[r]);
+                }
+                const float bj = bet[o32 + col];
+                bf16* tcol = reinterpret_cast<bf16*>(tb);
+#pragma unroll
+                for (int r = 0; r < 32; r++) {
+                    const float tv = r < col ? 0.f : x[r];
+                    Tm[(o32 + r) * LDT + o32 + col] = tv;
+                    const int t = o32 + r, j = o32 + col;
+                    tcol[(sw128_offset(t, j >> 3) >> 1) + (j & 7)] = to_bf16(tv * bj);
+                }
+            } else if (ok && pt < C + 32 * 4) {
+                // tb's upper block (rows 0..31, columns 32..63) is zero
+                const int u = pt - C, t = u >> 2, ch = 4 + (u & 3);
+                *reinterpret_cast<uint4*>(tb + sw128_offset(t, ch)) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            named_bar_sync(BAR_PREP, NPREP);
+            // X = A_10 T_00, then T_10 = -T_11 X; thread = (row r, 4 columns c4)
+            {
+                const int r = pt >> 3, c4 = (pt & 7) * 4;
+                const float* arow = A + (32 + r) * LDT;
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 8
+                for (int m = 0; m < 32; m++) {
+                    const float av = arow[m];
+                    const float4 tv = *reinterpret_cast<const float4*>(Tm + m * LDT + c4);
+                    a0 = fmaf(av, tv.x, a0);
+                    a1 = fmaf(av, tv.y, a1);
+                    a2 = fmaf(av, tv.z, a2);
+                    a3 = fmaf(av, tv.w, a3);
+                }
+                *reinterpret_cast<float4*>(X + r * 32 + c4) = make_float4(a0, a1, a2, a3);
+                named_bar_sync(BAR_PREP, NPREP);
+                const float* trow = Tm + (32 + r) * LDT + 32;
+                a0 = a1 = a2 = a3 = 0.f;
+#pragma unroll 8
+                for (int m = 0; m < 32; m++) {
+                    if (m <= r) {
+                        const float tv = trow[m];
+                        const float4 xv = *reinterpret_cast<const float4*>(X + m * 32 + c4);
+                        a0 = fmaf(tv, xv.x, a0);
+                        a1 = fmaf(tv, xv.y, a1);
+                        a2 = fmaf(tv, xv.z, a2);
+                        a3 = fmaf(tv, xv.w, a3);
+                    }
+                }
+                if (ok) {
+                    const int t = 32 + r;
+                    uint2 pk;
+                    pk.x = pack_bf16x2(-a0 * bet[c4], -a1 * bet[c4 + 1]);
+                    pk.y = pack_bf16x2(-a2 * bet[c4 + 2], -a3 * bet[c4 + 3]);
+                    *reinterpret_cast<uint2*>(tb + sw128_offset(t, c4 >> 3) + (c4 & 7) * 2) = pk;
+                }
+            }
+            fence_async_smem();
             tc_fence_before();  // the D1 loads are complete before MMA2 rewrites those columns
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(bar(B_TB_READY));
             // w^T from TMEM (lane = k) into the MN-major [128 k][64 t] operand tile, once the
-            // previous chunk's first scan MMAs have read the tile
+            // previous chunk's first scan MMAs have read it
             ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_MMA2_DONE), (uint32_t)c & 1u) &&
                                                    mbar_wait(bar(B_OPS_W_FREE), (uint32_t)(c + 1) & 1u));
             if (ok) {
@@ -630,32 +765,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int c4 = 0; c4 < 4; c4++)
                     *reinterpret_cast<Pack8*>(sm + OFF_W + sw128_offset(kr, (t0w >> 3) + c4)) = pack8(x + 8 * c4);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bar(B_D1W_FREE));
-            }
-            // qd and kd, once the previous chunk's update MMAs have read kd
-            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_OPS_KD_FREE), (uint32_t)(c + 1) & 1u));
-            if (ok) {
-                for (int u = pt; u < C * 16; u += NPREP) {
-                    const int t = u >> 4, b = (u >> 3) & 1, ch = u & 7;
-                    float kx[8], qx[8];
-                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(t, ch)), kx);
-                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + BOX + sw128_offset(t, ch)), qx);
-                    const float kv = kinv[t], qv = qinv[t], ec = ecum[t], er = erem[t];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        qx[e] = (qx[e] * qv) * ec;
-                        kx[e] = (kx[e] * kv) * er;
-                    }
-                    *reinterpret_cast<Pack8*>(sm + OFF_QD + b * BOX + sw128_offset(t, ch)) = pack8(qx);
-                    *reinterpret_cast<Pack8*>(sm + OFF_KD + b * BOX + sw128_offset(t, ch)) = pack8(kx);
-                }
                 fence_async_smem();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(bar(B_OPS_READY));
-                    mbar_arrive(bar(B_IN_KQ_FREE + slot));
+                    mbar_arrive(bar(B_D1W_FREE));
+                    mbar_arrive(bar(B_VEC_FREE + slot));
                 }
             }
         }
