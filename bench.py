@@ -354,6 +354,63 @@ def gemm_roofline(cs1, cfg, M, stream, torch):
     return flops / (ms * 1e-3) / 1e12, ms, flops, per_shape
 
 
+def op_rooflines(cs1, cfg, lens, stream, torch, peak_tf, peak_bw, reps=10):
+    """The GDN prefill and the gated attention at the workload's packed lengths, timed alone
+    with CUDA events on the launching stream (after 3 warm-up calls; inputs ~N(0,1) or
+    U(0,1) as in the reference's tests), against their algorithmic bounds: GDN bytes
+    q, k (2 HK 128 2), v, o (2 H 128 2), g (4 H), beta (2 H) per token against the HBM peak
+    (its 6.7 MFLOP per token at 27B are under the ridge); attention 4 Hq 256 T(T+1)/2 FLOP
+    per sequence against the bf16 peak."""
+    import ctypes
+    T, n = int(sum(lens)), len(lens)
+    arr = np.asarray(lens, dtype=np.uintp)
+    H, HK, hq, hkv = cfg.lin_v_heads, cfg.lin_k_heads, cfg.heads, cfg.kv_heads
+    out = {}
+
+    def timed(call):
+        for _ in range(3):
+            assert call() == 0
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record(torch.cuda.current_stream())
+        for _ in range(reps):
+            call()
+        e.record(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / reps
+
+    q = torch.randn(T, HK, 128, device="cuda").to(torch.bfloat16)
+    k = torch.randn(T, HK, 128, device="cuda").to(torch.bfloat16)
+    v = torch.randn(T, H, 128, device="cuda").to(torch.bfloat16)
+    g = -torch.rand(T, H, device="cuda") * 0.25
+    beta = torch.rand(T, H, device="cuda").to(torch.bfloat16)
+    o = torch.empty(T, H, 128, device="cuda", dtype=torch.bfloat16)
+    ws = torch.empty(64, dtype=torch.float32, device="cuda")  # the fused kernel reads no workspace
+    ms = timed(lambda: cs1.raw.cs1_gdn_prefill_batch_x(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), o.data_ptr(), ws.data_ptr(),
+        ws.numel() * 4, arr.ctypes.data, n, H, HK, ctypes.c_float(128 ** -0.5), None, 0, None, stream))
+    byt = T * (2 * HK * 128 * 2 + 2 * H * 128 * 2 + H * 4 + H * 2)
+    gbs = byt / (ms * 1e-3) / 1e9
+    out["gdn"] = {"kernel": "gdn_fused (preparation and scan of each head and sequence in one CTA)",
+                  "ms_per_launch": ms, "bound": "hbm", "algorithmic_bytes_per_launch": byt, "achieved": gbs,
+                  "peak": peak_bw, "unit": "GB/s", "frac": gbs / peak_bw}
+    del q, k, v, g, beta, o, ws
+    qa = torch.randn(T, hq, 256, device="cuda").to(torch.bfloat16)
+    ka = torch.randn(T, hkv, 256, device="cuda").to(torch.bfloat16)
+    va = torch.randn(T, hkv, 256, device="cuda").to(torch.bfloat16)
+    ga = torch.randn(T, hq, 256, device="cuda").to(torch.bfloat16)
+    oa = torch.empty(T, hq, 256, device="cuda", dtype=torch.bfloat16)
+    ms = timed(lambda: cs1.raw.cs1_attention_gated_batch(
+        qa.data_ptr(), ka.data_ptr(), va.data_ptr(), hkv * 256, ga.data_ptr(), oa.data_ptr(), arr.ctypes.data, n, hq,
+        hkv, 256, ctypes.c_float(256 ** -0.5), stream))
+    fl = sum(4.0 * hq * 256 * L * (L + 1) / 2 for L in lens)
+    tf = fl / (ms * 1e-3) / 1e12
+    out["attention"] = {"kernel": "flash_tc (S, P, O in TMEM)", "ms_per_launch": ms, "bound": "tensor",
+                        "algorithmic_flops_per_launch": fl, "achieved": tf, "peak": peak_tf, "unit": "TFLOP/s",
+                        "frac": tf / peak_tf}
+    return out
+
+
 def long_prefill(model, torch, stream, steps=3):
     """Workload (b): one 32,768-token prefill, staged in HBM, CUDA-graph replay timed with
     CUDA events on the model's stream."""
@@ -573,6 +630,8 @@ def run_ours(args, rank, world, local):
         tflops, gms, gflops, per_shape = gemm_roofline(cs1, cfg, tokens, torch.cuda.current_stream().cuda_stream,
                                                        torch)
         peak_tf, peak_bw, peak_kind = measured_peaks()
+        ops = op_rooflines(cs1, cfg, [len(s) for s in seqs], torch.cuda.current_stream().cuda_stream, torch, peak_tf,
+                           peak_bw)
         _, sw_n, sw_k, sw_ms = next(x for x in per_shape if x[0] == "swiglu")
         sw_flops = 2.0 * tokens * sw_n * sw_k
         sw_tf = sw_flops / (sw_ms * 1e-3) / 1e12
@@ -605,7 +664,8 @@ def run_ours(args, rank, world, local):
                                             "per_shape": [{"epilogue": k, "n": n_, "k": k_, "ms": round(t_, 4),
                                                            "tflops": round(2.0 * tokens * n_ * k_ / (t_ * 1e-3) / 1e12, 1)}
                                                           for k, n_, k_, t_ in per_shape]},
-                         "forward_projection_tflops": proj / (ms_max * 1e-3) / 1e12},
+                         "forward_projection_tflops": proj / (ms_max * 1e-3) / 1e12,
+                         "operators": ops},
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "reference",
                              "sample": cpu_sample_desc()} if use_cpu else None,
             "p50_decision_latency_ms": lat,
