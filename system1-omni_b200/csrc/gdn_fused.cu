@@ -70,13 +70,14 @@ constexpr int OFF_KQ = 0;                     // two slots
 constexpr int OFF_V = OFF_KQ + 2 * KQ_TILE;   // v [64 j][128 v] as two MN blocks
 constexpr int OFF_KW = OFF_V + 2 * BOX;       // k^ e^cum [64 j][128 k] as two MN blocks
 constexpr int OFF_TB = OFF_KW + 2 * BOX;      // tb [64 t][64 j] K-major
-constexpr int OFF_W = OFF_TB + BOX;           // w^T [128 k][64 t]: the MN-major B operand of (wS)^T
-constexpr int OFF_QD = OFF_W + 2 * BOX;       // qd [64 t][128 k] K-major (two sub-tiles)
+constexpr int OFF_W = OFF_TB + BOX;           // w^T [128 k][64 t]: the MN-major B operand of (wS)^T, two chunk buffers
+constexpr int OFF_QD = OFF_W + 4 * BOX;       // qd [64 t][128 k] K-major (two sub-tiles)
 constexpr int OFF_KD = OFF_QD + 2 * BOX;      // kd [64 t][128 k] MN-major (two blocks)
 constexpr int OFF_P = OFF_KD + 2 * BOX;       // P [64 t][64 j] K-major, two chunk buffers
 constexpr int OFF_A = OFF_P + 2 * BOX;        // A fp32 [64][LDT]
-constexpr int OFF_T = OFF_A + C * LDT * 4;    // T fp32 [64][LDT] (its two diagonal 32 x 32 blocks)
-constexpr int OFF_X = OFF_T + C * LDT * 4;    // inverse scratch [32][32] fp32
+constexpr int LDD = 36;                       // fp32 row stride of the diagonal blocks of T
+constexpr int OFF_T = OFF_A + C * LDT * 4;    // T's two diagonal 32 x 32 blocks, fp32 [2][32][LDD]
+constexpr int OFF_X = OFF_T + 2 * 32 * LDD * 4;  // inverse scratch [32][32] fp32
 constexpr int OFF_VEC = OFF_X + 32 * 32 * 4;  // per-chunk vectors (floats)
 // two chunk slots of VEC_SLOT floats: cum * log2(e), beta, e^cum, e^{last - cum}, g
 // (scratch), written by the vector warp, and the inverse norms of k and q (q's times the
@@ -85,7 +86,7 @@ constexpr int VEC_CUM2 = 0, VEC_BET = 64, VEC_ECUM = 128, VEC_EREM = 192, VEC_G 
               VEC_QINV = 384, VEC_SLOT = 448;
 constexpr int VEC_DECAY = 2 * VEC_SLOT;
 constexpr int OFF_BAR = OFF_VEC + (VEC_DECAY + 8) * 4;
-constexpr int NBAR = 32;
+constexpr int NBAR = 40;
 constexpr int SMEM = OFF_BAR + NBAR * 8 + 64 + 1024;
 
 // TMEM columns
@@ -101,9 +102,7 @@ enum Bar : int {
     B_TB_READY = 7,     // tb and kw tiles written (count 8)
     B_MMA2_DONE = 8,    // u^T and w^T in TMEM
     B_U_FREE = 9,       // [2] scan read u^T of the slot (count 4)
-    B_OPS_READY = 11,   // w of the chunk written by the preparation (count 8)
-    B_OPS_W_FREE = 12,  // the first scan MMAs read w and qd
-    B_OPS_KD_FREE = 13, // the second scan MMAs read kd and P
+    B_OPS_READY = 11,   // [2] w of the chunk written into the slot by the preparation (count 8)
     B_S_READY = 14,     // S^T bf16 copy and e^{last} S^T written (count 4)
     B_WS_DONE = 15,     // (wS)^T and (qd S)^T in TMEM
     B_VN_READY = 16,    // v_new^T written (count 4)
@@ -113,9 +112,11 @@ enum Bar : int {
     B_VEC_READY = 20,   // [2] the vector warp wrote the slot's vectors (count 1)
     B_VEC_FREE = 22,    // [2] preparation and scan warps are done with the slot (count 12)
     B_DEC_READY = 24,   // [4] the chunk's decay is in the ring (count 1)
-    B_OPS2_READY = 28,  // P of the chunk written by the preparation (count 8)
     B_QD_READY = 29,    // qd of the chunk written by the scan warps (count 4)
     B_KD_READY = 30,    // kd of the chunk written by the scan warps (count 4)
+    B_W_FREE = 32,      // [2] the first scan MMAs read the slot's w
+    B_P_FREE = 34,      // [2] the second scan MMAs read the slot's P
+    B_OPS2_READY = 36,  // [2] P of the chunk written into the slot by the preparation (count 8)
 };
 
 struct Maps {
@@ -163,6 +164,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(bar(B_U_FREE + i), 4);
             mbar_init(bar(B_VEC_READY + i), 1);
             mbar_init(bar(B_VEC_FREE + i), 12);
+            mbar_init(bar(B_OPS_READY + i), 8);
+            mbar_init(bar(B_W_FREE + i), 1);
+            mbar_init(bar(B_P_FREE + i), 1);
+            mbar_init(bar(B_OPS2_READY + i), 8);
         }
         for (int i = 0; i < 4; i++) mbar_init(bar(B_DEC_READY + i), 1);
         mbar_init(bar(B_IN_V_FREE), 1);
@@ -170,16 +175,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(bar(B_D1W_FREE), 8);
         mbar_init(bar(B_TB_READY), 8);
         mbar_init(bar(B_MMA2_DONE), 1);
-        mbar_init(bar(B_OPS_READY), 8);
-        mbar_init(bar(B_OPS_W_FREE), 1);
-        mbar_init(bar(B_OPS_KD_FREE), 1);
         mbar_init(bar(B_S_READY), 4);
         mbar_init(bar(B_WS_DONE), 1);
         mbar_init(bar(B_VN_READY), 4);
         mbar_init(bar(B_UPD_DONE), 1);
         mbar_init(bar(B_DRAIN_SCAN), 1);
         mbar_init(bar(B_DRAIN_PREP), 1);
-        mbar_init(bar(B_OPS2_READY), 8);
         mbar_init(bar(B_QD_READY), 4);
         mbar_init(bar(B_KD_READY), 4);
         *abort_flag = 0;
@@ -236,8 +237,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             bool ok = true;
             for (int c = 0; c < NC; c++) {
                 if (*abort_flag) break;
-                const uint32_t par = (uint32_t)c & 1u;
-                if (!mbar_wait(bar(B_OPS_READY), par) || !mbar_wait(bar(B_QD_READY), par) ||
+                const uint32_t par = (uint32_t)c & 1u, spar = (uint32_t)(c >> 1) & 1u;
+                const int slot = c & 1;
+                if (!mbar_wait(bar(B_OPS_READY + slot), spar) || !mbar_wait(bar(B_QD_READY), par) ||
                     !mbar_wait(bar(B_S_READY), par)) {
                     ok = false;
                     break;
@@ -246,13 +248,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int kk = 0; kk < 8; kk++) {
                     const uint32_t a = tmem + TM_ST + (uint32_t)kk * 8;
-                    mma_bf16_ts(tmem + TM_WS, a, desc_sw128_mn(base + OFF_W + kk * 2048, BOX, 1024), ID_W, kk > 0);
+                    mma_bf16_ts(tmem + TM_WS, a, desc_sw128_mn(base + OFF_W + slot * 2 * BOX + kk * 2048, BOX, 1024),
+                                ID_W, kk > 0);
                     mma_bf16_ts(tmem + TM_O, a, desc_sw128(base + OFF_QD + (kk >> 2) * BOX + (kk & 3) * 32), ID_K64,
                                 kk > 0);
                 }
                 mma_commit(bar(B_WS_DONE));
-                mma_commit(bar(B_OPS_W_FREE));
-                if (!mbar_wait(bar(B_VN_READY), par) || !mbar_wait(bar(B_OPS2_READY), par) ||
+                mma_commit(bar(B_W_FREE + slot));
+                if (!mbar_wait(bar(B_VN_READY), par) || !mbar_wait(bar(B_OPS2_READY + slot), spar) ||
                     !mbar_wait(bar(B_KD_READY), par)) {
                     ok = false;
                     break;
@@ -266,7 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     mma_bf16_ts(tmem + TM_S, a, desc_sw128_mn(base + OFF_KD + kk * 2048, BOX, 1024), ID_KD, 1);
                 }
                 mma_commit(bar(B_UPD_DONE));
-                mma_commit(bar(B_OPS_KD_FREE));
+                mma_commit(bar(B_P_FREE + slot));
             }
             if (!ok) fail(FAULT_WAIT_MMA, abort_flag);
             mma_commit(bar(B_DRAIN_SCAN));
@@ -416,15 +419,21 @@ __global__ void __launch_bounds__(THREADS, 1)
         };
         // The o rows of chunk c: this thread's column v of each row, 2-byte stores (a warp
         // writes 64 contiguous bytes of a row per store).
+        // Adjacent lanes swap halves so that each stores two adjacent columns of one row: the
+        // even lane rows 2i, the odd lane rows 2i + 1 (a warp writes 64 contiguous bytes of each
+        // of two rows per store).
         auto write_o = [&](int c, const uint32_t (&opk)[32]) {
             const int rows = min(C, len - c * C);
-            bf16* dst = o + ((size_t)(start + c * C) * H + h) * V + v;
-            const size_t pitch = (size_t)H * V;
+            const bool odd = lane & 1;
+            uint32_t* dst = reinterpret_cast<uint32_t*>(o + ((size_t)(start + c * C) * H + h) * V + (v & ~1)) +
+                            (odd ? (size_t)H * V / 2 : 0);
+            const size_t pitch2 = (size_t)H * V;  // two rows, in 32-bit words
 #pragma unroll
             for (int i = 0; i < 32; i++) {
-                const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(&opk[i]);
-                if (2 * i < rows) dst[(size_t)(2 * i) * pitch] = p2.x;
-                if (2 * i + 1 < rows) dst[(size_t)(2 * i + 1) * pitch] = p2.y;
+                const uint32_t mine = opk[i];  // (row 2i, row 2i + 1) of column v
+                const uint32_t other = __shfl_xor_sync(0xffffffffu, odd ? (mine & 0xFFFFu) : (mine >> 16), 1);
+                const uint32_t pair = odd ? (other | (mine & 0xFFFF0000u)) : ((mine & 0xFFFFu) | (other << 16));
+                if (2 * i + (odd ? 1 : 0) < rows) dst[(size_t)i * pitch2] = pair;
             }
         };
         // qd = bf16(q^ e^cum) and kd = bf16(k^ e^{last - cum}) of chunk c from its q, k rows, once
@@ -581,16 +590,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             const float* ecum = vs + VEC_ECUM;
             float* kinv = vs + VEC_KINV;
             float* qinv = vs + VEC_QINV;
-            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_IN_FULL + slot), (uint32_t)(c >> 1) & 1u));
+            ok = __all_sync(0xffffffffu, mbar_wait(bar(B_IN_FULL + slot), (uint32_t)(c >> 1) & 1u) &&
+                                             mbar_wait(bar(B_VEC_READY + slot), (uint32_t)(c >> 1) & 1u));
             // norms: four threads per row (32 dims each: two 16-byte chunks of each box half),
-            // rows pt / 4 of k and of q
+            // rows pt / 4 of k and of q; the same threads then form their part of
+            // kw = bf16(k^ e^cum), the MN-major A operand of w^T = kw^T tb^T, while MMA1 runs
             if (ok) {
                 const int r = pt >> 2, qq = pt & 3, b = qq >> 1, ch0 = (qq & 1) * 4;
+                Pack8 kr[4];
                 float ks = 0.f, qs = 0.f;
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     float kx[8], qx[8];
-                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(r, ch0 + i)), kx);
+                    kr[i] = *reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(r, ch0 + i));
+                    unpack8(kr[i], kx);
                     unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + BOX + sw128_offset(r, ch0 + i)), qx);
 #pragma unroll
                     for (int e = 0; e < 8; e++) {
@@ -602,34 +615,30 @@ __global__ void __launch_bounds__(THREADS, 1)
                 qs += __shfl_xor_sync(0xffffffffu, qs, 1);
                 ks += __shfl_xor_sync(0xffffffffu, ks, 2);
                 qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+                const float kv = rsqrtf(ks + 1e-6f), ec = ecum[r];
                 if (qq == 0) {
-                    kinv[r] = rsqrtf(ks + 1e-6f);
+                    kinv[r] = kv;
                     qinv[r] = rsqrtf(qs + 1e-6f) * scale;
                 }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    float f[8];
+                    unpack8(kr[i], f);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) f[e] = (f[e] * kv) * ec;
+                    *reinterpret_cast<Pack8*>(sm + OFF_KW + b * BOX + sw128_offset(r, ch0 + i)) = pack8(f);
+                }
             }
-            ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_VEC_READY + slot), (uint32_t)(c >> 1) & 1u));
-            named_bar_sync(BAR_PREP, NPREP);  // norms and the chunk's vectors are in
+            named_bar_sync(BAR_PREP, NPREP);  // norms and kw are in
             if (pt == 0) {
                 __threadfence_block();
                 *norms_done = c + 1;
             }
-            // kw = bf16(k^ e^cum), the MN-major A operand of w^T = kw^T tb^T, while MMA1 runs
-            if (ok) {
-                for (int u = pt; u < C * 16; u += NPREP) {
-                    const int j = u >> 4, b = (u >> 3) & 1, ch = u & 7;
-                    float f[8];
-                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(j, ch)), f);
-                    const float kv = kinv[j], ec = ecum[j];
-#pragma unroll
-                    for (int e = 0; e < 8; e++) f[e] = (f[e] * kv) * ec;
-                    *reinterpret_cast<Pack8*>(sm + OFF_KW + b * BOX + sw128_offset(j, ch)) = pack8(f);
-                }
-            }
             // A (rows of k, TMEM lanes 0..63) and P (rows of q, lanes 64..127) from D1;
             // warp pw reads lane quarter pw % 4, columns 32 (pw / 4) .. + 31. P goes into this
-            // chunk's buffer once the previous chunk's update MMAs have read it.
+            // chunk's buffer once the update MMAs of chunk c - 2 have read it.
             ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_D1_FULL), (uint32_t)c & 1u) &&
-                                                   mbar_wait(bar(B_OPS_KD_FREE), (uint32_t)(c + 1) & 1u));
+                                                   mbar_wait(bar(B_P_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u));
             if (ok) {
                 tc_fence_after();
                 const int j0 = (pw >> 2) * 32, row = wq * 32 + lane;
@@ -646,11 +655,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const float ci = cum2[i], si = bet[i] * kinv[i];
 #pragma unroll
                         for (int j4 = 0; j4 < 8; j4++) {
+                            const float4 kv4 = *reinterpret_cast<const float4*>(kinv + j0 + j4 * 4);
+                            const float4 cv4 = *reinterpret_cast<const float4*>(cum2 + j0 + j4 * 4);
+                            const float kv[4] = {kv4.x, kv4.y, kv4.z, kv4.w}, cv[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
                             float f[4];
 #pragma unroll
                             for (int e = 0; e < 4; e++) {
                                 const int j = j0 + j4 * 4 + e;
-                                f[e] = j < i ? si * (d[j4 * 4 + e] * kinv[j]) * ex2(ci - cum2[j]) : 0.f;
+                                f[e] = j < i ? si * (d[j4 * 4 + e] * kv[e]) * ex2(ci - cv[e]) : 0.f;
                             }
                             *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(f[0], f[1], f[2], f[3]);
                         }
@@ -661,11 +673,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const float ct = cum2[t], st_ = qinv[t];
 #pragma unroll
                     for (int c8 = 0; c8 < 4; c8++) {
-                        float f[8];
+                        float f[8], kv[8], cv[8];
+                        *reinterpret_cast<float4*>(kv) = *reinterpret_cast<const float4*>(kinv + j0 + c8 * 8);
+                        *reinterpret_cast<float4*>(kv + 4) = *reinterpret_cast<const float4*>(kinv + j0 + c8 * 8 + 4);
+                        *reinterpret_cast<float4*>(cv) = *reinterpret_cast<const float4*>(cum2 + j0 + c8 * 8);
+                        *reinterpret_cast<float4*>(cv + 4) = *reinterpret_cast<const float4*>(cum2 + j0 + c8 * 8 + 4);
 #pragma unroll
                         for (int e = 0; e < 8; e++) {
                             const int j = j0 + c8 * 8 + e;
-                            f[e] = (live && j <= t) ? (d[c8 * 8 + e] * st_) * kinv[j] * ex2(ct - cum2[j]) : 0.f;
+                            f[e] = (live && j <= t) ? (d[c8 * 8 + e] * st_) * kv[e] * ex2(ct - cv[e]) : 0.f;
                         }
                         *reinterpret_cast<Pack8*>(pt_tile + sw128_offset(t, (j0 >> 3) + c8)) = pack8(f);
                     }
@@ -674,8 +690,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(bar(B_OPS2_READY));
-                    mbar_arrive(bar(B_IN_KQ_FREE + slot));  // MMA1 is done and kw is formed
+                    mbar_arrive(bar(B_OPS2_READY + slot));
+                    mbar_arrive(bar(B_IN_KQ_FREE + slot));  // MMA1 is done and the norms pass read k, q
                 }
             }
             named_bar_sync(BAR_PREP, NPREP);  // A complete
@@ -701,7 +717,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int r = 0; r < 32; r++) {
                     const float tv = r < col ? 0.f : x[r];
-                    Tm[(o32 + r) * LDT + o32 + col] = tv;
+                    Tm[(b * 32 + r) * LDD + col] = tv;
                     const int t = o32 + r, j = o32 + col;
                     tcol[(sw128_offset(t, j >> 3) >> 1) + (j & 7)] = to_bf16(tv * bj);
                 }
@@ -716,28 +732,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int r = pt >> 3, c4 = (pt & 7) * 4;
                 const float* arow = A + (32 + r) * LDT;
                 float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 8
-                for (int m = 0; m < 32; m++) {
-                    const float av = arow[m];
-                    const float4 tv = *reinterpret_cast<const float4*>(Tm + m * LDT + c4);
-                    a0 = fmaf(av, tv.x, a0);
-                    a1 = fmaf(av, tv.y, a1);
-                    a2 = fmaf(av, tv.z, a2);
-                    a3 = fmaf(av, tv.w, a3);
+#pragma unroll 2
+                for (int m4 = 0; m4 < 32; m4 += 4) {
+                    const float4 av4 = *reinterpret_cast<const float4*>(arow + m4);
+                    const float av[4] = {av4.x, av4.y, av4.z, av4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float4 tv = *reinterpret_cast<const float4*>(Tm + (m4 + e) * LDD + c4);
+                        a0 = fmaf(av[e], tv.x, a0);
+                        a1 = fmaf(av[e], tv.y, a1);
+                        a2 = fmaf(av[e], tv.z, a2);
+                        a3 = fmaf(av[e], tv.w, a3);
+                    }
                 }
                 *reinterpret_cast<float4*>(X + r * 32 + c4) = make_float4(a0, a1, a2, a3);
                 named_bar_sync(BAR_PREP, NPREP);
-                const float* trow = Tm + (32 + r) * LDT + 32;
+                const float* trow = Tm + (32 + r) * LDD;
                 a0 = a1 = a2 = a3 = 0.f;
-#pragma unroll 8
-                for (int m = 0; m < 32; m++) {
-                    if (m <= r) {
-                        const float tv = trow[m];
-                        const float4 xv = *reinterpret_cast<const float4*>(X + m * 32 + c4);
-                        a0 = fmaf(tv, xv.x, a0);
-                        a1 = fmaf(tv, xv.y, a1);
-                        a2 = fmaf(tv, xv.z, a2);
-                        a3 = fmaf(tv, xv.w, a3);
+                for (int m4 = 0; m4 <= r; m4 += 4) {  // T_11 is lower triangular: rows r >= m
+                    const float4 tv4 = *reinterpret_cast<const float4*>(trow + m4);
+                    const float tv[4] = {tv4.x, tv4.y, tv4.z, tv4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float4 xv = *reinterpret_cast<const float4*>(X + (m4 + e) * 32 + c4);
+                        const float t_ = m4 + e <= r ? tv[e] : 0.f;
+                        a0 = fmaf(t_, xv.x, a0);
+                        a1 = fmaf(t_, xv.y, a1);
+                        a2 = fmaf(t_, xv.z, a2);
+                        a3 = fmaf(t_, xv.w, a3);
                     }
                 }
                 if (ok) {
@@ -752,10 +774,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_before();  // the D1 loads are complete before MMA2 rewrites those columns
             __syncwarp();
             if (ok && lane == 0) mbar_arrive(bar(B_TB_READY));
-            // w^T from TMEM (lane = k) into the MN-major [128 k][64 t] operand tile, once the
-            // previous chunk's first scan MMAs have read it
+            // w^T from TMEM (lane = k) into this chunk's MN-major [128 k][64 t] operand tile, once
+            // the first scan MMAs of chunk c - 2 have read it
             ok = ok && __all_sync(0xffffffffu, mbar_wait(bar(B_MMA2_DONE), (uint32_t)c & 1u) &&
-                                                   mbar_wait(bar(B_OPS_W_FREE), (uint32_t)(c + 1) & 1u));
+                                                   mbar_wait(bar(B_W_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u));
             if (ok) {
                 tc_fence_after();
                 const int t0w = (pw >> 2) * 32, kr = wq * 32 + lane;
@@ -764,12 +786,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_ld_wait();
 #pragma unroll
                 for (int c4 = 0; c4 < 4; c4++)
-                    *reinterpret_cast<Pack8*>(sm + OFF_W + sw128_offset(kr, (t0w >> 3) + c4)) = pack8(x + 8 * c4);
+                    *reinterpret_cast<Pack8*>(sm + OFF_W + slot * 2 * BOX + sw128_offset(kr, (t0w >> 3) + c4)) =
+                        pack8(x + 8 * c4);
                 fence_async_smem();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(bar(B_OPS_READY));
+                    mbar_arrive(bar(B_OPS_READY + slot));
                     mbar_arrive(bar(B_D1W_FREE));
                     mbar_arrive(bar(B_VEC_FREE + slot));
                 }
