@@ -22,7 +22,9 @@ own Qwen3.5 decoder layers (the reference's CPU parity anchor, FLA and causal-co
 float32) on one 771-token prompt (the median of the concurrency-1 workload) through one
 4-layer period of the 27B shape, extrapolated x16 to 64 layers; every host thread is used.
 `--ref-cuda` times the reference's own CUDA library (built from its sources by
-oracle/Makefile) through the same C++ host on the same GPU instead, and prints its own line.
+oracle/Makefile) through the same C++ host on the same GPU instead, and prints its own line
+with `gdn_same_box`: the complete GDN prefill call of both libraries at the reference's own
+GDN benchmark points (`--gdn-only` prints that table alone).
 """
 import argparse
 import json
@@ -242,6 +244,64 @@ def run_reference(args, rank, world):
     }), flush=True)
 
 
+def gdn_same_box(torch, stream, ref_path, points=(107, 936, 3399), H=48, HK=16, calls=100, seed=20261003):
+    """The complete GDN prefill call (`cs1_gdn_prefill`, batch 1, 16 q/k heads, 48 value
+    heads, head dim 128) through this build's library and the reference's (oracle/_ref) on
+    the same GPU, same stream, same device inputs and workspace size, at the token counts
+    of the reference's own GDN benchmark (benchmarks/gdn/README.md:56-61): per point and
+    arm one excluded feasibility call, ten excluded warm-ups, then two passes of `calls`
+    calls (the second pass in reversed arm order), wall time per call with eager
+    submission included and the CUDA event span beside it. Inputs: q ~ N(0,1), k = 0.6 q
+    + 0.8 N(0,1) (correlated q/k), v ~ N(0,1), beta ~ U(0,1), weak decay g ~ -U(0, 0.05),
+    seeded; synthetic, as the reference's are."""
+    import ctypes
+    from s1omni import Cs1
+    libs = {"ours": Cs1(), "reference": Cs1(ref_path)}
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    rows = []
+    for T in points:
+        q32 = torch.randn(T, HK, 128, device="cuda", generator=gen)
+        k = (0.6 * q32 + 0.8 * torch.randn(T, HK, 128, device="cuda", generator=gen)).to(torch.bfloat16)
+        q = q32.to(torch.bfloat16)
+        v = torch.randn(T, H, 128, device="cuda", generator=gen).to(torch.bfloat16)
+        g = -torch.rand(T, H, device="cuda", generator=gen) * 0.05
+        beta = torch.rand(T, H, device="cuda", generator=gen).to(torch.bfloat16)
+        nws = max(lib.cs1_gdn_workspace_floats(T, H) for lib in libs.values())
+        ws = torch.empty(nws, dtype=torch.float32, device="cuda")
+        outs = {a: torch.empty(T, H, 128, device="cuda", dtype=torch.bfloat16) for a in libs}
+
+        def call(a):
+            return libs[a].raw.cs1_gdn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(),
+                                               beta.data_ptr(), outs[a].data_ptr(), ws.data_ptr(), T, H, HK,
+                                               ctypes.c_float(128 ** -0.5), stream)
+        wall = {a: [] for a in libs}
+        event = {a: [] for a in libs}
+        for a in libs:
+            assert call(a) == 0
+            for _ in range(10):
+                call(a)
+        torch.cuda.synchronize()
+        for order in (("reference", "ours"), ("ours", "reference")):
+            for a in order:
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                t0 = time.perf_counter()
+                s.record(torch.cuda.current_stream())
+                for _ in range(calls):
+                    call(a)
+                e.record(torch.cuda.current_stream())
+                torch.cuda.synchronize()
+                wall[a].append((time.perf_counter() - t0) * 1e3 / calls)
+                event[a].append(s.elapsed_time(e) / calls)
+        o_ours, o_ref = outs["ours"].float(), outs["reference"].float()
+        rows.append({"tokens": T, "ms_wall": {a: [round(x, 6) for x in wall[a]] for a in libs},
+                     "ms_event": {a: [round(x, 6) for x in event[a]] for a in libs},
+                     "speedup_wall": round(min(wall["reference"]) / min(wall["ours"]), 3),
+                     "max_diff_rel": float((o_ours - o_ref).abs().max() / o_ref.abs().max())})
+    return {"heads": [HK, H], "calls_per_pass": calls, "points": rows,
+            "published_h200_ms": {"107": 0.050957, "936": 0.214178, "3399": 0.697262}}
+
+
 def run_reference_cuda(args, rank, world, local):
     """The reference's own CUDA library (built from its sources by oracle/Makefile into
     oracle/_ref/, recompiled for sm_100a: cuBLASLt GEMMs, mma.sync attention and GDN)
@@ -257,6 +317,10 @@ def run_reference_cuda(args, rank, world, local):
     import torch
     from s1omni import Model, lib_path, pack_ranges, preset
     torch.cuda.set_device(local)
+    gdn = gdn_same_box(torch, torch.cuda.current_stream().cuda_stream, ref)
+    if args.gdn_only:
+        print(json.dumps({"impl": "reference-cuda-same-gpu", "gdn_same_box": gdn}), flush=True)
+        return
     cfg = preset("27b")
     seqs = requests(0)
     tokens = int(sum(len(s) for s in seqs))
@@ -297,7 +361,7 @@ def run_reference_cuda(args, rank, world, local):
         "library": "reference src/backends/cuda/qwen3_5 built for sm_100a (oracle/Makefile)",
         "host": "this build's C++ host, eager, host-side scorer head (the reference's executor path)",
         "timing": "wall clock around synchronous forward calls (host copies included)",
-        "logits_sample": logits[:4].round(4).tolist()}), flush=True)
+        "logits_sample": logits[:4].round(4).tolist(), "gdn_same_box": gdn}), flush=True)
 
 
 # ------------------------------------------------------------------ GPU arm ----
@@ -692,6 +756,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-cuda", action="store_true",
                     help="time the reference's own CUDA library (oracle/_ref) through the same host, same GPU")
+    ap.add_argument("--gdn-only", action="store_true",
+                    help="with --ref-cuda: only the same-GPU GDN operator table against the reference library")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-long", action="store_true", help="skip workload (b), the 32,768-token prefill")
     ap.add_argument("--no-c3", action="store_true", help="skip configuration C3 (9B, 256 requests x 4 candidates)")
