@@ -649,8 +649,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_ld32(lrow + TM_D1 + (uint32_t)j0, d);
                 tmem_ld_wait();
                 if (row < C) {
+                    // the off-diagonal block A_10 row-major at A[i][j]; the diagonal blocks
+                    // transposed in place, A_bb[i][j] at A[j][i] (conflict-free: lane = i)
                     const int i = row;
-                    float* arow = A + i * LDT + j0;
+                    const bool diag = (i >> 5) == (j0 >> 5);
                     if (live) {
                         const float ci = cum2[i], si = bet[i] * kinv[i];
 #pragma unroll
@@ -664,7 +666,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 const int j = j0 + j4 * 4 + e;
                                 f[e] = j < i ? si * (d[j4 * 4 + e] * kv[e]) * ex2(ci - cv[e]) : 0.f;
                             }
-                            *reinterpret_cast<float4*>(arow + j4 * 4) = make_float4(f[0], f[1], f[2], f[3]);
+                            if (diag) {
+#pragma unroll
+                                for (int e = 0; e < 4; e++) A[(j0 + j4 * 4 + e) * LDT + i] = f[e];
+                            } else {
+                                *reinterpret_cast<float4*>(A + i * LDT + j0 + j4 * 4) = make_float4(f[0], f[1], f[2], f[3]);
+                            }
                         }
                     }
                 } else {
@@ -699,10 +706,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             // as tb = bf16(T diag(beta)) (K-major [64 t][64 j]) as the entries become final.
             // Diagonal blocks: one thread per (block, column), right-looking substitution (each
             // solved entry updates the later rows at once: a chain 32 steps deep, the terms of
-            // every entry added in the order of the plain forward substitution).
+            // every entry added in the order of the plain forward substitution); column m of
+            // a diagonal block is a row of its transposed copy, read 4 entries at a time.
             uint8_t* tb = sm + OFF_TB;
             if (ok && pt < C) {
                 const int b = pt >> 5, col = pt & 31, o32 = b * 32;
+                const float* at = A + o32 * LDT + o32;  // A[o32 + r][o32 + m] at at[m * LDT + r]
                 float x[32];
 #pragma unroll
                 for (int r = 0; r < 32; r++) x[r] = r == col ? 1.f : 0.f;
@@ -710,7 +719,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int m = 0; m < 31; m++) {
                     const float xm = x[m];
 #pragma unroll
-                    for (int r = m + 1; r < 32; r++) x[r] = fmaf(-A[(o32 + r) * LDT + o32 + m], xm, x[r]);
+                    for (int r4 = (m + 1) & ~3; r4 < 32; r4 += 4) {
+                        const float4 a4 = *reinterpret_cast<const float4*>(at + m * LDT + r4);
+                        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++)
+                            if (r4 + e > m) x[r4 + e] = fmaf(-av[e], xm, x[r4 + e]);
+                    }
                 }
                 const float bj = bet[o32 + col];
                 bf16* tcol = reinterpret_cast<bf16*>(tb);
