@@ -9,8 +9,8 @@ library has it, else one `cs1_gdn_prefill` per sequence (the reference library: 
 entry point takes at most 16 sequences). Inputs q, k, v ~ N(0,1), g ~ -U(0, 0.25),
 beta ~ U(0,1), seeded. Times `reps` calls with CUDA events on the calling stream after
 three warm-up calls and prints one JSON line with the fraction of the HBM bound (q, k,
-v, o, g and beta bytes once, against the measured copy bandwidth). `--once` makes exactly
-one call (for a profiler capture).
+v, o, g and beta bytes once, against the measured copy bandwidth of MEASURED_PEAKS.json).
+`--once` makes exactly one call (for a profiler capture).
 """
 import argparse
 import ctypes
@@ -22,7 +22,16 @@ import torch
 
 from .cs1 import Cs1
 
-HBM_GBS = 6453.7  # measured copy bandwidth of this pool's B200s
+
+def hbm_gbs():
+    """The measured copy bandwidth (MEASURED_PEAKS.json at the repository root), else the
+    pool's earlier measurement."""
+    try:
+        root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        with open(os.path.join(root, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0
 
 
 def algorithmic_bytes(T, H, HK, d=128):
@@ -96,7 +105,7 @@ def main():
     ms = s.elapsed_time(e) / a.reps
     byt = algorithmic_bytes(T, H, HK)
     print(json.dumps({"lengths": lengths if len(lengths) <= 8 else f"{len(lengths)} sequences, {T} tokens",
-                      "h": H, "hk": HK, "ms": ms, "gbs": byt / ms / 1e6, "frac_hbm": byt / ms / 1e6 / HBM_GBS,
+                      "h": H, "hk": HK, "ms": ms, "gbs": byt / ms / 1e6, "frac_hbm": byt / ms / 1e6 / hbm_gbs(),
                       "finite": bool(torch.isfinite(out.float()).all()), "lib": lib.path}))
 
 
