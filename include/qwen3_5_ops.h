@@ -191,6 +191,51 @@ int cs1_head_score(const void* hidden, int ldh, const int32_t* rows, int n, cons
 // by (seed, index): kind 0 a + b*N(0,1), 1 U(a,b), 2 log U(a,b). For benchmark weights.
 int cs1_fill_random(void* dst, size_t n, int kind, uint64_t seed, float a, float b, int dtype, void* stream);
 
+// ---- capacity path (additive) ----
+// Device-side batching: the `*_dyn` entry points size their launches for capacities
+// (cap_rows packed rows, cap_seqs sequences) and take the batch itself from a descriptor
+// in device memory (`desc`: cs1_batch_desc_bytes() bytes, 16-byte aligned, filled on the
+// host by cs1_batch_desc_pack and copied to the device before the launches run). A CUDA
+// graph captured once per capacity therefore serves every batch that fits it, where the
+// reference captures one graph per length vector (model.rs:1583-1614) and groups requests
+// on the host (open_jev executor/batched.rs:28-31). Rows past the descriptor's count
+// inside the capacity are scratch: they may be read and written, their values are
+// unspecified. Each result equals its host-length entry point's bit for bit.
+size_t cs1_batch_desc_bytes(void);
+// lengths: host array of `count` (1..256) nonzero sequence lengths.
+int cs1_batch_desc_pack(const size_t* lengths, size_t count, void* out, size_t bytes);
+int cs1_embed_dyn(const int32_t* ids, const void* table, void* out, int cap_rows, int D, const void* desc,
+                  void* stream);
+int cs1_rms_norm_dyn(const void* x, const void* w, void* out, int cap_rows, int D, float eps, const void* desc,
+                     void* stream);
+int cs1_add_rms_norm_dyn(void* residual, const void* delta, const void* w, void* out, int cap_rows, int D,
+                         float eps, const void* desc, void* stream);
+int cs1_gated_rms_norm_dyn(const void* x, const void* z, int ldz, const void* w, void* out, int cap_rows, int H,
+                           int D, float eps, const void* desc, void* stream);
+// epilogue: 0 store (cs1_gemm), 1 residual (cs1_gemm_residual), 2 SwiGLU (cs1_gemm_swiglu,
+// N = 2I interleaved rows).
+int cs1_gemm_dyn(void* gemm, const void* x, const void* w, void* y, int cap_rows, int N, int K, int ldy,
+                 int epilogue, const void* desc, void* stream);
+int cs1_gdn_conv_dyn(const void* qkv, const void* history, int ld, const void* w, void* q, void* k, void* v,
+                     int cap_rows, int cap_seqs, int key_dim, int value_dim, const void* desc, void* stream);
+int cs1_gdn_gates_dyn(const void* b, const void* a, int ld, const void* A_log, const void* dt_bias, void* beta,
+                      float* g, int cap_rows, int H, const void* desc, void* stream);
+// state_in / state_out as cs1_gdn_prefill_batch_x; no workspace.
+int cs1_gdn_prefill_dyn(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                        int cap_rows, int cap_seqs, int H, int HK, float scale, const void* state_in,
+                        int state_stride, void* state_out, const void* desc, void* stream);
+int cs1_attn_prep_dyn(const void* qg, const void* kr, int ld, const void* qw, const void* kw, const void* cos,
+                      const void* sin, void* q, void* gate, void* k, int cap_rows, int Hq, int Hk, int Dh, int half,
+                      float eps, const void* desc, void* stream);
+// prefix 0: cs1_attention_gated_batch; prefix > 0: cs1_attention_gated_shared_batch.
+int cs1_attention_dyn(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
+                      const void* prefix_k, const void* prefix_v, int prefix, int cap_rows, int cap_seqs, int Hq,
+                      int Hk, int Dh, float scale, const void* desc, void* stream);
+// The first (descriptor's sequence count) of cap_n candidates are scored; rows: device
+// int32 [cap_n] rows of `hidden`, or null for each sequence's final row.
+int cs1_head_score_dyn(const void* hidden, int ldh, const int32_t* rows, int cap_n, const float* W,
+                       const float* bias, int L, int D, float* logits, const void* desc, void* stream);
+
 // ---- vision (ops.h:231-236): required by the reference loader; this library does
 // not implement the vision path and returns cudaErrorNotSupported ----
 int cs1_vision_linear(void* gemm, const void* x, const void* w, const void* bias, void* y, int M, int N, int K,

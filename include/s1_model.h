@@ -12,6 +12,9 @@
 //                                                shared_prefix_with_original_rows (model.rs:1634-1907)
 //   s1_model_set_graphs                          the CUDA-graph cache keyed by the length vector
 //                                                (model.rs:1583-1614, 1959)
+//   s1_model_set_dynamic                         device-side batching: graphs keyed by capacity
+//                                                (replaces the host grouping of open_jev
+//                                                executor/batched.rs:28-31)
 // The model binds a cs1_* library by path at run time (dlopen, ABI version 9 check,
 // required + optional symbols), as the reference's loader does (cuda.rs:673-698), so
 // the same host drives this build's library or any other ABI-9 library.
@@ -98,6 +101,16 @@ int s1_model_run_layers(void* model, const int32_t* ids, const size_t* lengths, 
 
 // CUDA graphs for repeated length vectors (default off): 0 = eager, 1 = capture/replay.
 int s1_model_set_graphs(void* model, int enabled);
+// Device-side batching (default off; needs the library's cs1_*_dyn entry points): every
+// forward other than a prefix-capture pass and a context-parallel piece sizes its launches
+// for capacities (rows rounded up to a power of two >= 64, sequences to a power of two)
+// and reads the batch from a descriptor in device memory uploaded with the ids, so with
+// graphs on one captured graph per (capacities, shared prefix) serves every length vector
+// that fits, instead of one per length vector (the reference's cache, model.rs:1583-1614).
+// Logits and hidden rows are the same bits either way.
+int s1_model_set_dynamic(void* model, int enabled);
+// Graphs held in the model's cache.
+int s1_model_graph_count(void* model);
 // The model's cudaStream_t (for timing with events on the launching stream).
 void* s1_model_stream(void* model);
 // Kernel launches the last forward issued through the cs1 library (eager count).

@@ -35,9 +35,10 @@ __global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restric
                                  const bf16* __restrict__ qw, const bf16* __restrict__ kw,
                                  const bf16* __restrict__ cosb, const bf16* __restrict__ sinb, bf16* __restrict__ q,
                                  bf16* __restrict__ gate, bf16* __restrict__ k, int T, int Hq, int Hk, int half,
-                                 float eps) {
+                                 float eps, const DevBatch* dyn) {
     grid_dep_wait();
     grid_dep_launch();
+    T = dyn_rows(dyn, T);
     const int unit0 = (blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * PREP_UNITS;
     const int lane = threadIdx.x & 31;
     const int heads = Hq + Hk;
@@ -196,9 +197,13 @@ __device__ __forceinline__ int query_blocks(const SeqTable& tab, int i, int q_ba
 // P is double-buffered with S: the softmax of tile j + 1 does not wait for PV_j (only a
 // rescale of O does), and S_{j+2} is issued into a buffer once PV_j, its last reader, is
 // complete.
+// Dyn: the capacity path. The table is the descriptor's in device memory and the grid is
+// sized for the capacity; CTAs past the batch's query blocks return at once.
+template <bool Dyn>
 __global__ void __launch_bounds__(THREADS, 1)
-    flash_tc(const __grid_constant__ Maps maps, Args a, SeqTable tab) {
+    flash_tc(const __grid_constant__ Maps maps, Args a, const __grid_constant__ SeqTable tab_arg, const DevBatch* dyn) {
     using namespace tc;
+    const SeqTable& tab = Dyn ? dyn->tab : tab_arg;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -219,6 +224,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // blockIdx.y -> (sequence, query block): sequences in the table's order (longest
         // first), the blocks of one sequence last-first (the most key tiles first)
         const int target = blockIdx.y;
+        if (Dyn && lane == 0) info[0] = -1;
+        __syncwarp();
         int cnt[8], local = 0;
 #pragma unroll
         for (int e = 0; e < 8; e++) {
@@ -243,6 +250,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 first += cnt[e];
             }
         }
+    }
+    if constexpr (Dyn) {
+        __syncthreads();
+        if (info[0] < 0) return;  // past the batch: nothing allocated or armed yet
     }
     if (threadIdx.x == 32) {
         mbar_init(q_full, 1);
@@ -568,10 +579,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
+int launch_tc(const Args& a, const SeqTable& tab, int blocks, const DevBatch* dyn, cudaStream_t st) {
     static const cudaError_t configured =
-        cudaFuncSetAttribute(flash_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        cudaFuncSetAttribute(flash_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (configured != cudaSuccess) return configured;
+    static const cudaError_t configured_dyn =
+        cudaFuncSetAttribute(flash_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (configured_dyn != cudaSuccess) return configured_dyn;
     const int rows = tab.offset[tab.count];
     Maps maps;
     memset(&maps, 0, sizeof(maps));
@@ -581,13 +595,16 @@ int launch_tc(const Args& a, const SeqTable& tab, int blocks, cudaStream_t st) {
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pk, a.pk, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (!e && a.P > 0) e = host::make_map_3d_bf16(&maps.pv, a.pv, DH, a.Hk, a.P, DH, (uint64_t)a.Hk * DH, 64, 64);
     if (e) return e;
-    return launch_pdl(flash_tc, dim3(a.Hq, blocks), dim3(THREADS), SMEM, st,
-                      maps, a, tab);
+    return launch_pdl(dyn ? flash_tc<true> : flash_tc<false>, dim3(a.Hq, blocks), dim3(THREADS), SMEM, st, maps, a,
+                      tab, dyn);
 }
 
 }  // namespace tca
 
-int launch(Args a, const SeqTable& tab, cudaStream_t st) {
+// `tab` holds the batch, or, on the capacity path (dyn non-null), one sequence of
+// cap_rows rows standing for the capacity, with `cap_seqs` sequences at most: the grid
+// then covers every batch that fits (sum of ceil(L_i / BM) <= cap_rows / BM + cap_seqs).
+int launch(Args a, const SeqTable& tab, cudaStream_t st, const DevBatch* dyn = nullptr, int cap_seqs = 0) {
     if (a.Hq <= 0 || a.Hk <= 0 || a.Hq % a.Hk || a.ldv % 8 || a.ldv < a.Hk * DH) return cudaErrorInvalidValue;
     int max_rows = 0, blocks = 0;
     for (int i = 0; i < tab.count; i++) {
@@ -596,13 +613,17 @@ int launch(Args a, const SeqTable& tab, cudaStream_t st) {
         if (rows > 0) blocks += (rows + tca::BM - 1) / tca::BM;
     }
     if (max_rows <= 0) return cudaSuccess;
+    if (dyn) {
+        if (a.q_base != 0 || cap_seqs <= 0 || cap_seqs > MAX_SEQS) return cudaErrorInvalidValue;
+        blocks = tab.offset[tab.count] / tca::BM + cap_seqs;
+    }
     // TMA tiles: every operand starts on a 16-byte boundary and the shared prefix is whole
     // 64-key tiles (the reference's own shared-prefix entry point asks the same of it)
     const bool aligned = aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.out) &&
                          (!a.gated || aligned16(a.gate)) &&
                          (a.P == 0 || (a.P % 64 == 0 && aligned16(a.pk) && aligned16(a.pv)));
     if (!aligned) return cudaErrorInvalidValue;
-    return tca::launch_tc(a, tab, blocks, st);
+    return tca::launch_tc(a, tab, blocks, dyn, st);
 }
 
 Args make_args(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out, int Hq, int Hk,
@@ -663,7 +684,28 @@ int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const 
                       static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg), static_cast<const bf16*>(kr),
                       ld, static_cast<const bf16*>(qw), static_cast<const bf16*>(kw), static_cast<const bf16*>(cos),
                       static_cast<const bf16*>(sin), static_cast<bf16*>(q), static_cast<bf16*>(gate),
-                      static_cast<bf16*>(k), T, Hq, Hk, half, eps);
+                      static_cast<bf16*>(k), T, Hq, Hk, half, eps, static_cast<const DevBatch*>(nullptr));
+}
+
+int cs1_attn_prep_dyn(const void* qg, const void* kr, int ld, const void* qw, const void* kw, const void* cos,
+                      const void* sin, void* q, void* gate, void* k, int cap_rows, int Hq, int Hk, int Dh, int half,
+                      float eps, const void* desc, void* stream) {
+    if (!desc || ld % 8 != 0 || cap_rows < 0 || Hq < 1 || Hk < 1) return cudaErrorInvalidValue;
+    if (Dh != attn::DH || half <= 0 || half % 8 != 0 || 2 * half > Dh || ((half / 8) & (half / 8 - 1)))
+        return cudaErrorInvalidValue;
+    const long units = (long)cap_rows * (Hq + Hk);
+    if (units == 0) return cudaSuccess;
+    if (units > INT_MAX - 64) return cudaErrorInvalidValue;
+    const long warps = (units + attn::PREP_UNITS - 1) / attn::PREP_UNITS;
+    if (!aligned16(qg) || !aligned16(kr) || !aligned16(qw) || !aligned16(kw) || !aligned16(q) || !aligned16(gate) ||
+        !aligned16(k) || !aligned16(cos) || !aligned16(sin))
+        return cudaErrorInvalidValue;
+    constexpr int WPB = 8;
+    return launch_pdl(attn::prep_fast_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
+                      static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg), static_cast<const bf16*>(kr),
+                      ld, static_cast<const bf16*>(qw), static_cast<const bf16*>(kw), static_cast<const bf16*>(cos),
+                      static_cast<const bf16*>(sin), static_cast<bf16*>(q), static_cast<bf16*>(gate),
+                      static_cast<bf16*>(k), cap_rows, Hq, Hk, half, eps, static_cast<const DevBatch*>(desc));
 }
 
 int cs1_attention(const void* q, const void* k, const void* v, int ldv, void* out, int T, int Hq, int Hk, int Dh,
@@ -729,6 +771,23 @@ int cs1_attention_gated_batch(const void* q, const void* k, const void* v, int l
                               void* stream) {
     return cs1_attention_gated_shared_batch(q, k, v, ldv, gate, out, nullptr, nullptr, lengths, count, 0, Hq, Hk,
                                             Dh, scale, stream);
+}
+
+int cs1_attention_dyn(const void* q, const void* k, const void* v, int ldv, const void* gate, void* out,
+                      const void* prefix_k, const void* prefix_v, int prefix, int cap_rows, int cap_seqs, int Hq,
+                      int Hk, int Dh, float scale, const void* desc, void* stream) {
+    if (!desc || !q || !k || !v || !gate || !out || Dh != attn::DH || prefix < 0 || cap_rows <= 0)
+        return cudaErrorInvalidValue;
+    if (prefix > 0 && (!prefix_k || !prefix_v)) return cudaErrorInvalidValue;
+    SeqTable cap;  // launch geometry and tensor-map extents only
+    memset(&cap, 0, sizeof(cap));
+    cap.count = 1;
+    cap.offset[1] = cap_rows;
+    attn::Args a = attn::make_args(q, k, v, ldv, gate, out, Hq, Hk, scale, true);
+    a.pk = static_cast<const bf16*>(prefix_k);
+    a.pv = static_cast<const bf16*>(prefix_v);
+    a.P = prefix;
+    return attn::launch(a, cap, static_cast<cudaStream_t>(stream), static_cast<const DevBatch*>(desc), cap_seqs);
 }
 
 }  // extern "C"

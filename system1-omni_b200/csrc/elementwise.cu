@@ -42,9 +42,10 @@ namespace {
 constexpr int THREADS = 256;
 
 __global__ void embed_kernel(const int32_t* __restrict__ ids, const Pack8* __restrict__ table,
-                             Pack8* __restrict__ out, int packs, int T) {
+                             Pack8* __restrict__ out, int packs, int T, const DevBatch* dyn) {
     grid_dep_wait();
     grid_dep_launch();
+    T = dyn_rows(dyn, T);
     for (int t = blockIdx.x; t < T; t += gridDim.x) {
         const size_t id = (size_t)ids[t];
         for (int i = threadIdx.x; i < packs; i += blockDim.x) out[(size_t)t * packs + i] = table[id * packs + i];
@@ -64,11 +65,13 @@ struct alignas(4 * NP) PackN {
     __nv_bfloat162 h[NP];
 };
 
-template <int NP>
+template <int NP, bool Dyn>
 __global__ void __launch_bounds__(128, NP == 2 ? 8 : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
-                                bf16* __restrict__ v, int key_packs, int value_packs, int run, SeqTable tab) {
+                                bf16* __restrict__ v, int key_packs, int value_packs, int run,
+                                const __grid_constant__ SeqTable tab_arg, const DevBatch* dyn) {
     using P = PackN<NP>;
+    const SeqTable& tab = Dyn ? dyn->tab : tab_arg;  // the capacity path's table is in device memory
     constexpr int CH = 2 * NP;  // channels per thread
     grid_dep_wait();
     grid_dep_launch();
@@ -197,9 +200,10 @@ __global__ void conv_scalar_kernel(const bf16* __restrict__ qkv, const bf16* __r
 
 __global__ void gates_kernel(const bf16* __restrict__ b, const bf16* __restrict__ a, int ld,
                              const bf16* __restrict__ A_log, const bf16* __restrict__ dt_bias,
-                             bf16* __restrict__ beta, float* __restrict__ g, long n, int H) {
+                             bf16* __restrict__ beta, float* __restrict__ g, long n, int H, const DevBatch* dyn) {
     grid_dep_wait();
     grid_dep_launch();
+    if (dyn) n = min(n, (long)dyn->rows * H);
     for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
         const int h = (int)(i % H);
         const size_t src = (size_t)(i / H) * ld + h;
@@ -264,8 +268,10 @@ unsigned grid_for(size_t n) {
     return (unsigned)(b < 148 * 32 ? (b ? b : 1) : 148 * 32);
 }
 
+// `tab` holds the batch, or, on the capacity path (dyn non-null), only its capacity
+// (offset[count] = cap_rows) while the kernels read the batch from the descriptor.
 int conv_launch(const void* qkv, const void* history, int ld, const void* w, void* q, void* k, void* v,
-                const SeqTable& tab, int key_dim, int value_dim, cudaStream_t st) {
+                const SeqTable& tab, int key_dim, int value_dim, const DevBatch* dyn, cudaStream_t st) {
     const int T = tab.offset[tab.count];
     const int rows = T < 65535 ? T : 65535;
     const bool vec = key_dim % 8 == 0 && value_dim % 8 == 0 && ld % 8 == 0 && aligned16(qkv) && aligned16(w) &&
@@ -284,12 +290,15 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
         while (run > 16 && groups * ((T + run - 1) / run) < waves2 && (T + run / 2 - 1) / (run / 2) <= 65535)
             run /= 2;
         if ((T + run - 1) / run > 65535) return cudaErrorInvalidValue;
-        return launch_pdl(narrow ? conv_vec_kernel<2> : conv_vec_kernel<4>,
+        auto kernel = dyn ? (narrow ? conv_vec_kernel<2, true> : conv_vec_kernel<4, true>)
+                          : (narrow ? conv_vec_kernel<2, false> : conv_vec_kernel<4, false>);
+        return launch_pdl(kernel,
                           dim3((unsigned)groups, (T + run - 1) / run), dim3(128), 0, st,
                           static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
                           static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
-                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, run, tab);
+                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, run, tab, dyn);
     } else {
+        if (dyn) return cudaErrorInvalidValue;  // the capacity path needs the vector kernel
         const int ch = 2 * key_dim + value_dim;
         conv_scalar_kernel<<<dim3((ch + 127) / 128, rows), 128, 0, st>>>(
             static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld, static_cast<const bf16*>(w),
@@ -309,7 +318,8 @@ extern "C" int cs1_embed(const int32_t* ids, const void* table, void* out, int T
     if (!aligned16(table) || !aligned16(out)) return cudaErrorInvalidValue;
     const int grid = T < 65535 ? T : 65535;
     return launch_pdl(embed_kernel, dim3(grid), dim3(128), 0, static_cast<cudaStream_t>(stream), ids,
-                      static_cast<const Pack8*>(table), static_cast<Pack8*>(out), D / 8, T);
+                      static_cast<const Pack8*>(table), static_cast<Pack8*>(out), D / 8, T,
+                      static_cast<const DevBatch*>(nullptr));
 }
 
 extern "C" int cs1_gdn_conv(const void* qkv, int ld, const void* w, void* q, void* k, void* v, int T, int key_dim,
@@ -319,7 +329,8 @@ extern "C" int cs1_gdn_conv(const void* qkv, int ld, const void* w, void* q, voi
     SeqTable tab;
     const size_t len = (size_t)T;
     make_table(tab, &len, 1);
-    return conv_launch(qkv, nullptr, ld, w, q, k, v, tab, key_dim, value_dim, static_cast<cudaStream_t>(stream));
+    return conv_launch(qkv, nullptr, ld, w, q, k, v, tab, key_dim, value_dim, nullptr,
+                       static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cs1_gdn_conv_vector(const void* qkv, int ld, const void* w, void* q, void* k, void* v, int T,
@@ -335,7 +346,8 @@ extern "C" int cs1_gdn_conv_prefix(const void* qkv, const void* history, int ld,
     SeqTable tab;
     const size_t len = (size_t)T;
     make_table(tab, &len, 1);
-    return conv_launch(qkv, history, ld, w, q, k, v, tab, key_dim, value_dim, static_cast<cudaStream_t>(stream));
+    return conv_launch(qkv, history, ld, w, q, k, v, tab, key_dim, value_dim, nullptr,
+                       static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cs1_gdn_conv_batch(const void* qkv, const void* history, int ld, const void* w, void* q, void* k,
@@ -345,7 +357,8 @@ extern "C" int cs1_gdn_conv_batch(const void* qkv, const void* history, int ld, 
     if (!qkv || !w || !q || !k || !v || key_dim <= 0 || value_dim <= 0 || ld < 2 * key_dim + value_dim ||
         !make_table(tab, lengths, count))
         return cudaErrorInvalidValue;
-    return conv_launch(qkv, history, ld, w, q, k, v, tab, key_dim, value_dim, static_cast<cudaStream_t>(stream));
+    return conv_launch(qkv, history, ld, w, q, k, v, tab, key_dim, value_dim, nullptr,
+                       static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int cs1_gdn_gates(const void* b, const void* a, int ld, const void* A_log, const void* dt_bias,
@@ -355,7 +368,58 @@ extern "C" int cs1_gdn_gates(const void* b, const void* a, int ld, const void* A
     if (n == 0) return cudaSuccess;
     return launch_pdl(gates_kernel, dim3(grid_for(n)), dim3(THREADS), 0, static_cast<cudaStream_t>(stream),
                       static_cast<const bf16*>(b), static_cast<const bf16*>(a), ld, static_cast<const bf16*>(A_log),
-                      static_cast<const bf16*>(dt_bias), static_cast<bf16*>(beta), g, n, H);
+                      static_cast<const bf16*>(dt_bias), static_cast<bf16*>(beta), g, n, H,
+                      static_cast<const DevBatch*>(nullptr));
+}
+
+// ---- capacity path ----
+
+extern "C" size_t cs1_batch_desc_bytes(void) { return sizeof(DevBatch); }
+
+extern "C" int cs1_batch_desc_pack(const size_t* lengths, size_t count, void* out, size_t bytes) {
+    if (!out || bytes < sizeof(DevBatch)) return cudaErrorInvalidValue;
+    DevBatch d;
+    memset(&d, 0, sizeof(d));
+    if (!make_table(d.tab, lengths, count)) return cudaErrorInvalidValue;
+    d.rows = d.tab.offset[d.tab.count];
+    memcpy(out, &d, sizeof(d));
+    return cudaSuccess;
+}
+
+extern "C" int cs1_embed_dyn(const int32_t* ids, const void* table, void* out, int cap_rows, int D, const void* desc,
+                             void* stream) {
+    if (!desc || D <= 0 || D % 8 != 0 || cap_rows < 0) return cudaErrorInvalidValue;
+    if (cap_rows == 0) return cudaSuccess;
+    if (!aligned16(table) || !aligned16(out)) return cudaErrorInvalidValue;
+    const int grid = cap_rows < 65535 ? cap_rows : 65535;
+    return launch_pdl(embed_kernel, dim3(grid), dim3(128), 0, static_cast<cudaStream_t>(stream), ids,
+                      static_cast<const Pack8*>(table), static_cast<Pack8*>(out), D / 8, cap_rows,
+                      static_cast<const DevBatch*>(desc));
+}
+
+extern "C" int cs1_gdn_conv_dyn(const void* qkv, const void* history, int ld, const void* w, void* q, void* k,
+                                void* v, int cap_rows, int cap_seqs, int key_dim, int value_dim, const void* desc,
+                                void* stream) {
+    if (!desc || !qkv || !w || !q || !k || !v || key_dim <= 0 || value_dim <= 0 || ld < 2 * key_dim + value_dim ||
+        cap_rows <= 0 || cap_seqs <= 0 || cap_seqs > MAX_SEQS)
+        return cudaErrorInvalidValue;
+    SeqTable cap;  // launch geometry only
+    memset(&cap, 0, sizeof(cap));
+    cap.count = 1;
+    cap.offset[1] = cap_rows;
+    return conv_launch(qkv, history, ld, w, q, k, v, cap, key_dim, value_dim, static_cast<const DevBatch*>(desc),
+                       static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int cs1_gdn_gates_dyn(const void* b, const void* a, int ld, const void* A_log, const void* dt_bias,
+                                 void* beta, float* g, int cap_rows, int H, const void* desc, void* stream) {
+    if (!desc || cap_rows < 0 || H < 0 || ld < H) return cudaErrorInvalidValue;
+    const long n = (long)cap_rows * H;
+    if (n == 0) return cudaSuccess;
+    return launch_pdl(gates_kernel, dim3(grid_for(n)), dim3(THREADS), 0, static_cast<cudaStream_t>(stream),
+                      static_cast<const bf16*>(b), static_cast<const bf16*>(a), ld, static_cast<const bf16*>(A_log),
+                      static_cast<const bf16*>(dt_bias), static_cast<bf16*>(beta), g, n, H,
+                      static_cast<const DevBatch*>(desc));
 }
 
 extern "C" int cs1_sigmoid_gate(void* x, const void* gate, size_t n, void* stream) {

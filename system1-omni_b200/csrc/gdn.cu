@@ -32,6 +32,7 @@
 #include <algorithm>
 #include <climits>
 #include <cmath>
+#include <cstring>
 #include <new>
 #include <type_traits>
 
@@ -1146,6 +1147,19 @@ int cs1_gdn_prefill_batch_x(const void* q, const void* k, const void* v, const f
     const long stride = state_stride ? (long)H * 128 * 128 : 0;
     return gdn::run(q, k, v, g, beta, o, ws, bytes, tab, H, HK, scale, state_in, stride, state_out,
                     static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gdn_prefill_dyn(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
+                        int cap_rows, int cap_seqs, int H, int HK, float scale, const void* state_in,
+                        int state_stride, void* state_out, const void* desc, void* stream) {
+    if (!desc || cap_rows <= 0 || (state_stride != 0 && state_stride != 1)) return cudaErrorInvalidValue;
+    SeqTable cap;  // tensor-map extents only
+    memset(&cap, 0, sizeof(cap));
+    cap.count = 1;
+    cap.offset[1] = cap_rows;
+    const long stride = state_stride ? (long)H * 128 * 128 : 0;
+    return gdn::run_fused(q, k, v, g, beta, o, cap, H, HK, scale, state_in, stride, state_out,
+                          static_cast<cudaStream_t>(stream), static_cast<const DevBatch*>(desc), cap_seqs);
 }
 
 int cs1_gdn_prefill_batch_shared(const void* q, const void* k, const void* v, const float* g, const void* beta,

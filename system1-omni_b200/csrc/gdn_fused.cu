@@ -134,10 +134,11 @@ __device__ __forceinline__ void fail(uint32_t bit, volatile int* abort_flag) {
     *abort_flag = 1;
 }
 
+template <bool Dyn>
 __global__ void __launch_bounds__(THREADS, 1)
     gdn_fused(const __grid_constant__ Maps maps, const float* __restrict__ g, const bf16* __restrict__ beta,
               const __grid_constant__ SeqTable tab, bf16* __restrict__ o, int H, int HK, float scale,
-              const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out) {
+              const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out, const DevBatch* dyn) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -151,10 +152,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int* norms_done = reinterpret_cast<volatile int*>(sm + OFF_BAR + NBAR * 8 + 20);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    const int h = blockIdx.x, seq = tab.order[blockIdx.y];
+    // the capacity path (dyn): the table is the descriptor's, the grid covers the capacity
+    int seq, start, len;
+    if constexpr (Dyn) {
+        if ((int)blockIdx.y >= dyn->tab.count) return;  // past the batch: nothing allocated or armed
+        seq = dyn->tab.order[blockIdx.y];
+        start = dyn->tab.offset[seq];
+        len = dyn->tab.offset[seq + 1] - start;
+    } else {
+        seq = tab.order[blockIdx.y];
+        start = tab.offset[seq];
+        len = tab.offset[seq + 1] - start;
+    }
+    const int h = blockIdx.x;
     const int hk = h / (H / HK);
-    const int start = tab.offset[seq];
-    const int len = tab.offset[seq + 1] - start;
     const int NC = (len + C - 1) / C;
 
     if (threadIdx.x == 0) {
@@ -833,23 +844,27 @@ namespace gdn {
 // for every sequence).
 int run_fused(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
               const SeqTable& seqs, int H, int HK, float scale, const void* s_in, long s_in_stride, void* s_out,
-              cudaStream_t st) {
+              cudaStream_t st, const DevBatch* dyn, int cap_seqs) {
     using namespace gdnf;
     if (!q || !k || !v || !g || !beta || !o || H <= 0 || HK <= 0 || H % HK || H > 65535 || seqs.count > 65535)
         return cudaErrorInvalidValue;
+    if (dyn && (cap_seqs <= 0 || cap_seqs > MAX_SEQS)) return cudaErrorInvalidValue;
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return cudaErrorInvalidValue;
     static const cudaError_t configured =
-        cudaFuncSetAttribute(gdn_fused, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+        cudaFuncSetAttribute(gdn_fused<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     if (configured != cudaSuccess) return configured;
+    static const cudaError_t configured_dyn =
+        cudaFuncSetAttribute(gdn_fused<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (configured_dyn != cudaSuccess) return configured_dyn;
     const uint64_t rows = (uint64_t)seqs.offset[seqs.count];
     Maps maps;
     int e = host::make_map_3d_bf16(&maps.q, q, K, HK, rows, K, (uint64_t)HK * K, 64, 64);
     if (!e) e = host::make_map_3d_bf16(&maps.k, k, K, HK, rows, K, (uint64_t)HK * K, 64, 64);
     if (!e) e = host::make_map_3d_bf16(&maps.v, v, V, H, rows, V, (uint64_t)H * V, 64, 64);
     if (e) return e;
-    return launch_pdl(gdn_fused, dim3(H, seqs.count), dim3(THREADS), SMEM, st, maps, g,
+    return launch_pdl(dyn ? gdn_fused<true> : gdn_fused<false>, dim3(H, dyn ? cap_seqs : seqs.count), dim3(THREADS), SMEM, st, maps, g,
                       static_cast<const bf16*>(beta), seqs, static_cast<bf16*>(o), H, HK, scale,
-                      static_cast<const float*>(s_in), s_in_stride, static_cast<float*>(s_out));
+                      static_cast<const float*>(s_in), s_in_stride, static_cast<float*>(s_out), dyn);
 }
 
 }  // namespace gdn

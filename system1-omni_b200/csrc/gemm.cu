@@ -59,6 +59,7 @@ struct Params {
     int M, N, K;
     int tiles_m, tiles_n;
     int group;  // > 0: tiles walked in groups of `group` row blocks; < 0: groups of -group column blocks
+    const DevBatch* dyn;  // capacity path: M is the capacity, the batch's rows come from here
 };
 
 // Tile t -> (row block m, column block n). With group g > 0 the CTAs resident at one time
@@ -141,6 +142,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::BAR_OFFSET + 8 * (2 * C::STAGES + 5));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (p.dyn) {  // capacity path: only the batch's row blocks
+        p.M = min(p.M, p.dyn->rows);
+        p.tiles_m = (p.M + BM - 1) / BM;
+    }
     const int num_tiles = p.tiles_m * p.tiles_n;
     const int KB = (p.K + BK - 1) / BK;
 
@@ -341,6 +346,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (p.dyn) {  // capacity path: only the batch's row blocks (both CTAs of a pair agree)
+        p.M = min(p.M, p.dyn->rows);
+        p.tiles_m = (p.M + 255) / 256;
+    }
     const int num_tiles = p.tiles_m * p.tiles_n;
     const int KB = (p.K + BK - 1) / BK;
     const int cid = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
@@ -534,7 +543,35 @@ struct SwapParams {
     int split;    // parts per remaining tile, of `sub` rows of x each
     int sub;
     int items;    // full + (tiles_w * tiles_t - full) * split
+    int units;    // SMs (CTA pairs for the pair kernel) the split plan spreads a partial wave over
+    const DevBatch* dyn;  // capacity path: M is the capacity, the batch's rows come from here
 };
+
+// Whole waves of tiles stay whole; the tiles of a last partial wave are split along x
+// into parts of at least 64 rows so that they spread over the idle SMs.
+__host__ __device__ inline void swap_split(int tiles, int sms, int nt, int& full, int& split, int& sub) {
+    full = tiles / sms * sms;
+    const int rem = tiles - full;
+    split = 1;
+    if (rem > 0) {
+        const int by_sms = (sms + rem - 1) / rem;
+        const int by_rows = nt / 64 > 1 ? nt / 64 : 1;
+        split = by_sms < by_rows ? by_sms : by_rows;
+        while (split > 1 && rem * split > sms) split--;
+    }
+    sub = ((nt + split - 1) / split + 15) & ~15;
+    if (split == 1) full = tiles;
+}
+
+// The capacity path's plan for the batch's rows (the same plan the host makes for them).
+__device__ __forceinline__ void swap_dyn(SwapParams& p) {
+    if (!p.dyn) return;
+    p.M = min(p.M, p.dyn->rows);
+    p.tiles_t = (p.M + p.nt - 1) / p.nt;
+    const int tiles = p.tiles_w * p.tiles_t;
+    swap_split(tiles, p.units, p.nt, p.full, p.split, p.sub);
+    p.items = p.full + (tiles - p.full) * p.split;
+}
 
 // Work item -> (w tile, first row of x, rows of x). Items past `full` are parts of the
 // last partial wave's tiles, so that wave spreads over every SM; a part can be empty.
@@ -572,6 +609,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S_BAR_OFFSET + 8 * (2 * S_STAGES + 5));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    swap_dyn(p);
     const int num_tiles = p.items;
     const int KB = (p.K + BK - 1) / BK;
 
@@ -805,6 +843,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t rank = cluster_rank();
     const bool leader = rank == 0;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    swap_dyn(p);
     const int num_items = p.items;
     const int KB = (p.K + BK - 1) / BK;
     const int cid = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
@@ -1069,7 +1108,7 @@ enum Force : int { FORCE_NONE = 0, FORCE_PAIR, FORCE_ROW256, FORCE_ROW128, FORCE
 
 template <int BN, int EPI>
 int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy,
-              cudaStream_t st) {
+              cudaStream_t st, const DevBatch* dyn) {
     using C = Cfg<BN>;
     static const cudaError_t configured =
         cudaFuncSetAttribute(gemm_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -1089,6 +1128,7 @@ int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int
     p.tiles_m = (M + BM - 1) / BM;
     p.tiles_n = (N + BN - 1) / BN;
     p.group = h->group ? h->group : GROUP_M;
+    p.dyn = dyn;
     const int tiles = p.tiles_m * p.tiles_n;
     const int grid = std::min(tiles, h->sms);
     return launch_pdl(gemm_kernel<BN, EPI>, dim3(grid), dim3(THREADS), C::SMEM, st, ma, mb, p);
@@ -1096,7 +1136,7 @@ int launch_tc(const Handle* h, const void* x, const void* w, void* y, int M, int
 
 template <int EPI>
 int launch_pair(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy,
-                cudaStream_t st) {
+                cudaStream_t st, const DevBatch* dyn) {
     static const cudaError_t configured =
         cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
     if (configured != cudaSuccess) return configured;
@@ -1115,30 +1155,16 @@ int launch_pair(const Handle* h, const void* x, const void* w, void* y, int M, i
     p.tiles_m = (M + 255) / 256;
     p.tiles_n = (N + 255) / 256;
     p.group = h->group ? h->group : P_GROUP_M;
+    p.dyn = dyn;
     const int tiles = p.tiles_m * p.tiles_n;
     const int grid = 2 * std::min(tiles, h->sms / 2);
     return launch_pdl(gemm_pair_kernel<EPI>, dim3(grid), dim3(THREADS), P_SMEM, st, ma, mb, p);
 }
 
-// Whole waves of tiles stay whole; the tiles of a last partial wave are split along x
-// into parts of at least 64 rows so that they spread over the idle SMs.
-void swap_split(int tiles, int sms, int nt, int& full, int& split, int& sub) {
-    full = tiles / sms * sms;
-    const int rem = tiles - full;
-    split = 1;
-    if (rem > 0) {
-        const int by_sms = (sms + rem - 1) / rem;
-        const int by_rows = nt / 64 > 1 ? nt / 64 : 1;
-        split = by_sms < by_rows ? by_sms : by_rows;
-        while (split > 1 && rem * split > sms) split--;
-    }
-    sub = ((nt + split - 1) / split + 15) & ~15;
-    if (split == 1) full = tiles;
-}
 
 template <int EPI>
 int launch_swap(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int nt,
-                cudaStream_t st) {
+                cudaStream_t st, const DevBatch* dyn) {
     static const cudaError_t configured =
         cudaFuncSetAttribute(gemm_swap_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_SMEM);
     if (configured != cudaSuccess) return configured;
@@ -1161,12 +1187,16 @@ int launch_swap(const Handle* h, const void* x, const void* w, void* y, int M, i
     const int tiles = p.tiles_w * p.tiles_t;
     swap_split(tiles, h->sms, nt, p.full, p.split, p.sub);
     p.items = p.full + (tiles - p.full) * p.split;
-    return launch_pdl(gemm_swap_kernel<EPI>, dim3(std::min(p.items, h->sms)), dim3(THREADS), S_SMEM, st, mw, mx, p);
+    p.units = h->sms;
+    p.dyn = dyn;
+    // the capacity path's plan is made in the kernel: every SM may get an item
+    const int grid = dyn ? h->sms : std::min(p.items, h->sms);
+    return launch_pdl(gemm_swap_kernel<EPI>, dim3(grid), dim3(THREADS), S_SMEM, st, mw, mx, p);
 }
 
 template <int EPI>
 int launch_swap_pair(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int nt,
-                     cudaStream_t st) {
+                     cudaStream_t st, const DevBatch* dyn) {
     static const cudaError_t configured =
         cudaFuncSetAttribute(gemm_swap_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, SPCfg<EPI>::SMEM);
     if (configured != cudaSuccess) return configured;
@@ -1189,7 +1219,10 @@ int launch_swap_pair(const Handle* h, const void* x, const void* w, void* y, int
     const int tiles = p.tiles_w * p.tiles_t, pairs = h->sms / 2;
     swap_split(tiles, pairs, nt, p.full, p.split, p.sub);
     p.items = p.full + (tiles - p.full) * p.split;
-    return launch_pdl(gemm_swap_pair_kernel<EPI>, dim3(2 * std::min(p.items, pairs)), dim3(THREADS), SPCfg<EPI>::SMEM, st,
+    p.units = pairs;
+    p.dyn = dyn;
+    const int grid = 2 * (dyn ? pairs : std::min(p.items, pairs));
+    return launch_pdl(gemm_swap_pair_kernel<EPI>, dim3(grid), dim3(THREADS), SPCfg<EPI>::SMEM, st,
                       mw, mx, p);
 }
 
@@ -1246,7 +1279,7 @@ double swap_pair_cost(int M, int N, int epi, int sms, int& best_nt) {
 }
 
 int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, int K, int ldy, int epi,
-        cudaStream_t st) {
+        cudaStream_t st, const DevBatch* dyn = nullptr) {
     if (!h || M < 0 || N <= 0 || K <= 0 || !x || !w || !y) return cudaErrorInvalidValue;
     const int out_n = epi == EPI_SWIGLU ? N / 2 : N;
     if (ldy < out_n) return cudaErrorInvalidValue;
@@ -1254,6 +1287,7 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
     if (M == 0) return cudaSuccess;
     const bool tc_ok = K % 8 == 0 && N % 8 == 0 && ldy % 8 == 0 && aligned16(x) && aligned16(w) && aligned16(y);
     if (!tc_ok) {
+        if (dyn) return cudaErrorInvalidValue;  // the capacity path needs the tensor-core kernels
         const dim3 grid((out_n + 127) / 128, M);
         switch (epi) {
             case EPI_SWIGLU:
@@ -1309,43 +1343,43 @@ int run(const Handle* h, const void* x, const void* w, void* y, int M, int N, in
     if (nt2 > 0 && c_swap2 < cp && c_swap2 < c2 && c_swap2 < c1 && c_swap2 <= c_swap) {
         switch (epi) {
             case EPI_SWIGLU:
-                return launch_swap_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, nt2, st);
+                return launch_swap_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, nt2, st, dyn);
             case EPI_RESIDUAL:
-                return launch_swap_pair<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, nt2, st);
+                return launch_swap_pair<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, nt2, st, dyn);
             default:
-                return launch_swap_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, nt2, st);
+                return launch_swap_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, nt2, st, dyn);
         }
     }
     if (nt > 0 && c_swap < cp && c_swap < c2 && c_swap < c1) {
         switch (epi) {
             case EPI_SWIGLU:
-                return launch_swap<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, nt, st);
+                return launch_swap<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, nt, st, dyn);
             case EPI_RESIDUAL:
-                return launch_swap<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, nt, st);
+                return launch_swap<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, nt, st, dyn);
             default:
-                return launch_swap<EPI_STORE>(h, x, w, y, M, N, K, ldy, nt, st);
+                return launch_swap<EPI_STORE>(h, x, w, y, M, N, K, ldy, nt, st, dyn);
         }
     }
     if (h->pairs && cp <= c2 && cp <= c1) {
         switch (epi) {
             case EPI_SWIGLU:
-                return launch_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);
+                return launch_pair<EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st, dyn);
             case EPI_RESIDUAL:
-                return launch_pair<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st);
+                return launch_pair<EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st, dyn);
             default:
-                return launch_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, st);
+                return launch_pair<EPI_STORE>(h, x, w, y, M, N, K, ldy, st, dyn);
         }
     }
     const bool wide = epi == EPI_SWIGLU || c2 <= c1;
     switch (epi) {
         case EPI_SWIGLU:
-            return launch_tc<256, EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st);
+            return launch_tc<256, EPI_SWIGLU>(h, x, w, y, M, N, K, ldy, st, dyn);
         case EPI_RESIDUAL:
-            return wide ? launch_tc<256, EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st)
-                        : launch_tc<128, EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st);
+            return wide ? launch_tc<256, EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st, dyn)
+                        : launch_tc<128, EPI_RESIDUAL>(h, x, w, y, M, N, K, ldy, st, dyn);
         default:
-            return wide ? launch_tc<256, EPI_STORE>(h, x, w, y, M, N, K, ldy, st)
-                        : launch_tc<128, EPI_STORE>(h, x, w, y, M, N, K, ldy, st);
+            return wide ? launch_tc<256, EPI_STORE>(h, x, w, y, M, N, K, ldy, st, dyn)
+                        : launch_tc<128, EPI_STORE>(h, x, w, y, M, N, K, ldy, st, dyn);
     }
 }
 
@@ -1452,6 +1486,15 @@ int cs1_gemm_swiglu(void* gemm, const void* x, const void* w, void* out, int M, 
     if (I <= 0 || I % 128 != 0) return cudaErrorInvalidValue;
     return gemm::run(static_cast<const gemm::Handle*>(gemm), x, w, out, M, 2 * I, K, ldo, gemm::EPI_SWIGLU,
                      static_cast<cudaStream_t>(stream));
+}
+
+int cs1_gemm_dyn(void* gemm, const void* x, const void* w, void* y, int cap_rows, int N, int K, int ldy,
+                 int epilogue, const void* desc, void* stream) {
+    if (!desc || cap_rows <= 0 || epilogue < gemm::EPI_STORE || epilogue > gemm::EPI_SWIGLU)
+        return cudaErrorInvalidValue;
+    if (epilogue == gemm::EPI_SWIGLU && (N <= 0 || N % 256 != 0)) return cudaErrorInvalidValue;
+    return gemm::run(static_cast<const gemm::Handle*>(gemm), x, w, y, cap_rows, N, K, ldy, epilogue,
+                     static_cast<cudaStream_t>(stream), static_cast<const DevBatch*>(desc));
 }
 
 }  // extern "C"

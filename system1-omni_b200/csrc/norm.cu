@@ -74,10 +74,12 @@ constexpr int RW_WARPS = 8;
 template <bool Add>
 __global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
                                                                  const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                                 bf16* __restrict__ out, int rows, int D, float eps) {
+                                                                 bf16* __restrict__ out, int rows, int D, float eps,
+                                                                 const DevBatch* dyn) {
     __shared__ Pack8 wsm[32 * PPL];
     grid_dep_wait();
     grid_dep_launch();
+    rows = dyn_rows(dyn, rows);
     const int packs = D >> 3, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < packs; i += blockDim.x) wsm[i] = ld8(w + (size_t)i * 8);
     __syncthreads();
@@ -190,10 +192,11 @@ constexpr int GA_SMEM = GA_WARPS * GA_STAGES * GA_SLOTS * 32 * 16;
 __global__ void __launch_bounds__(GA_WARPS * 32) gated_async_kernel(const bf16* __restrict__ x,
                                                                   const bf16* __restrict__ z, int ldz,
                                                                   const bf16* __restrict__ w, bf16* __restrict__ out,
-                                                                  int rows, int H, float eps) {
+                                                                  int rows, int H, float eps, const DevBatch* dyn) {
     extern __shared__ Pack8 gring[];  // [GA_WARPS][GA_STAGES][GA_SLOTS][32]
     grid_dep_wait();
     grid_dep_launch();
+    if (dyn) rows = min(rows, dyn->rows * H);
     const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4, wib = threadIdx.x >> 5;
     const int groups = (rows + G_ROWS - 1) / G_ROWS;
     const int g0 = blockIdx.x * GA_WARPS + wib, gstep = gridDim.x * GA_WARPS;
@@ -277,7 +280,11 @@ bool vec_ok(int D, const void* a, const void* b, const void* c, const void* d) {
 
 using namespace s1;
 
-extern "C" int cs1_rms_norm(const void* x, const void* w, void* out, int rows, int D, float eps, void* stream) {
+namespace s1 {
+namespace {
+
+int rms_norm(const void* x, const void* w, void* out, int rows, int D, float eps, const DevBatch* dyn,
+             void* stream) {
     if (rows < 0 || D <= 0) return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
     auto st = static_cast<cudaStream_t>(stream);
@@ -288,16 +295,18 @@ extern "C" int cs1_rms_norm(const void* x, const void* w, void* out, int rows, i
         dim3 grid, block;
         rms_warp_shape(rows, grid, block);
         return launch_pdl(rms_warp_kernel<false>, grid, block, 0, st, static_cast<bf16*>(nullptr),
-                          static_cast<const bf16*>(nullptr), X, Wt, O, rows, D, eps);
-    } else if (vec_ok(D, x, w, out, out))
+                          static_cast<const bf16*>(nullptr), X, Wt, O, rows, D, eps, dyn);
+    }
+    if (dyn) return cudaErrorInvalidValue;  // the capacity path needs the warp-per-row kernel
+    if (vec_ok(D, x, w, out, out))
         rms_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
     else
         rms_scalar_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
     return cudaGetLastError();
 }
 
-extern "C" int cs1_add_rms_norm(void* residual, const void* delta, const void* w, void* out, int rows, int D,
-                                float eps, void* stream) {
+int add_rms_norm(void* residual, const void* delta, const void* w, void* out, int rows, int D, float eps,
+                 const DevBatch* dyn, void* stream) {
     if (rows < 0 || D <= 0) return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
     auto st = static_cast<cudaStream_t>(stream);
@@ -309,16 +318,18 @@ extern "C" int cs1_add_rms_norm(void* residual, const void* delta, const void* w
         dim3 grid, block;
         rms_warp_shape(rows, grid, block);
         return launch_pdl(rms_warp_kernel<true>, grid, block, 0, st, R, Dl, static_cast<const bf16*>(nullptr), Wt,
-                          O, rows, D, eps);
-    } else if (vec_ok(D, residual, delta, w, out))
+                          O, rows, D, eps, dyn);
+    }
+    if (dyn) return cudaErrorInvalidValue;
+    if (vec_ok(D, residual, delta, w, out))
         rms_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
     else
         rms_scalar_kernel<true><<<rows, NT, 0, st>>>(R, Dl, nullptr, Wt, O, D, eps);
     return cudaGetLastError();
 }
 
-extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const void* w, void* out, int T, int H,
-                                  int D, float eps, void* stream) {
+int gated_rms_norm(const void* x, const void* z, int ldz, const void* w, void* out, int T, int H, int D, float eps,
+                   const DevBatch* dyn, void* stream) {
     if (D != 128 || T < 0 || H <= 0 || ldz < H * D) return cudaErrorInvalidValue;
     const int rows = T * H;
     if (rows == 0) return cudaSuccess;
@@ -335,10 +346,46 @@ extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const v
         const int grid = need < sm_count() * 2 ? need : sm_count() * 2;  // two resident per SM
         return launch_pdl(gated_async_kernel, dim3(grid), dim3(GA_WARPS * 32), GA_SMEM, st,
                           static_cast<const bf16*>(x), static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w),
-                          static_cast<bf16*>(out), rows, H, eps);
+                          static_cast<bf16*>(out), rows, H, eps, dyn);
     }
+    if (dyn) return cudaErrorInvalidValue;
     // operands not on 16-byte boundaries: one warp per row, scalar accesses
     gated_scalar_kernel<<<(rows + WARPS - 1) / WARPS, WARPS * 32, 0, st>>>(static_cast<const bf16*>(x),
         static_cast<const bf16*>(z), ldz, static_cast<const bf16*>(w), static_cast<bf16*>(out), rows, H, eps);
     return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace s1
+
+extern "C" int cs1_rms_norm(const void* x, const void* w, void* out, int rows, int D, float eps, void* stream) {
+    return rms_norm(x, w, out, rows, D, eps, nullptr, stream);
+}
+
+extern "C" int cs1_add_rms_norm(void* residual, const void* delta, const void* w, void* out, int rows, int D,
+                                float eps, void* stream) {
+    return add_rms_norm(residual, delta, w, out, rows, D, eps, nullptr, stream);
+}
+
+extern "C" int cs1_gated_rms_norm(const void* x, const void* z, int ldz, const void* w, void* out, int T, int H,
+                                  int D, float eps, void* stream) {
+    return gated_rms_norm(x, z, ldz, w, out, T, H, D, eps, nullptr, stream);
+}
+
+extern "C" int cs1_rms_norm_dyn(const void* x, const void* w, void* out, int cap_rows, int D, float eps,
+                                const void* desc, void* stream) {
+    if (!desc) return cudaErrorInvalidValue;
+    return rms_norm(x, w, out, cap_rows, D, eps, static_cast<const DevBatch*>(desc), stream);
+}
+
+extern "C" int cs1_add_rms_norm_dyn(void* residual, const void* delta, const void* w, void* out, int cap_rows, int D,
+                                    float eps, const void* desc, void* stream) {
+    if (!desc) return cudaErrorInvalidValue;
+    return add_rms_norm(residual, delta, w, out, cap_rows, D, eps, static_cast<const DevBatch*>(desc), stream);
+}
+
+extern "C" int cs1_gated_rms_norm_dyn(const void* x, const void* z, int ldz, const void* w, void* out, int cap_rows,
+                                      int H, int D, float eps, const void* desc, void* stream) {
+    if (!desc) return cudaErrorInvalidValue;
+    return gated_rms_norm(x, z, ldz, w, out, cap_rows, H, D, eps, static_cast<const DevBatch*>(desc), stream);
 }

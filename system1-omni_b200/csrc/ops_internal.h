@@ -27,6 +27,17 @@ struct SeqTable {
 // zero, or the rows overflow int.
 bool make_table(SeqTable& t, const size_t* lengths, size_t count);
 
+// The batch descriptor of the capacity path (the `*_dyn` entry points): the packed rows
+// and the sequence table in device memory, written by one host-to-device copy before the
+// launches (or a captured graph of them) run. Launch geometry comes from the caller's
+// capacities (rows, sequences), the work from the descriptor, so one captured graph
+// serves every batch within its capacities.
+struct DevBatch {
+    int rows;  // packed rows of the batch, <= the capacity the launches were sized for
+    int pad[3];
+    SeqTable tab;
+};
+
 #ifdef __CUDACC__
 // Programmatic dependent launch. The forward's kernels are launched with programmatic
 // stream serialisation, so a kernel's CTAs may start while the previous kernel's last
@@ -60,6 +71,12 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Rows to process: the descriptor's when a launch runs on the capacity path, else the
+// launch's own count.
+__device__ __forceinline__ int dyn_rows(const DevBatch* d, int rows) {
+    return d ? min(d->rows, rows) : rows;
 }
 
 // Sequence index of row `row` (binary search over the offsets).

@@ -18,6 +18,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <deque>
@@ -93,6 +94,30 @@ struct Api {
     int (*head_score)(const void*, int, const int32_t*, int, const float*, const float*, int, int, float*,
                       void*) = nullptr;
     int (*fill_random)(void*, size_t, int, uint64_t, float, float, int, void*) = nullptr;
+    // additive: the capacity path (device-resident batch descriptor; one graph per capacity)
+    size_t (*batch_desc_bytes)() = nullptr;
+    int (*batch_desc_pack)(const size_t*, size_t, void*, size_t) = nullptr;
+    int (*embed_dyn)(const int32_t*, const void*, void*, int, int, const void*, void*) = nullptr;
+    int (*rms_norm_dyn)(const void*, const void*, void*, int, int, float, const void*, void*) = nullptr;
+    int (*gated_rms_norm_dyn)(const void*, const void*, int, const void*, void*, int, int, int, float, const void*,
+                              void*) = nullptr;
+    int (*gemm_dyn)(void*, const void*, const void*, void*, int, int, int, int, int, const void*, void*) = nullptr;
+    int (*gdn_conv_dyn)(const void*, const void*, int, const void*, void*, void*, void*, int, int, int, int,
+                        const void*, void*) = nullptr;
+    int (*gdn_gates_dyn)(const void*, const void*, int, const void*, const void*, void*, float*, int, int, const void*,
+                         void*) = nullptr;
+    int (*gdn_prefill_dyn)(const void*, const void*, const void*, const float*, const void*, void*, int, int, int, int,
+                           float, const void*, int, void*, const void*, void*) = nullptr;
+    int (*attn_prep_dyn)(const void*, const void*, int, const void*, const void*, const void*, const void*, void*,
+                         void*, void*, int, int, int, int, int, float, const void*, void*) = nullptr;
+    int (*attention_dyn)(const void*, const void*, const void*, int, const void*, void*, const void*, const void*, int,
+                         int, int, int, int, int, float, const void*, void*) = nullptr;
+    int (*head_score_dyn)(const void*, int, const int32_t*, int, const float*, const float*, int, int, float*,
+                          const void*, void*) = nullptr;
+    bool has_dyn() const {
+        return batch_desc_bytes && batch_desc_pack && embed_dyn && rms_norm_dyn && gated_rms_norm_dyn && gemm_dyn &&
+               gdn_conv_dyn && gdn_gates_dyn && gdn_prefill_dyn && attn_prep_dyn && attention_dyn && head_score_dyn;
+    }
 };
 
 template <typename F>
@@ -172,6 +197,18 @@ bool load_api(const char* spec, Api& a, std::string& err) {
     bind(h, "cs1_gemm_swiglu", a.gemm_swiglu, false, err);
     bind(h, "cs1_head_score", a.head_score, false, err);
     bind(h, "cs1_fill_random", a.fill_random, false, err);
+    bind(h, "cs1_batch_desc_bytes", a.batch_desc_bytes, false, err);
+    bind(h, "cs1_batch_desc_pack", a.batch_desc_pack, false, err);
+    bind(h, "cs1_embed_dyn", a.embed_dyn, false, err);
+    bind(h, "cs1_rms_norm_dyn", a.rms_norm_dyn, false, err);
+    bind(h, "cs1_gated_rms_norm_dyn", a.gated_rms_norm_dyn, false, err);
+    bind(h, "cs1_gemm_dyn", a.gemm_dyn, false, err);
+    bind(h, "cs1_gdn_conv_dyn", a.gdn_conv_dyn, false, err);
+    bind(h, "cs1_gdn_gates_dyn", a.gdn_gates_dyn, false, err);
+    bind(h, "cs1_gdn_prefill_dyn", a.gdn_prefill_dyn, false, err);
+    bind(h, "cs1_attn_prep_dyn", a.attn_prep_dyn, false, err);
+    bind(h, "cs1_attention_dyn", a.attention_dyn, false, err);
+    bind(h, "cs1_head_score_dyn", a.head_score_dyn, false, err);
     a.max_batch = a.gdn_prefill_batch_x ? 256 : 16;
     if (!a.fill_random && !aux.empty()) {
         void* ah = dlopen(aux.c_str(), RTLD_NOW | RTLD_LOCAL);
@@ -204,6 +241,10 @@ struct Batch {
     bool capture = false;  // capture prefix state (prefix pass)
     bool cp = false;       // context-parallel piece: prefix state from rank - 1, own state to rank + 1
     size_t rows = 0;
+    // capacity path: launches sized for (cap_rows, cap_seqs), the batch read from the
+    // device descriptor, so one captured graph serves every batch of that capacity
+    bool dyn = false;
+    int cap_rows = 0, cap_seqs = 0;
 };
 
 // NCCL, bound at run time (the library torch or the system provides) for the
@@ -276,6 +317,10 @@ struct Model {
     int table_positions = 0;
     // graphs
     bool graphs = false;
+    // capacity path (s1_model_set_dynamic): the batch descriptor in device memory
+    bool dynamic = false;
+    uint8_t* desc = nullptr;
+    size_t desc_bytes = 0;
     std::map<std::vector<size_t>, void*> graph_cache;
     std::deque<std::vector<size_t>> graph_order;
     // context parallelism: rank of `cp_world` processes that split one prompt in order
@@ -421,14 +466,25 @@ int layout_scratch(Model* m) {
 }
 
 // ------------------------------------------------------------- the forward ----
-int gemm_store(Model* m, size_t x, const Region& w, size_t y, int M, int N, int K) {
+int gemm_store(Model* m, size_t x, const Region& w, size_t y, int M, int N, int K, bool dyn = false) {
     m->launches++;
+    if (dyn) return m->api.gemm_dyn(m->gemm, m->S(x), m->W(w), m->S(y), M, N, K, N, 0, m->desc, m->stream);
     return m->api.gemm(m->gemm, m->S(x), m->W(w), m->S(y), M, N, K, N, m->stream);
 }
 
-// residual += x w^T, then x_next = rms_norm(residual, norm_w)
-int project_residual(Model* m, size_t x, const Region& w, int M, int K, const Region& norm_w) {
+// residual += x w^T, then x_next = rms_norm(residual, norm_w). On the capacity path M is
+// the capacity and the batch's rows come from the descriptor.
+int project_residual(Model* m, size_t x, const Region& w, int M, int K, const Region& norm_w, bool dyn = false) {
     const s1_config& c = m->cfg;
+    if (dyn) {
+        m->launches += 2;
+        CK(m->api.gemm_dyn(m->gemm, m->S(x), m->W(w), m->S(m->s_res), M, c.hidden, K, c.hidden, 1, m->desc,
+                           m->stream),
+           "residual projection");
+        CK(m->api.rms_norm_dyn(m->S(m->s_res), m->W(norm_w), m->S(m->s_x), M, c.hidden, c.eps, m->desc, m->stream),
+           "rms norm");
+        return 0;
+    }
     if (m->fused) {
         m->launches += 2;
         CK(m->api.gemm_residual(m->gemm, m->S(x), m->W(w), m->S(m->s_res), M, c.hidden, K, c.hidden, m->stream),
@@ -466,6 +522,10 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
     if (last < 0) last = c.n_layers;
     const int T = (int)b.rows;
     const int n = (int)b.lengths.size();
+    // capacity path: launches sized for cap_rows rows and cap_seqs sequences, the batch
+    // itself read from the device descriptor (m->desc)
+    const bool dyn = b.dyn;
+    const int TL = dyn ? b.cap_rows : T;
     std::vector<size_t> offs(n + 1, 0);
     for (int i = 0; i < n; i++) offs[i + 1] = offs[i] + b.lengths[i];
     const float gdn_scale = 1.0f / std::sqrt((float)c.lin_k_dim);
@@ -474,20 +534,23 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
     const bool cp_send = b.cp && m->cp_rank + 1 < m->cp_world, cp_recv = b.cp && m->cp_rank > 0;
     if (first == 0) {
         m->launches++;
-        CK(m->api.embed(static_cast<const int32_t*>((const void*)m->S(m->s_ids)), m->W(m->embed), m->S(m->s_res), T,
-                        c.hidden, m->stream),
+        const int32_t* ids = static_cast<const int32_t*>((const void*)m->S(m->s_ids));
+        CK(dyn ? m->api.embed_dyn(ids, m->W(m->embed), m->S(m->s_res), TL, c.hidden, m->desc, m->stream)
+               : m->api.embed(ids, m->W(m->embed), m->S(m->s_res), T, c.hidden, m->stream),
            "embed");
     }
     m->launches++;
-    CK(m->api.rms_norm(m->S(m->s_res), m->W(m->layers[first].input_norm), m->S(m->s_x), T, c.hidden, c.eps,
-                       m->stream),
+    CK(dyn ? m->api.rms_norm_dyn(m->S(m->s_res), m->W(m->layers[first].input_norm), m->S(m->s_x), TL, c.hidden,
+                                 c.eps, m->desc, m->stream)
+           : m->api.rms_norm(m->S(m->s_res), m->W(m->layers[first].input_norm), m->S(m->s_x), T, c.hidden, c.eps,
+                             m->stream),
        "input norm");
     int gi = 0, ai = 0;  // index of the layer among the GDN / attention layers (prefix buffers)
     for (int li = 0; li < first; li++) (m->types[li] == 0 ? gi : ai)++;
     for (int li = first; li < last; li++) {
         const Layer& L = m->layers[li];
         if (L.type == 0) {
-            CK(gemm_store(m, m->s_x, L.in_proj, m->s_gdn_in, T, m->gdn_in, c.hidden), "gdn input projection");
+            CK(gemm_store(m, m->s_x, L.in_proj, m->s_gdn_in, TL, m->gdn_in, c.hidden, dyn), "gdn input projection");
             const int ld = m->gdn_in;
             uint8_t* gin = m->S(m->s_gdn_in);
             if (cp_send || cp_recv) {  // the last three pre-conv rows go to the next piece's conv
@@ -497,7 +560,12 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
                 if (rc) return rc;
             }
             const void* hist = suffix ? m->prefix_buf + m->p_tail[gi] : nullptr;
-            if (m->api.gdn_conv_batch && n <= m->api.max_batch) {
+            if (dyn) {
+                m->launches++;
+                CK(m->api.gdn_conv_dyn(gin, hist, ld, m->W(L.conv), m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv), TL,
+                                       b.cap_seqs, m->kd, m->vd, m->desc, m->stream),
+                   "gdn conv");
+            } else if (m->api.gdn_conv_batch && n <= m->api.max_batch) {
                 m->launches++;
                 CK(m->api.gdn_conv_batch(gin, hist, ld, m->W(L.conv), m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
                                          b.lengths.data(), n, m->kd, m->vd, m->stream),
@@ -523,8 +591,11 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
             const size_t zoff = (size_t)m->conv * 2, boff = zoff + (size_t)m->vd * 2,
                          aoff = boff + (size_t)c.lin_v_heads * 2;
             m->launches++;
-            CK(m->api.gdn_gates(gin + boff, gin + aoff, ld, m->W(L.A_log), m->W(L.dt_bias), m->S(m->s_beta),
-                                reinterpret_cast<float*>(m->S(m->s_g)), T, c.lin_v_heads, m->stream),
+            CK(dyn ? m->api.gdn_gates_dyn(gin + boff, gin + aoff, ld, m->W(L.A_log), m->W(L.dt_bias), m->S(m->s_beta),
+                                          reinterpret_cast<float*>(m->S(m->s_g)), TL, c.lin_v_heads, m->desc,
+                                          m->stream)
+                   : m->api.gdn_gates(gin + boff, gin + aoff, ld, m->W(L.A_log), m->W(L.dt_bias), m->S(m->s_beta),
+                                      reinterpret_cast<float*>(m->S(m->s_g)), T, c.lin_v_heads, m->stream),
                "gdn gates");
             float* ws = reinterpret_cast<float*>(m->S(m->s_ws));
             const size_t state_bytes = (size_t)c.lin_v_heads * c.lin_k_dim * c.lin_v_dim * 4;
@@ -534,7 +605,14 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
             }
             const void* s_in = suffix ? m->prefix_buf + m->p_state[gi] : nullptr;
             void* s_out = b.capture ? m->prefix_buf + m->p_state[gi] : cp_send ? m->cp_state : nullptr;
-            if (m->api.gdn_prefill_batch_x && n <= m->api.max_batch) {
+            if (dyn) {
+                m->launches++;
+                CK(m->api.gdn_prefill_dyn(m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
+                                          reinterpret_cast<const float*>(m->S(m->s_g)), m->S(m->s_beta),
+                                          m->S(m->s_lo), TL, b.cap_seqs, c.lin_v_heads, c.lin_k_heads, gdn_scale, s_in,
+                                          0, nullptr, m->desc, m->stream),
+                   "gdn prefill");
+            } else if (m->api.gdn_prefill_batch_x && n <= m->api.max_batch) {
                 m->launches += 2;
                 CK(m->api.gdn_prefill_batch_x(m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
                                               reinterpret_cast<const float*>(m->S(m->s_g)), m->S(m->s_beta),
@@ -566,8 +644,10 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
                 if (rc) return rc;
             }
             m->launches++;
-            CK(m->api.gated_rms_norm(m->S(m->s_lo), gin + zoff, ld, m->W(L.norm), m->S(m->s_ln), T, c.lin_v_heads,
-                                     c.lin_v_dim, c.eps, m->stream),
+            CK(dyn ? m->api.gated_rms_norm_dyn(m->S(m->s_lo), gin + zoff, ld, m->W(L.norm), m->S(m->s_ln), TL,
+                                               c.lin_v_heads, c.lin_v_dim, c.eps, m->desc, m->stream)
+                   : m->api.gated_rms_norm(m->S(m->s_lo), gin + zoff, ld, m->W(L.norm), m->S(m->s_ln), T,
+                                           c.lin_v_heads, c.lin_v_dim, c.eps, m->stream),
                "gated norm");
             if (b.capture) {
                 // the last three pre-conv rows of the prefix, in rows of ld
@@ -577,18 +657,21 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
                                  (size_t)ld * 2, (size_t)m->conv * 2, 3, m->stream),
                    "capture conv history");
             }
-            CK(project_residual(m, m->s_ln, L.out, T, m->vd, L.post_norm), "gdn output projection");
+            CK(project_residual(m, m->s_ln, L.out, TL, m->vd, L.post_norm, dyn), "gdn output projection");
             gi++;
         } else {
-            CK(gemm_store(m, m->s_x, L.qkv, m->s_attn_in, T, m->attn_in, c.hidden), "attention input projection");
+            CK(gemm_store(m, m->s_x, L.qkv, m->s_attn_in, TL, m->attn_in, c.hidden, dyn), "attention input projection");
             const int ld = m->attn_in;
             uint8_t* ain = m->S(m->s_attn_in);
             uint8_t* kptr = ain + (size_t)m->attn_q * 2;
             uint8_t* vptr = kptr + (size_t)m->kvd * 2;
             m->launches++;
-            CK(m->api.attn_prep(ain, kptr, ld, m->W(L.q_norm), m->W(L.k_norm), m->S(m->s_cos), m->S(m->s_sin),
-                                m->S(m->s_aq), m->S(m->s_agate), m->S(m->s_ak), T, c.heads, c.kv_heads, c.head_dim,
-                                c.rotary_half, c.eps, m->stream),
+            CK(dyn ? m->api.attn_prep_dyn(ain, kptr, ld, m->W(L.q_norm), m->W(L.k_norm), m->S(m->s_cos), m->S(m->s_sin),
+                                          m->S(m->s_aq), m->S(m->s_agate), m->S(m->s_ak), TL, c.heads, c.kv_heads,
+                                          c.head_dim, c.rotary_half, c.eps, m->desc, m->stream)
+                   : m->api.attn_prep(ain, kptr, ld, m->W(L.q_norm), m->W(L.k_norm), m->S(m->s_cos), m->S(m->s_sin),
+                                      m->S(m->s_aq), m->S(m->s_agate), m->S(m->s_ak), T, c.heads, c.kv_heads,
+                                      c.head_dim, c.rotary_half, c.eps, m->stream),
                "attention prep");
             const size_t kv_prefix = (size_t)b.prefix * m->kvd * 2;
             if (cp_recv) {  // K (normed, rotated) and V of every earlier piece
@@ -598,7 +681,13 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
             }
             const void* pk = suffix ? m->prefix_buf + m->p_k[ai] : nullptr;
             const void* pv = suffix ? m->prefix_buf + m->p_v[ai] : nullptr;
-            if (suffix && m->api.attention_gated_shared_batch && n <= m->api.max_batch) {
+            if (dyn) {
+                m->launches++;
+                CK(m->api.attention_dyn(m->S(m->s_aq), m->S(m->s_ak), vptr, ld, m->S(m->s_agate), m->S(m->s_ao), pk,
+                                        pv, suffix ? b.prefix : 0, TL, b.cap_seqs, c.heads, c.kv_heads, c.head_dim,
+                                        attn_scale, m->desc, m->stream),
+                   "attention");
+            } else if (suffix && m->api.attention_gated_shared_batch && n <= m->api.max_batch) {
                 m->launches++;
                 CK(m->api.attention_gated_shared_batch(m->S(m->s_aq), m->S(m->s_ak), vptr, ld, m->S(m->s_agate),
                                                        m->S(m->s_ao), pk, pv, b.lengths.data(), n, b.prefix,
@@ -653,11 +742,16 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
                 if (!rc) rc = cp_xfer(m, m->prefix_buf + m->p_v[ai], bytes, nullptr, 0, "prefix V send");
                 if (rc) return rc;
             }
-            CK(project_residual(m, m->s_ao, L.o, T, m->qd, L.post_norm), "attention output projection");
+            CK(project_residual(m, m->s_ao, L.o, TL, m->qd, L.post_norm, dyn), "attention output projection");
             ai++;
         }
         const Region& next = li + 1 < c.n_layers ? m->layers[li + 1].input_norm : m->final_norm;
-        if (m->fused) {
+        if (dyn) {
+            m->launches++;
+            CK(m->api.gemm_dyn(m->gemm, m->S(m->s_x), m->W(L.gate_up), m->S(m->s_act), TL, 2 * c.intermediate,
+                               c.hidden, c.intermediate, 2, m->desc, m->stream),
+               "gate/up projection");
+        } else if (m->fused) {
             m->launches++;
             CK(m->api.gemm_swiglu(m->gemm, m->S(m->s_x), m->W(L.gate_up), m->S(m->s_act), T, c.intermediate,
                                   c.hidden, c.intermediate, m->stream),
@@ -668,7 +762,7 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
             CK(m->api.silu_mul(m->S(m->s_gate_up), 2 * c.intermediate, m->S(m->s_act), T, c.intermediate, m->stream),
                "silu mul");
         }
-        CK(project_residual(m, m->s_act, L.down, T, c.intermediate, next), "down projection");
+        CK(project_residual(m, m->s_act, L.down, TL, c.intermediate, next, dyn), "down projection");
     }
     return 0;
 }
@@ -701,10 +795,19 @@ int host_head(Model* m, int n, float* logits) {
     return 0;
 }
 
-int run_head(Model* m, int n) {
+int run_head(Model* m, const Batch& b) {
     const s1_config& c = m->cfg;
+    const int n = (int)b.lengths.size();
     if (!m->api.head_score) return 0;  // host head after the forward (host_head)
     m->launches++;
+    if (b.dyn) {
+        CK(m->api.head_score_dyn(m->S(m->s_x), c.hidden, reinterpret_cast<const int32_t*>(m->S(m->s_rows)), b.cap_seqs,
+                                 reinterpret_cast<const float*>(m->W(m->head_w)),
+                                 reinterpret_cast<const float*>(m->W(m->head_b)), c.labels, c.hidden,
+                                 reinterpret_cast<float*>(m->S(m->s_logits)), m->desc, m->stream),
+           "scorer head");
+        return 0;
+    }
     CK(m->api.head_score(m->S(m->s_x), c.hidden, reinterpret_cast<const int32_t*>(m->S(m->s_rows)), n,
                          reinterpret_cast<const float*>(m->W(m->head_w)), reinterpret_cast<const float*>(m->W(m->head_b)),
                          c.labels, c.hidden, reinterpret_cast<float*>(m->S(m->s_logits)), m->stream),
@@ -712,8 +815,10 @@ int run_head(Model* m, int n) {
     return 0;
 }
 
-// Upload ids, per-row rotary tables and the last-token rows of a batch.
-int stage_inputs(Model* m, const int32_t* ids, const Batch& b) {
+// Upload ids, per-row rotary tables and the last-token rows of a batch; on the capacity
+// path (s1_model_set_dynamic) also its descriptor, after choosing the capacities: rows
+// rounded up to a power of two (at least 64, at most the model's), sequences likewise.
+int stage_inputs(Model* m, const int32_t* ids, Batch& b) {
     // Every id indexes the embedding table, so one out of range would read past it on the
     // device: the batch is refused before anything is copied or launched.
     for (size_t i = 0; i < b.rows; i++)
@@ -740,10 +845,26 @@ int stage_inputs(Model* m, const int32_t* ids, const Batch& b) {
     CK(m->api.upload(m->S(m->s_cos), cs.data(), cs.size() * 2, m->stream), "upload cos");
     CK(m->api.upload(m->S(m->s_sin), sn.data(), sn.size() * 2, m->stream), "upload sin");
     CK(m->api.upload(m->S(m->s_rows), rows.data(), rows.size() * 4, m->stream), "upload rows");
+    b.dyn = m->dynamic && m->desc && !b.capture && !b.cp && n <= 256;
+    if (b.dyn) {
+        int r = 64;
+        while (r < (int)b.rows) r <<= 1;
+        b.cap_rows = std::min(r, m->cap_tokens);
+        int q = 1;
+        while (q < n) q <<= 1;
+        b.cap_seqs = std::min(q, std::min(m->cap_seqs, 256));
+        std::vector<uint8_t> d(m->desc_bytes);
+        if (m->api.batch_desc_pack(b.lengths.data(), b.lengths.size(), d.data(), d.size()) != 0)
+            return fail(m, -1, "batch descriptor");
+        CK(m->api.upload(m->desc, d.data(), d.size(), m->stream), "upload batch descriptor");
+    }
     return 0;
 }
 
+// A graph serves the batches of its key: on the capacity path every batch of its
+// capacities and prefix (the last field cannot be a capture flag), else one length vector.
 std::vector<size_t> graph_key(const Batch& b) {
+    if (b.dyn) return {(size_t)b.cap_rows, (size_t)b.cap_seqs, (size_t)b.prefix, SIZE_MAX};
     std::vector<size_t> k = b.lengths;
     k.push_back((size_t)b.prefix);
     k.push_back(b.capture ? 1 : 0);
@@ -752,11 +873,10 @@ std::vector<size_t> graph_key(const Batch& b) {
 
 // Run the layers and the head of a staged batch, eagerly or through a cached graph.
 int execute(Model* m, const Batch& b, bool head) {
-    const int n = (int)b.lengths.size();
     m->launches = 0;
     if (!m->graphs || b.capture) {
         int rc = run_layers(m, b);
-        if (!rc && head) rc = run_head(m, n);
+        if (!rc && head) rc = run_head(m, b);
         return rc;
     }
     std::vector<size_t> key = graph_key(b);
@@ -767,13 +887,13 @@ int execute(Model* m, const Batch& b, bool head) {
         return 0;
     }
     int rc = run_layers(m, b);
-    if (!rc && head) rc = run_head(m, n);
+    if (!rc && head) rc = run_head(m, b);
     if (rc) return rc;
     const long eager = m->launches;
     // capture the same sequence for the next call with this length vector
     if (m->api.graph_begin(m->stream) == 0) {
         int crc = run_layers(m, b);
-        if (!crc && head) crc = run_head(m, n);
+        if (!crc && head) crc = run_head(m, b);
         void* exec = nullptr;
         const int erc = m->api.graph_end(m->stream, &exec);
         if (!crc && !erc && exec) {
@@ -947,6 +1067,7 @@ __attribute__((visibility("default"))) void s1_model_destroy(void* mp) {
     if (m->prefix_buf) m->api.free_(m->prefix_buf);
     if (m->cp_state) m->api.free_(m->cp_state);
     if (m->cp_table) m->api.free_(m->cp_table);
+    if (m->desc) m->api.free_(m->desc);
     if (m->comm) m->nccl.comm_destroy(m->comm);
     if (m->stream) m->api.stream_destroy(m->stream);
     // the library stays loaded: CUDA state it owns must outlive this model
@@ -1201,6 +1322,26 @@ __attribute__((visibility("default"))) int s1_model_set_graphs(void* mp, int ena
     return 0;
 }
 
+__attribute__((visibility("default"))) int s1_model_set_dynamic(void* mp, int enabled) {
+    auto* m = static_cast<Model*>(mp);
+    if (!m) return -1;
+    if (enabled && (!m->api.has_dyn() || !m->fused || !m->api.head_score))
+        return fail(m, -1, "the library has no capacity-path entry points");
+    if (enabled && !m->desc) {
+        m->desc_bytes = m->api.batch_desc_bytes();
+        void* p = nullptr;
+        CK(m->api.malloc_(&p, m->desc_bytes), "batch descriptor");
+        m->desc = static_cast<uint8_t*>(p);
+    }
+    m->dynamic = enabled != 0;
+    return 0;
+}
+
+__attribute__((visibility("default"))) int s1_model_graph_count(void* mp) {
+    auto* m = static_cast<Model*>(mp);
+    return m ? (int)m->graph_cache.size() : -1;
+}
+
 __attribute__((visibility("default"))) void* s1_model_stream(void* mp) {
     auto* m = static_cast<Model*>(mp);
     return m ? m->stream : nullptr;
@@ -1291,7 +1432,7 @@ __attribute__((visibility("default"))) int s1_model_forward_cp(void* mp, const i
     if (rc) return rc;
     m->launches = 0;
     rc = run_layers(m, b);
-    if (!rc && last) rc = run_head(m, 1);
+    if (!rc && last) rc = run_head(m, b);
     if (rc) return rc;
     return read_outputs(m, b, last ? logits : nullptr, last ? hidden : nullptr);
 }

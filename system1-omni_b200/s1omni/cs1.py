@@ -86,6 +86,19 @@ SIGNATURES = {
     "cs1_gemm_residual": (I, [P, P, P, P, I, I, I, I, P]),
     "cs1_gemm_swiglu": (I, [P, P, P, P, I, I, I, I, P]),
     "cs1_head_score": (I, [P, I, P, I, P, P, I, I, P, P]),
+    "cs1_batch_desc_bytes": (Z, []),
+    "cs1_batch_desc_pack": (I, [P, Z, P, Z]),
+    "cs1_embed_dyn": (I, [P, P, P, I, I, P, P]),
+    "cs1_rms_norm_dyn": (I, [P, P, P, I, I, F, P, P]),
+    "cs1_add_rms_norm_dyn": (I, [P, P, P, P, I, I, F, P, P]),
+    "cs1_gated_rms_norm_dyn": (I, [P, P, I, P, P, I, I, I, F, P, P]),
+    "cs1_gemm_dyn": (I, [P, P, P, P, I, I, I, I, I, P, P]),
+    "cs1_gdn_conv_dyn": (I, [P, P, I, P, P, P, P, I, I, I, I, P, P]),
+    "cs1_gdn_gates_dyn": (I, [P, P, I, P, P, P, P, I, I, P, P]),
+    "cs1_gdn_prefill_dyn": (I, [P, P, P, P, P, P, I, I, I, I, F, P, I, P, P, P]),
+    "cs1_attn_prep_dyn": (I, [P, P, I, P, P, P, P, P, P, P, I, I, I, I, I, F, P, P]),
+    "cs1_attention_dyn": (I, [P, P, P, I, P, P, P, P, I, I, I, I, I, I, F, P, P]),
+    "cs1_head_score_dyn": (I, [P, I, P, I, P, P, I, I, P, P, P]),
     "cs1_fill_random": (I, [P, Z, I, U64, F, F, I, P]),
     "cs1_vision_linear": (I, [P, P, P, P, P, I, I, I, P]),
     "cs1_gemm_f32": (I, [P, P, P, P, I, I, I, P]),

@@ -105,6 +105,8 @@ def _lib():
     lib.s1_model_run_staged.argtypes = [P]
     lib.s1_model_fetch_logits.argtypes = [P, P]
     lib.s1_model_set_graphs.argtypes = [P, I]
+    lib.s1_model_set_dynamic.argtypes = [P, I]
+    lib.s1_model_graph_count.argtypes = [P]
     lib.s1_model_stream.restype = P
     lib.s1_model_stream.argtypes = [P]
     lib.s1_model_last_launches.restype = ctypes.c_long
@@ -402,6 +404,15 @@ class Model:
 
     def set_graphs(self, on):
         self._check(self._lib.s1_model_set_graphs(self._h, 1 if on else 0), "set_graphs")
+
+    def set_dynamic(self, on):
+        """Device-side batching: launches sized for capacities, the batch read from a device
+        descriptor, so one captured graph serves every length vector of its capacities."""
+        self._check(self._lib.s1_model_set_dynamic(self._h, 1 if on else 0), "set_dynamic")
+
+    @property
+    def graph_count(self):
+        return int(self._lib.s1_model_graph_count(self._h))
 
     @property
     def stream(self):
