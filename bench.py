@@ -622,6 +622,37 @@ def latency(model, args, repeats=3):
             "repeats_per_request": repeats, "tokens_median": int(np.median([len(r) for r in reqs]))}
 
 
+def latency_dynamic(model, repeats=3):
+    """The same requests through device-side batching with CUDA graphs: one graph per
+    capacity (rows rounded up to a power of two), captured once per capacity before the
+    timing as a server does at start-up, then every request replays its capacity's graph
+    whatever its length."""
+    reqs = single_requests()
+    model.set_graphs(True)
+    model.set_dynamic(True)
+    try:
+        seen = set()
+        for r in reqs:  # warm: capture each capacity once
+            cap = max(64, 1 << (len(r) - 1).bit_length())
+            if cap not in seen:
+                seen.add(cap)
+                model.forward([r])
+                model.forward([r])
+        ms = []
+        for r in reqs:
+            one = []
+            for _ in range(repeats):
+                t0 = time.perf_counter()
+                model.forward([r])
+                one.append((time.perf_counter() - t0) * 1e3)
+            ms.append(float(np.median(one)))
+        return {"p50_ms": float(np.median(ms)), "mean_ms": float(np.mean(ms)), "requests": len(reqs),
+                "repeats_per_request": repeats, "graphs": model.graph_count, "capacities": sorted(seen)}
+    finally:
+        model.set_dynamic(False)
+        model.set_graphs(False)
+
+
 def run_ours(args, rank, world, local):
     import torch
     from s1omni import Cs1, Model, preset
@@ -672,6 +703,7 @@ def run_ours(args, rank, world, local):
         e2e_ms.append((time.perf_counter() - t0) * 1e3)
     e2e = float(np.median(e2e_ms[1:]))
     lat = latency(model, args)
+    lat["dynamic_graphs"] = latency_dynamic(model)
     long = long_prefill(model, torch, stream) if rank == 0 and not args.no_long else None
     one_gpu = long.pop("_raw") if long else None
     long_cp = long_prefill_cp(model, torch, dist, rank, world, stream, one_gpu) if dist and not args.no_long else None
