@@ -624,20 +624,16 @@ def latency(model, args, repeats=3):
 
 def latency_dynamic(model, repeats=3):
     """The same requests through device-side batching with CUDA graphs: one graph per
-    capacity (rows rounded up to a power of two), captured once per capacity before the
-    timing as a server does at start-up, then every request replays its capacity's graph
-    whatever its length."""
+    capacity (rows rounded up to an eighth of their octave), captured once per capacity
+    before the timing as a server does at start-up, then every request replays its
+    capacity's graph whatever its length."""
     reqs = single_requests()
     model.set_graphs(True)
     model.set_dynamic(True)
     try:
-        seen = set()
-        for r in reqs:  # warm: capture each capacity once
-            cap = max(64, 1 << (len(r) - 1).bit_length())
-            if cap not in seen:
-                seen.add(cap)
-                model.forward([r])
-                model.forward([r])
+        before = model.graph_count
+        for r in reqs:  # warm: the first request of each capacity captures its graph
+            model.forward([r])
         ms = []
         for r in reqs:
             one = []
@@ -647,7 +643,7 @@ def latency_dynamic(model, repeats=3):
                 one.append((time.perf_counter() - t0) * 1e3)
             ms.append(float(np.median(one)))
         return {"p50_ms": float(np.median(ms)), "mean_ms": float(np.mean(ms)), "requests": len(reqs),
-                "repeats_per_request": repeats, "graphs": model.graph_count, "capacities": sorted(seen)}
+                "repeats_per_request": repeats, "graphs": model.graph_count - before}
     finally:
         model.set_dynamic(False)
         model.set_graphs(False)

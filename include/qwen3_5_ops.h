@@ -91,6 +91,20 @@ int cs1_attention_gated_batch(const void* q, const void* k, const void* v, int l
                               void* stream);                      // ops.h:92
 int cs1_gdn_gates(const void* b, const void* a, int ld, const void* A_log, const void* dt_bias, void* beta,
                   float* g, int T, int H, void* stream);          // ops.h:98
+// Additive: the GDN front end in one launch: cs1_gdn_conv_batch (causal conv + SiLU of q, k,
+// v), the inverse L2 norm of every (row, head) of q and k (rnorm_q, rnorm_k: [T, key_dim /
+// 128] float32, rsqrt(sum y^2 + 1e-6) over the head's bf16 outputs) and cs1_gdn_gates of
+// the same rows (b, a: gate columns in rows of ld; H gates). key_dim a multiple of 128.
+int cs1_gdn_front_batch(const void* qkv, const void* history, int ld, const void* w, void* q, void* k, void* v,
+                        float* rnorm_q, float* rnorm_k, const void* b, const void* a, const void* A_log,
+                        const void* dt_bias, void* beta, float* g, int H, const size_t* lengths, size_t count,
+                        int key_dim, int value_dim, void* stream);
+// Additive: cs1_gdn_prefill_batch_x with the front end's inverse norms of q and k in place
+// of the prefill's own (no workspace).
+int cs1_gdn_prefill_batch_xn(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                             const float* rnorm_q, const float* rnorm_k, void* o, const size_t* lengths, size_t count,
+                             int H, int HK, float scale, const void* state_in, int state_stride, void* state_out,
+                             void* stream);
 size_t cs1_gdn_batch_workspace_floats(int tokens, int H, int count);   // ops.h:104
 int cs1_gdn_prefill_batch(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
                           float* workspace, size_t workspace_bytes, const size_t* lengths, size_t count, int H,
@@ -206,6 +220,12 @@ size_t cs1_batch_desc_bytes(void);
 int cs1_batch_desc_pack(const size_t* lengths, size_t count, void* out, size_t bytes);
 int cs1_embed_dyn(const int32_t* ids, const void* table, void* out, int cap_rows, int D, const void* desc,
                   void* stream);
+// Zero width_bytes of rows [rows, min(rows + margin, cap_rows)) of x (rows of ld_bytes; both
+// multiples of 16, x 16-byte aligned): the rows just past the batch that a last GDN chunk
+// or attention key tile reads (masked, but they must be finite; the host-length entry
+// points read zeros there through their tensor-map bounds).
+int cs1_clear_tail_dyn(void* x, size_t ld_bytes, size_t width_bytes, int cap_rows, int margin, const void* desc,
+                       void* stream);
 int cs1_rms_norm_dyn(const void* x, const void* w, void* out, int cap_rows, int D, float eps, const void* desc,
                      void* stream);
 int cs1_add_rms_norm_dyn(void* residual, const void* delta, const void* w, void* out, int cap_rows, int D,
@@ -220,10 +240,17 @@ int cs1_gdn_conv_dyn(const void* qkv, const void* history, int ld, const void* w
                      int cap_rows, int cap_seqs, int key_dim, int value_dim, const void* desc, void* stream);
 int cs1_gdn_gates_dyn(const void* b, const void* a, int ld, const void* A_log, const void* dt_bias, void* beta,
                       float* g, int cap_rows, int H, const void* desc, void* stream);
-// state_in / state_out as cs1_gdn_prefill_batch_x; no workspace.
-int cs1_gdn_prefill_dyn(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
-                        int cap_rows, int cap_seqs, int H, int HK, float scale, const void* state_in,
-                        int state_stride, void* state_out, const void* desc, void* stream);
+// state_in / state_out as cs1_gdn_prefill_batch_x; no workspace. rnorm_q, rnorm_k: the
+// inverse norms from cs1_gdn_front_dyn, or both null (computed in the prefill).
+int cs1_gdn_prefill_dyn(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                        const float* rnorm_q, const float* rnorm_k, void* o, int cap_rows, int cap_seqs, int H,
+                        int HK, float scale, const void* state_in, int state_stride, void* state_out, const void* desc,
+                        void* stream);
+// cs1_gdn_front_batch on the capacity path.
+int cs1_gdn_front_dyn(const void* qkv, const void* history, int ld, const void* w, void* q, void* k, void* v,
+                      float* rnorm_q, float* rnorm_k, const void* b, const void* a, const void* A_log,
+                      const void* dt_bias, void* beta, float* g, int H, int cap_rows, int cap_seqs, int key_dim,
+                      int value_dim, const void* desc, void* stream);
 int cs1_attn_prep_dyn(const void* qg, const void* kr, int ld, const void* qw, const void* kw, const void* cos,
                       const void* sin, void* q, void* gate, void* k, int cap_rows, int Hq, int Hk, int Dh, int half,
                       float eps, const void* desc, void* stream);

@@ -103,7 +103,8 @@ int s1_model_run_layers(void* model, const int32_t* ids, const size_t* lengths, 
 int s1_model_set_graphs(void* model, int enabled);
 // Device-side batching (default off; needs the library's cs1_*_dyn entry points): every
 // forward other than a prefix-capture pass and a context-parallel piece sizes its launches
-// for capacities (rows rounded up to a power of two >= 64, sequences to a power of two)
+// for capacities (rows rounded up to an eighth of their power-of-two octave, a multiple of
+// 64; sequences to a power of two)
 // and reads the batch from a descriptor in device memory uploaded with the ids, so with
 // graphs on one captured graph per (capacities, shared prefix) serves every length vector
 // that fits, instead of one per length vector (the reference's cache, model.rs:1583-1614).

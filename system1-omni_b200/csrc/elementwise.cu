@@ -65,16 +65,54 @@ struct alignas(4 * NP) PackN {
     __nv_bfloat162 h[NP];
 };
 
-template <int NP, bool Dyn>
-__global__ void __launch_bounds__(128, NP == 2 ? 8 : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
+// The GDN front end (Front): besides q, k and v, the inverse L2 norm of every (row, head)
+// of q and k, rsqrt(sum y^2 + 1e-6) over the bf16 outputs y of the head (the norm the GDN
+// prefill applies in fp32, here reduced across the head's lanes), and, in one extra CTA
+// column per run of rows, the gates of those rows: beta = bf16(sigmoid(b)) and
+// g = -exp(A_log) softplus(a + dt_bias) (the arithmetic of cs1_gdn_gates).
+struct FrontArgs {
+    float* rnq;  // [T, HK] inverse norms of q
+    float* rnk;  // [T, HK] inverse norms of k
+    const bf16* b;
+    const bf16* a;  // gate inputs, rows of ld (the conv input's row stride)
+    const bf16* A_log;
+    const bf16* dt_bias;
+    bf16* beta;  // [T, H]
+    float* g;    // [T, H]
+    int H;
+};
+
+// The gate CTA's work, out of line so that its registers do not count against the conv's.
+__device__ __noinline__ void front_gates(const FrontArgs& fr, int ld, int t_begin, int t_end) {
+    for (int i = threadIdx.x; i < (t_end - t_begin) * fr.H; i += blockDim.x) {
+        const int t = t_begin + i / fr.H, h = i % fr.H;
+        const size_t src = (size_t)t * ld + h;
+        fr.beta[(size_t)t * fr.H + h] = to_bf16(sigmoid(f32(fr.b[src])));
+        const float x = f32(fr.a[src]) + f32(fr.dt_bias[h]);
+        const float sp = x > 20.f ? x : log1pf(expf(x));
+        fr.g[(size_t)t * fr.H + h] = -expf(f32(fr.A_log[h])) * sp;
+    }
+}
+
+template <int NP, bool Dyn, bool Front>
+__global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
                                 bf16* __restrict__ v, int key_packs, int value_packs, int run,
-                                const __grid_constant__ SeqTable tab_arg, const DevBatch* dyn) {
+                                const __grid_constant__ SeqTable tab_arg, const DevBatch* dyn,
+                                const __grid_constant__ FrontArgs fr) {
     using P = PackN<NP>;
     const SeqTable& tab = Dyn ? dyn->tab : tab_arg;  // the capacity path's table is in device memory
     constexpr int CH = 2 * NP;  // channels per thread
     grid_dep_wait();
     grid_dep_launch();
+    if constexpr (Front) {
+        if (blockIdx.x == gridDim.x - 1) {  // the gate CTA of this run of rows
+            const int T = tab.offset[tab.count];
+            const int t_begin = blockIdx.y * run, t_end = min(T, t_begin + run);
+            front_gates(fr, ld_, t_begin, t_end);
+            return;
+        }
+    }
     const int c = blockIdx.x * blockDim.x + threadIdx.x;  // pack of CH channels
     const int packs = 2 * key_packs + value_packs;
     if (c >= packs) return;
@@ -158,6 +196,27 @@ __global__ void __launch_bounds__(128, NP == 2 ? 8 : 4) conv_vec_kernel(const bf
                 out.h[p] = __floats2bfloat162_rn(y.x, y.y);
             }
             *reinterpret_cast<P*>(dst + (size_t)t * dst_ld) = out;
+            if constexpr (Front) {
+                // q and k packs: a head is 128 / CH consecutive lanes of one warp (heads start on
+                // pack multiples of 128 / CH), so the branch and the shuffles are warp-uniform
+                constexpr int LANES = 128 / CH;
+                if (c < 2 * key_packs) {
+                    float ss = 0.f;
+#pragma unroll
+                    for (int p = 0; p < NP; p++) {
+                        const float2 yy = __bfloat1622float2(out.h[p]);
+                        ss = fmaf(yy.x, yy.x, ss);
+                        ss = fmaf(yy.y, yy.y, ss);
+                    }
+#pragma unroll
+                    for (int o = LANES / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+                    if ((threadIdx.x & (LANES - 1)) == 0) {
+                        const int HK = key_packs / LANES, head = c / LANES;
+                        float* dn = head < HK ? fr.rnq : fr.rnk;
+                        dn[(size_t)t * HK + (head < HK ? head : head - HK)] = rsqrtf(ss + 1e-6f);
+                    }
+                }
+            }
 #pragma unroll
             for (int p = 0; p < NP; p++) {
                 x1[p] = x2[p];
@@ -271,7 +330,8 @@ unsigned grid_for(size_t n) {
 // `tab` holds the batch, or, on the capacity path (dyn non-null), only its capacity
 // (offset[count] = cap_rows) while the kernels read the batch from the descriptor.
 int conv_launch(const void* qkv, const void* history, int ld, const void* w, void* q, void* k, void* v,
-                const SeqTable& tab, int key_dim, int value_dim, const DevBatch* dyn, cudaStream_t st) {
+                const SeqTable& tab, int key_dim, int value_dim, const DevBatch* dyn, cudaStream_t st,
+                const FrontArgs* front = nullptr) {
     const int T = tab.offset[tab.count];
     const int rows = T < 65535 ? T : 65535;
     const bool vec = key_dim % 8 == 0 && value_dim % 8 == 0 && ld % 8 == 0 && aligned16(qkv) && aligned16(w) &&
@@ -290,15 +350,25 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
         while (run > 16 && groups * ((T + run - 1) / run) < waves2 && (T + run / 2 - 1) / (run / 2) <= 65535)
             run /= 2;
         if ((T + run - 1) / run > 65535) return cudaErrorInvalidValue;
-        auto kernel = dyn ? (narrow ? conv_vec_kernel<2, true> : conv_vec_kernel<4, true>)
-                          : (narrow ? conv_vec_kernel<2, false> : conv_vec_kernel<4, false>);
+        FrontArgs fr{};
+        if (front) fr = *front;
+        void (*kernel)(const bf16*, const bf16*, int, const bf16*, bf16*, bf16*, bf16*, int, int, int, SeqTable,
+                       const DevBatch*, FrontArgs);
+        if (front)
+            kernel = dyn ? (narrow ? conv_vec_kernel<2, true, true> : conv_vec_kernel<4, true, true>)
+                         : (narrow ? conv_vec_kernel<2, false, true> : conv_vec_kernel<4, false, true>);
+        else
+            kernel = dyn ? (narrow ? conv_vec_kernel<2, true, false> : conv_vec_kernel<4, true, false>)
+                         : (narrow ? conv_vec_kernel<2, false, false> : conv_vec_kernel<4, false, false>);
+        // the front end adds one gate CTA per run of rows
         return launch_pdl(kernel,
-                          dim3((unsigned)groups, (T + run - 1) / run), dim3(128), 0, st,
+                          dim3((unsigned)(groups + (front ? 1 : 0)), (T + run - 1) / run), dim3(128), 0, st,
                           static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
                           static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
-                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, run, tab, dyn);
+                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, run, tab, dyn, fr);
     } else {
-        if (dyn) return cudaErrorInvalidValue;  // the capacity path needs the vector kernel
+        // the capacity path and the front end need the vector kernel
+        if (dyn || front) return cudaErrorInvalidValue;
         const int ch = 2 * key_dim + value_dim;
         conv_scalar_kernel<<<dim3((ch + 127) / 128, rows), 128, 0, st>>>(
             static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld, static_cast<const bf16*>(w),
@@ -372,7 +442,88 @@ extern "C" int cs1_gdn_gates(const void* b, const void* a, int ld, const void* A
                       static_cast<const DevBatch*>(nullptr));
 }
 
+namespace s1 {
+namespace {
+int front_args(FrontArgs& fr, float* rnorm_q, float* rnorm_k, const void* b, const void* a, const void* A_log,
+               const void* dt_bias, void* beta, float* g, int H) {
+    if (!rnorm_q || !rnorm_k || !b || !a || !A_log || !dt_bias || !beta || !g || H <= 0) return cudaErrorInvalidValue;
+    fr.rnq = rnorm_q;
+    fr.rnk = rnorm_k;
+    fr.b = static_cast<const bf16*>(b);
+    fr.a = static_cast<const bf16*>(a);
+    fr.A_log = static_cast<const bf16*>(A_log);
+    fr.dt_bias = static_cast<const bf16*>(dt_bias);
+    fr.beta = static_cast<bf16*>(beta);
+    fr.g = g;
+    fr.H = H;
+    return cudaSuccess;
+}
+}  // namespace
+}  // namespace s1
+
+extern "C" int cs1_gdn_front_batch(const void* qkv, const void* history, int ld, const void* w, void* q, void* k,
+                                   void* v, float* rnorm_q, float* rnorm_k, const void* b, const void* a,
+                                   const void* A_log, const void* dt_bias, void* beta, float* g, int H,
+                                   const size_t* lengths, size_t count, int key_dim, int value_dim, void* stream) {
+    SeqTable tab;
+    FrontArgs fr{};
+    if (!qkv || !w || !q || !k || !v || key_dim <= 0 || key_dim % 128 || value_dim <= 0 ||
+        ld < 2 * key_dim + value_dim || ld < H || !make_table(tab, lengths, count) ||
+        front_args(fr, rnorm_q, rnorm_k, b, a, A_log, dt_bias, beta, g, H) != cudaSuccess)
+        return cudaErrorInvalidValue;
+    return conv_launch(qkv, history, ld, w, q, k, v, tab, key_dim, value_dim, nullptr,
+                       static_cast<cudaStream_t>(stream), &fr);
+}
+
 // ---- capacity path ----
+
+extern "C" int cs1_gdn_front_dyn(const void* qkv, const void* history, int ld, const void* w, void* q, void* k,
+                                 void* v, float* rnorm_q, float* rnorm_k, const void* b, const void* a,
+                                 const void* A_log, const void* dt_bias, void* beta, float* g, int H, int cap_rows,
+                                 int cap_seqs, int key_dim, int value_dim, const void* desc, void* stream) {
+    FrontArgs fr{};
+    if (!desc || !qkv || !w || !q || !k || !v || key_dim <= 0 || key_dim % 128 || value_dim <= 0 ||
+        ld < 2 * key_dim + value_dim || ld < H || cap_rows <= 0 || cap_seqs <= 0 || cap_seqs > MAX_SEQS ||
+        front_args(fr, rnorm_q, rnorm_k, b, a, A_log, dt_bias, beta, g, H) != cudaSuccess)
+        return cudaErrorInvalidValue;
+    SeqTable cap;  // launch geometry only
+    memset(&cap, 0, sizeof(cap));
+    cap.count = 1;
+    cap.offset[1] = cap_rows;
+    return conv_launch(qkv, history, ld, w, q, k, v, cap, key_dim, value_dim, static_cast<const DevBatch*>(desc),
+                       static_cast<cudaStream_t>(stream), &fr);
+}
+
+namespace s1 {
+namespace {
+// Zero `width` bytes (a multiple of 16) of rows [rows, min(rows + margin, cap_rows)) of a
+// strided matrix, rows from the descriptor.
+__global__ void clear_tail_kernel(uint8_t* __restrict__ x, size_t ld, size_t width, int cap_rows, int margin,
+                                  const DevBatch* __restrict__ dyn) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int r0 = dyn->rows, r1 = min(r0 + margin, cap_rows);
+    const size_t packs = width / 16;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < (size_t)(r1 - r0) * packs;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = (size_t)r0 + i / packs, p = i % packs;
+        *reinterpret_cast<uint4*>(x + r * ld + p * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+}  // namespace
+}  // namespace s1
+
+extern "C" int cs1_clear_tail_dyn(void* x, size_t ld_bytes, size_t width_bytes, int cap_rows, int margin,
+                                  const void* desc, void* stream) {
+    if (!desc || !x || cap_rows < 0 || margin < 0 || width_bytes % 16 || ld_bytes % 16 || width_bytes > ld_bytes ||
+        !aligned16(x))
+        return cudaErrorInvalidValue;
+    if (cap_rows == 0 || margin == 0 || width_bytes == 0) return cudaSuccess;
+    const size_t n = (size_t)margin * (width_bytes / 16);
+    return launch_pdl(clear_tail_kernel, dim3(grid_for(n)), dim3(THREADS), 0, static_cast<cudaStream_t>(stream),
+                      static_cast<uint8_t*>(x), ld_bytes, width_bytes, cap_rows, margin,
+                      static_cast<const DevBatch*>(desc));
+}
 
 extern "C" size_t cs1_batch_desc_bytes(void) { return sizeof(DevBatch); }
 

@@ -1149,9 +1149,22 @@ int cs1_gdn_prefill_batch_x(const void* q, const void* k, const void* v, const f
                     static_cast<cudaStream_t>(stream));
 }
 
-int cs1_gdn_prefill_dyn(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
-                        int cap_rows, int cap_seqs, int H, int HK, float scale, const void* state_in,
-                        int state_stride, void* state_out, const void* desc, void* stream) {
+int cs1_gdn_prefill_batch_xn(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                             const float* rnorm_q, const float* rnorm_k, void* o, const size_t* lengths, size_t count,
+                             int H, int HK, float scale, const void* state_in, int state_stride, void* state_out,
+                             void* stream) {
+    SeqTable tab;
+    if (!rnorm_q || !rnorm_k || !make_table(tab, lengths, count) || (state_stride != 0 && state_stride != 1))
+        return cudaErrorInvalidValue;
+    const long stride = state_stride ? (long)H * 128 * 128 : 0;
+    return gdn::run_fused(q, k, v, g, beta, o, tab, H, HK, scale, state_in, stride, state_out,
+                          static_cast<cudaStream_t>(stream), nullptr, 0, rnorm_q, rnorm_k);
+}
+
+int cs1_gdn_prefill_dyn(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                        const float* rnorm_q, const float* rnorm_k, void* o, int cap_rows, int cap_seqs, int H, int HK,
+                        float scale, const void* state_in, int state_stride, void* state_out, const void* desc,
+                        void* stream) {
     if (!desc || cap_rows <= 0 || (state_stride != 0 && state_stride != 1)) return cudaErrorInvalidValue;
     SeqTable cap;  // tensor-map extents only
     memset(&cap, 0, sizeof(cap));
@@ -1159,7 +1172,8 @@ int cs1_gdn_prefill_dyn(const void* q, const void* k, const void* v, const float
     cap.offset[1] = cap_rows;
     const long stride = state_stride ? (long)H * 128 * 128 : 0;
     return gdn::run_fused(q, k, v, g, beta, o, cap, H, HK, scale, state_in, stride, state_out,
-                          static_cast<cudaStream_t>(stream), static_cast<const DevBatch*>(desc), cap_seqs);
+                          static_cast<cudaStream_t>(stream), static_cast<const DevBatch*>(desc), cap_seqs, rnorm_q,
+                          rnorm_k);
 }
 
 int cs1_gdn_prefill_batch_shared(const void* q, const void* k, const void* v, const float* g, const void* beta,

@@ -48,10 +48,12 @@ int run(const void* q, const void* k, const void* v, const float* g, const void*
         long s_in_stride, void* s_out, cudaStream_t st);
 // The fused kernel: preparation and scan of a (head, sequence) in one CTA (gdn_fused.cu).
 // On the capacity path (dyn non-null) `seqs` stands for the capacity (offset[count] =
-// cap_rows: tensor-map extents) and the grid covers cap_seqs sequences.
+// cap_rows: tensor-map extents) and the grid covers cap_seqs sequences. rnorm_q, rnorm_k:
+// the front end's inverse norms of q and k ([T, HK] float32), or both null (computed here).
 int run_fused(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
               const SeqTable& seqs, int H, int HK, float scale, const void* s_in, long s_in_stride, void* s_out,
-              cudaStream_t st, const DevBatch* dyn = nullptr, int cap_seqs = 0);
+              cudaStream_t st, const DevBatch* dyn = nullptr, int cap_seqs = 0, const float* rnorm_q = nullptr,
+              const float* rnorm_k = nullptr);
 // The two-kernel form with its tiles in a caller-provided (1024-byte aligned) workspace of
 // workspace_bytes (gdn.cu).
 int run_two_pass(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,

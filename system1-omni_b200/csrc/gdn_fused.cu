@@ -138,7 +138,8 @@ template <bool Dyn>
 __global__ void __launch_bounds__(THREADS, 1)
     gdn_fused(const __grid_constant__ Maps maps, const float* __restrict__ g, const bf16* __restrict__ beta,
               const __grid_constant__ SeqTable tab, bf16* __restrict__ o, int H, int HK, float scale,
-              const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out, const DevBatch* dyn) {
+              const float* __restrict__ s_in, long s_in_stride, float* __restrict__ s_out, const DevBatch* dyn,
+              const float* __restrict__ rnq, const float* __restrict__ rnk) {
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
@@ -335,13 +336,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         // Per chunk, ahead of the preparation: g and beta of the chunk (rows past the
         // sequence's end: 0), the sequential fp32 cumsum of g (the reference's order),
         // cum * log2(e), e^cum, e^{last - cum} and the decay e^{last}.
+        // With the front end's inverse norms (rnk, rnq: [T, HK]) it also fills the chunk's
+        // norm vectors (q's times the scale); rows past the sequence get 0.
         float gn[2] = {0.f, 0.f}, bn[2] = {0.f, 0.f};  // this lane's rows lane, lane + 32 of the next chunk
+        float kn[2] = {0.f, 0.f}, qn[2] = {0.f, 0.f};
         auto fetch = [&](int c) {
 #pragma unroll
             for (int i = 0; i < 2; i++) {
                 const int row = c * C + lane + 32 * i;
                 gn[i] = row < len ? g[(size_t)(start + row) * H + h] : 0.f;
                 bn[i] = row < len ? f32(beta[(size_t)(start + row) * H + h]) : 0.f;
+                if (rnk) {
+                    kn[i] = row < len ? rnk[(size_t)(start + row) * HK + hk] : 0.f;
+                    qn[i] = row < len ? rnq[(size_t)(start + row) * HK + hk] * scale : 0.f;
+                }
             }
         };
         fetch(0);
@@ -357,6 +365,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int i = 0; i < 2; i++) {
                 vs[VEC_G + lane + 32 * i] = gn[i];
                 vs[VEC_BET + lane + 32 * i] = bn[i];
+                if (rnk) {
+                    vs[VEC_KINV + lane + 32 * i] = kn[i];
+                    vs[VEC_QINV + lane + 32 * i] = qn[i];
+                }
             }
             if (c + 1 < NC) fetch(c + 1);  // in flight behind this chunk's arithmetic
             __syncwarp();
@@ -609,28 +621,38 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (ok) {
                 const int r = pt >> 2, qq = pt & 3, b = qq >> 1, ch0 = (qq & 1) * 4;
                 Pack8 kr[4];
-                float ks = 0.f, qs = 0.f;
+                float kv;
+                if (rnk) {  // the front end's norms, already in the slot
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    float kx[8], qx[8];
-                    kr[i] = *reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(r, ch0 + i));
-                    unpack8(kr[i], kx);
-                    unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + BOX + sw128_offset(r, ch0 + i)), qx);
+                    for (int i = 0; i < 4; i++)
+                        kr[i] = *reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(r, ch0 + i));
+                    kv = kinv[r];
+                } else {
+                    float ks = 0.f, qs = 0.f;
 #pragma unroll
-                    for (int e = 0; e < 8; e++) {
-                        ks = fmaf(kx[e], kx[e], ks);
-                        qs = fmaf(qx[e], qx[e], qs);
+                    for (int i = 0; i < 4; i++) {
+                        float kx[8], qx[8];
+                        kr[i] = *reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + sw128_offset(r, ch0 + i));
+                        unpack8(kr[i], kx);
+                        unpack8(*reinterpret_cast<const Pack8*>(kqp + b * 2 * BOX + BOX + sw128_offset(r, ch0 + i)),
+                                qx);
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            ks = fmaf(kx[e], kx[e], ks);
+                            qs = fmaf(qx[e], qx[e], qs);
+                        }
+                    }
+                    ks += __shfl_xor_sync(0xffffffffu, ks, 1);
+                    qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+                    ks += __shfl_xor_sync(0xffffffffu, ks, 2);
+                    qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+                    kv = rsqrtf(ks + 1e-6f);
+                    if (qq == 0) {
+                        kinv[r] = kv;
+                        qinv[r] = rsqrtf(qs + 1e-6f) * scale;
                     }
                 }
-                ks += __shfl_xor_sync(0xffffffffu, ks, 1);
-                qs += __shfl_xor_sync(0xffffffffu, qs, 1);
-                ks += __shfl_xor_sync(0xffffffffu, ks, 2);
-                qs += __shfl_xor_sync(0xffffffffu, qs, 2);
-                const float kv = rsqrtf(ks + 1e-6f), ec = ecum[r];
-                if (qq == 0) {
-                    kinv[r] = kv;
-                    qinv[r] = rsqrtf(qs + 1e-6f) * scale;
-                }
+                const float ec = ecum[r];
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     float f[8];
@@ -844,11 +866,12 @@ namespace gdn {
 // for every sequence).
 int run_fused(const void* q, const void* k, const void* v, const float* g, const void* beta, void* o,
               const SeqTable& seqs, int H, int HK, float scale, const void* s_in, long s_in_stride, void* s_out,
-              cudaStream_t st, const DevBatch* dyn, int cap_seqs) {
+              cudaStream_t st, const DevBatch* dyn, int cap_seqs, const float* rnorm_q, const float* rnorm_k) {
     using namespace gdnf;
     if (!q || !k || !v || !g || !beta || !o || H <= 0 || HK <= 0 || H % HK || H > 65535 || seqs.count > 65535)
         return cudaErrorInvalidValue;
     if (dyn && (cap_seqs <= 0 || cap_seqs > MAX_SEQS)) return cudaErrorInvalidValue;
+    if ((rnorm_q == nullptr) != (rnorm_k == nullptr)) return cudaErrorInvalidValue;
     if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o)) return cudaErrorInvalidValue;
     static const cudaError_t configured =
         cudaFuncSetAttribute(gdn_fused<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
@@ -864,7 +887,7 @@ int run_fused(const void* q, const void* k, const void* v, const float* g, const
     if (e) return e;
     return launch_pdl(dyn ? gdn_fused<true> : gdn_fused<false>, dim3(H, dyn ? cap_seqs : seqs.count), dim3(THREADS), SMEM, st, maps, g,
                       static_cast<const bf16*>(beta), seqs, static_cast<bf16*>(o), H, HK, scale,
-                      static_cast<const float*>(s_in), s_in_stride, static_cast<float*>(s_out), dyn);
+                      static_cast<const float*>(s_in), s_in_stride, static_cast<float*>(s_out), dyn, rnorm_q, rnorm_k);
 }
 
 }  // namespace gdn

@@ -87,6 +87,14 @@ struct Api {
                                         void*) = nullptr;
     int (*attention_gated_batch)(const void*, const void*, const void*, int, const void*, void*, const size_t*,
                                  size_t, int, int, int, float, void*) = nullptr;
+    // the GDN front end (conv + SiLU + q/k inverse norms + gates in one launch) and the
+    // prefill that takes its norms
+    int (*gdn_front_batch)(const void*, const void*, int, const void*, void*, void*, void*, float*, float*,
+                           const void*, const void*, const void*, const void*, void*, float*, int, const size_t*,
+                           size_t, int, int, void*) = nullptr;
+    int (*gdn_prefill_batch_xn)(const void*, const void*, const void*, const float*, const void*, const float*,
+                                const float*, void*, const size_t*, size_t, int, int, float, const void*, int, void*,
+                                void*) = nullptr;
     // most sequences one batched launch takes: 256 in this build, 16 in the reference (ops.h:83-94)
     int max_batch = 16;
     int (*gemm_residual)(void*, const void*, const void*, void*, int, int, int, int, void*) = nullptr;
@@ -102,21 +110,22 @@ struct Api {
     int (*gated_rms_norm_dyn)(const void*, const void*, int, const void*, void*, int, int, int, float, const void*,
                               void*) = nullptr;
     int (*gemm_dyn)(void*, const void*, const void*, void*, int, int, int, int, int, const void*, void*) = nullptr;
-    int (*gdn_conv_dyn)(const void*, const void*, int, const void*, void*, void*, void*, int, int, int, int,
-                        const void*, void*) = nullptr;
-    int (*gdn_gates_dyn)(const void*, const void*, int, const void*, const void*, void*, float*, int, int, const void*,
+    int (*gdn_prefill_dyn)(const void*, const void*, const void*, const float*, const void*, const float*,
+                           const float*, void*, int, int, int, int, float, const void*, int, void*, const void*,
+                           void*) = nullptr;
+    int (*gdn_front_dyn)(const void*, const void*, int, const void*, void*, void*, void*, float*, float*, const void*,
+                         const void*, const void*, const void*, void*, float*, int, int, int, int, int, const void*,
                          void*) = nullptr;
-    int (*gdn_prefill_dyn)(const void*, const void*, const void*, const float*, const void*, void*, int, int, int, int,
-                           float, const void*, int, void*, const void*, void*) = nullptr;
     int (*attn_prep_dyn)(const void*, const void*, int, const void*, const void*, const void*, const void*, void*,
                          void*, void*, int, int, int, int, int, float, const void*, void*) = nullptr;
     int (*attention_dyn)(const void*, const void*, const void*, int, const void*, void*, const void*, const void*, int,
                          int, int, int, int, int, float, const void*, void*) = nullptr;
     int (*head_score_dyn)(const void*, int, const int32_t*, int, const float*, const float*, int, int, float*,
                           const void*, void*) = nullptr;
+    int (*clear_tail_dyn)(void*, size_t, size_t, int, int, const void*, void*) = nullptr;
     bool has_dyn() const {
-        return batch_desc_bytes && batch_desc_pack && embed_dyn && rms_norm_dyn && gated_rms_norm_dyn && gemm_dyn &&
-               gdn_conv_dyn && gdn_gates_dyn && gdn_prefill_dyn && attn_prep_dyn && attention_dyn && head_score_dyn;
+        return batch_desc_bytes && batch_desc_pack && clear_tail_dyn && gdn_front_dyn && embed_dyn && rms_norm_dyn &&
+               gated_rms_norm_dyn && gemm_dyn && gdn_prefill_dyn && attn_prep_dyn && attention_dyn && head_score_dyn;
     }
 };
 
@@ -203,12 +212,14 @@ bool load_api(const char* spec, Api& a, std::string& err) {
     bind(h, "cs1_rms_norm_dyn", a.rms_norm_dyn, false, err);
     bind(h, "cs1_gated_rms_norm_dyn", a.gated_rms_norm_dyn, false, err);
     bind(h, "cs1_gemm_dyn", a.gemm_dyn, false, err);
-    bind(h, "cs1_gdn_conv_dyn", a.gdn_conv_dyn, false, err);
-    bind(h, "cs1_gdn_gates_dyn", a.gdn_gates_dyn, false, err);
     bind(h, "cs1_gdn_prefill_dyn", a.gdn_prefill_dyn, false, err);
     bind(h, "cs1_attn_prep_dyn", a.attn_prep_dyn, false, err);
     bind(h, "cs1_attention_dyn", a.attention_dyn, false, err);
     bind(h, "cs1_head_score_dyn", a.head_score_dyn, false, err);
+    bind(h, "cs1_clear_tail_dyn", a.clear_tail_dyn, false, err);
+    bind(h, "cs1_gdn_front_dyn", a.gdn_front_dyn, false, err);
+    bind(h, "cs1_gdn_front_batch", a.gdn_front_batch, false, err);
+    bind(h, "cs1_gdn_prefill_batch_xn", a.gdn_prefill_batch_xn, false, err);
     a.max_batch = a.gdn_prefill_batch_x ? 256 : 16;
     if (!a.fill_random && !aux.empty()) {
         void* ah = dlopen(aux.c_str(), RTLD_NOW | RTLD_LOCAL);
@@ -306,7 +317,7 @@ struct Model {
     // scratch
     uint8_t* scratch = nullptr;
     size_t s_ids, s_cos, s_sin, s_res, s_x, s_delta, s_gdn_in, s_lq, s_lk, s_lv, s_beta, s_g, s_lo, s_ln, s_attn_in,
-        s_aq, s_agate, s_ak, s_ao, s_gate_up, s_act, s_rows, s_logits, s_ws;
+        s_aq, s_agate, s_ak, s_ao, s_gate_up, s_act, s_rows, s_logits, s_ws, s_rnq, s_rnk;
     size_t ws_bytes = 0;
     // shared-prefix buffers (allocated on first use)
     uint8_t* prefix_buf = nullptr;
@@ -440,6 +451,8 @@ int layout_scratch(Model* m) {
     m->s_lv = t(T * m->vd * 2);
     m->s_beta = t(T * c.lin_v_heads * 2);
     m->s_g = t(T * c.lin_v_heads * 4);
+    m->s_rnq = t(T * c.lin_k_heads * 4);  // the front end's inverse norms of q and k
+    m->s_rnk = t(T * c.lin_k_heads * 4);
     m->s_lo = t(T * m->vd * 2);
     m->s_ln = t(T * m->vd * 2);
     m->s_attn_in = t(T * m->attn_in * 2);
@@ -545,6 +558,22 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
            : m->api.rms_norm(m->S(m->s_res), m->W(m->layers[first].input_norm), m->S(m->s_x), T, c.hidden, c.eps,
                              m->stream),
        "input norm");
+    if (dyn) {
+        // Rows just past the batch that a last GDN chunk or attention key tile reads (masked
+        // there, but they must be finite): zero, as the host-length launches' tensor-map
+        // bounds give them. Nothing on the capacity path writes past the batch afterwards.
+        const int margin = 256;
+        const struct { size_t off; size_t ld, width; } tails[] = {
+            {m->s_lq, (size_t)m->kd * 2, (size_t)m->kd * 2},
+            {m->s_lk, (size_t)m->kd * 2, (size_t)m->kd * 2},
+            {m->s_lv, (size_t)m->vd * 2, (size_t)m->vd * 2},
+            {m->s_ak, (size_t)m->kvd * 2, (size_t)m->kvd * 2},
+            {m->s_attn_in + (size_t)(m->attn_q + m->kvd) * 2, (size_t)m->attn_in * 2, (size_t)m->kvd * 2}};
+        for (const auto& t : tails) {
+            m->launches++;
+            CK(m->api.clear_tail_dyn(m->S(t.off), t.ld, t.width, TL, margin, m->desc, m->stream), "clear tail rows");
+        }
+    }
     int gi = 0, ai = 0;  // index of the layer among the GDN / attention layers (prefix buffers)
     for (int li = 0; li < first; li++) (m->types[li] == 0 ? gi : ai)++;
     for (int li = first; li < last; li++) {
@@ -560,11 +589,26 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
                 if (rc) return rc;
             }
             const void* hist = suffix ? m->prefix_buf + m->p_tail[gi] : nullptr;
+            const size_t zoff = (size_t)m->conv * 2, boff = zoff + (size_t)m->vd * 2,
+                         aoff = boff + (size_t)c.lin_v_heads * 2;
+            float* rnq = reinterpret_cast<float*>(m->S(m->s_rnq));
+            float* rnk = reinterpret_cast<float*>(m->S(m->s_rnk));
+            // the fused front end: conv + SiLU, q/k inverse norms and gates in one launch
+            const bool front = dyn || (m->api.gdn_front_batch && m->api.gdn_prefill_batch_xn && n <= m->api.max_batch);
             if (dyn) {
                 m->launches++;
-                CK(m->api.gdn_conv_dyn(gin, hist, ld, m->W(L.conv), m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv), TL,
-                                       b.cap_seqs, m->kd, m->vd, m->desc, m->stream),
-                   "gdn conv");
+                CK(m->api.gdn_front_dyn(gin, hist, ld, m->W(L.conv), m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv), rnq,
+                                        rnk, gin + boff, gin + aoff, m->W(L.A_log), m->W(L.dt_bias), m->S(m->s_beta),
+                                        reinterpret_cast<float*>(m->S(m->s_g)), c.lin_v_heads, TL, b.cap_seqs, m->kd,
+                                        m->vd, m->desc, m->stream),
+                   "gdn front end");
+            } else if (front) {
+                m->launches++;
+                CK(m->api.gdn_front_batch(gin, hist, ld, m->W(L.conv), m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv), rnq,
+                                          rnk, gin + boff, gin + aoff, m->W(L.A_log), m->W(L.dt_bias),
+                                          m->S(m->s_beta), reinterpret_cast<float*>(m->S(m->s_g)), c.lin_v_heads,
+                                          b.lengths.data(), n, m->kd, m->vd, m->stream),
+                   "gdn front end");
             } else if (m->api.gdn_conv_batch && n <= m->api.max_batch) {
                 m->launches++;
                 CK(m->api.gdn_conv_batch(gin, hist, ld, m->W(L.conv), m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
@@ -588,15 +632,12 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
                     }
                 }
             }
-            const size_t zoff = (size_t)m->conv * 2, boff = zoff + (size_t)m->vd * 2,
-                         aoff = boff + (size_t)c.lin_v_heads * 2;
-            m->launches++;
-            CK(dyn ? m->api.gdn_gates_dyn(gin + boff, gin + aoff, ld, m->W(L.A_log), m->W(L.dt_bias), m->S(m->s_beta),
-                                          reinterpret_cast<float*>(m->S(m->s_g)), TL, c.lin_v_heads, m->desc,
-                                          m->stream)
-                   : m->api.gdn_gates(gin + boff, gin + aoff, ld, m->W(L.A_log), m->W(L.dt_bias), m->S(m->s_beta),
-                                      reinterpret_cast<float*>(m->S(m->s_g)), T, c.lin_v_heads, m->stream),
-               "gdn gates");
+            if (!front) {
+                m->launches++;
+                CK(m->api.gdn_gates(gin + boff, gin + aoff, ld, m->W(L.A_log), m->W(L.dt_bias), m->S(m->s_beta),
+                                    reinterpret_cast<float*>(m->S(m->s_g)), T, c.lin_v_heads, m->stream),
+                   "gdn gates");
+            }
             float* ws = reinterpret_cast<float*>(m->S(m->s_ws));
             const size_t state_bytes = (size_t)c.lin_v_heads * c.lin_k_dim * c.lin_v_dim * 4;
             if (cp_recv) {  // the previous piece's final state of this layer
@@ -608,9 +649,16 @@ int run_layers(Model* m, const Batch& b, int first = 0, int last = -1) {
             if (dyn) {
                 m->launches++;
                 CK(m->api.gdn_prefill_dyn(m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
-                                          reinterpret_cast<const float*>(m->S(m->s_g)), m->S(m->s_beta),
+                                          reinterpret_cast<const float*>(m->S(m->s_g)), m->S(m->s_beta), rnq, rnk,
                                           m->S(m->s_lo), TL, b.cap_seqs, c.lin_v_heads, c.lin_k_heads, gdn_scale, s_in,
                                           0, nullptr, m->desc, m->stream),
+                   "gdn prefill");
+            } else if (front) {
+                m->launches++;
+                CK(m->api.gdn_prefill_batch_xn(m->S(m->s_lq), m->S(m->s_lk), m->S(m->s_lv),
+                                               reinterpret_cast<const float*>(m->S(m->s_g)), m->S(m->s_beta), rnq, rnk,
+                                               m->S(m->s_lo), b.lengths.data(), n, c.lin_v_heads, c.lin_k_heads,
+                                               gdn_scale, s_in, 0, s_out, m->stream),
                    "gdn prefill");
             } else if (m->api.gdn_prefill_batch_x && n <= m->api.max_batch) {
                 m->launches += 2;
@@ -817,7 +865,9 @@ int run_head(Model* m, const Batch& b) {
 
 // Upload ids, per-row rotary tables and the last-token rows of a batch; on the capacity
 // path (s1_model_set_dynamic) also its descriptor, after choosing the capacities: rows
-// rounded up to a power of two (at least 64, at most the model's), sequences likewise.
+// rounded up to an eighth of their power-of-two octave (a multiple of 64, at most the
+// model's: at most 12.5% of launched rows idle, eight capacities per octave), sequences
+// to a power of two.
 int stage_inputs(Model* m, const int32_t* ids, Batch& b) {
     // Every id indexes the embedding table, so one out of range would read past it on the
     // device: the batch is refused before anything is copied or launched.
@@ -847,9 +897,10 @@ int stage_inputs(Model* m, const int32_t* ids, Batch& b) {
     CK(m->api.upload(m->S(m->s_rows), rows.data(), rows.size() * 4, m->stream), "upload rows");
     b.dyn = m->dynamic && m->desc && !b.capture && !b.cp && n <= 256;
     if (b.dyn) {
-        int r = 64;
-        while (r < (int)b.rows) r <<= 1;
-        b.cap_rows = std::min(r, m->cap_tokens);
+        int octave = 64;
+        while (octave * 2 <= (int)b.rows) octave <<= 1;
+        const int step = std::max(64, octave / 8);
+        b.cap_rows = std::min(((int)b.rows + step - 1) / step * step, m->cap_tokens);
         int q = 1;
         while (q < n) q <<= 1;
         b.cap_seqs = std::min(q, std::min(m->cap_seqs, 256));

@@ -89,13 +89,17 @@ SIGNATURES = {
     "cs1_batch_desc_bytes": (Z, []),
     "cs1_batch_desc_pack": (I, [P, Z, P, Z]),
     "cs1_embed_dyn": (I, [P, P, P, I, I, P, P]),
+    "cs1_clear_tail_dyn": (I, [P, Z, Z, I, I, P, P]),
     "cs1_rms_norm_dyn": (I, [P, P, P, I, I, F, P, P]),
     "cs1_add_rms_norm_dyn": (I, [P, P, P, P, I, I, F, P, P]),
     "cs1_gated_rms_norm_dyn": (I, [P, P, I, P, P, I, I, I, F, P, P]),
     "cs1_gemm_dyn": (I, [P, P, P, P, I, I, I, I, I, P, P]),
     "cs1_gdn_conv_dyn": (I, [P, P, I, P, P, P, P, I, I, I, I, P, P]),
     "cs1_gdn_gates_dyn": (I, [P, P, I, P, P, P, P, I, I, P, P]),
-    "cs1_gdn_prefill_dyn": (I, [P, P, P, P, P, P, I, I, I, I, F, P, I, P, P, P]),
+    "cs1_gdn_prefill_dyn": (I, [P, P, P, P, P, P, P, P, I, I, I, I, F, P, I, P, P, P]),
+    "cs1_gdn_front_dyn": (I, [P, P, I, P, P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, P, P]),
+    "cs1_gdn_front_batch": (I, [P, P, I, P, P, P, P, P, P, P, P, P, P, P, P, I, P, Z, I, I, P]),
+    "cs1_gdn_prefill_batch_xn": (I, [P, P, P, P, P, P, P, P, P, Z, I, I, F, P, I, P, P]),
     "cs1_attn_prep_dyn": (I, [P, P, I, P, P, P, P, P, P, P, I, I, I, I, I, F, P, P]),
     "cs1_attention_dyn": (I, [P, P, P, I, P, P, P, P, I, I, I, I, I, I, F, P, P]),
     "cs1_head_score_dyn": (I, [P, I, P, I, P, P, I, I, P, P, P]),

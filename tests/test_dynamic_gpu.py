@@ -170,11 +170,59 @@ def test_gdn_dyn_equals_batch_x(cs1, stream, state):
                                            oa.data_ptr(), ws.data_ptr(), 256, arr.ctypes.data, len(LENS), H, HK,
                                            ctypes.c_float(128 ** -0.5), sp, 0, None, stream) == 0
     assert cs1.raw.cs1_gdn_prefill_dyn(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
-                                       ob.data_ptr(), CAP_ROWS, CAP_SEQS, H, HK, ctypes.c_float(128 ** -0.5), sp, 0,
-                                       None, d.data_ptr(), stream) == 0
+                                       None, None, ob.data_ptr(), CAP_ROWS, CAP_SEQS, H, HK,
+                                       ctypes.c_float(128 ** -0.5), sp, 0, None, d.data_ptr(), stream) == 0
     torch.cuda.synchronize()
     assert torch.equal(oa[:T], ob[:T])
+    # with inverse norms handed in (as the front end computes them): the same bits as the
+    # host-length entry point given the same norms
+    kf = torch.from_numpy(np.asarray(k, np.float32)).reshape(CAP_ROWS, HK, 128)
+    qf = torch.from_numpy(np.asarray(q, np.float32)).reshape(CAP_ROWS, HK, 128)
+    rnk = (1.0 / torch.sqrt((kf.double() ** 2).sum(-1) + 1e-6)).float().cuda().contiguous()
+    rnq = (1.0 / torch.sqrt((qf.double() ** 2).sum(-1) + 1e-6)).float().cuda().contiguous()
+    oc, od = empty_bf16(CAP_ROWS, H, 128), empty_bf16(CAP_ROWS, H, 128)
+    assert cs1.raw.cs1_gdn_prefill_batch_xn(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
+                                            rnq.data_ptr(), rnk.data_ptr(), oc.data_ptr(), arr.ctypes.data, len(LENS),
+                                            H, HK, ctypes.c_float(128 ** -0.5), sp, 0, None, stream) == 0
+    assert cs1.raw.cs1_gdn_prefill_dyn(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), dg.data_ptr(), db.data_ptr(),
+                                       rnq.data_ptr(), rnk.data_ptr(), od.data_ptr(), CAP_ROWS, CAP_SEQS, H, HK,
+                                       ctypes.c_float(128 ** -0.5), sp, 0, None, d.data_ptr(), stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(oc[:T], od[:T])
+    # and within the GDN gate of the prefill's own norms
+    a, c = host(oa[:T]), host(oc[:T])
+    assert np.abs(a - c).max() <= 2e-2 * np.abs(a).max()
     assert cs1.cs1_fault_status(1) == 0
+
+
+@pytest.mark.parametrize("with_history", [False, True])
+def test_front_dyn_equals_front_batch(cs1, stream, with_history):
+    T, kd, vd, H = sum(LENS), 2048, 4096, 32
+    ld = 2 * kd + vd + 2 * H + 64
+    qkv, w = _rand((CAP_ROWS, ld), 25), _rand((2 * kd + vd, 4), 26, 0.3)
+    A_log, dt = _rand((H,), 27, 0.5), _rand((H,), 28, 0.5)
+    hist = _rand((3, ld), 29) if with_history else None
+    hp = hist.data_ptr() if hist is not None else None
+    d = _desc(cs1, LENS)
+    bptr = qkv.data_ptr() + (2 * kd + vd) * 2
+    outs = []
+    for dyn in (False, True):
+        q, k, v = empty_bf16(CAP_ROWS, kd), empty_bf16(CAP_ROWS, kd), empty_bf16(CAP_ROWS, vd)
+        rq = torch.empty(CAP_ROWS, kd // 128, device="cuda")
+        rk = torch.empty(CAP_ROWS, kd // 128, device="cuda")
+        beta, g = empty_bf16(CAP_ROWS, H), torch.empty(CAP_ROWS, H, device="cuda")
+        common = (qkv.data_ptr(), hp, ld, w.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), rq.data_ptr(),
+                  rk.data_ptr(), bptr, bptr + H * 2, A_log.data_ptr(), dt.data_ptr(), beta.data_ptr(), g.data_ptr(), H)
+        if dyn:
+            rc = cs1.raw.cs1_gdn_front_dyn(*common, CAP_ROWS, CAP_SEQS, kd, vd, d.data_ptr(), stream)
+        else:
+            arr = np.asarray(LENS, dtype=np.uintp)
+            rc = cs1.raw.cs1_gdn_front_batch(*common, arr.ctypes.data, len(LENS), kd, vd, stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        outs.append([t[:T].clone() for t in (q, k, v, rq, rk, beta, g)])
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("prefix", [0, 128])
@@ -259,8 +307,8 @@ def tiny_pair(cs1):
 def test_one_graph_per_capacity_serves_every_length_vector(tiny_pair):
     cfg, ref, dyn = tiny_pair
     rng = np.random.default_rng(11)
-    # every batch below has 129..256 rows and 3..4 sequences: one capacity (256 rows, 4 sequences)
-    batches = [[100, 60, 7], [1, 64, 65, 70], [130, 1, 1, 2], [200, 30, 20], [64, 64, 64, 64]]
+    # every batch below has 193..256 rows and 3..4 sequences: one capacity (256 rows, 4 sequences)
+    batches = [[100, 60, 40], [1, 64, 65, 70], [130, 60, 1, 2], [200, 30, 20], [64, 64, 64, 64]]
     before = dyn.graph_count
     for lens in batches:
         seqs = [rng.integers(0, cfg.vocab, n).astype(np.int32) for n in lens]
