@@ -26,7 +26,7 @@ CUDA_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompil
 
 CU_SOURCES = ["runtime.cu", "norm.cu", "elementwise.cu", "gemm.cu", "attention.cu", "gdn.cu",
               "head.cu", "gdn_noalloc.cu", "gdn_fused.cu"]
-CPP_SOURCES = ["model.cpp", "checkpoint.cpp"]
+CPP_SOURCES = ["model.cpp", "checkpoint.cpp", "tokenizer.cpp", "processing.cpp"]
 
 
 def _newer(target, deps):

@@ -35,7 +35,8 @@ def test_cs1_library_exports_every_declared_symbol():
 
 def test_model_library_exports_every_declared_symbol():
     from s1omni import lib_path
-    names = _declared("s1_model.h")
+    names = _declared("s1_model.h") + _declared("s1_processing.h")
+    assert "s1_processor_prepare" in names and "s1_tokenizer_encode" in names
     exported = _exported(lib_path("libs1_model.so"))
     missing = [n for n in names if n not in exported]
     assert not missing, missing
