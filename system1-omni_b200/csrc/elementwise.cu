@@ -170,6 +170,9 @@ __global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_k
     // rows in batches of 8: all loads of a batch are in flight before the first is used
     for (int tb = t_begin; tb < t_end; tb += 8) {
         P raw[8];
+        float ss8[8];  // Front: this thread's part of each row's sum of squares
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss8[i] = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; i++)
             if (tb + i < t_end) raw[i] = ld(col + (size_t)(tb + i) * ld_);
@@ -197,24 +200,11 @@ __global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_k
             }
             *reinterpret_cast<P*>(dst + (size_t)t * dst_ld) = out;
             if constexpr (Front) {
-                // q and k packs: a head is 128 / CH consecutive lanes of one warp (heads start on
-                // pack multiples of 128 / CH), so the branch and the shuffles are warp-uniform
-                constexpr int LANES = 128 / CH;
-                if (c < 2 * key_packs) {
-                    float ss = 0.f;
 #pragma unroll
-                    for (int p = 0; p < NP; p++) {
-                        const float2 yy = __bfloat1622float2(out.h[p]);
-                        ss = fmaf(yy.x, yy.x, ss);
-                        ss = fmaf(yy.y, yy.y, ss);
-                    }
-#pragma unroll
-                    for (int o = LANES / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-                    if ((threadIdx.x & (LANES - 1)) == 0) {
-                        const int HK = key_packs / LANES, head = c / LANES;
-                        float* dn = head < HK ? fr.rnq : fr.rnk;
-                        dn[(size_t)t * HK + (head < HK ? head : head - HK)] = rsqrtf(ss + 1e-6f);
-                    }
+                for (int p = 0; p < NP; p++) {
+                    const float2 yy = __bfloat1622float2(out.h[p]);
+                    ss8[i] = fmaf(yy.x, yy.x, ss8[i]);
+                    ss8[i] = fmaf(yy.y, yy.y, ss8[i]);
                 }
             }
 #pragma unroll
@@ -222,6 +212,44 @@ __global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_k
                 x1[p] = x2[p];
                 x2[p] = x3[p];
                 x3[p] = x0[p];
+            }
+        }
+        if constexpr (Front) {
+            // q and k packs: a head is LANES = 128 / CH consecutive lanes of one warp (heads start
+            // on pack multiples of LANES), so the branch and the shuffles are warp-uniform. The
+            // eight rows' sums are reduced together: three exchange steps halve the values a lane
+            // holds (lane bit LANES/2 -> rows +4, LANES/4 -> +2, LANES/8 -> +1), then plain steps
+            // finish each sum; lanes whose bits below LANES/8 are 0 hold one row's total.
+            constexpr int LANES = 128 / CH;
+            if (c < 2 * key_packs) {
+                const int lane = threadIdx.x & 31;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const bool hi = lane & (LANES / 2);
+                    const float send = hi ? ss8[k] : ss8[k + 4], keep = hi ? ss8[k + 4] : ss8[k];
+                    ss8[k] = keep + __shfl_xor_sync(0xffffffffu, send, LANES / 2);
+                }
+#pragma unroll
+                for (int k = 0; k < 2; k++) {
+                    const bool hi = lane & (LANES / 4);
+                    const float send = hi ? ss8[k] : ss8[k + 2], keep = hi ? ss8[k + 2] : ss8[k];
+                    ss8[k] = keep + __shfl_xor_sync(0xffffffffu, send, LANES / 4);
+                }
+                {
+                    const bool hi = lane & (LANES / 8);
+                    const float send = hi ? ss8[0] : ss8[1], keep = hi ? ss8[1] : ss8[0];
+                    ss8[0] = keep + __shfl_xor_sync(0xffffffffu, send, LANES / 8);
+                }
+#pragma unroll
+                for (int o = LANES / 16; o > 0; o >>= 1) ss8[0] += __shfl_xor_sync(0xffffffffu, ss8[0], o);
+                const int row = ((lane & (LANES / 2)) ? 4 : 0) + ((lane & (LANES / 4)) ? 2 : 0) +
+                                ((lane & (LANES / 8)) ? 1 : 0);
+                const int t = tb + row;
+                if ((lane & (LANES / 8 - 1)) == 0 && t < t_end) {
+                    const int HK = key_packs / LANES, head = c / LANES;
+                    float* dn = head < HK ? fr.rnq : fr.rnk;
+                    dn[(size_t)t * HK + (head < HK ? head : head - HK)] = rsqrtf(ss8[0] + 1e-6f);
+                }
             }
         }
     }

@@ -11,6 +11,7 @@ tensors exceed L2 (126 MB) at the default 29,122 tokens. `--once` calls every op
 (for a profiler capture). Prints one JSON line per op.
 """
 import argparse
+import ctypes
 import json
 import os
 
@@ -72,12 +73,24 @@ def main():
     I_ = 17408
     gu = rnd(T, 2 * I_)
     act = torch.empty(T, I_, device=dev, dtype=bf)
+    rnq = torch.empty(T, HK, device=dev)
+    rnk = torch.empty(T, HK, device=dev)
+    A_log, dt_bias = rnd(HV, scale=0.5), rnd(HV, scale=0.5)
+    beta = torch.empty(T, HV, device=dev, dtype=bf)
+    gf = torch.empty(T, HV, device=dev)
+    lens = (ctypes.c_size_t * 1)(T)
+    boff = 2 * KEY + 2 * VAL
 
     ops = {
         "rms_norm": (lambda: lib.cs1_rms_norm(x, w, out, T, H, 1e-6, st), T * H * 2 * 2 + H * 2),
         "add_rms_norm": (lambda: lib.cs1_add_rms_norm(res, x, w, out, T, H, 1e-6, st), T * H * 2 * 4 + H * 2),
         "gdn_conv": (lambda: lib.cs1_gdn_conv(gdn_in, GDN_IN, conv_w, q, k, v, T, KEY, VAL, st),
                      T * (2 * KEY + VAL) * 2 * 2 + (2 * KEY + VAL) * 8),
+        # the fused front end: conv + SiLU, q/k inverse norms, gates (reads the gate columns too)
+        "gdn_front": (lambda: lib.cs1_gdn_front_batch(gdn_in, None, GDN_IN, conv_w, q, k, v, rnq, rnk,
+                                                      gdn_in[:, boff:], gdn_in[:, boff + HV:], A_log, dt_bias, beta, gf,
+                                                      HV, ctypes.addressof(lens), 1, KEY, VAL, st),
+                      T * (2 * KEY + VAL) * 2 * 2 + (2 * KEY + VAL) * 8 + T * (2 * HK * 4 + HV * (2 + 2 + 2 + 4))),
         "gated_rms_norm": (lambda: lib.cs1_gated_rms_norm(o, gdn_in[:, 2 * KEY + VAL:], GDN_IN, gw, go, T, HV, 128,
                                                           1e-6, st), T * HV * 128 * 2 * 3 + 256),
         "attn_prep": (lambda: lib.cs1_attn_prep(attn_in, attn_in[:, HQ * 512:], ATTN_IN, qw, kw, cos, sin, aq, agate, ak,
