@@ -547,13 +547,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int t = threadIdx.x - 64, chunk = t & 31;
             const bf16* gs = reinterpret_cast<const bf16*>(smem + OFF_K);
             if (a.gated) cp_async_wait_all();  // this thread's own gate units (fetched at the last tile)
-#pragma unroll 4
+            // every row's loads unconditional (the staging tile is whole), only the stores past
+            // the sequence's end skipped, so the loads of several rows can be in flight
+            const int rows = min(BM, len - q0);
+#pragma unroll 8
             for (int i = 0; i < BM / 4; i++) {
                 const int row = (t >> 5) + 4 * i;
-                const int lrow = q0 + row;
-                if (lrow >= len) break;
                 const Pack8 xv = ld8(stage + row * DH + ((chunk ^ row) & 31) * 8);
-                const size_t o_off = ((size_t)(off + lrow) * a.Hq + h) * DH + chunk * 8;
+                const size_t o_off = ((size_t)(off + q0 + row) * a.Hq + h) * DH + chunk * 8;
                 if (a.gated) {
                     const Pack8 gv = ld8(gs + row * DH + chunk * 8);
                     Pack8 y;
@@ -564,8 +565,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const float2 o2 = mul2(__bfloat1622float2(xv.h[p2]), sg);
                         y.h[p2] = __floats2bfloat162_rn(o2.x, o2.y);
                     }
-                    st8(a.out + o_off, y);
-                } else {
+                    if (row < rows) st8(a.out + o_off, y);
+                } else if (row < rows) {
                     st8(a.out + o_off, xv);
                 }
             }

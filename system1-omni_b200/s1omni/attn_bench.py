@@ -3,7 +3,8 @@
     cd system1-omni_b200 && python -m s1omni.attn_bench --lengths 4096 [--hq 24 --hk 4]
         [--lib PATH] [--reps 10] [--once]
 
-Packed sequences of the given lengths (comma-separated), head dim 256, gated, causal.
+Packed sequences of the given lengths (comma-separated; `bench32` is the bench's batch of 32
+prompts), head dim 256, gated, causal.
 Times `reps` calls with CUDA events on the calling stream after three warm-up calls and
 prints one JSON line: TFLOP/s at the causal algorithmic count 4*Hq*256*sum(T(T+1)/2)
 (QK^T and PV). `--once` makes exactly one call (for a profiler capture). Works with any
@@ -33,7 +34,14 @@ def main():
     ap.add_argument("--once", action="store_true")
     a = ap.parse_args()
     lib = Cs1(a.lib)
-    lengths = [int(x) for x in a.lengths.split(",")]
+    if a.lengths == "bench32":  # the bench's batch of 32 prompts
+        import os
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+        import bench
+        lengths = [len(r) for r in bench.pool(32)]
+    else:
+        lengths = [int(x) for x in a.lengths.split(",")]
     T, Hq, Hk, D = sum(lengths), a.hq, a.hk, 256
     g = torch.Generator(device="cuda").manual_seed(0)
     q = torch.randn(T, Hq, D, device="cuda", generator=g).to(torch.bfloat16)
