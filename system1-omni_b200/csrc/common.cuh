@@ -133,10 +133,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
 }
 // bf16 rounding of a pair (one paired conversion), back in fp32.
 __device__ __forceinline__ float2 rbf2(float2 v) { return __bfloat1622float2(__floats2bfloat162_rn(v.x, v.y)); }
-// SiLU of a pair from the identity y / (1 + 2^(-y log2 e)) with the hardware base-2
-// exponential and reciprocal (relative error ~1e-7, far below the bf16 rounding that
-// follows): one packed multiply, add and multiply and two special-function operations
-// per lane.
 // Sigmoid of a pair from 1 / (1 + 2^(-y log2 e)) with the hardware base-2 exponential and
 // reciprocal (relative error ~1e-7).
 __device__ __forceinline__ float2 sigmoid2_fast(float2 y) {
@@ -164,6 +160,10 @@ __device__ __forceinline__ float silu_hw(float y) {
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.f));
     return y * r;
 }
+// SiLU of a pair from the identity y / (1 + 2^(-y log2 e)) with the hardware base-2
+// exponential and reciprocal (relative error ~1e-7, far below the bf16 rounding that
+// follows): one packed multiply, add and multiply and two special-function operations
+// per lane; rounds lane for lane like silu_hw.
 __device__ __forceinline__ float2 silu2_fast(float2 y) {
     constexpr float kLog2e = 1.4426950408889634f;
     const float2 t = mul2(y, make_float2(-kLog2e, -kLog2e));
@@ -176,5 +176,4 @@ __device__ __forceinline__ float2 silu2_fast(float2 y) {
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(d.y));
     return mul2(y, r);
 }
-
 }  // namespace s1

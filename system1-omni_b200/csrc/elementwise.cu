@@ -7,9 +7,13 @@
 //   gates  beta = bf16(sigmoid(b)); g = -exp(A_log) softplus(a + dt_bias) (fp32, threshold 20)
 //   silu   out = bf16(bf16(silu(gate)) * up)
 #include <climits>
+#include <type_traits>
 
 #include "common.cuh"
 #include "ops_internal.h"
+#include "tc.cuh"
+
+S1_FAULT_WORD(elementwise)
 
 namespace s1 {
 
@@ -94,8 +98,18 @@ __device__ __noinline__ void front_gates(const FrontArgs& fr, int ld, int t_begi
     }
 }
 
-template <int NP, bool Dyn, bool Front>
-__global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
+// Staged variant (Bulk, 4 channels per thread): each CTA's slice of a row (128 packs of
+// 8 bytes, contiguous) is copied into a ring of CB_STAGES batches of 8 rows by bulk copies
+// that one thread issues, so up to 32 KB per CTA are in flight without holding registers;
+// the threads read their packs from shared memory. A batch's stage is refilled once every
+// thread has passed the barrier of the next batch.
+constexpr int CB_STAGES = 4;
+constexpr int CB_ROW = 128 * 8;               // bytes of a row slice (128 threads x 8 bytes)
+constexpr int CB_STAGE = 8 * CB_ROW;          // 8 rows
+constexpr int CB_SMEM = CB_STAGES * CB_STAGE + 8 * CB_STAGES;
+
+template <int NP, bool Dyn, bool Front, bool Bulk = false>
+__global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
                                 bf16* __restrict__ v, int key_packs, int value_packs, int run,
                                 const __grid_constant__ SeqTable tab_arg, const DevBatch* dyn,
@@ -113,21 +127,30 @@ __global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_k
             return;
         }
     }
+    static_assert(!Bulk || NP == 2, "the staged variant takes 4 channels per thread");
     const int c = blockIdx.x * blockDim.x + threadIdx.x;  // pack of CH channels
     const int packs = 2 * key_packs + value_packs;
-    if (c >= packs) return;
+    // the staged variant keeps every thread for the CTA's barriers
+    const bool active = c < packs;
+    if (!Bulk && !active) return;
+    // Front: a q or k pack (warp-uniform: a head's packs are whole warps), whose rows' sums
+    // of squares are taken
+    const bool qk = Front && c < 2 * key_packs;
     // channel pairs (2p, 2p + 1) in f32x2 lanes: wt[p][j] = tap j of both channels
     float2 wt[NP][4];
 #pragma unroll
     for (int i = 0; i < NP; i++) {
         float f[8];
-        unpack8(ld8(w + (size_t)c * CH * 4 + i * 8), f);  // channels 2i, 2i + 1, four taps each
+        if (active) unpack8(ld8(w + (size_t)c * CH * 4 + i * 8), f);  // channels 2i, 2i + 1, four taps each
 #pragma unroll
-        for (int j = 0; j < 4; j++) wt[i][j] = make_float2(f[j], f[4 + j]);
+        for (int j = 0; j < 4; j++) wt[i][j] = active ? make_float2(f[j], f[4 + j]) : make_float2(0.f, 0.f);
     }
     bf16* dst;
     int dst_ld;
-    if (c < key_packs) {
+    if (!active) {
+        dst = nullptr;
+        dst_ld = 0;
+    } else if (c < key_packs) {
         dst = q + (size_t)c * CH;
         dst_ld = key_packs * CH;
     } else if (c < 2 * key_packs) {
@@ -166,27 +189,68 @@ __global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_k
             }
         }
     };
-    window(t_begin);
+    // Bulk: the ring and its barriers; thread 0 issues the copies
+    extern __shared__ __align__(128) uint8_t cbuf[];
+    const int batches = (t_end - t_begin + 7) / 8;
+    const uint32_t ring = Bulk ? tc::smem_u32(cbuf) : 0u, bars = ring + CB_STAGES * CB_STAGE;
+    const int slice = Bulk ? min(128, packs - (int)blockIdx.x * 128) * (int)sizeof(P) : 0;
+    int issued = 0;  // thread 0: batches whose copies were issued
+    auto issue = [&](int b) {
+        const int st = b % CB_STAGES, r0 = t_begin + 8 * b, nr = min(8, t_end - r0);
+        const uint32_t bar = bars + 8u * st;
+        tc::mbar_expect_tx(bar, (uint32_t)(nr * slice));
+        const bf16* src = qkv + (size_t)blockIdx.x * 128 * CH + (size_t)r0 * ld_;
+        for (int i = 0; i < nr; i++)
+            tc::bulk_load(ring + st * CB_STAGE + i * CB_ROW, src + (size_t)i * ld_, (uint32_t)slice, bar);
+        issued = b + 1;
+    };
+    if constexpr (Bulk) {
+        if (threadIdx.x == 0) {
+            for (int i = 0; i < CB_STAGES; i++) tc::mbar_init(bars + 8u * i, 1);
+            tc::mbar_fence_init();
+        }
+        __syncthreads();
+        if (threadIdx.x == 0)
+            for (int b = 0; b < min(CB_STAGES, batches); b++) issue(b);
+    }
+    if (active) window(t_begin);
     // rows in batches of 8: all loads of a batch are in flight before the first is used
-    for (int tb = t_begin; tb < t_end; tb += 8) {
+    for (int bi = 0; bi < batches; bi++) {
+        const int tb = t_begin + 8 * bi;
         P raw[8];
+        if constexpr (Bulk) {
+            const int st = bi % CB_STAGES;
+            bool bad = !tc::mbar_wait(bars + 8u * st, (uint32_t)(bi / CB_STAGES) & 1u);
+            // every thread is past batch bi - 1: its stage takes batch bi - 1 + CB_STAGES
+            bad = __syncthreads_or(bad);
+            if (bad) {
+                if (threadIdx.x == 0) {
+                    atomicOr(&g_fault_word, tc::FAULT_WAIT_OTHER);
+                    for (int b = bi; b < issued; b++)  // the copies still in flight land first
+                        (void)tc::mbar_wait(bars + 8u * (b % CB_STAGES), (uint32_t)(b / CB_STAGES) & 1u);
+                }
+                break;
+            }
+            if (threadIdx.x == 0 && bi >= 1 && bi - 1 + CB_STAGES < batches) issue(bi - 1 + CB_STAGES);
+            if (!active) continue;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+                if (tb + i < t_end) raw[i] = ld(col + (size_t)(tb + i) * ld_);
+        }
         float ss8[8];  // Front: this thread's part of each row's sum of squares
 #pragma unroll
         for (int i = 0; i < 8; i++) ss8[i] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; i++)
-            if (tb + i < t_end) raw[i] = ld(col + (size_t)(tb + i) * ld_);
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
+        // one row: the conv over the window and row i of the batch, its store, the row's
+        // part of the sum of squares, the window moved on by one row
+        auto row = [&](int i, auto with_ss) {
             const int t = tb + i;
-            if (t >= t_end) break;
-            if (t == next) {
-                s++;
-                next = tab.offset[s + 1];
-                window(t);
-            }
             float2 x0[NP];
-            unpack(raw[i], x0);
+            if constexpr (Bulk)  // row i of the batch's stage, read where it is used
+                unpack(*reinterpret_cast<const P*>(cbuf + (bi % CB_STAGES) * CB_STAGE + i * CB_ROW +
+                                                   threadIdx.x * sizeof(P)), x0);
+            else
+                unpack(raw[i], x0);
             P out;
 #pragma unroll
             for (int p = 0; p < NP; p++) {
@@ -199,19 +263,48 @@ __global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_k
                 out.h[p] = __floats2bfloat162_rn(y.x, y.y);
             }
             *reinterpret_cast<P*>(dst + (size_t)t * dst_ld) = out;
-            if constexpr (Front) {
+            if constexpr (decltype(with_ss)::value) {
+                float2 sq = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int p = 0; p < NP; p++) {
                     const float2 yy = __bfloat1622float2(out.h[p]);
-                    ss8[i] = fmaf(yy.x, yy.x, ss8[i]);
-                    ss8[i] = fmaf(yy.y, yy.y, ss8[i]);
+                    sq = fma2(yy, yy, sq);
                 }
+                ss8[i] = sq.x + sq.y;
             }
 #pragma unroll
             for (int p = 0; p < NP; p++) {
                 x1[p] = x2[p];
                 x2[p] = x3[p];
                 x3[p] = x0[p];
+            }
+        };
+        using SS = std::integral_constant<bool, Front>;
+        using NoSS = std::false_type;
+        if (tb + 8 <= t_end && next >= tb + 8) {
+            // the common batch: eight rows of one sequence, straight-line code (the window
+            // lives in renamed registers, no moves); sums of squares for q and k only
+            if (qk) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) row(i, SS{});
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) row(i, NoSS{});
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int t = tb + i;
+                if (t >= t_end) break;
+                if (t == next) {
+                    s++;
+                    next = tab.offset[s + 1];
+                    window(t);
+                }
+                if (qk)
+                    row(i, SS{});
+                else
+                    row(i, NoSS{});
             }
         }
         if constexpr (Front) {
@@ -221,7 +314,7 @@ __global__ void __launch_bounds__(128, NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_k
             // holds (lane bit LANES/2 -> rows +4, LANES/4 -> +2, LANES/8 -> +1), then plain steps
             // finish each sum; lanes whose bits below LANES/8 are 0 hold one row's total.
             constexpr int LANES = 128 / CH;
-            if (c < 2 * key_packs) {
+            if (qk) {
                 const int lane = threadIdx.x & 31;
 #pragma unroll
                 for (int k = 0; k < 4; k++) {
@@ -373,7 +466,9 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
         // Runs of 64 rows, shortened (to 32, then 16) while the grid is below two waves of
         // resident CTAs: a short prompt's CTAs each wait on a few batches of loads in series,
         // so more and shorter runs finish sooner.
-        const long waves2 = 2L * sm_count() * (narrow ? 8 : 4);
+        // staged through shared memory when every CTA's row slice is a multiple of 16 bytes
+        const bool bulk = narrow && tpacks % 2 == 0;
+        const long waves2 = 2L * sm_count() * (bulk ? 6 : narrow ? 8 : 4);
         int run = 64;
         while (run > 16 && groups * ((T + run - 1) / run) < waves2 && (T + run / 2 - 1) / (run / 2) <= 65535)
             run /= 2;
@@ -382,15 +477,22 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
         if (front) fr = *front;
         void (*kernel)(const bf16*, const bf16*, int, const bf16*, bf16*, bf16*, bf16*, int, int, int, SeqTable,
                        const DevBatch*, FrontArgs);
-        if (front)
+        if (bulk) {
+            if (front)
+                kernel = dyn ? conv_vec_kernel<2, true, true, true> : conv_vec_kernel<2, false, true, true>;
+            else
+                kernel = dyn ? conv_vec_kernel<2, true, false, true> : conv_vec_kernel<2, false, false, true>;
+        } else if (front) {
             kernel = dyn ? (narrow ? conv_vec_kernel<2, true, true> : conv_vec_kernel<4, true, true>)
                          : (narrow ? conv_vec_kernel<2, false, true> : conv_vec_kernel<4, false, true>);
-        else
+        } else {
             kernel = dyn ? (narrow ? conv_vec_kernel<2, true, false> : conv_vec_kernel<4, true, false>)
                          : (narrow ? conv_vec_kernel<2, false, false> : conv_vec_kernel<4, false, false>);
+        }
         // the front end adds one gate CTA per run of rows
         return launch_pdl(kernel,
-                          dim3((unsigned)(groups + (front ? 1 : 0)), (T + run - 1) / run), dim3(128), 0, st,
+                          dim3((unsigned)(groups + (front ? 1 : 0)), (T + run - 1) / run), dim3(128),
+                          bulk ? (size_t)CB_SMEM : 0, st,
                           static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
                           static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
                           static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, run, tab, dyn, fr);
