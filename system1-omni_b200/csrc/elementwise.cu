@@ -99,14 +99,19 @@ __device__ __noinline__ void front_gates(const FrontArgs& fr, int ld, int t_begi
 }
 
 // Staged variant (Bulk, 4 channels per thread): each CTA's slice of a row (128 packs of
-// 8 bytes, contiguous) is copied into a ring of CB_STAGES batches of 8 rows by bulk copies
-// that one thread issues, so up to 32 KB per CTA are in flight without holding registers;
-// the threads read their packs from shared memory. A batch's stage is refilled once every
-// thread has passed the barrier of the next batch.
+// 8 bytes, contiguous) is copied into a ring of CB_STAGES batches of 8 rows by bulk copies,
+// so up to 32 KB per CTA are in flight without holding registers; the threads read their
+// packs from shared memory. The warps do not wait for one another: each counts itself out
+// of a batch's stage when it is done with it, and the last of the four issues the copies of
+// the batch CB_STAGES ahead into that stage.
 constexpr int CB_STAGES = 4;
+constexpr int CB_WARPS = 4;
 constexpr int CB_ROW = 128 * 8;               // bytes of a row slice (128 threads x 8 bytes)
 constexpr int CB_STAGE = 8 * CB_ROW;          // 8 rows
-constexpr int CB_SMEM = CB_STAGES * CB_STAGE + 8 * CB_STAGES;
+// ring | full barriers | per-stage warp counts | batches issued | abort flag
+constexpr int CB_BAR = CB_STAGES * CB_STAGE;
+constexpr int CB_CNT = CB_BAR + 8 * CB_STAGES;
+constexpr int CB_SMEM = CB_CNT + 4 * CB_STAGES + 8;
 
 template <int NP, bool Dyn, bool Front, bool Bulk = false>
 __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
@@ -189,12 +194,15 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
             }
         }
     };
-    // Bulk: the ring and its barriers; thread 0 issues the copies
+    // Bulk: the ring, its barriers and counts
     extern __shared__ __align__(128) uint8_t cbuf[];
     const int batches = (t_end - t_begin + 7) / 8;
-    const uint32_t ring = Bulk ? tc::smem_u32(cbuf) : 0u, bars = ring + CB_STAGES * CB_STAGE;
+    const uint32_t ring = Bulk ? tc::smem_u32(cbuf) : 0u, bars = ring + CB_BAR;
+    int* cnt = reinterpret_cast<int*>(cbuf + CB_CNT);
+    volatile int* issued = reinterpret_cast<volatile int*>(cbuf + CB_CNT + 4 * CB_STAGES);
+    volatile int* abort_flag = issued + 1;
     const int slice = Bulk ? min(128, packs - (int)blockIdx.x * 128) * (int)sizeof(P) : 0;
-    int issued = 0;  // thread 0: batches whose copies were issued
+    const int lane = threadIdx.x & 31;
     auto issue = [&](int b) {
         const int st = b % CB_STAGES, r0 = t_begin + 8 * b, nr = min(8, t_end - r0);
         const uint32_t bar = bars + 8u * st;
@@ -202,11 +210,16 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
         const bf16* src = qkv + (size_t)blockIdx.x * 128 * CH + (size_t)r0 * ld_;
         for (int i = 0; i < nr; i++)
             tc::bulk_load(ring + st * CB_STAGE + i * CB_ROW, src + (size_t)i * ld_, (uint32_t)slice, bar);
-        issued = b + 1;
+        *issued = b + 1;
     };
     if constexpr (Bulk) {
         if (threadIdx.x == 0) {
-            for (int i = 0; i < CB_STAGES; i++) tc::mbar_init(bars + 8u * i, 1);
+            for (int i = 0; i < CB_STAGES; i++) {
+                tc::mbar_init(bars + 8u * i, 1);
+                cnt[i] = 0;
+            }
+            *issued = 0;
+            *abort_flag = 0;
             tc::mbar_fence_init();
         }
         __syncthreads();
@@ -220,24 +233,39 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
         P raw[8];
         if constexpr (Bulk) {
             const int st = bi % CB_STAGES;
-            bool bad = !tc::mbar_wait(bars + 8u * st, (uint32_t)(bi / CB_STAGES) & 1u);
-            // every thread is past batch bi - 1: its stage takes batch bi - 1 + CB_STAGES
-            bad = __syncthreads_or(bad);
-            if (bad) {
-                if (threadIdx.x == 0) {
+            const bool waited = tc::mbar_wait(bars + 8u * st, (uint32_t)(bi / CB_STAGES) & 1u);
+            // warp-uniform decisions: a wait that gave up here, or another warp's
+            const bool timeout = __any_sync(0xffffffffu, !waited);
+            if (timeout || __any_sync(0xffffffffu, *abort_flag != 0)) {
+                if (timeout && lane == 0) {
                     atomicOr(&g_fault_word, tc::FAULT_WAIT_OTHER);
-                    for (int b = bi; b < issued; b++)  // the copies still in flight land first
-                        (void)tc::mbar_wait(bars + 8u * (b % CB_STAGES), (uint32_t)(b / CB_STAGES) & 1u);
+                    *abort_flag = 1;
                 }
                 break;
             }
-            if (threadIdx.x == 0 && bi >= 1 && bi - 1 + CB_STAGES < batches) issue(bi - 1 + CB_STAGES);
-            if (!active) continue;
         } else {
 #pragma unroll
             for (int i = 0; i < 8; i++)
                 if (tb + i < t_end) raw[i] = ld(col + (size_t)(tb + i) * ld_);
         }
+        // this warp is done with the batch's stage: the last warp out refills it
+        auto release = [&]() {
+            if constexpr (Bulk) {
+                __syncwarp();
+                if (lane == 0) {
+                    __threadfence_block();
+                    const int st = bi % CB_STAGES;
+                    if (atomicAdd(&cnt[st], 1) == CB_WARPS - 1) {
+                        cnt[st] = 0;
+                        if (bi + CB_STAGES < batches) {
+                            tc::fence_async_smem();
+                            issue(bi + CB_STAGES);
+                        }
+                    }
+                }
+            }
+        };
+        if (active) {  // (the staged variant keeps lanes past the last pack for its counts)
         float ss8[8];  // Front: this thread's part of each row's sum of squares
 #pragma unroll
         for (int i = 0; i < 8; i++) ss8[i] = 0.f;
@@ -344,6 +372,18 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
                     dn[(size_t)t * HK + (head < HK ? head : head - HK)] = rsqrtf(ss8[0] + 1e-6f);
                 }
             }
+        }
+        }
+        release();
+    }
+    if constexpr (Bulk) {
+        // after a wait gave up: the copies still in flight (the last CB_STAGES issued) land
+        // before the CTA's shared memory is released
+        __syncthreads();
+        if (threadIdx.x == 0 && *abort_flag) {
+            const int n = *issued;
+            for (int b = max(0, n - CB_STAGES); b < n; b++)
+                (void)tc::mbar_wait(bars + 8u * (b % CB_STAGES), (uint32_t)(b / CB_STAGES) & 1u);
         }
     }
 }
