@@ -31,6 +31,9 @@ constexpr int DH = 256;
 
 // ---------------------------------------------------------------- prep ----
 constexpr int PREP_UNITS = 4;  // (token, head) units per warp, loads of all issued first
+// Aligned: Hq and Hk multiples of PREP_UNITS, so a warp's units are heads of one token and
+// all of q or all of k (one rotary row, no bounds or token checks per unit).
+template <bool Aligned>
 __global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restrict__ qg, const bf16* __restrict__ kr, int ld,
                                  const bf16* __restrict__ qw, const bf16* __restrict__ kw,
                                  const bf16* __restrict__ cosb, const bf16* __restrict__ sinb, bf16* __restrict__ q,
@@ -53,19 +56,21 @@ __global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restric
         for (int i = 0; i < PREP_UNITS; i++) {
             ti[i] = t;
             hi[i] = hh;
-            if (++hh == heads) {
+            if (Aligned) {
+                hh++;
+            } else if (++hh == heads) {
                 hh = 0;
                 t++;
             }
         }
     }
-    const int n = min(PREP_UNITS, units - unit0);
+    const int n = Aligned ? PREP_UNITS : min(PREP_UNITS, units - unit0);
     Pack8 xr[PREP_UNITS], gr[PREP_UNITS];
 #pragma unroll
     for (int i = 0; i < PREP_UNITS; i++) {
-        if (i < n) {
+        if (Aligned || i < n) {
             const bf16* row = qg + (size_t)ti[i] * ld;
-            if (hi[i] < Hq) {
+            if (Aligned ? hi[0] < Hq : hi[i] < Hq) {
                 const bf16* src = row + hi[i] * 2 * DH;
                 xr[i] = ld8(src + d0);
                 gr[i] = ld8(src + DH + d0);
@@ -93,8 +98,8 @@ __global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restric
     if (rotated) rot_rows(ca, sa);
 #pragma unroll
     for (int i = 0; i < PREP_UNITS; i++) {
-        if (i >= n) break;  // uniform over the warp
-        const bool is_q = hi[i] < Hq;
+        if (!Aligned && i >= n) break;  // uniform over the warp
+        const bool is_q = Aligned ? hi[0] < Hq : hi[i] < Hq;
         float2 x[4];
         float ss = 0.f;
 #pragma unroll
@@ -111,7 +116,7 @@ __global__ void __launch_bounds__(256, 3) prep_fast_kernel(const bf16* __restric
             const float2 w = __bfloat1622float2(wv.h[p]);
             x[p] = rbf2(mul2(mul2(x[p], inv2), make_float2(1.f + w.x, 1.f + w.y)));
         }
-        if (rotated && i > 0 && ti[i] != ti[i - 1])  // the warp's second token: its rotary rows, on demand
+        if (!Aligned && rotated && i > 0 && ti[i] != ti[i - 1])  // the warp's second token: its rotary rows
             rot_rows(ld8(cosb + (size_t)ti[i] * half + f), ld8(sinb + (size_t)ti[i] * half + f));
         Pack8 out;
 #pragma unroll
@@ -681,7 +686,9 @@ int cs1_attn_prep(const void* qg, const void* kr, int ld, const void* qw, const 
     if (!aligned16(cos) || !aligned16(sin)) return cudaErrorInvalidValue;
     constexpr int WPB = 8;
     // (Hq >= Hk >= 1, so Hq + Hk >= 2: the PREP_UNITS = 4 units of a warp fall in at most two tokens)
-    return launch_pdl(attn::prep_fast_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
+    const bool aligned = Hq % attn::PREP_UNITS == 0 && Hk % attn::PREP_UNITS == 0;
+    return launch_pdl(aligned ? attn::prep_fast_kernel<true> : attn::prep_fast_kernel<false>,
+                      dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
                       static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg), static_cast<const bf16*>(kr),
                       ld, static_cast<const bf16*>(qw), static_cast<const bf16*>(kw), static_cast<const bf16*>(cos),
                       static_cast<const bf16*>(sin), static_cast<bf16*>(q), static_cast<bf16*>(gate),
@@ -702,7 +709,9 @@ int cs1_attn_prep_dyn(const void* qg, const void* kr, int ld, const void* qw, co
         !aligned16(k) || !aligned16(cos) || !aligned16(sin))
         return cudaErrorInvalidValue;
     constexpr int WPB = 8;
-    return launch_pdl(attn::prep_fast_kernel, dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
+    const bool aligned = Hq % attn::PREP_UNITS == 0 && Hk % attn::PREP_UNITS == 0;
+    return launch_pdl(aligned ? attn::prep_fast_kernel<true> : attn::prep_fast_kernel<false>,
+                      dim3((unsigned)((warps + WPB - 1) / WPB)), dim3(WPB * 32), 0,
                       static_cast<cudaStream_t>(stream), static_cast<const bf16*>(qg), static_cast<const bf16*>(kr),
                       ld, static_cast<const bf16*>(qw), static_cast<const bf16*>(kw), static_cast<const bf16*>(cos),
                       static_cast<const bf16*>(sin), static_cast<bf16*>(q), static_cast<bf16*>(gate),
