@@ -8,6 +8,9 @@
 // the fp32 sum of squares is reduced in a different order (tree over packs).
 #include "common.cuh"
 #include "ops_internal.h"
+#include "tc.cuh"
+
+S1_FAULT_WORD(norm)
 
 namespace s1 {
 namespace {
@@ -140,6 +143,108 @@ __global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restric
                 st8(out + off + (size_t)pk * 8, pack8(o));
             }
         }
+    }
+}
+
+// Staged variant of the warp-per-row kernel: each warp owns a ring of RB_STAGES row slots in
+// shared memory (the residual and the delta row for the add variant); its lane 0 copies the
+// warp's next row in by bulk copies while the warp normalises the current one, so a row's
+// bytes are in flight without registers and the warps never wait for one another. The
+// weights sit in shared memory, loaded once per CTA; each warp walks rows with a grid stride.
+__host__ __device__ constexpr int rb_warps(bool add) { return 8; }
+__host__ __device__ constexpr int rb_stages(bool add) { return add ? 1 : 2; }
+__host__ __device__ constexpr int rb_smem(bool add, int D) {
+    return D * 2 + rb_warps(add) * rb_stages(add) * (add ? 2 : 1) * D * 2 + 8 * rb_warps(add) * rb_stages(add);
+}
+template <bool Add>
+__global__ void __launch_bounds__(rb_warps(Add) * 32, 1) rms_bulk_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
+                                                                 const bf16* __restrict__ x, const bf16* __restrict__ w,
+                                                                 bf16* __restrict__ out, int rows, int D, float eps,
+                                                                 const DevBatch* dyn) {
+    constexpr int W = rb_warps(Add), BUFS = Add ? 2 : 1, RB_STAGES = rb_stages(Add);
+    extern __shared__ __align__(128) uint8_t rsm[];
+    const int packs = D >> 3, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t row_bytes = (uint32_t)D * 2;
+    const Pack8* wsm = reinterpret_cast<const Pack8*>(rsm);
+    uint8_t* ring = rsm + row_bytes + (size_t)warp * RB_STAGES * BUFS * row_bytes;
+    const uint32_t bars = tc::smem_u32(rsm) + row_bytes + W * RB_STAGES * BUFS * row_bytes + 8u * warp * RB_STAGES;
+    if (lane == 0)
+        for (int st = 0; st < RB_STAGES; st++) tc::mbar_init(bars + 8u * st, 1);
+    tc::mbar_fence_init();
+    grid_dep_wait();
+    grid_dep_launch();
+    rows = dyn_rows(dyn, rows);
+    for (int i = threadIdx.x; i < packs; i += blockDim.x) reinterpret_cast<Pack8*>(rsm)[i] = ld8(w + (size_t)i * 8);
+    __syncthreads();
+    const int g0 = blockIdx.x * W + warp, gstep = gridDim.x * W;
+    const bf16* src0 = Add ? res : x;
+    auto issue = [&](int k) {  // the warp's k-th row into stage k % RB_STAGES
+        const int row = g0 + k * gstep, st = k % RB_STAGES;
+        const uint32_t bar = bars + 8u * st, dst = tc::smem_u32(ring + (size_t)st * BUFS * row_bytes);
+        tc::mbar_expect_tx(bar, BUFS * row_bytes);
+        tc::bulk_load(dst, src0 + (size_t)row * D, row_bytes, bar);
+        if constexpr (Add) tc::bulk_load(dst + row_bytes, delta + (size_t)row * D, row_bytes, bar);
+    };
+    if (lane == 0)
+        for (int k = 0; k < RB_STAGES && g0 + k * gstep < rows; k++) issue(k);
+    int k = 0;
+    for (; g0 + k * gstep < rows; k++) {
+        const int row = g0 + k * gstep, st = k % RB_STAGES;
+        const bool waited = tc::mbar_wait(bars + 8u * st, (uint32_t)(k / RB_STAGES) & 1u);
+        if (__any_sync(0xffffffffu, !waited)) {
+            if (lane == 0) atomicOr(&g_fault_word, tc::FAULT_WAIT_OTHER);
+            break;
+        }
+        const Pack8* a = reinterpret_cast<const Pack8*>(ring + (size_t)st * BUFS * row_bytes);
+        const size_t off = (size_t)row * D;
+        Pack8 v[PPL];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < PPL; i++) {
+            const int pk = lane + 32 * i;
+            if (pk < packs) {
+                float f[8];
+                if constexpr (Add) {
+                    float fb[8];
+                    unpack8(a[pk], f);
+                    unpack8(a[packs + pk], fb);
+#pragma unroll
+                    for (int e = 0; e < 8; e++) f[e] += fb[e];
+                    v[i] = pack8(f);
+                    st8(res + off + (size_t)pk * 8, v[i]);
+                    unpack8(v[i], f);
+                } else {
+                    v[i] = a[pk];
+                    unpack8(v[i], f);
+                }
+#pragma unroll
+                for (int e = 0; e < 8; e++) ss = fmaf(f[e], f[e], ss);
+            }
+        }
+        // the stage is read: lane 0 refills it with the warp's row RB_STAGES ahead
+        __syncwarp();
+        if (lane == 0 && g0 + (k + RB_STAGES) * gstep < rows) {
+            tc::fence_async_smem();
+            issue(k + RB_STAGES);
+        }
+        const float inv = rsqrtf(warp_sum(ss) / D + eps);
+#pragma unroll
+        for (int i = 0; i < PPL; i++) {
+            const int pk = lane + 32 * i;
+            if (pk < packs) {
+                float f[8], wv[8], o[8];
+                unpack8(v[i], f);
+                unpack8(wsm[pk], wv);
+#pragma unroll
+                for (int e = 0; e < 8; e++) o[e] = f[e] * inv * (1.f + wv[e]);
+                st8(out + off + (size_t)pk * 8, pack8(o));
+            }
+        }
+    }
+    if (lane == 0 && g0 + k * gstep < rows) {
+        // a wait gave up: the copies still in flight land before the CTA's memory is released
+        for (int j = k; j < k + RB_STAGES && g0 + j * gstep < rows; j++)
+            (void)tc::mbar_wait(bars + 8u * (j % RB_STAGES), (uint32_t)(j / RB_STAGES) & 1u);
     }
 }
 
@@ -292,9 +397,13 @@ int rms_norm(const void* x, const void* w, void* out, int rows, int D, float eps
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
     if (vec_ok(D, x, w, out, out) && D <= 256 * PPL) {
-        dim3 grid, block;
-        rms_warp_shape(rows, grid, block);
-        return launch_pdl(rms_warp_kernel<false>, grid, block, 0, st, static_cast<bf16*>(nullptr),
+        static const cudaError_t configured =
+            cudaFuncSetAttribute(rms_bulk_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 rb_smem(false, 256 * PPL));
+        if (configured != cudaSuccess) return configured;
+        const int need = (rows + rb_warps(false) - 1) / rb_warps(false);
+        return launch_pdl(rms_bulk_kernel<false>, dim3(need < sm_count() ? need : sm_count()),
+                          dim3(rb_warps(false) * 32), (size_t)rb_smem(false, D), st, static_cast<bf16*>(nullptr),
                           static_cast<const bf16*>(nullptr), X, Wt, O, rows, D, eps, dyn);
     }
     if (dyn) return cudaErrorInvalidValue;  // the capacity path needs the warp-per-row kernel
@@ -315,10 +424,14 @@ int add_rms_norm(void* residual, const void* delta, const void* w, void* out, in
     auto Wt = static_cast<const bf16*>(w);
     auto O = static_cast<bf16*>(out);
     if (vec_ok(D, residual, delta, w, out) && D <= 256 * PPL) {
-        dim3 grid, block;
-        rms_warp_shape(rows, grid, block);
-        return launch_pdl(rms_warp_kernel<true>, grid, block, 0, st, R, Dl, static_cast<const bf16*>(nullptr), Wt,
-                          O, rows, D, eps, dyn);
+        static const cudaError_t configured =
+            cudaFuncSetAttribute(rms_bulk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 rb_smem(true, 256 * PPL));
+        if (configured != cudaSuccess) return configured;
+        const int need = (rows + rb_warps(true) - 1) / rb_warps(true);
+        return launch_pdl(rms_bulk_kernel<true>, dim3(need < sm_count() ? need : sm_count()),
+                          dim3(rb_warps(true) * 32), (size_t)rb_smem(true, D), st, R, Dl,
+                          static_cast<const bf16*>(nullptr), Wt, O, rows, D, eps, dyn);
     }
     if (dyn) return cudaErrorInvalidValue;
     if (vec_ok(D, residual, delta, w, out))

@@ -121,6 +121,7 @@ extern "C" uint32_t s1_fault_read_gdn(int clear);
 extern "C" uint32_t s1_fault_read_gdn_fused(int clear);
 extern "C" uint32_t s1_fault_read_attention(int clear);
 extern "C" uint32_t s1_fault_read_elementwise(int clear);
+extern "C" uint32_t s1_fault_read_norm(int clear);
 
 extern "C" {
 
@@ -198,7 +199,8 @@ int cs1_wait_selftest(long long cycles, void* stream) {
 
 uint32_t cs1_fault_status(int clear) {
     return s1_fault_read_gemm(clear) | s1_fault_read_gdn(clear) | s1_fault_read_gdn_fused(clear) |
-           s1_fault_read_attention(clear) | s1_fault_read_elementwise(clear) | s1_fault_read_selftest(clear);
+           s1_fault_read_attention(clear) | s1_fault_read_elementwise(clear) | s1_fault_read_norm(clear) |
+           s1_fault_read_selftest(clear);
 }
 
 // ---- vision entry points: required symbols of the loader; the vision path is
