@@ -86,9 +86,10 @@ struct FrontArgs {
     int H;
 };
 
-// The gate CTA's work, out of line so that its registers do not count against the conv's.
-__device__ __noinline__ void front_gates(const FrontArgs& fr, int ld, int t_begin, int t_end) {
-    for (int i = threadIdx.x; i < (t_end - t_begin) * fr.H; i += blockDim.x) {
+// Gates of items [i0, i1) of rows t_begin.. (item i = row t_begin + i / H, head i % H), out
+// of line so that its registers do not count against the conv's.
+__device__ __noinline__ void front_gates(const FrontArgs& fr, int ld, int t_begin, int i0, int i1) {
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
         const int t = t_begin + i / fr.H, h = i % fr.H;
         const size_t src = (size_t)t * ld + h;
         fr.beta[(size_t)t * fr.H + h] = to_bf16(sigmoid(f32(fr.b[src])));
@@ -124,11 +125,11 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
     constexpr int CH = 2 * NP;  // channels per thread
     grid_dep_wait();
     grid_dep_launch();
-    if constexpr (Front) {
+    if constexpr (Front && !Bulk) {
         if (blockIdx.x == gridDim.x - 1) {  // the gate CTA of this run of rows
             const int T = tab.offset[tab.count];
             const int t_begin = blockIdx.y * run, t_end = min(T, t_begin + run);
-            front_gates(fr, ld_, t_begin, t_end);
+            front_gates(fr, ld_, t_begin, 0, (t_end - t_begin) * fr.H);
             return;
         }
     }
@@ -385,6 +386,17 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
             for (int b = max(0, n - CB_STAGES); b < n; b++)
                 (void)tc::mbar_wait(bars + 8u * (b % CB_STAGES), (uint32_t)(b / CB_STAGES) & 1u);
         }
+        if constexpr (Front) {
+            // the gates of this run's rows, shared out over the CTAs of v packs (which have no
+            // norms to take), or over every CTA when there are none
+            const int groups = (packs + 127) / 128, first_v = min(groups, (2 * key_packs + 127) / 128);
+            const int g0 = first_v < groups ? first_v : 0, ng = groups - g0;
+            if ((int)blockIdx.x >= g0) {
+                const int items = (t_end - t_begin) * fr.H, per = (items + ng - 1) / ng;
+                const int i0 = ((int)blockIdx.x - g0) * per;
+                front_gates(fr, ld_, t_begin, i0, min(items, i0 + per));
+            }
+        }
     }
 }
 
@@ -529,9 +541,10 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
             kernel = dyn ? (narrow ? conv_vec_kernel<2, true, false> : conv_vec_kernel<4, true, false>)
                          : (narrow ? conv_vec_kernel<2, false, false> : conv_vec_kernel<4, false, false>);
         }
-        // the front end adds one gate CTA per run of rows
+        // the front end adds one gate CTA per run of rows (the staged kernel shares the gates
+        // out over its CTAs of v packs instead)
         return launch_pdl(kernel,
-                          dim3((unsigned)(groups + (front ? 1 : 0)), (T + run - 1) / run), dim3(128),
+                          dim3((unsigned)(groups + (front && !bulk ? 1 : 0)), (T + run - 1) / run), dim3(128),
                           bulk ? (size_t)CB_SMEM : 0, st,
                           static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
                           static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
