@@ -41,6 +41,7 @@
 // behind (which a parity wait would misread); the one hand-off without that order, the
 // norms of the next chunk read by the scan warps, is a monotonic counter.
 #include <algorithm>
+#include <type_traits>
 
 #include "common.cuh"
 #include "gdn.cuh"
@@ -735,46 +736,96 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
             }
             named_bar_sync(BAR_PREP, NPREP);  // A complete
-            // T = (I + A)^-1 in two diagonal 32 x 32 blocks and the block below them, written out
-            // as tb = bf16(T diag(beta)) (K-major [64 t][64 j]) as the entries become final.
-            // Diagonal blocks: one thread per (block, column), right-looking substitution (each
-            // solved entry updates the later rows at once: a chain 32 steps deep, the terms of
-            // every entry added in the order of the plain forward substitution); column m of
-            // a diagonal block is a row of its transposed copy, read 4 entries at a time.
+            // T = (I + A)^-1 by block doubling, written out as tb = bf16(T diag(beta)) (K-major
+            // [64 t][64 j]) as the entries become final. Level 0: the eight 8 x 8 diagonal
+            // blocks by right-looking substitution, one thread per (block, column). Levels 1 and
+            // 2: the block below the diagonal of each 16 x 16, then 32 x 32 diagonal block,
+            // T_10 = -T_11 (A_10 T_00), one thread per entry (two at level 2). Level 3, the 32 x 32
+            // block below the two diagonal ones, follows in the same form. Inside the diagonal
+            // 32-blocks A(r, c) sits at A[c][r] (transposed) and T(r, c) at Tm[r][c mod 32];
+            // every entry above the diagonal of those blocks is written as 0, so the sums below
+            // run over whole blocks.
             uint8_t* tb = sm + OFF_TB;
+            bf16* tcol = reinterpret_cast<bf16*>(tb);
+            auto put_tb = [&](int t, int jj, float tv) {
+                tcol[(sw128_offset(t, jj >> 3) >> 1) + (jj & 7)] = to_bf16(tv * bet[jj]);
+            };
+            auto adiag = [&](int r, int cc) { return A[cc * LDT + r]; };
+            auto tdiag = [&](int r, int cc) -> float& { return Tm[r * LDD + (cc & 31)]; };
             if (ok && pt < C) {
-                const int b = pt >> 5, col = pt & 31, o32 = b * 32;
-                const float* at = A + o32 * LDT + o32;  // A[o32 + r][o32 + m] at at[m * LDT + r]
-                float x[32];
+                const int o8 = (pt >> 3) * 8, col = pt & 7;
+                float x[8];
 #pragma unroll
-                for (int r = 0; r < 32; r++) x[r] = r == col ? 1.f : 0.f;
+                for (int r = 0; r < 8; r++) x[r] = r == col ? 1.f : 0.f;
 #pragma unroll
-                for (int m = 0; m < 31; m++) {
+                for (int m = 0; m < 7; m++) {
                     const float xm = x[m];
 #pragma unroll
-                    for (int r4 = (m + 1) & ~3; r4 < 32; r4 += 4) {
-                        const float4 a4 = *reinterpret_cast<const float4*>(at + m * LDT + r4);
-                        const float av[4] = {a4.x, a4.y, a4.z, a4.w};
-#pragma unroll
-                        for (int e = 0; e < 4; e++)
-                            if (r4 + e > m) x[r4 + e] = fmaf(-av[e], xm, x[r4 + e]);
-                    }
+                    for (int r = m + 1; r < 8; r++) x[r] = fmaf(-adiag(o8 + r, o8 + m), xm, x[r]);
                 }
-                const float bj = bet[o32 + col];
-                bf16* tcol = reinterpret_cast<bf16*>(tb);
 #pragma unroll
-                for (int r = 0; r < 32; r++) {
+                for (int r = 0; r < 8; r++) {
                     const float tv = r < col ? 0.f : x[r];
-                    Tm[(b * 32 + r) * LDD + col] = tv;
-                    const int t = o32 + r, j = o32 + col;
-                    tcol[(sw128_offset(t, j >> 3) >> 1) + (j & 7)] = to_bf16(tv * bj);
+                    tdiag(o8 + r, o8 + col) = tv;
+                    put_tb(o8 + r, o8 + col, tv);
                 }
-            } else if (ok && pt < C + 32 * 4) {
-                // tb's upper block (rows 0..31, columns 32..63) is zero
-                const int u = pt - C, t = u >> 2, ch = 4 + (u & 3);
-                *reinterpret_cast<uint4*>(tb + sw128_offset(t, ch)) = make_uint4(0u, 0u, 0u, 0u);
+            } else if (ok) {
+                // zeros: the six 8 x 8 blocks above the diagonal ones inside each 32-block (Tm and
+                // tb), four entries per thread, and tb's upper block (rows 0..31, columns 32..63)
+                const int u = pt - C;
+#pragma unroll
+                for (int e4 = 0; e4 < 4; e4++) {
+                    const int e = u + (NPREP - C) * e4, b = e / 384, rem = e - b * 384, blk = rem >> 6;
+                    const int bi = blk < 3 ? 0 : blk < 5 ? 1 : 2, bj = blk < 3 ? blk + 1 : blk < 5 ? blk - 1 : 3;
+                    const int r = b * 32 + bi * 8 + ((rem >> 3) & 7), cc = b * 32 + bj * 8 + (rem & 7);
+                    tdiag(r, cc) = 0.f;
+                    put_tb(r, cc, 0.f);
+                }
+                if (u < 32 * 4) {
+                    const int t = u >> 2, ch = 4 + (u & 3);
+                    *reinterpret_cast<uint4*>(tb + sw128_offset(t, ch)) = make_uint4(0u, 0u, 0u, 0u);
+                }
             }
             named_bar_sync(BAR_PREP, NPREP);
+            // levels 1 (8 -> 16) and 2 (16 -> 32), each sum unrolled over its block so that
+            // the loads are in flight together
+            auto join = [&](auto hb_c) {
+                constexpr int HB = decltype(hb_c)::value;  // size of the blocks being joined
+                constexpr int PER = HB * HB, N = HB == 8 ? 1 : 2, TPJ = PER / N;
+                const int pair = pt / TPJ, o0 = pair * 2 * HB, o1 = o0 + HB;
+                const int idx = (pt - pair * TPJ) * N, i = idx / HB, j0 = idx % HB;
+                float* xs = X + pair * PER;
+                float acc[N];
+#pragma unroll
+                for (int e = 0; e < N; e++) acc[e] = 0.f;
+#pragma unroll
+                for (int m = 0; m < HB; m++) {
+                    const float a = adiag(o1 + i, o0 + m);
+#pragma unroll
+                    for (int e = 0; e < N; e++) acc[e] = fmaf(a, tdiag(o0 + m, o0 + j0 + e), acc[e]);
+                }
+#pragma unroll
+                for (int e = 0; e < N; e++) xs[idx + e] = acc[e];
+                named_bar_sync(BAR_PREP, NPREP);
+#pragma unroll
+                for (int e = 0; e < N; e++) acc[e] = 0.f;
+#pragma unroll
+                for (int m = 0; m < HB; m++) {
+                    const float t_ = tdiag(o1 + i, o1 + m);
+#pragma unroll
+                    for (int e = 0; e < N; e++) acc[e] = fmaf(t_, xs[m * HB + j0 + e], acc[e]);
+                }
+                if (ok) {
+#pragma unroll
+                    for (int e = 0; e < N; e++) {
+                        tdiag(o1 + i, o0 + j0 + e) = -acc[e];
+                        put_tb(o1 + i, o0 + j0 + e, -acc[e]);
+                    }
+                }
+                named_bar_sync(BAR_PREP, NPREP);
+            };
+            join(std::integral_constant<int, 8>{});
+            join(std::integral_constant<int, 16>{});
             // X = A_10 T_00, then T_10 = -T_11 X; thread = (row r, 4 columns c4)
             {
                 const int r = pt >> 3, c4 = (pt & 7) * 4;
