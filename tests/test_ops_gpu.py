@@ -30,20 +30,24 @@ def test_embed(cs1, stream):
     assert np.array_equal(host(out), ops.embed(ids, table))
 
 
-@pytest.mark.parametrize("D", [256, 2560, 4096, 5120, 100])
-def test_rms_norm(cs1, stream, D):
-    x, w = _r((33, D), 3), _r((D,), 4, 0.1)
-    out = empty_bf16(33, D)
-    cs1.cs1_rms_norm(dev_bf16(x), dev_bf16(w), out, 33, D, 1e-6, stream)
+# D up to 5,120 takes the warp-per-row kernel with rows staged in shared memory (3,000 rows:
+# several rows per warp, so every slot is refilled), 8,192 the CTA-per-row kernel, 100 and 72
+# (not multiples of 8) the scalar one
+@pytest.mark.parametrize("rows,D", [(33, 256), (33, 2560), (3000, 2560), (33, 4096), (33, 5120), (33, 8192),
+                                    (33, 100)])
+def test_rms_norm(cs1, stream, rows, D):
+    x, w = _r((rows, D), 3), _r((D,), 4, 0.1)
+    out = empty_bf16(rows, D)
+    cs1.cs1_rms_norm(dev_bf16(x), dev_bf16(w), out, rows, D, 1e-6, stream)
     assert max_rel(host(out), ops.rms_norm(x, w, 1e-6)) <= ULP
 
 
-@pytest.mark.parametrize("D", [2560, 5120, 72])
-def test_add_rms_norm(cs1, stream, D):
-    r, d, w = _r((20, D), 5), _r((20, D), 6), _r((D,), 7, 0.1)
+@pytest.mark.parametrize("rows,D", [(20, 2560), (3000, 2560), (20, 5120), (20, 8192), (20, 72)])
+def test_add_rms_norm(cs1, stream, rows, D):
+    r, d, w = _r((rows, D), 5), _r((rows, D), 6), _r((D,), 7, 0.1)
     res = dev_bf16(r)
-    out = empty_bf16(20, D)
-    cs1.cs1_add_rms_norm(res, dev_bf16(d), dev_bf16(w), out, 20, D, 1e-6, stream)
+    out = empty_bf16(rows, D)
+    cs1.cs1_add_rms_norm(res, dev_bf16(d), dev_bf16(w), out, rows, D, 1e-6, stream)
     er, eo = ops.add_rms_norm(r, d, w, 1e-6)
     assert np.array_equal(host(res), er)
     assert max_rel(host(out), eo) <= ULP
@@ -77,6 +81,33 @@ def test_gdn_conv_batch(cs1, stream, lengths, with_history):
         for g, e in zip(got, (eq, ek, ev)):
             assert max_rel(g[off:off + n], e) <= ULP
         off += n
+
+
+# Channel layouts of the conv kernel: 128 packs of 4 channels per CTA, so (128, 192) leaves the
+# last CTA part-filled (lanes past the last pack keep the staged ring's counts), (8, 16) is a
+# single small CTA, and (4, 4) (channel counts not multiples of 8) takes the scalar kernel.
+@pytest.mark.parametrize("kd,vd", [(128, 192), (8, 16), (4, 4)])
+@pytest.mark.parametrize("with_history", [False, True])
+def test_gdn_conv_channel_layouts(cs1, stream, kd, vd, with_history):
+    lengths = [150, 1, 77]
+    C = 2 * kd + vd
+    ld = C + 8
+    T = sum(lengths)
+    qkv = _r((T, ld), 14)
+    w = rnd(np.random.default_rng(15).uniform(-0.5, 0.5, (C, 4)).astype(np.float32))
+    hist = _r((3, ld), 16) if with_history else None
+    q, k, v = empty_bf16(T, kd), empty_bf16(T, kd), empty_bf16(T, vd)
+    lens = np.asarray(lengths, dtype=np.uintp)
+    assert cs1.cs1_gdn_conv_batch(dev_bf16(qkv), dev_bf16(hist) if with_history else None, ld, dev_bf16(w), q, k,
+                                  v, lens.ctypes.data, len(lengths), kd, vd, stream) == 0
+    off = 0
+    got = [host(q), host(k), host(v)]
+    for n in lengths:
+        eq, ek, ev = ops.gdn_conv(qkv[off:off + n, :C], w, kd, vd, history=hist[:, :C] if with_history else None)
+        for g, e in zip(got, (eq, ek, ev)):
+            assert max_rel(g[off:off + n], e) <= ULP
+        off += n
+    assert cs1.cs1_fault_status(1) == 0
 
 
 def test_gdn_conv_single_and_prefix_entry_points(cs1, stream):
