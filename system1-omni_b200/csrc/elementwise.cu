@@ -99,10 +99,10 @@ __device__ __noinline__ void front_gates(const FrontArgs& fr, int ld, int t_begi
     }
 }
 
-// Staged variant (Bulk, 4 channels per thread): each CTA's slice of a row (128 packs of
-// 8 bytes, contiguous) is copied into a ring of CB_STAGES batches of 8 rows by bulk copies,
-// so up to 32 KB per CTA are in flight without holding registers; the threads read their
-// packs from shared memory. The warps do not wait for one another: each counts itself out
+// The conv kernel takes 4 channels per thread (one 8-byte pack); a CTA of 128 threads covers
+// 128 packs of a run of rows. Each CTA's slice of a row (contiguous) is copied into a ring of
+// CB_STAGES batches of 8 rows by bulk copies, so up to 32 KB per CTA are in flight without
+// holding registers; the threads read their packs from shared memory. The warps do not wait for one another: each counts itself out
 // of a batch's stage when it is done with it, and the last of the four issues the copies of
 // the batch CB_STAGES ahead into that stage.
 constexpr int CB_STAGES = 4;
@@ -114,31 +114,22 @@ constexpr int CB_BAR = CB_STAGES * CB_STAGE;
 constexpr int CB_CNT = CB_BAR + 8 * CB_STAGES;
 constexpr int CB_SMEM = CB_CNT + 4 * CB_STAGES + 8;
 
-template <int NP, bool Dyn, bool Front, bool Bulk = false>
-__global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
+template <bool Dyn, bool Front>
+__global__ void __launch_bounds__(128, 6) conv_vec_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ history, int ld_,
                                 const bf16* __restrict__ w, bf16* __restrict__ q, bf16* __restrict__ k,
                                 bf16* __restrict__ v, int key_packs, int value_packs, int run,
                                 const __grid_constant__ SeqTable tab_arg, const DevBatch* dyn,
                                 const __grid_constant__ FrontArgs fr) {
+    constexpr int NP = 2;  // channel pairs per thread
     using P = PackN<NP>;
     const SeqTable& tab = Dyn ? dyn->tab : tab_arg;  // the capacity path's table is in device memory
     constexpr int CH = 2 * NP;  // channels per thread
     grid_dep_wait();
     grid_dep_launch();
-    if constexpr (Front && !Bulk) {
-        if (blockIdx.x == gridDim.x - 1) {  // the gate CTA of this run of rows
-            const int T = tab.offset[tab.count];
-            const int t_begin = blockIdx.y * run, t_end = min(T, t_begin + run);
-            front_gates(fr, ld_, t_begin, 0, (t_end - t_begin) * fr.H);
-            return;
-        }
-    }
-    static_assert(!Bulk || NP == 2, "the staged variant takes 4 channels per thread");
     const int c = blockIdx.x * blockDim.x + threadIdx.x;  // pack of CH channels
     const int packs = 2 * key_packs + value_packs;
-    // the staged variant keeps every thread for the CTA's barriers
+    // lanes past the last pack stay for the ring's counts and barriers
     const bool active = c < packs;
-    if (!Bulk && !active) return;
     // Front: a q or k pack (warp-uniform: a head's packs are whole warps), whose rows' sums
     // of squares are taken
     const bool qk = Front && c < 2 * key_packs;
@@ -195,14 +186,14 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
             }
         }
     };
-    // Bulk: the ring, its barriers and counts
+    // the ring, its barriers and counts
     extern __shared__ __align__(128) uint8_t cbuf[];
     const int batches = (t_end - t_begin + 7) / 8;
-    const uint32_t ring = Bulk ? tc::smem_u32(cbuf) : 0u, bars = ring + CB_BAR;
+    const uint32_t ring = tc::smem_u32(cbuf), bars = ring + CB_BAR;
     int* cnt = reinterpret_cast<int*>(cbuf + CB_CNT);
     volatile int* issued = reinterpret_cast<volatile int*>(cbuf + CB_CNT + 4 * CB_STAGES);
     volatile int* abort_flag = issued + 1;
-    const int slice = Bulk ? min(128, packs - (int)blockIdx.x * 128) * (int)sizeof(P) : 0;
+    const int slice = min(128, packs - (int)blockIdx.x * 128) * (int)sizeof(P);
     const int lane = threadIdx.x & 31;
     auto issue = [&](int b) {
         const int st = b % CB_STAGES, r0 = t_begin + 8 * b, nr = min(8, t_end - r0);
@@ -213,7 +204,7 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
             tc::bulk_load(ring + st * CB_STAGE + i * CB_ROW, src + (size_t)i * ld_, (uint32_t)slice, bar);
         *issued = b + 1;
     };
-    if constexpr (Bulk) {
+    {
         if (threadIdx.x == 0) {
             for (int i = 0; i < CB_STAGES; i++) {
                 tc::mbar_init(bars + 8u * i, 1);
@@ -228,11 +219,10 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
             for (int b = 0; b < min(CB_STAGES, batches); b++) issue(b);
     }
     if (active) window(t_begin);
-    // rows in batches of 8: all loads of a batch are in flight before the first is used
+    // rows in batches of 8 (one stage of the ring each)
     for (int bi = 0; bi < batches; bi++) {
         const int tb = t_begin + 8 * bi;
-        P raw[8];
-        if constexpr (Bulk) {
+        {
             const int st = bi % CB_STAGES;
             const bool waited = tc::mbar_wait(bars + 8u * st, (uint32_t)(bi / CB_STAGES) & 1u);
             // warp-uniform decisions: a wait that gave up here, or another warp's
@@ -244,29 +234,23 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
                 }
                 break;
             }
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; i++)
-                if (tb + i < t_end) raw[i] = ld(col + (size_t)(tb + i) * ld_);
         }
         // this warp is done with the batch's stage: the last warp out refills it
         auto release = [&]() {
-            if constexpr (Bulk) {
-                __syncwarp();
-                if (lane == 0) {
-                    __threadfence_block();
-                    const int st = bi % CB_STAGES;
-                    if (atomicAdd(&cnt[st], 1) == CB_WARPS - 1) {
-                        cnt[st] = 0;
-                        if (bi + CB_STAGES < batches) {
-                            tc::fence_async_smem();
-                            issue(bi + CB_STAGES);
-                        }
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();
+                const int st = bi % CB_STAGES;
+                if (atomicAdd(&cnt[st], 1) == CB_WARPS - 1) {
+                    cnt[st] = 0;
+                    if (bi + CB_STAGES < batches) {
+                        tc::fence_async_smem();
+                        issue(bi + CB_STAGES);
                     }
                 }
             }
         };
-        if (active) {  // (the staged variant keeps lanes past the last pack for its counts)
+        if (active) {
         float ss8[8];  // Front: this thread's part of each row's sum of squares
 #pragma unroll
         for (int i = 0; i < 8; i++) ss8[i] = 0.f;
@@ -274,12 +258,9 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
         // part of the sum of squares, the window moved on by one row
         auto row = [&](int i, auto with_ss) {
             const int t = tb + i;
-            float2 x0[NP];
-            if constexpr (Bulk)  // row i of the batch's stage, read where it is used
-                unpack(*reinterpret_cast<const P*>(cbuf + (bi % CB_STAGES) * CB_STAGE + i * CB_ROW +
-                                                   threadIdx.x * sizeof(P)), x0);
-            else
-                unpack(raw[i], x0);
+            float2 x0[NP];  // row i of the batch's stage, read where it is used
+            unpack(*reinterpret_cast<const P*>(cbuf + (bi % CB_STAGES) * CB_STAGE + i * CB_ROW +
+                                               threadIdx.x * sizeof(P)), x0);
             P out;
 #pragma unroll
             for (int p = 0; p < NP; p++) {
@@ -377,7 +358,7 @@ __global__ void __launch_bounds__(128, Bulk ? 6 : NP == 2 ? (Front ? 6 : 8) : 4)
         }
         release();
     }
-    if constexpr (Bulk) {
+    {
         // after a wait gave up: the copies still in flight (the last CB_STAGES issued) land
         // before the CTA's shared memory is released
         __syncthreads();
@@ -510,17 +491,15 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
     const bool vec = key_dim % 8 == 0 && value_dim % 8 == 0 && ld % 8 == 0 && aligned16(qkv) && aligned16(w) &&
                      aligned16(q) && aligned16(k) && aligned16(v) && (!history || aligned16(history));
     if (vec) {
-        // 4 channels per thread: twice the threads at half the registers each (64: 8 CTAs of 128
-        // threads per SM instead of 4), which keeps more rows in flight
-        const bool narrow = key_dim % 4 == 0;  // 4 channels per thread (8 per thread otherwise)
-        const int cpt = narrow ? 4 : 8, tpacks = (2 * key_dim + value_dim) / cpt;
+        // 4 channels per thread (one 8-byte pack): with key and value widths multiples of 8,
+        // every CTA's row slice (up to 128 packs) is a multiple of 16 bytes, as the ring's
+        // bulk copies need
+        const int tpacks = (2 * key_dim + value_dim) / 4;
         const long groups = (tpacks + 127) / 128;
         // Runs of 64 rows, shortened (to 32, then 16) while the grid is below two waves of
-        // resident CTAs: a short prompt's CTAs each wait on a few batches of loads in series,
+        // resident CTAs (6 per SM): a short prompt's CTAs each wait on a few batches in series,
         // so more and shorter runs finish sooner.
-        // staged through shared memory when every CTA's row slice is a multiple of 16 bytes
-        const bool bulk = narrow && tpacks % 2 == 0;
-        const long waves2 = 2L * sm_count() * (bulk ? 6 : narrow ? 8 : 4);
+        const long waves2 = 2L * sm_count() * 6;
         int run = 64;
         while (run > 16 && groups * ((T + run - 1) / run) < waves2 && (T + run / 2 - 1) / (run / 2) <= 65535)
             run /= 2;
@@ -529,26 +508,14 @@ int conv_launch(const void* qkv, const void* history, int ld, const void* w, voi
         if (front) fr = *front;
         void (*kernel)(const bf16*, const bf16*, int, const bf16*, bf16*, bf16*, bf16*, int, int, int, SeqTable,
                        const DevBatch*, FrontArgs);
-        if (bulk) {
-            if (front)
-                kernel = dyn ? conv_vec_kernel<2, true, true, true> : conv_vec_kernel<2, false, true, true>;
-            else
-                kernel = dyn ? conv_vec_kernel<2, true, false, true> : conv_vec_kernel<2, false, false, true>;
-        } else if (front) {
-            kernel = dyn ? (narrow ? conv_vec_kernel<2, true, true> : conv_vec_kernel<4, true, true>)
-                         : (narrow ? conv_vec_kernel<2, false, true> : conv_vec_kernel<4, false, true>);
-        } else {
-            kernel = dyn ? (narrow ? conv_vec_kernel<2, true, false> : conv_vec_kernel<4, true, false>)
-                         : (narrow ? conv_vec_kernel<2, false, false> : conv_vec_kernel<4, false, false>);
-        }
-        // the front end adds one gate CTA per run of rows (the staged kernel shares the gates
-        // out over its CTAs of v packs instead)
-        return launch_pdl(kernel,
-                          dim3((unsigned)(groups + (front && !bulk ? 1 : 0)), (T + run - 1) / run), dim3(128),
-                          bulk ? (size_t)CB_SMEM : 0, st,
+        if (front)
+            kernel = dyn ? conv_vec_kernel<true, true> : conv_vec_kernel<false, true>;
+        else
+            kernel = dyn ? conv_vec_kernel<true, false> : conv_vec_kernel<false, false>;
+        return launch_pdl(kernel, dim3((unsigned)groups, (T + run - 1) / run), dim3(128), (size_t)CB_SMEM, st,
                           static_cast<const bf16*>(qkv), static_cast<const bf16*>(history), ld,
                           static_cast<const bf16*>(w), static_cast<bf16*>(q), static_cast<bf16*>(k),
-                          static_cast<bf16*>(v), key_dim / cpt, value_dim / cpt, run, tab, dyn, fr);
+                          static_cast<bf16*>(v), key_dim / 4, value_dim / 4, run, tab, dyn, fr);
     } else {
         // the capacity path and the front end need the vector kernel
         if (dyn || front) return cudaErrorInvalidValue;
