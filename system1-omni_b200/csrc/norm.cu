@@ -68,90 +68,16 @@ __global__ void __launch_bounds__(NT) rms_kernel(bf16* __restrict__ res, const b
     }
 }
 
-// One warp per row for D <= 32 * 8 * PPL: every 16-byte pack of the row is loaded before
-// the warp reduces it (no block barrier), the weights sit in shared memory, and each warp
-// walks rows with a grid stride. The add variant keeps the bf16 sums packed in registers.
-// Up to RW_WARPS warps per CTA; fewer when the rows do not fill every SM (rms_warp_shape).
-constexpr int PPL = 20;  // packs per lane: D <= 5120
-constexpr int RW_WARPS = 8;
-template <bool Add>
-__global__ void __launch_bounds__(RW_WARPS * 32) rms_warp_kernel(bf16* __restrict__ res, const bf16* __restrict__ delta,
-                                                                 const bf16* __restrict__ x, const bf16* __restrict__ w,
-                                                                 bf16* __restrict__ out, int rows, int D, float eps,
-                                                                 const DevBatch* dyn) {
-    __shared__ Pack8 wsm[32 * PPL];
-    grid_dep_wait();
-    grid_dep_launch();
-    rows = dyn_rows(dyn, rows);
-    const int packs = D >> 3, lane = threadIdx.x & 31;
-    for (int i = threadIdx.x; i < packs; i += blockDim.x) wsm[i] = ld8(w + (size_t)i * 8);
-    __syncthreads();
-    const int cta_warps = blockDim.x >> 5, warps = gridDim.x * cta_warps;
-    for (int row = blockIdx.x * cta_warps + (threadIdx.x >> 5); row < rows; row += warps) {
-        const size_t off = (size_t)row * D;
-        Pack8 v[PPL];
-        if constexpr (Add) {
-            Pack8 b[PPL];
-#pragma unroll
-            for (int i = 0; i < PPL; i++) {
-                const int pk = lane + 32 * i;
-                if (pk < packs) {
-                    v[i] = ld8(res + off + (size_t)pk * 8);
-                    b[i] = ld8(delta + off + (size_t)pk * 8);
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < PPL; i++) {
-                const int pk = lane + 32 * i;
-                if (pk < packs) {
-                    float fa[8], fb[8];
-                    unpack8(v[i], fa);
-                    unpack8(b[i], fb);
-#pragma unroll
-                    for (int e = 0; e < 8; e++) fa[e] += fb[e];
-                    v[i] = pack8(fa);
-                    st8(res + off + (size_t)pk * 8, v[i]);
-                }
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < PPL; i++) {
-                const int pk = lane + 32 * i;
-                if (pk < packs) v[i] = ld8(x + off + (size_t)pk * 8);
-            }
-        }
-        float ss = 0.f;
-#pragma unroll
-        for (int i = 0; i < PPL; i++) {
-            if (lane + 32 * i < packs) {
-                float f[8];
-                unpack8(v[i], f);
-#pragma unroll
-                for (int e = 0; e < 8; e++) ss = fmaf(f[e], f[e], ss);
-            }
-        }
-        const float inv = rsqrtf(warp_sum(ss) / D + eps);
-#pragma unroll
-        for (int i = 0; i < PPL; i++) {
-            const int pk = lane + 32 * i;
-            if (pk < packs) {
-                float f[8], wv[8], o[8];
-                unpack8(v[i], f);
-                unpack8(wsm[pk], wv);
-#pragma unroll
-                for (int e = 0; e < 8; e++) o[e] = f[e] * inv * (1.f + wv[e]);
-                st8(out + off + (size_t)pk * 8, pack8(o));
-            }
-        }
-    }
-}
+constexpr int PPL = 20;  // packs of 8 per lane in the warp-per-row kernel: D <= 5120
 
-// Staged variant of the warp-per-row kernel: each warp owns a ring of RB_STAGES row slots in
-// shared memory (the residual and the delta row for the add variant); its lane 0 copies the
-// warp's next row in by bulk copies while the warp normalises the current one, so a row's
-// bytes are in flight without registers and the warps never wait for one another. The
-// weights sit in shared memory, loaded once per CTA; each warp walks rows with a grid stride.
-__host__ __device__ constexpr int rb_warps(bool add) { return 8; }
+// One warp per row for D <= 32 * 8 * PPL, rows staged in shared memory: each warp owns a
+// ring of row slots (the residual and the delta row for the add variant, one slot; two slots
+// otherwise); its lane 0 copies the warp's next row in by bulk copies while the warp
+// normalises the current one, so a row's bytes are in flight without registers and the warps
+// never wait for one another. The weights sit in shared memory, loaded once per CTA; each
+// warp walks rows with a grid stride; one CTA of 8 warps per SM.
+constexpr int RB_WARPS = 8;
+__host__ __device__ constexpr int rb_warps(bool) { return RB_WARPS; }
 __host__ __device__ constexpr int rb_stages(bool add) { return add ? 1 : 2; }
 __host__ __device__ constexpr int rb_smem(bool add, int D) {
     return D * 2 + rb_warps(add) * rb_stages(add) * (add ? 2 : 1) * D * 2 + 8 * rb_warps(add) * rb_stages(add);
@@ -246,18 +172,6 @@ __global__ void __launch_bounds__(rb_warps(Add) * 32, 1) rms_bulk_kernel(bf16* _
         for (int j = k; j < k + RB_STAGES && g0 + j * gstep < rows; j++)
             (void)tc::mbar_wait(bars + 8u * (j % RB_STAGES), (uint32_t)(j / RB_STAGES) & 1u);
     }
-}
-
-// Grid and block of rms_warp_kernel: RW_WARPS warps per CTA and at most 8 CTAs per SM
-// (grid stride beyond), or, when the rows are fewer than RW_WARPS per SM, ceil(rows / SMs)
-// warps per CTA, so that every SM takes a share instead of a few SMs taking 8 rows each.
-void rms_warp_shape(int rows, dim3& grid, dim3& block) {
-    const int sms = sm_count();
-    int w = (rows + sms - 1) / sms;
-    w = w < 1 ? 1 : w > RW_WARPS ? RW_WARPS : w;
-    const int need = (rows + w - 1) / w;
-    grid = dim3(need < sms * 8 ? need : sms * 8);
-    block = dim3(32 * w);
 }
 
 // Any D: scalar path, two passes over the row.
@@ -406,7 +320,7 @@ int rms_norm(const void* x, const void* w, void* out, int rows, int D, float eps
                           dim3(rb_warps(false) * 32), (size_t)rb_smem(false, D), st, static_cast<bf16*>(nullptr),
                           static_cast<const bf16*>(nullptr), X, Wt, O, rows, D, eps, dyn);
     }
-    if (dyn) return cudaErrorInvalidValue;  // the capacity path needs the warp-per-row kernel
+    if (dyn) return cudaErrorInvalidValue;  // the capacity path needs the staged warp-per-row kernel
     if (vec_ok(D, x, w, out, out))
         rms_kernel<false><<<rows, NT, 0, st>>>(nullptr, nullptr, X, Wt, O, D, eps);
     else
