@@ -16,7 +16,8 @@
 // One CTA (512 threads, one per SM: ~205 KB of shared memory, all 512 TMEM columns) per
 // (value head, sequence), longest sequences first, walking the chunks in order:
 //   warp 0       TMA producer: q and k rows of the key head (double-buffered), v rows of
-//                the value head (single buffer, refilled as soon as its MMA has read it)
+//                the value head (single buffer, refilled as soon as its MMA has read it, on
+//                its own barrier so that the next q and k do not wait for it)
 //   warp 1       scan MMA issuer:  (wS)^T, (qd S)^T = S^T [w^T | qd^T]   (A = S^T in TMEM)
 //                                  o^T += v_new^T P^T,  S^T += v_new^T kd  (A = v_new^T in TMEM)
 //   warp 2       prep MMA issuer:  D1 = [k; q] k^T                         (raw bf16, K = 128)
@@ -95,7 +96,7 @@ constexpr uint32_t TM_S = 0, TM_ST = 128, TM_WS = 192, TM_O = 256, TM_D1 = 320, 
 
 // barrier indices (8 bytes each)
 enum Bar : int {
-    B_IN_FULL = 0,      // [2] q, k (slot) and v landed
+    B_IN_FULL = 0,      // [2] q, k (slot) landed
     B_IN_KQ_FREE = 2,   // [2] preparation and scan warps done with the q, k slot (count 12)
     B_IN_V_FREE = 4,    // MMA2 read v
     B_D1_FULL = 5,      // MMA1 done
@@ -118,6 +119,7 @@ enum Bar : int {
     B_W_FREE = 32,      // [2] the first scan MMAs read the slot's w
     B_P_FREE = 34,      // [2] the second scan MMAs read the slot's P
     B_OPS2_READY = 36,  // [2] P of the chunk written into the slot by the preparation (count 8)
+    B_V_FULL = 38,      // v landed (its own barrier: q and k need not wait for v's buffer)
 };
 
 struct Maps {
@@ -184,6 +186,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int i = 0; i < 4; i++) mbar_init(bar(B_DEC_READY + i), 1);
         mbar_init(bar(B_IN_V_FREE), 1);
+        mbar_init(bar(B_V_FULL), 1);
         mbar_init(bar(B_D1_FULL), 1);
         mbar_init(bar(B_D1W_FREE), 8);
         mbar_init(bar(B_TB_READY), 8);
@@ -217,29 +220,38 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_prefetch_desc(&maps.q);
             tma_prefetch_desc(&maps.k);
             tma_prefetch_desc(&maps.v);
-            int issued = 0;
+            int issued = 0, issued_v = 0;
             for (int c = 0; c < NC; c++) {
                 if (*abort_flag) break;
                 const int slot = c & 1;
-                if (!mbar_wait(bar(B_IN_KQ_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u) ||
-                    !mbar_wait(bar(B_IN_V_FREE), (uint32_t)(c + 1) & 1u)) {
+                const int t0 = start + c * C;
+                // q and k into their slot as soon as it is free; v (one buffer) once the
+                // previous chunk's MMA2 has read it, on its own barrier
+                if (!mbar_wait(bar(B_IN_KQ_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u)) {
                     fail(FAULT_WAIT_PRODUCER, abort_flag);
                     break;
                 }
                 const uint32_t kq = base + OFF_KQ + slot * KQ_TILE, full = bar(B_IN_FULL + slot);
-                const int t0 = start + c * C;
-                mbar_expect_tx(full, 6 * BOX);
+                mbar_expect_tx(full, 4 * BOX);
 #pragma unroll
                 for (int b = 0; b < 2; b++) {
                     tma_load_3d(kq + b * 2 * BOX, &maps.k, full, 64 * b, hk, t0);
                     tma_load_3d(kq + b * 2 * BOX + BOX, &maps.q, full, 64 * b, hk, t0);
-                    tma_load_3d(base + OFF_V + b * BOX, &maps.v, full, 64 * b, h, t0);
                 }
                 issued++;
+                if (!mbar_wait(bar(B_IN_V_FREE), (uint32_t)(c + 1) & 1u)) {
+                    fail(FAULT_WAIT_PRODUCER, abort_flag);
+                    break;
+                }
+                mbar_expect_tx(bar(B_V_FULL), 2 * BOX);
+#pragma unroll
+                for (int b = 0; b < 2; b++) tma_load_3d(base + OFF_V + b * BOX, &maps.v, bar(B_V_FULL), 64 * b, h, t0);
+                issued_v++;
             }
             // the copies in flight land before the CTA can leave
             for (int c = issued > 2 ? issued - 2 : 0; c < issued; c++)
                 (void)mbar_wait(bar(B_IN_FULL + (c & 1)), (uint32_t)(c >> 1) & 1u);
+            if (issued_v > 0) (void)mbar_wait(bar(B_V_FULL), (uint32_t)(issued_v - 1) & 1u);
         }
     } else if (warp == 1) {
         // ---------------------------------------------------------------- scan MMAs
@@ -312,7 +324,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 mma_commit(bar(B_D1_FULL));
                 if (!mbar_wait(bar(B_TB_READY), (uint32_t)c & 1u) ||
-                    !mbar_wait(bar(B_U_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u)) {
+                    !mbar_wait(bar(B_U_FREE + slot), (uint32_t)((c >> 1) + 1) & 1u) ||
+                    !mbar_wait(bar(B_V_FULL), (uint32_t)c & 1u)) {
                     ok = false;
                     break;
                 }
