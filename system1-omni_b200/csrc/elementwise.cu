@@ -102,9 +102,9 @@ __device__ __noinline__ void front_gates(const FrontArgs& fr, int ld, int t_begi
 // The conv kernel takes 4 channels per thread (one 8-byte pack); a CTA of 128 threads covers
 // 128 packs of a run of rows. Each CTA's slice of a row (contiguous) is copied into a ring of
 // CB_STAGES batches of 8 rows by bulk copies, so up to 32 KB per CTA are in flight without
-// holding registers; the threads read their packs from shared memory. The warps do not wait for one another: each counts itself out
-// of a batch's stage when it is done with it, and the last of the four issues the copies of
-// the batch CB_STAGES ahead into that stage.
+// holding registers; the threads read their packs from shared memory. The warps do not wait
+// for one another: each counts itself out of a batch's stage when it is done with it, and the
+// last of the four issues the copies of the batch CB_STAGES ahead into that stage.
 constexpr int CB_STAGES = 4;
 constexpr int CB_WARPS = 4;
 constexpr int CB_ROW = 128 * 8;               // bytes of a row slice (128 threads x 8 bytes)
