@@ -40,8 +40,10 @@ def _run(cs1, stream, q, k, v, g, beta, H, HK, s_in=None, want_state=False):
     return host(o), (host(s_out) if want_state else None)
 
 
+# (4096, 4, 2): 64 chunks, many turns of the double-buffered operand slots and of the single
+# v buffer that loads on its own barrier
 @pytest.mark.parametrize("T,H,HK", [(1, 4, 2), (16, 4, 2), (63, 4, 2), (64, 4, 4), (65, 4, 2), (129, 8, 4),
-                                    (300, 4, 2), (936, 48, 16)])
+                                    (300, 4, 2), (936, 48, 16), (4096, 4, 2)])
 def test_gdn_matches_float64_recurrence(cs1, stream, T, H, HK):
     q, k, v, g, beta = _inputs(T, H, HK, seed=T)
     o, s = _run(cs1, stream, q, k, v, g, beta, H, HK, want_state=True)
