@@ -811,22 +811,40 @@ __global__ void __launch_bounds__(THREADS, 1)
                 float acc[N];
 #pragma unroll
                 for (int e = 0; e < N; e++) acc[e] = 0.f;
+                // (entry pairs, N = 2, are read as float2: j0 is even)
+                auto pair2 = [](const float* p2) { return *reinterpret_cast<const float2*>(p2); };
 #pragma unroll
                 for (int m = 0; m < HB; m++) {
                     const float a = adiag(o1 + i, o0 + m);
-#pragma unroll
-                    for (int e = 0; e < N; e++) acc[e] = fmaf(a, tdiag(o0 + m, o0 + j0 + e), acc[e]);
+                    if constexpr (N == 2) {
+                        const float2 t2 = pair2(&tdiag(o0 + m, o0 + j0));
+                        acc[0] = fmaf(a, t2.x, acc[0]);
+                        acc[1] = fmaf(a, t2.y, acc[1]);
+                    } else {
+                        acc[0] = fmaf(a, tdiag(o0 + m, o0 + j0), acc[0]);
+                    }
                 }
 #pragma unroll
                 for (int e = 0; e < N; e++) xs[idx + e] = acc[e];
                 named_bar_sync(BAR_PREP, NPREP);
 #pragma unroll
                 for (int e = 0; e < N; e++) acc[e] = 0.f;
+                const float* trow = &tdiag(o1 + i, o1);  // row o1 + i of the diagonal block, 16-byte aligned
 #pragma unroll
-                for (int m = 0; m < HB; m++) {
-                    const float t_ = tdiag(o1 + i, o1 + m);
+                for (int m4 = 0; m4 < HB; m4 += 4) {
+                    const float4 t4 = *reinterpret_cast<const float4*>(trow + m4);
+                    const float tv[4] = {t4.x, t4.y, t4.z, t4.w};
 #pragma unroll
-                    for (int e = 0; e < N; e++) acc[e] = fmaf(t_, xs[m * HB + j0 + e], acc[e]);
+                    for (int e4 = 0; e4 < 4; e4++) {
+                        const int m = m4 + e4;
+                        if constexpr (N == 2) {
+                            const float2 x2 = pair2(xs + m * HB + j0);
+                            acc[0] = fmaf(tv[e4], x2.x, acc[0]);
+                            acc[1] = fmaf(tv[e4], x2.y, acc[1]);
+                        } else {
+                            acc[0] = fmaf(tv[e4], xs[m * HB + j0], acc[0]);
+                        }
+                    }
                 }
                 if (ok) {
 #pragma unroll
