@@ -29,9 +29,9 @@
 //                v_new^T = bf16(bf16(u) - wS) (TMEM), the next chunk's qd and kd operand
 //                tiles, o rows straight to global memory
 //   warps 8-15   preparation of the next chunk while the scan runs: norms, kw, A and P from
-//                D1, the 64 x 64 inverse (two 32 x 32 diagonal blocks by right-looking
-//                substitution, then the block below them) written out as tb, then w (from
-//                TMEM)
+//                D1, the 64 x 64 inverse by block doubling (8 x 8 diagonal blocks by
+//                substitution, then the blocks below the diagonal at 16, 32 and 64) written
+//                out as tb, then w (from TMEM)
 // TMEM columns: [0,128) S^T fp32 | [128,192) S^T bf16 pairs | [192,256) wS fp32, then
 // v_new^T bf16 pairs | [256,320) o^T fp32 | [320,384) D1 fp32, then w^T fp32 |
 // [384,512) u^T fp32, two chunk buffers.
