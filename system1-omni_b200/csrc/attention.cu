@@ -162,7 +162,7 @@ struct Args {
 // A CTA takes 128 queries of one head. Per 128-key tile j:
 //   S_j = Q K_j^T   tcgen05.mma M=128 N=128 K=256 into one of two TMEM buffers
 //   softmax         4 warps, thread = query row = TMEM lane: masked row max, exp2,
-//                   bf16 P_j into shared memory (the A operand of the next MMA)
+//                   bf16 P_j into tensor memory over S_j (the A operand of PV_j)
 //   O += P_j V_j    tcgen05.mma M=128 N=256 K=128 into TMEM (V as an MN-major B operand)
 // The MMA thread issues S_{j+1} before PV_j, so the tensor pipe computes the next
 // scores while the softmax warps work. O is rescaled only when a row's maximum grows
@@ -552,27 +552,38 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int t = threadIdx.x - 64, chunk = t & 31;
             const bf16* gs = reinterpret_cast<const bf16*>(smem + OFF_K);
             if (a.gated) cp_async_wait_all();  // this thread's own gate units (fetched at the last tile)
-            // every row's loads unconditional (the staging tile is whole), only the stores past
-            // the sequence's end skipped, so the loads of several rows can be in flight
+            // groups of 8 rows: the group's shared-memory loads (all unconditional, the staging
+            // tile is whole) are written before its stores, since a store through the generic
+            // output pointer may alias shared memory as far as the compiler knows and no load
+            // written after it could be issued ahead of it; only stores past the end are skipped
             const int rows = min(BM, len - q0);
-#pragma unroll 8
-            for (int i = 0; i < BM / 4; i++) {
-                const int row = (t >> 5) + 4 * i;
-                const Pack8 xv = ld8(stage + row * DH + ((chunk ^ row) & 31) * 8);
-                const size_t o_off = ((size_t)(off + q0 + row) * a.Hq + h) * DH + chunk * 8;
-                if (a.gated) {
-                    const Pack8 gv = ld8(gs + row * DH + chunk * 8);
-                    Pack8 y;
+            constexpr int GR = 8;
+#pragma unroll 1
+            for (int i0 = 0; i0 < BM / 4; i0 += GR) {
+                Pack8 xv[GR], gv[GR];
 #pragma unroll
-                    for (int p2 = 0; p2 < 4; p2++) {
-                        // out = x * bf16(sigmoid(gate))
-                        const float2 sg = rbf2(sigmoid2_fast(__bfloat1622float2(gv.h[p2])));
-                        const float2 o2 = mul2(__bfloat1622float2(xv.h[p2]), sg);
-                        y.h[p2] = __floats2bfloat162_rn(o2.x, o2.y);
+                for (int u = 0; u < GR; u++) {
+                    const int row = (t >> 5) + 4 * (i0 + u);
+                    xv[u] = ld8(stage + row * DH + ((chunk ^ row) & 31) * 8);
+                    if (a.gated) gv[u] = ld8(gs + row * DH + chunk * 8);
+                }
+#pragma unroll
+                for (int u = 0; u < GR; u++) {
+                    const int row = (t >> 5) + 4 * (i0 + u);
+                    const size_t o_off = ((size_t)(off + q0 + row) * a.Hq + h) * DH + chunk * 8;
+                    if (a.gated) {
+                        Pack8 y;
+#pragma unroll
+                        for (int p2 = 0; p2 < 4; p2++) {
+                            // out = x * bf16(sigmoid(gate))
+                            const float2 sg = rbf2(sigmoid2_fast(__bfloat1622float2(gv[u].h[p2])));
+                            const float2 o2 = mul2(__bfloat1622float2(xv[u].h[p2]), sg);
+                            y.h[p2] = __floats2bfloat162_rn(o2.x, o2.y);
+                        }
+                        if (row < rows) st8(a.out + o_off, y);
+                    } else if (row < rows) {
+                        st8(a.out + o_off, xv[u]);
                     }
-                    if (row < rows) st8(a.out + o_off, y);
-                } else if (row < rows) {
-                    st8(a.out + o_off, xv);
                 }
             }
         }

@@ -454,11 +454,10 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (lane == 0) mbar_arrive(bar(B_S_READY));
             return true;
         };
-        // The o rows of chunk c: this thread's column v of each row, 2-byte stores (a warp
-        // writes 64 contiguous bytes of a row per store).
-        // Adjacent lanes swap halves so that each stores two adjacent columns of one row: the
-        // even lane rows 2i, the odd lane rows 2i + 1 (a warp writes 64 contiguous bytes of each
-        // of two rows per store).
+        // The o rows of chunk c from this thread's column v of each row. Adjacent lanes swap
+        // halves so that each stores two adjacent columns of one row: the even lane rows 2i,
+        // the odd lane rows 2i + 1 (a warp writes 64 contiguous bytes of each of two rows per
+        // store).
         auto write_o = [&](int c, const uint32_t (&opk)[32]) {
             const int rows = min(C, len - c * C);
             const bool odd = lane & 1;
