@@ -225,9 +225,28 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 192);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    if (warp == 0) {
+    if (warp == 0 && a.q_base == 0) {
         // blockIdx.y -> (sequence, query block): sequences in the table's order (longest
-        // first), the blocks of one sequence last-first (the most key tiles first)
+        // first), the blocks of one sequence last-first (the most key tiles first), by a
+        // binary search of the block prefix sums (every access the same for the warp)
+        if (lane == 0) {
+            const int target = blockIdx.y;
+            info[0] = -1;
+            if (target < tab.qcum[tab.count]) {
+                int lo = 0, hi = tab.count;  // qcum[lo] <= target < qcum[hi]
+                while (hi - lo > 1) {
+                    const int mid = (lo + hi) >> 1;
+                    if (tab.qcum[mid] <= target)
+                        lo = mid;
+                    else
+                        hi = mid;
+                }
+                info[0] = tab.order[lo];
+                info[1] = tab.qcum[lo + 1] - 1 - target;
+            }
+        }
+    } else if (warp == 0) {
+        // the same mapping for a first query row q_base > 0 (blocks counted from it)
         const int target = blockIdx.y;
         if (Dyn && lane == 0) info[0] = -1;
         __syncwarp();

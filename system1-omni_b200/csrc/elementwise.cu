@@ -38,6 +38,8 @@ bool make_table(SeqTable& t, const size_t* lengths, size_t count) {
         }
         t.order[j] = (int)i;
     }
+    t.qcum[0] = 0;
+    for (size_t i = 0; i < count; i++) t.qcum[i + 1] = t.qcum[i] + (int)((lengths[t.order[i]] + 127) / 128);
     return true;
 }
 

@@ -21,6 +21,9 @@ struct SeqTable {
     int max_len;
     int offset[MAX_SEQS + 1];
     int order[MAX_SEQS];  // sequence indices by decreasing length (longest work scheduled first)
+    // prefix sums of 128-row query blocks in `order`: the blocks of sequence order[i] are
+    // [qcum[i], qcum[i + 1]) (the attention kernel's work index, found by a uniform search)
+    int qcum[MAX_SEQS + 1];
 };
 
 // Build a table from host lengths; false if count is 0 or above MAX_SEQS, a length is
