@@ -169,3 +169,46 @@ def test_request_cost_counts_candidates_over_the_prompt():
     lin = cfg.projection_flops_per_token()
     assert request_cost(cfg, 100, [10, 20]) > request_cost(cfg, 100) + lin * 30
     assert request_cost(cfg, 0, [64]) == request_cost(cfg, 64)
+
+
+def test_batch_descriptor_layout_and_work_index():
+    """The capacity path's descriptor, packed on the host without a GPU: packed row
+    offsets, sequences by decreasing length (stable), and the prefix sums of 128-row
+    query blocks in that order that the attention kernel's CTAs search for their
+    (sequence, query block)."""
+    from s1omni import Cs1
+    cs1 = Cs1()
+    MAX = 256
+    n = cs1.cs1_batch_desc_bytes()
+    assert n == 4 * (4 + 2 + (MAX + 1) + MAX + (MAX + 1))
+    rng = np.random.default_rng(11)
+    for lengths in ([1], [128], [129], [37, 100, 5, 64, 100, 300], list(rng.integers(1, 3000, 256))):
+        buf = np.zeros(n, np.uint8)
+        arr = np.asarray(lengths, dtype=np.uintp)
+        assert cs1.raw.cs1_batch_desc_pack(arr.ctypes.data, len(lengths), buf.ctypes.data, n) == 0
+        w = buf.view(np.int32)
+        rows, tab = w[0], w[4:]
+        count, max_len = tab[0], tab[1]
+        offset = tab[2:2 + MAX + 1]
+        order = tab[2 + MAX + 1:2 + MAX + 1 + MAX]
+        qcum = tab[2 + MAX + 1 + MAX:]
+        c = len(lengths)
+        assert (rows, count, max_len) == (sum(lengths), c, max(lengths))
+        assert list(offset[:c + 1]) == [0] + list(np.cumsum(lengths))
+        want_order = sorted(range(c), key=lambda i: (-lengths[i], i))
+        assert list(order[:c]) == want_order
+        blocks = [(lengths[i] + 127) // 128 for i in want_order]
+        assert list(qcum[:c + 1]) == [0] + list(np.cumsum(blocks))
+        # the kernel's search: the last i with qcum[i] <= target, block counted from the end
+        for target in range(int(qcum[c])):
+            lo, hi = 0, c
+            while hi - lo > 1:
+                mid = (lo + hi) // 2
+                lo, hi = (mid, hi) if qcum[mid] <= target else (lo, mid)
+            seq, qb = order[lo], qcum[lo + 1] - 1 - target
+            assert 0 <= qb < (lengths[seq] + 127) // 128
+        seen = set()
+        for target in range(int(qcum[c])):
+            lo = int(np.searchsorted(qcum[:c + 1], target, side="right")) - 1
+            seen.add((int(order[lo]), int(qcum[lo + 1] - 1 - target)))
+        assert seen == {(i, b) for i in range(c) for b in range((lengths[i] + 127) // 128)}
